@@ -1,0 +1,63 @@
+// Host-side helpers shared by the library's translation units (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstddef>
+#include <cstdio>
+#include <string>
+
+#include "vella_cuda.h"
+
+namespace vella {
+
+// Per-thread message of the last failing call (vella_last_error).
+std::string& last_error_slot();
+
+inline int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  last_error_slot() = buf;
+  return code;
+}
+
+inline int cuda_fail(cudaError_t e, const char* what) {
+  return fail(VELLA_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define VELLA_CUDA_TRY(call)                                   \
+  do {                                                         \
+    cudaError_t e_ = (call);                                   \
+    if (e_ != cudaSuccess) return ::vella::cuda_fail(e_, #call); \
+  } while (0)
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int num_sms(int device);
+
+// Library-owned per-device workspace (vella_qgemm with workspace == NULL).  Grows on
+// demand; the returned memory is zero-filled when first handed out.
+int device_workspace(size_t bytes, void** out);
+
+// ---- GEMM (qgemm.cu) -------------------------------------------------------------------
+struct QgemmPlan {
+  int rows_out;   // output rows per CTA (128, or 64 with the SiLU gate)
+  int rowblocks;  // ceil(N / rows_out)
+  int kc;         // groups of 64 per CTA
+  int splits;     // CTAs along K
+  int zchunks;    // ceil(M / 16)
+  size_t workspace;
+};
+
+bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* plan);
+
+int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& plan, const void* x, const void* w,
+                 const void* scales, const void* biases, const void* up_w, const void* up_scales,
+                 const void* up_biases, const void* bias, const void* residual, void* out, void* ws,
+                 cudaStream_t stream);
+
+}  // namespace vella

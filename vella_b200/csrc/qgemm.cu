@@ -1,0 +1,488 @@
+// K1: small-M (1-16 rows per pass) GEMM over MLX-affine int4/int8 or dense bf16/fp16
+// weights, out[M, N] = epilogue(x[M, K] . W^T).
+//
+// Reference: Worker/Sources/SmallMGEMM/SmallMGEMM.swift:662-755 (smallm_gemv_affine, the
+// product form acc += s * sum(x*q) + b * sum(x), fp32 accumulation, epilogue GATE -> bias
+// -> residual, one rounding) and :585-656 (dense GEMV).
+//
+// B200 design.  The kernel streams the weights once from HBM; x is tiny.  Each warp owns
+// 32 weight rows (two m16 tiles; with the SiLU gate: 16 gate rows + the same 16 up rows)
+// and issues tensor-core m16n8k16 MMAs with the *weights as the A operand* and x^T as B,
+// so M <= 8 needs one n8 tile and M <= 16 two.  Weights are dequantized in registers:
+// (word >> s) & 0x000F000F | 0x43004300 turns two 4-bit codes into the bf16 pair
+// (128 + q_a, 128 + q_b) in one LOP3, which is exact; the 128 offset is removed in the
+// per-group scale step, acc += s * D + (b - 128 s) * sum(x), i.e. the reference's product
+// form with D = sum(x * (128 + q)).  8-bit codes are split into low and high nibbles (two
+// MMAs, D = D_lo + 16 D_hi).  Within one MMA the k positions may be permuted freely as
+// long as A and B agree, so each thread's four k slots are the nibbles its one 8/16-byte
+// load delivers, and x is staged in shared memory in the matching permuted order
+// (with the per-group sums sum(x) precomputed), once per CTA.
+//
+// Work split: a CTA (4 warps) covers 128 output rows (64 with the gate) x KC groups of
+// 64 along K; `splits` CTAs along K write fp32 partial tiles to a workspace and the CTA
+// that arrives last (atomic ticket, no waiting) adds them in split order and runs the
+// epilogue.  The plan depends on (N, K, bits, gate) only, never on M, and every output
+// row is computed by the same instruction sequence whatever the other rows are: a row of
+// a batched call is bit-identical to the same row computed alone (verify == greedy).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace vella {
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kSlots = 128;  // weight rows staged per CTA (gate: 64 gate + 64 up)
+constexpr int kKCMax = 32;
+constexpr int kTokMax = 16;  // tokens per pass (z chunk)
+
+struct Args {
+  const void* x;
+  const uint32_t* w;
+  const void* sc;
+  const void* bi;
+  const uint32_t* uw;
+  const void* usc;
+  const void* ubi;
+  const void* bias;
+  const void* res;
+  void* out;
+  float* partial;
+  int* counters;
+  int M, N, K, G, KC, S, rowblocks;
+  int has_bias, has_res;
+  int sb_stride;  // float2 per slot row in shared memory
+};
+
+// Words of packed weight per row and group of 64, and per thread (k quarter) of a group.
+template <int BITS> struct Fmt;
+template <> struct Fmt<4> { static constexpr int kWordsPerGroup = 8, kWordsPerThread = 2; };
+template <> struct Fmt<8> { static constexpr int kWordsPerGroup = 16, kWordsPerThread = 4; };
+template <> struct Fmt<0> { static constexpr int kWordsPerGroup = 32, kWordsPerThread = 8; };
+
+// Register prefetch depth (groups in flight per warp): about 3-4 KB per warp.
+template <int BITS> struct Depth { static constexpr int kPF = BITS == 4 ? 4 : 2; };
+
+template <int BITS>
+__device__ __forceinline__ void load_words(uint32_t* dst, const uint32_t* p) {
+  if constexpr (BITS == 4) {
+    uint2 v = ld_stream2(p);
+    dst[0] = v.x; dst[1] = v.y;
+  } else if constexpr (BITS == 8) {
+    uint4 v = ld_stream4(p);
+    dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+  } else {
+    uint4 v = ld_stream4(p);
+    uint4 u = ld_stream4(p + 4);
+    dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+    dst[4] = u.x; dst[5] = u.y; dst[6] = u.z; dst[7] = u.w;
+  }
+}
+
+// Natural x words n[0..7] (n[i] = x[2i], x[2i+1]) -> the k order the A dequant delivers.
+template <int BITS>
+__device__ __forceinline__ void permute_x(uint32_t (&p)[8], const uint32_t (&n)[8]) {
+  if constexpr (BITS == 4) {
+    // pairs (0,4) (1,5) (2,6) (3,7) (8,12) (9,13) (10,14) (11,15)
+    p[0] = __byte_perm(n[0], n[2], 0x5410); p[1] = __byte_perm(n[0], n[2], 0x7632);
+    p[2] = __byte_perm(n[1], n[3], 0x5410); p[3] = __byte_perm(n[1], n[3], 0x7632);
+    p[4] = __byte_perm(n[4], n[6], 0x5410); p[5] = __byte_perm(n[4], n[6], 0x7632);
+    p[6] = __byte_perm(n[5], n[7], 0x5410); p[7] = __byte_perm(n[5], n[7], 0x7632);
+  } else if constexpr (BITS == 8) {
+    // pairs (0,2) (1,3) (4,6) (5,7) ...
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      p[2 * j] = __byte_perm(n[2 * j], n[2 * j + 1], 0x5410);
+      p[2 * j + 1] = __byte_perm(n[2 * j], n[2 * j + 1], 0x7632);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) p[i] = n[i];
+  }
+}
+
+template <typename T, int BITS, int NT, bool GATE>
+__global__ void __launch_bounds__(kThreads) qgemm_kernel(const Args a) {
+  using A = Act<T>;
+  constexpr int WPG = Fmt<BITS>::kWordsPerGroup;
+  constexpr int WPT = Fmt<BITS>::kWordsPerThread;
+  constexpr int PF = Depth<BITS>::kPF;
+  constexpr int TOK = NT * 8;
+  constexpr uint32_t kMask = 0x000F000Fu;
+  constexpr uint32_t kMag = A::kMagic2;
+  constexpr float kOff = BITS == 4 ? A::kMagic : 17.0f * A::kMagic;
+  constexpr int kRowsOut = GATE ? 64 : 128;
+
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int KC = a.KC;
+  const int tok_stride_w = KC * 32 + 4;  // words per token row of sx (bank offset 4)
+  uint32_t* sx = reinterpret_cast<uint32_t*>(smem);
+  float* sxs = reinterpret_cast<float*>(sx + TOK * tok_stride_w);          // [KC][16]
+  float2* ssb = reinterpret_cast<float2*>(sxs + KC * kTokMax);             // [128][sb_stride]
+  float* sacc = reinterpret_cast<float*>(ssb + kSlots * a.sb_stride);      // [16][132]
+  constexpr int kAccStride = kSlots + 4;
+  __shared__ int s_last;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = lane >> 2, c = lane & 3;
+  const int nb = blockIdx.x, split = blockIdx.y, z = blockIdx.z;
+  const int g0 = split * KC;
+  const int ng = min(KC, a.G - g0);
+  const int m0 = z * kTokMax;
+  const int mc = min(kTokMax, a.M - m0);
+  const int N = a.N;
+  const int wpr = a.K / 64 * WPG;  // words per weight row
+
+  // ---- the four weight rows of this thread: q = tile * 2 + half --------------------
+  const uint32_t* rowp[4];
+  int slot[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int t = q >> 1, h = q & 1;
+    int n;
+    const uint32_t* base;
+    if constexpr (GATE) {
+      slot[q] = t * 64 + warp * 16 + h * 8 + r;
+      n = nb * 64 + warp * 16 + h * 8 + r;
+      base = t == 0 ? a.w : a.uw;
+    } else {
+      slot[q] = warp * 32 + t * 16 + h * 8 + r;
+      n = nb * 128 + slot[q];
+      base = a.w;
+    }
+    n = min(n, N - 1);
+    rowp[q] = base + (size_t)n * wpr + (size_t)g0 * WPG + c * WPT;
+  }
+
+  // ---- prefetch the first PF groups ------------------------------------------------
+  uint32_t st[PF][4][WPT];
+#pragma unroll
+  for (int s = 0; s < PF; ++s)
+    if (s < ng)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) load_words<BITS>(st[s][q], rowp[q] + s * WPG);
+
+  // ---- stage x (permuted) and sum(x) per group -------------------------------------
+  {
+    const T* x = static_cast<const T*>(a.x);
+    for (int item = tid; item < TOK * KC; item += kThreads) {
+      const int m = item / KC, g = item % KC;
+      float xs = 0.0f;
+      uint32_t* dst = sx + m * tok_stride_w + g * 32;
+      if (m < mc && g < ng) {
+        const uint4* src =
+            reinterpret_cast<const uint4*>(x + (size_t)(m0 + m) * a.K + (size_t)(g0 + g) * 64);
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const uint4 v0 = src[2 * cc], v1 = src[2 * cc + 1];
+          const uint32_t nat[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) xs += A::lo(nat[i]) + A::hi(nat[i]);
+          uint32_t p[8];
+          permute_x<BITS>(p, nat);
+          reinterpret_cast<uint4*>(dst + cc * 8)[0] = make_uint4(p[0], p[1], p[2], p[3]);
+          reinterpret_cast<uint4*>(dst + cc * 8)[1] = make_uint4(p[4], p[5], p[6], p[7]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
+      }
+      sxs[g * kTokMax + m] = xs;
+    }
+  }
+  // ---- stage scale and (bias - offset * scale) as fp32 ------------------------------
+  if constexpr (BITS != 0) {
+    const T* sc = static_cast<const T*>(a.sc);
+    const T* bi = static_cast<const T*>(a.bi);
+    for (int item = tid; item < kSlots * KC; item += kThreads) {
+      const int sl = item / KC, g = item % KC;
+      int n;
+      const T* s_src = sc;
+      const T* b_src = bi;
+      if constexpr (GATE) {
+        n = nb * 64 + (sl & 63);
+        if (sl >= 64) { s_src = static_cast<const T*>(a.usc); b_src = static_cast<const T*>(a.ubi); }
+      } else {
+        n = nb * 128 + sl;
+      }
+      n = min(n, N - 1);
+      float s = 0.0f, b = 0.0f;
+      if (g < ng) {
+        const size_t gi = (size_t)n * a.G + g0 + g;
+        s = A::to_f(s_src[gi]);
+        b = A::to_f(b_src[gi]);
+      }
+      ssb[sl * a.sb_stride + g] = make_float2(s, fmaf(-kOff, s, b));
+    }
+  }
+  __syncthreads();
+
+  // ---- main loop over this CTA's groups --------------------------------------------
+  float acc[2][NT][4];
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[t][nt][i] = 0.0f;
+
+  for (int gb = 0; gb < ng; gb += PF) {
+#pragma unroll
+    for (int s = 0; s < PF; ++s) {
+      const int g = gb + s;
+      if (g < ng) {
+        uint32_t B[NT][8];
+        float2 xsv[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const uint4* src = reinterpret_cast<const uint4*>(sx + (nt * 8 + r) * tok_stride_w + g * 32 + c * 8);
+          const uint4 v0 = src[0], v1 = src[1];
+          B[nt][0] = v0.x; B[nt][1] = v0.y; B[nt][2] = v0.z; B[nt][3] = v0.w;
+          B[nt][4] = v1.x; B[nt][5] = v1.y; B[nt][6] = v1.z; B[nt][7] = v1.w;
+          xsv[nt] = *reinterpret_cast<const float2*>(sxs + g * kTokMax + nt * 8 + 2 * c);
+        }
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const uint32_t* w0 = st[s][2 * t];      // row r of tile t
+          const uint32_t* w1 = st[s][2 * t + 1];  // row r + 8 of tile t
+          if constexpr (BITS == 0) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t af[4] = {w0[2 * j], w1[2 * j], w0[2 * j + 1], w1[2 * j + 1]};
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) mma16816<T>(acc[t][nt], af, B[nt][2 * j], B[nt][2 * j + 1]);
+            }
+          } else {
+            float d[NT][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int i = 0; i < 4; ++i) d[nt][i] = 0.0f;
+            if constexpr (BITS == 4) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int sh = (j & 1) * 8;
+                const uint32_t u0 = w0[j >> 1], u1 = w1[j >> 1];
+                const uint32_t af[4] = {and_or(u0 >> sh, kMask, kMag), and_or(u1 >> sh, kMask, kMag),
+                                        and_or(u0 >> (sh + 4), kMask, kMag), and_or(u1 >> (sh + 4), kMask, kMag)};
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) mma16816<T>(d[nt], af, B[nt][2 * j], B[nt][2 * j + 1]);
+              }
+            } else {
+              float dh[NT][4];
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) dh[nt][i] = 0.0f;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t u0 = w0[j], u1 = w1[j];
+                const uint32_t lo[4] = {and_or(u0, kMask, kMag), and_or(u1, kMask, kMag),
+                                        and_or(u0 >> 8, kMask, kMag), and_or(u1 >> 8, kMask, kMag)};
+                const uint32_t hi[4] = {and_or(u0 >> 4, kMask, kMag), and_or(u1 >> 4, kMask, kMag),
+                                        and_or(u0 >> 12, kMask, kMag), and_or(u1 >> 12, kMask, kMag)};
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                  mma16816<T>(d[nt], lo, B[nt][2 * j], B[nt][2 * j + 1]);
+                  mma16816<T>(dh[nt], hi, B[nt][2 * j], B[nt][2 * j + 1]);
+                }
+              }
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) d[nt][i] = fmaf(16.0f, dh[nt][i], d[nt][i]);
+            }
+            const float2 sb0 = ssb[slot[2 * t] * a.sb_stride + g];
+            const float2 sb1 = ssb[slot[2 * t + 1] * a.sb_stride + g];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              acc[t][nt][0] = fmaf(sb0.x, d[nt][0], fmaf(sb0.y, xsv[nt].x, acc[t][nt][0]));
+              acc[t][nt][1] = fmaf(sb0.x, d[nt][1], fmaf(sb0.y, xsv[nt].y, acc[t][nt][1]));
+              acc[t][nt][2] = fmaf(sb1.x, d[nt][2], fmaf(sb1.y, xsv[nt].x, acc[t][nt][2]));
+              acc[t][nt][3] = fmaf(sb1.x, d[nt][3], fmaf(sb1.y, xsv[nt].y, acc[t][nt][3]));
+            }
+          }
+        }
+        if (g + PF < ng)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) load_words<BITS>(st[s][q], rowp[q] + (g + PF) * WPG);
+      }
+    }
+  }
+
+  // ---- CTA tile -> shared memory [token][slot] ---------------------------------------
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int tk = nt * 8 + 2 * c;
+      sacc[tk * kAccStride + slot[2 * t]] = acc[t][nt][0];
+      sacc[(tk + 1) * kAccStride + slot[2 * t]] = acc[t][nt][1];
+      sacc[tk * kAccStride + slot[2 * t + 1]] = acc[t][nt][2];
+      sacc[(tk + 1) * kAccStride + slot[2 * t + 1]] = acc[t][nt][3];
+    }
+  __syncthreads();
+
+  // ---- split-K: publish the partial tile; the last CTA of the row block adds them ----
+  if (a.S > 1) {
+    const int wd = a.rowblocks * kSlots;
+    float* part = a.partial + (size_t)(z * a.S + split) * kTokMax * wd + (size_t)nb * kSlots;
+    for (int e = tid; e < mc * kSlots; e += kThreads) {
+      const int m = e / kSlots, sl = e % kSlots;
+      part[(size_t)m * wd + sl] = sacc[m * kAccStride + sl];
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      int* ctr = a.counters + z * a.rowblocks + nb;
+      const int prev = atomicAdd(ctr, 1);
+      const int last = prev == a.S - 1;
+      if (last) *ctr = 0;  // every CTA of this row block has arrived: reset for the next call
+      s_last = last;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* base = a.partial + (size_t)z * a.S * kTokMax * wd + (size_t)nb * kSlots;
+    for (int e = tid; e < mc * kSlots; e += kThreads) {
+      const int m = e / kSlots, sl = e % kSlots;
+      float v = 0.0f;
+      for (int sp = 0; sp < a.S; ++sp) v += __ldcg(base + ((size_t)sp * kTokMax + m) * wd + sl);
+      sacc[m * kAccStride + sl] = v;
+    }
+    __syncthreads();
+  }
+
+  // ---- epilogue: GATE -> bias -> residual, one rounding --------------------------------
+  const T* bias = static_cast<const T*>(a.bias);
+  const T* res = static_cast<const T*>(a.res);
+  T* out = static_cast<T*>(a.out);
+  for (int e = tid; e < mc * kRowsOut; e += kThreads) {
+    const int m = e / kRowsOut, j = e % kRowsOut;
+    const int n = nb * kRowsOut + j;
+    if (n >= N) continue;
+    float v = sacc[m * kAccStride + j];
+    if constexpr (GATE) {
+      const float u = sacc[m * kAccStride + 64 + j];
+      v = v / (1.0f + expf(-v)) * u;
+    }
+    const size_t o = (size_t)(m0 + m) * N + n;
+    if (a.has_bias) v += A::to_f(bias[n]);
+    if (a.has_res) v += A::to_f(res[o]);
+    out[o] = A::from_f(v);
+  }
+}
+
+size_t smem_bytes(int nt, int kc, int sb_stride) {
+  const size_t tok = nt * 8;
+  return tok * (kc * 32 + 4) * 4 + (size_t)kc * kTokMax * 4 + (size_t)kSlots * sb_stride * 8 +
+         (size_t)kTokMax * (kSlots + 4) * 4;
+}
+
+int sb_stride_for(int kc) {
+  int s = kc + 1;
+  if ((2 * s) % 32 == 0) s += 1;
+  return s;
+}
+
+template <typename T, int BITS, int NT, bool GATE>
+int launch_t(const Args& a, dim3 grid, size_t smem, cudaStream_t stream) {
+  auto k = qgemm_kernel<T, BITS, NT, GATE>;
+  // One attribute call per instantiation and device.
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  VELLA_CUDA_TRY(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    VELLA_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)smem_bytes(2, kKCMax, sb_stride_for(kKCMax))));
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  k<<<grid, kThreads, smem, stream>>>(a);
+  VELLA_CUDA_TRY(cudaGetLastError());
+  return VELLA_OK;
+}
+
+template <typename T, int BITS>
+int dispatch_nt(const Args& a, bool gate, int nt, dim3 grid, size_t smem, cudaStream_t s) {
+  if (gate) return nt == 1 ? launch_t<T, BITS, 1, true>(a, grid, smem, s) : launch_t<T, BITS, 2, true>(a, grid, smem, s);
+  return nt == 1 ? launch_t<T, BITS, 1, false>(a, grid, smem, s) : launch_t<T, BITS, 2, false>(a, grid, smem, s);
+}
+
+}  // namespace
+
+bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* p) {
+  if (d.m < 0 || d.n < 0 || d.k <= 0) return false;
+  if (d.bits != 0 && d.bits != 4 && d.bits != 8) return false;
+  if (d.bits != 0 && d.group_size != 64) return false;
+  if (d.k % 64 != 0) return false;
+  if (d.dtype != VELLA_BF16 && d.dtype != VELLA_F16) return false;
+  if (d.epilogue < VELLA_EPI_NONE || d.epilogue > VELLA_EPI_SILU_GATE) return false;
+  if (d.m > 256) return false;
+  const bool gate = d.epilogue == VELLA_EPI_SILU_GATE;
+  p->rows_out = gate ? 64 : 128;
+  p->rowblocks = (d.n + p->rows_out - 1) / p->rows_out;
+  const int G = d.k / 64;
+  // Enough CTAs for ~4 per SM on a 148-SM B200; depends on (N, K, gate) only.
+  const int target = 4 * 148;
+  int want = (target + std::max(p->rowblocks, 1) - 1) / std::max(p->rowblocks, 1);
+  want = std::max(1, std::min(want, G));
+  int kc = (G + want - 1) / want;
+  kc = std::max(kc, std::min(G, 4));
+  kc = std::min(kc, kKCMax);
+  p->kc = kc;
+  p->splits = (G + kc - 1) / kc;
+  p->zchunks = std::max(1, (d.m + kTokMax - 1) / kTokMax);
+  if (p->splits > 1) {
+    const size_t part = (size_t)p->zchunks * p->splits * kTokMax * (size_t)p->rowblocks * kSlots * sizeof(float);
+    const size_t ctr = (size_t)p->zchunks * p->rowblocks * sizeof(int);
+    p->workspace = ((ctr + 255) / 256) * 256 + part;
+  } else {
+    p->workspace = 0;
+  }
+  return true;
+}
+
+int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& p, const void* x, const void* w,
+                 const void* scales, const void* biases, const void* up_w, const void* up_scales,
+                 const void* up_biases, const void* bias, const void* residual, void* out, void* ws,
+                 cudaStream_t stream) {
+  if (d.m == 0 || d.n == 0) return VELLA_OK;
+  Args a{};
+  a.x = x; a.w = static_cast<const uint32_t*>(w); a.sc = scales; a.bi = biases;
+  a.uw = static_cast<const uint32_t*>(up_w); a.usc = up_scales; a.ubi = up_biases;
+  a.bias = bias; a.res = residual; a.out = out;
+  a.M = d.m; a.N = d.n; a.K = d.k; a.G = d.k / 64; a.KC = p.kc; a.S = p.splits; a.rowblocks = p.rowblocks;
+  a.has_bias = d.epilogue == VELLA_EPI_BIAS || d.epilogue == VELLA_EPI_BIAS_RESIDUAL;
+  a.has_res = d.epilogue == VELLA_EPI_RESIDUAL || d.epilogue == VELLA_EPI_BIAS_RESIDUAL;
+  a.sb_stride = sb_stride_for(p.kc);
+  if (p.splits > 1) {
+    const size_t ctr = (size_t)p.zchunks * p.rowblocks * sizeof(int);
+    a.counters = static_cast<int*>(ws);
+    a.partial = reinterpret_cast<float*>(static_cast<char*>(ws) + ((ctr + 255) / 256) * 256);
+  }
+  const bool gate = d.epilogue == VELLA_EPI_SILU_GATE;
+  const int nt = d.m <= 8 ? 1 : 2;
+  const size_t smem = smem_bytes(nt, p.kc, a.sb_stride);
+  const dim3 grid(p.rowblocks, p.splits, p.zchunks);
+  if (d.dtype == VELLA_BF16) {
+    switch (d.bits) {
+      case 4: return dispatch_nt<__nv_bfloat16, 4>(a, gate, nt, grid, smem, stream);
+      case 8: return dispatch_nt<__nv_bfloat16, 8>(a, gate, nt, grid, smem, stream);
+      default: return dispatch_nt<__nv_bfloat16, 0>(a, gate, nt, grid, smem, stream);
+    }
+  }
+  switch (d.bits) {
+    case 4: return dispatch_nt<__half, 4>(a, gate, nt, grid, smem, stream);
+    case 8: return dispatch_nt<__half, 8>(a, gate, nt, grid, smem, stream);
+    default: return dispatch_nt<__half, 0>(a, gate, nt, grid, smem, stream);
+  }
+}
+
+}  // namespace vella
