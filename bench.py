@@ -150,17 +150,20 @@ def run_gemm(args, rank, world):
                     out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
                     plans.append((bits, n, k, m, ws, x, out))
     torch.cuda.synchronize()
+    # one workspace for every graph (they replay one after another on one stream)
+    ws_bytes = max(S.workspace_size(m, n, k, torch.bfloat16, bits) for bits, n, k, m, *_ in plans)
+    workspace = torch.zeros(max(ws_bytes, 256) // 4 + 64, dtype=torch.int32, device=dev)
     # one CUDA graph per (bits, shape, M): `reps` calls cycling through the weight copies
     reps = 8
     graphs = []
     for bits, n, k, m, ws, x, out in plans:
         with torch.cuda.stream(stream):
-            S.matmul(x, ws[0], out=out)  # workspace allocation outside capture
+            S.matmul(x, ws[0], out=out, workspace=workspace)
         torch.cuda.synchronize()
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gr, stream=stream):
             for i in range(reps):
-                S.matmul(x, ws[i % len(ws)], out=out)
+                S.matmul(x, ws[i % len(ws)], out=out, workspace=workspace)
         graphs.append(gr)
     torch.cuda.synchronize()
 

@@ -86,10 +86,13 @@ VELLA_API size_t vella_qgemm_workspace_size(const vella_qgemm_desc* desc);
 /*
  * Runs the GEMM.  `up_w/up_scales/up_biases` are read only for VELLA_EPI_SILU_GATE,
  * `bias` only for the bias epilogues, `residual` only for the residual epilogues.
- * `workspace`: device memory of at least vella_qgemm_workspace_size bytes, zero-filled
- * before its first use (every call leaves it zero-filled again), used by one stream at a
- * time.  NULL selects a per-device workspace owned by the library (allocated on the first
- * call that needs it, so make that first call outside CUDA graph capture).
+ * `workspace`: device memory of at least vella_qgemm_workspace_size bytes, 256-byte
+ * aligned, zero-filled before its first use (every completed call leaves its counter words
+ * zero again), used by one stream at a time.  NULL selects a per-device workspace owned
+ * by the library: it is allocated or grown by the first call that needs more, so that
+ * call must not be inside CUDA graph capture; a grown workspace keeps the old buffer
+ * alive, so graphs captured earlier stay valid, but they all share one buffer and must
+ * not run concurrently.
  * The reduction order of a row depends only on (N, K, bits): a row of a batched call is
  * bit-identical to the same row computed alone.
  */

@@ -35,6 +35,9 @@ namespace {
 struct DeviceWorkspace {
   void* ptr = nullptr;
   size_t bytes = 0;
+  // Buffers replaced by a larger one.  They are never freed: a CUDA graph captured with an
+  // earlier call still holds their address and must stay valid when it is replayed.
+  std::vector<void*> retired;
 };
 std::mutex g_ws_mu;
 std::vector<DeviceWorkspace> g_ws;
@@ -50,9 +53,7 @@ int device_workspace(size_t bytes, void** out) {
     size_t want = std::max(bytes, ws.bytes * 2);
     want = std::max<size_t>(want, 1 << 20);
     if (ws.ptr) {
-      // Work queued on the old buffer must finish before it is released.
-      VELLA_CUDA_TRY(cudaDeviceSynchronize());
-      VELLA_CUDA_TRY(cudaFree(ws.ptr));
+      ws.retired.push_back(ws.ptr);
       ws.ptr = nullptr;
       ws.bytes = 0;
     }

@@ -1,0 +1,548 @@
+// Transformer decode-step kernels of the draft-and-verify path (Qwen3-style dense GQA
+// layer: RMSNorm, RoPE, causal attention over a preallocated KV cache, SwiGLU through the
+// GEMM's SiLU-gate epilogue).
+//
+// Reference: Worker/Sources/MLXAudioSTT/Qwen3ASR/Qwen3ASRTextDecoder.swift:17-214 (layer
+// recipe, RoPE with the pre-update cache offset :76-82), NemotronTranscribeDecoder.swift:
+// 96-117 (KV cache: append, trim) and :382-390 (causal attention when more than one query).
+//
+// Every kernel computes each row (token position) with an instruction sequence that does
+// not depend on the other rows of the launch: the attention splits keys at absolute
+// positions (multiples of kAttnChunk) and combines the chunks in order, masked keys add
+// exact zeros.  So a verify pass over K+1 positions gives bit-identical hidden states,
+// logits and tokens to K+1 single-token greedy steps.
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <cstdint>
+
+#include "common.cuh"
+#include "internal.h"
+#include "layers.cuh"
+
+namespace vella {
+namespace {
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = Act<T>::lo(w[i]);
+    v[2 * i + 1] = Act<T>::hi(w[i]);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// embedding rows: position < P reads the caller's input embeddings, else the token table
+// ---------------------------------------------------------------------------------------
+template <typename T>
+__global__ void embed_rows_kernel(T* __restrict__ h, const T* __restrict__ table, const T* __restrict__ prefix,
+                                  const int* __restrict__ tok, PosRef pr, int P, int d, int vocab, int max_seq,
+                                  int* err) {
+  const int m = blockIdx.x;
+  const int pos = *pr.base + pr.off + m;
+  const T* src;
+  if (pos >= 0 && pos < P) {
+    src = prefix + (size_t)pos * d;
+  } else {
+    int t = (pos >= 0 && pos < max_seq) ? tok[pos] : -1;
+    if (t < 0 || t >= vocab) {
+      if (threadIdx.x == 0) atomicOr(err, 1);
+      t = 0;
+    }
+    src = table + (size_t)t * d;
+  }
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+  uint4* d4 = reinterpret_cast<uint4*>(h + (size_t)m * d);
+  for (int i = threadIdx.x; i < d / 8; i += blockDim.x) d4[i] = s4[i];
+}
+
+// ---------------------------------------------------------------------------------------
+// RMSNorm: y = w * T(x * rsqrt(mean(x^2) + eps)), sums in fp32 in a fixed order
+// ---------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(T* __restrict__ out, const T* __restrict__ x,
+                                                      const T* __restrict__ w, int d, float eps) {
+  using A = Act<T>;
+  const int row = blockIdx.x;
+  const T* xr = x + (size_t)row * d;
+  float ss = 0.0f;
+  for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
+    float v[8];
+    load8(xr + i, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+  }
+  __shared__ float red[32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float r = 1.0f / sqrtf(red[0] / (float)d + eps);
+  T* o = out + (size_t)row * d;
+  for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
+    float v[8], g[8];
+    load8(xr + i, v);
+    load8(w + i, g);
+    uint32_t pk[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a0 = g[2 * j] * A::to_f(A::from_f(v[2 * j] * r));
+      const float a1 = g[2 * j + 1] * A::to_f(A::from_f(v[2 * j + 1] * r));
+      const T t0 = A::from_f(a0), t1 = A::from_f(a1);
+      pk[j] = (uint32_t)reinterpret_cast<const unsigned short&>(t0) |
+              ((uint32_t)reinterpret_cast<const unsigned short&>(t1) << 16);
+    }
+    *reinterpret_cast<uint4*>(o + i) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// RoPE (half rotation, table of fp32 cos/sin per position) + KV append; optional per-head
+// q/k RMSNorm before the rotation (Qwen3 q_norm / k_norm).
+// ---------------------------------------------------------------------------------------
+template <typename T>
+__global__ void rope_append_kernel(const T* __restrict__ qkv, T* __restrict__ q_out, T* __restrict__ kc,
+                                   T* __restrict__ vc, const float2* __restrict__ cs, const T* __restrict__ qn,
+                                   const T* __restrict__ kn, float eps, PosRef pr, int H, int KV, int hd,
+                                   int max_seq, int* err) {
+  using A = Act<T>;
+  const int m = blockIdx.x, hidx = blockIdx.y, i = threadIdx.x;
+  const int half = hd / 2;
+  const int pos = *pr.base + pr.off + m;
+  if (pos < 0 || pos >= max_seq) {
+    if (i == 0) atomicOr(err, 2);
+    return;
+  }
+  const T* row = qkv + (size_t)m * (H + 2 * KV) * hd;
+  const bool is_q = hidx < H;
+  const T* src = row + (size_t)hidx * hd;  // q heads, then k heads
+  float x1 = A::to_f(src[i]), x2 = A::to_f(src[i + half]);
+  const T* nw = is_q ? qn : kn;
+  if (nw != nullptr) {
+    __shared__ float red[32];
+    float ss = warp_sum(fmaf(x1, x1, x2 * x2));
+    if ((i & 31) == 0) red[i >> 5] = ss;
+    __syncthreads();
+    float t = 0.0f;
+    for (int w = 0; w < (half + 31) / 32; ++w) t += red[w];
+    const float r = 1.0f / sqrtf(t / (float)hd + eps);
+    x1 = A::to_f(A::from_f(A::to_f(nw[i]) * A::to_f(A::from_f(x1 * r))));
+    x2 = A::to_f(A::from_f(A::to_f(nw[i + half]) * A::to_f(A::from_f(x2 * r))));
+  }
+  const float2 c = cs[(size_t)pos * half + i];
+  const float y1 = x1 * c.x - x2 * c.y;
+  const float y2 = x1 * c.y + x2 * c.x;
+  if (is_q) {
+    T* o = q_out + ((size_t)m * H + hidx) * hd;
+    o[i] = A::from_f(y1);
+    o[i + half] = A::from_f(y2);
+  } else {
+    const int kv = hidx - H;
+    T* ko = kc + ((size_t)kv * max_seq + pos) * hd;
+    ko[i] = A::from_f(y1);
+    ko[i + half] = A::from_f(y2);
+    const T* vs = row + (size_t)(H + KV + kv) * hd;
+    T* vo = vc + ((size_t)kv * max_seq + pos) * hd;
+    vo[i] = vs[i];
+    vo[i + half] = vs[i + half];
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Decode attention (flash-decoding): CTA (kv head, key chunk, query block).  Scores and
+// probabilities in fp32; the last CTA of a (kv head, query block) combines the chunks in
+// chunk order.  Query at position p sees keys 0..p.
+// ---------------------------------------------------------------------------------------
+struct AttnArgs {
+  const void* q;
+  const void* kc;
+  const void* vc;
+  void* out;
+  float* part;
+  float2* ml;
+  int* ctr;
+  PosRef pr;
+  int M, H, KV, S, nch, nqb;
+  float scale;
+};
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(256) attn_kernel(const AttnArgs a) {
+  constexpr int C = kAttnChunk;
+  constexpr int QB = kAttnQBlock;
+  constexpr int KS = HD + 4;  // padded fp32 row stride of K/V/Q in shared memory
+  constexpr int PS = C + 4;
+  extern __shared__ __align__(16) float sm[];
+  __shared__ int s_last;
+  const int GQ = a.H / a.KV;
+  const int QRmax = QB * GQ;
+  float* Ks = sm;
+  float* Vs = Ks + C * KS;
+  float* Qs = Vs + C * KS;
+  float* Ps = Qs + QRmax * KS;
+  float2* ML = reinterpret_cast<float2*>(Ps + QRmax * PS);
+
+  const int kvh = blockIdx.x, ch = blockIdx.y, qb = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int pos0 = *a.pr.base + a.pr.off;
+  const int mq0 = qb * QB;
+  const int nq = min(QB, a.M - mq0);
+  const int tmax = pos0 + mq0 + nq;  // keys needed by the last query of this block
+  const int k0 = ch * C;
+  if (k0 >= tmax) return;
+  const int nact = (tmax + C - 1) / C;
+  const int nvalid = min(C, tmax - k0);
+  const int QR = nq * GQ;
+  const T* q = static_cast<const T*>(a.q);
+  const T* kc = static_cast<const T*>(a.kc) + ((size_t)kvh * a.S + k0) * HD;
+  const T* vc = static_cast<const T*>(a.vc) + ((size_t)kvh * a.S + k0) * HD;
+
+  for (int e = tid; e < C * (HD / 8); e += 256) {
+    const int j = e / (HD / 8), d8 = (e % (HD / 8)) * 8;
+    float kv8[8], vv8[8];
+    if (j < nvalid) {
+      load8(kc + (size_t)j * HD + d8, kv8);
+      load8(vc + (size_t)j * HD + d8, vv8);
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) kv8[t] = vv8[t] = 0.0f;
+    }
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      Ks[j * KS + d8 + t] = kv8[t];
+      Vs[j * KS + d8 + t] = vv8[t];
+    }
+  }
+  for (int e = tid; e < QR * (HD / 8); e += 256) {
+    const int qr = e / (HD / 8), d8 = (e % (HD / 8)) * 8;
+    const int mi = qr / GQ, g = qr % GQ;
+    float v8[8];
+    load8(q + ((size_t)(mq0 + mi) * a.H + kvh * GQ + g) * HD + d8, v8);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) Qs[qr * KS + d8 + t] = v8[t];
+  }
+  __syncthreads();
+
+  // ---- scores: warp w takes 4-row blocks, lane j takes keys j and j + 32 -------------
+  for (int rb = warp * 4; rb < QR; rb += 32) {
+    float s[4][2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) s[i][0] = s[i][1] = 0.0f;
+    for (int d = 0; d < HD; d += 4) {
+      const float4 ka = *reinterpret_cast<const float4*>(Ks + lane * KS + d);
+      const float4 kb = *reinterpret_cast<const float4*>(Ks + (lane + 32) * KS + d);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 qv = *reinterpret_cast<const float4*>(Qs + min(rb + i, QR - 1) * KS + d);
+        s[i][0] = fmaf(qv.x, ka.x, s[i][0]); s[i][0] = fmaf(qv.y, ka.y, s[i][0]);
+        s[i][0] = fmaf(qv.z, ka.z, s[i][0]); s[i][0] = fmaf(qv.w, ka.w, s[i][0]);
+        s[i][1] = fmaf(qv.x, kb.x, s[i][1]); s[i][1] = fmaf(qv.y, kb.y, s[i][1]);
+        s[i][1] = fmaf(qv.z, kb.z, s[i][1]); s[i][1] = fmaf(qv.w, kb.w, s[i][1]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int qr = rb + i;
+      if (qr < QR) {
+        const int pq = pos0 + mq0 + qr / GQ;
+        Ps[qr * PS + lane] = (k0 + lane <= pq) ? s[i][0] * a.scale : -INFINITY;
+        Ps[qr * PS + lane + 32] = (k0 + lane + 32 <= pq) ? s[i][1] * a.scale : -INFINITY;
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- softmax within the chunk: warp per row ----------------------------------------
+  for (int qr = warp; qr < QR; qr += 8) {
+    const float v0 = Ps[qr * PS + lane], v1 = Ps[qr * PS + lane + 32];
+    const float mx = warp_max(fmaxf(v0, v1));
+    float p0 = 0.0f, p1 = 0.0f, l = 0.0f;
+    if (mx != -INFINITY) {
+      p0 = v0 == -INFINITY ? 0.0f : expf(v0 - mx);
+      p1 = v1 == -INFINITY ? 0.0f : expf(v1 - mx);
+      l = warp_sum(p0 + p1);
+    }
+    Ps[qr * PS + lane] = p0;
+    Ps[qr * PS + lane + 32] = p1;
+    if (lane == 0) ML[qr] = make_float2(mx, l);
+  }
+  __syncthreads();
+
+  // ---- P.V: thread (d, row set), 4 rows at a time ------------------------------------
+  constexpr int RS = 256 / HD;
+  const int d = tid % HD, rset = tid / HD;
+  const size_t cta = ((size_t)(kvh * a.nqb + qb) * a.nch + ch) * QRmax;
+  for (int rb = rset * 4; rb < QR; rb += RS * 4) {
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int j = 0; j < C; j += 4) {
+      const float v0 = Vs[j * KS + d], v1 = Vs[(j + 1) * KS + d], v2 = Vs[(j + 2) * KS + d],
+                  v3 = Vs[(j + 3) * KS + d];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 p = *reinterpret_cast<const float4*>(Ps + min(rb + i, QR - 1) * PS + j);
+        acc[i] = fmaf(p.x, v0, acc[i]); acc[i] = fmaf(p.y, v1, acc[i]);
+        acc[i] = fmaf(p.z, v2, acc[i]); acc[i] = fmaf(p.w, v3, acc[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (rb + i < QR) a.part[(cta + rb + i) * HD + d] = acc[i];
+  }
+  for (int qr = tid; qr < QR; qr += 256) a.ml[cta + qr] = ML[qr];
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    int* c = a.ctr + kvh * a.nqb + qb;
+    const int prev = atomicAdd(c, 1);
+    const int last = prev == nact - 1;
+    if (last) *c = 0;
+    s_last = last;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+
+  // ---- combine the chunks of every query in chunk order --------------------------------
+  T* out = static_cast<T*>(a.out);
+  const size_t base = (size_t)(kvh * a.nqb + qb) * a.nch * QRmax;
+  for (int qr = rset; qr < QR; qr += RS) {
+    const int pq = pos0 + mq0 + qr / GQ;
+    const int nch_q = pq / C + 1;
+    float mx = -INFINITY;
+    for (int c = 0; c < nch_q; ++c) mx = fmaxf(mx, __ldcg(&a.ml[base + (size_t)c * QRmax + qr].x));
+    float o = 0.0f, l = 0.0f;
+    for (int c = 0; c < nch_q; ++c) {
+      const float2 ml = __ldcg(&a.ml[base + (size_t)c * QRmax + qr]);
+      const float w = expf(ml.x - mx);
+      o = fmaf(w, __ldcg(&a.part[(base + (size_t)c * QRmax + qr) * HD + d]), o);
+      l = fmaf(w, ml.y, l);
+    }
+    const int mi = qr / GQ, g = qr % GQ;
+    out[((size_t)(mq0 + mi) * a.H + kvh * GQ + g) * HD + d] = Act<T>::from_f(o / l);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// argmax per row with the lowest index on ties; NaN/Inf anywhere sets the flag
+// ---------------------------------------------------------------------------------------
+constexpr int kArgBlocks = 32;
+
+__device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
+  if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logits, int V, size_t ld,
+                                                     int* __restrict__ ys, float2* part, int* ctr, int* nonfinite) {
+  using A = Act<T>;
+  const int m = blockIdx.x, b = blockIdx.y;
+  const int per = ((V + kArgBlocks - 1) / kArgBlocks + 7) / 8 * 8;
+  const int lo = b * per, hi = min(V, lo + per);
+  const T* row = logits + (size_t)m * ld;
+  float bv = -INFINITY;
+  int bi = INT32_MAX;
+  bool bad = false;
+  const bool vec = (ld % 8 == 0);
+  for (int i = lo + threadIdx.x * 8; i < hi; i += 256 * 8) {
+    if (vec && i + 8 <= hi) {
+      float v[8];
+      load8(row + i, v);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        if (!isfinite(v[t])) { bad = true; if (isnan(v[t])) continue; }
+        better(bv, bi, v[t], i + t);
+      }
+    } else {
+      for (int t = i; t < min(i + 8, hi); ++t) {
+        const float v = A::to_f(row[t]);
+        if (!isfinite(v)) { bad = true; if (isnan(v)) continue; }
+        better(bv, bi, v, t);
+      }
+    }
+  }
+  if (bad) atomicOr(nonfinite, 1);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    better(bv, bi, ov, oi);
+  }
+  __shared__ float sv[8];
+  __shared__ int si[8];
+  __shared__ int s_last;
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; ++w) better(bv, bi, sv[w], si[w]);
+    part[m * kArgBlocks + b] = make_float2(bv, __int_as_float(bi));
+    __threadfence();
+    const int prev = atomicAdd(ctr + m, 1);
+    s_last = prev == kArgBlocks - 1;
+    if (s_last) {
+      ctr[m] = 0;
+      __threadfence();
+      float fv = -INFINITY;
+      int fi = INT32_MAX;
+      for (int k = 0; k < kArgBlocks; ++k) {
+        const float2 p = __ldcg(part + m * kArgBlocks + k);
+        better(fv, fi, p.x, __float_as_int(p.y));
+      }
+      ys[m] = fi == INT32_MAX ? 0 : fi;
+    }
+  }
+}
+
+template <typename T>
+size_t attn_smem(int gq) {
+  const int hd = sizeof(T) == 2 ? 0 : 0;
+  (void)hd;
+  return 0;
+}
+
+size_t attn_smem_bytes(int hd, int gq) {
+  const size_t ks = hd + 4, ps = kAttnChunk + 4, qr = (size_t)kAttnQBlock * gq;
+  return (2 * kAttnChunk * ks + qr * ks + qr * ps) * sizeof(float) + qr * sizeof(float2);
+}
+
+template <typename T, int HD>
+int launch_attn_t(const AttnArgs& a, int gq, cudaStream_t s) {
+  const size_t smem = attn_smem_bytes(HD, gq);
+  static int configured[64] = {0};
+  int dev = 0;
+  VELLA_CUDA_TRY(cudaGetDevice(&dev));
+  if (!configured[dev & 63]) {
+    VELLA_CUDA_TRY(cudaFuncSetAttribute(attn_kernel<T, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)attn_smem_bytes(HD, 8)));
+    configured[dev & 63] = 1;
+  }
+  attn_kernel<T, HD><<<dim3(a.KV, a.nch, a.nqb), 256, smem, s>>>(a);
+  VELLA_CUDA_TRY(cudaGetLastError());
+  return VELLA_OK;
+}
+
+}  // namespace
+
+size_t attn_scratch_bytes(int kv, int gq, int hd, int max_rows, int max_seq) {
+  const size_t nqb = (max_rows + kAttnQBlock - 1) / kAttnQBlock;
+  const size_t nch = (max_seq + kAttnChunk - 1) / kAttnChunk;
+  const size_t qr = (size_t)kAttnQBlock * gq;
+  const size_t part = (size_t)kv * nqb * nch * qr * hd * sizeof(float);
+  const size_t ml = (size_t)kv * nqb * nch * qr * sizeof(float2);
+  const size_t ctr = (size_t)kv * nqb * sizeof(int);
+  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+  return up(ctr) + up(ml) + up(part);
+}
+
+void attn_scratch_carve(void* base, int kv, int gq, int hd, int max_rows, int max_seq, AttnScratch* s) {
+  const size_t nqb = (max_rows + kAttnQBlock - 1) / kAttnQBlock;
+  const size_t nch = (max_seq + kAttnChunk - 1) / kAttnChunk;
+  const size_t qr = (size_t)kAttnQBlock * gq;
+  const size_t ml = (size_t)kv * nqb * nch * qr * sizeof(float2);
+  const size_t ctr = (size_t)kv * nqb * sizeof(int);
+  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+  char* p = static_cast<char*>(base);
+  s->counters = reinterpret_cast<int*>(p);
+  s->ml = reinterpret_cast<float2*>(p + up(ctr));
+  s->part = reinterpret_cast<float*>(p + up(ctr) + up(ml));
+}
+
+int launch_embed_rows(int dtype, void* h, const void* table, const void* prefix, const int* tok, PosRef pr,
+                      int rows, int P, int d, int vocab, int max_seq, int* err, cudaStream_t s) {
+  if (rows <= 0) return VELLA_OK;
+  if (dtype == VELLA_BF16)
+    embed_rows_kernel<__nv_bfloat16><<<rows, 256, 0, s>>>(
+        static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(table),
+        static_cast<const __nv_bfloat16*>(prefix), tok, pr, P, d, vocab, max_seq, err);
+  else
+    embed_rows_kernel<__half><<<rows, 256, 0, s>>>(static_cast<__half*>(h), static_cast<const __half*>(table),
+                                                   static_cast<const __half*>(prefix), tok, pr, P, d, vocab,
+                                                   max_seq, err);
+  VELLA_CUDA_TRY(cudaGetLastError());
+  return VELLA_OK;
+}
+
+int launch_rmsnorm(int dtype, void* out, const void* x, const void* w, int rows, int d, float eps,
+                   cudaStream_t s) {
+  if (rows <= 0) return VELLA_OK;
+  if (dtype == VELLA_BF16)
+    rmsnorm_kernel<__nv_bfloat16><<<rows, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out),
+                                                       static_cast<const __nv_bfloat16*>(x),
+                                                       static_cast<const __nv_bfloat16*>(w), d, eps);
+  else
+    rmsnorm_kernel<__half><<<rows, 256, 0, s>>>(static_cast<__half*>(out), static_cast<const __half*>(x),
+                                                static_cast<const __half*>(w), d, eps);
+  VELLA_CUDA_TRY(cudaGetLastError());
+  return VELLA_OK;
+}
+
+int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* vc, const float2* cs,
+                       const void* qn, const void* kn, float eps, PosRef pr, int rows, int H, int KV, int hd,
+                       int max_seq, int* err, cudaStream_t s) {
+  if (rows <= 0) return VELLA_OK;
+  const dim3 grid(rows, H + KV);
+  if (dtype == VELLA_BF16)
+    rope_append_kernel<__nv_bfloat16><<<grid, hd / 2, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(q_out),
+        static_cast<__nv_bfloat16*>(kc), static_cast<__nv_bfloat16*>(vc), cs,
+        static_cast<const __nv_bfloat16*>(qn), static_cast<const __nv_bfloat16*>(kn), eps, pr, H, KV, hd, max_seq,
+        err);
+  else
+    rope_append_kernel<__half><<<grid, hd / 2, 0, s>>>(
+        static_cast<const __half*>(qkv), static_cast<__half*>(q_out), static_cast<__half*>(kc),
+        static_cast<__half*>(vc), cs, static_cast<const __half*>(qn), static_cast<const __half*>(kn), eps, pr, H,
+        KV, hd, max_seq, err);
+  VELLA_CUDA_TRY(cudaGetLastError());
+  return VELLA_OK;
+}
+
+int launch_attention(int dtype, const void* q, const void* kc, const void* vc, void* out, const AttnScratch& sc,
+                     PosRef pr, int rows, int H, int KV, int hd, int max_seq, float scale, cudaStream_t s) {
+  if (rows <= 0) return VELLA_OK;
+  AttnArgs a{};
+  a.q = q; a.kc = kc; a.vc = vc; a.out = out;
+  a.part = sc.part; a.ml = sc.ml; a.ctr = sc.counters;
+  a.pr = pr; a.M = rows; a.H = H; a.KV = KV; a.S = max_seq;
+  a.nch = (max_seq + kAttnChunk - 1) / kAttnChunk;
+  a.nqb = (rows + kAttnQBlock - 1) / kAttnQBlock;
+  a.scale = scale;
+  const int gq = H / KV;
+  if (gq * KV != H || gq > 8) return fail(VELLA_E_UNSUPPORTED, "attention: H/KV = %d/%d not supported", H, KV);
+  if (dtype == VELLA_BF16) {
+    if (hd == 128) return launch_attn_t<__nv_bfloat16, 128>(a, gq, s);
+    if (hd == 64) return launch_attn_t<__nv_bfloat16, 64>(a, gq, s);
+  } else {
+    if (hd == 128) return launch_attn_t<__half, 128>(a, gq, s);
+    if (hd == 64) return launch_attn_t<__half, 64>(a, gq, s);
+  }
+  return fail(VELLA_E_UNSUPPORTED, "attention: head_dim %d not supported", hd);
+}
+
+size_t argmax_scratch_bytes(int max_rows) {
+  return (size_t)max_rows * kArgBlocks * sizeof(float2) + 256 + (size_t)max_rows * sizeof(int);
+}
+
+int launch_argmax(int dtype, const void* logits, int rows, int V, size_t ld, int* ys, void* scratch,
+                  int* nonfinite, cudaStream_t s) {
+  if (rows <= 0) return VELLA_OK;
+  // layout: counters [rows] first (256-byte slot... sized by the caller), then partials
+  int* ctr = static_cast<int*>(scratch);
+  float2* part = reinterpret_cast<float2*>(static_cast<char*>(scratch) + 256 + ((size_t)rows * sizeof(int) + 255) / 256 * 256);
+  const dim3 grid(rows, kArgBlocks);
+  if (dtype == VELLA_BF16)
+    argmax_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(logits), V, ld, ys, part,
+                                                      ctr, nonfinite);
+  else
+    argmax_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(logits), V, ld, ys, part, ctr, nonfinite);
+  VELLA_CUDA_TRY(cudaGetLastError());
+  return VELLA_OK;
+}
+
+}  // namespace vella

@@ -12,11 +12,15 @@
 // (word >> s) & 0x000F000F | 0x43004300 turns two 4-bit codes into the bf16 pair
 // (128 + q_a, 128 + q_b) in one LOP3, which is exact; the 128 offset is removed in the
 // per-group scale step, acc += s * D + (b - 128 s) * sum(x), i.e. the reference's product
-// form with D = sum(x * (128 + q)).  8-bit codes are split into low and high nibbles (two
-// MMAs, D = D_lo + 16 D_hi).  Within one MMA the k positions may be permuted freely as
-// long as A and B agree, so each thread's four k slots are the nibbles its one 8/16-byte
-// load delivers, and x is staged in shared memory in the matching permuted order
-// (with the per-group sums sum(x) precomputed), once per CTA.
+// form with D = sum(x * (128 + q)).  sum(x) per group comes from the same MMA with an
+// all-ones A operand.  8-bit codes are split into low and high nibbles (two MMAs,
+// D = D_lo + 16 D_hi).  Within one MMA the k positions may be permuted freely as long as
+// A and B agree, so each thread's k slots are the nibbles its own 8/16-byte load
+// delivers, and x is permuted to match when its fragment is read from shared memory.
+//
+// Pipeline: weights and their scales/biases for the next PF groups are in flight in
+// registers (no shared-memory staging of the weight stream); x for the CTA's K range is
+// copied to shared memory once with cp.async.
 //
 // Work split: a CTA (4 warps) covers 128 output rows (64 with the gate) x KC groups of
 // 64 along K; `splits` CTAs along K write fp32 partial tiles to a workspace and the CTA
@@ -38,9 +42,10 @@ namespace {
 
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kSlots = 128;  // weight rows staged per CTA (gate: 64 gate + 64 up)
+constexpr int kSlots = 128;  // weight rows per CTA (gate: 64 gate + 64 up)
 constexpr int kKCMax = 32;
 constexpr int kTokMax = 16;  // tokens per pass (z chunk)
+constexpr int kAccStride = kSlots + 4;
 
 struct Args {
   const void* x;
@@ -57,17 +62,13 @@ struct Args {
   int* counters;
   int M, N, K, G, KC, S, rowblocks;
   int has_bias, has_res;
-  int sb_stride;  // float2 per slot row in shared memory
 };
 
 // Words of packed weight per row and group of 64, and per thread (k quarter) of a group.
 template <int BITS> struct Fmt;
-template <> struct Fmt<4> { static constexpr int kWordsPerGroup = 8, kWordsPerThread = 2; };
-template <> struct Fmt<8> { static constexpr int kWordsPerGroup = 16, kWordsPerThread = 4; };
-template <> struct Fmt<0> { static constexpr int kWordsPerGroup = 32, kWordsPerThread = 8; };
-
-// Register prefetch depth (groups in flight per warp): about 3-4 KB per warp.
-template <int BITS> struct Depth { static constexpr int kPF = BITS == 4 ? 4 : 2; };
+template <> struct Fmt<4> { static constexpr int kWordsPerGroup = 8, kWordsPerThread = 2, kPF = 4; };
+template <> struct Fmt<8> { static constexpr int kWordsPerGroup = 16, kWordsPerThread = 4, kPF = 3; };
+template <> struct Fmt<0> { static constexpr int kWordsPerGroup = 32, kWordsPerThread = 8, kPF = 2; };
 
 template <int BITS>
 __device__ __forceinline__ void load_words(uint32_t* dst, const uint32_t* p) {
@@ -83,6 +84,12 @@ __device__ __forceinline__ void load_words(uint32_t* dst, const uint32_t* p) {
     dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
     dst[4] = u.x; dst[5] = u.y; dst[6] = u.z; dst[7] = u.w;
   }
+}
+
+__device__ __forceinline__ uint32_t ld_u16(const void* p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
 }
 
 // Natural x words n[0..7] (n[i] = x[2i], x[2i+1]) -> the k order the A dequant delivers.
@@ -107,26 +114,31 @@ __device__ __forceinline__ void permute_x(uint32_t (&p)[8], const uint32_t (&n)[
   }
 }
 
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
+}
+
 template <typename T, int BITS, int NT, bool GATE>
 __global__ void __launch_bounds__(kThreads) qgemm_kernel(const Args a) {
   using A = Act<T>;
+  constexpr bool kQuant = BITS != 0;
   constexpr int WPG = Fmt<BITS>::kWordsPerGroup;
   constexpr int WPT = Fmt<BITS>::kWordsPerThread;
-  constexpr int PF = Depth<BITS>::kPF;
+  constexpr int PF = Fmt<BITS>::kPF;
   constexpr int TOK = NT * 8;
   constexpr uint32_t kMask = 0x000F000Fu;
   constexpr uint32_t kMag = A::kMagic2;
   constexpr float kOff = BITS == 4 ? A::kMagic : 17.0f * A::kMagic;
   constexpr int kRowsOut = GATE ? 64 : 128;
+  // all-ones A operand (1.0 in both halves) for sum(x) through the tensor core
+  constexpr uint32_t kOne2 = sizeof(T) == 2 && A::kMagic == 128.0f ? 0x3F803F80u : 0x3C003C00u;
 
   extern __shared__ __align__(16) unsigned char smem[];
   const int KC = a.KC;
-  const int tok_stride_w = KC * 32 + 4;  // words per token row of sx (bank offset 4)
-  uint32_t* sx = reinterpret_cast<uint32_t*>(smem);
-  float* sxs = reinterpret_cast<float*>(sx + TOK * tok_stride_w);          // [KC][16]
-  float2* ssb = reinterpret_cast<float2*>(sxs + KC * kTokMax);             // [128][sb_stride]
-  float* sacc = reinterpret_cast<float*>(ssb + kSlots * a.sb_stride);      // [16][132]
-  constexpr int kAccStride = kSlots + 4;
+  const int xs_stride = KC * 64 + 8;  // elements per token row of the staged x (16-byte bank offset)
+  T* sx = reinterpret_cast<T*>(smem);
+  float* sacc = reinterpret_cast<float*>(smem);  // reused after the main loop: [16][kAccStride]
   __shared__ int s_last;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -139,18 +151,36 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const Args a) {
   const int N = a.N;
   const int wpr = a.K / 64 * WPG;  // words per weight row
 
+  // ---- x for this CTA's K range -> shared memory (natural order), one async copy -------
+  {
+    const T* x = static_cast<const T*>(a.x);
+    const int chunks = ng * 8;  // 16-byte chunks per token row
+    for (int e = tid; e < TOK * chunks; e += kThreads) {
+      const int m = e / chunks, i = e % chunks;
+      const bool ok = m < mc;
+      const T* src = ok ? x + (size_t)(m0 + m) * a.K + (size_t)g0 * 64 + i * 8 : x;
+      cp_async16(sx + m * xs_stride + i * 8, src, ok ? 16 : 0);
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+  }
+
   // ---- the four weight rows of this thread: q = tile * 2 + half --------------------
   const uint32_t* rowp[4];
+  const unsigned short* sp[4];
+  const unsigned short* bp[4];
   int slot[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const int t = q >> 1, h = q & 1;
     int n;
     const uint32_t* base;
+    const void* sbase = a.sc;
+    const void* bbase = a.bi;
     if constexpr (GATE) {
       slot[q] = t * 64 + warp * 16 + h * 8 + r;
       n = nb * 64 + warp * 16 + h * 8 + r;
       base = t == 0 ? a.w : a.uw;
+      if (t == 1) { sbase = a.usc; bbase = a.ubi; }
     } else {
       slot[q] = warp * 32 + t * 16 + h * 8 + r;
       n = nb * 128 + slot[q];
@@ -158,72 +188,29 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const Args a) {
     }
     n = min(n, N - 1);
     rowp[q] = base + (size_t)n * wpr + (size_t)g0 * WPG + c * WPT;
+    sp[q] = bp[q] = nullptr;
+    if constexpr (kQuant) {
+      sp[q] = static_cast<const unsigned short*>(sbase) + (size_t)n * a.G + g0;
+      bp[q] = static_cast<const unsigned short*>(bbase) + (size_t)n * a.G + g0;
+    }
   }
 
-  // ---- prefetch the first PF groups ------------------------------------------------
+  // ---- register ring: weights (+ scale, bias) of the next PF groups ------------------
   uint32_t st[PF][4][WPT];
+  uint32_t sb[PF][4][2];
 #pragma unroll
   for (int s = 0; s < PF; ++s)
-    if (s < ng)
+    if (s < ng) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) load_words<BITS>(st[s][q], rowp[q] + s * WPG);
+      for (int q = 0; q < 4; ++q) {
+        load_words<BITS>(st[s][q], rowp[q] + s * WPG);
+        if constexpr (kQuant) { sb[s][q][0] = ld_u16(sp[q] + s); sb[s][q][1] = ld_u16(bp[q] + s); }
+      }
+    }
 
-  // ---- stage x (permuted) and sum(x) per group -------------------------------------
-  {
-    const T* x = static_cast<const T*>(a.x);
-    for (int item = tid; item < TOK * KC; item += kThreads) {
-      const int m = item / KC, g = item % KC;
-      float xs = 0.0f;
-      uint32_t* dst = sx + m * tok_stride_w + g * 32;
-      if (m < mc && g < ng) {
-        const uint4* src =
-            reinterpret_cast<const uint4*>(x + (size_t)(m0 + m) * a.K + (size_t)(g0 + g) * 64);
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const uint4 v0 = src[2 * cc], v1 = src[2 * cc + 1];
-          const uint32_t nat[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-          for (int i = 0; i < 8; ++i) xs += A::lo(nat[i]) + A::hi(nat[i]);
-          uint32_t p[8];
-          permute_x<BITS>(p, nat);
-          reinterpret_cast<uint4*>(dst + cc * 8)[0] = make_uint4(p[0], p[1], p[2], p[3]);
-          reinterpret_cast<uint4*>(dst + cc * 8)[1] = make_uint4(p[4], p[5], p[6], p[7]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
-      }
-      sxs[g * kTokMax + m] = xs;
-    }
-  }
-  // ---- stage scale and (bias - offset * scale) as fp32 ------------------------------
-  if constexpr (BITS != 0) {
-    const T* sc = static_cast<const T*>(a.sc);
-    const T* bi = static_cast<const T*>(a.bi);
-    for (int item = tid; item < kSlots * KC; item += kThreads) {
-      const int sl = item / KC, g = item % KC;
-      int n;
-      const T* s_src = sc;
-      const T* b_src = bi;
-      if constexpr (GATE) {
-        n = nb * 64 + (sl & 63);
-        if (sl >= 64) { s_src = static_cast<const T*>(a.usc); b_src = static_cast<const T*>(a.ubi); }
-      } else {
-        n = nb * 128 + sl;
-      }
-      n = min(n, N - 1);
-      float s = 0.0f, b = 0.0f;
-      if (g < ng) {
-        const size_t gi = (size_t)n * a.G + g0 + g;
-        s = A::to_f(s_src[gi]);
-        b = A::to_f(b_src[gi]);
-      }
-      ssb[sl * a.sb_stride + g] = make_float2(s, fmaf(-kOff, s, b));
-    }
-  }
+  asm volatile("cp.async.wait_all;\n" ::);
   __syncthreads();
 
-  // ---- main loop over this CTA's groups --------------------------------------------
   float acc[2][NT][4];
 #pragma unroll
   for (int t = 0; t < 2; ++t)
@@ -232,20 +219,28 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const Args a) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[t][nt][i] = 0.0f;
 
+  const uint32_t ones[4] = {kOne2, kOne2, kOne2, kOne2};
+
   for (int gb = 0; gb < ng; gb += PF) {
 #pragma unroll
     for (int s = 0; s < PF; ++s) {
       const int g = gb + s;
       if (g < ng) {
+        // x fragments of this group (token r of each n8 tile, k quarter c), permuted
         uint32_t B[NT][8];
-        float2 xsv[NT];
+        float X[NT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          const uint4* src = reinterpret_cast<const uint4*>(sx + (nt * 8 + r) * tok_stride_w + g * 32 + c * 8);
+          const uint4* src = reinterpret_cast<const uint4*>(sx + (nt * 8 + r) * xs_stride + g * 64 + c * 16);
           const uint4 v0 = src[0], v1 = src[1];
-          B[nt][0] = v0.x; B[nt][1] = v0.y; B[nt][2] = v0.z; B[nt][3] = v0.w;
-          B[nt][4] = v1.x; B[nt][5] = v1.y; B[nt][6] = v1.z; B[nt][7] = v1.w;
-          xsv[nt] = *reinterpret_cast<const float2*>(sxs + g * kTokMax + nt * 8 + 2 * c);
+          const uint32_t nat[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+          permute_x<BITS>(B[nt], nat);
+          if constexpr (kQuant) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) X[nt][i] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) mma16816<T>(X[nt], ones, B[nt][2 * j], B[nt][2 * j + 1]);
+          }
         }
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
@@ -298,25 +293,31 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const Args a) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) d[nt][i] = fmaf(16.0f, dh[nt][i], d[nt][i]);
             }
-            const float2 sb0 = ssb[slot[2 * t] * a.sb_stride + g];
-            const float2 sb1 = ssb[slot[2 * t + 1] * a.sb_stride + g];
+            const float s0 = A::lo(sb[s][2 * t][0]), s1 = A::lo(sb[s][2 * t + 1][0]);
+            const float b0 = fmaf(-kOff, s0, A::lo(sb[s][2 * t][1]));
+            const float b1 = fmaf(-kOff, s1, A::lo(sb[s][2 * t + 1][1]));
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              acc[t][nt][0] = fmaf(sb0.x, d[nt][0], fmaf(sb0.y, xsv[nt].x, acc[t][nt][0]));
-              acc[t][nt][1] = fmaf(sb0.x, d[nt][1], fmaf(sb0.y, xsv[nt].y, acc[t][nt][1]));
-              acc[t][nt][2] = fmaf(sb1.x, d[nt][2], fmaf(sb1.y, xsv[nt].x, acc[t][nt][2]));
-              acc[t][nt][3] = fmaf(sb1.x, d[nt][3], fmaf(sb1.y, xsv[nt].y, acc[t][nt][3]));
+              acc[t][nt][0] = fmaf(s0, d[nt][0], fmaf(b0, X[nt][0], acc[t][nt][0]));
+              acc[t][nt][1] = fmaf(s0, d[nt][1], fmaf(b0, X[nt][1], acc[t][nt][1]));
+              acc[t][nt][2] = fmaf(s1, d[nt][2], fmaf(b1, X[nt][0], acc[t][nt][2]));
+              acc[t][nt][3] = fmaf(s1, d[nt][3], fmaf(b1, X[nt][1], acc[t][nt][3]));
             }
           }
         }
-        if (g + PF < ng)
+        if (g + PF < ng) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) load_words<BITS>(st[s][q], rowp[q] + (g + PF) * WPG);
+          for (int q = 0; q < 4; ++q) {
+            load_words<BITS>(st[s][q], rowp[q] + (g + PF) * WPG);
+            if constexpr (kQuant) { sb[s][q][0] = ld_u16(sp[q] + g + PF); sb[s][q][1] = ld_u16(bp[q] + g + PF); }
+          }
+        }
       }
     }
   }
 
-  // ---- CTA tile -> shared memory [token][slot] ---------------------------------------
+  // ---- CTA tile -> shared memory [token][slot] (x is no longer needed) -----------------
+  __syncthreads();
 #pragma unroll
   for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -353,7 +354,7 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const Args a) {
     for (int e = tid; e < mc * kSlots; e += kThreads) {
       const int m = e / kSlots, sl = e % kSlots;
       float v = 0.0f;
-      for (int sp = 0; sp < a.S; ++sp) v += __ldcg(base + ((size_t)sp * kTokMax + m) * wd + sl);
+      for (int sp2 = 0; sp2 < a.S; ++sp2) v += __ldcg(base + ((size_t)sp2 * kTokMax + m) * wd + sl);
       sacc[m * kAccStride + sl] = v;
     }
     __syncthreads();
@@ -379,16 +380,10 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const Args a) {
   }
 }
 
-size_t smem_bytes(int nt, int kc, int sb_stride) {
-  const size_t tok = nt * 8;
-  return tok * (kc * 32 + 4) * 4 + (size_t)kc * kTokMax * 4 + (size_t)kSlots * sb_stride * 8 +
-         (size_t)kTokMax * (kSlots + 4) * 4;
-}
-
-int sb_stride_for(int kc) {
-  int s = kc + 1;
-  if ((2 * s) % 32 == 0) s += 1;
-  return s;
+size_t smem_bytes(int nt, int kc) {
+  const size_t x = (size_t)nt * 8 * (kc * 64 + 8) * 2;
+  const size_t accb = (size_t)kTokMax * kAccStride * 4;
+  return std::max(x, accb);
 }
 
 template <typename T, int BITS, int NT, bool GATE>
@@ -400,8 +395,7 @@ int launch_t(const Args& a, dim3 grid, size_t smem, cudaStream_t stream) {
   VELLA_CUDA_TRY(cudaGetDevice(&dev));
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load(std::memory_order_acquire) & bit)) {
-    VELLA_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)smem_bytes(2, kKCMax, sb_stride_for(kKCMax))));
+    VELLA_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes(2, kKCMax)));
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
   k<<<grid, kThreads, smem, stream>>>(a);
@@ -461,7 +455,6 @@ int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& p, const void* x, c
   a.M = d.m; a.N = d.n; a.K = d.k; a.G = d.k / 64; a.KC = p.kc; a.S = p.splits; a.rowblocks = p.rowblocks;
   a.has_bias = d.epilogue == VELLA_EPI_BIAS || d.epilogue == VELLA_EPI_BIAS_RESIDUAL;
   a.has_res = d.epilogue == VELLA_EPI_RESIDUAL || d.epilogue == VELLA_EPI_BIAS_RESIDUAL;
-  a.sb_stride = sb_stride_for(p.kc);
   if (p.splits > 1) {
     const size_t ctr = (size_t)p.zchunks * p.rowblocks * sizeof(int);
     a.counters = static_cast<int*>(ws);
@@ -469,7 +462,7 @@ int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& p, const void* x, c
   }
   const bool gate = d.epilogue == VELLA_EPI_SILU_GATE;
   const int nt = d.m <= 8 ? 1 : 2;
-  const size_t smem = smem_bytes(nt, p.kc, a.sb_stride);
+  const size_t smem = smem_bytes(nt, p.kc);
   const dim3 grid(p.rowblocks, p.splits, p.zchunks);
   if (d.dtype == VELLA_BF16) {
     switch (d.bits) {
