@@ -101,6 +101,23 @@ VELLA_API int vella_qgemm(const vella_qgemm_desc* desc, const void* x, const voi
                 const void* bias, const void* residual, void* out, void* workspace,
                 size_t workspace_bytes, vella_stream_t stream);
 
+/*
+ * vella_qgemm without any device allocation, for callers that cannot allocate: code that
+ * runs during CUDA graph capture, a real-time audio thread that must not block on an
+ * allocation, or an embedder whose device memory belongs to another allocator.  It has no
+ * counterpart in the reference (MLX allocates for its caller).  Same arguments and result
+ * as vella_qgemm minus the workspace: the split-K scratch is one static device array of
+ * 32 MiB inside the library, held by every GPU that loads the library until exit.  A
+ * shape whose scratch (vella_qgemm_workspace_size) exceeds 32 MiB is rejected with
+ * VELLA_E_INVALID.  The first call on a device looks the array up and clears it, waiting
+ * on `stream`, so make it before any stream capture.  All calls share the array: calls
+ * that overlap on the GPU race and must be serialised by the caller.
+ */
+VELLA_API int vella_qgemm_noalloc(const vella_qgemm_desc* desc, const void* x, const void* w, const void* scales,
+                                  const void* biases, const void* up_w, const void* up_scales,
+                                  const void* up_biases, const void* bias, const void* residual, void* out,
+                                  vella_stream_t stream);
+
 /* Message of the last failing call on this thread ("" when none); returns its length. */
 VELLA_API size_t vella_last_error(char* buf, size_t cap);
 
