@@ -48,7 +48,7 @@ enum {
 };
 
 /* ---- element types ------------------------------------------------------------------ */
-enum { VELLA_BF16 = 0, VELLA_F16 = 1 };
+enum { VELLA_BF16 = 0, VELLA_F16 = 1, VELLA_F32 = 2 };
 
 /* ---- GEMM epilogues (reference SmallMGEMM.EpilogueKind, SmallMGEMM.swift:41) --------- */
 enum {
@@ -117,6 +117,133 @@ VELLA_API int vella_qgemm_noalloc(const vella_qgemm_desc* desc, const void* x, c
                                   const void* biases, const void* up_w, const void* up_scales,
                                   const void* up_biases, const void* bias, const void* residual, void* out,
                                   vella_stream_t stream);
+
+/* ---- weight preparation ------------------------------------------------------------- */
+
+/*
+ * MLX-affine quantize on the device (quantize-at-load): w [N, K] in `src_dtype` (VELLA_F32,
+ * VELLA_BF16 or VELLA_F16) -> packed uint32 [N, K*bits/32], scales and biases [N, K/64] in
+ * desc->dtype.  desc supplies n, k, bits (4 | 8), group_size (64), dtype; m and epilogue are
+ * ignored.  Replaces MLX.quantized(_:groupSize:bits:mode: .affine) at
+ * Worker/Sources/MLXAudioSTT/Precision/DerivedPrecision.swift:138 and
+ * NemotronTranscribe/NemotronTranscribeRecipe.swift:48.
+ */
+VELLA_API int vella_quantize(const vella_qgemm_desc* desc, int32_t src_dtype, const void* w, void* packed,
+                             void* scales, void* biases, vella_stream_t stream);
+
+/* n values ~ N(mean, std^2) in `dtype` from Philox-4x32-10 keyed by (seed, tensor): the
+ * synthetic inputs and weights of the benchmarks (value i uses counter i/4, lane i%4). */
+VELLA_API int vella_fill_normal(void* out, size_t n, int32_t dtype, uint64_t seed, uint32_t tensor, float mean,
+                                float std, vella_stream_t stream);
+
+/* ---- resident decoder model ------------------------------------------------------------
+ * A dense GQA transformer (Qwen3 text-decoder recipe, Worker/Sources/MLXAudioSTT/Qwen3ASR/
+ * Qwen3ASRTextDecoder.swift:17-214): RMSNorm, RoPE (half rotation, base rope_theta),
+ * optional per-head q/k RMSNorm, SwiGLU MLP, final RMSNorm, LM head.  Every linear
+ * (q|k|v, o, gate, up, down, lm_head) is `bits` = 0 (dense) or MLX-affine 4/8-bit g64; the
+ * token embedding is dense.  The model owns its weights, one KV cache of max_seq positions
+ * and a buffer of max_prefix input embeddings (positions below the prefix length take
+ * their input embedding from it, later positions from the token table).
+ */
+typedef struct vella_model_cfg {
+  int32_t n_layers, d_model, n_heads, n_kv_heads, head_dim, ffn, vocab;
+  int32_t bits;       /* 0, 4 or 8 */
+  int32_t dtype;      /* VELLA_BF16 | VELLA_F16 */
+  int32_t qk_norm;    /* 1: RMSNorm over head_dim on q and k before RoPE */
+  int32_t max_seq;    /* KV capacity in positions */
+  int32_t max_prefix; /* capacity of the input-embedding prefix */
+  float rms_eps;
+  float rope_theta;
+} vella_model_cfg;
+
+typedef struct vella_model vella_model;
+
+VELLA_API int vella_model_create(const vella_model_cfg* cfg, int32_t device, vella_model** out);
+VELLA_API int vella_model_destroy(vella_model* model);
+/* Synthetic weights: linears ~N(0, std^2) (quantized on the device when bits != 0), norm
+ * weights ~N(1, 0.1^2), token embedding ~N(0, 1); Philox keyed by `seed`. */
+VELLA_API int vella_model_init_random(vella_model* model, uint64_t seed, float std);
+/* Device pointer and size of a tensor, for loading real weights or reading them back.
+ * Names: "embed", "final_norm", "prefix", "logits", "kv", "lm_head.w|s|b", and per layer
+ * "attn_norm", "mlp_norm", "q_norm", "k_norm", "qkv.w|s|b" (rows q, then k, then v),
+ * "o.w|s|b", "gate.w|s|b", "up.w|s|b", "down.w|s|b". */
+VELLA_API int vella_model_tensor(vella_model* model, const char* name, int32_t layer, void** ptr, size_t* bytes);
+VELLA_API size_t vella_model_weight_bytes(const vella_model* model);
+/*
+ * Teacher-forced scoring (the backbone over a whole prompt, as llm.backbone(...) +
+ * lmHead in NemotronTranscribeModel.swift:316-322): runs the prefix embeddings [P, d]
+ * (host or device, model dtype) then tokens[0..T-1] (host) through a fresh cache and
+ * writes the logits that predict each token, rows for positions P-1 .. P+T-2, to
+ * logits_out [T, vocab] (host when on_host, else device).  Synchronous.
+ */
+VELLA_API int vella_model_score(vella_model* model, const void* prefix, int32_t P, const int32_t* tokens, int32_t T,
+                                void* logits_out, int32_t on_host);
+
+/* ---- draft-and-verify decode (NemotronTranscribeModel.decodeMTP, :306-396) ---------- */
+enum { VELLA_DRAFT_MODEL = 0, VELLA_DRAFT_ORACLE = 1 };
+enum { VELLA_DECODE_AUTO = 0, VELLA_DECODE_SPEC = 1, VELLA_DECODE_GREEDY = 2 };
+enum { VELLA_FAULT_NONE = 0, VELLA_FAULT_THROW = 1, VELLA_FAULT_NONFINITE = 2 };
+enum { VELLA_FLAG_LOOPED = 1, VELLA_FLAG_FELL_BACK = 2, VELLA_FLAG_RUNAWAY_RETRY = 4, VELLA_FLAG_CAPACITY = 8 };
+
+typedef struct vella_spec_cfg {
+  int32_t draft_k;    /* drafts per pass, 1..15 (reference draftDepth, :23-24) */
+  int32_t draft_mode; /* VELLA_DRAFT_MODEL: the draft model's greedy tokens;
+                         VELLA_DRAFT_ORACLE: each proposal is the reference token with
+                         probability oracle_p, else uniform over the vocabulary (Philox) */
+  float oracle_p;
+  uint64_t seed;      /* Philox key of the oracle proposals */
+  int32_t n_eos;
+  int32_t eos[8];
+  int32_t use_graphs; /* 1: replay each pass as one CUDA graph */
+} vella_spec_cfg;
+
+typedef struct vella_spec_stats {
+  int64_t passes;          /* draft+verify passes          */
+  int64_t greedy_steps;    /* single-token target steps    */
+  int64_t accepted[16];    /* passes that accepted i drafts */
+  int64_t fallbacks;       /* runtime failures -> greedy (sticky) */
+  int64_t runaway_retries; /* looping draft-and-verify runs decoded again greedy */
+  int32_t draft_disabled;  /* sticky fallback in force */
+  float last_decode_ms;    /* device time of the last vella_spec_decode */
+  int32_t last_tokens;
+} vella_spec_stats;
+
+typedef struct vella_spec vella_spec;
+
+/* target: the verifying model; draft: the proposing model (NULL: greedy only).  Both
+ * must share the vocabulary; the handle owns its stream and is single-threaded. */
+VELLA_API int vella_spec_create(vella_model* target, vella_model* draft, const vella_spec_cfg* cfg, vella_spec** out);
+VELLA_API int vella_spec_destroy(vella_spec* spec);
+/* Input embeddings of the request: [T, d_target] and [T, d_draft] (NULL keeps what is
+ * already in the models' "prefix" buffers). */
+VELLA_API int vella_spec_set_prefix(vella_spec* spec, const void* target_embeds, const void* draft_embeds, int32_t T,
+                                    int32_t on_host);
+/* Reference continuation for VELLA_DRAFT_ORACLE (token i is the one at position T + i). */
+VELLA_API int vella_spec_set_reference(vella_spec* spec, const int32_t* tokens, int32_t n);
+/* Prefill both models over the prefix; *first = the target's greedy token after it. */
+VELLA_API int vella_spec_prefill(vella_spec* spec, int32_t* first);
+/* One pass: K draft steps, one target forward over K+1 positions (causal KV append),
+ * greedy acceptance, KV rollback past the first mismatch.  Writes the accepted drafts and
+ * the target's bonus token (1..K+1 tokens).  VELLA_E_NONFINITE when the verify logits
+ * hold NaN/Inf (reference :356-363). */
+VELLA_API int vella_spec_step(vella_spec* spec, int32_t* out_tokens, int32_t* n_out);
+/* One plain greedy target step (reference decodeGreedy, :266-290). */
+VELLA_API int vella_spec_greedy_step(vella_spec* spec, int32_t* out_token);
+/*
+ * A whole decode (reference decode/decodeMTP/decodeGreedy/retryingRunaway, :266-443):
+ * prefill, then passes (SPEC), single steps (GREEDY) or, for AUTO, draft-and-verify with
+ * the reference's fallbacks: a runtime failure re-decodes plain greedy and keeps the draft
+ * off until vella_spec_reset (sticky); a run that loops or reaches max_tokens is decoded
+ * again greedy.  Stops at an EOS token (not emitted), at max_tokens, or at a repetition
+ * loop (cut to one copy).  *flags: VELLA_FLAG_*.
+ */
+VELLA_API int vella_spec_decode(vella_spec* spec, int32_t mode, int32_t max_tokens, int32_t* out_tokens, int32_t cap,
+                                int32_t* n_out, int32_t* flags);
+VELLA_API int vella_spec_get_stats(const vella_spec* spec, vella_spec_stats* out);
+/* Test hook mirroring VELLA_TEST_OPTIMIZED_FAULT (NemotronTranscribeModel.swift:398-399). */
+VELLA_API int vella_spec_set_fault(vella_spec* spec, int32_t fault);
+/* Clear the sticky fallback and the statistics. */
+VELLA_API int vella_spec_reset(vella_spec* spec);
 
 /* Message of the last failing call on this thread ("" when none); returns its length. */
 VELLA_API size_t vella_last_error(char* buf, size_t cap);

@@ -1,0 +1,260 @@
+"""Parity of the resident decoder and the draft-and-verify loop (through the C ABI) with
+the CPU oracle, on small seeded models.
+
+Bars: logits max |error| <= 2e-2 against the oracle (teacher forced); greedy tokens equal
+the oracle's argmax wherever its top-2 margin exceeds that tolerance; draft-and-verify
+emits exactly the greedy tokens (bit-exact, any K, any acceptance rate); the accepted-
+length histogram equals the oracle's simulation with the same Philox proposals.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import affine as A
+from oracle import decoder as D
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2
+
+
+class _Dev:
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+
+def download(model, name, layer=-1):
+    ptr, nbytes = model.tensor(name, layer)
+    return torch.as_tensor(_Dev(ptr, nbytes), device="cuda").cpu().numpy()
+
+
+def upload(model, name, arr, layer=-1):
+    ptr, nbytes = model.tensor(name, layer)
+    raw = np.ascontiguousarray(arr).view(np.uint8).reshape(-1)
+    assert raw.nbytes <= nbytes
+    torch.as_tensor(_Dev(ptr, raw.nbytes), device="cuda").copy_(torch.from_numpy(raw.copy()))
+
+
+def oracle_weights(model, cfg: D.Config):
+    d, V = cfg.d_model, cfg.vocab
+    f = lambda a: A.bf16_from_bits(a.view(np.uint16))  # noqa: E731
+
+    def lin(name, layer, n, k):
+        w = download(model, f"{name}.w", layer)
+        if cfg.bits:
+            return {"w": w.view(np.uint32).reshape(n, k * cfg.bits // 32),
+                    "s": download(model, f"{name}.s", layer).view(np.uint16).reshape(n, k // 64),
+                    "b": download(model, f"{name}.b", layer).view(np.uint16).reshape(n, k // 64)}
+        return {"w": w.view(np.uint16).reshape(n, k)}
+
+    H, KV, hd, F = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn
+    W = {"embed": f(download(model, "embed")).reshape(V, d),
+         "final_norm": f(download(model, "final_norm")),
+         "lm_head": lin("lm_head", -1, V, d), "layers": []}
+    for l in range(cfg.n_layers):
+        L = {"attn_norm": f(download(model, "attn_norm", l)), "mlp_norm": f(download(model, "mlp_norm", l)),
+             "qkv": lin("qkv", l, (H + 2 * KV) * hd, d), "o": lin("o", l, d, H * hd),
+             "gate": lin("gate", l, F, d), "up": lin("up", l, F, d), "down": lin("down", l, d, F)}
+        if cfg.qk_norm:
+            L["q_norm"] = f(download(model, "q_norm", l))
+            L["k_norm"] = f(download(model, "k_norm", l))
+        W["layers"].append(L)
+    return W
+
+
+def make(n_layers=2, d=256, H=4, KV=2, hd=64, ffn=512, V=1000, bits=4, qk_norm=False, seed=1, max_seq=512):
+    from vella_b200 import decode as VD
+    mc = VD.ModelConfig(n_layers, d, H, KV, hd, ffn, V, bits=bits, qk_norm=qk_norm, max_seq=max_seq, max_prefix=128)
+    m = VD.Model(mc)
+    m.init_random(seed, 0.02 if d > 128 else 0.05)
+    oc = D.Config(n_layers, d, H, KV, hd, ffn, V, bits=bits, qk_norm=qk_norm)
+    return m, oc
+
+
+def prefix_of(P, d, seed):
+    x = np.random.default_rng(seed).standard_normal((P, d)).astype(np.float32)
+    return A.bf16_bits(x)
+
+
+@pytest.fixture(scope="module")
+def pair():
+    """Target (int4, 2 layers) and draft (dense bf16, 1 layer), same vocabulary."""
+    t, tc = make(bits=4, seed=1)
+    d, dc = make(n_layers=1, d=128, H=2, KV=1, ffn=256, bits=0, seed=2)
+    return t, tc, d, dc
+
+
+@pytest.mark.parametrize("bits,qk", [(4, False), (8, False), (0, False), (4, True)])
+def test_score_matches_oracle(bits, qk):
+    m, oc = make(bits=bits, qk_norm=qk, seed=3 + bits)
+    W = oracle_weights(m, oc)
+    table = D.rope_table(64, oc.head_dim, oc.rope_theta)
+    P = 20
+    pre = prefix_of(P, oc.d_model, 5)
+    toks = list(np.random.default_rng(6).integers(0, oc.vocab, 30))
+    got = A.bf16_from_bits(m.score(pre, toks))
+    ref = D.score(oc, W, A.bf16_from_bits(pre), toks, table)
+    assert got.shape == ref.shape == (30, oc.vocab)
+    assert np.isfinite(got).all()
+    err = np.abs(got - ref).max()
+    assert err <= LOGIT_TOL, err
+
+
+def greedy_tokens(t, d, P, pre_t, pre_d, n, **kw):
+    from vella_b200 import decode as VD
+    sd = VD.SpecDecoder(t, d, **kw)
+    sd.set_prefix(pre_t, pre_d, P)
+    return sd.decode_greedy(n).tokens, sd
+
+
+def test_greedy_matches_oracle_teacher_forced(pair):
+    t, tc, d, dc = pair
+    P = 24
+    pre_t, pre_d = prefix_of(P, tc.d_model, 11), prefix_of(P, dc.d_model, 12)
+    toks, _ = greedy_tokens(t, d, P, pre_t, pre_d, 48)
+    assert len(toks) == 48
+    W = oracle_weights(t, tc)
+    logits = D.score(tc, W, A.bf16_from_bits(pre_t), toks, D.rope_table(P + 64, tc.head_dim, tc.rope_theta))
+    for j, tok in enumerate(toks):
+        row = logits[j]
+        best = int(np.argmax(row))
+        assert tok == best or row[best] - row[tok] <= LOGIT_TOL, (j, tok, best, row[best] - row[tok])
+
+
+@pytest.mark.parametrize("k", [1, 2, 4, 8])
+@pytest.mark.parametrize("p", [0.0, 0.5, 0.9, 1.0])
+def test_draft_and_verify_is_bit_exact_greedy(pair, k, p):
+    from vella_b200 import decode as VD
+    t, tc, d, dc = pair
+    P, N = 24, 64
+    pre_t, pre_d = prefix_of(P, tc.d_model, 11), prefix_of(P, dc.d_model, 12)
+    ref, _ = greedy_tokens(t, d, P, pre_t, pre_d, N + 16)
+    sd = VD.SpecDecoder(t, d, k=k, mode=VD.DRAFT_ORACLE, oracle_p=p, seed=99)
+    sd.set_prefix(pre_t, pre_d, P)
+    sd.set_reference(ref)
+    res = sd.decode_mtp(N)
+    assert res.tokens == ref[:N]
+    # pass-by-pass acceptance replayed by the oracle with the same Philox proposals
+    def propose(out, pi):
+        return [D.oracle_proposal(99, pi, i, ref[len(out) + i] if len(out) + i < len(ref) else None, p, tc.vocab)
+                for i in range(k)]
+
+    def verify(out, drafts):
+        return [ref[len(out) + j] for j in range(k + 1)]
+
+    toks, _, hist = D.draft_and_verify(verify, propose, ref[0], N, k)
+    assert toks == ref[:N]
+    expect = np.bincount(np.asarray(hist, dtype=np.int64), minlength=16)[:16]
+    got = np.asarray(res.stats["accepted"])  # passes by number of accepted drafts
+    assert np.array_equal(got[: k + 1], expect[: k + 1]), (got, expect)
+    assert res.stats["passes"] == len(hist)
+
+
+def test_model_draft_and_self_speculation(pair):
+    from vella_b200 import decode as VD
+    t, tc, d, dc = pair
+    P = 24
+    pre_t, pre_d = prefix_of(P, tc.d_model, 11), prefix_of(P, dc.d_model, 12)
+    ref, _ = greedy_tokens(t, d, P, pre_t, pre_d, 40)
+    # a real (random) draft: output still equals greedy
+    sd = VD.SpecDecoder(t, d, k=4, mode=VD.DRAFT_MODEL)
+    sd.set_prefix(pre_t, pre_d, P)
+    assert sd.decode_mtp(40).tokens == ref
+    # draft = a second copy of the target: every draft is accepted
+    t2, _ = make(bits=4, seed=1)
+    sd2 = VD.SpecDecoder(t, t2, k=4, mode=VD.DRAFT_MODEL)
+    sd2.set_prefix(pre_t, pre_t, P)
+    res = sd2.decode_mtp(40)
+    assert res.tokens == ref
+    assert res.stats["accepted"][4] == res.stats["passes"] > 0
+
+
+def test_graph_replay_equals_eager(pair):
+    from vella_b200 import decode as VD
+    t, tc, d, dc = pair
+    P = 24
+    pre_t, pre_d = prefix_of(P, tc.d_model, 13), prefix_of(P, dc.d_model, 14)
+    outs = []
+    for graphs in (False, True):
+        sd = VD.SpecDecoder(t, d, k=3, mode=VD.DRAFT_ORACLE, oracle_p=0.6, seed=5, use_graphs=graphs)
+        sd.set_prefix(pre_t, pre_d, P)
+        g = sd.decode_greedy(50).tokens
+        sd.set_reference(g)
+        outs.append((g, sd.decode_mtp(50).tokens))
+    assert outs[0] == outs[1] and outs[0][0] == outs[0][1]
+
+
+@pytest.mark.parametrize("fault", [1, 2])  # FAULT_THROW, FAULT_NONFINITE
+def test_runtime_failure_falls_back_to_greedy_sticky(pair, fault):
+    from vella_b200 import decode as VD
+    t, tc, d, dc = pair
+    P = 24
+    pre_t, pre_d = prefix_of(P, tc.d_model, 11), prefix_of(P, dc.d_model, 12)
+    ref, _ = greedy_tokens(t, d, P, pre_t, pre_d, 30)
+    sd = VD.SpecDecoder(t, d, k=4, mode=VD.DRAFT_MODEL)
+    sd.set_prefix(pre_t, pre_d, P)
+    sd.set_fault(fault)
+    res = sd.decode(30)
+    assert res.tokens == ref and res.flags & VD.FLAG_FELL_BACK
+    st = sd.stats()
+    assert st["fallbacks"] == 1 and st["draft_disabled"]
+    sd.set_fault(VD.FAULT_NONE)
+    res2 = sd.decode(30)  # sticky: plain greedy until reset, no second fallback
+    assert res2.tokens == ref and not res2.flags & VD.FLAG_FELL_BACK and sd.stats()["fallbacks"] == 1
+    sd.reset()
+    res3 = sd.decode(29)
+    assert res3.tokens == ref[:29] and sd.stats()["passes"] > 0 and not sd.stats()["draft_disabled"]
+
+
+def test_eos_stops_and_is_not_emitted(pair):
+    from vella_b200 import decode as VD
+    t, tc, d, dc = pair
+    P = 24
+    pre_t, pre_d = prefix_of(P, tc.d_model, 11), prefix_of(P, dc.d_model, 12)
+    ref, _ = greedy_tokens(t, d, P, pre_t, pre_d, 40)
+    stop = ref[17]
+    first = ref.index(stop)
+    for mode in (VD.DECODE_GREEDY, VD.DECODE_SPEC):
+        sd = VD.SpecDecoder(t, d, k=4, mode=VD.DRAFT_MODEL, eos=[stop])
+        sd.set_prefix(pre_t, pre_d, P)
+        assert sd.decode(40, mode).tokens == ref[:first]
+
+
+def test_runaway_retry_when_max_tokens_reached(pair):
+    from vella_b200 import decode as VD
+    t, tc, d, dc = pair
+    P = 24
+    pre_t, pre_d = prefix_of(P, tc.d_model, 11), prefix_of(P, dc.d_model, 12)
+    sd = VD.SpecDecoder(t, d, k=2, mode=VD.DRAFT_MODEL)
+    sd.set_prefix(pre_t, pre_d, P)
+    res = sd.decode(16)  # AUTO: reaching max_tokens counts as a runaway -> greedy retry
+    assert res.flags & VD.FLAG_RUNAWAY_RETRY and sd.stats()["runaway_retries"] == 1 and len(res.tokens) == 16
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_device_quantizer_matches_oracle_bitwise(bits, dtype):
+    import ctypes
+    from vella_b200 import _lib as L
+    from vella_b200 import decode as VD  # noqa: F401  (declares vella_quantize)
+    rng = np.random.default_rng(bits)
+    n, k = 300, 1024
+    w = (rng.standard_normal((n, k)) * np.float32(0.02) * (1 + 10 * rng.random((n, 1)))).astype(np.float32)
+    w[0, :64] = 0.0          # all-zero group
+    w[1, :64] = -0.5         # constant negative group
+    wd = torch.from_numpy(w).cuda()
+    packed = torch.zeros(n, k * bits // 32, dtype=torch.int32, device="cuda")
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
+    sc = torch.zeros(n, k // 64, dtype=tdt, device="cuda")
+    bi = torch.zeros(n, k // 64, dtype=tdt, device="cuda")
+    desc = L.QgemmDesc(0, n, k, bits, 64, L.BF16 if dtype == "bf16" else L.F16, 0)
+    L.check(L.lib().vella_quantize(ctypes.byref(desc), 2, wd.data_ptr(), packed.data_ptr(), sc.data_ptr(),
+                                   bi.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    p, s, b = A.quantize(w, bits, dtype)
+    assert np.array_equal(packed.cpu().numpy().view(np.uint32), p)
+    if dtype == "bf16":
+        assert np.array_equal(sc.cpu().view(torch.int16).numpy().view(np.uint16), s)
+        assert np.array_equal(bi.cpu().view(torch.int16).numpy().view(np.uint16), b)
+    else:
+        assert np.array_equal(sc.cpu().numpy(), s) and np.array_equal(bi.cpu().numpy(), b)

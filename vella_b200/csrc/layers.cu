@@ -39,10 +39,11 @@ __device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
 // ---------------------------------------------------------------------------------------
 template <typename T>
 __global__ void embed_rows_kernel(T* __restrict__ h, const T* __restrict__ table, const T* __restrict__ prefix,
-                                  const int* __restrict__ tok, PosRef pr, int P, int d, int vocab, int max_seq,
-                                  int* err) {
+                                  const int* __restrict__ tok, PosRef pr, const int* __restrict__ Pdev, int d,
+                                  int vocab, int max_seq, int* err) {
   const int m = blockIdx.x;
   const int pos = *pr.base + pr.off + m;
+  const int P = *Pdev;
   const T* src;
   if (pos >= 0 && pos < P) {
     src = prefix + (size_t)pos * d;
@@ -400,13 +401,6 @@ __global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logit
   }
 }
 
-template <typename T>
-size_t attn_smem(int gq) {
-  const int hd = sizeof(T) == 2 ? 0 : 0;
-  (void)hd;
-  return 0;
-}
-
 size_t attn_smem_bytes(int hd, int gq) {
   const size_t ks = hd + 4, ps = kAttnChunk + 4, qr = (size_t)kAttnQBlock * gq;
   return (2 * kAttnChunk * ks + qr * ks + qr * ps) * sizeof(float) + qr * sizeof(float2);
@@ -454,8 +448,8 @@ void attn_scratch_carve(void* base, int kv, int gq, int hd, int max_rows, int ma
   s->part = reinterpret_cast<float*>(p + up(ctr) + up(ml));
 }
 
-int launch_embed_rows(int dtype, void* h, const void* table, const void* prefix, const int* tok, PosRef pr,
-                      int rows, int P, int d, int vocab, int max_seq, int* err, cudaStream_t s) {
+int launch_embed_rows_dev(int dtype, void* h, const void* table, const void* prefix, const int* tok, PosRef pr,
+                          int rows, const int* P, int d, int vocab, int max_seq, int* err, cudaStream_t s) {
   if (rows <= 0) return VELLA_OK;
   if (dtype == VELLA_BF16)
     embed_rows_kernel<__nv_bfloat16><<<rows, 256, 0, s>>>(

@@ -28,8 +28,10 @@ size_t attn_scratch_bytes(int kv, int gq, int hd, int max_rows, int max_seq);
 void attn_scratch_carve(void* base, int kv, int gq, int hd, int max_rows, int max_seq, AttnScratch* s);
 
 // dtype: 0 = bf16, 1 = fp16 everywhere below.
-int launch_embed_rows(int dtype, void* h, const void* table, const void* prefix, const int* tok, PosRef pr,
-                      int rows, int P, int d, int vocab, int max_seq, int* err, cudaStream_t s);
+// Row m holds position p = *pr.base + pr.off + m: the caller's input embedding p when
+// p < *P (device scalar), else the token table row tok[p].
+int launch_embed_rows_dev(int dtype, void* h, const void* table, const void* prefix, const int* tok, PosRef pr,
+                          int rows, const int* P, int d, int vocab, int max_seq, int* err, cudaStream_t s);
 int launch_rmsnorm(int dtype, void* out, const void* x, const void* w, int rows, int d, float eps,
                    cudaStream_t s);
 int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* vc, const float2* cs,

@@ -1,0 +1,598 @@
+// Draft-and-verify decode loop on one GPU: prefill, one CUDA graph per pass (K draft
+// steps, one batched target verify, acceptance, KV rollback), and the host loop with the
+// reference's stop rules and fallbacks.
+//
+// Reference: Worker/Sources/MLXAudioSTT/NemotronTranscribe/NemotronTranscribeModel.swift
+//   decodeMTP :306-396 (greedy draft-and-verify: accepted = longest prefix where the
+//   target's argmax equals the draft, bonus = the target's token after it, one host sync
+//   per pass, non-finite verify logits are an error), decodeGreedy :266-290, decode
+//   :412-431 (sticky fallback to plain greedy after a runtime failure), retryingRunaway
+//   :436-443, endsInLoop :296-302; NTKVCache.trim NemotronTranscribeDecoder.swift:111-116.
+//
+// B200 design.  All sequence state lives on the device: token history tok[pos], the
+// committed length L and the prefix length P.  Every kernel of a pass reads its positions
+// from L, so one captured graph replays every pass.  Draft tokens are written straight into
+// tok[L..L+K) (speculatively); the target verifies positions L-1..L+K-1 in one forward and
+// appends their K/V; acceptance rewrites tok[L+a] with the bonus token and advances L by
+// a+1.  Rolling back the KV cache is free: the cache is valid below L-1 by construction and
+// the next pass overwrites everything from there on (no copies, no trims).  The draft runs
+// its first step over the two positions L-2, L-1, so it catches up after a full acceptance
+// and after a rejection with the same graph.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "layers.cuh"
+#include "loopguard.h"
+#include "model.h"
+#include "philox.h"
+
+namespace vella {
+namespace {
+
+struct DevState {
+  int L;          // committed positions (prefix + emitted tokens)
+  int P;          // prefix length
+  int pass;       // passes run since the prefill (Philox counter of the oracle draft)
+  int n_new;      // tokens committed by the last pass / step
+  int nonfinite;  // the last verify logits held NaN/Inf
+  int err;        // bit 0 bad token id, bit 1 bad position, bit 2 capacity
+  int ref_len;    // length of the oracle reference
+  int newtok[16];
+};
+
+__global__ void prefill_finish_kernel(DevState* st, int* tok, const int* ys, int* nf, const int* err_t,
+                                      int max_seq) {
+  const int P = st->P, t = ys[0];
+  if (P < max_seq) tok[P] = t; else st->err |= 4;
+  st->L = P + 1;
+  st->n_new = 1;
+  st->newtok[0] = t;
+  st->pass = 0;
+  st->nonfinite = *nf;
+  st->err |= *err_t;
+  *nf = 0;
+}
+
+__global__ void greedy_commit_kernel(DevState* st, int* tok, const int* ys, int* nf, const int* err_t, int max_seq) {
+  const int L = st->L, t = ys[0];
+  if (L < max_seq) tok[L] = t; else st->err |= 4;
+  st->L = L + 1;
+  st->n_new = 1;
+  st->newtok[0] = t;
+  st->nonfinite = *nf;
+  st->err |= *err_t;
+  *nf = 0;
+}
+
+// Draft step i proposes the token at position L + i.
+__global__ void propose_kernel(DevState* st, int* tok, const int* ys_draft, int* nf_draft, int i, int mode, float p,
+                               uint64_t seed, const int* ref, int vocab, int max_seq) {
+  const int pos = st->L + i;
+  int t = ys_draft[0];
+  if (mode == VELLA_DRAFT_ORACLE) {
+    const U4 r = philox4x32_10(U4{(uint32_t)st->pass, (uint32_t)i, 0x0D4A7u, 0u}, (uint32_t)seed,
+                               (uint32_t)(seed >> 32));
+    const int ri = pos - st->P;
+    if (u01(r.x) < p && ri >= 0 && ri < st->ref_len) t = ref[ri];
+    else t = min((int)(u01(r.y) * (float)vocab), vocab - 1);
+  }
+  if (pos < max_seq) tok[pos] = t; else st->err |= 4;
+  *nf_draft = 0;  // the draft's own logits never gate acceptance
+}
+
+// Greedy acceptance over the verify argmax ys[0..K] (ys[j] predicts position L + j).
+__global__ void accept_kernel(DevState* st, int* tok, const int* ys, int K, int* nf, const int* err_t,
+                              const int* err_d, int max_seq) {
+  const int L = st->L;
+  int a = 0;
+  while (a < K && ys[a] == tok[L + a]) ++a;
+  const int bonus = ys[a];
+  if (L + a < max_seq) tok[L + a] = bonus; else st->err |= 4;
+  for (int j = 0; j <= a; ++j) st->newtok[j] = tok[L + j];
+  st->n_new = a + 1;
+  st->L = L + a + 1;
+  st->pass += 1;
+  st->nonfinite = *nf;
+  st->err |= *err_t | *err_d;
+  *nf = 0;
+}
+
+}  // namespace
+
+struct Spec {
+  Model* target = nullptr;
+  Model* draft = nullptr;
+  vella_spec_cfg cfg{};
+  int device = 0;
+  int max_seq = 0;
+  cudaStream_t stream = nullptr;
+  DevState* dstate = nullptr;
+  DevState* hstate = nullptr;  // pinned
+  int* tok = nullptr;          // [max_seq]
+  int* ref = nullptr;          // [max_seq]
+  int P = 0;
+  cudaGraphExec_t pass_exec = nullptr;
+  cudaGraphExec_t greedy_exec = nullptr;
+  bool pass_warm = false, greedy_warm = false;
+  int fault = VELLA_FAULT_NONE;
+  bool draft_disabled = false;
+  std::string failure;
+  vella_spec_stats stats{};
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+};
+
+namespace {
+
+int sync_state(Spec* s) {
+  VELLA_CUDA_TRY(cudaMemcpyAsync(s->hstate, s->dstate, sizeof(DevState), cudaMemcpyDeviceToHost, s->stream));
+  VELLA_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  if (s->hstate->err) return fail(VELLA_E_INVALID, "decode state error flags 0x%x (bad token id, position or capacity)", s->hstate->err);
+  return VELLA_OK;
+}
+
+int enqueue_pass(Spec* s) {
+  Model* t = s->target;
+  Model* d = s->draft;
+  const int K = s->cfg.draft_k;
+  const int* Lp = &s->dstate->L;
+  const int* Pp = &s->dstate->P;
+  int rc;
+  for (int i = 0; i < K; ++i) {
+    const PosRef pr{Lp, i == 0 ? -2 : i - 1};
+    if ((rc = model_forward(d, pr, i == 0 ? 2 : 1, s->tok, Pp, 1, s->stream))) return rc;
+    propose_kernel<<<1, 1, 0, s->stream>>>(s->dstate, s->tok, d->ys, d->nonfinite, i, s->cfg.draft_mode,
+                                           s->cfg.oracle_p, s->cfg.seed, s->ref, t->cfg.vocab, s->max_seq);
+    VELLA_CUDA_TRY(cudaGetLastError());
+  }
+  if ((rc = model_forward(t, PosRef{Lp, -1}, K + 1, s->tok, Pp, K + 1, s->stream))) return rc;
+  accept_kernel<<<1, 1, 0, s->stream>>>(s->dstate, s->tok, t->ys, K, t->nonfinite, t->err, d->err, s->max_seq);
+  VELLA_CUDA_TRY(cudaGetLastError());
+  return VELLA_OK;
+}
+
+int enqueue_greedy(Spec* s) {
+  Model* t = s->target;
+  int rc;
+  if ((rc = model_forward(t, PosRef{&s->dstate->L, -1}, 1, s->tok, &s->dstate->P, 1, s->stream))) return rc;
+  greedy_commit_kernel<<<1, 1, 0, s->stream>>>(s->dstate, s->tok, t->ys, t->nonfinite, t->err, s->max_seq);
+  VELLA_CUDA_TRY(cudaGetLastError());
+  return VELLA_OK;
+}
+
+int capture(Spec* s, int (*enqueue)(Spec*), cudaGraphExec_t* exec) {
+  VELLA_CUDA_TRY(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  const int rc = enqueue(s);
+  cudaGraph_t g = nullptr;
+  const cudaError_t e = cudaStreamEndCapture(s->stream, &g);
+  if (rc != VELLA_OK) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+  const cudaError_t ie = cudaGraphInstantiate(exec, g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) return cuda_fail(ie, "cudaGraphInstantiate");
+  return VELLA_OK;
+}
+
+// Runs one unit of work (pass or greedy step), eagerly the first time (kernel attributes
+// are configured outside capture), then as a replayed graph.
+int run_unit(Spec* s, bool pass) {
+  int rc;
+  bool& warm = pass ? s->pass_warm : s->greedy_warm;
+  cudaGraphExec_t& exec = pass ? s->pass_exec : s->greedy_exec;
+  int (*enqueue)(Spec*) = pass ? enqueue_pass : enqueue_greedy;
+  if (!s->cfg.use_graphs || !warm) {
+    if ((rc = enqueue(s))) return rc;
+    warm = true;
+  } else {
+    if (!exec && (rc = capture(s, enqueue, &exec))) return rc;
+    VELLA_CUDA_TRY(cudaGraphLaunch(exec, s->stream));
+  }
+  return sync_state(s);
+}
+
+int prefill(Spec* s, int* first) {
+  if (s->P < 1) return fail(VELLA_E_INVALID, "prefill: the prefix is empty (vella_spec_set_prefix)");
+  DevState init{};
+  init.P = s->P;
+  init.L = s->P;
+  init.ref_len = s->hstate->ref_len;
+  VELLA_CUDA_TRY(cudaMemcpyAsync(s->dstate, &init, sizeof(DevState), cudaMemcpyHostToDevice, s->stream));
+  const int* Pp = &s->dstate->P;
+  int rc;
+  if (s->draft) {
+    for (int s0 = 0; s0 < s->P; s0 += kMaxRows) {
+      const int rows = std::min(kMaxRows, s->P - s0);
+      if ((rc = model_forward(s->draft, PosRef{s->draft->dzero, s0}, rows, s->tok, Pp, 0, s->stream))) return rc;
+    }
+  }
+  Model* t = s->target;
+  for (int s0 = 0; s0 < s->P; s0 += kMaxRows) {
+    const int rows = std::min(kMaxRows, s->P - s0);
+    const bool last = s0 + rows >= s->P;
+    if ((rc = model_forward(t, PosRef{t->dzero, s0}, rows, s->tok, Pp, last ? 1 : 0, s->stream))) return rc;
+  }
+  prefill_finish_kernel<<<1, 1, 0, s->stream>>>(s->dstate, s->tok, t->ys, t->nonfinite, t->err, s->max_seq);
+  VELLA_CUDA_TRY(cudaGetLastError());
+  if ((rc = sync_state(s))) return rc;
+  *first = s->hstate->newtok[0];
+  return VELLA_OK;
+}
+
+bool is_eos(const Spec* s, int t) {
+  for (int i = 0; i < s->cfg.n_eos && i < 8; ++i)
+    if (s->cfg.eos[i] == t) return true;
+  return false;
+}
+
+struct Decoded {
+  std::vector<int> tokens;
+  bool looped = false;
+  bool capacity = false;
+};
+
+// decodeGreedy (reference :266-290).
+int decode_greedy(Spec* s, int max_tokens, Decoded* out) {
+  int y = 0, rc;
+  if ((rc = prefill(s, &y))) return rc;
+  while ((int)out->tokens.size() < max_tokens) {
+    if (is_eos(s, y)) break;
+    out->tokens.push_back(y);
+    if (ends_in_loop(out->tokens)) {
+      out->looped = true;
+      break;
+    }
+    if ((int)out->tokens.size() >= max_tokens) break;
+    if (s->hstate->L + 1 > s->max_seq) {
+      out->capacity = true;
+      break;
+    }
+    if ((rc = run_unit(s, false))) return rc;
+    s->stats.greedy_steps++;
+    y = s->hstate->newtok[0];
+  }
+  return VELLA_OK;
+}
+
+// decodeMTP (reference :306-396).
+int decode_mtp(Spec* s, int max_tokens, Decoded* out) {
+  int t = 0, rc;
+  if ((rc = prefill(s, &t))) return rc;
+  if (is_eos(s, t) || max_tokens == 0) return VELLA_OK;
+  out->tokens.push_back(t);
+  const int K = s->cfg.draft_k;
+  while ((int)out->tokens.size() < max_tokens) {
+    if (s->hstate->L + K + 1 > s->max_seq) {
+      out->capacity = true;
+      return VELLA_OK;
+    }
+    if ((rc = run_unit(s, true))) return rc;
+    s->stats.passes++;
+    const int n = s->hstate->n_new;
+    if (n >= 1 && n <= 16) s->stats.accepted[n - 1]++;
+    if (s->fault == VELLA_FAULT_THROW) return fail(VELLA_E_INVALID, "injected draft-and-verify fault");
+    if (s->hstate->nonfinite || s->fault == VELLA_FAULT_NONFINITE) return fail(VELLA_E_NONFINITE, "non-finite logits");
+    for (int j = 0; j < n; ++j) {
+      const int tk = s->hstate->newtok[j];
+      if (is_eos(s, tk)) return VELLA_OK;
+      out->tokens.push_back(tk);
+      if ((int)out->tokens.size() >= max_tokens) return VELLA_OK;
+      if (ends_in_loop(out->tokens)) {
+        out->looped = true;
+        return VELLA_OK;
+      }
+    }
+  }
+  return VELLA_OK;
+}
+
+}  // namespace
+}  // namespace vella
+
+using namespace vella;
+
+struct vella_model : Model {};
+struct vella_spec : Spec {};
+
+extern "C" {
+
+int vella_quantize(const vella_qgemm_desc* desc, int32_t src_dtype, const void* w, void* packed, void* scales,
+                   void* biases, vella_stream_t stream) {
+  last_error_slot().clear();
+  if (!desc || !w || !packed || !scales || !biases) return fail(VELLA_E_INVALID, "vella_quantize: NULL argument");
+  const vella_qgemm_desc& d = *desc;
+  if ((d.bits != 4 && d.bits != 8) || d.group_size != 64 || d.n <= 0 || d.k <= 0 || d.k % 64 ||
+      (d.dtype != VELLA_BF16 && d.dtype != VELLA_F16) ||
+      (src_dtype != VELLA_F32 && src_dtype != VELLA_BF16 && src_dtype != VELLA_F16))
+    return fail(VELLA_E_UNSUPPORTED, "vella_quantize: n=%d k=%d bits=%d group=%d dtype=%d src=%d", d.n, d.k, d.bits,
+                d.group_size, d.dtype, src_dtype);
+  if (!aligned(packed, 4) || !aligned(scales, 2) || !aligned(biases, 2) || !aligned(w, src_dtype == VELLA_F32 ? 4 : 2))
+    return fail(VELLA_E_INVALID, "vella_quantize: misaligned pointer");
+  return quantize_device(src_dtype, w, d.dtype, d.bits, d.n, d.k, packed, scales, biases,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int vella_fill_normal(void* out, size_t n, int32_t dtype, uint64_t seed, uint32_t tensor, float mean, float std,
+                      vella_stream_t stream) {
+  last_error_slot().clear();
+  if (!out && n) return fail(VELLA_E_INVALID, "vella_fill_normal: out is NULL");
+  return fill_normal(out, n, dtype, seed, tensor, mean, std, static_cast<cudaStream_t>(stream));
+}
+
+int vella_model_create(const vella_model_cfg* cfg, int32_t device, vella_model** out) {
+  last_error_slot().clear();
+  if (!cfg || !out) return fail(VELLA_E_INVALID, "vella_model_create: NULL argument");
+  Model* m = nullptr;
+  const int rc = model_create(*cfg, device, &m);
+  if (rc) return rc;
+  *out = static_cast<vella_model*>(m);
+  return VELLA_OK;
+}
+
+int vella_model_destroy(vella_model* model) {
+  model_destroy(model);
+  return VELLA_OK;
+}
+
+int vella_model_init_random(vella_model* model, uint64_t seed, float std) {
+  last_error_slot().clear();
+  if (!model) return fail(VELLA_E_INVALID, "vella_model_init_random: NULL model");
+  VELLA_CUDA_TRY(cudaSetDevice(model->device));
+  return model_init_random(model, seed, std, model->stream);
+}
+
+int vella_model_tensor(vella_model* model, const char* name, int32_t layer, void** ptr, size_t* bytes) {
+  last_error_slot().clear();
+  if (!model || !name || !ptr || !bytes) return fail(VELLA_E_INVALID, "vella_model_tensor: NULL argument");
+  return model_tensor(model, name, layer, ptr, bytes);
+}
+
+size_t vella_model_weight_bytes(const vella_model* model) { return model ? model->arena_bytes : 0; }
+
+int vella_model_score(vella_model* m, const void* prefix, int32_t P, const int32_t* tokens, int32_t T,
+                      void* logits_out, int32_t on_host) {
+  last_error_slot().clear();
+  if (!m || !logits_out || (T > 0 && !tokens)) return fail(VELLA_E_INVALID, "vella_model_score: NULL argument");
+  const vella_model_cfg& c = m->cfg;
+  if (P < 1 || P > c.max_prefix || T < 1 || P + T - 1 > c.max_seq)
+    return fail(VELLA_E_INVALID, "vella_model_score: P=%d T=%d (max_prefix %d, max_seq %d)", P, T, c.max_prefix, c.max_seq);
+  VELLA_CUDA_TRY(cudaSetDevice(m->device));
+  cudaStream_t s = m->stream;
+  const size_t row = (size_t)c.d_model * m->elt;
+  if (prefix)
+    VELLA_CUDA_TRY(cudaMemcpyAsync(m->prefix, prefix, (size_t)P * row,
+                                   on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, s));
+  VELLA_CUDA_TRY(cudaMemcpyAsync(m->score_tok + P, tokens, (size_t)T * sizeof(int), cudaMemcpyHostToDevice, s));
+  VELLA_CUDA_TRY(cudaMemcpyAsync(m->score_P, &P, sizeof(int), cudaMemcpyHostToDevice, s));
+  const int last_pos = P + T - 2;  // the last position whose logits are needed
+  const size_t lrow = (size_t)c.vocab * m->elt;
+  int rc;
+  for (int s0 = 0; s0 <= last_pos; s0 += kMaxRows) {
+    const int rows = std::min(kMaxRows, last_pos + 1 - s0);
+    const int first_scored = std::max(s0, P - 1);
+    const int lr = s0 + rows - first_scored;  // rows with position >= P - 1
+    if ((rc = model_forward(m, PosRef{m->dzero, s0}, rows, m->score_tok, m->score_P, std::max(lr, 0), s))) return rc;
+    if (lr > 0) {
+      char* dst = static_cast<char*>(logits_out) + (size_t)(first_scored - (P - 1)) * lrow;
+      VELLA_CUDA_TRY(cudaMemcpyAsync(dst, m->logits, (size_t)lr * lrow,
+                                     on_host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, s));
+    }
+  }
+  VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+  int err = 0;
+  VELLA_CUDA_TRY(cudaMemcpy(&err, m->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) return fail(VELLA_E_INVALID, "vella_model_score: error flags 0x%x (token id out of range?)", err);
+  return VELLA_OK;
+}
+
+int vella_spec_create(vella_model* target, vella_model* draft, const vella_spec_cfg* cfg, vella_spec** out) {
+  last_error_slot().clear();
+  if (!target || !cfg || !out) return fail(VELLA_E_INVALID, "vella_spec_create: NULL argument");
+  if (draft) {
+    if (draft->cfg.vocab != target->cfg.vocab || draft->cfg.dtype != target->cfg.dtype)
+      return fail(VELLA_E_INVALID, "vella_spec_create: draft and target must share vocabulary and dtype");
+    if (draft->cfg.max_seq < target->cfg.max_seq || draft->device != target->device)
+      return fail(VELLA_E_INVALID, "vella_spec_create: the draft needs max_seq >= the target's, on the same device");
+  }
+  if (cfg->draft_k < 1 || cfg->draft_k + 1 > kMaxRows)
+    return fail(VELLA_E_UNSUPPORTED, "vella_spec_create: draft_k %d (1..%d)", cfg->draft_k, kMaxRows - 1);
+  if (cfg->n_eos < 0 || cfg->n_eos > 8) return fail(VELLA_E_INVALID, "vella_spec_create: n_eos %d", cfg->n_eos);
+  VELLA_CUDA_TRY(cudaSetDevice(target->device));
+  vella_spec* s = new vella_spec();
+  s->target = target;
+  s->draft = draft;
+  s->cfg = *cfg;
+  s->device = target->device;
+  s->max_seq = target->cfg.max_seq;
+  int rc = VELLA_OK;
+  auto cuda = [&](cudaError_t e, const char* what) {
+    if (e != cudaSuccess && rc == VELLA_OK) rc = cuda_fail(e, what);
+  };
+  cuda(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  cuda(cudaMalloc(&s->dstate, sizeof(DevState)), "cudaMalloc(state)");
+  cuda(cudaMallocHost(&s->hstate, sizeof(DevState)), "cudaMallocHost(state)");
+  cuda(cudaMalloc(&s->tok, (size_t)s->max_seq * sizeof(int)), "cudaMalloc(tokens)");
+  cuda(cudaMalloc(&s->ref, (size_t)s->max_seq * sizeof(int)), "cudaMalloc(reference)");
+  cuda(cudaEventCreate(&s->ev0), "cudaEventCreate");
+  cuda(cudaEventCreate(&s->ev1), "cudaEventCreate");
+  if (rc == VELLA_OK) {
+    std::memset(s->hstate, 0, sizeof(DevState));
+    cuda(cudaMemset(s->dstate, 0, sizeof(DevState)), "cudaMemset");
+    cuda(cudaMemset(s->tok, 0, (size_t)s->max_seq * sizeof(int)), "cudaMemset");
+  }
+  if (rc != VELLA_OK) {
+    vella_spec_destroy(s);
+    return rc;
+  }
+  *out = s;
+  return VELLA_OK;
+}
+
+int vella_spec_destroy(vella_spec* s) {
+  if (!s) return VELLA_OK;
+  cudaSetDevice(s->device);
+  if (s->stream) cudaStreamSynchronize(s->stream);
+  if (s->pass_exec) cudaGraphExecDestroy(s->pass_exec);
+  if (s->greedy_exec) cudaGraphExecDestroy(s->greedy_exec);
+  if (s->dstate) cudaFree(s->dstate);
+  if (s->hstate) cudaFreeHost(s->hstate);
+  if (s->tok) cudaFree(s->tok);
+  if (s->ref) cudaFree(s->ref);
+  if (s->ev0) cudaEventDestroy(s->ev0);
+  if (s->ev1) cudaEventDestroy(s->ev1);
+  if (s->stream) cudaStreamDestroy(s->stream);
+  delete s;
+  return VELLA_OK;
+}
+
+int vella_spec_set_prefix(vella_spec* s, const void* target_embeds, const void* draft_embeds, int32_t T,
+                          int32_t on_host) {
+  last_error_slot().clear();
+  if (!s) return fail(VELLA_E_INVALID, "vella_spec_set_prefix: NULL spec");
+  if (T < 1 || T > s->target->cfg.max_prefix || (s->draft && T > s->draft->cfg.max_prefix))
+    return fail(VELLA_E_INVALID, "vella_spec_set_prefix: T=%d exceeds max_prefix", T);
+  VELLA_CUDA_TRY(cudaSetDevice(s->device));
+  const cudaMemcpyKind kind = on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+  if (target_embeds)
+    VELLA_CUDA_TRY(cudaMemcpyAsync(s->target->prefix, target_embeds,
+                                   (size_t)T * s->target->cfg.d_model * s->target->elt, kind, s->stream));
+  if (s->draft && draft_embeds)
+    VELLA_CUDA_TRY(cudaMemcpyAsync(s->draft->prefix, draft_embeds,
+                                   (size_t)T * s->draft->cfg.d_model * s->draft->elt, kind, s->stream));
+  VELLA_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  s->P = T;
+  return VELLA_OK;
+}
+
+int vella_spec_set_reference(vella_spec* s, const int32_t* tokens, int32_t n) {
+  last_error_slot().clear();
+  if (!s || (n > 0 && !tokens)) return fail(VELLA_E_INVALID, "vella_spec_set_reference: NULL argument");
+  if (n < 0 || n > s->max_seq) return fail(VELLA_E_INVALID, "vella_spec_set_reference: n=%d", n);
+  VELLA_CUDA_TRY(cudaSetDevice(s->device));
+  if (n) VELLA_CUDA_TRY(cudaMemcpyAsync(s->ref, tokens, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, s->stream));
+  VELLA_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  s->hstate->ref_len = n;
+  return VELLA_OK;
+}
+
+int vella_spec_prefill(vella_spec* s, int32_t* first) {
+  last_error_slot().clear();
+  if (!s || !first) return fail(VELLA_E_INVALID, "vella_spec_prefill: NULL argument");
+  VELLA_CUDA_TRY(cudaSetDevice(s->device));
+  return prefill(s, first);
+}
+
+int vella_spec_step(vella_spec* s, int32_t* out_tokens, int32_t* n_out) {
+  last_error_slot().clear();
+  if (!s || !out_tokens || !n_out) return fail(VELLA_E_INVALID, "vella_spec_step: NULL argument");
+  if (!s->draft) return fail(VELLA_E_UNSUPPORTED, "vella_spec_step: no draft model");
+  if (s->hstate->L < s->P + 1) return fail(VELLA_E_INVALID, "vella_spec_step: prefill first");
+  if (s->hstate->L + s->cfg.draft_k + 1 > s->max_seq) return fail(VELLA_E_INVALID, "vella_spec_step: KV capacity reached");
+  VELLA_CUDA_TRY(cudaSetDevice(s->device));
+  const int rc = run_unit(s, true);
+  if (rc) return rc;
+  s->stats.passes++;
+  const int n = s->hstate->n_new;
+  if (n >= 1 && n <= 16) s->stats.accepted[n - 1]++;
+  *n_out = n;
+  for (int j = 0; j < n; ++j) out_tokens[j] = s->hstate->newtok[j];
+  if (s->hstate->nonfinite) return fail(VELLA_E_NONFINITE, "non-finite logits in the verify pass");
+  return VELLA_OK;
+}
+
+int vella_spec_greedy_step(vella_spec* s, int32_t* out_token) {
+  last_error_slot().clear();
+  if (!s || !out_token) return fail(VELLA_E_INVALID, "vella_spec_greedy_step: NULL argument");
+  if (s->hstate->L < s->P + 1) return fail(VELLA_E_INVALID, "vella_spec_greedy_step: prefill first");
+  if (s->hstate->L + 1 > s->max_seq) return fail(VELLA_E_INVALID, "vella_spec_greedy_step: KV capacity reached");
+  VELLA_CUDA_TRY(cudaSetDevice(s->device));
+  const int rc = run_unit(s, false);
+  if (rc) return rc;
+  s->stats.greedy_steps++;
+  *out_token = s->hstate->newtok[0];
+  if (s->hstate->nonfinite) return fail(VELLA_E_NONFINITE, "non-finite logits");
+  return VELLA_OK;
+}
+
+int vella_spec_decode(vella_spec* s, int32_t mode, int32_t max_tokens, int32_t* out_tokens, int32_t cap,
+                      int32_t* n_out, int32_t* flags) {
+  last_error_slot().clear();
+  if (!s || !n_out || !flags || (cap > 0 && !out_tokens)) return fail(VELLA_E_INVALID, "vella_spec_decode: NULL argument");
+  if (max_tokens < 0) return fail(VELLA_E_INVALID, "vella_spec_decode: max_tokens < 0");
+  VELLA_CUDA_TRY(cudaSetDevice(s->device));
+  *flags = 0;
+  Decoded result;
+  int rc = VELLA_OK;
+  VELLA_CUDA_TRY(cudaEventRecord(s->ev0, s->stream));
+  const bool spec_ok = s->draft != nullptr && !s->draft_disabled;
+  if (mode == VELLA_DECODE_SPEC) {
+    if (!s->draft) return fail(VELLA_E_UNSUPPORTED, "vella_spec_decode: no draft model");
+    rc = decode_mtp(s, max_tokens, &result);
+  } else if (mode == VELLA_DECODE_GREEDY || !spec_ok) {
+    rc = decode_greedy(s, max_tokens, &result);
+    if (rc == VELLA_OK && (int)result.tokens.size() >= max_tokens) result.looped = true;
+  } else {
+    // decode(): draft-and-verify with runaway retry; a runtime failure falls back to greedy, sticky.
+    rc = decode_mtp(s, max_tokens, &result);
+    if (rc == VELLA_OK && (result.looped || (int)result.tokens.size() >= max_tokens)) {
+      s->stats.runaway_retries++;
+      *flags |= VELLA_FLAG_RUNAWAY_RETRY;
+      result = Decoded();
+      rc = decode_greedy(s, max_tokens, &result);
+      if (rc == VELLA_OK && (int)result.tokens.size() >= max_tokens) result.looped = true;
+    } else if (rc != VELLA_OK && rc != VELLA_E_OOM) {
+      s->failure = last_error_slot();
+      s->draft_disabled = true;
+      s->stats.fallbacks++;
+      *flags |= VELLA_FLAG_FELL_BACK;
+      VELLA_CUDA_TRY(cudaStreamSynchronize(s->stream));
+      result = Decoded();
+      last_error_slot().clear();
+      rc = decode_greedy(s, max_tokens, &result);
+      if (rc == VELLA_OK && (int)result.tokens.size() >= max_tokens) result.looped = true;
+    }
+  }
+  VELLA_CUDA_TRY(cudaEventRecord(s->ev1, s->stream));
+  VELLA_CUDA_TRY(cudaEventSynchronize(s->ev1));
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, s->ev0, s->ev1);
+  s->stats.last_decode_ms = ms;
+  if (rc != VELLA_OK) return rc;
+  if (result.looped) *flags |= VELLA_FLAG_LOOPED;
+  if (result.capacity) *flags |= VELLA_FLAG_CAPACITY;
+  const int n = (int)result.tokens.size();
+  *n_out = n;
+  s->stats.last_tokens = n;
+  for (int i = 0; i < std::min(n, cap); ++i) out_tokens[i] = result.tokens[i];
+  return VELLA_OK;
+}
+
+int vella_spec_get_stats(const vella_spec* s, vella_spec_stats* out) {
+  if (!s || !out) return fail(VELLA_E_INVALID, "vella_spec_get_stats: NULL argument");
+  *out = s->stats;
+  out->draft_disabled = s->draft_disabled ? 1 : 0;
+  return VELLA_OK;
+}
+
+int vella_spec_set_fault(vella_spec* s, int32_t fault) {
+  if (!s) return fail(VELLA_E_INVALID, "vella_spec_set_fault: NULL spec");
+  s->fault = fault;
+  return VELLA_OK;
+}
+
+int vella_spec_reset(vella_spec* s) {
+  if (!s) return fail(VELLA_E_INVALID, "vella_spec_reset: NULL spec");
+  s->draft_disabled = false;
+  s->failure.clear();
+  s->stats = vella_spec_stats{};
+  return VELLA_OK;
+}
+
+}  // extern "C"
