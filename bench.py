@@ -1,4 +1,4 @@
-"""Benchmark of the int4 decode path on B200.
+"""Benchmark of the int4 draft-and-verify decode path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload spec|gemm] [--impl vella|reference]
 
@@ -220,21 +220,327 @@ def run_gemm(args, rank, world):
     return line
 
 
+# ---------------------------------------------------------------------------------------
+# 30B-class int4 draft-and-verify (the headline)
+# ---------------------------------------------------------------------------------------
+
+TARGET = dict(n_layers=64, d_model=5120, n_heads=40, n_kv_heads=8, head_dim=128, ffn=25600, vocab=151936, bits=4)
+DRAFT = dict(n_layers=28, d_model=2048, n_heads=16, n_kv_heads=8, head_dim=128, ffn=6144, vocab=151936, bits=0)
+PREFIX, NEW_TOKENS = 750, 448
+SWEEP = [(4, 0.5), (4, 0.7), (4, 0.9), (8, 0.5), (8, 0.7), (8, 0.9)]
+HEADLINE = (4, 0.7)
+
+
+def expected_tokens_per_pass(k, p):
+    return (1 - p ** (k + 1)) / (1 - p)
+
+
+def dist_setup(world):
+    if world <= 1:
+        return None
+    import datetime
+    import torch.distributed as dist
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    return dist
+
+
+def dist_max(dist, value, dev):
+    if dist is None:
+        return value
+    import torch
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def verify_gemm_roofline(target, k, dev, reps=3):
+    """Replays the target's verify GEMMs (all 64 layers + LM head, M = k+1) in a CUDA graph on
+    one stream and times them with CUDA events: the dominant kernel's achieved HBM rate."""
+    import torch
+    from vella_b200 import smallm as S
+    from vella_b200 import _lib as L
+
+    class Dev:
+        def __init__(self, ptr, n):
+            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i4", "data": (ptr, False), "version": 3}
+
+    def view(name, layer, dtype, shape):
+        ptr, nbytes = target.tensor(name, layer)
+        t = torch.as_tensor(Dev(ptr, nbytes // 4), device=dev)
+        return t.view(dtype).view(*shape)
+
+    c = TARGET
+    d, H, KV, hd, F, V = c["d_model"], c["n_heads"], c["n_kv_heads"], c["head_dim"], c["ffn"], c["vocab"]
+    m = k + 1
+
+    def qw(name, layer, n, kk):
+        return S.Weights(view(f"{name}.w", layer, torch.int32, (n, kk // 8)),
+                         view(f"{name}.s", layer, torch.bfloat16, (n, kk // 64)),
+                         view(f"{name}.b", layer, torch.bfloat16, (n, kk // 64)), 4)
+
+    calls, nbytes = [], 0
+    xs = {kk: torch.randn(m, kk, device=dev).to(torch.bfloat16) for kk in (d, H * hd, F)}
+    outs = {n: torch.empty(m, n, device=dev, dtype=torch.bfloat16) for n in (d, (H + 2 * KV) * hd, F, V)}
+    for layer in range(c["n_layers"]):
+        for name, n, kk, epi in (("qkv", (H + 2 * KV) * hd, d, "none"), ("o", d, H * hd, "residual"),
+                                 ("gate", F, d, "siluGate"), ("down", d, F, "residual")):
+            w = qw(name, layer, n, kk)
+            up = qw("up", layer, F, d) if epi == "siluGate" else None
+            calls.append((w, kk, n, epi, up))
+            nbytes += gemm_bytes(m, n, kk, 4) * (2 if up is not None else 1)
+    calls.append((qw("lm_head", -1, V, d), d, V, "none", None))
+    nbytes += gemm_bytes(m, V, d, 4)
+    ws_bytes = max(S.workspace_size(m, n, kk, torch.bfloat16, 4, epi) for _, kk, n, epi, _ in calls)
+    ws = torch.zeros(max(ws_bytes, 256) // 4 + 64, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def run():
+        for w, kk, n, epi, up in calls:
+            res = outs[n] if epi == "residual" else None
+            S.matmul(xs[kk], w, epilogue=epi, residual=res, up=up, out=outs[n], workspace=ws)
+
+    with torch.cuda.stream(stream):
+        run()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        run()
+    with torch.cuda.stream(stream):
+        g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    return {"bytes_per_pass": nbytes, "ms_per_pass": ms, "gbs": nbytes / ms / 1e6, "launches": len(calls)}
+
+
+def run_spec(args, rank, world):
+    import torch
+    from vella_b200 import _lib as L
+    from vella_b200 import decode as VD
+    dist = dist_setup(world)
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    hbm, _, peak_kind = peaks()
+    max_seq = PREFIX + NEW_TOKENS + 64
+    tc = VD.ModelConfig(**TARGET, max_seq=max_seq, max_prefix=PREFIX, rope_theta=1e6)
+    dc = VD.ModelConfig(**DRAFT, max_seq=max_seq, max_prefix=PREFIX, rope_theta=1e6)
+    t0 = time.time()
+    target = VD.Model(tc, local)
+    target.init_random(1, 0.02)   # the same random-init replica on every GPU
+    draft = VD.Model(dc, local)
+    draft.init_random(2, 0.02)
+    init_s = time.time() - t0
+    # each GPU decodes its own stream: prefix embeddings ~N(0, 1) seeded by rank
+    fill = L.lib().vella_fill_normal
+    for m, dd, tid in ((target, TARGET["d_model"], 11), (draft, DRAFT["d_model"], 12)):
+        ptr, _ = m.tensor("prefix")
+        L.check(fill(ptr, PREFIX * dd, L.BF16, 3 + rank, tid, 0.0, 1.0, None))
+    torch.cuda.synchronize()
+
+    # plain greedy decode: the reference continuation of the oracle draft, and the baseline
+    sd = VD.SpecDecoder(target, draft, k=HEADLINE[0], mode=VD.DRAFT_ORACLE, oracle_p=HEADLINE[1], seed=7 + rank)
+    sd.set_prefix(None, None, PREFIX)
+    greedy = sd.decode_greedy(NEW_TOKENS + 16)
+    ref = greedy.tokens
+    greedy_tps = (len(ref) - 1) / (greedy.ms / 1e3)  # the first token comes from the prefill
+    sweep = []
+    for (k, p) in SWEEP:
+        s2 = VD.SpecDecoder(target, draft, k=k, mode=VD.DRAFT_ORACLE, oracle_p=p, seed=7 + rank)
+        s2.set_prefix(None, None, PREFIX)
+        s2.set_reference(ref)
+        r = s2.decode_mtp(NEW_TOKENS)
+        exact = r.tokens == ref[:NEW_TOKENS]
+        st = r.stats
+        sweep.append({"k": k, "p": p, "tokens_per_s": round((len(r.tokens) - 1) / (r.ms / 1e3), 1),
+                      "passes": st["passes"], "tokens_per_pass": round((len(r.tokens) - 1) / max(st["passes"], 1), 3),
+                      "expected_tokens_per_pass": round(expected_tokens_per_pass(k, p), 3),
+                      "accepted_hist": st["accepted"][:k + 1], "bit_exact_vs_greedy": exact,
+                      "decode_ms": round(r.ms, 2), "prefill_ms": round(st["last_prefill_ms"], 2)})
+        s2.close()
+
+    # headline: K=4, p=0.7, timed `steps` decodes after `warmup`
+    k, p = HEADLINE
+    sd.close()
+    sd = VD.SpecDecoder(target, draft, k=k, mode=VD.DRAFT_ORACLE, oracle_p=p, seed=7 + rank)
+    sd.set_prefix(None, None, PREFIX)
+    sd.set_reference(ref)
+    for _ in range(args.warmup):
+        sd.decode_mtp(NEW_TOKENS)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    decode_ms, tokens, passes = 0.0, 0, 0
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            r = sd.decode_mtp(NEW_TOKENS)
+            decode_ms += r.ms
+            tokens += len(r.tokens) - 1
+            passes += r.stats["passes"]
+            exact = r.tokens == ref[:NEW_TOKENS]
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    decode_ms = dist_max(dist, decode_ms, dev)
+    value = tokens * world / (decode_ms / 1e3)
+
+    # end to end through the public API: host (pinned) prefix -> device, prefill, decode, tokens -> host
+    # (the host copy holds the same prefix, so the reference continuation still applies)
+    class DevView:
+        def __init__(self, ptr, n):
+            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i2", "data": (ptr, False), "version": 3}
+
+    def host_prefix(model, dd):
+        ptr, _ = model.tensor("prefix")
+        return torch.as_tensor(DevView(ptr, PREFIX * dd), device=dev).cpu().pin_memory()
+
+    pin_t, pin_d = host_prefix(target, TARGET["d_model"]), host_prefix(draft, DRAFT["d_model"])
+    se = VD.SpecDecoder(target, draft, k=k, mode=VD.DRAFT_ORACLE, oracle_p=p, seed=7 + rank)
+    se.set_reference(ref)
+    e2e_s, e2e_tokens = 0.0, 0
+    for it in range(max(1, args.steps)):
+        w0 = time.perf_counter()
+        L.check(L.lib().vella_spec_set_prefix(se.handle, pin_t.data_ptr(), pin_d.data_ptr(), PREFIX, 1))
+        r = se.decode(NEW_TOKENS, VD.DECODE_SPEC)
+        e2e_s += time.perf_counter() - w0
+        e2e_tokens += len(r.tokens)
+    e2e_s = dist_max(dist, e2e_s, dev)
+    h2d = PREFIX * (TARGET["d_model"] + DRAFT["d_model"]) * 2
+    d2h = NEW_TOKENS * 4
+
+    roof = verify_gemm_roofline(target, k, dev)
+    launches_per_pass = k * (1 + 8 * DRAFT["n_layers"] + 3 + 1) + (1 + 8 * TARGET["n_layers"] + 3) + 1
+    weights_gb = (target.weight_bytes() + draft.weight_bytes()) / 1e9
+    line = {
+        "metric": "int4 draft-verify tokens/s/GPU (30B-class target, K=4, acceptance p=0.7)",
+        "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(decode_ms / args.steps, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u4 weights x bf16 activations (draft bf16)", "data": "synthetic",
+        "config": {"workload": "30B-class int4 target (64L d5120 GQA40/8x128 FFN25600 V151936, g64 bf16 scale/bias) "
+                               "+ bf16 draft (28L d2048 16/8x128 FFN6144); 750-position ~N(0,1) prefix; 448 tokens; "
+                               "oracle draft; 1 stream per GPU; step = one 448-token decode after the prefill",
+                   "k": k, "p": p, "streams_per_gpu": 1, "l2": f"weights {weights_gb:.1f} GB >> 126 MB L2"},
+        "bit_exact_vs_greedy": exact,
+        "greedy_tokens_per_s": round(greedy_tps, 1),
+        "tokens_per_pass": round(tokens / max(passes, 1), 3),
+        "sweep": sweep,
+        "e2e": {"value": round(e2e_tokens * world / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "includes": "prefix H2D from pinned memory, prefill, decode, token D2H"},
+        "roofline": {"bound": "hbm", "achieved": round(roof["gbs"], 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(roof["gbs"] / hbm, 3), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": f"qgemm int4 at M={k + 1}: the verify pass's {roof['launches']} GEMM launches "
+                               f"({roof['bytes_per_pass'] / 1e9:.2f} GB algorithmic) replayed in a graph",
+                     "verify_gemm_ms": round(roof["ms_per_pass"], 3)},
+        "clocks": clk.summary(),
+        "gpu_launches": passes * launches_per_pass,
+        "init_s": round(init_s, 1),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(k, p)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return line
+
+
+# ---------------------------------------------------------------------------------------
+# CPU baseline: the oracle's C restatement of the same pass, timed on the host cores
+# ---------------------------------------------------------------------------------------
+
+def cpu_pass_seconds(k, layers_sampled=1):
+    """Times one target layer's verify GEMMs (M=k+1), one draft layer step (M=1) and both LM
+    heads with the oracle's C GEMM (OpenMP); extrapolates a whole pass."""
+    import numpy as np
+    from oracle import cgemm as C
+    rng = np.random.default_rng(0)
+    m = k + 1
+
+    def q(n, kk):
+        return (rng.integers(0, 2 ** 32, size=(n, kk // 8), dtype=np.uint32),
+                np.full((n, kk // 64), 0x3C00, np.uint16), np.full((n, kk // 64), 0xBC00, np.uint16))
+
+    c, d = TARGET, DRAFT
+    t_shapes = [((c["n_heads"] + 2 * c["n_kv_heads"]) * c["head_dim"], c["d_model"]), (c["d_model"], c["n_heads"] * c["head_dim"]),
+                (c["ffn"], c["d_model"]), (c["ffn"], c["d_model"]), (c["d_model"], c["ffn"])]
+    t_layer = 0.0
+    for n, kk in t_shapes:
+        w = q(n, kk)
+        x = rng.standard_normal((m, kk)).astype(np.float32)
+        s0 = time.perf_counter()
+        C.qgemm(x, *w, 4)
+        t_layer += time.perf_counter() - s0
+    wl = q(c["vocab"] // 8, c["d_model"])
+    s0 = time.perf_counter()
+    C.qgemm(rng.standard_normal((m, c["d_model"])).astype(np.float32), *wl, 4)
+    t_lm = (time.perf_counter() - s0) * 8
+    d_shapes = [((d["n_heads"] + 2 * d["n_kv_heads"]) * d["head_dim"], d["d_model"]), (d["d_model"], d["n_heads"] * d["head_dim"]),
+                (d["ffn"], d["d_model"]), (d["ffn"], d["d_model"]), (d["d_model"], d["ffn"])]
+    d_layer = 0.0
+    for n, kk in d_shapes:
+        w = (rng.integers(0, 2 ** 16, size=(n, kk), dtype=np.uint16) & 0x3FFF)
+        x = rng.standard_normal((1, kk)).astype(np.float32)
+        s0 = time.perf_counter()
+        C.gemm_dense(x, w)
+        d_layer += time.perf_counter() - s0
+    wd = rng.integers(0, 2 ** 16, size=(d["vocab"] // 8, d["d_model"]), dtype=np.uint16) & 0x3FFF
+    s0 = time.perf_counter()
+    C.gemm_dense(rng.standard_normal((1, d["d_model"])).astype(np.float32), wd)
+    d_lm = (time.perf_counter() - s0) * 8
+    per_pass = c["n_layers"] * t_layer + t_lm + k * (d["n_layers"] * d_layer + d_lm)
+    return per_pass, C.threads()
+
+
+def cpu_baseline(k, p):
+    per_pass, threads = cpu_pass_seconds(k)
+    tps = expected_tokens_per_pass(k, p) / per_pass
+    return {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"C/OpenMP oracle GEMMs of 1 target layer (M={k + 1}), 1 draft layer (M=1) and 1/8 of each "
+                      f"LM head timed once, extrapolated to one pass (64+{k}x28 layers, both heads) and to "
+                      f"E[tokens/pass]={expected_tokens_per_pass(k, p):.2f}; attention and norms not counted"}
+
+
+def run_reference(args, rank, world):
+    """The reference's own CPU path cannot run here (Swift + MLX on Apple Silicon); its CPU
+    restatement (the oracle's C GEMMs) is timed instead on the same config."""
+    k, p = HEADLINE
+    for _ in range(args.warmup):
+        cpu_pass_seconds(k)
+    total, threads = 0.0, 1
+    for _ in range(args.steps):
+        s, threads = cpu_pass_seconds(k)
+        total += s
+    per_pass = total / max(args.steps, 1)
+    tps = expected_tokens_per_pass(k, p) / per_pass
+    sample = (f"one draft-and-verify pass per step (64 target layers at M={k + 1}, {k} draft steps of 28 layers, "
+              f"both LM heads) extrapolated from 1 timed layer each, C/OpenMP oracle GEMMs")
+    return {"impl": "reference", "metric": "int4 draft-verify tokens/s/GPU (30B-class target, K=4, acceptance p=0.7)",
+            "value": round(tps, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4 x fp32 (CPU)",
+            "data": "synthetic", "config": {"workload": "30B-class int4 target + bf16 draft, K=4, p=0.7 (CPU restatement)"},
+            "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": round(tps, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="gemm", choices=["gemm"])
+    ap.add_argument("--workload", default="spec", choices=["spec", "gemm"])
     ap.add_argument("--impl", default="vella", choices=["vella", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": "reference arm not wired yet"}))
+            print(json.dumps(run_reference(args, rank, world)))
         return
-    line = run_gemm(args, rank, world)
+    line = run_gemm(args, rank, world) if args.workload == "gemm" else run_spec(args, rank, world)
     if rank == 0:
         print(json.dumps(line))
 

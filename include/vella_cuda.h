@@ -88,7 +88,8 @@ VELLA_API size_t vella_qgemm_workspace_size(const vella_qgemm_desc* desc);
  * `bias` only for the bias epilogues, `residual` only for the residual epilogues.
  * `workspace`: device memory of at least vella_qgemm_workspace_size bytes, 256-byte
  * aligned, zero-filled before its first use (every completed call leaves its counter words
- * zero again), used by one stream at a time.  NULL selects a per-device workspace owned
+ * zero again), used by one stream at a time; calls of different shapes may share it (the
+ * counters occupy a fixed 128 KiB region at its front).  NULL selects a per-device workspace owned
  * by the library: it is allocated or grown by the first call that needs more, so that
  * call must not be inside CUDA graph capture; a grown workspace keeps the old buffer
  * alive, so graphs captured earlier stay valid, but they all share one buffer and must
@@ -204,8 +205,9 @@ typedef struct vella_spec_stats {
   int64_t fallbacks;       /* runtime failures -> greedy (sticky) */
   int64_t runaway_retries; /* looping draft-and-verify runs decoded again greedy */
   int32_t draft_disabled;  /* sticky fallback in force */
-  float last_decode_ms;    /* device time of the last vella_spec_decode */
+  float last_decode_ms;    /* device time of the last vella_spec_decode after its prefill */
   int32_t last_tokens;
+  float last_prefill_ms;   /* device time of the last prefill */
 } vella_spec_stats;
 
 typedef struct vella_spec vella_spec;

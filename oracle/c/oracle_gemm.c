@@ -1,0 +1,80 @@
+/*
+ * CPU restatement of the MLX-affine small-M GEMM (test and CPU-baseline infrastructure only;
+ * the library never links it).
+ *
+ * Follows Worker/Sources/SmallMGEMM/SmallMGEMM.swift:662-755 (smallm_gemv_affine): per group
+ * of 64 along K, acc += scale * sum(x * q) + bias * sum(x), fp32 accumulation; codes are
+ * packed low bits first in uint32 words (:658-661).  Dense rows (bf16 bit patterns) follow
+ * the dense GEMV (:585-656).  Parallel over output rows with OpenMP; x and the results are
+ * fp32 (the caller rounds).
+ */
+#include <stdint.h>
+#include <string.h>
+
+static inline float bf16_to_f32(uint16_t v) {
+  uint32_t u = (uint32_t)v << 16;
+  float f;
+  memcpy(&f, &u, sizeof f);
+  return f;
+}
+
+/* out[M, N] = x[M, K] . W^T, W MLX-affine (bits 4 | 8), scales/biases as bf16 bits. */
+void oracle_qgemm_bf16(int M, int N, int K, int bits, const float* x, const uint32_t* w, const uint16_t* scales,
+                       const uint16_t* biases, float* out) {
+  const int G = K / 64, per = 32 / bits, wpr = K / per;
+  const uint32_t mask = (1u << bits) - 1u;
+  /* per-row group sums of x, shared by all output rows */
+  float xs[16 * 1024];
+  float* xsum = (M * G <= 16 * 1024) ? xs : 0;
+  if (!xsum) return;
+  for (int m = 0; m < M; ++m)
+    for (int g = 0; g < G; ++g) {
+      float s = 0.0f;
+      for (int k = 0; k < 64; ++k) s += x[(size_t)m * K + g * 64 + k];
+      xsum[m * G + g] = s;
+    }
+#pragma omp parallel for schedule(static)
+  for (int n = 0; n < N; ++n) {
+    float acc[16];
+    for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+    const uint32_t* row = w + (size_t)n * wpr;
+    for (int g = 0; g < G; ++g) {
+      float q[64];
+      for (int i = 0; i < 64 / per; ++i) {
+        const uint32_t word = row[g * (64 / per) + i];
+        for (int j = 0; j < per; ++j) q[i * per + j] = (float)((word >> (bits * j)) & mask);
+      }
+      const float s = bf16_to_f32(scales[(size_t)n * G + g]), b = bf16_to_f32(biases[(size_t)n * G + g]);
+      for (int m = 0; m < M; ++m) {
+        const float* xr = x + (size_t)m * K + g * 64;
+        float d = 0.0f;
+        for (int k = 0; k < 64; ++k) d += xr[k] * q[k];
+        acc[m] += s * d + b * xsum[m * G + g];
+      }
+    }
+    for (int m = 0; m < M; ++m) out[(size_t)m * N + n] = acc[m];
+  }
+}
+
+/* out[M, N] = x[M, K] . W^T, W dense bf16 bits [N, K]. */
+void oracle_gemm_dense_bf16(int M, int N, int K, const float* x, const uint16_t* w, float* out) {
+#pragma omp parallel for schedule(static)
+  for (int n = 0; n < N; ++n) {
+    const uint16_t* row = w + (size_t)n * K;
+    for (int m = 0; m < M; ++m) {
+      const float* xr = x + (size_t)m * K;
+      float d = 0.0f;
+      for (int k = 0; k < K; ++k) d += xr[k] * bf16_to_f32(row[k]);
+      out[(size_t)m * N + n] = d;
+    }
+  }
+}
+
+int oracle_threads(void) {
+#ifdef _OPENMP
+  extern int omp_get_max_threads(void);
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}

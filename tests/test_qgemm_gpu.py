@@ -145,6 +145,31 @@ def test_writes_stay_inside_output_and_workspace_is_reusable():
     assert_close(host(r1), ref, "bf16")
 
 
+def test_workspace_shared_across_shapes():
+    """A GEMM with many split-K row blocks (counters past the first 256 bytes) alternating on
+    one workspace with a GEMM of few row blocks (partials early in the workspace): neither
+    corrupts the other's ticket counters."""
+    S = smallm()
+    rng = np.random.default_rng(21)
+    shapes = [(20000, 2048), (256, 4096), (7168, 5120)]
+    mats = []
+    for n, k in shapes:
+        p = rng.integers(0, 2 ** 32, size=(n, k // 8), dtype=np.uint32)
+        sc = A.to_storage((0.005 * (0.5 + rng.random((n, k // 64)))).astype(np.float32), "bf16")
+        bi = A.to_storage((-0.04 * (0.5 + rng.random((n, k // 64)))).astype(np.float32), "bf16")
+        x = A.to_storage(rng.standard_normal((5, k)).astype(np.float32), "bf16")
+        mats.append((p, sc, bi, x, S.Weights(dev(p), dev(sc), dev(bi), 4), dev(x)))
+    need = max(S.workspace_size(5, n, k, torch.bfloat16, 4) for n, k in shapes)
+    assert all(S.workspace_size(5, n, k, torch.bfloat16, 4) > 0 for n, k in shapes)
+    ws = torch.zeros(need // 4 + 64, dtype=torch.int32, device="cuda")
+    refs = [A.qgemm(x, p, sc, bi, bits=4) for p, sc, bi, x, _, _ in mats]
+    for rnd in range(3):
+        for (p, sc, bi, x, w, xd), ref in zip(mats, refs):
+            out = S.matmul(xd, w, workspace=ws)
+            torch.cuda.synchronize()
+            assert_close(host(out), ref, "bf16")
+
+
 def test_empty_batch_and_unsupported():
     S = smallm()
     p, sc, bi = A.quantize(np.zeros((64, 512), np.float32), 4)

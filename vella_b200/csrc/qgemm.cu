@@ -46,6 +46,15 @@ constexpr int kSlots = 128;  // weight rows per CTA (gate: 64 gate + 64 up)
 constexpr int kKCMax = 32;
 constexpr int kTokMax = 16;  // tokens per pass (z chunk)
 constexpr int kAccStride = kSlots + 4;
+// The ticket counters sit at the front of the workspace in a region of this fixed size
+// (32768 counters), and the fp32 partials after it, so that calls of different shapes can
+// share one workspace: no shape's partials ever overwrite another shape's counters.
+constexpr size_t kCounterRegion = size_t(128) << 10;
+
+size_t counter_region(size_t counters) {
+  const size_t bytes = (counters * sizeof(int) + 255) / 256 * 256;
+  return bytes > kCounterRegion ? bytes : kCounterRegion;
+}
 
 struct Args {
   const void* x;
@@ -435,8 +444,7 @@ bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* p) {
   p->zchunks = std::max(1, (d.m + kTokMax - 1) / kTokMax);
   if (p->splits > 1) {
     const size_t part = (size_t)p->zchunks * p->splits * kTokMax * (size_t)p->rowblocks * kSlots * sizeof(float);
-    const size_t ctr = (size_t)p->zchunks * p->rowblocks * sizeof(int);
-    p->workspace = ((ctr + 255) / 256) * 256 + part;
+    p->workspace = counter_region((size_t)p->zchunks * p->rowblocks) + part;
   } else {
     p->workspace = 0;
   }
@@ -456,9 +464,8 @@ int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& p, const void* x, c
   a.has_bias = d.epilogue == VELLA_EPI_BIAS || d.epilogue == VELLA_EPI_BIAS_RESIDUAL;
   a.has_res = d.epilogue == VELLA_EPI_RESIDUAL || d.epilogue == VELLA_EPI_BIAS_RESIDUAL;
   if (p.splits > 1) {
-    const size_t ctr = (size_t)p.zchunks * p.rowblocks * sizeof(int);
     a.counters = static_cast<int*>(ws);
-    a.partial = reinterpret_cast<float*>(static_cast<char*>(ws) + ((ctr + 255) / 256) * 256);
+    a.partial = reinterpret_cast<float*>(static_cast<char*>(ws) + counter_region((size_t)p.zchunks * p.rowblocks));
   }
   const bool gate = d.epilogue == VELLA_EPI_SILU_GATE;
   const int nt = d.m <= 8 ? 1 : 2;

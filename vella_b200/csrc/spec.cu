@@ -124,7 +124,7 @@ struct Spec {
   bool draft_disabled = false;
   std::string failure;
   vella_spec_stats stats{};
-  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr, evp = nullptr;  // decode start, end, prefill end
 };
 
 namespace {
@@ -221,6 +221,7 @@ int prefill(Spec* s, int* first) {
   }
   prefill_finish_kernel<<<1, 1, 0, s->stream>>>(s->dstate, s->tok, t->ys, t->nonfinite, t->err, s->max_seq);
   VELLA_CUDA_TRY(cudaGetLastError());
+  VELLA_CUDA_TRY(cudaEventRecord(s->evp, s->stream));
   if ((rc = sync_state(s))) return rc;
   *first = s->hstate->newtok[0];
   return VELLA_OK;
@@ -422,6 +423,7 @@ int vella_spec_create(vella_model* target, vella_model* draft, const vella_spec_
   cuda(cudaMalloc(&s->ref, (size_t)s->max_seq * sizeof(int)), "cudaMalloc(reference)");
   cuda(cudaEventCreate(&s->ev0), "cudaEventCreate");
   cuda(cudaEventCreate(&s->ev1), "cudaEventCreate");
+  cuda(cudaEventCreate(&s->evp), "cudaEventCreate");
   if (rc == VELLA_OK) {
     std::memset(s->hstate, 0, sizeof(DevState));
     cuda(cudaMemset(s->dstate, 0, sizeof(DevState)), "cudaMemset");
@@ -447,6 +449,7 @@ int vella_spec_destroy(vella_spec* s) {
   if (s->ref) cudaFree(s->ref);
   if (s->ev0) cudaEventDestroy(s->ev0);
   if (s->ev1) cudaEventDestroy(s->ev1);
+  if (s->evp) cudaEventDestroy(s->evp);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
   return VELLA_OK;
@@ -561,9 +564,11 @@ int vella_spec_decode(vella_spec* s, int32_t mode, int32_t max_tokens, int32_t* 
   }
   VELLA_CUDA_TRY(cudaEventRecord(s->ev1, s->stream));
   VELLA_CUDA_TRY(cudaEventSynchronize(s->ev1));
-  float ms = 0.0f;
-  cudaEventElapsedTime(&ms, s->ev0, s->ev1);
+  float ms = 0.0f, pms = 0.0f;
+  cudaEventElapsedTime(&pms, s->ev0, s->evp);
+  cudaEventElapsedTime(&ms, s->evp, s->ev1);
   s->stats.last_decode_ms = ms;
+  s->stats.last_prefill_ms = pms;
   if (rc != VELLA_OK) return rc;
   if (result.looped) *flags |= VELLA_FLAG_LOOPED;
   if (result.capacity) *flags |= VELLA_FLAG_CAPACITY;

@@ -40,7 +40,7 @@ class SpecStats(ctypes.Structure):
     _fields_ = [("passes", ctypes.c_int64), ("greedy_steps", ctypes.c_int64), ("accepted", ctypes.c_int64 * 16),
                 ("fallbacks", ctypes.c_int64), ("runaway_retries", ctypes.c_int64),
                 ("draft_disabled", ctypes.c_int32), ("last_decode_ms", ctypes.c_float),
-                ("last_tokens", ctypes.c_int32)]
+                ("last_tokens", ctypes.c_int32), ("last_prefill_ms", ctypes.c_float)]
 
 
 _vp, _i32, _pi32 = ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)
@@ -214,7 +214,7 @@ class SpecDecoder:
         return {"passes": s.passes, "greedy_steps": s.greedy_steps, "accepted": list(s.accepted),
                 "fallbacks": s.fallbacks, "runaway_retries": s.runaway_retries,
                 "draft_disabled": bool(s.draft_disabled), "last_decode_ms": s.last_decode_ms,
-                "last_tokens": s.last_tokens}
+                "last_tokens": s.last_tokens, "last_prefill_ms": s.last_prefill_ms}
 
     def set_fault(self, fault: int):
         _lib.check(_lib.lib().vella_spec_set_fault(self.handle, fault))
