@@ -51,7 +51,19 @@ struct QgemmPlan {
   int splits;     // CTAs along K
   int zchunks;    // ceil(M / 16)
   size_t workspace;
+  bool stream = false;  // persistent bulk-copy kernel (qgemm_stream.cu)
+  int ctas = 0;         // its grid (one CTA per SM)
 };
+
+// qgemm_stream.cu
+bool stream_eligible(const vella_qgemm_desc& d);
+int stream_units(const vella_qgemm_desc& d, int* rowblocks, int* nkc);
+size_t stream_partial_bytes(int P);
+int stream_launch(const vella_qgemm_desc& d, int P, const void* x, const void* w, const void* scales,
+                  const void* biases, const void* up_w, const void* up_scales, const void* up_biases,
+                  const void* bias, const void* residual, void* out, int* counters, float* partial,
+                  cudaStream_t stream);
+int stream_fault_status(int clear);
 
 bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* plan);
 

@@ -442,6 +442,22 @@ bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* p) {
   p->kc = kc;
   p->splits = (G + kc - 1) / kc;
   p->zchunks = std::max(1, (d.m + kTokMax - 1) / kTokMax);
+  p->stream = false;
+  if (stream_eligible(d)) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+      cudaGetLastError();
+      dev = -1;
+    }
+    int rb = 0, nkc = 0;
+    stream_units(d, &rb, &nkc);
+    p->stream = true;
+    // one CTA per SM, but never more CTAs than units: every CTA owns at least one unit
+    p->ctas = (int)std::min<long long>(num_sms(dev), (long long)rb * nkc);
+    p->rowblocks = rb;
+    p->workspace = counter_region((size_t)rb) + stream_partial_bytes(p->ctas);
+    return true;
+  }
   if (p->splits > 1) {
     const size_t part = (size_t)p->zchunks * p->splits * kTokMax * (size_t)p->rowblocks * kSlots * sizeof(float);
     p->workspace = counter_region((size_t)p->zchunks * p->rowblocks) + part;
@@ -456,6 +472,12 @@ int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& p, const void* x, c
                  const void* up_biases, const void* bias, const void* residual, void* out, void* ws,
                  cudaStream_t stream) {
   if (d.m == 0 || d.n == 0) return VELLA_OK;
+  if (p.stream) {
+    int* counters = static_cast<int*>(ws);
+    float* partial = reinterpret_cast<float*>(static_cast<char*>(ws) + counter_region((size_t)p.rowblocks));
+    return stream_launch(d, p.ctas, x, w, scales, biases, up_w, up_scales, up_biases, bias, residual, out, counters,
+                         partial, stream);
+  }
   Args a{};
   a.x = x; a.w = static_cast<const uint32_t*>(w); a.sc = scales; a.bi = biases;
   a.uw = static_cast<const uint32_t*>(up_w); a.usc = up_scales; a.ubi = up_biases;
