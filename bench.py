@@ -235,12 +235,14 @@ def expected_tokens_per_pass(k, p):
     return (1 - p ** (k + 1)) / (1 - p)
 
 
-def dist_setup(world):
+def dist_setup(world, backend="nccl"):
+    """One process per GPU; the process group only carries the barrier and the max-over-ranks
+    of the timings (the decode path itself has no collective: every GPU owns whole streams)."""
     if world <= 1:
         return None
     import datetime
     import torch.distributed as dist
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
     return dist
 
 
@@ -251,6 +253,11 @@ def dist_max(dist, value, dev):
     t = torch.tensor([value], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def weak_scaling_value(units_per_rank, world, seconds_max):
+    """Whole-job throughput: the units all ranks processed over the slowest rank's time."""
+    return units_per_rank * world / seconds_max
 
 
 def verify_gemm_roofline(target, k, dev, reps=3):
@@ -386,7 +393,7 @@ def run_spec(args, rank, world):
     if dist:
         dist.barrier()
     decode_ms = dist_max(dist, decode_ms, dev)
-    value = tokens * world / (decode_ms / 1e3)
+    value = weak_scaling_value(tokens, world, decode_ms / 1e3)
 
     # end to end through the public API: host (pinned) prefix -> device, prefill, decode, tokens -> host
     # (the host copy holds the same prefix, so the reference continuation still applies)
@@ -525,6 +532,31 @@ def run_reference(args, rank, world):
             "e2e": {"value": round(tps, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_profile_pass(args):
+    """A short run for an ncu launch list: the headline models, a 16-position prefix, the
+    prefill and two draft-and-verify passes (one eager, one graph replay)."""
+    import torch
+    from vella_b200 import _lib as L
+    from vella_b200 import decode as VD
+    dev = torch.device("cuda", 0)
+    P = 16
+    target = VD.Model(VD.ModelConfig(**TARGET, max_seq=128, max_prefix=P, rope_theta=1e6), 0)
+    target.init_random(1, 0.02)
+    draft = VD.Model(VD.ModelConfig(**DRAFT, max_seq=128, max_prefix=P, rope_theta=1e6), 0)
+    draft.init_random(2, 0.02)
+    for m, dd, tid in ((target, TARGET["d_model"], 11), (draft, DRAFT["d_model"], 12)):
+        ptr, _ = m.tensor("prefix")
+        L.check(L.lib().vella_fill_normal(ptr, P * dd, L.BF16, 3, tid, 0.0, 1.0, None))
+    torch.cuda.synchronize()
+    sd = VD.SpecDecoder(target, draft, k=HEADLINE[0], mode=VD.DRAFT_ORACLE, oracle_p=HEADLINE[1], seed=7)
+    sd.set_prefix(None, None, P)
+    sd.prefill()
+    sd.step()
+    sd.step()
+    torch.cuda.synchronize()
+    return {"profile": "prefill(16) + 2 passes", "passes": sd.stats()["passes"]}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -533,7 +565,11 @@ def main():
     ap.add_argument("--workload", default="spec", choices=["spec", "gemm"])
     ap.add_argument("--impl", default="vella", choices=["vella", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-pass", action="store_true", help="short run for an ncu launch list")
     args = ap.parse_args()
+    if args.profile_pass:
+        print(json.dumps(run_profile_pass(args)))
+        return
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     if args.impl == "reference":

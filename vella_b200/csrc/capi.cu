@@ -2,6 +2,7 @@
 // the library-owned per-device workspace.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -15,6 +16,14 @@ namespace vella {
 std::string& last_error_slot() {
   static thread_local std::string msg;
   return msg;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("VELLA_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 int num_sms(int device) {

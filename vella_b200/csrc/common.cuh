@@ -93,6 +93,12 @@ __device__ __forceinline__ uint4 ld_stream4(const void* p) {
   return v;
 }
 
+// Programmatic dependent launch: wait until the preceding kernel of the stream has finished
+// and its writes are visible (a no-op when launched without the attribute), and let the
+// next kernel start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_next() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -7,6 +7,7 @@
 #include <cstddef>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "vella_cuda.h"
 
@@ -38,6 +39,28 @@ inline int cuda_fail(cudaError_t e, const char* what) {
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 int num_sms(int device);
+
+// Launch with programmatic stream serialization (the kernel overlaps the tail of the
+// preceding kernel and calls griddepcontrol.wait before touching its results).  Set
+// VELLA_PDL=0 to launch with plain stream order.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+int launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+  return VELLA_OK;
+}
 
 // Library-owned per-device workspace (vella_qgemm with workspace == NULL).  Grows on
 // demand; the returned memory is zero-filled when first handed out.

@@ -41,6 +41,8 @@ template <typename T>
 __global__ void embed_rows_kernel(T* __restrict__ h, const T* __restrict__ table, const T* __restrict__ prefix,
                                   const int* __restrict__ tok, PosRef pr, const int* __restrict__ Pdev, int d,
                                   int vocab, int max_seq, int* err) {
+  pdl_wait();
+  pdl_launch_next();
   const int m = blockIdx.x;
   const int pos = *pr.base + pr.off + m;
   const int P = *Pdev;
@@ -67,6 +69,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(T* __restrict__ out, const T* __restrict__ x,
                                                       const T* __restrict__ w, int d, float eps) {
   using A = Act<T>;
+  pdl_wait();
+  pdl_launch_next();
   const int row = blockIdx.x;
   const T* xr = x + (size_t)row * d;
   float ss = 0.0f;
@@ -115,6 +119,8 @@ __global__ void rope_append_kernel(const T* __restrict__ qkv, T* __restrict__ q_
                                    const T* __restrict__ kn, float eps, PosRef pr, int H, int KV, int hd,
                                    int max_seq, int* err) {
   using A = Act<T>;
+  pdl_wait();
+  pdl_launch_next();
   const int m = blockIdx.x, hidx = blockIdx.y, i = threadIdx.x;
   const int half = hd / 2;
   const int pos = *pr.base + pr.off + m;
@@ -193,6 +199,8 @@ __global__ void __launch_bounds__(256) attn_kernel(const AttnArgs a) {
 
   const int kvh = blockIdx.x, ch = blockIdx.y, qb = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  pdl_wait();
+  pdl_launch_next();
   const int pos0 = *a.pr.base + a.pr.off;
   const int mq0 = qb * QB;
   const int nq = min(QB, a.M - mq0);
@@ -344,6 +352,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logits, int V, size_t ld,
                                                      int* __restrict__ ys, float2* part, int* ctr, int* nonfinite) {
   using A = Act<T>;
+  pdl_wait();
+  pdl_launch_next();
   const int m = blockIdx.x, b = blockIdx.y;
   const int per = ((V + kArgBlocks - 1) / kArgBlocks + 7) / 8 * 8;
   const int lo = b * per, hi = min(V, lo + per);
@@ -417,9 +427,7 @@ int launch_attn_t(const AttnArgs& a, int gq, cudaStream_t s) {
                                         (int)attn_smem_bytes(HD, 8)));
     configured[dev & 63] = 1;
   }
-  attn_kernel<T, HD><<<dim3(a.KV, a.nch, a.nqb), 256, smem, s>>>(a);
-  VELLA_CUDA_TRY(cudaGetLastError());
-  return VELLA_OK;
+  return launch_kernel(attn_kernel<T, HD>, dim3(a.KV, a.nch, a.nqb), dim3(256), smem, s, a);
 }
 
 }  // namespace
@@ -452,29 +460,22 @@ int launch_embed_rows_dev(int dtype, void* h, const void* table, const void* pre
                           int rows, const int* P, int d, int vocab, int max_seq, int* err, cudaStream_t s) {
   if (rows <= 0) return VELLA_OK;
   if (dtype == VELLA_BF16)
-    embed_rows_kernel<__nv_bfloat16><<<rows, 256, 0, s>>>(
-        static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(table),
-        static_cast<const __nv_bfloat16*>(prefix), tok, pr, P, d, vocab, max_seq, err);
-  else
-    embed_rows_kernel<__half><<<rows, 256, 0, s>>>(static_cast<__half*>(h), static_cast<const __half*>(table),
-                                                   static_cast<const __half*>(prefix), tok, pr, P, d, vocab,
-                                                   max_seq, err);
-  VELLA_CUDA_TRY(cudaGetLastError());
-  return VELLA_OK;
+    return launch_kernel(embed_rows_kernel<__nv_bfloat16>, dim3(rows), dim3(256), 0, s, static_cast<__nv_bfloat16*>(h),
+                         static_cast<const __nv_bfloat16*>(table), static_cast<const __nv_bfloat16*>(prefix), tok, pr,
+                         P, d, vocab, max_seq, err);
+  return launch_kernel(embed_rows_kernel<__half>, dim3(rows), dim3(256), 0, s, static_cast<__half*>(h),
+                       static_cast<const __half*>(table), static_cast<const __half*>(prefix), tok, pr, P, d, vocab,
+                       max_seq, err);
 }
 
 int launch_rmsnorm(int dtype, void* out, const void* x, const void* w, int rows, int d, float eps,
                    cudaStream_t s) {
   if (rows <= 0) return VELLA_OK;
   if (dtype == VELLA_BF16)
-    rmsnorm_kernel<__nv_bfloat16><<<rows, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out),
-                                                       static_cast<const __nv_bfloat16*>(x),
-                                                       static_cast<const __nv_bfloat16*>(w), d, eps);
-  else
-    rmsnorm_kernel<__half><<<rows, 256, 0, s>>>(static_cast<__half*>(out), static_cast<const __half*>(x),
-                                                static_cast<const __half*>(w), d, eps);
-  VELLA_CUDA_TRY(cudaGetLastError());
-  return VELLA_OK;
+    return launch_kernel(rmsnorm_kernel<__nv_bfloat16>, dim3(rows), dim3(256), 0, s, static_cast<__nv_bfloat16*>(out),
+                         static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), d, eps);
+  return launch_kernel(rmsnorm_kernel<__half>, dim3(rows), dim3(256), 0, s, static_cast<__half*>(out),
+                       static_cast<const __half*>(x), static_cast<const __half*>(w), d, eps);
 }
 
 int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* vc, const float2* cs,
@@ -483,18 +484,15 @@ int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* 
   if (rows <= 0) return VELLA_OK;
   const dim3 grid(rows, H + KV);
   if (dtype == VELLA_BF16)
-    rope_append_kernel<__nv_bfloat16><<<grid, hd / 2, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(q_out),
-        static_cast<__nv_bfloat16*>(kc), static_cast<__nv_bfloat16*>(vc), cs,
-        static_cast<const __nv_bfloat16*>(qn), static_cast<const __nv_bfloat16*>(kn), eps, pr, H, KV, hd, max_seq,
-        err);
-  else
-    rope_append_kernel<__half><<<grid, hd / 2, 0, s>>>(
-        static_cast<const __half*>(qkv), static_cast<__half*>(q_out), static_cast<__half*>(kc),
-        static_cast<__half*>(vc), cs, static_cast<const __half*>(qn), static_cast<const __half*>(kn), eps, pr, H,
-        KV, hd, max_seq, err);
-  VELLA_CUDA_TRY(cudaGetLastError());
-  return VELLA_OK;
+    return launch_kernel(rope_append_kernel<__nv_bfloat16>, grid, dim3(hd / 2), 0, s,
+                         static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(q_out),
+                         static_cast<__nv_bfloat16*>(kc), static_cast<__nv_bfloat16*>(vc), cs,
+                         static_cast<const __nv_bfloat16*>(qn), static_cast<const __nv_bfloat16*>(kn), eps, pr, H, KV,
+                         hd, max_seq, err);
+  return launch_kernel(rope_append_kernel<__half>, grid, dim3(hd / 2), 0, s, static_cast<const __half*>(qkv),
+                       static_cast<__half*>(q_out), static_cast<__half*>(kc), static_cast<__half*>(vc), cs,
+                       static_cast<const __half*>(qn), static_cast<const __half*>(kn), eps, pr, H, KV, hd, max_seq,
+                       err);
 }
 
 int launch_attention(int dtype, const void* q, const void* kc, const void* vc, void* out, const AttnScratch& sc,
@@ -531,12 +529,10 @@ int launch_argmax(int dtype, const void* logits, int rows, int V, size_t ld, int
   float2* part = reinterpret_cast<float2*>(static_cast<char*>(scratch) + 256 + ((size_t)rows * sizeof(int) + 255) / 256 * 256);
   const dim3 grid(rows, kArgBlocks);
   if (dtype == VELLA_BF16)
-    argmax_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(logits), V, ld, ys, part,
-                                                      ctr, nonfinite);
-  else
-    argmax_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(logits), V, ld, ys, part, ctr, nonfinite);
-  VELLA_CUDA_TRY(cudaGetLastError());
-  return VELLA_OK;
+    return launch_kernel(argmax_kernel<__nv_bfloat16>, grid, dim3(256), 0, s,
+                         static_cast<const __nv_bfloat16*>(logits), V, ld, ys, part, ctr, nonfinite);
+  return launch_kernel(argmax_kernel<__half>, grid, dim3(256), 0, s, static_cast<const __half*>(logits), V, ld, ys,
+                       part, ctr, nonfinite);
 }
 
 }  // namespace vella

@@ -160,6 +160,8 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const Args a) {
   const int N = a.N;
   const int wpr = a.K / 64 * WPG;  // words per weight row
 
+  pdl_wait();
+  pdl_launch_next();
   // ---- x for this CTA's K range -> shared memory (natural order), one async copy -------
   {
     const T* x = static_cast<const T*>(a.x);
@@ -407,9 +409,7 @@ int launch_t(const Args& a, dim3 grid, size_t smem, cudaStream_t stream) {
     VELLA_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes(2, kKCMax)));
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
-  k<<<grid, kThreads, smem, stream>>>(a);
-  VELLA_CUDA_TRY(cudaGetLastError());
-  return VELLA_OK;
+  return launch_kernel(k, grid, dim3(kThreads), smem, stream, a);
 }
 
 template <typename T, int BITS>

@@ -37,7 +37,8 @@ __device__ int g_stream_fault = 0;  // set when a pipeline wait ran out of time
 
 namespace {
 
-constexpr int kConsumerWarps = 8;
+constexpr int kGroupSets = 2;                  // consumer warps split each unit's groups this many ways
+constexpr int kConsumerWarps = 4 * kGroupSets;  // 4 row sets x kGroupSets group sets
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kSlots = 128;
 constexpr int kTokMax = 16;
@@ -59,8 +60,8 @@ struct Layout {
   static constexpr int XCHUNK = TOK * 512;                    // one [TOK x 256 elements] box
   static constexpr int X_BYTES = SFmt<BITS>::XCH * XCHUNK;
   static constexpr int STAGE = W_BYTES + SB_BYTES + X_BYTES;  // multiple of 1024
-  static constexpr int NS = BITS == 8 ? 2 : (BITS == 4 ? 4 : 3);
-  static constexpr int RED = TOK * (kSlots + 4) * 4;
+  static constexpr int NS = BITS == 8 ? 2 : (BITS == 4 ? (NT == 1 ? 4 : 3) : (NT == 1 ? 3 : 2));
+  static constexpr int RED = (kGroupSets - 1) * TOK * (kSlots + 4) * 4;  // partial tiles of group sets 1..3
   static constexpr int TOTAL = 1024 + NS * STAGE + RED + 2 * NS * 8 + 16;
 };
 
@@ -150,7 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_stream_kernel(const __grid_
   using A = Act<T>;
   using LY = Layout<BITS, NT>;
   constexpr int UG = SFmt<BITS>::UG, BPG = SFmt<BITS>::BPG, NS = LY::NS, TOK = LY::TOK;
-  constexpr int GPW = UG / 2;  // groups per consumer warp and unit
+  constexpr int GPW = UG / kGroupSets;  // groups per consumer warp and unit
+  constexpr int REDSET = LY::TOK * (kSlots + 4);
   constexpr bool kQuant = BITS != 0;
   constexpr uint32_t kMask = 0x000F000Fu;
   constexpr uint32_t kMag = A::kMagic2;
@@ -183,6 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_stream_kernel(const __grid_
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  pdl_launch_next();
 
   if (warp == kConsumerWarps) {
     // ------------------------------- producer (one thread) ------------------------------
@@ -190,18 +193,9 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_stream_kernel(const __grid_
     int fills[NS];
 #pragma unroll
     for (int s = 0; s < NS; ++s) fills[s] = 0;
-    long long i = 0;
-    for (long long u = u0; u < u1; ++u, ++i) {
-      const int s = (int)(i % NS);
-      const uint32_t ph = (uint32_t)((i / NS) & 1);
-      if (flags[0]) break;
-      if (!mbar_wait(&empty[s], ph ^ 1)) {
-        flags[0] = 1;
-        atomicOr(&g_stream_fault, 1);
-        break;
-      }
-      mbar_expect_tx(&full[s], kBytes);
-      fills[s]++;
+    // weights, scales and biases of a unit (constant data: may be read before the
+    // preceding kernel has finished)
+    auto issue_w = [&](long long u, int s) {
       const int rb = (int)(u / a.nkc), kc = (int)(u % a.nkc);
       unsigned char* st = smem + s * LY::STAGE;
       const int w0 = kc * UG * BPG / 4;  // first 32-bit word of the unit in a weight row
@@ -227,9 +221,38 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_stream_kernel(const __grid_
           tma2d(ssb + kSlots * 16, &a.tb, kc * 8, rb * 128, &full[s]);
         }
       }
+    };
+    // the x slice of a unit (written by the preceding kernel)
+    auto issue_x = [&](long long u, int s) {
+      const int kc = (int)(u % a.nkc);
+      unsigned char* st = smem + s * LY::STAGE;
 #pragma unroll
       for (int j = 0; j < SFmt<BITS>::XCH; ++j)
         tma2d(st + LY::W_BYTES + LY::SB_BYTES + j * LY::XCHUNK, &a.tx, kc * UG * 64 + j * 256, 0, &full[s]);
+    };
+    // first round of the ring: weights before the dependency wait, x after it
+    const long long npre = (u1 - u0) < NS ? (u1 - u0) : NS;
+    for (long long j = 0; j < npre; ++j) {
+      mbar_expect_tx(&full[j], kBytes);
+      fills[j]++;
+      issue_w(u0 + j, (int)j);
+    }
+    pdl_wait();
+    for (long long j = 0; j < npre; ++j) issue_x(u0 + j, (int)j);
+    long long i = npre;
+    for (long long u = u0 + npre; u < u1; ++u, ++i) {
+      const int s = (int)(i % NS);
+      const uint32_t ph = (uint32_t)((i / NS) & 1);
+      if (flags[0]) break;
+      if (!mbar_wait(&empty[s], ph ^ 1)) {
+        flags[0] = 1;
+        atomicOr(&g_stream_fault, 1);
+        break;
+      }
+      mbar_expect_tx(&full[s], kBytes);
+      fills[s]++;
+      issue_w(u, s);
+      issue_x(u, s);
     }
     // Never leave with copies in flight: wait for the last fill of every stage.
     for (int s = 0; s < NS; ++s)
@@ -238,6 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_stream_kernel(const __grid_
   }
 
   // --------------------------------- consumers ------------------------------------------
+  pdl_wait();  // outputs, residuals and the workspace belong to the preceding kernel until now
   const int r = lane >> 2, cq = lane & 3;
   const int rs = warp & 3, gs = warp >> 2;
   int slot[4];
@@ -296,14 +320,18 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_stream_kernel(const __grid_
       const unsigned char* st = smem + s * LY::STAGE;
       const unsigned char* sx = st + LY::W_BYTES + LY::SB_BYTES;
       // this warp's scales and biases for its GPW groups, 4 rows
-      uint32_t sw[4][2], bw[4][2];
+      constexpr int SBW = (GPW + 1) / 2;  // 32-bit words holding this warp's GPW scales (biases)
+      uint32_t sw[4][SBW], bw[4][SBW];
       if constexpr (kQuant) {
+        static_assert(GPW % 2 == 0, "quantized group sets own whole 32-bit words of scales");
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint2 sv = *reinterpret_cast<const uint2*>(st + LY::W_BYTES + slot[q] * 16 + gs * 8);
-          const uint2 bv = *reinterpret_cast<const uint2*>(st + LY::W_BYTES + kSlots * 16 + slot[q] * 16 + gs * 8);
-          sw[q][0] = sv.x; sw[q][1] = sv.y; bw[q][0] = bv.x; bw[q][1] = bv.y;
-        }
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int wd = 0; wd < SBW; ++wd) {
+            sw[q][wd] = *reinterpret_cast<const uint32_t*>(st + LY::W_BYTES + slot[q] * 16 + gs * GPW * 2 + 4 * wd);
+            bw[q][wd] =
+                *reinterpret_cast<const uint32_t*>(st + LY::W_BYTES + kSlots * 16 + slot[q] * 16 + gs * GPW * 2 + 4 * wd);
+          }
       }
 #pragma unroll
       for (int gi = 0; gi < GPW; ++gi) {
@@ -414,24 +442,28 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_stream_kernel(const __grid_
     if (u + 1 == u1 || (u + 1) / a.nkc != rb) {
       const long long rb_u0 = (long long)rb * a.nkc, rb_u1 = rb_u0 + a.nkc - 1;
       const int cf = cta_of(rb_u0, U, P), cl = cta_of(rb_u1, U, P);
-      if (gs == 1) {
+      if (gs > 0) {
+        float* rd = red + (gs - 1) * REDSET;
 #pragma unroll
         for (int t = 0; t < 2; ++t)
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int e = 0; e < 4; ++e)
-              red[(nt * 8 + 2 * cq + (e & 1)) * (kSlots + 4) + slot[2 * t + (e >> 1)]] = acc[t][nt][e];
+              rd[(nt * 8 + 2 * cq + (e & 1)) * (kSlots + 4) + slot[2 * t + (e >> 1)]] = acc[t][nt][e];
       }
       named_sync(1, kConsumerWarps * 32);
       if (gs == 0) {
+        // group sets added in order 0 + 1 + 2 + 3
 #pragma unroll
-        for (int t = 0; t < 2; ++t)
+        for (int gsi = 0; gsi < kGroupSets - 1; ++gsi)
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
+          for (int t = 0; t < 2; ++t)
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              acc[t][nt][e] += red[(nt * 8 + 2 * cq + (e & 1)) * (kSlots + 4) + slot[2 * t + (e >> 1)]];
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                acc[t][nt][e] += red[gsi * REDSET + (nt * 8 + 2 * cq + (e & 1)) * (kSlots + 4) + slot[2 * t + (e >> 1)]];
         if (cf == cl) {
           epilogue(rb);
         } else {
@@ -458,18 +490,34 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_stream_kernel(const __grid_
           if (flags[1]) {
             __threadfence();
             zero_acc();
-            for (int cc = cf; cc <= cl; ++cc) {
-              const int si = (rb == (int)(unit0(cc, U, P) / a.nkc)) ? 0 : 1;
-              const float* pp = a.partial + ((size_t)cc * 2 + si) * kTokMax * kSlots;
+            // the contributors' partials, added in CTA order; loads of four CTAs in flight at once
+#pragma unroll 1
+            for (int cc = cf; cc <= cl; cc += 4) {
+              float tmp[4][2][NT][4];
 #pragma unroll
-              for (int t = 0; t < 2; ++t)
+              for (int q = 0; q < 4; ++q) {
+                const int c2 = cc + q;
+                const int si = (c2 <= cl && rb == (int)(unit0(c2, U, P) / a.nkc)) ? 0 : 1;
+                const float* pp = a.partial + ((size_t)min(c2, cl) * 2 + si) * kTokMax * kSlots;
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
+                for (int t = 0; t < 2; ++t)
 #pragma unroll
-                  for (int e = 0; e < 4; ++e) {
-                    const int tok = nt * 8 + 2 * cq + (e & 1);
-                    if (tok < mc) acc[t][nt][e] += __ldcg(pp + tok * kSlots + slot[2 * t + (e >> 1)]);
-                  }
+                  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                      const int tok = nt * 8 + 2 * cq + (e & 1);
+                      tmp[q][t][nt][e] = (c2 <= cl && tok < mc) ? __ldcg(pp + tok * kSlots + slot[2 * t + (e >> 1)]) : 0.0f;
+                    }
+              }
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                if (cc + q <= cl)
+#pragma unroll
+                  for (int t = 0; t < 2; ++t)
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                      for (int e = 0; e < 4; ++e) acc[t][nt][e] += tmp[q][t][nt][e];
             }
             epilogue(rb);
           }
@@ -527,9 +575,7 @@ int launch_stream_t(const SArgs& a, cudaStream_t stream) {
     VELLA_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::TOTAL));
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
-  k<<<a.P, kThreads, LY::TOTAL, stream>>>(a);
-  VELLA_CUDA_TRY(cudaGetLastError());
-  return VELLA_OK;
+  return launch_kernel(k, dim3(a.P), dim3(kThreads), LY::TOTAL, stream, a);
 }
 
 template <typename T, int BITS>

@@ -48,6 +48,8 @@ struct DevState {
 
 __global__ void prefill_finish_kernel(DevState* st, int* tok, const int* ys, int* nf, const int* err_t,
                                       int max_seq) {
+  pdl_wait();
+  pdl_launch_next();
   const int P = st->P, t = ys[0];
   if (P < max_seq) tok[P] = t; else st->err |= 4;
   st->L = P + 1;
@@ -60,6 +62,8 @@ __global__ void prefill_finish_kernel(DevState* st, int* tok, const int* ys, int
 }
 
 __global__ void greedy_commit_kernel(DevState* st, int* tok, const int* ys, int* nf, const int* err_t, int max_seq) {
+  pdl_wait();
+  pdl_launch_next();
   const int L = st->L, t = ys[0];
   if (L < max_seq) tok[L] = t; else st->err |= 4;
   st->L = L + 1;
@@ -73,6 +77,8 @@ __global__ void greedy_commit_kernel(DevState* st, int* tok, const int* ys, int*
 // Draft step i proposes the token at position L + i.
 __global__ void propose_kernel(DevState* st, int* tok, const int* ys_draft, int* nf_draft, int i, int mode, float p,
                                uint64_t seed, const int* ref, int vocab, int max_seq) {
+  pdl_wait();
+  pdl_launch_next();
   const int pos = st->L + i;
   int t = ys_draft[0];
   if (mode == VELLA_DRAFT_ORACLE) {
@@ -89,6 +95,8 @@ __global__ void propose_kernel(DevState* st, int* tok, const int* ys_draft, int*
 // Greedy acceptance over the verify argmax ys[0..K] (ys[j] predicts position L + j).
 __global__ void accept_kernel(DevState* st, int* tok, const int* ys, int K, int* nf, const int* err_t,
                               const int* err_d, int max_seq) {
+  pdl_wait();
+  pdl_launch_next();
   const int L = st->L;
   int a = 0;
   while (a < K && ys[a] == tok[L + a]) ++a;
@@ -146,23 +154,21 @@ int enqueue_pass(Spec* s) {
   for (int i = 0; i < K; ++i) {
     const PosRef pr{Lp, i == 0 ? -2 : i - 1};
     if ((rc = model_forward(d, pr, i == 0 ? 2 : 1, s->tok, Pp, 1, s->stream))) return rc;
-    propose_kernel<<<1, 1, 0, s->stream>>>(s->dstate, s->tok, d->ys, d->nonfinite, i, s->cfg.draft_mode,
-                                           s->cfg.oracle_p, s->cfg.seed, s->ref, t->cfg.vocab, s->max_seq);
-    VELLA_CUDA_TRY(cudaGetLastError());
+    if ((rc = launch_kernel(propose_kernel, dim3(1), dim3(1), 0, s->stream, s->dstate, s->tok, d->ys, d->nonfinite,
+                            i, s->cfg.draft_mode, s->cfg.oracle_p, s->cfg.seed, s->ref, t->cfg.vocab, s->max_seq)))
+      return rc;
   }
   if ((rc = model_forward(t, PosRef{Lp, -1}, K + 1, s->tok, Pp, K + 1, s->stream))) return rc;
-  accept_kernel<<<1, 1, 0, s->stream>>>(s->dstate, s->tok, t->ys, K, t->nonfinite, t->err, d->err, s->max_seq);
-  VELLA_CUDA_TRY(cudaGetLastError());
-  return VELLA_OK;
+  return launch_kernel(accept_kernel, dim3(1), dim3(1), 0, s->stream, s->dstate, s->tok, t->ys, K, t->nonfinite,
+                       t->err, d->err, s->max_seq);
 }
 
 int enqueue_greedy(Spec* s) {
   Model* t = s->target;
   int rc;
   if ((rc = model_forward(t, PosRef{&s->dstate->L, -1}, 1, s->tok, &s->dstate->P, 1, s->stream))) return rc;
-  greedy_commit_kernel<<<1, 1, 0, s->stream>>>(s->dstate, s->tok, t->ys, t->nonfinite, t->err, s->max_seq);
-  VELLA_CUDA_TRY(cudaGetLastError());
-  return VELLA_OK;
+  return launch_kernel(greedy_commit_kernel, dim3(1), dim3(1), 0, s->stream, s->dstate, s->tok, t->ys, t->nonfinite,
+                       t->err, s->max_seq);
 }
 
 int capture(Spec* s, int (*enqueue)(Spec*), cudaGraphExec_t* exec) {
@@ -219,8 +225,9 @@ int prefill(Spec* s, int* first) {
     const bool last = s0 + rows >= s->P;
     if ((rc = model_forward(t, PosRef{t->dzero, s0}, rows, s->tok, Pp, last ? 1 : 0, s->stream))) return rc;
   }
-  prefill_finish_kernel<<<1, 1, 0, s->stream>>>(s->dstate, s->tok, t->ys, t->nonfinite, t->err, s->max_seq);
-  VELLA_CUDA_TRY(cudaGetLastError());
+  if ((rc = launch_kernel(prefill_finish_kernel, dim3(1), dim3(1), 0, s->stream, s->dstate, s->tok, t->ys,
+                          t->nonfinite, t->err, s->max_seq)))
+    return rc;
   VELLA_CUDA_TRY(cudaEventRecord(s->evp, s->stream));
   if ((rc = sync_state(s))) return rc;
   *first = s->hstate->newtok[0];
