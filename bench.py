@@ -135,20 +135,23 @@ def run_gemm(args, rank, world):
     g = torch.Generator(device=dev).manual_seed(0)
     stream = torch.cuda.Stream(device=dev)
     plans = []  # (bits, n, k, m, copies, x, out, graph_calls)
+    cases = [(b, n, k, GEMM_MS) for b in (4, 8) for (n, k) in GEMM_SHAPES]
+    if args.shape:  # one (bits, N, K, M) case, e.g. a small capture for a profiler
+        b, n, k, m = (int(v) for v in args.shape.split(","))
+        cases = [(b, n, k, [m])]
     with torch.cuda.stream(stream):
-        for bits in (4, 8):
-            for (n, k) in GEMM_SHAPES:
-                w = torch.randn(n, k, generator=g, device=dev) * 0.02
-                packed, sc, bi = quantize_gpu(w, bits)
-                del w
-                wbytes = gemm_bytes(0, n, k, bits)
-                copies = max(2, -(-3 * L2_BYTES // wbytes))
-                ws = [S.Weights(packed, sc, bi, bits)] + [
-                    S.Weights(packed.clone(), sc.clone(), bi.clone(), bits) for _ in range(copies - 1)]
-                for m in GEMM_MS:
-                    x = (torch.randn(m, k, generator=g, device=dev)).to(torch.bfloat16)
-                    out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
-                    plans.append((bits, n, k, m, ws, x, out))
+        for bits, n, k, ms in cases:
+            w = torch.randn(n, k, generator=g, device=dev) * 0.02
+            packed, sc, bi = quantize_gpu(w, bits)
+            del w
+            wbytes = gemm_bytes(0, n, k, bits)
+            copies = max(2, -(-3 * L2_BYTES // wbytes))
+            ws = [S.Weights(packed, sc, bi, bits)] + [
+                S.Weights(packed.clone(), sc.clone(), bi.clone(), bits) for _ in range(copies - 1)]
+            for m in ms:
+                x = (torch.randn(m, k, generator=g, device=dev)).to(torch.bfloat16)
+                out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+                plans.append((bits, n, k, m, ws, x, out))
     torch.cuda.synchronize()
     # one workspace for every graph (they replay one after another on one stream)
     ws_bytes = max(S.workspace_size(m, n, k, torch.bfloat16, bits) for bits, n, k, m, *_ in plans)
@@ -199,8 +202,8 @@ def run_gemm(args, rank, world):
         ms = e0.elapsed_time(e1)
     total_bytes = sum(gemm_bytes(m, n, k, bits) for bits, n, k, m, *_ in plans) * reps * args.steps
     value = total_bytes / (ms / 1e3) / 1e9
-    m8 = [p for p in per if p["bits"] == 4 and p["m"] <= 8]
-    m8_bytes = sum(gemm_bytes(p["m"], p["n"], p["k"], 4) for p in m8)
+    m8 = [p for p in per if p["bits"] == 4 and p["m"] <= 8] or per
+    m8_bytes = sum(gemm_bytes(p["m"], p["n"], p["k"], p["bits"]) for p in m8)
     m8_us = sum(p["us"] for p in m8)
     dominant = m8_bytes / m8_us / 1e3
     line = {
@@ -565,6 +568,7 @@ def main():
     ap.add_argument("--workload", default="spec", choices=["spec", "gemm"])
     ap.add_argument("--impl", default="vella", choices=["vella", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shape", default="", help="gemm workload: one case 'bits,N,K,M' instead of the sweep")
     ap.add_argument("--profile-pass", action="store_true", help="short run for an ncu launch list")
     args = ap.parse_args()
     if args.profile_pass:
