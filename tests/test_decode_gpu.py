@@ -62,9 +62,11 @@ def oracle_weights(model, cfg: D.Config):
     return W
 
 
-def make(n_layers=2, d=256, H=4, KV=2, hd=64, ffn=512, V=1000, bits=4, qk_norm=False, seed=1, max_seq=512):
+def make(n_layers=2, d=256, H=4, KV=2, hd=64, ffn=512, V=1000, bits=4, qk_norm=False, seed=1, max_seq=512,
+         max_prefix=128):
     from vella_b200 import decode as VD
-    mc = VD.ModelConfig(n_layers, d, H, KV, hd, ffn, V, bits=bits, qk_norm=qk_norm, max_seq=max_seq, max_prefix=128)
+    mc = VD.ModelConfig(n_layers, d, H, KV, hd, ffn, V, bits=bits, qk_norm=qk_norm, max_seq=max_seq,
+                        max_prefix=max_prefix)
     m = VD.Model(mc)
     m.init_random(seed, 0.02 if d > 128 else 0.05)
     oc = D.Config(n_layers, d, H, KV, hd, ffn, V, bits=bits, qk_norm=qk_norm)
@@ -98,6 +100,40 @@ def test_score_matches_oracle(bits, qk):
     assert np.isfinite(got).all()
     err = np.abs(got - ref).max()
     assert err <= LOGIT_TOL, err
+
+
+@pytest.mark.parametrize("H,KV,hd", [(4, 2, 64), (8, 1, 64), (4, 1, 128)])
+def test_long_context_score_matches_oracle(H, KV, hd):
+    """700 positions: every CTA of an attention cluster owns several 64-key chunks."""
+    m, oc = make(bits=4, H=H, KV=KV, hd=hd, seed=9, max_seq=1024)
+    W = oracle_weights(m, oc)
+    P, T = 100, 600
+    pre = prefix_of(P, oc.d_model, 7)
+    toks = list(np.random.default_rng(8).integers(0, oc.vocab, T))
+    got = A.bf16_from_bits(m.score(pre, toks))
+    ref = D.score(oc, W, A.bf16_from_bits(pre), toks, D.rope_table(P + T, oc.head_dim, oc.rope_theta))
+    assert np.isfinite(got).all()
+    err = np.abs(got - ref).max()
+    assert err <= LOGIT_TOL, err
+    m.close()
+
+
+def test_long_context_draft_and_verify_is_bit_exact_greedy():
+    """A 600-position prefix: the verify rows' attention spans 10+ chunks per kv head."""
+    from vella_b200 import decode as VD
+    t, tc = make(bits=4, seed=21, max_seq=1024, max_prefix=640)
+    d, dc = make(n_layers=1, d=128, H=2, KV=1, ffn=256, bits=0, seed=22, max_seq=1024, max_prefix=640)
+    P = 600
+    pre_t, pre_d = prefix_of(P, tc.d_model, 23), prefix_of(P, dc.d_model, 24)
+    ref, sd = greedy_tokens(t, d, P, pre_t, pre_d, 40)
+    sd.close()
+    sd = VD.SpecDecoder(t, d, k=4, mode=VD.DRAFT_ORACLE, oracle_p=0.5, seed=3)
+    sd.set_prefix(pre_t, pre_d, P)
+    sd.set_reference(ref)
+    assert sd.decode_mtp(40).tokens == ref
+    sd.close()
+    for x in (t, d):
+        x.close()
 
 
 def greedy_tokens(t, d, P, pre_t, pre_d, n, **kw):

@@ -8,10 +8,12 @@
 //
 // Every kernel computes each row (token position) with an instruction sequence that does
 // not depend on the other rows of the launch: the attention splits keys at absolute
-// positions (multiples of kAttnChunk) and combines the chunks in order, masked keys add
-// exact zeros.  So a verify pass over K+1 positions gives bit-identical hidden states,
+// positions (multiples of kAttnChunk) owned by fixed CTAs of a cluster and combines them
+// in a fixed order; masked keys add exact zeros.  So a verify pass over K+1 positions gives bit-identical hidden states,
 // logits and tokens to K+1 single-token greedy steps.
 #include <cuda_runtime.h>
+
+#include <cooperative_groups.h>
 
 #include <cfloat>
 #include <cstdint>
@@ -22,6 +24,8 @@
 
 namespace vella {
 namespace {
+
+namespace cg = cooperative_groups;
 
 template <typename T>
 __device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
@@ -164,179 +168,227 @@ __global__ void rope_append_kernel(const T* __restrict__ qkv, T* __restrict__ q_
 }
 
 // ---------------------------------------------------------------------------------------
-// Decode attention (flash-decoding): CTA (kv head, key chunk, query block).  Scores and
-// probabilities in fp32; the last CTA of a (kv head, query block) combines the chunks in
-// chunk order.  Query at position p sees keys 0..p.
+// Decode attention.  One thread-block cluster of kAttnCluster CTAs per (kv head, query
+// block).  Keys are cut into chunks of kAttnChunk at absolute positions and chunk c is
+// processed by CTA c % kAttnCluster, which keeps a running (max, sum, output) per query
+// row over its chunks in chunk order (fp32 scores and probabilities).  The CTAs then
+// combine their partial rows through distributed shared memory in rank order.  Query at
+// position p sees keys 0..p; a chunk with no visible key leaves a row's state unchanged
+// bit for bit (scale exp(0) = 1, added terms exact zeros), so a row's result does not
+// depend on the other rows of the launch.
 // ---------------------------------------------------------------------------------------
 struct AttnArgs {
   const void* q;
   const void* kc;
   const void* vc;
   void* out;
-  float* part;
-  float2* ml;
-  int* ctr;
   PosRef pr;
-  int M, H, KV, S, nch, nqb;
+  int M, H, KV, S;
   float scale;
 };
 
 template <typename T, int HD>
-__global__ void __launch_bounds__(256) attn_kernel(const AttnArgs a) {
+__global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn_kernel(const AttnArgs a) {
   constexpr int C = kAttnChunk;
   constexpr int QB = kAttnQBlock;
-  constexpr int KS = HD + 4;  // padded fp32 row stride of K/V/Q in shared memory
+  constexpr int CS = kAttnCluster;
+  constexpr int KS = HD + 4;  // padded fp32 row stride of K/V/Q/O in shared memory
   constexpr int PS = C + 4;
+  constexpr int V8 = HD / 8;            // 16-byte vectors per key row
+  constexpr int LDI = C * V8 / 256;     // vectors of K (and of V) per thread and chunk
+  static_assert(LDI * 256 == C * V8, "chunk loads must tile the block");
   extern __shared__ __align__(16) float sm[];
-  __shared__ int s_last;
   const int GQ = a.H / a.KV;
   const int QRmax = QB * GQ;
   float* Ks = sm;
   float* Vs = Ks + C * KS;
   float* Qs = Vs + C * KS;
-  float* Ps = Qs + QRmax * KS;
-  float2* ML = reinterpret_cast<float2*>(Ps + QRmax * PS);
+  float* Os = Qs + QRmax * KS;
+  float* Ps = Os + QRmax * KS;
+  float* Mx = Ps + QRmax * PS;  // running max per row
+  float* Ls = Mx + QRmax;       // running sum of probabilities
+  float* Al = Ls + QRmax;       // rescale factor of the current chunk
 
-  const int kvh = blockIdx.x, ch = blockIdx.y, qb = blockIdx.z;
+  cg::cluster_group cl = cg::this_cluster();
+  const int r = (int)cl.block_rank();
+  const int kvh = blockIdx.x / CS, qb = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
   pdl_launch_next();
   const int pos0 = *a.pr.base + a.pr.off;
   const int mq0 = qb * QB;
   const int nq = min(QB, a.M - mq0);
-  const int tmax = pos0 + mq0 + nq;  // keys needed by the last query of this block
-  const int k0 = ch * C;
-  if (k0 >= tmax) return;
-  const int nact = (tmax + C - 1) / C;
-  const int nvalid = min(C, tmax - k0);
   const int QR = nq * GQ;
+  const int tmax = pos0 + mq0 + nq;  // keys needed by the last query of this block
+  const int nact = (tmax + C - 1) / C;
+  const int kend = min(tmax, a.S);   // cache rows that exist
   const T* q = static_cast<const T*>(a.q);
-  const T* kc = static_cast<const T*>(a.kc) + ((size_t)kvh * a.S + k0) * HD;
-  const T* vc = static_cast<const T*>(a.vc) + ((size_t)kvh * a.S + k0) * HD;
+  const T* kbase = static_cast<const T*>(a.kc) + (size_t)kvh * a.S * HD;
+  const T* vbase = static_cast<const T*>(a.vc) + (size_t)kvh * a.S * HD;
 
-  for (int e = tid; e < C * (HD / 8); e += 256) {
-    const int j = e / (HD / 8), d8 = (e % (HD / 8)) * 8;
-    float kv8[8], vv8[8];
-    if (j < nvalid) {
-      load8(kc + (size_t)j * HD + d8, kv8);
-      load8(vc + (size_t)j * HD + d8, vv8);
-    } else {
+  for (int i = tid; i < QR * KS; i += 256) Os[i] = 0.0f;
+  for (int i = tid; i < QR; i += 256) { Mx[i] = -INFINITY; Ls[i] = 0.0f; }
+  for (int e0 = 0; e0 < QR * V8; e0 += 4 * 256) {
+    uint4 raw[4];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) kv8[t] = vv8[t] = 0.0f;
-    }
-#pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      Ks[j * KS + d8 + t] = kv8[t];
-      Vs[j * KS + d8 + t] = vv8[t];
-    }
-  }
-  for (int e = tid; e < QR * (HD / 8); e += 256) {
-    const int qr = e / (HD / 8), d8 = (e % (HD / 8)) * 8;
-    const int mi = qr / GQ, g = qr % GQ;
-    float v8[8];
-    load8(q + ((size_t)(mq0 + mi) * a.H + kvh * GQ + g) * HD + d8, v8);
-#pragma unroll
-    for (int t = 0; t < 8; ++t) Qs[qr * KS + d8 + t] = v8[t];
-  }
-  __syncthreads();
-
-  // ---- scores: warp w takes 4-row blocks, lane j takes keys j and j + 32 -------------
-  for (int rb = warp * 4; rb < QR; rb += 32) {
-    float s[4][2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) s[i][0] = s[i][1] = 0.0f;
-    for (int d = 0; d < HD; d += 4) {
-      const float4 ka = *reinterpret_cast<const float4*>(Ks + lane * KS + d);
-      const float4 kb = *reinterpret_cast<const float4*>(Ks + (lane + 32) * KS + d);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 qv = *reinterpret_cast<const float4*>(Qs + min(rb + i, QR - 1) * KS + d);
-        s[i][0] = fmaf(qv.x, ka.x, s[i][0]); s[i][0] = fmaf(qv.y, ka.y, s[i][0]);
-        s[i][0] = fmaf(qv.z, ka.z, s[i][0]); s[i][0] = fmaf(qv.w, ka.w, s[i][0]);
-        s[i][1] = fmaf(qv.x, kb.x, s[i][1]); s[i][1] = fmaf(qv.y, kb.y, s[i][1]);
-        s[i][1] = fmaf(qv.z, kb.z, s[i][1]); s[i][1] = fmaf(qv.w, kb.w, s[i][1]);
+    for (int u = 0; u < 4; ++u) {
+      const int e = e0 + u * 256 + tid;
+      if (e < QR * V8) {
+        const int qr = e / V8, d8 = (e % V8) * 8;
+        raw[u] = *reinterpret_cast<const uint4*>(q + ((size_t)(mq0 + qr / GQ) * a.H + kvh * GQ + qr % GQ) * HD + d8);
       }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int qr = rb + i;
-      if (qr < QR) {
-        const int pq = pos0 + mq0 + qr / GQ;
-        Ps[qr * PS + lane] = (k0 + lane <= pq) ? s[i][0] * a.scale : -INFINITY;
-        Ps[qr * PS + lane + 32] = (k0 + lane + 32 <= pq) ? s[i][1] * a.scale : -INFINITY;
+    for (int u = 0; u < 4; ++u) {
+      const int e = e0 + u * 256 + tid;
+      if (e < QR * V8) {
+        const int qr = e / V8, d8 = (e % V8) * 8;
+        const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          Qs[qr * KS + d8 + 2 * t] = Act<T>::lo(w[t]);
+          Qs[qr * KS + d8 + 2 * t + 1] = Act<T>::hi(w[t]);
+        }
       }
     }
   }
-  __syncthreads();
 
-  // ---- softmax within the chunk: warp per row ----------------------------------------
-  for (int qr = warp; qr < QR; qr += 8) {
-    const float v0 = Ps[qr * PS + lane], v1 = Ps[qr * PS + lane + 32];
-    const float mx = warp_max(fmaxf(v0, v1));
-    float p0 = 0.0f, p1 = 0.0f, l = 0.0f;
-    if (mx != -INFINITY) {
-      p0 = v0 == -INFINITY ? 0.0f : expf(v0 - mx);
-      p1 = v1 == -INFINITY ? 0.0f : expf(v1 - mx);
-      l = warp_sum(p0 + p1);
+  // K/V of a chunk travel through registers so that the next chunk's loads overlap this
+  // chunk's arithmetic; keys at or past tmax read as zeros (their rows may be stale).
+  uint4 kr[LDI], vr[LDI];
+  auto fetch = [&](int c) {
+    const int k0 = c * C;
+#pragma unroll
+    for (int u = 0; u < LDI; ++u) {
+      const int e = u * 256 + tid, j = e / V8, d8 = (e % V8) * 8;
+      if (k0 + j < kend) {
+        kr[u] = *reinterpret_cast<const uint4*>(kbase + (size_t)(k0 + j) * HD + d8);
+        vr[u] = *reinterpret_cast<const uint4*>(vbase + (size_t)(k0 + j) * HD + d8);
+      } else {
+        kr[u] = vr[u] = make_uint4(0u, 0u, 0u, 0u);
+      }
     }
-    Ps[qr * PS + lane] = p0;
-    Ps[qr * PS + lane + 32] = p1;
-    if (lane == 0) ML[qr] = make_float2(mx, l);
-  }
-  __syncthreads();
+  };
+  auto stash = [&]() {
+#pragma unroll
+    for (int u = 0; u < LDI; ++u) {
+      const int e = u * 256 + tid, j = e / V8, d8 = (e % V8) * 8;
+      const uint32_t kw[4] = {kr[u].x, kr[u].y, kr[u].z, kr[u].w};
+      const uint32_t vw[4] = {vr[u].x, vr[u].y, vr[u].z, vr[u].w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        Ks[j * KS + d8 + 2 * t] = Act<T>::lo(kw[t]);
+        Ks[j * KS + d8 + 2 * t + 1] = Act<T>::hi(kw[t]);
+        Vs[j * KS + d8 + 2 * t] = Act<T>::lo(vw[t]);
+        Vs[j * KS + d8 + 2 * t + 1] = Act<T>::hi(vw[t]);
+      }
+    }
+  };
 
-  // ---- P.V: thread (d, row set), 4 rows at a time ------------------------------------
   constexpr int RS = 256 / HD;
   const int d = tid % HD, rset = tid / HD;
-  const size_t cta = ((size_t)(kvh * a.nqb + qb) * a.nch + ch) * QRmax;
-  for (int rb = rset * 4; rb < QR; rb += RS * 4) {
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int j = 0; j < C; j += 4) {
-      const float v0 = Vs[j * KS + d], v1 = Vs[(j + 1) * KS + d], v2 = Vs[(j + 2) * KS + d],
-                  v3 = Vs[(j + 3) * KS + d];
+  if (r < nact) fetch(r);
+  for (int c = r; c < nact; c += CS) {
+    const int k0 = c * C;
+    __syncthreads();  // the previous chunk's P.V has finished reading Ks/Vs
+    stash();
+    if (c + CS < nact) fetch(c + CS);
+    __syncthreads();
+
+    // ---- scores: warp w takes 4-row blocks, lane j takes keys j and j + 32 -----------
+    for (int rb = warp * 4; rb < QR; rb += 32) {
+      float s[4][2];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s[i][0] = s[i][1] = 0.0f;
+      for (int dd = 0; dd < HD; dd += 4) {
+        const float4 ka = *reinterpret_cast<const float4*>(Ks + lane * KS + dd);
+        const float4 kb = *reinterpret_cast<const float4*>(Ks + (lane + 32) * KS + dd);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 qv = *reinterpret_cast<const float4*>(Qs + min(rb + i, QR - 1) * KS + dd);
+          s[i][0] = fmaf(qv.x, ka.x, s[i][0]); s[i][0] = fmaf(qv.y, ka.y, s[i][0]);
+          s[i][0] = fmaf(qv.z, ka.z, s[i][0]); s[i][0] = fmaf(qv.w, ka.w, s[i][0]);
+          s[i][1] = fmaf(qv.x, kb.x, s[i][1]); s[i][1] = fmaf(qv.y, kb.y, s[i][1]);
+          s[i][1] = fmaf(qv.z, kb.z, s[i][1]); s[i][1] = fmaf(qv.w, kb.w, s[i][1]);
+        }
+      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float4 p = *reinterpret_cast<const float4*>(Ps + min(rb + i, QR - 1) * PS + j);
-        acc[i] = fmaf(p.x, v0, acc[i]); acc[i] = fmaf(p.y, v1, acc[i]);
-        acc[i] = fmaf(p.z, v2, acc[i]); acc[i] = fmaf(p.w, v3, acc[i]);
+        const int qr = rb + i;
+        if (qr < QR) {
+          const int pq = pos0 + mq0 + qr / GQ;
+          Ps[qr * PS + lane] = (k0 + lane <= pq) ? s[i][0] * a.scale : -INFINITY;
+          Ps[qr * PS + lane + 32] = (k0 + lane + 32 <= pq) ? s[i][1] * a.scale : -INFINITY;
+        }
       }
     }
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (rb + i < QR) a.part[(cta + rb + i) * HD + d] = acc[i];
-  }
-  for (int qr = tid; qr < QR; qr += 256) a.ml[cta + qr] = ML[qr];
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    int* c = a.ctr + kvh * a.nqb + qb;
-    const int prev = atomicAdd(c, 1);
-    const int last = prev == nact - 1;
-    if (last) *c = 0;
-    s_last = last;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
+    __syncthreads();
 
-  // ---- combine the chunks of every query in chunk order --------------------------------
-  T* out = static_cast<T*>(a.out);
-  const size_t base = (size_t)(kvh * a.nqb + qb) * a.nch * QRmax;
-  for (int qr = rset; qr < QR; qr += RS) {
-    const int pq = pos0 + mq0 + qr / GQ;
-    const int nch_q = pq / C + 1;
-    float mx = -INFINITY;
-    for (int c = 0; c < nch_q; ++c) mx = fmaxf(mx, __ldcg(&a.ml[base + (size_t)c * QRmax + qr].x));
-    float o = 0.0f, l = 0.0f;
-    for (int c = 0; c < nch_q; ++c) {
-      const float2 ml = __ldcg(&a.ml[base + (size_t)c * QRmax + qr]);
-      const float w = expf(ml.x - mx);
-      o = fmaf(w, __ldcg(&a.part[(base + (size_t)c * QRmax + qr) * HD + d]), o);
-      l = fmaf(w, ml.y, l);
+    // ---- running softmax: warp per row --------------------------------------------------
+    for (int qr = warp; qr < QR; qr += 8) {
+      const float v0 = Ps[qr * PS + lane], v1 = Ps[qr * PS + lane + 32];
+      const float mo = Mx[qr];
+      const float mn = fmaxf(mo, warp_max(fmaxf(v0, v1)));
+      float p0 = 0.0f, p1 = 0.0f, alpha = 1.0f;
+      if (mn != -INFINITY) {
+        p0 = v0 == -INFINITY ? 0.0f : expf(v0 - mn);
+        p1 = v1 == -INFINITY ? 0.0f : expf(v1 - mn);
+        alpha = mo == -INFINITY ? 0.0f : expf(mo - mn);
+      }
+      const float l = warp_sum(p0 + p1);
+      Ps[qr * PS + lane] = p0;
+      Ps[qr * PS + lane + 32] = p1;
+      if (lane == 0) {
+        Mx[qr] = mn;
+        Ls[qr] = fmaf(Ls[qr], alpha, l);
+        Al[qr] = alpha;
+      }
     }
-    const int mi = qr / GQ, g = qr % GQ;
-    out[((size_t)(mq0 + mi) * a.H + kvh * GQ + g) * HD + d] = Act<T>::from_f(o / l);
+    __syncthreads();
+
+    // ---- O = O * alpha + P.V: thread (d, row set), 4 rows at a time --------------------
+    for (int rb = rset * 4; rb < QR; rb += RS * 4) {
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int j = 0; j < C; j += 4) {
+        const float v0 = Vs[j * KS + d], v1 = Vs[(j + 1) * KS + d], v2 = Vs[(j + 2) * KS + d],
+                    v3 = Vs[(j + 3) * KS + d];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 p = *reinterpret_cast<const float4*>(Ps + min(rb + i, QR - 1) * PS + j);
+          acc[i] = fmaf(p.x, v0, acc[i]); acc[i] = fmaf(p.y, v1, acc[i]);
+          acc[i] = fmaf(p.z, v2, acc[i]); acc[i] = fmaf(p.w, v3, acc[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (rb + i < QR) Os[(rb + i) * KS + d] = fmaf(Os[(rb + i) * KS + d], Al[rb + i], acc[i]);
+    }
   }
+
+  // ---- combine the cluster's partial rows in rank order; CTA r owns rows r, r + CS, … --
+  cl.sync();
+  T* out = static_cast<T*>(a.out);
+  for (int qr = r + CS * rset; qr < QR; qr += CS * RS) {
+    float mr[CS], lr[CS], orr[CS];
+#pragma unroll
+    for (int i = 0; i < CS; ++i) {
+      mr[i] = *cl.map_shared_rank(Mx + qr, i);
+      lr[i] = *cl.map_shared_rank(Ls + qr, i);
+      orr[i] = *cl.map_shared_rank(Os + qr * KS + d, i);
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < CS; ++i) mx = fmaxf(mx, mr[i]);
+    float o = 0.0f, l = 0.0f;
+#pragma unroll
+    for (int i = 0; i < CS; ++i) {
+      const float w = mr[i] == -INFINITY ? 0.0f : expf(mr[i] - mx);
+      o = fmaf(w, orr[i], o);
+      l = fmaf(w, lr[i], l);
+    }
+    out[((size_t)(mq0 + qr / GQ) * a.H + kvh * GQ + qr % GQ) * HD + d] = Act<T>::from_f(o / l);
+  }
+  cl.sync();  // keep this CTA's shared memory alive until every peer has read it
 }
 
 // ---------------------------------------------------------------------------------------
@@ -413,7 +465,7 @@ __global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logit
 
 size_t attn_smem_bytes(int hd, int gq) {
   const size_t ks = hd + 4, ps = kAttnChunk + 4, qr = (size_t)kAttnQBlock * gq;
-  return (2 * kAttnChunk * ks + qr * ks + qr * ps) * sizeof(float) + qr * sizeof(float2);
+  return (2 * kAttnChunk * ks + 2 * qr * ks + qr * ps + 3 * qr) * sizeof(float);
 }
 
 template <typename T, int HD>
@@ -424,37 +476,14 @@ int launch_attn_t(const AttnArgs& a, int gq, cudaStream_t s) {
   VELLA_CUDA_TRY(cudaGetDevice(&dev));
   if (!configured[dev & 63]) {
     VELLA_CUDA_TRY(cudaFuncSetAttribute(attn_kernel<T, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)attn_smem_bytes(HD, 8)));
+                                        (int)attn_smem_bytes(HD, kAttnMaxGQ)));
     configured[dev & 63] = 1;
   }
-  return launch_kernel(attn_kernel<T, HD>, dim3(a.KV, a.nch, a.nqb), dim3(256), smem, s, a);
+  const int nqb = (a.M + kAttnQBlock - 1) / kAttnQBlock;
+  return launch_kernel(attn_kernel<T, HD>, dim3(a.KV * kAttnCluster, nqb), dim3(256), smem, s, a);
 }
 
 }  // namespace
-
-size_t attn_scratch_bytes(int kv, int gq, int hd, int max_rows, int max_seq) {
-  const size_t nqb = (max_rows + kAttnQBlock - 1) / kAttnQBlock;
-  const size_t nch = (max_seq + kAttnChunk - 1) / kAttnChunk;
-  const size_t qr = (size_t)kAttnQBlock * gq;
-  const size_t part = (size_t)kv * nqb * nch * qr * hd * sizeof(float);
-  const size_t ml = (size_t)kv * nqb * nch * qr * sizeof(float2);
-  const size_t ctr = (size_t)kv * nqb * sizeof(int);
-  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
-  return up(ctr) + up(ml) + up(part);
-}
-
-void attn_scratch_carve(void* base, int kv, int gq, int hd, int max_rows, int max_seq, AttnScratch* s) {
-  const size_t nqb = (max_rows + kAttnQBlock - 1) / kAttnQBlock;
-  const size_t nch = (max_seq + kAttnChunk - 1) / kAttnChunk;
-  const size_t qr = (size_t)kAttnQBlock * gq;
-  const size_t ml = (size_t)kv * nqb * nch * qr * sizeof(float2);
-  const size_t ctr = (size_t)kv * nqb * sizeof(int);
-  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
-  char* p = static_cast<char*>(base);
-  s->counters = reinterpret_cast<int*>(p);
-  s->ml = reinterpret_cast<float2*>(p + up(ctr));
-  s->part = reinterpret_cast<float*>(p + up(ctr) + up(ml));
-}
 
 int launch_embed_rows_dev(int dtype, void* h, const void* table, const void* prefix, const int* tok, PosRef pr,
                           int rows, const int* P, int d, int vocab, int max_seq, int* err, cudaStream_t s) {
@@ -495,18 +524,16 @@ int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* 
                        err);
 }
 
-int launch_attention(int dtype, const void* q, const void* kc, const void* vc, void* out, const AttnScratch& sc,
-                     PosRef pr, int rows, int H, int KV, int hd, int max_seq, float scale, cudaStream_t s) {
+int launch_attention(int dtype, const void* q, const void* kc, const void* vc, void* out, PosRef pr, int rows,
+                     int H, int KV, int hd, int max_seq, float scale, cudaStream_t s) {
   if (rows <= 0) return VELLA_OK;
   AttnArgs a{};
   a.q = q; a.kc = kc; a.vc = vc; a.out = out;
-  a.part = sc.part; a.ml = sc.ml; a.ctr = sc.counters;
   a.pr = pr; a.M = rows; a.H = H; a.KV = KV; a.S = max_seq;
-  a.nch = (max_seq + kAttnChunk - 1) / kAttnChunk;
-  a.nqb = (rows + kAttnQBlock - 1) / kAttnQBlock;
   a.scale = scale;
   const int gq = H / KV;
-  if (gq * KV != H || gq > 8) return fail(VELLA_E_UNSUPPORTED, "attention: H/KV = %d/%d not supported", H, KV);
+  if (gq * KV != H || gq > kAttnMaxGQ)
+    return fail(VELLA_E_UNSUPPORTED, "attention: H/KV = %d/%d not supported", H, KV);
   if (dtype == VELLA_BF16) {
     if (hd == 128) return launch_attn_t<__nv_bfloat16, 128>(a, gq, s);
     if (hd == 64) return launch_attn_t<__nv_bfloat16, 64>(a, gq, s);

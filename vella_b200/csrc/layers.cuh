@@ -15,17 +15,10 @@ struct PosRef {
   int off;
 };
 
-constexpr int kAttnChunk = 64;   // keys per attention CTA (absolute-position aligned)
-constexpr int kAttnQBlock = 16;  // query rows per attention CTA
-
-struct AttnScratch {
-  float* part = nullptr;   // [KV][nqb][nch][QB*GQ][HD]
-  float2* ml = nullptr;    // [KV][nqb][nch][QB*GQ]
-  int* counters = nullptr; // [KV][nqb], zero between launches
-};
-
-size_t attn_scratch_bytes(int kv, int gq, int hd, int max_rows, int max_seq);
-void attn_scratch_carve(void* base, int kv, int gq, int hd, int max_rows, int max_seq, AttnScratch* s);
+constexpr int kAttnChunk = 64;   // keys per chunk (absolute-position aligned)
+constexpr int kAttnQBlock = 8;   // query rows per cluster
+constexpr int kAttnCluster = 8;  // CTAs per (kv head, query block); chunk c goes to CTA c % 8
+constexpr int kAttnMaxGQ = 8;    // query heads per kv head
 
 // dtype: 0 = bf16, 1 = fp16 everywhere below.
 // Row m holds position p = *pr.base + pr.off + m: the caller's input embedding p when
@@ -37,8 +30,8 @@ int launch_rmsnorm(int dtype, void* out, const void* x, const void* w, int rows,
 int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* vc, const float2* cs,
                        const void* qn, const void* kn, float eps, PosRef pr, int rows, int H, int KV, int hd,
                        int max_seq, int* err, cudaStream_t s);
-int launch_attention(int dtype, const void* q, const void* kc, const void* vc, void* out, const AttnScratch& sc,
-                     PosRef pr, int rows, int H, int KV, int hd, int max_seq, float scale, cudaStream_t s);
+int launch_attention(int dtype, const void* q, const void* kc, const void* vc, void* out, PosRef pr, int rows,
+                     int H, int KV, int hd, int max_seq, float scale, cudaStream_t s);
 // ys[m] = first index of the row maximum of logits[m][0..V) (row stride ld); any NaN/Inf
 // sets *nonfinite.  `part`/`counters` scratch from argmax_scratch_bytes.
 size_t argmax_scratch_bytes(int max_rows);

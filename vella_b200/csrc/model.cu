@@ -302,7 +302,6 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
   ws = std::max(ws, gemm_ws_for(m->lm_head, bits, c.dtype, VELLA_EPI_NONE));
   m->gemm_ws_bytes = ws;
   const size_t R = kMaxRows;
-  const size_t attn_b = attn_scratch_bytes(KV, H / KV, hd, kMaxRows, c.max_seq);
   const size_t sizes[] = {
       m->kv_bytes,                                  // 0 kv
       (size_t)std::max(c.max_prefix, 1) * d * e,   // 1 prefix
@@ -314,7 +313,7 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
       R * (size_t)c.vocab * e,                      // 9 logits
       R * sizeof(int),                              // 10 ys
       ws,                                           // 11 gemm workspace
-      attn_b,                                       // 12 attention scratch
+      0,                                            // 12 (unused)
       argmax_scratch_bytes(kMaxRows) + 512,         // 13 argmax scratch
       4 * sizeof(int),                              // 14 flags
       (size_t)c.max_seq * sizeof(int),              // 15 scoring token ids
@@ -344,7 +343,6 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
   m->logits = slots[9];
   m->ys = static_cast<int*>(slots[10]);
   m->gemm_ws = ws ? slots[11] : nullptr;
-  attn_scratch_carve(slots[12], KV, H / KV, hd, kMaxRows, c.max_seq, &m->attn_sc);
   m->argmax_sc = slots[13];
   int* flags = static_cast<int*>(slots[14]);
   m->err = flags;
@@ -463,7 +461,7 @@ int model_forward(Model* m, PosRef pr, int rows, const int* tok, const int* P, i
     if ((rc = launch_rope_append(dt, m->qkv_out, m->q, m->kcache(l), m->vcache(l), m->rope, L.q_norm, L.k_norm,
                                  c.rms_eps, pr, rows, H, KV, hd, c.max_seq, m->err, s)))
       return rc;
-    if ((rc = launch_attention(dt, m->q, m->kcache(l), m->vcache(l), m->attn, m->attn_sc, pr, rows, H, KV, hd,
+    if ((rc = launch_attention(dt, m->q, m->kcache(l), m->vcache(l), m->attn, pr, rows, H, KV, hd,
                                c.max_seq, scale, s)))
       return rc;
     if ((rc = model_gemm(m, L.o, m->attn, rows, m->h, VELLA_EPI_RESIDUAL, m->h, nullptr, s))) return rc;

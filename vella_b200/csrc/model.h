@@ -54,7 +54,6 @@ struct Model {
   int* ys = nullptr;       // [kMaxRows]
   void* gemm_ws = nullptr;
   size_t gemm_ws_bytes = 0;
-  AttnScratch attn_sc;
   void* argmax_sc = nullptr;
   int* err = nullptr;        // bit flags set by kernels (bad token, bad position)
   int* nonfinite = nullptr;  // set by argmax over logits
