@@ -64,10 +64,12 @@ enum {
  *   bits = 0     W is dense [N, K] in `dtype` (scales/biases unused).
  *   bits = 4 | 8 W is MLX-affine: packed uint32 [N, K*bits/32] (element i of a word at bits
  *                [bits*i, bits*(i+1)), low first), scales and biases [N, K/64] in `dtype`,
- *                element = scale * q + bias; accumulated in the product form
+ *                element = scale * q + bias.  M <= 16: accumulated in the product form
  *                sum_g (scale * sum(x*q) + bias * sum(x)) as SmallMGEMM.swift:724.
+ *                M > 16 (tensor cores): each weight is rounded once to `dtype` as
+ *                scale * q + bias, then accumulated in fp32.
  * group_size must be 64 when bits != 0.  x, residual, out are row-major with row stride K
- * (x) or N (residual, out).
+ * (x) or N (residual, out).  M may be any size; K a multiple of 64.
  */
 typedef struct vella_qgemm_desc {
   int32_t m, n, k;
@@ -94,8 +96,9 @@ VELLA_API size_t vella_qgemm_workspace_size(const vella_qgemm_desc* desc);
  * call must not be inside CUDA graph capture; a grown workspace keeps the old buffer
  * alive, so graphs captured earlier stay valid, but they all share one buffer and must
  * not run concurrently.
- * The reduction order of a row depends only on (N, K, bits): a row of a batched call is
- * bit-identical to the same row computed alone.
+ * The reduction order of a row depends only on (N, K, bits) and on which side of 16 rows the
+ * call falls: a row of a call of M <= 16 rows is bit-identical to the same row computed alone,
+ * and a row of a call above 16 rows to the same row in any other call above 16 rows.
  */
 VELLA_API int vella_qgemm(const vella_qgemm_desc* desc, const void* x, const void* w, const void* scales,
                 const void* biases, const void* up_w, const void* up_scales, const void* up_biases,
@@ -249,6 +252,12 @@ VELLA_API int vella_spec_reset(vella_spec* spec);
 
 /* Message of the last failing call on this thread ("" when none); returns its length. */
 VELLA_API size_t vella_last_error(char* buf, size_t cap);
+
+/* Diagnostic with no counterpart in the reference: nonzero when a TMA/tensor-core pipeline
+ * wait inside a kernel ran out of time since the last clear (bits 0-7: small-M streaming GEMM,
+ * bits 8-15: tensor-core GEMM).  The kernel that gave up finished without its result.
+ * Synchronises with the device; clear != 0 resets the flags. */
+VELLA_API int32_t vella_fault_flags(int32_t clear);
 
 /* Library version string, e.g. "vella-b200 0.1 sm_100a". */
 VELLA_API const char* vella_version(void);

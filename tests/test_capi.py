@@ -47,7 +47,8 @@ def test_version_and_last_error():
     (9, 25600, 5120, 8, "siluGate", True),
     (4, 96, 512, 0, "bias", True),
     (256, 64, 448, 4, "residual", True),
-    (257, 64, 448, 4, "none", False),   # beyond the small-M range
+    (257, 64, 448, 4, "none", True),    # above 16 rows: the tensor-core kernel
+    (1500, 1280, 1280, 0, "bias", True),
     (4, 96, 520, 4, "none", False),     # K not a multiple of the group
     (4, 96, 512, 5, "none", False),     # unsupported bit width
     (0, 96, 512, 4, "none", True),      # empty batch is a no-op

@@ -182,16 +182,47 @@ def test_empty_batch_and_unsupported():
     assert S.matmul(torch.zeros(2, 512, device="cuda", dtype=torch.float16), w) is None
 
 
-def test_large_m_chunks():
-    """M 17..256 runs in 16-row chunks with the same per-row arithmetic."""
+def test_large_m_tensor_core_rows_invariant():
+    """M > 16 runs on the tensor cores; a row depends only on its own activations."""
     S = smallm()
     n, k = 320, 1024
     p, sc, bi = A.quantize((np.random.default_rng(4).standard_normal((n, k)) * 0.02).astype(np.float32), 8)
     w = S.Weights(dev(p), dev(sc), dev(bi), 8)
-    x = A.to_storage(np.random.default_rng(5).standard_normal((100, k)).astype(np.float32), "bf16")
+    x = A.to_storage(np.random.default_rng(5).standard_normal((300, k)).astype(np.float32), "bf16")
     out = S.matmul(dev(x), w)
     torch.cuda.synchronize()
     assert_close(host(out), A.qgemm(x, p, sc, bi, bits=8), "bf16")
-    # batches above 16 rows share one per-row reduction order (row 37 of 100 == row 17 of 40)
-    other = S.matmul(dev(x)[20:60], w)
-    assert torch.equal(out[37].view(torch.int16), other[17].view(torch.int16))
+    # row 137 of 300 (second token tile) == row 17 of 40 (first tile) == row 117 of 200
+    other = S.matmul(dev(x)[120:160], w)
+    third = S.matmul(dev(x)[20:220], w)
+    assert torch.equal(out[137].view(torch.int16), other[17].view(torch.int16))
+    assert torch.equal(out[137].view(torch.int16), third[117].view(torch.int16))
+
+
+@pytest.mark.parametrize("bits", [0, 4, 8])
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("epi", ["none", "bias", "residual", "biasResidual", "siluGate"])
+def test_tensor_core_every_class(bits, dtype, epi):
+    """Calls above 16 rows (tcgen05 path): partial token tiles, N not a multiple of 128,
+    fewer K stages than pipeline stages, and several token tiles."""
+    for m, n, k in [(17, 200, 1088), (40, 64, 128), (130, 257, 576), (300, 136, 2048)]:
+        case = make(m, n, k, bits, dtype, epi, seed=m * 5 + bits)
+        assert_close(run_case(case, m, n, k, bits, dtype, epi), case["out"], dtype)
+
+
+def test_tensor_core_config2_shape_sampled():
+    """A prefill-sized call (M 256, N 25600, K 5120, int4) against sampled oracle rows."""
+    S = smallm()
+    n, k, m = 25600, 5120, 256
+    rng = np.random.default_rng(77)
+    sample = np.sort(rng.choice(n, size=256, replace=False))
+    packed = rng.integers(0, 2 ** 32, size=(n, k // 8), dtype=np.uint32)
+    span = 0.1 / 15
+    sc = A.to_storage((span * (0.5 + rng.random((n, k // 64)))).astype(np.float32), "bf16")
+    bi = A.to_storage((-0.05 * (0.5 + rng.random((n, k // 64)))).astype(np.float32), "bf16")
+    x = A.to_storage(rng.standard_normal((m, k)).astype(np.float32), "bf16")
+    out = S.matmul(dev(x), S.Weights(dev(packed), dev(sc), dev(bi), 4))
+    torch.cuda.synchronize()
+    got = host(out)[:, sample]
+    ref = A.qgemm(x, packed[sample], sc[sample], bi[sample], bits=4)
+    assert_close(got, ref, "bf16")

@@ -68,8 +68,9 @@ def test_noalloc_matches_qgemm_on_two_calls(bits, m, n, k, epi):
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
     L = _lib()
-    # the lm_head-sized GEMM at 256 rows needs far more than the 32 MiB static array
-    d = L.QgemmDesc(256, 151936, 5120, 4, 64, L.BF16, 0)
+    # an lm_head-sized GEMM at 16 rows with K = 25664 (not a multiple of 512: the split-K
+    # register kernel) needs far more than the 32 MiB static array
+    d = L.QgemmDesc(16, 151936, 25664, 4, 64, L.BF16, 0)
     assert L.lib().vella_qgemm_workspace_size(ctypes.byref(d)) > 32 << 20
     x = torch.zeros(8, device="cuda")
     rc = L.lib().vella_qgemm_noalloc(ctypes.byref(d), *([x.data_ptr()] * 4), None, None, None, None, None,

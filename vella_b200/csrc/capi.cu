@@ -95,6 +95,13 @@ size_t vella_last_error(char* buf, size_t cap) {
   return m.size();
 }
 
+int32_t vella_fault_flags(int32_t clear) {
+  const int st = stream_fault_status(clear);
+  const int tc = tc_fault_status(clear);
+  if (st < 0 || tc < 0) return -1;
+  return (st & 0xFF) | ((tc & 0xFF) << 8);
+}
+
 const char* vella_version(void) { return "vella-b200 0.1 sm_100a"; }
 
 int vella_qgemm_supports(const vella_qgemm_desc* desc) {

@@ -1,6 +1,7 @@
 // Host-side helpers shared by the library's translation units (not part of the C ABI).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -76,6 +77,7 @@ struct QgemmPlan {
   size_t workspace;
   bool stream = false;  // persistent bulk-copy kernel (qgemm_stream.cu)
   int ctas = 0;         // its grid (one CTA per SM)
+  bool tc = false;      // tensor-core kernel for M > 16 (tc_gemm.cu)
 };
 
 // qgemm_stream.cu
@@ -88,11 +90,24 @@ int stream_launch(const vella_qgemm_desc& d, int P, const void* x, const void* w
                   cudaStream_t stream);
 int stream_fault_status(int clear);
 
+// tc_gemm.cu
+bool tc_eligible(const vella_qgemm_desc& d);
+int tc_launch(const vella_qgemm_desc& d, const void* x, const void* w, const void* scales, const void* biases,
+              const void* up_w, const void* up_scales, const void* up_biases, const void* bias,
+              const void* residual, void* out, cudaStream_t stream);
+int tc_fault_status(int clear);
+
 bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* plan);
 
 int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& plan, const void* x, const void* w,
                  const void* scales, const void* biases, const void* up_w, const void* up_scales,
                  const void* up_biases, const void* bias, const void* residual, void* out, void* ws,
                  cudaStream_t stream);
+
+// 2D tensor map over a row-major array of `rows` rows of `inner` elements (`row_bytes`
+// apart), copied in boxes of box_inner x box_rows with the given swizzle; out-of-range
+// elements read as zeros (tma.cu).
+int make_tensor_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz);
 
 }  // namespace vella

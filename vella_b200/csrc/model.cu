@@ -301,7 +301,7 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
   }
   ws = std::max(ws, gemm_ws_for(m->lm_head, bits, c.dtype, VELLA_EPI_NONE));
   m->gemm_ws_bytes = ws;
-  const size_t R = kMaxRows;
+  const size_t R = kChunkRows, RL = kMaxRows;
   const size_t sizes[] = {
       m->kv_bytes,                                  // 0 kv
       (size_t)std::max(c.max_prefix, 1) * d * e,   // 1 prefix
@@ -310,8 +310,8 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
       R * m->qkv_n() * e,                           // 5 qkv
       R * H * hd * e, R * H * hd * e,               // 6 q, 7 attn
       R * c.ffn * e,                                // 8 mlp
-      R * (size_t)c.vocab * e,                      // 9 logits
-      R * sizeof(int),                              // 10 ys
+      RL * (size_t)c.vocab * e,                     // 9 logits
+      RL * sizeof(int),                             // 10 ys
       ws,                                           // 11 gemm workspace
       0,                                            // 12 (unused)
       argmax_scratch_bytes(kMaxRows) + 512,         // 13 argmax scratch
@@ -448,7 +448,8 @@ int model_gemm(Model* m, const QWeight& w, const void* x, int rows, void* out, i
 
 int model_forward(Model* m, PosRef pr, int rows, const int* tok, const int* P, int logits_rows, cudaStream_t s) {
   const vella_model_cfg& c = m->cfg;
-  if (rows <= 0 || rows > kMaxRows) return fail(VELLA_E_INVALID, "forward: %d rows", rows);
+  if (rows <= 0 || rows > kChunkRows || logits_rows > std::min(rows, kMaxRows))
+    return fail(VELLA_E_INVALID, "forward: %d rows, %d logits rows", rows, logits_rows);
   const int d = c.d_model, H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, dt = c.dtype;
   const float scale = 1.0f / std::sqrt((float)hd);
   int rc;

@@ -13,7 +13,8 @@
 
 namespace vella {
 
-constexpr int kMaxRows = 16;  // rows (positions) per forward launch
+constexpr int kMaxRows = 16;     // rows per decode forward and per logits launch
+constexpr int kChunkRows = 256;  // rows per prefill forward (tensor-core GEMMs above 16 rows)
 
 struct QWeight {
   void* w = nullptr;  // packed uint32 [N, K*bits/32] or dense [N, K]

@@ -427,6 +427,13 @@ bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* p) {
   if (d.k % 64 != 0) return false;
   if (d.dtype != VELLA_BF16 && d.dtype != VELLA_F16) return false;
   if (d.epilogue < VELLA_EPI_NONE || d.epilogue > VELLA_EPI_SILU_GATE) return false;
+  p->stream = false;
+  p->tc = false;
+  if (tc_eligible(d) && d.m <= (1 << 24)) {  // more than 16 rows: tensor cores, no workspace
+    p->tc = true;
+    p->workspace = 0;
+    return true;
+  }
   if (d.m > 256) return false;
   const bool gate = d.epilogue == VELLA_EPI_SILU_GATE;
   p->rows_out = gate ? 64 : 128;
@@ -472,6 +479,7 @@ int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& p, const void* x, c
                  const void* up_biases, const void* bias, const void* residual, void* out, void* ws,
                  cudaStream_t stream) {
   if (d.m == 0 || d.n == 0) return VELLA_OK;
+  if (p.tc) return tc_launch(d, x, w, scales, biases, up_w, up_scales, up_biases, bias, residual, out, stream);
   if (p.stream) {
     int* counters = static_cast<int*>(ws);
     float* partial = reinterpret_cast<float*>(static_cast<char*>(ws) + counter_region((size_t)p.rowblocks));

@@ -30,6 +30,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "sm100.cuh"
 
 namespace vella {
 
@@ -42,7 +43,6 @@ constexpr int kConsumerWarps = 4 * kGroupSets;  // 4 row sets x kGroupSets group
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kSlots = 128;
 constexpr int kTokMax = 16;
-constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at the B200 clock
 
 // UG groups of 64 per unit; BPG bytes per row and group; WCH 128-byte column chunks of the
 // weight tile; XCH 256-element chunks of the x slice.
@@ -76,46 +76,7 @@ struct SArgs {
   int has_bias, has_res;
 };
 
-__device__ __forceinline__ uint32_t saddr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-
-__device__ __forceinline__ void mbar_init(uint64_t* b, int count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(b)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(saddr(b)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait: false when the clock limit ran out (the caller records a fault).
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
-  if (mbar_try(b, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try(b, parity)) {
-    if (clock64() - t0 > kWaitCycles) return false;
-  }
-  return true;
-}
-// 2D tensor-map load (no multicast) of box (c0, c1) into shared memory, completing on bar.
-__device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          saddr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(saddr(bar))
-      : "memory");
-}
-__device__ __forceinline__ void named_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
+using namespace sm100;
 
 // CTA holding unit u when U units are split over P CTAs as [c U/P, (c+1) U/P) (U >= P).
 __device__ __forceinline__ int cta_of(long long u, long long U, int P) { return (int)(((u + 1) * P - 1) / U); }
@@ -529,40 +490,6 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_stream_kernel(const __grid_
   }
 }
 
-// ---- tensor maps --------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static std::once_flag once;
-  static EncodeTiledFn fn = nullptr;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-    else
-      cudaGetLastError();
-  });
-  return fn;
-}
-
-int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
-             uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return fail(VELLA_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  const cuuint64_t dims[2] = {inner, rows};
-  const cuuint64_t strides[1] = {row_bytes};
-  const cuuint32_t box[2] = {box_inner, box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(VELLA_E_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return VELLA_OK;
-}
-
 template <typename T, int BITS, int NT, bool GATE>
 int launch_stream_t(const SArgs& a, cudaStream_t stream) {
   using LY = Layout<BITS, NT>;
@@ -616,29 +543,29 @@ int stream_launch(const vella_qgemm_desc& d, int P, const void* x, const void* w
   const uint64_t words = (uint64_t)d.k * wbits / 32, row_bytes = (uint64_t)d.k * wbits / 8;
   const uint64_t G = d.k / 64;
   int rc;
-  if ((rc = make_map(&a.tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, words, d.n, row_bytes, 32, rows_box,
+  if ((rc = make_tensor_map(&a.tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, words, d.n, row_bytes, 32, rows_box,
                      CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
-  if (gate && (rc = make_map(&a.tu, CU_TENSOR_MAP_DATA_TYPE_UINT32, up_w, words, d.n, row_bytes, 32, rows_box,
+  if (gate && (rc = make_tensor_map(&a.tu, CU_TENSOR_MAP_DATA_TYPE_UINT32, up_w, words, d.n, row_bytes, 32, rows_box,
                              CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if (d.bits) {
-    if ((rc = make_map(&a.ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, scales, G, d.n, G * 2, 8, rows_box,
+    if ((rc = make_tensor_map(&a.ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, scales, G, d.n, G * 2, 8, rows_box,
                        CU_TENSOR_MAP_SWIZZLE_NONE)))
       return rc;
-    if ((rc = make_map(&a.tb, CU_TENSOR_MAP_DATA_TYPE_UINT16, biases, G, d.n, G * 2, 8, rows_box,
+    if ((rc = make_tensor_map(&a.tb, CU_TENSOR_MAP_DATA_TYPE_UINT16, biases, G, d.n, G * 2, 8, rows_box,
                        CU_TENSOR_MAP_SWIZZLE_NONE)))
       return rc;
     if (gate) {
-      if ((rc = make_map(&a.tus, CU_TENSOR_MAP_DATA_TYPE_UINT16, up_scales, G, d.n, G * 2, 8, rows_box,
+      if ((rc = make_tensor_map(&a.tus, CU_TENSOR_MAP_DATA_TYPE_UINT16, up_scales, G, d.n, G * 2, 8, rows_box,
                          CU_TENSOR_MAP_SWIZZLE_NONE)))
         return rc;
-      if ((rc = make_map(&a.tub, CU_TENSOR_MAP_DATA_TYPE_UINT16, up_biases, G, d.n, G * 2, 8, rows_box,
+      if ((rc = make_tensor_map(&a.tub, CU_TENSOR_MAP_DATA_TYPE_UINT16, up_biases, G, d.n, G * 2, 8, rows_box,
                          CU_TENSOR_MAP_SWIZZLE_NONE)))
         return rc;
     }
   }
-  if ((rc = make_map(&a.tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, x, d.k, d.m, (uint64_t)d.k * 2, 256, nt * 8,
+  if ((rc = make_tensor_map(&a.tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, x, d.k, d.m, (uint64_t)d.k * 2, 256, nt * 8,
                      CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
   a.bias = bias; a.res = residual; a.out = out;
@@ -661,12 +588,15 @@ int stream_launch(const vella_qgemm_desc& d, int P, const void* x, const void* w
   }
 }
 
-int stream_fault_status(int clear) {
+int stream_fault_status(int clear) {  // the flags, or -1 when they cannot be read
   int v = 0;
-  VELLA_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_stream_fault, sizeof(int)));
+  if (cudaMemcpyFromSymbol(&v, g_stream_fault, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
   if (clear && v) {
     const int zero = 0;
-    VELLA_CUDA_TRY(cudaMemcpyToSymbol(g_stream_fault, &zero, sizeof(int)));
+    if (cudaMemcpyToSymbol(g_stream_fault, &zero, sizeof(int)) != cudaSuccess) cudaGetLastError();
   }
   return v;
 }

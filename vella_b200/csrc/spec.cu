@@ -137,6 +137,15 @@ struct Spec {
 
 namespace {
 
+// A GEMM pipeline whose wait ran out of time finished without its result: the decode that
+// used it is void.  Checked once per prefill and per decode call.
+int pipeline_faults() {
+  const int st = stream_fault_status(1), tc = tc_fault_status(1);
+  if (st < 0 || tc < 0) return fail(VELLA_E_CUDA, "cannot read the kernel fault flags");
+  if (st || tc) return fail(VELLA_E_CUDA, "a GEMM pipeline wait timed out (flags 0x%x / 0x%x)", st, tc);
+  return VELLA_OK;
+}
+
 int sync_state(Spec* s) {
   VELLA_CUDA_TRY(cudaMemcpyAsync(s->hstate, s->dstate, sizeof(DevState), cudaMemcpyDeviceToHost, s->stream));
   VELLA_CUDA_TRY(cudaStreamSynchronize(s->stream));
@@ -213,23 +222,28 @@ int prefill(Spec* s, int* first) {
   VELLA_CUDA_TRY(cudaMemcpyAsync(s->dstate, &init, sizeof(DevState), cudaMemcpyHostToDevice, s->stream));
   const int* Pp = &s->dstate->P;
   int rc;
-  if (s->draft) {
-    for (int s0 = 0; s0 < s->P; s0 += kMaxRows) {
-      const int rows = std::min(kMaxRows, s->P - s0);
-      if ((rc = model_forward(s->draft, PosRef{s->draft->dzero, s0}, rows, s->tok, Pp, 0, s->stream))) return rc;
+  // Chunks of up to kChunkRows positions (tensor-core GEMMs), except the last kMaxRows
+  // positions, which run as one small-M forward: the draft's first pass recomputes position
+  // P - 1 with the small-M kernels, and a draft that shares the target's weights then holds
+  // the target's KV rows bit for bit.
+  const int tail = std::min(s->P, kMaxRows);
+  auto run = [&](Model* m, bool logits) -> int {
+    int r;
+    for (int s0 = 0; s0 < s->P - tail; s0 += kChunkRows) {
+      const int rows = std::min(kChunkRows, s->P - tail - s0);
+      if ((r = model_forward(m, PosRef{m->dzero, s0}, rows, s->tok, Pp, 0, s->stream))) return r;
     }
-  }
+    return model_forward(m, PosRef{m->dzero, s->P - tail}, tail, s->tok, Pp, logits ? 1 : 0, s->stream);
+  };
+  if (s->draft && (rc = run(s->draft, false))) return rc;
   Model* t = s->target;
-  for (int s0 = 0; s0 < s->P; s0 += kMaxRows) {
-    const int rows = std::min(kMaxRows, s->P - s0);
-    const bool last = s0 + rows >= s->P;
-    if ((rc = model_forward(t, PosRef{t->dzero, s0}, rows, s->tok, Pp, last ? 1 : 0, s->stream))) return rc;
-  }
+  if ((rc = run(t, true))) return rc;
   if ((rc = launch_kernel(prefill_finish_kernel, dim3(1), dim3(1), 0, s->stream, s->dstate, s->tok, t->ys,
                           t->nonfinite, t->err, s->max_seq)))
     return rc;
   VELLA_CUDA_TRY(cudaEventRecord(s->evp, s->stream));
   if ((rc = sync_state(s))) return rc;
+  if ((rc = pipeline_faults())) return rc;
   *first = s->hstate->newtok[0];
   return VELLA_OK;
 }
@@ -577,6 +591,7 @@ int vella_spec_decode(vella_spec* s, int32_t mode, int32_t max_tokens, int32_t* 
   s->stats.last_decode_ms = ms;
   s->stats.last_prefill_ms = pms;
   if (rc != VELLA_OK) return rc;
+  if ((rc = pipeline_faults())) return rc;
   if (result.looped) *flags |= VELLA_FLAG_LOOPED;
   if (result.capacity) *flags |= VELLA_FLAG_CAPACITY;
   const int n = (int)result.tokens.size();

@@ -1,0 +1,411 @@
+// K2: tensor-core GEMM for calls of more than 16 rows (prefill chunks, batched verify,
+// encoder projections) on the 5th-generation tensor core (tcgen05, accumulators in tensor
+// memory, operands staged in shared memory by TMA).
+//
+//   out[m, n] = epilogue( sum_k x[m, k] * W'[n, k] ),   fp32 accumulation,
+//
+// with W' = T(scale * q + bias) (T = activation dtype, one rounding per weight) for the
+// MLX-affine formats (reference SmallMGEMM.swift:491-498 layout) and W' = W for dense weights;
+// the epilogue is the library's: SiLU gate, then bias, then residual, one rounding
+// (SmallMGEMM.swift:745-753).
+//
+// CTA tile: 128 weight rows (the MMA's M side) x 128 tokens (its N side) x all of K, streamed
+// in stages of 64 K elements (one quantization group):
+//   warp 0      TMA producer: the x tile [128 tokens x 64] (128-byte swizzle, out-of-range
+//               tokens zero-filled) and the stage's weights (dense: directly into the MMA's
+//               operand tile; quantized: the raw code rows).
+//   warp 1      allocates tensor memory; one thread issues 4 MMAs (K = 16 each) per stage and
+//               commits them to the stage's "empty" barrier; frees tensor memory at the end.
+//   warps 2..5  thread = weight row: turns the stage's codes into the operand tile (128-byte
+//               swizzled K-major rows), then runs the epilogue out of tensor memory.
+// Every wait is bounded (sm100::kWaitCycles); a wait that runs out records a fault
+// (vella_qgemm reports it) and the kernel finishes without waiting again.
+//
+// A row m of the output depends only on x[m, :] and the weights: the tensor core's per-
+// element accumulation order does not involve other tokens, so a row of a batched call is
+// bit-identical to the same row in any other call of more than 16 rows.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <type_traits>
+
+#include "common.cuh"
+#include "internal.h"
+#include "sm100.cuh"
+
+namespace vella {
+
+__device__ int g_tc_fault = 0;  // set when a pipeline wait ran out of time
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kTcRows = 128;     // weight rows per CTA (MMA M)
+constexpr int kTcTok = 128;      // tokens per CTA (MMA N)
+constexpr int kTcK = 64;         // K elements per stage
+constexpr int kTcThreads = 192;  // 6 warps
+
+template <int BITS, bool GATE>
+struct TcLayout {
+  static constexpr int NA = GATE ? 2 : 1;                         // operand tiles (gate, up)
+  static constexpr int A_BYTES = kTcRows * 128;                   // [128 rows x 64] bf16/fp16
+  static constexpr int B_BYTES = kTcTok * 128;                    // [128 tokens x 64]
+  static constexpr int RAW_BYTES = BITS ? kTcRows * kTcK * BITS / 8 : 0;
+  static constexpr int STAGE = NA * A_BYTES + B_BYTES + NA * RAW_BYTES;  // multiple of 1024
+  static constexpr int NS = STAGE <= 40 * 1024 ? 5 : (STAGE <= 48 * 1024 ? 4 : 3);
+  static constexpr int TX = B_BYTES + (BITS ? NA * RAW_BYTES : NA * A_BYTES);
+  static constexpr int BAR = NS * STAGE;  // barrier block offset
+  static constexpr int TOTAL = 1024 + BAR + (3 * NS + 1) * 8 + 16;
+  static constexpr uint32_t COLS = GATE ? 2 * kTcTok : kTcTok;  // tensor-memory columns
+  static_assert(STAGE % 1024 == 0, "stage tiles must stay 1024-byte aligned");
+  static_assert(TOTAL <= 227 * 1024, "shared memory");
+};
+
+struct TcArgs {
+  CUtensorMap tx, tw, tu;  // x; weights (dense tile or raw codes); up weights (gate)
+  const void* s;           // scales  [N, K/64]
+  const void* b;           // biases  [N, K/64]
+  const void* us;          // up scales
+  const void* ub;          // up biases
+  const void* bias;        // [N] or null
+  const void* res;         // [M, N] or null
+  void* out;               // [M, N]
+  int M, N, K, G;
+};
+
+// One weight row's 64 codes of a stage -> 8 chunks of 8 operand elements (16 bytes each).
+// Codes are exact in T as magic + q (bf16: 128 + q for 4-bit codes; fp16: 1024 + q for 4- and
+// 8-bit codes); subtracting the magic is exact, the fma rounds once.  8-bit codes with bf16
+// go through fp32 (bf16 cannot hold 128 + q for q >= 128).
+template <typename T, int BITS>
+__device__ __forceinline__ void dequant_row(const uint32_t* raw, T s, T b, uint4 (&o)[8]) {
+  using A = Act<T>;
+  if constexpr (BITS == 8 && sizeof(T) == 2 && A::kMagic == 128.0f) {  // bf16, 8-bit codes
+    const float fs = A::to_f(s), fb = A::to_f(b);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint32_t w2[2] = {raw[2 * c], raw[2 * c + 1]};
+      uint32_t r[4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const float f0 = __uint_as_float(__byte_perm(w2[h], 0x4B000000u, 0x7440 + 2 * p)) - 8388608.0f;
+          const float f1 = __uint_as_float(__byte_perm(w2[h], 0x4B000000u, 0x7441 + 2 * p)) - 8388608.0f;
+          const __nv_bfloat162 v = __floats2bfloat162_rn(fmaf(f0, fs, fb), fmaf(f1, fs, fb));
+          r[2 * h + p] = *reinterpret_cast<const uint32_t*>(&v);
+        }
+      }
+      o[c] = make_uint4(r[0], r[1], r[2], r[3]);
+    }
+  } else {
+    using V2 = typename std::conditional<sizeof(T) == 2 && A::kMagic == 128.0f, __nv_bfloat162, __half2>::type;
+    const uint32_t mag = A::kMagic2;
+    V2 s2, b2, m2;
+    *reinterpret_cast<T*>(&s2) = s; *(reinterpret_cast<T*>(&s2) + 1) = s;
+    *reinterpret_cast<T*>(&b2) = b; *(reinterpret_cast<T*>(&b2) + 1) = b;
+    *reinterpret_cast<uint32_t*>(&m2) = mag;
+    auto fin = [&](uint32_t v) {
+      V2 q = *reinterpret_cast<V2*>(&v);
+      q = __hsub2(q, m2);
+      const V2 r = __hfma2(q, s2, b2);
+      return *reinterpret_cast<const uint32_t*>(&r);
+    };
+    if constexpr (BITS == 4) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t w = raw[c];  // elements 8c .. 8c+7, low nibble first
+        const uint32_t p04 = and_or(w, 0x000F000Fu, mag), p15 = and_or(w >> 4, 0x000F000Fu, mag);
+        const uint32_t p26 = and_or(w >> 8, 0x000F000Fu, mag), p37 = and_or(w >> 12, 0x000F000Fu, mag);
+        o[c] = make_uint4(fin(__byte_perm(p04, p15, 0x5410)), fin(__byte_perm(p26, p37, 0x5410)),
+                          fin(__byte_perm(p04, p15, 0x7632)), fin(__byte_perm(p26, p37, 0x7632)));
+      }
+    } else {  // fp16, 8-bit codes
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t r[4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t w = raw[2 * c + h];  // elements 8c + 4h .. +3, low byte first
+          const uint32_t p02 = and_or(w, 0x00FF00FFu, mag), p13 = and_or(w >> 8, 0x00FF00FFu, mag);
+          r[2 * h] = fin(__byte_perm(p02, p13, 0x5410));
+          r[2 * h + 1] = fin(__byte_perm(p02, p13, 0x7632));
+        }
+        o[c] = make_uint4(r[0], r[1], r[2], r[3]);
+      }
+    }
+  }
+}
+
+template <typename T, int BITS, bool GATE>
+__global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ TcArgs a) {
+  using A = Act<T>;
+  using LY = TcLayout<BITS, GATE>;
+  constexpr int NS = LY::NS;
+  constexpr int WPG = BITS ? kTcK * BITS / 32 : 0;  // 32-bit code words per row and stage
+  constexpr uint32_t IDESC = f16_idesc(A::kMagic == 128.0f, kTcRows, kTcTok);
+
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + LY::BAR);
+  uint64_t* ready = full + NS;
+  uint64_t* empty = ready + NS;
+  uint64_t* accf = empty + NS;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
+  auto tileA = [&](int st, int i) { return smem + st * LY::STAGE + i * LY::A_BYTES; };
+  auto tileB = [&](int st) { return smem + st * LY::STAGE + LY::NA * LY::A_BYTES; };
+  auto tileR = [&](int st, int i) { return smem + st * LY::STAGE + LY::NA * LY::A_BYTES + LY::B_BYTES + i * LY::RAW_BYTES; };
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tok0 = blockIdx.x * kTcTok, row0 = blockIdx.y * kTcRows;
+  const int G = a.G;
+
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accf, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(tslot, LY::COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  pdl_launch_next();
+
+  if (warp == 0) {
+    // ---- TMA producer ---------------------------------------------------------------------
+    if (lane == 0) {
+      auto weights = [&](int g, int st) {
+        if constexpr (BITS == 0) {
+          tma2d(tileA(st, 0), &a.tw, g * kTcK, row0, &full[st]);
+          if constexpr (GATE) tma2d(tileA(st, 1), &a.tu, g * kTcK, row0, &full[st]);
+        } else {
+          tma2d(tileR(st, 0), &a.tw, g * WPG, row0, &full[st]);
+          if constexpr (GATE) tma2d(tileR(st, 1), &a.tu, g * WPG, row0, &full[st]);
+        }
+      };
+      const int npre = min(G, NS);
+      for (int g = 0; g < npre; ++g) {
+        mbar_expect_tx(&full[g], LY::TX);
+        weights(g, g);
+      }
+      pdl_wait();  // x is written by the previous kernel
+      for (int g = 0; g < npre; ++g) tma2d(tileB(g), &a.tx, g * kTcK, tok0, &full[g]);
+      int issued = npre;
+      for (int g = npre; g < G; ++g) {
+        const int st = g % NS, use = g / NS;
+        if (!mbar_wait(&empty[st], (uint32_t)((use - 1) & 1))) {
+          atomicOr(&g_tc_fault, 1);
+          break;
+        }
+        mbar_expect_tx(&full[st], LY::TX);
+        weights(g, st);
+        tma2d(tileB(st), &a.tx, g * kTcK, tok0, &full[st]);
+        issued = g + 1;
+      }
+      // every copy issued must land before the CTA may exit
+      for (int g = max(0, issued - NS); g < issued; ++g)
+        if (!mbar_wait(&full[g % NS], (uint32_t)((g / NS) & 1))) atomicOr(&g_tc_fault, 2);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ---------------------------------------------------------------------
+    pdl_wait();
+    if (lane == 0) {
+      for (int g = 0; g < G; ++g) {
+        const int st = g % NS;
+        const uint32_t par = (uint32_t)((g / NS) & 1);
+        if (!mbar_wait(BITS ? &ready[st] : &full[st], par)) {
+          atomicOr(&g_tc_fault, 4);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = saddr(tileA(st, 0)), b0 = saddr(tileB(st));
+#pragma unroll
+        for (int kk = 0; kk < kTcK / 16; ++kk) {
+          const uint64_t bd = kmajor_sw128_desc(b0 + kk * 32);
+          const uint32_t acc = (g > 0 || kk > 0) ? 1u : 0u;
+          mma_f16_ss(tmem, kmajor_sw128_desc(a0 + kk * 32), bd, IDESC, acc);
+          if constexpr (GATE) mma_f16_ss(tmem + kTcTok, kmajor_sw128_desc(saddr(tileA(st, 1)) + kk * 32), bd, IDESC, acc);
+        }
+        mma_commit(&empty[st]);
+      }
+      mma_commit(accf);  // arrives when every MMA above has completed
+    }
+    __syncwarp();
+  } else {
+    // ---- transform (quantized formats) and epilogue: thread = weight row -------------------
+    pdl_wait();
+    const int r = 32 * (warp & 3) + lane;  // tensor-memory lane of this warp's window
+    const int n = row0 + r;
+    const bool nv = n < a.N;
+    if constexpr (BITS != 0) {
+      const T* sp = static_cast<const T*>(a.s) + (size_t)(nv ? n : 0) * G;
+      const T* bp = static_cast<const T*>(a.b) + (size_t)(nv ? n : 0) * G;
+      const T* usp = static_cast<const T*>(a.us) + (size_t)(nv ? n : 0) * G;
+      const T* ubp = static_cast<const T*>(a.ub) + (size_t)(nv ? n : 0) * G;
+      const T zero = A::from_f(0.0f);
+      T s0 = nv ? sp[0] : zero, b0 = nv ? bp[0] : zero, us0 = zero, ub0 = zero;
+      if constexpr (GATE) { us0 = nv ? usp[0] : zero; ub0 = nv ? ubp[0] : zero; }
+      for (int g = 0; g < G; ++g) {
+        const int st = g % NS;
+        // next group's scale and bias, fetched while this stage's codes are in flight
+        const bool more = nv && g + 1 < G;
+        const T s1 = more ? sp[g + 1] : zero, b1 = more ? bp[g + 1] : zero;
+        T us1 = zero, ub1 = zero;
+        if constexpr (GATE) { us1 = more ? usp[g + 1] : zero; ub1 = more ? ubp[g + 1] : zero; }
+        if (!mbar_wait(&full[st], (uint32_t)((g / NS) & 1))) {
+          atomicOr(&g_tc_fault, 8);
+          break;
+        }
+#pragma unroll
+        for (int i = 0; i < LY::NA; ++i) {
+          const uint4* src = reinterpret_cast<const uint4*>(tileR(st, i) + r * WPG * 4);
+          uint32_t raw[WPG];
+#pragma unroll
+          for (int v = 0; v < WPG / 4; ++v) {
+            const uint4 q = src[v];
+            raw[4 * v] = q.x; raw[4 * v + 1] = q.y; raw[4 * v + 2] = q.z; raw[4 * v + 3] = q.w;
+          }
+          uint4 o[8];
+          dequant_row<T, BITS>(raw, i ? us0 : s0, i ? ub0 : b0, o);
+          unsigned char* dst = tileA(st, i) + r * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + ((c ^ (r & 7)) << 4)) = o[c];
+        }
+        fence_proxy_async();
+        mbar_arrive(&ready[st]);
+        s0 = s1; b0 = b1;
+        if constexpr (GATE) { us0 = us1; ub0 = ub1; }
+      }
+    }
+    // ---- epilogue ------------------------------------------------------------------------
+    const bool ok = mbar_wait(accf, 0);
+    tc_fence_after();
+    if (!ok) {
+      atomicOr(&g_tc_fault, 16);
+    } else {
+      const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+      const T* bias = static_cast<const T*>(a.bias);
+      const T* res = static_cast<const T*>(a.res);
+      T* out = static_cast<T*>(a.out);
+      const float bn = (bias && nv) ? A::to_f(bias[n]) : 0.0f;
+      for (int c0 = 0; c0 < kTcTok && tok0 + c0 < a.M; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_base + c0, v);
+        uint32_t u[32];
+        if constexpr (GATE) tmem_ld32(tmem + lane_base + kTcTok + c0, u);
+        if (nv) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int m = tok0 + c0 + j;
+            if (m < a.M) {
+              float y = __uint_as_float(v[j]);
+              if constexpr (GATE) y = y / (1.0f + expf(-y)) * __uint_as_float(u[j]);
+              y += bn;
+              if (res) y += A::to_f(res[(size_t)m * a.N + n]);
+              out[(size_t)m * a.N + n] = A::from_f(y);
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, LY::COLS);
+}
+
+template <typename T, int BITS, bool GATE>
+int launch_tc_t(const TcArgs& a, cudaStream_t stream) {
+  using LY = TcLayout<BITS, GATE>;
+  auto k = tc_gemm_kernel<T, BITS, GATE>;
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  VELLA_CUDA_TRY(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    VELLA_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::TOTAL));
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  const dim3 grid((a.M + kTcTok - 1) / kTcTok, (a.N + kTcRows - 1) / kTcRows);
+  return launch_kernel(k, grid, dim3(kTcThreads), LY::TOTAL, stream, a);
+}
+
+template <typename T, int BITS>
+int dispatch_tc(const TcArgs& a, bool gate, cudaStream_t s) {
+  return gate ? launch_tc_t<T, BITS, true>(a, s) : launch_tc_t<T, BITS, false>(a, s);
+}
+
+}  // namespace
+
+// Calls of more than 16 rows with K % 64 == 0 (and every pointer 16-byte aligned, checked by
+// the caller).
+bool tc_eligible(const vella_qgemm_desc& d) {
+  return d.m > 16 && d.k >= kTcK && d.k % kTcK == 0 && (d.bits == 0 || d.bits == 4 || d.bits == 8) &&
+         (d.dtype == VELLA_BF16 || d.dtype == VELLA_F16);
+}
+
+int tc_launch(const vella_qgemm_desc& d, const void* x, const void* w, const void* scales, const void* biases,
+              const void* up_w, const void* up_scales, const void* up_biases, const void* bias,
+              const void* residual, void* out, cudaStream_t stream) {
+  const bool gate = d.epilogue == VELLA_EPI_SILU_GATE;
+  TcArgs a{};
+  a.s = scales; a.b = biases; a.us = up_scales; a.ub = up_biases;
+  a.bias = (d.epilogue == VELLA_EPI_BIAS || d.epilogue == VELLA_EPI_BIAS_RESIDUAL) ? bias : nullptr;
+  a.res = (d.epilogue == VELLA_EPI_RESIDUAL || d.epilogue == VELLA_EPI_BIAS_RESIDUAL) ? residual : nullptr;
+  a.out = out;
+  a.M = d.m; a.N = d.n; a.K = d.k; a.G = d.k / kTcK;
+  int rc;
+  const uint64_t xrow = (uint64_t)d.k * 2;
+  if ((rc = make_tensor_map(&a.tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, x, d.k, d.m, xrow, kTcK, kTcTok,
+                            CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if (d.bits == 0) {
+    if ((rc = make_tensor_map(&a.tw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w, d.k, d.n, xrow, kTcK, kTcRows,
+                              CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
+    if (gate && (rc = make_tensor_map(&a.tu, CU_TENSOR_MAP_DATA_TYPE_UINT16, up_w, d.k, d.n, xrow, kTcK, kTcRows,
+                                      CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
+  } else {
+    const uint64_t words = (uint64_t)d.k * d.bits / 32;
+    const uint32_t wpg = kTcK * d.bits / 32;
+    if ((rc = make_tensor_map(&a.tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, words, d.n, words * 4, wpg, kTcRows,
+                              CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return rc;
+    if (gate && (rc = make_tensor_map(&a.tu, CU_TENSOR_MAP_DATA_TYPE_UINT32, up_w, words, d.n, words * 4, wpg,
+                                      kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return rc;
+  }
+  const bool bf = d.dtype == VELLA_BF16;
+  switch (d.bits) {
+    case 0: return bf ? dispatch_tc<__nv_bfloat16, 0>(a, gate, stream) : dispatch_tc<__half, 0>(a, gate, stream);
+    case 4: return bf ? dispatch_tc<__nv_bfloat16, 4>(a, gate, stream) : dispatch_tc<__half, 4>(a, gate, stream);
+    default: return bf ? dispatch_tc<__nv_bfloat16, 8>(a, gate, stream) : dispatch_tc<__half, 8>(a, gate, stream);
+  }
+}
+
+int tc_fault_status(int clear) {  // the flags, or -1 when they cannot be read
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_tc_fault, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  if (clear && v) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_tc_fault, &zero, sizeof(int)) != cudaSuccess) cudaGetLastError();
+  }
+  return v;
+}
+
+}  // namespace vella
