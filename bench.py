@@ -37,7 +37,9 @@ def peaks():
 
 
 def gemm_bytes(m, n, k, bits):
-    return n * k * bits // 8 + n * (k // 64) * 4 + m * k * 2 + m * n * 2
+    """Algorithmic bytes of one call: weights (+ bf16 scales/biases when quantized), x, out."""
+    wbytes = n * k * bits // 8 + n * (k // 64) * 4 if bits else n * k * 2
+    return wbytes + m * k * 2 + m * n * 2
 
 
 class ClockSampler:
@@ -142,12 +144,16 @@ def run_gemm(args, rank, world):
     with torch.cuda.stream(stream):
         for bits, n, k, ms in cases:
             w = torch.randn(n, k, generator=g, device=dev) * 0.02
-            packed, sc, bi = quantize_gpu(w, bits)
-            del w
             wbytes = gemm_bytes(0, n, k, bits)
             copies = max(2, -(-3 * L2_BYTES // wbytes))
-            ws = [S.Weights(packed, sc, bi, bits)] + [
-                S.Weights(packed.clone(), sc.clone(), bi.clone(), bits) for _ in range(copies - 1)]
+            if bits:
+                packed, sc, bi = quantize_gpu(w, bits)
+                ws = [S.Weights(packed, sc, bi, bits)] + [
+                    S.Weights(packed.clone(), sc.clone(), bi.clone(), bits) for _ in range(copies - 1)]
+            else:
+                wd = w.to(torch.bfloat16)
+                ws = [S.Weights(wd, bits=0)] + [S.Weights(wd.clone(), bits=0) for _ in range(copies - 1)]
+            del w
             for m in ms:
                 x = (torch.randn(m, k, generator=g, device=dev)).to(torch.bfloat16)
                 out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
@@ -189,7 +195,8 @@ def run_gemm(args, rank, world):
         e1.synchronize()
         us = e0.elapsed_time(e1) * 1000 / (4 * reps)
         per.append({"bits": bits, "n": n, "k": k, "m": m, "us": round(us, 3),
-                    "gbs": round(gemm_bytes(m, n, k, bits) / us / 1e3, 1)})
+                    "gbs": round(gemm_bytes(m, n, k, bits) / us / 1e3, 1),
+                    "tflops": round(2.0 * m * n * k / us / 1e6, 1)})
     with ClockSampler(dev.index) as clk:
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
