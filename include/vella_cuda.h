@@ -56,7 +56,11 @@ enum {
   VELLA_EPI_BIAS = 1,          /* + bias[n]                                               */
   VELLA_EPI_RESIDUAL = 2,      /* + residual[m, n]                                        */
   VELLA_EPI_BIAS_RESIDUAL = 3, /* + bias[n] + residual[m, n]                              */
-  VELLA_EPI_SILU_GATE = 4      /* silu(x . Wg^T) * (x . Wu^T); W = gate, `up_*` = up      */
+  VELLA_EPI_SILU_GATE = 4,     /* silu(x . Wg^T) * (x . Wu^T); W = gate, `up_*` = up      */
+  /* Whisper's fc1 and convolutions (no counterpart in SmallMGEMM, whose epilogues end above):
+   * gelu(acc + bias[n]) with the erf form of GELU, optionally + residual[m, n] after it. */
+  VELLA_EPI_BIAS_GELU = 5,
+  VELLA_EPI_BIAS_GELU_RESIDUAL = 6
 };
 
 /*
@@ -249,6 +253,67 @@ VELLA_API int vella_spec_get_stats(const vella_spec* spec, vella_spec_stats* out
 VELLA_API int vella_spec_set_fault(vella_spec* spec, int32_t fault);
 /* Clear the sticky fallback and the statistics. */
 VELLA_API int vella_spec_reset(vella_spec* spec);
+
+/* ---- Whisper encoder + decoder step ------------------------------------------------------
+ *
+ * Replaces WhisperModel's encoder call and WhisperFusedDecoder.step / pipelinedGreedy
+ * (Worker/Sources/MLXAudioSTT/Whisper/WhisperLayers.swift:110-329, WhisperFusedDecode.swift:
+ * 105-141, WhisperModel.swift:341-400) for one audio stream: the encoder (conv1 -> GELU ->
+ * conv2 -> GELU -> + sinusoid positions -> pre-LN blocks -> LayerNorm), the cross-attention
+ * K/V of every decoder layer projected once, then decoder steps (self-attention over the KV
+ * cache, cross-attention over the encoder frames, GELU MLP, tied vocabulary projection) with
+ * plain greedy argmax on the device, one CUDA graph per step.  The token rules of the
+ * reference's greedy (suppression, timestamps) are not applied.
+ */
+typedef struct vella_whisper_cfg {
+  int32_t n_mels;      /* mel bins (80 | 128)                                           */
+  int32_t d_model;     /* multiple of 64; head_dim = d_model / heads must be 64 or 128   */
+  int32_t heads;
+  int32_t enc_layers;
+  int32_t dec_layers;
+  int32_t ffn;         /* multiple of 64 */
+  int32_t vocab;
+  int32_t n_audio;     /* encoder frames = mel frames / 2 (1500 for 30 s) */
+  int32_t max_target;  /* decoder positions (448) */
+  int32_t bits;        /* decoder Linears and token embedding: 0 (dense), 4 or 8 (MLX affine, g64) */
+  int32_t dtype;       /* VELLA_F16 | VELLA_BF16 */
+  float eps;           /* LayerNorm epsilon (1e-5) */
+} vella_whisper_cfg;
+
+typedef struct vella_whisper_stats {
+  float encode_ms;   /* last vella_whisper_encode: encoder + cross K/V projections (device time) */
+  float prefill_ms;  /* last decode: the prompt's forward and first token                     */
+  float decode_ms;   /* last decode: every following step                                     */
+  int32_t tokens;    /* tokens produced by the last decode                                    */
+} vella_whisper_stats;
+
+typedef struct vella_whisper vella_whisper;
+
+VELLA_API int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whisper** out);
+VELLA_API int vella_whisper_destroy(vella_whisper* w);
+/* Synthetic weights: Linears ~N(0, std) (decoder Linears and the token embedding quantized
+ * when bits != 0), biases ~N(0, std) except k_proj's (zero), LayerNorm gains ~N(1, 0.1) and
+ * offsets ~N(0, std), encoder positions = the sinusoid table, decoder positions ~N(0, std). */
+VELLA_API int vella_whisper_init_random(vella_whisper* w, uint64_t seed, float std);
+/* Device view of a tensor (layer = -1 for whole-model tensors).  Linears: "<name>.w" (dense
+ * [N, K] or packed codes), "<name>.s", "<name>.b" (MLX scales/biases), "<name>.bias";
+ * LayerNorms: "<name>.weight", "<name>.bias".  Encoder layers: enc.ln1, enc.qkv (q|k|v rows,
+ * k's bias zero), enc.o, enc.ln2, enc.fc1, enc.fc2; decoder layers: dec.ln1, dec.qkv, dec.o,
+ * dec.ln2, dec.cq, dec.ckv (cross k|v rows, k's bias zero), dec.co, dec.ln3, dec.fc1, dec.fc2;
+ * whole model: conv1 (K padded to a multiple of 64 with zero columns), conv2, enc_pos,
+ * enc_ln, dec_ln, embed (token embedding = vocabulary projection), dec_pos, and the
+ * activation enc_out [n_audio, d_model]. */
+VELLA_API int vella_whisper_tensor(vella_whisper* w, const char* name, int32_t layer, void** ptr, size_t* bytes);
+/* Encoder over one window: mel fp32 [n_mels][2 * n_audio] (host or device), then the cross-
+ * attention K/V of every decoder layer. */
+VELLA_API int vella_whisper_encode(vella_whisper* w, const float* mel, int32_t on_host);
+/* Greedy decode after the prompt (n_prompt <= 16 tokens): up to max_tokens tokens, stopping
+ * after `eot` when eot >= 0 (not emitted).  out_tokens (host) receives *n_out tokens. */
+VELLA_API int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int32_t n_prompt, int32_t max_tokens,
+                                   int32_t eot, int32_t* out_tokens, int32_t* n_out);
+/* Teacher-forced logits [T, vocab] (dtype) of the token sequence (positions 0..T-1). */
+VELLA_API int vella_whisper_score(vella_whisper* w, const int32_t* tokens, int32_t T, void* logits, int32_t on_host);
+VELLA_API int vella_whisper_get_stats(const vella_whisper* w, vella_whisper_stats* out);
 
 /* Message of the last failing call on this thread ("" when none); returns its length. */
 VELLA_API size_t vella_last_error(char* buf, size_t cap);

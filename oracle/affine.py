@@ -168,7 +168,7 @@ def error_in_steps(source, packed, scales, biases, bits: int, dtype: str = "bf16
 # the GEMM
 # ---------------------------------------------------------------------------------------
 
-EPILOGUES = ("none", "bias", "residual", "biasResidual", "siluGate")
+EPILOGUES = ("none", "bias", "residual", "biasResidual", "siluGate", "biasGelu", "biasGeluResidual")
 
 
 def _affine_acc(x32: np.ndarray, packed, scales, biases, bits: int, dtype: str, chunk: int = 4096):
@@ -192,6 +192,13 @@ def _affine_acc(x32: np.ndarray, packed, scales, biases, bits: int, dtype: str, 
 
 def _dense_acc(x32: np.ndarray, w, dtype: str) -> np.ndarray:
     return x32 @ from_storage(w, dtype).T
+
+
+def gelu(a: np.ndarray) -> np.ndarray:
+    """GELU, erf form (MLX's default ``gelu``, used by the Whisper MLP and convolutions)."""
+    from scipy.special import erf
+    a = np.asarray(a, np.float32)
+    return (0.5 * a * (1.0 + erf(a / np.float32(np.sqrt(2.0))).astype(np.float32))).astype(np.float32)
 
 
 def silu(a: np.ndarray) -> np.ndarray:
@@ -218,9 +225,11 @@ def qgemm(x, w, scales=None, biases=None, *, bits: int = 4, dtype: str = "bf16",
     if epilogue == "siluGate":
         u = acc(*up)
         a = silu(a) * u
-    if epilogue in ("bias", "biasResidual"):
+    if epilogue in ("bias", "biasResidual", "biasGelu", "biasGeluResidual"):
         a = a + from_storage(bias, dtype)[None, :]
-    if epilogue in ("residual", "biasResidual"):
+    if epilogue in ("biasGelu", "biasGeluResidual"):
+        a = gelu(a)
+    if epilogue in ("residual", "biasResidual", "biasGeluResidual"):
         a = a + from_storage(residual, dtype)
     a = a.astype(np.float32)
     return a if raw else to_storage(a, dtype)

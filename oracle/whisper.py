@@ -1,0 +1,217 @@
+"""CPU restatement of the Whisper encoder and decoder step (test infrastructure only).
+
+Follows the reference's Whisper layers and fused decode step:
+  * encoder — ``Worker/Sources/MLXAudioSTT/Whisper/WhisperLayers.swift:110-157``: conv1 (k 3,
+    s 1, p 1) -> GELU -> conv2 (k 3, s 2, p 1) -> GELU -> + sinusoid positions -> pre-LN
+    blocks (self-attention without mask, GELU MLP) -> final LayerNorm;
+  * attention — ``:11-73``: k_proj has no bias, scale head_dim ** -0.5;
+  * decoder — ``:170-329`` and the fused step ``WhisperFusedDecode.swift:105-141``: token +
+    learned position embedding, per layer self-attention over the KV cache (causal), cross-
+    attention over the encoder output (K/V projected once), GELU MLP, each behind a
+    LayerNorm with a residual add; final LayerNorm; logits through the tied token embedding
+    (``:326-328``); q|k|v of the self-attention as one projection with k's bias zero
+    (``WhisperFusedDecode.swift:67-88``);
+  * sinusoids — ``WhisperModel.swift:554-569``: double-precision trig rounded to fp32, then
+    to the table dtype;
+  * quantization recipe of config 1 — ``WhisperModel.swift:697-703``: every decoder Linear and
+    the token embedding MLX-affine (group 64), positional tables float.
+
+Arithmetic as the library's kernels store it: every GEMM accumulates in fp32 and rounds
+once after its epilogue (bias, GELU, residual); LayerNorm statistics in fp32 with the
+normalised value rounded to the activation dtype before ``w * x + b`` (``WhisperFusedDecode
+.swift:204-251``, the MLX row algorithm, here with one final rounding); GELU is the erf form.
+Plain greedy argmax (the reference's suppress/timestamp rules are not part of this path).
+
+Parity: the reference (Swift + MLX) cannot run on this machine; the floating-point
+arithmetic is parity unpinned against MLX.  The sinusoid table rule is pinned by the
+reference test ``WhisperStockDTypeTests.swift:42-46`` (table shape and dtype).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import affine as A
+from . import decoder as D
+
+
+@dataclass
+class WhisperConfig:
+    n_mels: int = 80
+    d_model: int = 384
+    heads: int = 6
+    enc_layers: int = 4
+    dec_layers: int = 4
+    ffn: int = 1536
+    vocab: int = 51865
+    n_audio: int = 1500        # encoder frames (3000 mel frames / 2)
+    max_target: int = 448
+    bits: int = 4              # decoder Linears and token embedding (0: dense)
+    dtype: str = "f16"
+    eps: float = 1e-5
+
+    @property
+    def head_dim(self) -> int:
+        return self.d_model // self.heads
+
+
+def sinusoids(length: int, channels: int, dtype: str = "f16") -> np.ndarray:
+    """WhisperModel.swift:554-569: Double trig -> Float32, rounded once to the table dtype."""
+    half = channels // 2
+    inc = math.log(10000.0) / max(half - 1, 1)
+    out = np.empty((length, channels), np.float32)
+    for i in range(half):
+        t = np.arange(length, dtype=np.float64) * math.exp(-inc * i)
+        out[:, i] = np.sin(t).astype(np.float32)
+        out[:, half + i] = np.cos(t).astype(np.float32)
+    return A.from_storage(A.to_storage(out, dtype), dtype)
+
+
+def rnd(x: np.ndarray, dtype: str) -> np.ndarray:
+    return A.from_storage(A.to_storage(np.asarray(x, np.float32), dtype), dtype)
+
+
+def layernorm(x: np.ndarray, w: np.ndarray, b: np.ndarray, eps: float, dtype: str) -> np.ndarray:
+    x = x.astype(np.float32)
+    mean = x.mean(axis=-1, keepdims=True, dtype=np.float32)
+    c = x - mean
+    var = (c * c).mean(axis=-1, keepdims=True, dtype=np.float32)
+    xh = rnd(c / np.sqrt(var + np.float32(eps)), dtype)
+    return rnd(w.astype(np.float32) * xh + b.astype(np.float32), dtype)
+
+
+def linear(x, W, bits, dtype, bias=None, gelu_out=False, residual=None):
+    """GEMM with the library's epilogue: fp32 accumulation, + bias, GELU, + residual, one rounding."""
+    xs = A.to_storage(x, dtype)
+    acc = A.qgemm(xs, W["w"], W.get("s"), W.get("b"), bits=bits, dtype=dtype, raw=True)
+    if bias is not None:
+        acc = acc + bias.astype(np.float32)[None, :]
+    if gelu_out:
+        acc = A.gelu(acc)
+    if residual is not None:
+        acc = acc + residual.astype(np.float32)
+    return rnd(acc, dtype)
+
+
+def attention(q, k, v, heads, causal_pos=None):
+    """q [Tq, d], k/v [Tk, d] (rows = positions); causal_pos[i] = position of query i (keys
+    <= it visible) or None (all keys)."""
+    Tq, d = q.shape
+    hd = d // heads
+    pos = causal_pos if causal_pos is not None else np.full(Tq, k.shape[0] - 1)
+    out = D.attention(q.reshape(Tq, heads, hd), k.reshape(-1, heads, hd), v.reshape(-1, heads, hd),
+                      np.asarray(pos), hd ** -0.5, "f32")
+    return out.reshape(Tq, d)
+
+
+def im2col(x: np.ndarray, stride: int) -> np.ndarray:
+    """x [T, C] channels-last -> [T_out, 3*C] rows [x[s*t-1], x[s*t], x[s*t+1]] (zero padded)."""
+    T, C = x.shape
+    xp = np.zeros((T + 2, C), np.float32)
+    xp[1:-1] = x
+    To = (T + 2 - 3) // stride + 1
+    idx = np.arange(To) * stride
+    return np.concatenate([xp[idx], xp[idx + 1], xp[idx + 2]], axis=1)
+
+
+def encoder(cfg: WhisperConfig, W: dict, mel: np.ndarray) -> np.ndarray:
+    """mel [n_mels, 2 * n_audio] -> encoder output [n_audio, d] (values of the activation dtype)."""
+    dt = cfg.dtype
+    x = rnd(mel.T, dt)
+    c1 = im2col(x, 1)
+    kp = W["conv1"]["w"].shape[1]  # conv1's K padded to a multiple of 64 with zero columns
+    c1 = np.pad(c1, ((0, 0), (0, kp - c1.shape[1])))
+    h = linear(c1, W["conv1"], 0, dt, bias=W["conv1_b"], gelu_out=True)
+    h = linear(im2col(h, 2), W["conv2"], 0, dt, bias=W["conv2_b"], gelu_out=True, residual=W["enc_pos"])
+    d = cfg.d_model
+    for L in W["enc"]:
+        n = layernorm(h, L["ln1_w"], L["ln1_b"], cfg.eps, dt)
+        qkv = linear(n, L["qkv"], 0, dt, bias=L["qkv_b"])
+        a = rnd(attention(qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:], cfg.heads), dt)
+        h = linear(a, L["o"], 0, dt, bias=L["o_b"], residual=h)
+        n = layernorm(h, L["ln2_w"], L["ln2_b"], cfg.eps, dt)
+        f = linear(n, L["fc1"], 0, dt, bias=L["fc1_b"], gelu_out=True)
+        h = linear(f, L["fc2"], 0, dt, bias=L["fc2_b"], residual=h)
+    return layernorm(h, W["enc_ln_w"], W["enc_ln_b"], cfg.eps, dt)
+
+
+def cross_kv(cfg: WhisperConfig, W: dict, enc: np.ndarray):
+    """Cross-attention K/V of every decoder layer (k|v as one projection, k's bias zero),
+    projected once per audio window."""
+    d = cfg.d_model
+    out = []
+    for L in W["dec"]:
+        kv = linear(enc, L["ckv"], cfg.bits, cfg.dtype, bias=L["ckv_b"])
+        out.append((kv[:, :d], kv[:, d:]))
+    return out
+
+
+def token_embedding(cfg: WhisperConfig, W: dict, tokens) -> np.ndarray:
+    E = W["embed"]
+    toks = np.asarray(tokens)
+    if cfg.bits:
+        q = A.unpack(E["w"][toks], cfg.bits).astype(np.float32)
+        s = A.from_storage(E["s"][toks], cfg.dtype).repeat(64, axis=1)
+        b = A.from_storage(E["b"][toks], cfg.dtype).repeat(64, axis=1)
+        return rnd(s * q + b, cfg.dtype)
+    return A.from_storage(E["w"][toks], cfg.dtype)
+
+
+def decoder_forward(cfg: WhisperConfig, W: dict, xkv, tokens, start: int, cache: list) -> np.ndarray:
+    """Runs `tokens` at positions start.. through the decoder; appends to `cache` (per layer
+    [K rows, V rows]); returns the final-LayerNorm hidden states [T, d]."""
+    dt = cfg.dtype
+    T = len(tokens)
+    pos = np.arange(start, start + T)
+    h = rnd(token_embedding(cfg, W, tokens) + W["dec_pos"][pos], dt)
+    d = cfg.d_model
+    for li, L in enumerate(W["dec"]):
+        n = layernorm(h, L["ln1_w"], L["ln1_b"], cfg.eps, dt)
+        qkv = linear(n, L["qkv"], cfg.bits, dt, bias=L["qkv_b"])
+        q, k, v = qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:]
+        cache[li][0] = np.concatenate([cache[li][0], k]) if cache[li][0] is not None else k
+        cache[li][1] = np.concatenate([cache[li][1], v]) if cache[li][1] is not None else v
+        a = rnd(attention(q, cache[li][0], cache[li][1], cfg.heads, pos), dt)
+        h = linear(a, L["o"], cfg.bits, dt, bias=L["o_b"], residual=h)
+        n = layernorm(h, L["ln2_w"], L["ln2_b"], cfg.eps, dt)
+        q2 = linear(n, L["cq"], cfg.bits, dt, bias=L["cq_b"])
+        a = rnd(attention(q2, xkv[li][0], xkv[li][1], cfg.heads), dt)
+        h = linear(a, L["co"], cfg.bits, dt, bias=L["co_b"], residual=h)
+        n = layernorm(h, L["ln3_w"], L["ln3_b"], cfg.eps, dt)
+        f = linear(n, L["fc1"], cfg.bits, dt, bias=L["fc1_b"], gelu_out=True)
+        h = linear(f, L["fc2"], cfg.bits, dt, bias=L["fc2_b"], residual=h)
+    return layernorm(h, W["dec_ln_w"], W["dec_ln_b"], cfg.eps, dt)
+
+
+def logits(cfg: WhisperConfig, W: dict, hidden: np.ndarray) -> np.ndarray:
+    return linear(hidden, W["embed"], cfg.bits, cfg.dtype)
+
+
+def score(cfg: WhisperConfig, W: dict, enc: np.ndarray, tokens) -> np.ndarray:
+    """Teacher-forced logits of every position of `tokens` (prompt included), [T, vocab]."""
+    xkv = cross_kv(cfg, W, enc)
+    cache = [[None, None] for _ in W["dec"]]
+    return logits(cfg, W, decoder_forward(cfg, W, xkv, list(tokens), 0, cache))
+
+
+def greedy(cfg: WhisperConfig, W: dict, enc: np.ndarray, prompt, n_tokens: int):
+    """Prefill the prompt, then `n_tokens` greedy choices (no end-of-text stop); returns the
+    tokens and the logits rows that chose them."""
+    xkv = cross_kv(cfg, W, enc)
+    cache = [[None, None] for _ in W["dec"]]
+    hid = decoder_forward(cfg, W, xkv, list(prompt), 0, cache)
+    row = logits(cfg, W, hid[-1:])[0]
+    toks, rows = [], []
+    pos = len(prompt)
+    for i in range(n_tokens):
+        t = int(np.argmax(row))
+        toks.append(t)
+        rows.append(row)
+        if i + 1 == n_tokens:
+            break
+        hid = decoder_forward(cfg, W, xkv, [t], pos, cache)
+        row = logits(cfg, W, hid)[0]
+        pos += 1
+    return toks, np.stack(rows)

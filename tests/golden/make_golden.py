@@ -59,9 +59,9 @@ def make_case(seed: int, m: int, n: int, k: int, bits: int, dtype: str, epilogue
     if epilogue != "siluGate":
         for key in ("up_w", "up_scales", "up_biases"):
             case.pop(key, None)
-    if epilogue not in ("bias", "biasResidual"):
+    if epilogue not in ("bias", "biasResidual", "biasGelu", "biasGeluResidual"):
         case.pop("bias")
-    if epilogue not in ("residual", "biasResidual"):
+    if epilogue not in ("residual", "biasResidual", "biasGeluResidual"):
         case.pop("residual")
     case["meta"] = np.array([m, n, k, bits, 0 if dtype == "bf16" else 1, A.EPILOGUES.index(epilogue)], np.int64)
     return case

@@ -75,7 +75,8 @@ def make(m, n, k, bits, dtype, epi, seed=0, scale=0.02):
 
 @pytest.mark.parametrize("bits", [0, 4, 8])
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
-@pytest.mark.parametrize("epi", ["none", "bias", "residual", "biasResidual", "siluGate"])
+@pytest.mark.parametrize("epi", ["none", "bias", "residual", "biasResidual", "siluGate", "biasGelu",
+                                 "biasGeluResidual"])
 def test_every_class(bits, dtype, epi):
     # every row count 1..16, N not a multiple of the CTA tile, K not a multiple of 256
     for m, n, k in [(1, 200, 1088), (3, 64, 2048), (8, 257, 3072), (11, 136, 576), (16, 520, 1024)]:
@@ -201,7 +202,8 @@ def test_large_m_tensor_core_rows_invariant():
 
 @pytest.mark.parametrize("bits", [0, 4, 8])
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
-@pytest.mark.parametrize("epi", ["none", "bias", "residual", "biasResidual", "siluGate"])
+@pytest.mark.parametrize("epi", ["none", "bias", "residual", "biasResidual", "siluGate", "biasGelu",
+                                 "biasGeluResidual"])
 def test_tensor_core_every_class(bits, dtype, epi):
     """Calls above 16 rows (tcgen05 path): partial token tiles, N not a multiple of 128,
     fewer K stages than pipeline stages, and several token tiles."""

@@ -1,0 +1,176 @@
+"""Parity of the Whisper encoder and decoder step (vella_whisper_* through the C ABI) with
+the CPU oracle, at the Whisper-tiny shapes of config 1 (int4 decoder, fp16) and a dense one.
+
+Bars: encoder output relative RMS <= 1e-2; teacher-forced logits max |error| <= 2e-2;
+greedy tokens equal the oracle's argmax wherever its top-2 margin exceeds that tolerance;
+a replayed decoder-step graph gives the same tokens as the first (eager) step sequence.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import affine as A
+from oracle import whisper as Wh
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2
+
+
+class _Dev:
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+
+def download(model, name, layer=-1):
+    ptr, nbytes = model.tensor(name, layer)
+    return torch.as_tensor(_Dev(ptr, nbytes), device="cuda").cpu().numpy()
+
+
+def f16(raw):
+    return raw.view(np.float16)
+
+
+def oracle_weights(model, c):
+    d, F = c.d_model, c.ffn
+    val = lambda name, layer=-1: f16(download(model, name, layer)).astype(np.float32)  # noqa: E731
+
+    def lin(name, layer, n, k, bits):
+        w = download(model, f"{name}.w", layer)
+        if bits:
+            return {"w": w.view(np.uint32).reshape(n, k * bits // 32),
+                    "s": f16(download(model, f"{name}.s", layer)).reshape(n, k // 64),
+                    "b": f16(download(model, f"{name}.b", layer)).reshape(n, k // 64)}
+        return {"w": f16(w).reshape(n, k)}
+
+    kp1 = (3 * c.n_mels + 63) // 64 * 64
+    W = {"conv1": lin("conv1", -1, d, kp1, 0), "conv1_b": val("conv1.bias"),
+         "conv2": lin("conv2", -1, d, 3 * d, 0), "conv2_b": val("conv2.bias"),
+         "enc_pos": val("enc_pos").reshape(c.n_audio, d),
+         "enc_ln_w": val("enc_ln.weight"), "enc_ln_b": val("enc_ln.bias"),
+         "dec_ln_w": val("dec_ln.weight"), "dec_ln_b": val("dec_ln.bias"),
+         "embed": lin("embed", -1, c.vocab, d, c.bits), "dec_pos": val("dec_pos").reshape(c.max_target, d),
+         "enc": [], "dec": []}
+    for l in range(c.enc_layers):
+        W["enc"].append({"ln1_w": val("enc.ln1.weight", l), "ln1_b": val("enc.ln1.bias", l),
+                         "qkv": lin("enc.qkv", l, 3 * d, d, 0), "qkv_b": val("enc.qkv.bias", l),
+                         "o": lin("enc.o", l, d, d, 0), "o_b": val("enc.o.bias", l),
+                         "ln2_w": val("enc.ln2.weight", l), "ln2_b": val("enc.ln2.bias", l),
+                         "fc1": lin("enc.fc1", l, F, d, 0), "fc1_b": val("enc.fc1.bias", l),
+                         "fc2": lin("enc.fc2", l, d, F, 0), "fc2_b": val("enc.fc2.bias", l)})
+    b = c.bits
+    for l in range(c.dec_layers):
+        L = {}
+        for ln in ("ln1", "ln2", "ln3"):
+            L[f"{ln}_w"], L[f"{ln}_b"] = val(f"dec.{ln}.weight", l), val(f"dec.{ln}.bias", l)
+        for name, n, k in (("qkv", 3 * d, d), ("o", d, d), ("cq", d, d), ("ckv", 2 * d, d), ("co", d, d),
+                           ("fc1", F, d), ("fc2", d, F)):
+            L[name] = lin(f"dec.{name}", l, n, k, b)
+            L[f"{name}_b"] = val(f"dec.{name}.bias", l)
+        W["dec"].append(L)
+    return W
+
+
+def make(cfg, seed=1):
+    from vella_b200 import whisper as VW
+    m = VW.Whisper(cfg)
+    m.init_random(seed, 0.02)
+    oc = Wh.WhisperConfig(cfg.n_mels, cfg.d_model, cfg.heads, cfg.enc_layers, cfg.dec_layers, cfg.ffn, cfg.vocab,
+                          cfg.n_audio, cfg.max_target, cfg.bits, "f16", cfg.eps)
+    return m, oc
+
+
+def mel_of(cfg, seed):
+    return np.random.default_rng(seed).standard_normal((cfg.n_mels, 2 * cfg.n_audio)).astype(np.float32)
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    from vella_b200 import whisper as VW
+    m, oc = make(VW.TINY, seed=5)
+    W = oracle_weights(m, oc)
+    mel = mel_of(oc, 7)
+    m.encode(mel)
+    enc_ref = Wh.encoder(oc, W, mel)
+    yield m, oc, W, mel, enc_ref
+    m.close()
+
+
+def test_encoder_matches_oracle(tiny):
+    m, oc, W, mel, enc_ref = tiny
+    got = f16(download(m, "enc_out")).astype(np.float32).reshape(oc.n_audio, oc.d_model)
+    assert np.isfinite(got).all()
+    assert A.relative_rms(got, enc_ref) <= 1e-2
+
+
+def test_teacher_forced_logits_match_oracle(tiny):
+    m, oc, W, mel, enc_ref = tiny
+    toks = [50258, 50259, 50359, 50363] + list(np.random.default_rng(3).integers(0, 50000, 20))
+    got = m.score(toks).astype(np.float32)
+    ref = Wh.score(oc, W, enc_ref, toks)
+    assert got.shape == ref.shape == (len(toks), oc.vocab)
+    err = float(np.abs(got - ref).max())
+    assert err <= LOGIT_TOL, err
+
+
+def test_greedy_decode_matches_oracle_and_replays(tiny):
+    m, oc, W, mel, enc_ref = tiny
+    prompt = [50258, 50259, 50359, 50363]
+    res = m.decode(prompt, 24)
+    assert len(res.tokens) == 24
+    # teacher-forced oracle logits along the produced sequence: each token is the argmax
+    # wherever the oracle's top-2 margin exceeds the logits tolerance
+    logits = Wh.score(oc, W, enc_ref, prompt + res.tokens[:-1])[len(prompt) - 1:]
+    for j, t in enumerate(res.tokens):
+        row = logits[j]
+        best = int(np.argmax(row))
+        assert t == best or row[best] - row[t] <= LOGIT_TOL, (j, t, best)
+    # the second decode replays the captured step graph: identical tokens
+    again = m.decode(prompt, 24)
+    assert again.tokens == res.tokens
+
+
+def test_end_of_text_stops_and_is_not_emitted(tiny):
+    m, oc, W, mel, enc_ref = tiny
+    prompt = [50258, 50259, 50359, 50363]
+    full = m.decode(prompt, 12).tokens
+    eot = full[5]
+    first = full.index(eot)
+    cut = m.decode(prompt, 12, eot=eot).tokens
+    assert cut == full[:first]
+
+
+def test_dense_fp16_model_matches_oracle():
+    """The dense (config 3 style) decoder path at reduced sizes, encoder included."""
+    from vella_b200 import whisper as VW
+    cfg = VW.WhisperConfig(n_mels=128, d_model=256, heads=4, enc_layers=2, dec_layers=2, ffn=1024, vocab=4000,
+                           n_audio=300, max_target=64, bits=0)
+    m, oc = make(cfg, seed=9)
+    W = oracle_weights(m, oc)
+    mel = mel_of(oc, 11)
+    m.encode(mel)
+    enc_ref = Wh.encoder(oc, W, mel)
+    got = f16(download(m, "enc_out")).astype(np.float32).reshape(oc.n_audio, oc.d_model)
+    assert A.relative_rms(got, enc_ref) <= 1e-2
+    toks = [1, 2, 3, 4] + list(np.random.default_rng(12).integers(0, 4000, 12))
+    err = float(np.abs(m.score(toks).astype(np.float32) - Wh.score(oc, W, enc_ref, toks)).max())
+    assert err <= LOGIT_TOL, err
+    m.close()
+
+
+def test_bad_arguments_are_rejected():
+    from vella_b200 import _lib
+    from vella_b200 import whisper as VW
+    cfg = VW.WhisperConfig(n_mels=16, d_model=128, heads=2, enc_layers=1, dec_layers=1, ffn=256, vocab=500,
+                           n_audio=40, max_target=32, bits=4)
+    m = VW.Whisper(cfg)
+    m.init_random(1)
+    with pytest.raises(_lib.VellaError):
+        m.decode([1, 2], 4)                      # decode before encode
+    m.encode(mel_of(cfg, 1))
+    with pytest.raises(_lib.VellaError):
+        m.decode([1, 2], 31)                     # past max_target
+    with pytest.raises(_lib.VellaError):
+        m.score([1, 2, 700])                     # token id out of range
+    assert len(m.decode([1, 2], 8).tokens) == 8  # the handle still works afterwards
+    m.close()

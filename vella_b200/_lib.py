@@ -14,7 +14,8 @@ LIB_PATH = Path(os.environ.get("VELLA_LIB", _PKG / "_lib" / "libvella_cuda.so"))
 
 OK, E_UNSUPPORTED, E_INVALID, E_CUDA, E_NONFINITE, E_OOM = range(6)
 BF16, F16 = 0, 1
-EPI = {"none": 0, "bias": 1, "residual": 2, "biasResidual": 3, "siluGate": 4}
+EPI = {"none": 0, "bias": 1, "residual": 2, "biasResidual": 3, "siluGate": 4, "biasGelu": 5,
+       "biasGeluResidual": 6}
 STATUS_NAMES = {0: "VELLA_OK", 1: "VELLA_E_UNSUPPORTED", 2: "VELLA_E_INVALID", 3: "VELLA_E_CUDA",
                 4: "VELLA_E_NONFINITE", 5: "VELLA_E_OOM"}
 

@@ -110,4 +110,7 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// GELU, erf form: 0.5 x (1 + erf(x / sqrt(2))) (MLX's default gelu).
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
 }  // namespace vella

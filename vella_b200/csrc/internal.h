@@ -39,6 +39,17 @@ inline int cuda_fail(cudaError_t e, const char* what) {
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Epilogue parts of a VELLA_EPI_* code, applied in the order gate, bias, GELU, residual.
+inline bool epi_valid(int e) { return e >= VELLA_EPI_NONE && e <= VELLA_EPI_BIAS_GELU_RESIDUAL; }
+inline bool epi_bias(int e) {
+  return e == VELLA_EPI_BIAS || e == VELLA_EPI_BIAS_RESIDUAL || e == VELLA_EPI_BIAS_GELU ||
+         e == VELLA_EPI_BIAS_GELU_RESIDUAL;
+}
+inline bool epi_residual(int e) {
+  return e == VELLA_EPI_RESIDUAL || e == VELLA_EPI_BIAS_RESIDUAL || e == VELLA_EPI_BIAS_GELU_RESIDUAL;
+}
+inline bool epi_gelu(int e) { return e == VELLA_EPI_BIAS_GELU || e == VELLA_EPI_BIAS_GELU_RESIDUAL; }
+
 int num_sms(int device);
 
 // Launch with programmatic stream serialization (the kernel overlaps the tail of the

@@ -178,19 +178,18 @@ __global__ void rope_append_kernel(const T* __restrict__ qkv, T* __restrict__ q_
 // depend on the other rows of the launch.
 // ---------------------------------------------------------------------------------------
 struct AttnArgs {
-  const void* q;
-  const void* kc;
-  const void* vc;
-  void* out;
-  PosRef pr;
-  int M, H, KV, S;
+  AttnView v;
+  PosRef pr;   // causal: position of query row 0
+  int M, H, KV;
+  int S;       // key rows that exist (cache capacity; the key count when not causal)
+  int QB;      // query rows per cluster (QB * H / KV <= kAttnRows)
+  int causal;  // 1: the query at position p sees keys 0..p; 0: all S keys
   float scale;
 };
 
 template <typename T, int HD>
 __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn_kernel(const AttnArgs a) {
   constexpr int C = kAttnChunk;
-  constexpr int QB = kAttnQBlock;
   constexpr int CS = kAttnCluster;
   constexpr int KS = HD + 4;  // padded fp32 row stride of K/V/Q/O in shared memory
   constexpr int PS = C + 4;
@@ -199,7 +198,8 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn
   static_assert(LDI * 256 == C * V8, "chunk loads must tile the block");
   extern __shared__ __align__(16) float sm[];
   const int GQ = a.H / a.KV;
-  const int QRmax = QB * GQ;
+  const int QB = a.QB;
+  constexpr int QRmax = kAttnRows;
   float* Ks = sm;
   float* Vs = Ks + C * KS;
   float* Qs = Vs + C * KS;
@@ -211,20 +211,20 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn
 
   cg::cluster_group cl = cg::this_cluster();
   const int r = (int)cl.block_rank();
-  const int kvh = blockIdx.x / CS, qb = blockIdx.y;
+  const int kvh = blockIdx.x / CS, qb = blockIdx.y, bz = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
   pdl_launch_next();
-  const int pos0 = *a.pr.base + a.pr.off;
+  const int pos0 = a.causal ? *a.pr.base + a.pr.off : 0;
   const int mq0 = qb * QB;
   const int nq = min(QB, a.M - mq0);
   const int QR = nq * GQ;
-  const int tmax = pos0 + mq0 + nq;  // keys needed by the last query of this block
+  const int tmax = a.causal ? pos0 + mq0 + nq : a.S;  // keys needed by the last query of this block
   const int nact = (tmax + C - 1) / C;
-  const int kend = min(tmax, a.S);   // cache rows that exist
-  const T* q = static_cast<const T*>(a.q);
-  const T* kbase = static_cast<const T*>(a.kc) + (size_t)kvh * a.S * HD;
-  const T* vbase = static_cast<const T*>(a.vc) + (size_t)kvh * a.S * HD;
+  const int kend = min(tmax, a.S);   // key rows that exist
+  const T* q = static_cast<const T*>(a.v.q) + (size_t)bz * a.v.q_bs;
+  const T* kbase = static_cast<const T*>(a.v.k) + (size_t)bz * a.v.kv_bs + (size_t)kvh * a.v.kv_hs;
+  const T* vbase = static_cast<const T*>(a.v.v) + (size_t)bz * a.v.kv_bs + (size_t)kvh * a.v.kv_hs;
 
   for (int i = tid; i < QR * KS; i += 256) Os[i] = 0.0f;
   for (int i = tid; i < QR; i += 256) { Mx[i] = -INFINITY; Ls[i] = 0.0f; }
@@ -235,7 +235,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn
       const int e = e0 + u * 256 + tid;
       if (e < QR * V8) {
         const int qr = e / V8, d8 = (e % V8) * 8;
-        raw[u] = *reinterpret_cast<const uint4*>(q + ((size_t)(mq0 + qr / GQ) * a.H + kvh * GQ + qr % GQ) * HD + d8);
+        raw[u] = *reinterpret_cast<const uint4*>(q + (size_t)(mq0 + qr / GQ) * a.v.q_rs + (size_t)(kvh * GQ + qr % GQ) * HD + d8);
       }
     }
 #pragma unroll
@@ -262,8 +262,8 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn
     for (int u = 0; u < LDI; ++u) {
       const int e = u * 256 + tid, j = e / V8, d8 = (e % V8) * 8;
       if (k0 + j < kend) {
-        kr[u] = *reinterpret_cast<const uint4*>(kbase + (size_t)(k0 + j) * HD + d8);
-        vr[u] = *reinterpret_cast<const uint4*>(vbase + (size_t)(k0 + j) * HD + d8);
+        kr[u] = *reinterpret_cast<const uint4*>(kbase + (size_t)(k0 + j) * a.v.kv_rs + d8);
+        vr[u] = *reinterpret_cast<const uint4*>(vbase + (size_t)(k0 + j) * a.v.kv_rs + d8);
       } else {
         kr[u] = vr[u] = make_uint4(0u, 0u, 0u, 0u);
       }
@@ -316,9 +316,9 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn
       for (int i = 0; i < 4; ++i) {
         const int qr = rb + i;
         if (qr < QR) {
-          const int pq = pos0 + mq0 + qr / GQ;
-          Ps[qr * PS + lane] = (k0 + lane <= pq) ? s[i][0] * a.scale : -INFINITY;
-          Ps[qr * PS + lane + 32] = (k0 + lane + 32 <= pq) ? s[i][1] * a.scale : -INFINITY;
+          const int lim = a.causal ? pos0 + mq0 + qr / GQ : a.S - 1;  // last visible key
+          Ps[qr * PS + lane] = (k0 + lane <= lim) ? s[i][0] * a.scale : -INFINITY;
+          Ps[qr * PS + lane + 32] = (k0 + lane + 32 <= lim) ? s[i][1] * a.scale : -INFINITY;
         }
       }
     }
@@ -367,7 +367,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn
 
   // ---- combine the cluster's partial rows in rank order; CTA r owns rows r, r + CS, … --
   cl.sync();
-  T* out = static_cast<T*>(a.out);
+  T* out = static_cast<T*>(a.v.out) + (size_t)bz * a.v.o_bs;
   for (int qr = r + CS * rset; qr < QR; qr += CS * RS) {
     float mr[CS], lr[CS], orr[CS];
 #pragma unroll
@@ -386,7 +386,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn
       o = fmaf(w, orr[i], o);
       l = fmaf(w, lr[i], l);
     }
-    out[((size_t)(mq0 + qr / GQ) * a.H + kvh * GQ + qr % GQ) * HD + d] = Act<T>::from_f(o / l);
+    out[(size_t)(mq0 + qr / GQ) * a.v.o_rs + (size_t)(kvh * GQ + qr % GQ) * HD + d] = Act<T>::from_f(o / l);
   }
   cl.sync();  // keep this CTA's shared memory alive until every peer has read it
 }
@@ -463,24 +463,24 @@ __global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logit
   }
 }
 
-size_t attn_smem_bytes(int hd, int gq) {
-  const size_t ks = hd + 4, ps = kAttnChunk + 4, qr = (size_t)kAttnQBlock * gq;
+size_t attn_smem_bytes(int hd) {
+  const size_t ks = hd + 4, ps = kAttnChunk + 4, qr = kAttnRows;
   return (2 * kAttnChunk * ks + 2 * qr * ks + qr * ps + 3 * qr) * sizeof(float);
 }
 
 template <typename T, int HD>
-int launch_attn_t(const AttnArgs& a, int gq, cudaStream_t s) {
-  const size_t smem = attn_smem_bytes(HD, gq);
+int launch_attn_t(const AttnArgs& a, int batch, cudaStream_t s) {
+  const size_t smem = attn_smem_bytes(HD);
   static int configured[64] = {0};
   int dev = 0;
   VELLA_CUDA_TRY(cudaGetDevice(&dev));
   if (!configured[dev & 63]) {
     VELLA_CUDA_TRY(cudaFuncSetAttribute(attn_kernel<T, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)attn_smem_bytes(HD, kAttnMaxGQ)));
+                                        (int)attn_smem_bytes(HD)));
     configured[dev & 63] = 1;
   }
-  const int nqb = (a.M + kAttnQBlock - 1) / kAttnQBlock;
-  return launch_kernel(attn_kernel<T, HD>, dim3(a.KV * kAttnCluster, nqb), dim3(256), smem, s, a);
+  const int nqb = (a.M + a.QB - 1) / a.QB;
+  return launch_kernel(attn_kernel<T, HD>, dim3(a.KV * kAttnCluster, nqb, batch), dim3(256), smem, s, a);
 }
 
 }  // namespace
@@ -524,24 +524,37 @@ int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* 
                        err);
 }
 
-int launch_attention(int dtype, const void* q, const void* kc, const void* vc, void* out, PosRef pr, int rows,
-                     int H, int KV, int hd, int max_seq, float scale, cudaStream_t s) {
-  if (rows <= 0) return VELLA_OK;
-  AttnArgs a{};
-  a.q = q; a.kc = kc; a.vc = vc; a.out = out;
-  a.pr = pr; a.M = rows; a.H = H; a.KV = KV; a.S = max_seq;
-  a.scale = scale;
-  const int gq = H / KV;
-  if (gq * KV != H || gq > kAttnMaxGQ)
+int launch_attention_ex(int dtype, const AttnView& v, int batch, PosRef pr, int causal, int rows, int H, int KV,
+                        int hd, int S, float scale, cudaStream_t s) {
+  if (rows <= 0 || batch <= 0) return VELLA_OK;
+  const int gq = KV > 0 ? H / KV : 0;
+  if (gq < 1 || gq * KV != H || gq > kAttnMaxGQ)
     return fail(VELLA_E_UNSUPPORTED, "attention: H/KV = %d/%d not supported", H, KV);
+  if (S < 1 || batch > 65535) return fail(VELLA_E_INVALID, "attention: %d keys, batch %d", S, batch);
+  AttnArgs a{};
+  a.v = v;
+  a.pr = pr; a.M = rows; a.H = H; a.KV = KV; a.S = S;
+  a.QB = kAttnRows / gq;
+  a.causal = causal ? 1 : 0;
+  a.scale = scale;
   if (dtype == VELLA_BF16) {
-    if (hd == 128) return launch_attn_t<__nv_bfloat16, 128>(a, gq, s);
-    if (hd == 64) return launch_attn_t<__nv_bfloat16, 64>(a, gq, s);
+    if (hd == 128) return launch_attn_t<__nv_bfloat16, 128>(a, batch, s);
+    if (hd == 64) return launch_attn_t<__nv_bfloat16, 64>(a, batch, s);
   } else {
-    if (hd == 128) return launch_attn_t<__half, 128>(a, gq, s);
-    if (hd == 64) return launch_attn_t<__half, 64>(a, gq, s);
+    if (hd == 128) return launch_attn_t<__half, 128>(a, batch, s);
+    if (hd == 64) return launch_attn_t<__half, 64>(a, batch, s);
   }
   return fail(VELLA_E_UNSUPPORTED, "attention: head_dim %d not supported", hd);
+}
+
+int launch_attention(int dtype, const void* q, const void* kc, const void* vc, void* out, PosRef pr, int rows,
+                     int H, int KV, int hd, int max_seq, float scale, cudaStream_t s) {
+  AttnView v{};
+  v.q = q; v.k = kc; v.v = vc; v.out = out;
+  v.q_rs = v.o_rs = (long long)H * hd;
+  v.kv_hs = (long long)max_seq * hd;
+  v.kv_rs = hd;
+  return launch_attention_ex(dtype, v, 1, pr, 1, rows, H, KV, hd, max_seq, scale, s);
 }
 
 size_t argmax_scratch_bytes(int max_rows) {

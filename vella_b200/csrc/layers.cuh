@@ -16,9 +16,22 @@ struct PosRef {
 };
 
 constexpr int kAttnChunk = 64;   // keys per chunk (absolute-position aligned)
-constexpr int kAttnQBlock = 8;   // query rows per cluster
+constexpr int kAttnRows = 64;    // query rows x query heads per cluster (query block = 64 / GQ rows)
 constexpr int kAttnCluster = 8;  // CTAs per (kv head, query block); chunk c goes to CTA c % 8
 constexpr int kAttnMaxGQ = 8;    // query heads per kv head
+
+// Operands of an attention launch (element strides).  q/out rows hold the heads
+// [H][hd] contiguously; K/V of kv head h, key row j at k + h * kv_hs + j * kv_rs; launch
+// batch b adds b * {q,o,kv}_bs (independent streams).
+struct AttnView {
+  const void* q = nullptr;
+  const void* k = nullptr;
+  const void* v = nullptr;
+  void* out = nullptr;
+  long long q_rs = 0, o_rs = 0;
+  long long kv_hs = 0, kv_rs = 0;
+  long long q_bs = 0, o_bs = 0, kv_bs = 0;
+};
 
 // dtype: 0 = bf16, 1 = fp16 everywhere below.
 // Row m holds position p = *pr.base + pr.off + m: the caller's input embedding p when
@@ -32,6 +45,10 @@ int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* 
                        int max_seq, int* err, cudaStream_t s);
 int launch_attention(int dtype, const void* q, const void* kc, const void* vc, void* out, PosRef pr, int rows,
                      int H, int KV, int hd, int max_seq, float scale, cudaStream_t s);
+// General form: causal (query at position *pr.base + pr.off + m sees keys 0..that) or not
+// (every query sees the S keys), strided operands, `batch` independent streams.
+int launch_attention_ex(int dtype, const AttnView& v, int batch, PosRef pr, int causal, int rows, int H, int KV,
+                        int hd, int S, float scale, cudaStream_t s);
 // ys[m] = first index of the row maximum of logits[m][0..V) (row stride ld); any NaN/Inf
 // sets *nonfinite.  `part`/`counters` scratch from argmax_scratch_bytes.
 size_t argmax_scratch_bytes(int max_rows);

@@ -70,6 +70,8 @@ struct Model {
 
 int model_create(const vella_model_cfg& cfg, int device, Model** out);
 int fill_normal(void* out, size_t n, int dtype, uint64_t seed, uint32_t tensor, float mean, float std, cudaStream_t s);
+// Random MLX-affine weights: each group drawn ~N(0, std) and quantized on the device.
+int quantize_random(const QWeight& w, int bits, int dtype, uint64_t seed, uint32_t tensor, float std, cudaStream_t s);
 int quantize_device(int src_dtype, const void* w, int dtype, int bits, int N, int K, void* packed, void* scales,
                     void* biases, cudaStream_t s);
 void model_destroy(Model* m);

@@ -70,7 +70,7 @@ struct Args {
   float* partial;
   int* counters;
   int M, N, K, G, KC, S, rowblocks;
-  int has_bias, has_res;
+  int has_bias, has_res, gelu;
 };
 
 // Words of packed weight per row and group of 64, and per thread (k quarter) of a group.
@@ -386,6 +386,7 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const Args a) {
     }
     const size_t o = (size_t)(m0 + m) * N + n;
     if (a.has_bias) v += A::to_f(bias[n]);
+    if (a.gelu) v = gelu_erf(v);
     if (a.has_res) v += A::to_f(res[o]);
     out[o] = A::from_f(v);
   }
@@ -426,7 +427,7 @@ bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* p) {
   if (d.bits != 0 && d.group_size != 64) return false;
   if (d.k % 64 != 0) return false;
   if (d.dtype != VELLA_BF16 && d.dtype != VELLA_F16) return false;
-  if (d.epilogue < VELLA_EPI_NONE || d.epilogue > VELLA_EPI_SILU_GATE) return false;
+  if (!epi_valid(d.epilogue)) return false;
   p->stream = false;
   p->tc = false;
   if (tc_eligible(d) && d.m <= (1 << 24)) {  // more than 16 rows: tensor cores, no workspace
@@ -491,8 +492,9 @@ int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& p, const void* x, c
   a.uw = static_cast<const uint32_t*>(up_w); a.usc = up_scales; a.ubi = up_biases;
   a.bias = bias; a.res = residual; a.out = out;
   a.M = d.m; a.N = d.n; a.K = d.k; a.G = d.k / 64; a.KC = p.kc; a.S = p.splits; a.rowblocks = p.rowblocks;
-  a.has_bias = d.epilogue == VELLA_EPI_BIAS || d.epilogue == VELLA_EPI_BIAS_RESIDUAL;
-  a.has_res = d.epilogue == VELLA_EPI_RESIDUAL || d.epilogue == VELLA_EPI_BIAS_RESIDUAL;
+  a.has_bias = epi_bias(d.epilogue);
+  a.has_res = epi_residual(d.epilogue);
+  a.gelu = epi_gelu(d.epilogue);
   if (p.splits > 1) {
     a.counters = static_cast<int*>(ws);
     a.partial = reinterpret_cast<float*>(static_cast<char*>(ws) + counter_region((size_t)p.zchunks * p.rowblocks));

@@ -75,8 +75,8 @@ extern "C" int vella_qgemm_noalloc(const vella_qgemm_desc* desc, const void* x, 
   if (d.m == 0 || d.n == 0) return VELLA_OK;
   const bool quant = d.bits != 0;
   const bool gate = d.epilogue == VELLA_EPI_SILU_GATE;
-  const bool has_bias = d.epilogue == VELLA_EPI_BIAS || d.epilogue == VELLA_EPI_BIAS_RESIDUAL;
-  const bool has_res = d.epilogue == VELLA_EPI_RESIDUAL || d.epilogue == VELLA_EPI_BIAS_RESIDUAL;
+  const bool has_bias = epi_bias(d.epilogue);
+  const bool has_res = epi_residual(d.epilogue);
   if (!x || !w || !out) return fail(VELLA_E_INVALID, "vella_qgemm_noalloc: x, w and out must be non-NULL");
   if (quant && (!scales || !biases))
     return fail(VELLA_E_INVALID, "vella_qgemm_noalloc: scales and biases are required for bits=%d", d.bits);

@@ -73,7 +73,7 @@ struct SArgs {
   float* partial;  // [P][2][16][128]
   int* counters;   // [rowblocks]
   int M, N, K, G, rowblocks, nkc, P;
-  int has_bias, has_res;
+  int has_bias, has_res, gelu;
 };
 
 using namespace sm100;
@@ -263,6 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_stream_kernel(const __grid_
           if constexpr (GATE) v = v / (1.0f + expf(-v)) * acc[1][nt][e];
           const size_t o = (size_t)tok * N + n;
           if (a.has_bias) v += A::to_f(bias[n]);
+          if (a.gelu) v = gelu_erf(v);
           if (a.has_res) v += A::to_f(res[o]);
           out[o] = A::from_f(v);
         }
@@ -572,8 +573,9 @@ int stream_launch(const vella_qgemm_desc& d, int P, const void* x, const void* w
   a.partial = partial; a.counters = counters;
   a.M = d.m; a.N = d.n; a.K = d.k; a.G = d.k / 64; a.P = P;
   stream_units(d, &a.rowblocks, &a.nkc);
-  a.has_bias = d.epilogue == VELLA_EPI_BIAS || d.epilogue == VELLA_EPI_BIAS_RESIDUAL;
-  a.has_res = d.epilogue == VELLA_EPI_RESIDUAL || d.epilogue == VELLA_EPI_BIAS_RESIDUAL;
+  a.has_bias = epi_bias(d.epilogue);
+  a.has_res = epi_residual(d.epilogue);
+  a.gelu = epi_gelu(d.epilogue);
   if (d.dtype == VELLA_BF16) {
     switch (d.bits) {
       case 4: return dispatch_stream<__nv_bfloat16, 4>(a, gate, nt, stream);

@@ -6,7 +6,7 @@
 //
 // with W' = T(scale * q + bias) (T = activation dtype, one rounding per weight) for the
 // MLX-affine formats (reference SmallMGEMM.swift:491-498 layout) and W' = W for dense weights;
-// the epilogue is the library's: SiLU gate, then bias, then residual, one rounding
+// the epilogue is the library's: SiLU gate, then bias, then GELU, then residual, one rounding
 // (SmallMGEMM.swift:745-753).
 //
 // CTA tile: 128 weight rows (the MMA's M side) x 128 tokens (its N side) x all of K, streamed
@@ -75,6 +75,7 @@ struct TcArgs {
   const void* ub;          // up biases
   const void* bias;        // [N] or null
   const void* res;         // [M, N] or null
+  int gelu;                // GELU after the bias
   void* out;               // [M, N]
   int M, N, K, G;
 };
@@ -312,6 +313,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
               float y = __uint_as_float(v[j]);
               if constexpr (GATE) y = y / (1.0f + expf(-y)) * __uint_as_float(u[j]);
               y += bn;
+              if (a.gelu) y = gelu_erf(y);
               if (res) y += A::to_f(res[(size_t)m * a.N + n]);
               out[(size_t)m * a.N + n] = A::from_f(y);
             }
@@ -361,8 +363,9 @@ int tc_launch(const vella_qgemm_desc& d, const void* x, const void* w, const voi
   const bool gate = d.epilogue == VELLA_EPI_SILU_GATE;
   TcArgs a{};
   a.s = scales; a.b = biases; a.us = up_scales; a.ub = up_biases;
-  a.bias = (d.epilogue == VELLA_EPI_BIAS || d.epilogue == VELLA_EPI_BIAS_RESIDUAL) ? bias : nullptr;
-  a.res = (d.epilogue == VELLA_EPI_RESIDUAL || d.epilogue == VELLA_EPI_BIAS_RESIDUAL) ? residual : nullptr;
+  a.bias = epi_bias(d.epilogue) ? bias : nullptr;
+  a.res = epi_residual(d.epilogue) ? residual : nullptr;
+  a.gelu = epi_gelu(d.epilogue);
   a.out = out;
   a.M = d.m; a.N = d.n; a.K = d.k; a.G = d.k / kTcK;
   int rc;

@@ -1,0 +1,881 @@
+// Whisper encoder and decoder step on one GPU (one audio stream per handle).
+//
+// Reference: Worker/Sources/MLXAudioSTT/Whisper/WhisperLayers.swift:11-329 (attention with
+// k_proj unbiased, encoder conv1/conv2/positions/pre-LN blocks, decoder layers with self- and
+// cross-attention, tied vocabulary projection), WhisperFusedDecode.swift:105-259 (the fused
+// decode step: q|k|v as one projection with k's bias zero, the KV append, residual add +
+// LayerNorm), WhisperModel.swift:341-400 (greedy loop; its token rules are not applied) and
+// :554-569 (sinusoid table: double trig, rounded to fp32, then to the table dtype).
+//
+// B200 layout: every weight in one arena; the encoder runs its GEMMs on the tensor cores
+// (M = 3000 / 1500 rows) and the attention as the library's clustered flash-decoding kernel
+// without a mask; the cross-attention K/V of all decoder layers are projected once per audio
+// window into [layers][n_audio][2 * d] (k | v per row) and read in place; the decoder's self
+// K/V live in a preallocated [layers][2][heads][max_target][head_dim] cache written at
+// absolute positions.  A decoder step is embed, 4 kernels + 8 GEMM/attention launches per
+// layer, final LayerNorm, vocabulary GEMM and argmax, captured once into a CUDA graph whose
+// positions come from a device scalar.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "layers.cuh"
+#include "model.h"
+
+namespace vella {
+namespace {
+
+constexpr int kWRows = 16;      // decoder rows per forward (prompt chunk / teacher-forced chunk)
+constexpr int kLnMaxD = 2048;   // LayerNorm row length limit (8 values per thread)
+
+// ---- kernels -------------------------------------------------------------------------------
+
+__device__ __forceinline__ float block_sum256(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) t += red[w];
+  return t;
+}
+
+// LayerNorm of one row per CTA: fp32 mean and centred variance, x_hat rounded to T, then
+// T(w * x_hat + b) (WhisperFusedDecode.swift:204-251 row algorithm, one final rounding).
+template <typename T>
+__global__ void __launch_bounds__(256) layernorm_kernel(T* __restrict__ out, const T* __restrict__ x,
+                                                        const T* __restrict__ w, const T* __restrict__ b, int D,
+                                                        float eps) {
+  using A = Act<T>;
+  __shared__ float red[8];
+  pdl_wait();
+  pdl_launch_next();
+  const T* xr = x + (size_t)blockIdx.x * D;
+  T* orow = out + (size_t)blockIdx.x * D;
+  float v[kLnMaxD / 256];
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kLnMaxD / 256; ++j) {
+    const int i = threadIdx.x + 256 * j;
+    v[j] = i < D ? A::to_f(xr[i]) : 0.0f;
+    s += v[j];
+  }
+  const float mean = block_sum256(s, red) / (float)D;
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kLnMaxD / 256; ++j) {
+    const int i = threadIdx.x + 256 * j;
+    if (i < D) {
+      v[j] -= mean;
+      ss = fmaf(v[j], v[j], ss);
+    }
+  }
+  const float r = sqrtf(block_sum256(ss, red) / (float)D + eps);
+#pragma unroll
+  for (int j = 0; j < kLnMaxD / 256; ++j) {
+    const int i = threadIdx.x + 256 * j;
+    if (i < D) {
+      const float xh = A::to_f(A::from_f(v[j] / r));
+      orow[i] = A::from_f(fmaf(A::to_f(w[i]), xh, A::to_f(b[i])));
+    }
+  }
+}
+
+template <typename Tin> __device__ __forceinline__ float ld_f(const Tin* p) { return Act<Tin>::to_f(*p); }
+template <> __device__ __forceinline__ float ld_f<float>(const float* p) { return *p; }
+
+// im2col of a kernel-3, padding-1 Conv1d: row t = [x(s t - 1), x(s t), x(s t + 1)] over the
+// C channels, zero outside [0, T_in) and in the columns 3C..Kp (K padding).  x(t, c) sits at
+// x[t * t_stride + c * c_stride].
+template <typename Tin, typename T>
+__global__ void __launch_bounds__(256) im2col_kernel(T* __restrict__ out, const Tin* __restrict__ x, int C, int stride,
+                                                     int T_in, long long t_stride, long long c_stride, int Kp) {
+  pdl_wait();
+  pdl_launch_next();
+  const int t = blockIdx.x;
+  T* orow = out + (size_t)t * Kp;
+  for (int e = threadIdx.x; e < Kp; e += blockDim.x) {
+    float v = 0.0f;
+    if (e < 3 * C) {
+      const int j = e / C, c = e % C;
+      const int ti = stride * t - 1 + j;
+      if (ti >= 0 && ti < T_in) v = ld_f<Tin>(x + (size_t)ti * t_stride + (size_t)c * c_stride);
+    }
+    orow[e] = Act<T>::from_f(v);
+  }
+}
+
+// h[m] = T(T(embed[tok[p]]) + dec_pos[p]) at p = *pr.base + pr.off + m; a quantized row is
+// T(scale * q + bias) (multiply, then add, each rounded to fp32).
+template <typename T, int BITS>
+__global__ void __launch_bounds__(256) wembed_kernel(T* __restrict__ h, const void* __restrict__ E,
+                                                     const T* __restrict__ Es, const T* __restrict__ Eb,
+                                                     const T* __restrict__ pos, const int* __restrict__ tok, PosRef pr,
+                                                     int d, int vocab, int max_target, int* err) {
+  using A = Act<T>;
+  pdl_wait();
+  pdl_launch_next();
+  int p = *pr.base + pr.off + (int)blockIdx.x;
+  if (p >= max_target) {
+    if (threadIdx.x == 0) atomicOr(err, 4);
+    p = max_target - 1;
+  }
+  int t = tok[p];
+  if (t < 0 || t >= vocab) {
+    if (threadIdx.x == 0) atomicOr(err, 1);
+    t = 0;
+  }
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    float e;
+    if constexpr (BITS == 0) {
+      e = A::to_f(static_cast<const T*>(E)[(size_t)t * d + i]);
+    } else {
+      constexpr int PER = 32 / BITS;
+      const uint32_t wd = static_cast<const uint32_t*>(E)[(size_t)t * (d / PER) + i / PER];
+      const float q = (float)((wd >> ((i % PER) * BITS)) & ((1u << BITS) - 1));
+      const size_t g = (size_t)t * (d / 64) + i / 64;
+      e = A::to_f(A::from_f(__fadd_rn(__fmul_rn(A::to_f(Es[g]), q), A::to_f(Eb[g]))));
+    }
+    h[(size_t)blockIdx.x * d + i] = A::from_f(e + A::to_f(pos[(size_t)p * d + i]));
+  }
+}
+
+// Appends the k and v parts of qkv rows [rows, 3d] to the self-attention cache
+// [heads][S][hd] of one layer at positions *pr.base + pr.off + m.
+template <typename T>
+__global__ void __launch_bounds__(256) wappend_kernel(const T* __restrict__ qkv, T* __restrict__ kc,
+                                                      T* __restrict__ vc, PosRef pr, int d, int hd, int S) {
+  pdl_wait();
+  pdl_launch_next();
+  const int m = blockIdx.x;
+  const int p = *pr.base + pr.off + m;
+  if (p >= S) return;
+  const T* row = qkv + (size_t)m * 3 * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const int h = i / hd, j = i % hd;
+    kc[((size_t)h * S + p) * hd + j] = row[d + i];
+    vc[((size_t)h * S + p) * hd + j] = row[2 * d + i];
+  }
+}
+
+// tok[*L] = ys[0]; *L += 1.
+__global__ void wcommit_kernel(int* L, int* tok, const int* ys, int max_target, int* err) {
+  pdl_wait();
+  pdl_launch_next();
+  const int p = *L;
+  if (p < max_target) tok[p] = ys[0]; else *err |= 4;
+  *L = p + 1;
+}
+
+// Zeroes columns [c0, ld) of a row-major [rows, ld] array of 16-bit elements.
+__global__ void zero_cols_kernel(uint16_t* w, int ld, int c0) {
+  for (int c = c0 + threadIdx.x; c < ld; c += blockDim.x) w[(size_t)blockIdx.x * ld + c] = 0;
+}
+
+template <typename T>
+__global__ void to_dtype_kernel(T* out, const float* in, size_t n) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = Act<T>::from_f(in[i]);
+}
+
+// ---- the model ---------------------------------------------------------------------------
+
+struct WLin {
+  QWeight q;           // w [N, K] dense or packed; s/b for MLX affine
+  void* bias = nullptr;
+  int bits = 0;
+};
+struct WNorm {
+  void* w = nullptr;
+  void* b = nullptr;
+};
+struct WEnc {
+  WNorm ln1, ln2;
+  WLin qkv, o, fc1, fc2;
+};
+struct WDec {
+  WNorm ln1, ln2, ln3;
+  WLin qkv, o, cq, ckv, co, fc1, fc2;
+};
+
+size_t up256(size_t b) { return (b + 255) / 256 * 256; }
+
+}  // namespace
+}  // namespace vella
+
+struct vella_whisper {
+  vella_whisper_cfg cfg{};
+  int device = 0;
+  size_t elt = 2;
+  int kp1 = 0;  // conv1 K padded to a multiple of 64
+  void* arena = nullptr;
+  size_t arena_bytes = 0;
+  vella::WLin conv1, conv2, embed;
+  void* enc_pos = nullptr;
+  void* dec_pos = nullptr;
+  vella::WNorm enc_ln, dec_ln;
+  std::vector<vella::WEnc> enc;
+  std::vector<vella::WDec> dec;
+  // activations
+  void* act = nullptr;
+  float* mel = nullptr;                          // [n_mels][2 n_audio]
+  void *col = nullptr, *x0 = nullptr;            // im2col, conv1 output [2A, d]
+  void *eh = nullptr, *en = nullptr, *eqkv = nullptr, *eatt = nullptr, *ef = nullptr, *enc_out = nullptr;
+  void* xkv = nullptr;                           // [dec_layers][A][2d]
+  void* kv = nullptr;                            // [dec_layers][2][H][max_target][hd]
+  void *dh = nullptr, *dn = nullptr, *dqkv = nullptr, *datt = nullptr, *dq2 = nullptr, *df = nullptr;
+  void* logits = nullptr;                        // [kWRows, V]
+  int *ys = nullptr, *tok = nullptr, *L = nullptr, *dzero = nullptr, *err = nullptr, *nonfinite = nullptr;
+  void* argmax_sc = nullptr;
+  void* gemm_ws = nullptr;
+  size_t gemm_ws_bytes = 0;
+  cudaStream_t stream = nullptr;
+  cudaGraphExec_t step_exec = nullptr;
+  bool step_warm = false;
+  bool encoded = false;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
+  vella_whisper_stats stats{};
+};
+
+namespace vella {
+namespace {
+
+int gemm(vella_whisper* w, const WLin& L, const void* x, int rows, void* out, int epi, const void* residual,
+         cudaStream_t s) {
+  vella_qgemm_desc d{rows, L.q.n, L.q.k, L.bits, 64, w->cfg.dtype, epi};
+  QgemmPlan p;
+  if (!qgemm_plan(d, &p)) return fail(VELLA_E_UNSUPPORTED, "whisper gemm %dx%dx%d bits %d", rows, L.q.n, L.q.k, L.bits);
+  if (p.workspace > w->gemm_ws_bytes) return fail(VELLA_E_INVALID, "whisper gemm workspace too small");
+  return qgemm_launch(d, p, x, L.q.w, L.q.s, L.q.b, nullptr, nullptr, nullptr, L.bias, residual, out, w->gemm_ws, s);
+}
+
+template <typename T>
+int layernorm_t(void* out, const void* x, const WNorm& n, int rows, int D, float eps, cudaStream_t s) {
+  return launch_kernel(layernorm_kernel<T>, dim3(rows), dim3(256), 0, s, static_cast<T*>(out), static_cast<const T*>(x),
+                       static_cast<const T*>(n.w), static_cast<const T*>(n.b), D, eps);
+}
+int layernorm(vella_whisper* w, void* out, const void* x, const WNorm& n, int rows, cudaStream_t s) {
+  if (rows <= 0) return VELLA_OK;
+  const int D = w->cfg.d_model;
+  return w->cfg.dtype == VELLA_BF16 ? layernorm_t<__nv_bfloat16>(out, x, n, rows, D, w->cfg.eps, s)
+                                    : layernorm_t<__half>(out, x, n, rows, D, w->cfg.eps, s);
+}
+
+template <typename Tin>
+int im2col(vella_whisper* w, void* out, const Tin* x, int C, int stride, int T_in, long long ts, long long cs, int Kp,
+           int rows, cudaStream_t s) {
+  if (w->cfg.dtype == VELLA_BF16)
+    return launch_kernel(im2col_kernel<Tin, __nv_bfloat16>, dim3(rows), dim3(256), 0, s,
+                         static_cast<__nv_bfloat16*>(out), x, C, stride, T_in, ts, cs, Kp);
+  return launch_kernel(im2col_kernel<Tin, __half>, dim3(rows), dim3(256), 0, s, static_cast<__half*>(out), x, C,
+                       stride, T_in, ts, cs, Kp);
+}
+
+template <typename T>
+int embed_t(vella_whisper* w, PosRef pr, int rows, cudaStream_t s) {
+  const vella_whisper_cfg& c = w->cfg;
+  auto* h = static_cast<T*>(w->dh);
+  const auto* es = static_cast<const T*>(w->embed.q.s);
+  const auto* eb = static_cast<const T*>(w->embed.q.b);
+  const auto* pos = static_cast<const T*>(w->dec_pos);
+  if (c.bits == 4)
+    return launch_kernel(wembed_kernel<T, 4>, dim3(rows), dim3(256), 0, s, h, (const void*)w->embed.q.w, es, eb, pos,
+                         (const int*)w->tok, pr, c.d_model, c.vocab, c.max_target, w->err);
+  if (c.bits == 8)
+    return launch_kernel(wembed_kernel<T, 8>, dim3(rows), dim3(256), 0, s, h, (const void*)w->embed.q.w, es, eb, pos,
+                         (const int*)w->tok, pr, c.d_model, c.vocab, c.max_target, w->err);
+  return launch_kernel(wembed_kernel<T, 0>, dim3(rows), dim3(256), 0, s, h, (const void*)w->embed.q.w, es, eb, pos,
+                       (const int*)w->tok, pr, c.d_model, c.vocab, c.max_target, w->err);
+}
+
+template <typename T>
+int append_t(vella_whisper* w, int l, PosRef pr, int rows, cudaStream_t s) {
+  const vella_whisper_cfg& c = w->cfg;
+  const int hd = c.d_model / c.heads;
+  const size_t per = (size_t)c.heads * c.max_target * hd;
+  T* kc = static_cast<T*>(w->kv) + (size_t)l * 2 * per;
+  return launch_kernel(wappend_kernel<T>, dim3(rows), dim3(256), 0, s, static_cast<const T*>(w->dqkv), kc, kc + per, pr,
+                       c.d_model, hd, c.max_target);
+}
+
+void* kcache(vella_whisper* w, int l) {
+  const vella_whisper_cfg& c = w->cfg;
+  const size_t per = (size_t)c.heads * c.max_target * (c.d_model / c.heads) * w->elt;
+  return static_cast<char*>(w->kv) + (size_t)l * 2 * per;
+}
+void* vcache(vella_whisper* w, int l) {
+  const vella_whisper_cfg& c = w->cfg;
+  const size_t per = (size_t)c.heads * c.max_target * (c.d_model / c.heads) * w->elt;
+  return static_cast<char*>(w->kv) + ((size_t)l * 2 + 1) * per;
+}
+
+// Decoder over `rows` positions starting at *pr.base + pr.off (tokens from w->tok); the
+// last `logits_rows` rows go through the vocabulary projection and the argmax.
+int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, cudaStream_t s) {
+  const vella_whisper_cfg& c = w->cfg;
+  const int d = c.d_model, H = c.heads, hd = d / H, dt = c.dtype;
+  const float scale = 1.0f / std::sqrt((float)hd);
+  const bool bf = dt == VELLA_BF16;
+  int rc;
+  if ((rc = bf ? embed_t<__nv_bfloat16>(w, pr, rows, s) : embed_t<__half>(w, pr, rows, s))) return rc;
+  for (int l = 0; l < c.dec_layers; ++l) {
+    const WDec& L = w->dec[l];
+    if ((rc = layernorm(w, w->dn, w->dh, L.ln1, rows, s))) return rc;
+    if ((rc = gemm(w, L.qkv, w->dn, rows, w->dqkv, VELLA_EPI_BIAS, nullptr, s))) return rc;
+    if ((rc = bf ? append_t<__nv_bfloat16>(w, l, pr, rows, s) : append_t<__half>(w, l, pr, rows, s))) return rc;
+    AttnView sv;
+    sv.q = w->dqkv; sv.q_rs = 3LL * d;
+    sv.k = kcache(w, l); sv.v = vcache(w, l);
+    sv.kv_hs = (long long)c.max_target * hd; sv.kv_rs = hd;
+    sv.out = w->datt; sv.o_rs = d;
+    if ((rc = launch_attention_ex(dt, sv, 1, pr, 1, rows, H, H, hd, c.max_target, scale, s))) return rc;
+    if ((rc = gemm(w, L.o, w->datt, rows, w->dh, VELLA_EPI_BIAS_RESIDUAL, w->dh, s))) return rc;
+    if ((rc = layernorm(w, w->dn, w->dh, L.ln2, rows, s))) return rc;
+    if ((rc = gemm(w, L.cq, w->dn, rows, w->dq2, VELLA_EPI_BIAS, nullptr, s))) return rc;
+    AttnView cv;
+    char* xk = static_cast<char*>(w->xkv) + (size_t)l * c.n_audio * 2 * d * w->elt;
+    cv.q = w->dq2; cv.q_rs = d;
+    cv.k = xk; cv.v = xk + (size_t)d * w->elt;
+    cv.kv_hs = hd; cv.kv_rs = 2LL * d;
+    cv.out = w->datt; cv.o_rs = d;
+    if ((rc = launch_attention_ex(dt, cv, 1, PosRef{w->dzero, 0}, 0, rows, H, H, hd, c.n_audio, scale, s))) return rc;
+    if ((rc = gemm(w, L.co, w->datt, rows, w->dh, VELLA_EPI_BIAS_RESIDUAL, w->dh, s))) return rc;
+    if ((rc = layernorm(w, w->dn, w->dh, L.ln3, rows, s))) return rc;
+    if ((rc = gemm(w, L.fc1, w->dn, rows, w->df, VELLA_EPI_BIAS_GELU, nullptr, s))) return rc;
+    if ((rc = gemm(w, L.fc2, w->df, rows, w->dh, VELLA_EPI_BIAS_RESIDUAL, w->dh, s))) return rc;
+  }
+  if ((rc = layernorm(w, w->dn, w->dh, w->dec_ln, rows, s))) return rc;
+  if (logits_rows > 0) {
+    const char* xr = static_cast<const char*>(w->dn) + (size_t)(rows - logits_rows) * d * w->elt;
+    if ((rc = gemm(w, w->embed, xr, logits_rows, w->logits, VELLA_EPI_NONE, nullptr, s))) return rc;
+    if ((rc = launch_argmax(dt, w->logits, logits_rows, c.vocab, (size_t)c.vocab, w->ys, w->argmax_sc, w->nonfinite, s)))
+      return rc;
+  }
+  return VELLA_OK;
+}
+
+int encoder_forward(vella_whisper* w, cudaStream_t s) {
+  const vella_whisper_cfg& c = w->cfg;
+  const int d = c.d_model, H = c.heads, hd = d / H, A = c.n_audio, dt = c.dtype;
+  const float scale = 1.0f / std::sqrt((float)hd);
+  int rc;
+  // conv1 over the 2A mel frames (mel is [n_mels][2A]: x(t, c) = mel[c * 2A + t])
+  if ((rc = im2col<float>(w, w->col, w->mel, c.n_mels, 1, 2 * A, 1, 2LL * A, w->kp1, 2 * A, s))) return rc;
+  if ((rc = gemm(w, w->conv1, w->col, 2 * A, w->x0, VELLA_EPI_BIAS_GELU, nullptr, s))) return rc;
+  // conv2, stride 2, + positions
+  if (dt == VELLA_BF16) rc = im2col<__nv_bfloat16>(w, w->col, static_cast<const __nv_bfloat16*>(w->x0), d, 2, 2 * A, d, 1, 3 * d, A, s);
+  else rc = im2col<__half>(w, w->col, static_cast<const __half*>(w->x0), d, 2, 2 * A, d, 1, 3 * d, A, s);
+  if (rc) return rc;
+  if ((rc = gemm(w, w->conv2, w->col, A, w->eh, VELLA_EPI_BIAS_GELU_RESIDUAL, w->enc_pos, s))) return rc;
+  for (const WEnc& L : w->enc) {
+    if ((rc = layernorm(w, w->en, w->eh, L.ln1, A, s))) return rc;
+    if ((rc = gemm(w, L.qkv, w->en, A, w->eqkv, VELLA_EPI_BIAS, nullptr, s))) return rc;
+    AttnView v;
+    const char* qkv = static_cast<const char*>(w->eqkv);
+    v.q = qkv; v.q_rs = 3LL * d;
+    v.k = qkv + (size_t)d * w->elt; v.v = qkv + (size_t)2 * d * w->elt;
+    v.kv_hs = hd; v.kv_rs = 3LL * d;
+    v.out = w->eatt; v.o_rs = d;
+    if ((rc = launch_attention_ex(dt, v, 1, PosRef{w->dzero, 0}, 0, A, H, H, hd, A, scale, s))) return rc;
+    if ((rc = gemm(w, L.o, w->eatt, A, w->eh, VELLA_EPI_BIAS_RESIDUAL, w->eh, s))) return rc;
+    if ((rc = layernorm(w, w->en, w->eh, L.ln2, A, s))) return rc;
+    if ((rc = gemm(w, L.fc1, w->en, A, w->ef, VELLA_EPI_BIAS_GELU, nullptr, s))) return rc;
+    if ((rc = gemm(w, L.fc2, w->ef, A, w->eh, VELLA_EPI_BIAS_RESIDUAL, w->eh, s))) return rc;
+  }
+  if ((rc = layernorm(w, w->enc_out, w->eh, w->enc_ln, A, s))) return rc;
+  for (int l = 0; l < c.dec_layers; ++l) {
+    char* xk = static_cast<char*>(w->xkv) + (size_t)l * A * 2 * d * w->elt;
+    if ((rc = gemm(w, w->dec[l].ckv, w->enc_out, A, xk, VELLA_EPI_BIAS, nullptr, s))) return rc;
+  }
+  return VELLA_OK;
+}
+
+int check_flags(vella_whisper* w, const char* what) {
+  int f[2] = {0, 0};
+  VELLA_CUDA_TRY(cudaMemcpy(f, w->err, 2 * sizeof(int), cudaMemcpyDeviceToHost));
+  if (f[0]) {
+    VELLA_CUDA_TRY(cudaMemset(w->err, 0, sizeof(int)));
+    return fail(VELLA_E_INVALID, "%s: error flags 0x%x (token id out of range or past max_target)", what, f[0]);
+  }
+  if (f[1]) {
+    VELLA_CUDA_TRY(cudaMemset(w->nonfinite, 0, sizeof(int)));
+    return fail(VELLA_E_NONFINITE, "%s: non-finite logits", what);
+  }
+  const int st = stream_fault_status(1), tc = tc_fault_status(1);
+  if (st < 0 || tc < 0) return fail(VELLA_E_CUDA, "cannot read the kernel fault flags");
+  if (st || tc) return fail(VELLA_E_CUDA, "%s: a GEMM pipeline wait timed out (flags 0x%x / 0x%x)", what, st, tc);
+  return VELLA_OK;
+}
+
+// Byte offsets into one allocation.  Offsets start at 256 so that a planned tensor is never
+// offset 0: rebase() treats a null pointer as "tensor absent".
+struct Planner {
+  size_t off = 256;
+  size_t take(size_t bytes) {
+    const size_t o = off;
+    off += up256(bytes);
+    return o;
+  }
+};
+
+void plan_lin(WLin& L, int n, int k, int bits, size_t elt, Planner& P, bool has_bias) {
+  L.bits = bits;
+  L.q.n = n;
+  L.q.k = k;
+  if (bits) {
+    L.q.w_bytes = (size_t)n * k * bits / 8;
+    L.q.sb_bytes = (size_t)n * (k / 64) * elt;
+    L.q.w = reinterpret_cast<void*>(P.take(L.q.w_bytes));
+    L.q.s = reinterpret_cast<void*>(P.take(L.q.sb_bytes));
+    L.q.b = reinterpret_cast<void*>(P.take(L.q.sb_bytes));
+  } else {
+    L.q.w_bytes = (size_t)n * k * elt;
+    L.q.w = reinterpret_cast<void*>(P.take(L.q.w_bytes));
+  }
+  if (has_bias) L.bias = reinterpret_cast<void*>(P.take((size_t)n * elt));
+}
+void plan_norm(WNorm& N, int d, size_t elt, Planner& P) {
+  N.w = reinterpret_cast<void*>(P.take((size_t)d * elt));
+  N.b = reinterpret_cast<void*>(P.take((size_t)d * elt));
+}
+template <typename X> void rebase(X*& p, char* base) { if (p) p = reinterpret_cast<X*>(base + reinterpret_cast<uintptr_t>(p)); }
+void rebase_lin(WLin& L, char* base) {
+  rebase(L.q.w, base); rebase(L.q.s, base); rebase(L.q.b, base); rebase(L.bias, base);
+}
+void rebase_norm(WNorm& N, char* base) { rebase(N.w, base); rebase(N.b, base); }
+
+size_t ws_for(const WLin& L, int dtype, int epi) {
+  vella_qgemm_desc d{kWRows, L.q.n, L.q.k, L.bits, 64, dtype, epi};
+  QgemmPlan p;
+  return qgemm_plan(d, &p) ? p.workspace : 0;
+}
+
+int run_step(vella_whisper* w) {
+  cudaStream_t s = w->stream;
+  auto enqueue = [&]() -> int {
+    int rc;
+    if ((rc = decoder_forward(w, PosRef{w->L, -1}, 1, 1, s))) return rc;
+    return launch_kernel(wcommit_kernel, dim3(1), dim3(1), 0, s, w->L, w->tok, (const int*)w->ys, w->cfg.max_target,
+                         w->err);
+  };
+  if (!w->step_warm) {
+    const int rc = enqueue();
+    if (rc) return rc;
+    w->step_warm = true;
+    return VELLA_OK;
+  }
+  if (!w->step_exec) {
+    VELLA_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    const int rc = enqueue();
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    const cudaError_t ie = cudaGraphInstantiate(&w->step_exec, g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) return cuda_fail(ie, "cudaGraphInstantiate");
+  }
+  VELLA_CUDA_TRY(cudaGraphLaunch(w->step_exec, s));
+  return VELLA_OK;
+}
+
+template <typename T>
+int write_sinusoids(vella_whisper* w, cudaStream_t s) {
+  const int A = w->cfg.n_audio, C = w->cfg.d_model, half = C / 2;
+  std::vector<float> table((size_t)A * C);
+  const double inc = std::log(10000.0) / (double)std::max(half - 1, 1);
+  for (int p = 0; p < A; ++p)
+    for (int i = 0; i < half; ++i) {
+      const double t = (double)p * std::exp(-inc * (double)i);
+      table[(size_t)p * C + i] = (float)std::sin(t);
+      table[(size_t)p * C + half + i] = (float)std::cos(t);
+    }
+  float* tmp = nullptr;
+  VELLA_CUDA_TRY(cudaMalloc(&tmp, table.size() * sizeof(float)));
+  cudaError_t e = cudaMemcpyAsync(tmp, table.data(), table.size() * sizeof(float), cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) {
+    to_dtype_kernel<T><<<(unsigned)((table.size() + 255) / 256), 256, 0, s>>>(static_cast<T*>(w->enc_pos), tmp, table.size());
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaFree(tmp);
+  if (e != cudaSuccess) return cuda_fail(e, "whisper sinusoid table");
+  return VELLA_OK;
+}
+
+}  // namespace
+}  // namespace vella
+
+using namespace vella;
+
+extern "C" {
+
+int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whisper** out) {
+  if (!cfg || !out) return fail(VELLA_E_INVALID, "vella_whisper_create: NULL argument");
+  *out = nullptr;
+  const vella_whisper_cfg c = *cfg;
+  if (c.d_model <= 0 || c.heads <= 0 || c.d_model % 64 || c.d_model % c.heads || c.ffn <= 0 || c.ffn % 64 ||
+      c.n_mels <= 0 || c.vocab <= 0 || c.n_audio <= 0 || c.max_target <= 0 || c.enc_layers < 0 || c.dec_layers < 1)
+    return fail(VELLA_E_INVALID, "vella_whisper_create: bad dimensions");
+  const int hd = c.d_model / c.heads;
+  if (hd != 64 && hd != 128) return fail(VELLA_E_UNSUPPORTED, "vella_whisper_create: head_dim %d (64 or 128)", hd);
+  if (c.d_model > kLnMaxD) return fail(VELLA_E_UNSUPPORTED, "vella_whisper_create: d_model above %d", kLnMaxD);
+  if (c.bits != 0 && c.bits != 4 && c.bits != 8) return fail(VELLA_E_UNSUPPORTED, "vella_whisper_create: bits %d", c.bits);
+  if (c.dtype != VELLA_F16 && c.dtype != VELLA_BF16) return fail(VELLA_E_UNSUPPORTED, "vella_whisper_create: dtype");
+  if (!(c.eps > 0.0f)) return fail(VELLA_E_INVALID, "vella_whisper_create: eps");
+  VELLA_CUDA_TRY(cudaSetDevice(device));
+  auto* w = new vella_whisper();
+  w->cfg = c;
+  w->device = device;
+  w->elt = 2;
+  const size_t e = w->elt;
+  const int d = c.d_model, A = c.n_audio, F = c.ffn, V = c.vocab, B = c.bits;
+  w->kp1 = (3 * c.n_mels + 63) / 64 * 64;
+  Planner P;
+  plan_lin(w->conv1, d, w->kp1, 0, e, P, true);
+  plan_lin(w->conv2, d, 3 * d, 0, e, P, true);
+  w->enc_pos = reinterpret_cast<void*>(P.take((size_t)A * d * e));
+  w->enc.resize(c.enc_layers);
+  for (WEnc& L : w->enc) {
+    plan_norm(L.ln1, d, e, P);
+    plan_lin(L.qkv, 3 * d, d, 0, e, P, true);
+    plan_lin(L.o, d, d, 0, e, P, true);
+    plan_norm(L.ln2, d, e, P);
+    plan_lin(L.fc1, F, d, 0, e, P, true);
+    plan_lin(L.fc2, d, F, 0, e, P, true);
+  }
+  plan_norm(w->enc_ln, d, e, P);
+  w->dec.resize(c.dec_layers);
+  for (WDec& L : w->dec) {
+    plan_norm(L.ln1, d, e, P);
+    plan_lin(L.qkv, 3 * d, d, B, e, P, true);
+    plan_lin(L.o, d, d, B, e, P, true);
+    plan_norm(L.ln2, d, e, P);
+    plan_lin(L.cq, d, d, B, e, P, true);
+    plan_lin(L.ckv, 2 * d, d, B, e, P, true);
+    plan_lin(L.co, d, d, B, e, P, true);
+    plan_norm(L.ln3, d, e, P);
+    plan_lin(L.fc1, F, d, B, e, P, true);
+    plan_lin(L.fc2, d, F, B, e, P, true);
+  }
+  plan_norm(w->dec_ln, d, e, P);
+  plan_lin(w->embed, V, d, B, e, P, false);
+  w->dec_pos = reinterpret_cast<void*>(P.take((size_t)c.max_target * d * e));
+  w->arena_bytes = P.off;
+
+  // activations
+  size_t ws = 0;
+  for (const WDec& L : w->dec) {
+    for (const WLin* l : {&L.qkv, &L.cq, &L.ckv}) ws = std::max(ws, ws_for(*l, c.dtype, VELLA_EPI_BIAS));
+    for (const WLin* l : {&L.o, &L.co, &L.fc2}) ws = std::max(ws, ws_for(*l, c.dtype, VELLA_EPI_BIAS_RESIDUAL));
+    ws = std::max(ws, ws_for(L.fc1, c.dtype, VELLA_EPI_BIAS_GELU));
+    break;
+  }
+  ws = std::max(ws, ws_for(w->embed, c.dtype, VELLA_EPI_NONE));
+  w->gemm_ws_bytes = ws;
+  const size_t R = kWRows;
+  const size_t hdim = (size_t)hd;
+  Planner Q;
+  const size_t o_mel = Q.take((size_t)c.n_mels * 2 * A * sizeof(float));
+  const size_t o_col = Q.take(std::max((size_t)2 * A * w->kp1, (size_t)A * 3 * d) * e);
+  const size_t o_x0 = Q.take((size_t)2 * A * d * e);
+  const size_t o_eh = Q.take((size_t)A * d * e), o_en = Q.take((size_t)A * d * e);
+  const size_t o_eqkv = Q.take((size_t)A * 3 * d * e), o_eatt = Q.take((size_t)A * d * e);
+  const size_t o_ef = Q.take((size_t)A * F * e), o_out = Q.take((size_t)A * d * e);
+  const size_t o_xkv = Q.take((size_t)c.dec_layers * A * 2 * d * e);
+  const size_t o_kv = Q.take((size_t)c.dec_layers * 2 * c.heads * c.max_target * hdim * e);
+  const size_t o_dh = Q.take(R * d * e), o_dn = Q.take(R * d * e), o_dqkv = Q.take(R * 3 * d * e);
+  const size_t o_datt = Q.take(R * d * e), o_dq2 = Q.take(R * d * e), o_df = Q.take(R * F * e);
+  const size_t o_logits = Q.take(R * (size_t)V * e);
+  const size_t o_ints = Q.take((R + (size_t)c.max_target + 8) * sizeof(int));
+  const size_t o_amx = Q.take(argmax_scratch_bytes(kWRows) + 512);
+  const size_t o_ws = Q.take(std::max<size_t>(ws, 256));
+  auto cleanup = [&]() {
+    if (w->act) cudaFree(w->act);
+    if (w->arena) cudaFree(w->arena);
+    if (w->stream) cudaStreamDestroy(w->stream);
+    cudaGetLastError();
+    delete w;
+  };
+  if (cudaMalloc(&w->arena, w->arena_bytes) != cudaSuccess || cudaMalloc(&w->act, Q.off) != cudaSuccess) {
+    cleanup();
+    return fail(VELLA_E_OOM, "vella_whisper_create: %zu + %zu bytes", P.off, Q.off);
+  }
+  if (cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMemset(w->act, 0, Q.off) != cudaSuccess || cudaMemset(w->arena, 0, w->arena_bytes) != cudaSuccess ||
+      cudaEventCreate(&w->ev0) != cudaSuccess || cudaEventCreate(&w->ev1) != cudaSuccess ||
+      cudaEventCreate(&w->ev2) != cudaSuccess) {
+    cleanup();
+    return fail(VELLA_E_CUDA, "vella_whisper_create: stream, events or memset failed");
+  }
+  char* base = static_cast<char*>(w->arena);
+  rebase_lin(w->conv1, base); rebase_lin(w->conv2, base); rebase_lin(w->embed, base);
+  rebase(w->enc_pos, base); rebase(w->dec_pos, base);
+  rebase_norm(w->enc_ln, base); rebase_norm(w->dec_ln, base);
+  for (WEnc& L : w->enc) {
+    rebase_norm(L.ln1, base); rebase_norm(L.ln2, base);
+    for (WLin* l : {&L.qkv, &L.o, &L.fc1, &L.fc2}) rebase_lin(*l, base);
+  }
+  for (WDec& L : w->dec) {
+    rebase_norm(L.ln1, base); rebase_norm(L.ln2, base); rebase_norm(L.ln3, base);
+    for (WLin* l : {&L.qkv, &L.o, &L.cq, &L.ckv, &L.co, &L.fc1, &L.fc2}) rebase_lin(*l, base);
+  }
+  char* ab = static_cast<char*>(w->act);
+  w->mel = reinterpret_cast<float*>(ab + o_mel);
+  w->col = ab + o_col; w->x0 = ab + o_x0;
+  w->eh = ab + o_eh; w->en = ab + o_en; w->eqkv = ab + o_eqkv; w->eatt = ab + o_eatt; w->ef = ab + o_ef;
+  w->enc_out = ab + o_out; w->xkv = ab + o_xkv; w->kv = ab + o_kv;
+  w->dh = ab + o_dh; w->dn = ab + o_dn; w->dqkv = ab + o_dqkv; w->datt = ab + o_datt; w->dq2 = ab + o_dq2;
+  w->df = ab + o_df; w->logits = ab + o_logits;
+  int* ints = reinterpret_cast<int*>(ab + o_ints);
+  w->ys = ints;
+  w->tok = ints + R;
+  w->L = w->tok + c.max_target;
+  w->dzero = w->L + 1;
+  w->err = w->L + 2;
+  w->nonfinite = w->L + 3;
+  w->argmax_sc = ab + o_amx;
+  w->gemm_ws = ab + o_ws;
+  *out = w;
+  return VELLA_OK;
+}
+
+int vella_whisper_destroy(vella_whisper* w) {
+  if (!w) return VELLA_OK;
+  cudaSetDevice(w->device);
+  if (w->stream) cudaStreamSynchronize(w->stream);
+  if (w->step_exec) cudaGraphExecDestroy(w->step_exec);
+  for (cudaEvent_t e : {w->ev0, w->ev1, w->ev2})
+    if (e) cudaEventDestroy(e);
+  if (w->act) cudaFree(w->act);
+  if (w->arena) cudaFree(w->arena);
+  if (w->stream) cudaStreamDestroy(w->stream);
+  cudaGetLastError();
+  delete w;
+  return VELLA_OK;
+}
+
+int vella_whisper_init_random(vella_whisper* w, uint64_t seed, float std) {
+  if (!w) return fail(VELLA_E_INVALID, "vella_whisper_init_random: NULL handle");
+  VELLA_CUDA_TRY(cudaSetDevice(w->device));
+  const vella_whisper_cfg& c = w->cfg;
+  cudaStream_t s = w->stream;
+  const int dt = c.dtype, d = c.d_model;
+  uint32_t tid = 1;
+  int rc;
+  auto dense = [&](void* p, size_t n, float mean, float sd) { return fill_normal(p, n, dt, seed, tid++, mean, sd, s); };
+  auto lin = [&](WLin& L) -> int {
+    int r;
+    if (L.bits) r = quantize_random(L.q, L.bits, dt, seed, tid++, std, s);
+    else r = dense(L.q.w, (size_t)L.q.n * L.q.k, 0.0f, std);
+    if (r) return r;
+    return L.bias ? dense(L.bias, (size_t)L.q.n, 0.0f, std) : VELLA_OK;
+  };
+  auto norm = [&](WNorm& N) -> int {
+    int r = dense(N.w, (size_t)d, 1.0f, 0.1f);
+    return r ? r : dense(N.b, (size_t)d, 0.0f, std);
+  };
+  if ((rc = lin(w->conv1)) || (rc = lin(w->conv2))) return rc;
+  // conv1's K padding columns are zero
+  if (w->kp1 > 3 * c.n_mels) {
+    zero_cols_kernel<<<d, 64, 0, s>>>(static_cast<uint16_t*>(w->conv1.q.w), w->kp1, 3 * c.n_mels);
+    VELLA_CUDA_TRY(cudaGetLastError());
+  }
+  for (WEnc& L : w->enc) {
+    if ((rc = norm(L.ln1)) || (rc = lin(L.qkv)) || (rc = lin(L.o)) || (rc = norm(L.ln2)) || (rc = lin(L.fc1)) ||
+        (rc = lin(L.fc2)))
+      return rc;
+    VELLA_CUDA_TRY(cudaMemsetAsync(static_cast<char*>(L.qkv.bias) + (size_t)d * w->elt, 0, (size_t)d * w->elt, s));
+  }
+  if ((rc = norm(w->enc_ln))) return rc;
+  for (WDec& L : w->dec) {
+    if ((rc = norm(L.ln1)) || (rc = lin(L.qkv)) || (rc = lin(L.o)) || (rc = norm(L.ln2)) || (rc = lin(L.cq)) ||
+        (rc = lin(L.ckv)) || (rc = lin(L.co)) || (rc = norm(L.ln3)) || (rc = lin(L.fc1)) || (rc = lin(L.fc2)))
+      return rc;
+    VELLA_CUDA_TRY(cudaMemsetAsync(static_cast<char*>(L.qkv.bias) + (size_t)d * w->elt, 0, (size_t)d * w->elt, s));
+    VELLA_CUDA_TRY(cudaMemsetAsync(L.ckv.bias, 0, (size_t)d * w->elt, s));
+  }
+  if ((rc = norm(w->dec_ln)) || (rc = lin(w->embed))) return rc;
+  if ((rc = dense(w->dec_pos, (size_t)c.max_target * d, 0.0f, std))) return rc;
+  if ((rc = dt == VELLA_BF16 ? write_sinusoids<__nv_bfloat16>(w, s) : write_sinusoids<__half>(w, s))) return rc;
+  VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+  return VELLA_OK;
+}
+
+int vella_whisper_tensor(vella_whisper* w, const char* name, int32_t layer, void** ptr, size_t* bytes) {
+  if (!w || !name || !ptr || !bytes) return fail(VELLA_E_INVALID, "vella_whisper_tensor: NULL argument");
+  const vella_whisper_cfg& c = w->cfg;
+  const size_t e = w->elt;
+  const std::string n(name);
+  auto ret = [&](void* p, size_t b) {
+    *ptr = p;
+    *bytes = b;
+    return p ? VELLA_OK : fail(VELLA_E_INVALID, "vella_whisper_tensor: '%s' does not exist", name);
+  };
+  auto lin = [&](const WLin& L, const std::string& part) -> int {
+    if (part == "w") return ret(L.q.w, L.q.w_bytes);
+    if (part == "s") return ret(L.bits ? L.q.s : nullptr, L.q.sb_bytes);
+    if (part == "b") return ret(L.bits ? L.q.b : nullptr, L.q.sb_bytes);
+    if (part == "bias") return ret(L.bias, (size_t)L.q.n * e);
+    return fail(VELLA_E_INVALID, "vella_whisper_tensor: unknown part '%s'", name);
+  };
+  auto norm = [&](const WNorm& N, const std::string& part) -> int {
+    if (part == "weight") return ret(N.w, (size_t)c.d_model * e);
+    if (part == "bias") return ret(N.b, (size_t)c.d_model * e);
+    return fail(VELLA_E_INVALID, "vella_whisper_tensor: unknown part '%s'", name);
+  };
+  const size_t dot = n.rfind('.');
+  const std::string head = dot == std::string::npos ? n : n.substr(0, dot);
+  const std::string part = dot == std::string::npos ? "" : n.substr(dot + 1);
+  if (n == "enc_pos") return ret(w->enc_pos, (size_t)c.n_audio * c.d_model * e);
+  if (n == "dec_pos") return ret(w->dec_pos, (size_t)c.max_target * c.d_model * e);
+  if (n == "enc_out") return ret(w->enc_out, (size_t)c.n_audio * c.d_model * e);
+  if (head == "conv1") return lin(w->conv1, part);
+  if (head == "conv2") return lin(w->conv2, part);
+  if (head == "embed") return lin(w->embed, part);
+  if (head == "enc_ln") return norm(w->enc_ln, part);
+  if (head == "dec_ln") return norm(w->dec_ln, part);
+  if (head.rfind("enc.", 0) == 0) {
+    if (layer < 0 || layer >= c.enc_layers) return fail(VELLA_E_INVALID, "vella_whisper_tensor: encoder layer %d", layer);
+    const WEnc& L = w->enc[layer];
+    const std::string t = head.substr(4);
+    if (t == "ln1") return norm(L.ln1, part);
+    if (t == "ln2") return norm(L.ln2, part);
+    if (t == "qkv") return lin(L.qkv, part);
+    if (t == "o") return lin(L.o, part);
+    if (t == "fc1") return lin(L.fc1, part);
+    if (t == "fc2") return lin(L.fc2, part);
+  }
+  if (head.rfind("dec.", 0) == 0) {
+    if (layer < 0 || layer >= c.dec_layers) return fail(VELLA_E_INVALID, "vella_whisper_tensor: decoder layer %d", layer);
+    const WDec& L = w->dec[layer];
+    const std::string t = head.substr(4);
+    if (t == "ln1") return norm(L.ln1, part);
+    if (t == "ln2") return norm(L.ln2, part);
+    if (t == "ln3") return norm(L.ln3, part);
+    if (t == "qkv") return lin(L.qkv, part);
+    if (t == "o") return lin(L.o, part);
+    if (t == "cq") return lin(L.cq, part);
+    if (t == "ckv") return lin(L.ckv, part);
+    if (t == "co") return lin(L.co, part);
+    if (t == "fc1") return lin(L.fc1, part);
+    if (t == "fc2") return lin(L.fc2, part);
+  }
+  return fail(VELLA_E_INVALID, "vella_whisper_tensor: unknown tensor '%s'", name);
+}
+
+int vella_whisper_encode(vella_whisper* w, const float* mel, int32_t on_host) {
+  if (!w || !mel) return fail(VELLA_E_INVALID, "vella_whisper_encode: NULL argument");
+  VELLA_CUDA_TRY(cudaSetDevice(w->device));
+  const vella_whisper_cfg& c = w->cfg;
+  cudaStream_t s = w->stream;
+  VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
+  VELLA_CUDA_TRY(cudaMemcpyAsync(w->mel, mel, (size_t)c.n_mels * 2 * c.n_audio * sizeof(float),
+                                 on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, s));
+  int rc = encoder_forward(w, s);
+  if (rc) return rc;
+  VELLA_CUDA_TRY(cudaEventRecord(w->ev1, s));
+  VELLA_CUDA_TRY(cudaEventSynchronize(w->ev1));
+  cudaEventElapsedTime(&w->stats.encode_ms, w->ev0, w->ev1);
+  if ((rc = check_flags(w, "vella_whisper_encode"))) return rc;
+  w->encoded = true;
+  return VELLA_OK;
+}
+
+int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int32_t n_prompt, int32_t max_tokens, int32_t eot,
+                         int32_t* out_tokens, int32_t* n_out) {
+  if (!w || !prompt || !n_out || (max_tokens > 0 && !out_tokens))
+    return fail(VELLA_E_INVALID, "vella_whisper_decode: NULL argument");
+  const vella_whisper_cfg& c = w->cfg;
+  if (!w->encoded) return fail(VELLA_E_INVALID, "vella_whisper_decode: encode first");
+  if (n_prompt < 1 || n_prompt > kWRows) return fail(VELLA_E_INVALID, "vella_whisper_decode: prompt of %d tokens (1..%d)", n_prompt, kWRows);
+  if (max_tokens < 0 || n_prompt + max_tokens > c.max_target)
+    return fail(VELLA_E_INVALID, "vella_whisper_decode: %d + %d positions exceed max_target %d", n_prompt, max_tokens,
+                c.max_target);
+  *n_out = 0;
+  if (max_tokens == 0) return VELLA_OK;
+  VELLA_CUDA_TRY(cudaSetDevice(w->device));
+  cudaStream_t s = w->stream;
+  std::vector<int> init(n_prompt + 1);
+  std::copy(prompt, prompt + n_prompt, init.begin());
+  VELLA_CUDA_TRY(cudaMemcpyAsync(w->tok, init.data(), n_prompt * sizeof(int), cudaMemcpyHostToDevice, s));
+  VELLA_CUDA_TRY(cudaMemcpyAsync(w->L, &n_prompt, sizeof(int), cudaMemcpyHostToDevice, s));
+  VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
+  int rc = decoder_forward(w, PosRef{w->dzero, 0}, n_prompt, 1, s);
+  if (rc) return rc;
+  if ((rc = launch_kernel(wcommit_kernel, dim3(1), dim3(1), 0, s, w->L, w->tok, (const int*)w->ys, c.max_target, w->err)))
+    return rc;
+  VELLA_CUDA_TRY(cudaEventRecord(w->ev1, s));
+  int produced = 1;
+  std::vector<int> toks;
+  int t0 = 0;
+  if (eot >= 0) {
+    VELLA_CUDA_TRY(cudaMemcpyAsync(&t0, w->tok + n_prompt, sizeof(int), cudaMemcpyDeviceToHost, s));
+    VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+  }
+  bool stop = eot >= 0 && t0 == eot;
+  while (!stop && produced < max_tokens) {
+    if ((rc = run_step(w))) return rc;
+    ++produced;
+    if (eot >= 0) {
+      int t = 0;
+      VELLA_CUDA_TRY(cudaMemcpyAsync(&t, w->tok + n_prompt + produced - 1, sizeof(int), cudaMemcpyDeviceToHost, s));
+      VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+      stop = t == eot;
+    }
+  }
+  VELLA_CUDA_TRY(cudaEventRecord(w->ev2, s));
+  toks.resize(produced);
+  VELLA_CUDA_TRY(cudaMemcpyAsync(toks.data(), w->tok + n_prompt, produced * sizeof(int), cudaMemcpyDeviceToHost, s));
+  VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+  cudaEventElapsedTime(&w->stats.prefill_ms, w->ev0, w->ev1);
+  cudaEventElapsedTime(&w->stats.decode_ms, w->ev1, w->ev2);
+  if ((rc = check_flags(w, "vella_whisper_decode"))) return rc;
+  int n = produced;
+  if (eot >= 0 && n > 0 && toks[n - 1] == eot) --n;  // the end-of-text token is not emitted
+  std::copy(toks.begin(), toks.begin() + n, out_tokens);
+  *n_out = n;
+  w->stats.tokens = n;
+  return VELLA_OK;
+}
+
+int vella_whisper_score(vella_whisper* w, const int32_t* tokens, int32_t T, void* logits, int32_t on_host) {
+  if (!w || !tokens || !logits) return fail(VELLA_E_INVALID, "vella_whisper_score: NULL argument");
+  const vella_whisper_cfg& c = w->cfg;
+  if (!w->encoded) return fail(VELLA_E_INVALID, "vella_whisper_score: encode first");
+  if (T < 1 || T > c.max_target) return fail(VELLA_E_INVALID, "vella_whisper_score: %d tokens", T);
+  VELLA_CUDA_TRY(cudaSetDevice(w->device));
+  cudaStream_t s = w->stream;
+  VELLA_CUDA_TRY(cudaMemcpyAsync(w->tok, tokens, (size_t)T * sizeof(int), cudaMemcpyHostToDevice, s));
+  const size_t lrow = (size_t)c.vocab * w->elt;
+  int rc;
+  for (int s0 = 0; s0 < T; s0 += kWRows) {
+    const int rows = std::min(kWRows, T - s0);
+    if ((rc = decoder_forward(w, PosRef{w->dzero, s0}, rows, rows, s))) return rc;
+    VELLA_CUDA_TRY(cudaMemcpyAsync(static_cast<char*>(logits) + (size_t)s0 * lrow, w->logits, (size_t)rows * lrow,
+                                   on_host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, s));
+  }
+  VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+  return check_flags(w, "vella_whisper_score");
+}
+
+int vella_whisper_get_stats(const vella_whisper* w, vella_whisper_stats* out) {
+  if (!w || !out) return fail(VELLA_E_INVALID, "vella_whisper_get_stats: NULL argument");
+  *out = w->stats;
+  return VELLA_OK;
+}
+
+}  // extern "C"

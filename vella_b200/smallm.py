@@ -79,9 +79,9 @@ def matmul(x: torch.Tensor, weights: Weights, epilogue: str = "none", bias: Opti
     rows = x.numel() // max(k, 1)
     if not x.is_cuda or x.dtype not in _DTYPES or not _fits(weights, k, x.dtype):
         return None
-    if epilogue in ("bias", "biasResidual") and (bias is None or bias.numel() != n):
+    if epilogue in ("bias", "biasResidual", "biasGelu", "biasGeluResidual") and (bias is None or bias.numel() != n):
         return None
-    if epilogue in ("residual", "biasResidual") and (residual is None or residual.numel() != rows * n):
+    if epilogue in ("residual", "biasResidual", "biasGeluResidual") and (residual is None or residual.numel() != rows * n):
         return None
     if epilogue == "siluGate":
         if up is None or up.bits != weights.bits or up.w.shape != weights.w.shape or not _fits(up, k, x.dtype):
