@@ -1,8 +1,13 @@
 """Benchmark of the int4 draft-and-verify decode path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload spec|gemm] [--impl vella|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload spec|gemm|whisper] [--impl vella|reference]
 
 Prints ONE JSON line on rank 0.  Workloads:
+  spec  (default) the 30B-class int4 draft-and-verify decode: tokens/s/GPU at K=4, p=0.7 with
+        the K in {4,8} x p in {.5,.7,.9} sweep in the same line.
+  whisper  the Whisper decoder step at large-v3-turbo shapes (fp16, one stream, 224 greedy
+        tokens after a 4-token prompt, encoder included per step), with the Whisper-tiny
+        (config 1) GPU rate beside its CPU oracle rate.
   gemm  the small-M MLX-affine GEMM sweep: M in {1,2,4,5,8,9,16} x (N,K) in
         {(5120,5120),(1024,5120),(25600,5120),(5120,25600),(151936,5120)} x int4/int8,
         weights ~N(0,0.02) quantized group 64 with bf16 scale/bias, x ~N(0,1) bf16.
@@ -542,6 +547,171 @@ def run_reference(args, rank, world):
             "e2e": {"value": round(tps, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ---------------------------------------------------------------------------------------
+# Whisper decoder step (config 3: large-v3-turbo shapes, fp16) and the tiny-shaped config 1
+# ---------------------------------------------------------------------------------------
+
+WHISPER_PROMPT = [50258, 50259, 50359, 50363]  # <|startoftranscript|> <|en|> <|transcribe|> <|notimestamps|>
+WHISPER_TOKENS = 224
+
+
+def whisper_step_bytes(c):
+    """Algorithmic HBM bytes of one decoder step: the decoder Linears (cross k|v excluded:
+    projected once per window), the vocabulary projection, the cross K/V of every layer and
+    the self K/V up to the mean position."""
+    d, F, V, A = c.d_model, c.ffn, c.vocab, c.n_audio
+    wb = (c.bits / 8) if c.bits else 2
+    sb = (4 / 64) if c.bits else 0
+    per_layer = (3 * d * d + d * d + d * d + d * d + 2 * d * F) * (wb + sb)
+    vocab = V * d * (wb + sb)
+    cross = c.dec_layers * A * 2 * d * 2
+    self_kv = c.dec_layers * 2 * (len(WHISPER_PROMPT) + WHISPER_TOKENS // 2) * d * 2
+    return c.dec_layers * per_layer + vocab + cross + self_kv
+
+
+def whisper_encoder_flops(c):
+    d, F, A = c.d_model, c.ffn, c.n_audio
+    kp1 = (3 * c.n_mels + 63) // 64 * 64
+    conv = 2 * (2 * A) * d * kp1 + 2 * A * d * 3 * d
+    layer = 2 * A * (3 * d * d + d * d + 2 * d * F) + 2 * 2 * A * A * d
+    return conv + c.enc_layers * layer + 2 * A * 2 * d * d * c.dec_layers
+
+
+def whisper_oracle_tokens_per_s(seconds_budget=6.0):
+    """The oracle's greedy decode of the tiny config on this host's cores (numpy), a bounded
+    sample: the encoder once, then greedy steps until the budget is spent."""
+    import numpy as np
+    from oracle import affine as A
+    from oracle import whisper as Wh
+    c = Wh.WhisperConfig()  # Whisper-tiny shapes, int4 decoder
+    rng = np.random.default_rng(0)
+    d, F = c.d_model, c.ffn
+
+    def dense(n, k):
+        return {"w": A.to_storage(rng.standard_normal((n, k)).astype(np.float32) * 0.02, "f16")}
+
+    def qnt(n, k):
+        p, s_, b_ = A.quantize(rng.standard_normal((n, k)).astype(np.float32) * 0.02, 4, "f16")
+        return {"w": p, "s": s_, "b": b_}
+
+    def vec(n, mean=0.0, sd=0.02):
+        return A.from_storage(A.to_storage((mean + sd * rng.standard_normal(n)).astype(np.float32), "f16"), "f16")
+
+    W = {"conv1": dense(d, 256), "conv1_b": vec(d), "conv2": dense(d, 3 * d), "conv2_b": vec(d),
+         "enc_pos": Wh.sinusoids(c.n_audio, d), "enc_ln_w": vec(d, 1, .1), "enc_ln_b": vec(d),
+         "dec_ln_w": vec(d, 1, .1), "dec_ln_b": vec(d), "embed": qnt(c.vocab, d),
+         "dec_pos": vec((c.max_target, d)), "enc": [], "dec": []}
+    for _ in range(c.enc_layers):
+        W["enc"].append({"ln1_w": vec(d, 1, .1), "ln1_b": vec(d), "qkv": dense(3 * d, d), "qkv_b": vec(3 * d),
+                         "o": dense(d, d), "o_b": vec(d), "ln2_w": vec(d, 1, .1), "ln2_b": vec(d),
+                         "fc1": dense(F, d), "fc1_b": vec(F), "fc2": dense(d, F), "fc2_b": vec(d)})
+    for _ in range(c.dec_layers):
+        L = {f"{n}_{x}": vec(d, 1, .1) if x == "w" else vec(d) for n in ("ln1", "ln2", "ln3") for x in ("w", "b")}
+        for name, n, k in (("qkv", 3 * d, d), ("o", d, d), ("cq", d, d), ("ckv", 2 * d, d), ("co", d, d),
+                           ("fc1", F, d), ("fc2", d, F)):
+            L[name], L[name + "_b"] = qnt(n, k), vec(n)
+        W["dec"].append(L)
+    mel = rng.standard_normal((c.n_mels, 2 * c.n_audio)).astype(np.float32)
+    enc = Wh.encoder(c, W, mel)
+    xkv = Wh.cross_kv(c, W, enc)
+    cache = [[None, None] for _ in W["dec"]]
+    Wh.decoder_forward(c, W, xkv, WHISPER_PROMPT, 0, cache)
+    t0, n, pos, tok = time.perf_counter(), 0, len(WHISPER_PROMPT), 0
+    while time.perf_counter() - t0 < seconds_budget and pos < c.max_target:
+        hid = Wh.decoder_forward(c, W, xkv, [tok], pos, cache)
+        tok = int(np.argmax(Wh.logits(c, W, hid)[0]))
+        pos += 1
+        n += 1
+    return n / (time.perf_counter() - t0), n
+
+
+def run_whisper(args, rank, world):
+    import numpy as np
+    import torch
+    from vella_b200 import whisper as VW
+    dist = dist_setup(world)
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    hbm, tflops, peak_kind = peaks()
+    c = VW.TURBO
+    m = VW.Whisper(c, local)
+    m.init_random(1 + rank, 0.02)
+    mel = torch.from_numpy(np.random.default_rng(2 + rank).standard_normal((c.n_mels, 2 * c.n_audio))
+                           .astype(np.float32)).pin_memory()
+    for _ in range(args.warmup):
+        m.encode(mel.numpy())
+        m.decode(WHISPER_PROMPT, WHISPER_TOKENS)
+    enc_ms, dec_ms, pre_ms, wall = [], [], [], []
+    with ClockSampler(local) as clk:
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            m.encode(mel.numpy())        # host mel -> device inside the call
+            r = m.decode(WHISPER_PROMPT, WHISPER_TOKENS)
+            wall.append(time.perf_counter() - t0)
+            st = m.stats()
+            enc_ms.append(st["encode_ms"])
+            pre_ms.append(r.prefill_ms)
+            dec_ms.append(r.decode_ms)
+            assert len(r.tokens) == WHISPER_TOKENS
+        torch.cuda.synchronize()
+    dec_s = sum(pre_ms + dec_ms) / 1e3
+    tokens = WHISPER_TOKENS * args.steps
+    dec_s = dist_max(dist, dec_s, f"cuda:{local}") if dist else dec_s
+    wall_s = dist_max(dist, sum(wall), f"cuda:{local}") if dist else sum(wall)
+    value = weak_scaling_value(tokens, world, dec_s)
+    step_us = sum(dec_ms) / (args.steps * (WHISPER_TOKENS - 1)) * 1e3
+    sbytes = whisper_step_bytes(c)
+    achieved = sbytes / (step_us * 1e-6) / 1e9
+    enc_tflops = whisper_encoder_flops(c) / (sum(enc_ms) / args.steps * 1e-3) / 1e12
+    line = {
+        "metric": "Whisper decoder tokens/s/GPU (large-v3-turbo shapes, fp16, 1 stream, greedy 224 tokens)",
+        "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dec_s * 1e3 / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "Whisper large-v3-turbo shapes (32 enc / 4 dec layers, d 1280, 20x64 heads, FFN 5120, "
+                               "128 mels, 1500 frames, V 51866), fp16 random weights ~N(0,0.02); mel 128x3000 ~N(0,1); "
+                               "4-token prompt, 224 greedy tokens; step = encode + decode of one 30 s window",
+                   "streams_per_gpu": 1, "l2": "decoder weights 316 MB + cross K/V 31 MB per step > 126 MB L2"},
+        "step_us": round(step_us, 2),
+        "encode_ms": round(sum(enc_ms) / args.steps, 3),
+        "encoder_tflops": round(enc_tflops, 1),
+        "e2e": {"value": round(tokens / wall_s, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": c.n_mels * 2 * c.n_audio * 4, "d2h_bytes_per_step": WHISPER_TOKENS * 4,
+                "includes": "host mel -> device, encoder, cross K/V, prefill, 224 steps, token read-back"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 3), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": f"decoder step ({sbytes / 1e6:.1f} MB algorithmic: weights, vocabulary, cross and self "
+                               f"K/V) / measured step time"},
+        "clocks": clk.summary(),
+        "gpu_launches": args.steps * (WHISPER_TOKENS * (2 + 12 * c.dec_layers + 4)
+                                      + 4 + c.enc_layers * 8 + c.dec_layers),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        # config 1 (Whisper-tiny shapes, int4 decoder) on both sides
+        t = VW.Whisper(VW.TINY, local)
+        t.init_random(3, 0.02)
+        tmel = np.random.default_rng(4).standard_normal((VW.TINY.n_mels, 2 * VW.TINY.n_audio)).astype(np.float32)
+        t.encode(tmel)
+        t.decode(WHISPER_PROMPT, 64)
+        r = t.decode(WHISPER_PROMPT, 64)
+        gpu_tiny = 64 / ((r.prefill_ms + r.decode_ms) / 1e3)
+        t.close()
+        cpu_tps, n = whisper_oracle_tokens_per_s()
+        line["cpu_baseline"] = {"value": round(cpu_tps, 2), "unit": "tokens/s", "cores": os.cpu_count(),
+                                "kind": "port",
+                                "sample": f"numpy oracle, Whisper-tiny shapes (config 1), int4 decoder: {n} greedy "
+                                          f"steps after the prompt, encoder not timed"}
+        line["config1_gpu_tokens_per_s"] = round(gpu_tiny, 1)
+    m.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return line
+
+
 def run_profile_pass(args):
     """A short run for an ncu launch list: the headline models, a 16-position prefix, the
     prefill and two draft-and-verify passes (one eager, one graph replay)."""
@@ -572,7 +742,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="spec", choices=["spec", "gemm"])
+    ap.add_argument("--workload", default="spec", choices=["spec", "gemm", "whisper"])
     ap.add_argument("--impl", default="vella", choices=["vella", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--shape", default="", help="gemm workload: one case 'bits,N,K,M' instead of the sweep")
@@ -587,7 +757,8 @@ def main():
         if rank == 0:
             print(json.dumps(run_reference(args, rank, world)))
         return
-    line = run_gemm(args, rank, world) if args.workload == "gemm" else run_spec(args, rank, world)
+    run = {"gemm": run_gemm, "whisper": run_whisper, "spec": run_spec}[args.workload]
+    line = run(args, rank, world)
     if rank == 0:
         print(json.dumps(line))
 
