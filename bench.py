@@ -30,6 +30,11 @@ sys.path.insert(0, ROOT)
 GEMM_SHAPES = [(5120, 5120), (1024, 5120), (25600, 5120), (5120, 25600), (151936, 5120)]
 GEMM_MS = [1, 2, 4, 5, 8, 9, 16]
 L2_BYTES = 126 * 2 ** 20
+# DRAM bytes per algorithmic byte of the small-M int4 GEMM, from one ncu capture of
+# qgemm_stream_kernel at M=5, N=25600, K=5120 (75.04 MB read+write for 74.04 MB algorithmic;
+# profiles/qgemm_stream_int4_25600x5120_m5.txt).  Traffic scales with the weights read, so the
+# verify pass's average launch is reported as its algorithmic bytes times this ratio.
+STREAM_TRAFFIC_RATIO = 75.04 / 74.04
 
 
 def peaks():
@@ -453,7 +458,10 @@ def run_spec(args, rank, world):
         "e2e": {"value": round(e2e_tokens * world / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "includes": "prefix H2D from pinned memory, prefill, decode, token D2H"},
         "roofline": {"bound": "hbm", "achieved": round(roof["gbs"], 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(roof["gbs"] / hbm, 3), "traffic": None, "peak_kind": peak_kind,
+                     "frac": round(roof["gbs"] / hbm, 3),
+                     "traffic": int(roof["bytes_per_pass"] / roof["launches"] * STREAM_TRAFFIC_RATIO),
+                     "traffic_unit": "bytes per launch (scaled from the M=5 25600x5120 ncu capture)",
+                     "peak_kind": peak_kind,
                      "kernel": f"qgemm int4 at M={k + 1}: the verify pass's {roof['launches']} GEMM launches "
                                f"({roof['bytes_per_pass'] / 1e9:.2f} GB algorithmic) replayed in a graph",
                      "verify_gemm_ms": round(roof["ms_per_pass"], 3)},
