@@ -162,6 +162,8 @@ typedef struct vella_model_cfg {
   int32_t max_prefix; /* capacity of the input-embedding prefix */
   float rms_eps;
   float rope_theta;
+  int32_t streams;    /* independent sequences held at once (0 or 1: one); each has its own KV
+                         cache [max_seq] and prefix buffer [max_prefix] */
 } vella_model_cfg;
 
 typedef struct vella_model vella_model;
@@ -248,6 +250,22 @@ VELLA_API int vella_spec_greedy_step(vella_spec* spec, int32_t* out_token);
  */
 VELLA_API int vella_spec_decode(vella_spec* spec, int32_t mode, int32_t max_tokens, int32_t* out_tokens, int32_t cap,
                                 int32_t* n_out, int32_t* flags);
+/*
+ * Several independent streams at once (models created with cfg.streams = S > 1; the single-
+ * stream calls above then return VELLA_E_UNSUPPORTED).  vella_spec_set_prefix takes the
+ * embeddings stream-major [S][T][d], vella_spec_set_reference the continuations [S][n].
+ * Every pass runs the draft steps and the verify of all S streams as one batch (verify rows
+ * S * (K + 1)); each stream accepts on its own and stops advancing once it has max_tokens
+ * tokens.  out_tokens [S][max_tokens] receives each stream's first max_tokens tokens (no EOS
+ * or loop stop: the caller applies its own rules per stream); n_out[S] = max_tokens.
+ * mode: VELLA_DECODE_SPEC or VELLA_DECODE_GREEDY (one batched greedy step per token).
+ * Batching changes which GEMM path a row takes (at most 16 rows: the small-M kernels; above:
+ * tensor cores), so SPEC and GREEDY give bit-identical tokens when their batches fall on the
+ * same side (S * (K + 1) <= 16, or S > 16), and a stream's tokens can differ in rounding from
+ * a single-stream decode of the same prefix.
+ */
+VELLA_API int vella_spec_decode_batch(vella_spec* spec, int32_t mode, int32_t max_tokens, int32_t* out_tokens,
+                                      int32_t* n_out);
 VELLA_API int vella_spec_get_stats(const vella_spec* spec, vella_spec_stats* out);
 /* Test hook mirroring VELLA_TEST_OPTIMIZED_FAULT (NemotronTranscribeModel.swift:398-399). */
 VELLA_API int vella_spec_set_fault(vella_spec* spec, int32_t fault);

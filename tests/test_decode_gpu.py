@@ -294,3 +294,60 @@ def test_device_quantizer_matches_oracle_bitwise(bits, dtype):
         assert np.array_equal(bi.cpu().view(torch.int16).numpy().view(np.uint16), b)
     else:
         assert np.array_equal(sc.cpu().numpy(), s) and np.array_equal(bi.cpu().numpy(), b)
+
+
+def _batch_models(S, max_seq=160):
+    t, tc = make(bits=4, seed=31, max_seq=max_seq)
+    d, dc = make(n_layers=1, d=128, H=2, KV=1, ffn=256, bits=0, seed=32, max_seq=max_seq)
+    from vella_b200 import decode as VD
+    tb = VD.Model(VD.ModelConfig(2, 256, 4, 2, 64, 512, 1000, bits=4, max_seq=max_seq, max_prefix=128, streams=S))
+    tb.init_random(31, 0.02)
+    db = VD.Model(VD.ModelConfig(1, 128, 2, 1, 64, 256, 1000, bits=0, max_seq=max_seq, max_prefix=128, streams=S))
+    db.init_random(32, 0.05)
+    return t, d, tb, db
+
+
+def test_batched_greedy_equals_single_stream_greedy():
+    """Three streams decoded as one batch (3 rows, small-M kernels) give each stream exactly
+    the tokens of its own single-stream greedy decode."""
+    from vella_b200 import decode as VD
+    S, P, n = 3, 24, 32
+    t, d, tb, db = _batch_models(S)
+    pre_t = np.stack([prefix_of(P, 256, 40 + j) for j in range(S)])
+    pre_d = np.stack([prefix_of(P, 128, 50 + j) for j in range(S)])
+    sb = VD.SpecDecoder(tb, db, k=4)
+    sb.set_prefix(pre_t, pre_d)
+    batch = sb.decode_batch(n, VD.DECODE_GREEDY)
+    for j in range(S):
+        single, sd = greedy_tokens(t, d, P, pre_t[j], pre_d[j], n)
+        sd.close()
+        assert list(batch[j]) == single, j
+    sb.close()
+    for m in (t, d, tb, db):
+        m.close()
+
+
+@pytest.mark.parametrize("S,k", [(3, 4), (20, 3)])
+def test_batched_spec_equals_batched_greedy(S, k):
+    """Draft-and-verify over S streams in one batch emits each stream's greedy tokens bit for
+    bit; S=3, K=4 keeps every GEMM on the small-M kernels (15 verify rows), S=20 puts the
+    greedy step (20 rows) and the verify (80 rows) on the tensor cores."""
+    from vella_b200 import decode as VD
+    P, n = 20, 40
+    _, _, tb, db = _batch_models(S)
+    pre_t = np.stack([prefix_of(P, 256, 60 + j) for j in range(S)])
+    pre_d = np.stack([prefix_of(P, 128, 70 + j) for j in range(S)])
+    sb = VD.SpecDecoder(tb, db, k=k)
+    sb.set_prefix(pre_t, pre_d)
+    greedy = sb.decode_batch(n, VD.DECODE_GREEDY)
+    spec = sb.decode_batch(n, VD.DECODE_SPEC)
+    assert np.array_equal(spec, greedy)
+    # oracle draft over the batch: same tokens, acceptance follows the oracle rate
+    so = VD.SpecDecoder(tb, db, k=k, mode=VD.DRAFT_ORACLE, oracle_p=0.9, seed=5)
+    so.set_prefix(pre_t, pre_d)
+    so.set_reference(greedy)
+    assert np.array_equal(so.decode_batch(n, VD.DECODE_SPEC), greedy)
+    st = so.stats()
+    assert st["passes"] > 0 and sum(st["accepted"][1:]) > sum(st["accepted"][:1])
+    for x in (sb, so, tb, db):
+        x.close()

@@ -43,18 +43,19 @@ __device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
 // ---------------------------------------------------------------------------------------
 template <typename T>
 __global__ void embed_rows_kernel(T* __restrict__ h, const T* __restrict__ table, const T* __restrict__ prefix,
-                                  const int* __restrict__ tok, PosRef pr, const int* __restrict__ Pdev, int d,
-                                  int vocab, int max_seq, int* err) {
+                                  long long prefix_ss, const int* __restrict__ tok, int tok_ss, PosRef pr,
+                                  const int* __restrict__ Pdev, int d, int vocab, int max_seq, int* err) {
   pdl_wait();
   pdl_launch_next();
   const int m = blockIdx.x;
-  const int pos = *pr.base + pr.off + m;
-  const int P = *Pdev;
+  const int sidx = pr.stream_of(m);
+  const int pos = pr.pos(m);
+  const int P = Pdev[sidx * pr.stride];
   const T* src;
   if (pos >= 0 && pos < P) {
-    src = prefix + (size_t)pos * d;
+    src = prefix + (size_t)sidx * prefix_ss + (size_t)pos * d;
   } else {
-    int t = (pos >= 0 && pos < max_seq) ? tok[pos] : -1;
+    int t = (pos >= 0 && pos < max_seq) ? tok[(size_t)sidx * tok_ss + pos] : -1;
     if (t < 0 || t >= vocab) {
       if (threadIdx.x == 0) atomicOr(err, 1);
       t = 0;
@@ -71,12 +72,13 @@ __global__ void embed_rows_kernel(T* __restrict__ h, const T* __restrict__ table
 // ---------------------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(T* __restrict__ out, const T* __restrict__ x,
-                                                      const T* __restrict__ w, int d, float eps) {
+                                                      const T* __restrict__ w, int d, float eps, int group, int tail) {
   using A = Act<T>;
   pdl_wait();
   pdl_launch_next();
   const int row = blockIdx.x;
-  const T* xr = x + (size_t)row * d;
+  const int src = (row / tail) * group + group - tail + row % tail;
+  const T* xr = x + (size_t)src * d;
   float ss = 0.0f;
   for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
     float v[8];
@@ -121,13 +123,14 @@ template <typename T>
 __global__ void rope_append_kernel(const T* __restrict__ qkv, T* __restrict__ q_out, T* __restrict__ kc,
                                    T* __restrict__ vc, const float2* __restrict__ cs, const T* __restrict__ qn,
                                    const T* __restrict__ kn, float eps, PosRef pr, int H, int KV, int hd,
-                                   int max_seq, int* err) {
+                                   int max_seq, int* err, long long kv_ss) {
   using A = Act<T>;
   pdl_wait();
   pdl_launch_next();
   const int m = blockIdx.x, hidx = blockIdx.y, i = threadIdx.x;
   const int half = hd / 2;
-  const int pos = *pr.base + pr.off + m;
+  const int pos = pr.pos(m);
+  const size_t sbase = (size_t)pr.stream_of(m) * kv_ss;
   if (pos < 0 || pos >= max_seq) {
     if (i == 0) atomicOr(err, 2);
     return;
@@ -157,11 +160,11 @@ __global__ void rope_append_kernel(const T* __restrict__ qkv, T* __restrict__ q_
     o[i + half] = A::from_f(y2);
   } else {
     const int kv = hidx - H;
-    T* ko = kc + ((size_t)kv * max_seq + pos) * hd;
+    T* ko = kc + sbase + ((size_t)kv * max_seq + pos) * hd;
     ko[i] = A::from_f(y1);
     ko[i + half] = A::from_f(y2);
     const T* vs = row + (size_t)(H + KV + kv) * hd;
-    T* vo = vc + ((size_t)kv * max_seq + pos) * hd;
+    T* vo = vc + sbase + ((size_t)kv * max_seq + pos) * hd;
     vo[i] = vs[i];
     vo[i + half] = vs[i + half];
   }
@@ -215,7 +218,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
   pdl_launch_next();
-  const int pos0 = a.causal ? *a.pr.base + a.pr.off : 0;
+  const int pos0 = a.causal ? a.pr.base[bz * a.pr.stride] + a.pr.off : 0;
   const int mq0 = qb * QB;
   const int nq = min(QB, a.M - mq0);
   const int QR = nq * GQ;
@@ -485,31 +488,34 @@ int launch_attn_t(const AttnArgs& a, int batch, cudaStream_t s) {
 
 }  // namespace
 
-int launch_embed_rows_dev(int dtype, void* h, const void* table, const void* prefix, const int* tok, PosRef pr,
-                          int rows, const int* P, int d, int vocab, int max_seq, int* err, cudaStream_t s) {
+int launch_embed_rows_dev(int dtype, void* h, const void* table, const void* prefix, long long prefix_ss,
+                          const int* tok, int tok_ss, PosRef pr, int rows, const int* P, int d, int vocab, int max_seq,
+                          int* err, cudaStream_t s) {
   if (rows <= 0) return VELLA_OK;
   if (dtype == VELLA_BF16)
     return launch_kernel(embed_rows_kernel<__nv_bfloat16>, dim3(rows), dim3(256), 0, s, static_cast<__nv_bfloat16*>(h),
-                         static_cast<const __nv_bfloat16*>(table), static_cast<const __nv_bfloat16*>(prefix), tok, pr,
-                         P, d, vocab, max_seq, err);
+                         static_cast<const __nv_bfloat16*>(table), static_cast<const __nv_bfloat16*>(prefix), prefix_ss,
+                         tok, tok_ss, pr, P, d, vocab, max_seq, err);
   return launch_kernel(embed_rows_kernel<__half>, dim3(rows), dim3(256), 0, s, static_cast<__half*>(h),
-                       static_cast<const __half*>(table), static_cast<const __half*>(prefix), tok, pr, P, d, vocab,
-                       max_seq, err);
+                       static_cast<const __half*>(table), static_cast<const __half*>(prefix), prefix_ss, tok, tok_ss,
+                       pr, P, d, vocab, max_seq, err);
 }
 
 int launch_rmsnorm(int dtype, void* out, const void* x, const void* w, int rows, int d, float eps,
-                   cudaStream_t s) {
+                   cudaStream_t s, int group, int tail) {
   if (rows <= 0) return VELLA_OK;
+  if (group <= 0 || tail <= 0) group = tail = rows;
+  if (tail > group) return fail(VELLA_E_INVALID, "rmsnorm: tail %d of groups of %d rows", tail, group);
   if (dtype == VELLA_BF16)
     return launch_kernel(rmsnorm_kernel<__nv_bfloat16>, dim3(rows), dim3(256), 0, s, static_cast<__nv_bfloat16*>(out),
-                         static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), d, eps);
+                         static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), d, eps, group, tail);
   return launch_kernel(rmsnorm_kernel<__half>, dim3(rows), dim3(256), 0, s, static_cast<__half*>(out),
-                       static_cast<const __half*>(x), static_cast<const __half*>(w), d, eps);
+                       static_cast<const __half*>(x), static_cast<const __half*>(w), d, eps, group, tail);
 }
 
 int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* vc, const float2* cs,
                        const void* qn, const void* kn, float eps, PosRef pr, int rows, int H, int KV, int hd,
-                       int max_seq, int* err, cudaStream_t s) {
+                       int max_seq, int* err, cudaStream_t s, long long kv_ss) {
   if (rows <= 0) return VELLA_OK;
   const dim3 grid(rows, H + KV);
   if (dtype == VELLA_BF16)
@@ -517,11 +523,11 @@ int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* 
                          static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(q_out),
                          static_cast<__nv_bfloat16*>(kc), static_cast<__nv_bfloat16*>(vc), cs,
                          static_cast<const __nv_bfloat16*>(qn), static_cast<const __nv_bfloat16*>(kn), eps, pr, H, KV,
-                         hd, max_seq, err);
+                         hd, max_seq, err, kv_ss);
   return launch_kernel(rope_append_kernel<__half>, grid, dim3(hd / 2), 0, s, static_cast<const __half*>(qkv),
                        static_cast<__half*>(q_out), static_cast<__half*>(kc), static_cast<__half*>(vc), cs,
                        static_cast<const __half*>(qn), static_cast<const __half*>(kn), eps, pr, H, KV, hd, max_seq,
-                       err);
+                       err, kv_ss);
 }
 
 int launch_attention_ex(int dtype, const AttnView& v, int batch, PosRef pr, int causal, int rows, int H, int KV,

@@ -8,11 +8,17 @@
 
 namespace vella {
 
-// Position of row 0 of a launch = *base + off (device scalar, so captured graphs can be
-// replayed while the sequence grows).
+// Positions of the rows of a launch, read from device scalars so that captured graphs can
+// be replayed while the sequences grow.  One stream (group == 0): row m sits at position
+// *base + off + m.  Several streams in one launch (group = rows per stream): row m belongs
+// to stream m / group and sits at base[(m / group) * stride] + off + m % group.
 struct PosRef {
   const int* base;
   int off;
+  int group = 0;
+  int stride = 0;
+  __host__ __device__ int stream_of(int m) const { return group ? m / group : 0; }
+  __device__ int pos(int m) const { return group ? base[(m / group) * stride] + off + m % group : *base + off + m; }
 };
 
 constexpr int kAttnChunk = 64;   // keys per chunk (absolute-position aligned)
@@ -34,15 +40,20 @@ struct AttnView {
 };
 
 // dtype: 0 = bf16, 1 = fp16 everywhere below.
-// Row m holds position p = *pr.base + pr.off + m: the caller's input embedding p when
-// p < *P (device scalar), else the token table row tok[p].
-int launch_embed_rows_dev(int dtype, void* h, const void* table, const void* prefix, const int* tok, PosRef pr,
-                          int rows, const int* P, int d, int vocab, int max_seq, int* err, cudaStream_t s);
+// Row m of stream s = pr.stream_of(m) holds position p = pr.pos(m): the stream's input
+// embedding p (prefix + s * prefix_ss) when p < P[s * pr.stride], else the token table row
+// of tok[s * tok_ss + p].
+int launch_embed_rows_dev(int dtype, void* h, const void* table, const void* prefix, long long prefix_ss,
+                          const int* tok, int tok_ss, PosRef pr, int rows, const int* P, int d, int vocab, int max_seq,
+                          int* err, cudaStream_t s);
+// out row i = RMSNorm(x row src(i)), src(i) = (i / tail) * group + group - tail + i % tail:
+// the last `tail` rows of every `group` rows (group == tail: every row).
 int launch_rmsnorm(int dtype, void* out, const void* x, const void* w, int rows, int d, float eps,
-                   cudaStream_t s);
+                   cudaStream_t s, int group = 0, int tail = 0);
+// RoPE of q/k and K/V append; stream s's cache starts kv_ss elements after stream 0's.
 int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* vc, const float2* cs,
                        const void* qn, const void* kn, float eps, PosRef pr, int rows, int H, int KV, int hd,
-                       int max_seq, int* err, cudaStream_t s);
+                       int max_seq, int* err, cudaStream_t s, long long kv_ss = 0);
 int launch_attention(int dtype, const void* q, const void* kc, const void* vc, void* out, PosRef pr, int rows,
                      int H, int KV, int hd, int max_seq, float scale, cudaStream_t s);
 // General form: causal (query at position *pr.base + pr.off + m sees keys 0..that) or not

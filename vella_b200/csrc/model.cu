@@ -244,11 +244,13 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
   if (c.d_model % 64 || c.ffn % 64 || (c.n_heads * c.head_dim) % 64)
     return fail(VELLA_E_UNSUPPORTED, "vella_model_create: d_model, ffn and n_heads*head_dim must be multiples of 64");
   if (c.max_prefix > c.max_seq) return fail(VELLA_E_INVALID, "vella_model_create: max_prefix > max_seq");
+  if (c.streams < 0 || c.streams > 4096) return fail(VELLA_E_INVALID, "vella_model_create: streams %d", c.streams);
   VELLA_CUDA_TRY(cudaSetDevice(device));
   Model* m = new Model();
   m->cfg = c;
   m->device = device;
   m->elt = 2;
+  m->streams = std::max(1, c.streams);
   const int d = c.d_model, hd = c.head_dim, H = c.n_heads, KV = c.n_kv_heads, bits = c.bits, e = m->elt;
   // ---- weights arena ------------------------------------------------------------------
   size_t off = 0;
@@ -289,7 +291,10 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
     for (QWeight* q : {&L.qkv, &L.o, &L.gate, &L.up, &L.down}) rebase_q(*q, base, bits != 0);
   }
   // ---- KV cache, prefix, rope table -----------------------------------------------------
-  m->kv_bytes = (size_t)c.n_layers * 2 * KV * c.max_seq * hd * e;
+  m->kv_ss = (long long)c.n_layers * 2 * KV * c.max_seq * hd;
+  m->kv_bytes = (size_t)m->streams * m->kv_ss * e;
+  m->prefix_ss = (long long)std::max(c.max_prefix, 1) * d;
+  m->max_rows = std::max(kChunkRows, m->streams * kMaxRows);
   // ---- activations and scratch ------------------------------------------------------------
   size_t ws = 0;
   for (const Layer& L : m->layers) {
@@ -301,10 +306,10 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
   }
   ws = std::max(ws, gemm_ws_for(m->lm_head, bits, c.dtype, VELLA_EPI_NONE));
   m->gemm_ws_bytes = ws;
-  const size_t R = kChunkRows, RL = kMaxRows;
+  const size_t R = m->max_rows, RL = (size_t)m->streams * kMaxRows;
   const size_t sizes[] = {
       m->kv_bytes,                                  // 0 kv
-      (size_t)std::max(c.max_prefix, 1) * d * e,   // 1 prefix
+      (size_t)m->streams * m->prefix_ss * e,        // 1 prefix
       (size_t)c.max_seq * (hd / 2) * sizeof(float2),// 2 rope
       R * d * e, R * d * e,                         // 3 h, 4 xn
       R * m->qkv_n() * e,                           // 5 qkv
@@ -314,7 +319,7 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
       RL * sizeof(int),                             // 10 ys
       ws,                                           // 11 gemm workspace
       0,                                            // 12 (unused)
-      argmax_scratch_bytes(kMaxRows) + 512,         // 13 argmax scratch
+      argmax_scratch_bytes((int)RL) + 512,          // 13 argmax scratch
       4 * sizeof(int),                              // 14 flags
       (size_t)c.max_seq * sizeof(int),              // 15 scoring token ids
   };
@@ -446,36 +451,50 @@ int model_gemm(Model* m, const QWeight& w, const void* x, int rows, void* out, i
                       nullptr, residual, out, m->gemm_ws, s);
 }
 
-int model_forward(Model* m, PosRef pr, int rows, const int* tok, const int* P, int logits_rows, cudaStream_t s) {
+int model_forward(Model* m, PosRef pr, int rows, int streams, int stream0, const int* tok, int tok_ss, const int* P,
+                  int logits_rows, cudaStream_t s) {
   const vella_model_cfg& c = m->cfg;
-  if (rows <= 0 || rows > kChunkRows || logits_rows > std::min(rows, kMaxRows))
-    return fail(VELLA_E_INVALID, "forward: %d rows, %d logits rows", rows, logits_rows);
+  const int M = rows * streams;
+  if (rows <= 0 || streams <= 0 || stream0 < 0 || stream0 + streams > m->streams || M > m->max_rows ||
+      logits_rows > std::min(rows, kMaxRows) || logits_rows < 0)
+    return fail(VELLA_E_INVALID, "forward: %d rows x %d streams from %d, %d logits rows", rows, streams, stream0,
+                logits_rows);
   const int d = c.d_model, H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, dt = c.dtype;
   const float scale = 1.0f / std::sqrt((float)hd);
+  pr.group = streams > 1 ? rows : 0;
+  const size_t e = m->elt;
+  const char* prefix = static_cast<const char*>(m->prefix) + (size_t)stream0 * m->prefix_ss * e;
+  const size_t kv0 = (size_t)stream0 * m->kv_ss * e;
   int rc;
-  if ((rc = launch_embed_rows_dev(dt, m->h, m->embed, m->prefix, tok, pr, rows, P, d, c.vocab, c.max_seq, m->err, s)))
+  if ((rc = launch_embed_rows_dev(dt, m->h, m->embed, prefix, m->prefix_ss, tok, tok_ss, pr, M, P, d, c.vocab,
+                                  c.max_seq, m->err, s)))
     return rc;
   for (int l = 0; l < c.n_layers; ++l) {
     Layer& L = m->layers[l];
-    if ((rc = launch_rmsnorm(dt, m->xn, m->h, L.attn_norm, rows, d, c.rms_eps, s))) return rc;
-    if ((rc = model_gemm(m, L.qkv, m->xn, rows, m->qkv_out, VELLA_EPI_NONE, nullptr, nullptr, s))) return rc;
-    if ((rc = launch_rope_append(dt, m->qkv_out, m->q, m->kcache(l), m->vcache(l), m->rope, L.q_norm, L.k_norm,
-                                 c.rms_eps, pr, rows, H, KV, hd, c.max_seq, m->err, s)))
+    char* kc = static_cast<char*>(m->kcache(l)) + kv0;
+    char* vc = static_cast<char*>(m->vcache(l)) + kv0;
+    if ((rc = launch_rmsnorm(dt, m->xn, m->h, L.attn_norm, M, d, c.rms_eps, s))) return rc;
+    if ((rc = model_gemm(m, L.qkv, m->xn, M, m->qkv_out, VELLA_EPI_NONE, nullptr, nullptr, s))) return rc;
+    if ((rc = launch_rope_append(dt, m->qkv_out, m->q, kc, vc, m->rope, L.q_norm, L.k_norm, c.rms_eps, pr, M, H, KV, hd,
+                                 c.max_seq, m->err, s, m->kv_ss)))
       return rc;
-    if ((rc = launch_attention(dt, m->q, m->kcache(l), m->vcache(l), m->attn, pr, rows, H, KV, hd,
-                               c.max_seq, scale, s)))
-      return rc;
-    if ((rc = model_gemm(m, L.o, m->attn, rows, m->h, VELLA_EPI_RESIDUAL, m->h, nullptr, s))) return rc;
-    if ((rc = launch_rmsnorm(dt, m->xn, m->h, L.mlp_norm, rows, d, c.rms_eps, s))) return rc;
-    if ((rc = model_gemm(m, L.gate, m->xn, rows, m->mlp, VELLA_EPI_SILU_GATE, nullptr, &L.up, s))) return rc;
-    if ((rc = model_gemm(m, L.down, m->mlp, rows, m->h, VELLA_EPI_RESIDUAL, m->h, nullptr, s))) return rc;
+    AttnView v;
+    v.q = m->q; v.out = m->attn;
+    v.q_rs = v.o_rs = (long long)H * hd;
+    v.q_bs = v.o_bs = (long long)rows * H * hd;
+    v.k = kc; v.v = vc;
+    v.kv_hs = (long long)c.max_seq * hd; v.kv_rs = hd; v.kv_bs = m->kv_ss;
+    if ((rc = launch_attention_ex(dt, v, streams, pr, 1, rows, H, KV, hd, c.max_seq, scale, s))) return rc;
+    if ((rc = model_gemm(m, L.o, m->attn, M, m->h, VELLA_EPI_RESIDUAL, m->h, nullptr, s))) return rc;
+    if ((rc = launch_rmsnorm(dt, m->xn, m->h, L.mlp_norm, M, d, c.rms_eps, s))) return rc;
+    if ((rc = model_gemm(m, L.gate, m->xn, M, m->mlp, VELLA_EPI_SILU_GATE, nullptr, &L.up, s))) return rc;
+    if ((rc = model_gemm(m, L.down, m->mlp, M, m->h, VELLA_EPI_RESIDUAL, m->h, nullptr, s))) return rc;
   }
   if (logits_rows > 0) {
-    const int r0 = rows - logits_rows;
-    char* hrow = static_cast<char*>(m->h) + (size_t)r0 * d * m->elt;
-    if ((rc = launch_rmsnorm(dt, m->xn, hrow, m->final_norm, logits_rows, d, c.rms_eps, s))) return rc;
-    if ((rc = model_gemm(m, m->lm_head, m->xn, logits_rows, m->logits, VELLA_EPI_NONE, nullptr, nullptr, s))) return rc;
-    if ((rc = launch_argmax(dt, m->logits, logits_rows, c.vocab, (size_t)c.vocab, m->ys, m->argmax_sc, m->nonfinite, s)))
+    const int LR = logits_rows * streams;  // the last logits_rows rows of every stream, stream-major
+    if ((rc = launch_rmsnorm(dt, m->xn, m->h, m->final_norm, LR, d, c.rms_eps, s, rows, logits_rows))) return rc;
+    if ((rc = model_gemm(m, m->lm_head, m->xn, LR, m->logits, VELLA_EPI_NONE, nullptr, nullptr, s))) return rc;
+    if ((rc = launch_argmax(dt, m->logits, LR, c.vocab, (size_t)c.vocab, m->ys, m->argmax_sc, m->nonfinite, s)))
       return rc;
   }
   return VELLA_OK;

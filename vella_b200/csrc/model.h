@@ -43,16 +43,20 @@ struct Model {
   void* final_norm = nullptr;  // [d]
   QWeight lm_head;             // [V, d]
   std::vector<Layer> layers;
-  // per-sequence state
-  void* kv = nullptr;  // [L][2][KV][S][hd]
+  // per-sequence state (streams = max(1, cfg.streams) independent sequences)
+  int streams = 1;
+  void* kv = nullptr;  // [streams][L][2][KV][max_seq][hd]
   size_t kv_bytes = 0;
-  void* prefix = nullptr;  // [max_prefix][d]
+  long long kv_ss = 0;      // elements between consecutive streams' caches
+  void* prefix = nullptr;  // [streams][max_prefix][d]
+  long long prefix_ss = 0;  // elements between consecutive streams' prefixes
+  int max_rows = 0;         // rows of the activation buffers (max(kChunkRows, streams * kMaxRows))
   float2* rope = nullptr;  // [S][hd/2] (cos, sin)
   // activations and scratch
   void* act_arena = nullptr;
   void *h = nullptr, *xn = nullptr, *qkv_out = nullptr, *q = nullptr, *attn = nullptr, *mlp = nullptr;
-  void* logits = nullptr;  // [kMaxRows, V]
-  int* ys = nullptr;       // [kMaxRows]
+  void* logits = nullptr;  // [streams * kMaxRows, V]
+  int* ys = nullptr;       // [streams * kMaxRows]
   void* gemm_ws = nullptr;
   size_t gemm_ws_bytes = 0;
   void* argmax_sc = nullptr;
@@ -78,11 +82,15 @@ void model_destroy(Model* m);
 int model_init_random(Model* m, uint64_t seed, float std, cudaStream_t s);
 int model_tensor(Model* m, const std::string& name, int layer, void** ptr, size_t* bytes);
 
-// Runs `rows` (<= kMaxRows) positions starting at *pr.base + pr.off through every layer,
-// appending their K/V.  Token ids come from tok[pos] (pos >= *P) or the prefix embeddings
-// (pos < *P).  When logits_rows > 0 the last `logits_rows` rows go through the final norm
-// and the LM head into m->logits[0..logits_rows) and their argmax into m->ys.
-int model_forward(Model* m, PosRef pr, int rows, const int* tok, const int* P, int logits_rows, cudaStream_t s);
+// Runs `rows` positions of each of `streams` streams (stream0, stream0 + 1, ...) through every
+// layer in one batch of rows * streams rows, appending their K/V to each stream's cache.
+// Stream j's rows start at pr.base[j * pr.stride] + pr.off (pr.base, tok and P point at
+// stream0's values; tok advances tok_ss ints per stream, P pr.stride ints).  Token ids come
+// from tok (pos >= P) or the stream's prefix embeddings (pos < P).  When logits_rows > 0 the
+// last `logits_rows` rows of every stream go through the final norm and the LM head into
+// m->logits (stream-major) and their argmax into m->ys.
+int model_forward(Model* m, PosRef pr, int rows, int streams, int stream0, const int* tok, int tok_ss, const int* P,
+                  int logits_rows, cudaStream_t s);
 
 // GEMM with the model's workspace.
 int model_gemm(Model* m, const QWeight& w, const void* x, int rows, void* out, int epilogue, const void* residual,

@@ -39,14 +39,20 @@ struct DevState {
   int L;          // committed positions (prefix + emitted tokens)
   int P;          // prefix length
   int pass;       // passes run since the prefill (Philox counter of the oracle draft)
-  int n_new;      // tokens committed by the last pass / step
+  int n_new;      // tokens committed by the last pass / step (0: the stream is done)
   int nonfinite;  // the last verify logits held NaN/Inf
   int err;        // bit 0 bad token id, bit 1 bad position, bit 2 capacity
   int ref_len;    // length of the oracle reference
+  int produced;   // tokens committed since the prefill (its first token included)
+  int quota;      // stop advancing once produced >= quota (0: no limit)
   int newtok[16];
 };
+constexpr int kStateInts = sizeof(DevState) / sizeof(int);  // PosRef stride between streams
 
-__global__ void prefill_finish_kernel(DevState* st, int* tok, const int* ys, int* nf, const int* err_t,
+__device__ __forceinline__ bool done(const DevState& x) { return x.quota > 0 && x.produced >= x.quota; }
+
+// One stream: st, tok and the logits rows of that stream's prefill forward.
+__global__ void prefill_finish_kernel(DevState* st, int* tok, const int* ys, const int* nf, const int* err_t,
                                       int max_seq) {
   pdl_wait();
   pdl_launch_next();
@@ -56,59 +62,78 @@ __global__ void prefill_finish_kernel(DevState* st, int* tok, const int* ys, int
   st->n_new = 1;
   st->newtok[0] = t;
   st->pass = 0;
+  st->produced = 1;
   st->nonfinite = *nf;
   st->err |= *err_t;
-  *nf = 0;
 }
 
-__global__ void greedy_commit_kernel(DevState* st, int* tok, const int* ys, int* nf, const int* err_t, int max_seq) {
+// Stream blockIdx.x: commit the argmax of its one verify row.
+__global__ void greedy_commit_kernel(DevState* st, int* tok, const int* ys, const int* nf, const int* err_t,
+                                     int max_seq) {
   pdl_wait();
   pdl_launch_next();
-  const int L = st->L, t = ys[0];
-  if (L < max_seq) tok[L] = t; else st->err |= 4;
-  st->L = L + 1;
-  st->n_new = 1;
-  st->newtok[0] = t;
-  st->nonfinite = *nf;
-  st->err |= *err_t;
-  *nf = 0;
+  const int s = blockIdx.x;
+  DevState& x = st[s];
+  x.nonfinite = *nf;
+  x.err |= *err_t;
+  if (done(x)) {
+    x.n_new = 0;
+    return;
+  }
+  int* tk = tok + (size_t)s * max_seq;
+  const int L = x.L, t = ys[s];
+  if (L < max_seq) tk[L] = t; else x.err |= 4;
+  x.L = L + 1;
+  x.n_new = 1;
+  x.newtok[0] = t;
+  x.produced += 1;
 }
 
-// Draft step i proposes the token at position L + i.
-__global__ void propose_kernel(DevState* st, int* tok, const int* ys_draft, int* nf_draft, int i, int mode, float p,
-                               uint64_t seed, const int* ref, int vocab, int max_seq) {
+// Draft step i of stream blockIdx.x proposes the token at position L + i.
+__global__ void propose_kernel(DevState* st, int* tok, const int* ys_draft, int i, int mode, float p, uint64_t seed,
+                               const int* ref, int vocab, int max_seq) {
   pdl_wait();
   pdl_launch_next();
-  const int pos = st->L + i;
-  int t = ys_draft[0];
+  const int s = blockIdx.x;
+  const DevState& x = st[s];
+  const int pos = x.L + i;
+  int t = ys_draft[s];
   if (mode == VELLA_DRAFT_ORACLE) {
-    const U4 r = philox4x32_10(U4{(uint32_t)st->pass, (uint32_t)i, 0x0D4A7u, 0u}, (uint32_t)seed,
+    const U4 r = philox4x32_10(U4{(uint32_t)x.pass, (uint32_t)i, 0x0D4A7u, (uint32_t)s}, (uint32_t)seed,
                                (uint32_t)(seed >> 32));
-    const int ri = pos - st->P;
-    if (u01(r.x) < p && ri >= 0 && ri < st->ref_len) t = ref[ri];
+    const int ri = pos - x.P;
+    if (u01(r.x) < p && ri >= 0 && ri < x.ref_len) t = ref[(size_t)s * max_seq + ri];
     else t = min((int)(u01(r.y) * (float)vocab), vocab - 1);
   }
-  if (pos < max_seq) tok[pos] = t; else st->err |= 4;
-  *nf_draft = 0;  // the draft's own logits never gate acceptance
+  if (pos < max_seq) tok[(size_t)s * max_seq + pos] = t;
 }
 
-// Greedy acceptance over the verify argmax ys[0..K] (ys[j] predicts position L + j).
-__global__ void accept_kernel(DevState* st, int* tok, const int* ys, int K, int* nf, const int* err_t,
+// Greedy acceptance of stream blockIdx.x over its verify argmax ys[s(K+1) .. s(K+1)+K]
+// (ys[j] predicts position L + j).
+__global__ void accept_kernel(DevState* st, int* tok, const int* ys, int K, const int* nf, const int* err_t,
                               const int* err_d, int max_seq) {
   pdl_wait();
   pdl_launch_next();
-  const int L = st->L;
+  const int s = blockIdx.x;
+  DevState& x = st[s];
+  x.nonfinite = *nf;
+  x.err |= *err_t | *err_d;
+  if (done(x)) {
+    x.n_new = 0;
+    return;
+  }
+  int* tk = tok + (size_t)s * max_seq;
+  const int* y = ys + (size_t)s * (K + 1);
+  const int L = x.L;
   int a = 0;
-  while (a < K && ys[a] == tok[L + a]) ++a;
-  const int bonus = ys[a];
-  if (L + a < max_seq) tok[L + a] = bonus; else st->err |= 4;
-  for (int j = 0; j <= a; ++j) st->newtok[j] = tok[L + j];
-  st->n_new = a + 1;
-  st->L = L + a + 1;
-  st->pass += 1;
-  st->nonfinite = *nf;
-  st->err |= *err_t | *err_d;
-  *nf = 0;
+  while (a < K && y[a] == tk[L + a]) ++a;
+  const int bonus = y[a];
+  if (L + a < max_seq) tk[L + a] = bonus; else x.err |= 4;
+  for (int j = 0; j <= a; ++j) x.newtok[j] = tk[L + j];
+  x.n_new = a + 1;
+  x.L = L + a + 1;
+  x.pass += 1;
+  x.produced += a + 1;
 }
 
 }  // namespace
@@ -119,11 +144,13 @@ struct Spec {
   vella_spec_cfg cfg{};
   int device = 0;
   int max_seq = 0;
+  int streams = 1;
   cudaStream_t stream = nullptr;
-  DevState* dstate = nullptr;
-  DevState* hstate = nullptr;  // pinned
-  int* tok = nullptr;          // [max_seq]
-  int* ref = nullptr;          // [max_seq]
+  DevState* dstate = nullptr;  // [streams]
+  DevState* hstate = nullptr;  // [streams], pinned
+  int* tok = nullptr;          // [streams][max_seq]
+  int* ref = nullptr;          // [streams][max_seq]
+  int ref_len = 0;
   int P = 0;
   cudaGraphExec_t pass_exec = nullptr;
   cudaGraphExec_t greedy_exec = nullptr;
@@ -147,37 +174,53 @@ int pipeline_faults() {
 }
 
 int sync_state(Spec* s) {
-  VELLA_CUDA_TRY(cudaMemcpyAsync(s->hstate, s->dstate, sizeof(DevState), cudaMemcpyDeviceToHost, s->stream));
+  VELLA_CUDA_TRY(cudaMemcpyAsync(s->hstate, s->dstate, sizeof(DevState) * s->streams, cudaMemcpyDeviceToHost,
+                                 s->stream));
   VELLA_CUDA_TRY(cudaStreamSynchronize(s->stream));
-  if (s->hstate->err) return fail(VELLA_E_INVALID, "decode state error flags 0x%x (bad token id, position or capacity)", s->hstate->err);
+  for (int j = 0; j < s->streams; ++j)
+    if (s->hstate[j].err)
+      return fail(VELLA_E_INVALID, "decode state error flags 0x%x in stream %d (bad token id, position or capacity)",
+                  s->hstate[j].err, j);
   return VELLA_OK;
 }
+
+PosRef state_pos(Spec* s, int off) { return PosRef{&s->dstate[0].L, off, 0, kStateInts}; }
 
 int enqueue_pass(Spec* s) {
   Model* t = s->target;
   Model* d = s->draft;
-  const int K = s->cfg.draft_k;
-  const int* Lp = &s->dstate->L;
-  const int* Pp = &s->dstate->P;
+  const int K = s->cfg.draft_k, S = s->streams;
+  const int* Pp = &s->dstate[0].P;
   int rc;
   for (int i = 0; i < K; ++i) {
-    const PosRef pr{Lp, i == 0 ? -2 : i - 1};
-    if ((rc = model_forward(d, pr, i == 0 ? 2 : 1, s->tok, Pp, 1, s->stream))) return rc;
-    if ((rc = launch_kernel(propose_kernel, dim3(1), dim3(1), 0, s->stream, s->dstate, s->tok, d->ys, d->nonfinite,
-                            i, s->cfg.draft_mode, s->cfg.oracle_p, s->cfg.seed, s->ref, t->cfg.vocab, s->max_seq)))
+    if ((rc = model_forward(d, state_pos(s, i == 0 ? -2 : i - 1), i == 0 ? 2 : 1, S, 0, s->tok, s->max_seq, Pp, 1,
+                            s->stream)))
+      return rc;
+    if ((rc = launch_kernel(propose_kernel, dim3(S), dim3(1), 0, s->stream, s->dstate, s->tok, (const int*)d->ys, i,
+                            s->cfg.draft_mode, s->cfg.oracle_p, s->cfg.seed, (const int*)s->ref, t->cfg.vocab,
+                            s->max_seq)))
       return rc;
   }
-  if ((rc = model_forward(t, PosRef{Lp, -1}, K + 1, s->tok, Pp, K + 1, s->stream))) return rc;
-  return launch_kernel(accept_kernel, dim3(1), dim3(1), 0, s->stream, s->dstate, s->tok, t->ys, K, t->nonfinite,
-                       t->err, d->err, s->max_seq);
+  if ((rc = model_forward(t, state_pos(s, -1), K + 1, S, 0, s->tok, s->max_seq, Pp, K + 1, s->stream))) return rc;
+  if ((rc = launch_kernel(accept_kernel, dim3(S), dim3(1), 0, s->stream, s->dstate, s->tok, (const int*)t->ys, K,
+                          (const int*)t->nonfinite, (const int*)t->err, (const int*)d->err, s->max_seq)))
+    return rc;
+  // the draft's own logits never gate acceptance; the verify flag was copied into the states
+  VELLA_CUDA_TRY(cudaMemsetAsync(d->nonfinite, 0, sizeof(int), s->stream));
+  VELLA_CUDA_TRY(cudaMemsetAsync(t->nonfinite, 0, sizeof(int), s->stream));
+  return VELLA_OK;
 }
 
 int enqueue_greedy(Spec* s) {
   Model* t = s->target;
   int rc;
-  if ((rc = model_forward(t, PosRef{&s->dstate->L, -1}, 1, s->tok, &s->dstate->P, 1, s->stream))) return rc;
-  return launch_kernel(greedy_commit_kernel, dim3(1), dim3(1), 0, s->stream, s->dstate, s->tok, t->ys, t->nonfinite,
-                       t->err, s->max_seq);
+  if ((rc = model_forward(t, state_pos(s, -1), 1, s->streams, 0, s->tok, s->max_seq, &s->dstate[0].P, 1, s->stream)))
+    return rc;
+  if ((rc = launch_kernel(greedy_commit_kernel, dim3(s->streams), dim3(1), 0, s->stream, s->dstate, s->tok,
+                          (const int*)t->ys, (const int*)t->nonfinite, (const int*)t->err, s->max_seq)))
+    return rc;
+  VELLA_CUDA_TRY(cudaMemsetAsync(t->nonfinite, 0, sizeof(int), s->stream));
+  return VELLA_OK;
 }
 
 int capture(Spec* s, int (*enqueue)(Spec*), cudaGraphExec_t* exec) {
@@ -213,38 +256,53 @@ int run_unit(Spec* s, bool pass) {
   return sync_state(s);
 }
 
-int prefill(Spec* s, int* first) {
+// Prefill of every stream (one stream at a time), quota = 0 (no limit) or the batch quota.
+int prefill_all(Spec* s, int quota) {
   if (s->P < 1) return fail(VELLA_E_INVALID, "prefill: the prefix is empty (vella_spec_set_prefix)");
-  DevState init{};
-  init.P = s->P;
-  init.L = s->P;
-  init.ref_len = s->hstate->ref_len;
-  VELLA_CUDA_TRY(cudaMemcpyAsync(s->dstate, &init, sizeof(DevState), cudaMemcpyHostToDevice, s->stream));
-  const int* Pp = &s->dstate->P;
+  std::vector<DevState> init(s->streams);
+  for (DevState& x : init) {
+    std::memset(&x, 0, sizeof x);
+    x.P = x.L = s->P;
+    x.ref_len = s->ref_len;
+    x.quota = quota;
+  }
+  VELLA_CUDA_TRY(cudaMemcpyAsync(s->dstate, init.data(), sizeof(DevState) * s->streams, cudaMemcpyHostToDevice,
+                                 s->stream));
+  VELLA_CUDA_TRY(cudaStreamSynchronize(s->stream));
   int rc;
   // Chunks of up to kChunkRows positions (tensor-core GEMMs), except the last kMaxRows
   // positions, which run as one small-M forward: the draft's first pass recomputes position
   // P - 1 with the small-M kernels, and a draft that shares the target's weights then holds
   // the target's KV rows bit for bit.
   const int tail = std::min(s->P, kMaxRows);
-  auto run = [&](Model* m, bool logits) -> int {
-    int r;
-    for (int s0 = 0; s0 < s->P - tail; s0 += kChunkRows) {
-      const int rows = std::min(kChunkRows, s->P - tail - s0);
-      if ((r = model_forward(m, PosRef{m->dzero, s0}, rows, s->tok, Pp, 0, s->stream))) return r;
-    }
-    return model_forward(m, PosRef{m->dzero, s->P - tail}, tail, s->tok, Pp, logits ? 1 : 0, s->stream);
-  };
-  if (s->draft && (rc = run(s->draft, false))) return rc;
   Model* t = s->target;
-  if ((rc = run(t, true))) return rc;
-  if ((rc = launch_kernel(prefill_finish_kernel, dim3(1), dim3(1), 0, s->stream, s->dstate, s->tok, t->ys,
-                          t->nonfinite, t->err, s->max_seq)))
-    return rc;
+  for (int j = 0; j < s->streams; ++j) {
+    const int* Pp = &s->dstate[j].P;
+    int* tk = s->tok + (size_t)j * s->max_seq;
+    auto run = [&](Model* m, bool logits) -> int {
+      int r;
+      for (int s0 = 0; s0 < s->P - tail; s0 += kChunkRows) {
+        const int rows = std::min(kChunkRows, s->P - tail - s0);
+        if ((r = model_forward(m, PosRef{m->dzero, s0}, rows, 1, j, tk, 0, Pp, 0, s->stream))) return r;
+      }
+      return model_forward(m, PosRef{m->dzero, s->P - tail}, tail, 1, j, tk, 0, Pp, logits ? 1 : 0, s->stream);
+    };
+    if (s->draft && (rc = run(s->draft, false))) return rc;
+    if ((rc = run(t, true))) return rc;
+    if ((rc = launch_kernel(prefill_finish_kernel, dim3(1), dim3(1), 0, s->stream, &s->dstate[j], tk,
+                            (const int*)t->ys, (const int*)t->nonfinite, (const int*)t->err, s->max_seq)))
+      return rc;
+  }
+  VELLA_CUDA_TRY(cudaMemsetAsync(t->nonfinite, 0, sizeof(int), s->stream));
   VELLA_CUDA_TRY(cudaEventRecord(s->evp, s->stream));
   if ((rc = sync_state(s))) return rc;
-  if ((rc = pipeline_faults())) return rc;
-  *first = s->hstate->newtok[0];
+  return pipeline_faults();
+}
+
+int prefill(Spec* s, int* first) {
+  int rc;
+  if ((rc = prefill_all(s, 0))) return rc;
+  *first = s->hstate[0].newtok[0];
   return VELLA_OK;
 }
 
@@ -400,7 +458,8 @@ int vella_model_score(vella_model* m, const void* prefix, int32_t P, const int32
     const int rows = std::min(kMaxRows, last_pos + 1 - s0);
     const int first_scored = std::max(s0, P - 1);
     const int lr = s0 + rows - first_scored;  // rows with position >= P - 1
-    if ((rc = model_forward(m, PosRef{m->dzero, s0}, rows, m->score_tok, m->score_P, std::max(lr, 0), s))) return rc;
+    if ((rc = model_forward(m, PosRef{m->dzero, s0}, rows, 1, 0, m->score_tok, 0, m->score_P, std::max(lr, 0), s)))
+      return rc;
     if (lr > 0) {
       char* dst = static_cast<char*>(logits_out) + (size_t)(first_scored - (P - 1)) * lrow;
       VELLA_CUDA_TRY(cudaMemcpyAsync(dst, m->logits, (size_t)lr * lrow,
@@ -422,6 +481,8 @@ int vella_spec_create(vella_model* target, vella_model* draft, const vella_spec_
       return fail(VELLA_E_INVALID, "vella_spec_create: draft and target must share vocabulary and dtype");
     if (draft->cfg.max_seq < target->cfg.max_seq || draft->device != target->device)
       return fail(VELLA_E_INVALID, "vella_spec_create: the draft needs max_seq >= the target's, on the same device");
+    if (draft->streams != target->streams)
+      return fail(VELLA_E_INVALID, "vella_spec_create: draft and target must hold the same number of streams");
   }
   if (cfg->draft_k < 1 || cfg->draft_k + 1 > kMaxRows)
     return fail(VELLA_E_UNSUPPORTED, "vella_spec_create: draft_k %d (1..%d)", cfg->draft_k, kMaxRows - 1);
@@ -433,22 +494,24 @@ int vella_spec_create(vella_model* target, vella_model* draft, const vella_spec_
   s->cfg = *cfg;
   s->device = target->device;
   s->max_seq = target->cfg.max_seq;
+  s->streams = target->streams;
+  const size_t S = (size_t)s->streams;
   int rc = VELLA_OK;
   auto cuda = [&](cudaError_t e, const char* what) {
     if (e != cudaSuccess && rc == VELLA_OK) rc = cuda_fail(e, what);
   };
   cuda(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "cudaStreamCreate");
-  cuda(cudaMalloc(&s->dstate, sizeof(DevState)), "cudaMalloc(state)");
-  cuda(cudaMallocHost(&s->hstate, sizeof(DevState)), "cudaMallocHost(state)");
-  cuda(cudaMalloc(&s->tok, (size_t)s->max_seq * sizeof(int)), "cudaMalloc(tokens)");
-  cuda(cudaMalloc(&s->ref, (size_t)s->max_seq * sizeof(int)), "cudaMalloc(reference)");
+  cuda(cudaMalloc(&s->dstate, S * sizeof(DevState)), "cudaMalloc(state)");
+  cuda(cudaMallocHost(&s->hstate, S * sizeof(DevState)), "cudaMallocHost(state)");
+  cuda(cudaMalloc(&s->tok, S * s->max_seq * sizeof(int)), "cudaMalloc(tokens)");
+  cuda(cudaMalloc(&s->ref, S * s->max_seq * sizeof(int)), "cudaMalloc(reference)");
   cuda(cudaEventCreate(&s->ev0), "cudaEventCreate");
   cuda(cudaEventCreate(&s->ev1), "cudaEventCreate");
   cuda(cudaEventCreate(&s->evp), "cudaEventCreate");
   if (rc == VELLA_OK) {
-    std::memset(s->hstate, 0, sizeof(DevState));
-    cuda(cudaMemset(s->dstate, 0, sizeof(DevState)), "cudaMemset");
-    cuda(cudaMemset(s->tok, 0, (size_t)s->max_seq * sizeof(int)), "cudaMemset");
+    std::memset(s->hstate, 0, S * sizeof(DevState));
+    cuda(cudaMemset(s->dstate, 0, S * sizeof(DevState)), "cudaMemset");
+    cuda(cudaMemset(s->tok, 0, S * s->max_seq * sizeof(int)), "cudaMemset");
   }
   if (rc != VELLA_OK) {
     vella_spec_destroy(s);
@@ -484,12 +547,16 @@ int vella_spec_set_prefix(vella_spec* s, const void* target_embeds, const void* 
     return fail(VELLA_E_INVALID, "vella_spec_set_prefix: T=%d exceeds max_prefix", T);
   VELLA_CUDA_TRY(cudaSetDevice(s->device));
   const cudaMemcpyKind kind = on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
-  if (target_embeds)
-    VELLA_CUDA_TRY(cudaMemcpyAsync(s->target->prefix, target_embeds,
-                                   (size_t)T * s->target->cfg.d_model * s->target->elt, kind, s->stream));
-  if (s->draft && draft_embeds)
-    VELLA_CUDA_TRY(cudaMemcpyAsync(s->draft->prefix, draft_embeds,
-                                   (size_t)T * s->draft->cfg.d_model * s->draft->elt, kind, s->stream));
+  // [streams][T][d] into each stream's prefix slot ([streams][max_prefix][d])
+  auto put = [&](Model* m, const void* src) -> int {
+    const size_t row = (size_t)T * m->cfg.d_model * m->elt;
+    VELLA_CUDA_TRY(cudaMemcpy2DAsync(m->prefix, (size_t)m->prefix_ss * m->elt, src, row, row, (size_t)s->streams, kind,
+                                     s->stream));
+    return VELLA_OK;
+  };
+  int rc;
+  if (target_embeds && (rc = put(s->target, target_embeds))) return rc;
+  if (s->draft && draft_embeds && (rc = put(s->draft, draft_embeds))) return rc;
   VELLA_CUDA_TRY(cudaStreamSynchronize(s->stream));
   s->P = T;
   return VELLA_OK;
@@ -500,15 +567,18 @@ int vella_spec_set_reference(vella_spec* s, const int32_t* tokens, int32_t n) {
   if (!s || (n > 0 && !tokens)) return fail(VELLA_E_INVALID, "vella_spec_set_reference: NULL argument");
   if (n < 0 || n > s->max_seq) return fail(VELLA_E_INVALID, "vella_spec_set_reference: n=%d", n);
   VELLA_CUDA_TRY(cudaSetDevice(s->device));
-  if (n) VELLA_CUDA_TRY(cudaMemcpyAsync(s->ref, tokens, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, s->stream));
+  if (n)
+    VELLA_CUDA_TRY(cudaMemcpy2DAsync(s->ref, (size_t)s->max_seq * sizeof(int), tokens, (size_t)n * sizeof(int),
+                                     (size_t)n * sizeof(int), (size_t)s->streams, cudaMemcpyHostToDevice, s->stream));
   VELLA_CUDA_TRY(cudaStreamSynchronize(s->stream));
-  s->hstate->ref_len = n;
+  s->ref_len = n;
   return VELLA_OK;
 }
 
 int vella_spec_prefill(vella_spec* s, int32_t* first) {
   last_error_slot().clear();
   if (!s || !first) return fail(VELLA_E_INVALID, "vella_spec_prefill: NULL argument");
+  if (s->streams != 1) return fail(VELLA_E_UNSUPPORTED, "vella_spec_prefill: %d streams (use vella_spec_decode_batch)", s->streams);
   VELLA_CUDA_TRY(cudaSetDevice(s->device));
   return prefill(s, first);
 }
@@ -519,6 +589,7 @@ int vella_spec_step(vella_spec* s, int32_t* out_tokens, int32_t* n_out) {
   if (!s->draft) return fail(VELLA_E_UNSUPPORTED, "vella_spec_step: no draft model");
   if (s->hstate->L < s->P + 1) return fail(VELLA_E_INVALID, "vella_spec_step: prefill first");
   if (s->hstate->L + s->cfg.draft_k + 1 > s->max_seq) return fail(VELLA_E_INVALID, "vella_spec_step: KV capacity reached");
+  if (s->streams != 1) return fail(VELLA_E_UNSUPPORTED, "vella_spec_step: %d streams (use vella_spec_decode_batch)", s->streams);
   VELLA_CUDA_TRY(cudaSetDevice(s->device));
   const int rc = run_unit(s, true);
   if (rc) return rc;
@@ -536,6 +607,7 @@ int vella_spec_greedy_step(vella_spec* s, int32_t* out_token) {
   if (!s || !out_token) return fail(VELLA_E_INVALID, "vella_spec_greedy_step: NULL argument");
   if (s->hstate->L < s->P + 1) return fail(VELLA_E_INVALID, "vella_spec_greedy_step: prefill first");
   if (s->hstate->L + 1 > s->max_seq) return fail(VELLA_E_INVALID, "vella_spec_greedy_step: KV capacity reached");
+  if (s->streams != 1) return fail(VELLA_E_UNSUPPORTED, "vella_spec_greedy_step: %d streams (use vella_spec_decode_batch)", s->streams);
   VELLA_CUDA_TRY(cudaSetDevice(s->device));
   const int rc = run_unit(s, false);
   if (rc) return rc;
@@ -550,6 +622,7 @@ int vella_spec_decode(vella_spec* s, int32_t mode, int32_t max_tokens, int32_t* 
   last_error_slot().clear();
   if (!s || !n_out || !flags || (cap > 0 && !out_tokens)) return fail(VELLA_E_INVALID, "vella_spec_decode: NULL argument");
   if (max_tokens < 0) return fail(VELLA_E_INVALID, "vella_spec_decode: max_tokens < 0");
+  if (s->streams != 1) return fail(VELLA_E_UNSUPPORTED, "vella_spec_decode: %d streams (use vella_spec_decode_batch)", s->streams);
   VELLA_CUDA_TRY(cudaSetDevice(s->device));
   *flags = 0;
   Decoded result;
@@ -599,6 +672,54 @@ int vella_spec_decode(vella_spec* s, int32_t mode, int32_t max_tokens, int32_t* 
   s->stats.last_tokens = n;
   for (int i = 0; i < std::min(n, cap); ++i) out_tokens[i] = result.tokens[i];
   return VELLA_OK;
+}
+
+int vella_spec_decode_batch(vella_spec* s, int32_t mode, int32_t max_tokens, int32_t* out_tokens, int32_t* n_out) {
+  last_error_slot().clear();
+  if (!s || !out_tokens || !n_out) return fail(VELLA_E_INVALID, "vella_spec_decode_batch: NULL argument");
+  if (mode != VELLA_DECODE_SPEC && mode != VELLA_DECODE_GREEDY)
+    return fail(VELLA_E_INVALID, "vella_spec_decode_batch: mode %d (SPEC or GREEDY)", mode);
+  if (mode == VELLA_DECODE_SPEC && !s->draft) return fail(VELLA_E_UNSUPPORTED, "vella_spec_decode_batch: no draft model");
+  const int K = s->cfg.draft_k;
+  if (max_tokens < 1 || s->P + max_tokens + K + 1 > s->max_seq)
+    return fail(VELLA_E_INVALID, "vella_spec_decode_batch: prefix %d + %d tokens (+%d) exceed max_seq %d", s->P,
+                max_tokens, K + 1, s->max_seq);
+  VELLA_CUDA_TRY(cudaSetDevice(s->device));
+  VELLA_CUDA_TRY(cudaEventRecord(s->ev0, s->stream));
+  int rc;
+  if ((rc = prefill_all(s, max_tokens))) return rc;
+  const bool spec = mode == VELLA_DECODE_SPEC;
+  for (;;) {
+    bool all = true;
+    for (int j = 0; j < s->streams; ++j) {
+      if (s->hstate[j].nonfinite) return fail(VELLA_E_NONFINITE, "non-finite logits in stream %d", j);
+      all = all && s->hstate[j].produced >= max_tokens;
+    }
+    if (all) break;
+    if ((rc = run_unit(s, spec))) return rc;
+    if (spec) {
+      s->stats.passes++;
+      for (int j = 0; j < s->streams; ++j) {
+        const int n = s->hstate[j].n_new;
+        if (n >= 1 && n <= 16) s->stats.accepted[n - 1]++;
+      }
+    } else {
+      s->stats.greedy_steps++;
+    }
+  }
+  VELLA_CUDA_TRY(cudaEventRecord(s->ev1, s->stream));
+  VELLA_CUDA_TRY(cudaMemcpy2DAsync(out_tokens, (size_t)max_tokens * sizeof(int), s->tok + s->P,
+                                   (size_t)s->max_seq * sizeof(int), (size_t)max_tokens * sizeof(int),
+                                   (size_t)s->streams, cudaMemcpyDeviceToHost, s->stream));
+  VELLA_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  float ms = 0.0f, pms = 0.0f;
+  cudaEventElapsedTime(&pms, s->ev0, s->evp);
+  cudaEventElapsedTime(&ms, s->evp, s->ev1);
+  s->stats.last_decode_ms = ms;
+  s->stats.last_prefill_ms = pms;
+  s->stats.last_tokens = max_tokens * s->streams;
+  for (int j = 0; j < s->streams; ++j) n_out[j] = max_tokens;
+  return pipeline_faults();
 }
 
 int vella_spec_get_stats(const vella_spec* s, vella_spec_stats* out) {

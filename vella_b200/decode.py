@@ -27,7 +27,7 @@ class ModelCfg(ctypes.Structure):
                 ("n_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("ffn", ctypes.c_int32),
                 ("vocab", ctypes.c_int32), ("bits", ctypes.c_int32), ("dtype", ctypes.c_int32),
                 ("qk_norm", ctypes.c_int32), ("max_seq", ctypes.c_int32), ("max_prefix", ctypes.c_int32),
-                ("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float)]
+                ("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float), ("streams", ctypes.c_int32)]
 
 
 class SpecCfg(ctypes.Structure):
@@ -63,6 +63,7 @@ for _name, _res, _args in [
     ("vella_spec_step", ctypes.c_int, [_vp, _pi32, _pi32]),
     ("vella_spec_greedy_step", ctypes.c_int, [_vp, _pi32]),
     ("vella_spec_decode", ctypes.c_int, [_vp, _i32, _i32, _pi32, _i32, _pi32, _pi32]),
+    ("vella_spec_decode_batch", ctypes.c_int, [_vp, _i32, _i32, _pi32, _pi32]),
     ("vella_spec_get_stats", ctypes.c_int, [_vp, ctypes.POINTER(SpecStats)]),
     ("vella_spec_set_fault", ctypes.c_int, [_vp, _i32]),
     ("vella_spec_reset", ctypes.c_int, [_vp]),
@@ -91,11 +92,12 @@ class ModelConfig:
     max_prefix: int = 1024
     rms_eps: float = 1e-6
     rope_theta: float = 1e6
+    streams: int = 1
 
     def c(self) -> ModelCfg:
         return ModelCfg(self.n_layers, self.d_model, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn,
                         self.vocab, self.bits, self.dtype, int(self.qk_norm), self.max_seq, self.max_prefix,
-                        self.rms_eps, self.rope_theta)
+                        self.rms_eps, self.rope_theta, self.streams)
 
 
 class Model:
@@ -169,13 +171,14 @@ class SpecDecoder:
     def set_prefix(self, target_embeds: Optional[np.ndarray], draft_embeds: Optional[np.ndarray], T: int = None):
         t = None if target_embeds is None else np.ascontiguousarray(target_embeds)
         d = None if draft_embeds is None else np.ascontiguousarray(draft_embeds)
-        n = T if T is not None else t.shape[0]
+        n = T if T is not None else t.shape[-2]  # [T, d], or [streams, T, d] stream-major
         _lib.check(_lib.lib().vella_spec_set_prefix(self.handle, None if t is None else t.ctypes.data,
                                                     None if d is None else d.ctypes.data, n, 1))
 
-    def set_reference(self, tokens: Sequence[int]):
-        arr, ptr = _i32_array(tokens)
-        _lib.check(_lib.lib().vella_spec_set_reference(self.handle, ptr, len(arr)))
+    def set_reference(self, tokens):
+        """Oracle-draft continuation: [n] tokens, or [streams, n] for several streams."""
+        arr = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        _lib.check(_lib.lib().vella_spec_set_reference(self.handle, arr.ctypes.data_as(_pi32), arr.shape[-1]))
 
     def prefill(self) -> int:
         v = ctypes.c_int32()
@@ -207,6 +210,15 @@ class SpecDecoder:
 
     def decode_mtp(self, max_tokens: int) -> DecodeResult:
         return self.decode(max_tokens, DECODE_SPEC)
+
+    def decode_batch(self, max_tokens: int, mode: int = DECODE_SPEC) -> np.ndarray:
+        """Every stream's first max_tokens tokens, [streams, max_tokens] (models with streams > 1)."""
+        streams = self.target.cfg.streams
+        out = np.zeros((streams, max_tokens), np.int32)
+        n = np.zeros(streams, np.int32)
+        _lib.check(_lib.lib().vella_spec_decode_batch(self.handle, mode, max_tokens, out.ctypes.data_as(_pi32),
+                                                      n.ctypes.data_as(_pi32)))
+        return out
 
     def stats(self) -> dict:
         s = SpecStats()
