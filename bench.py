@@ -249,6 +249,7 @@ DRAFT = dict(n_layers=28, d_model=2048, n_heads=16, n_kv_heads=8, head_dim=128, 
 PREFIX, NEW_TOKENS = 750, 448
 SWEEP = [(4, 0.5), (4, 0.7), (4, 0.9), (8, 0.5), (8, 0.7), (8, 0.9)]
 HEADLINE = (4, 0.7)
+BATCH_STREAMS = 32  # streams per GPU of the batched measurement
 
 
 def expected_tokens_per_pass(k, p):
@@ -471,10 +472,60 @@ def run_spec(args, rank, world):
     }
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(k, p)
+    for x in (sd, se):
+        x.close()
+    target.close()
+    draft.close()
+    if not args.no_batched:
+        line["batched"] = run_spec_batched(rank, local, BATCH_STREAMS, k, p)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     return line
+
+
+def run_spec_batched(rank, local, S, k, p):
+    """S independent streams per GPU decoded as one batch: every draft step and every verify
+    runs all streams' rows together (verify M = S * (k + 1), the tensor-core GEMM path).
+    Same weights as the single-stream run, S different prefixes; the oracle draft follows
+    each stream's own greedy continuation (the batched greedy decode, same GEMM path)."""
+    import numpy as np
+    import torch
+    from vella_b200 import _lib as L
+    from vella_b200 import decode as VD
+    max_seq = PREFIX + NEW_TOKENS + 64
+    tc = VD.ModelConfig(**TARGET, max_seq=max_seq, max_prefix=PREFIX, rope_theta=1e6, streams=S)
+    dc = VD.ModelConfig(**DRAFT, max_seq=max_seq, max_prefix=PREFIX, rope_theta=1e6, streams=S)
+    target = VD.Model(tc, local)
+    target.init_random(1, 0.02)
+    draft = VD.Model(dc, local)
+    draft.init_random(2, 0.02)
+    fill = L.lib().vella_fill_normal
+    for m, dd, tid in ((target, TARGET["d_model"], 21), (draft, DRAFT["d_model"], 22)):
+        ptr, _ = m.tensor("prefix")
+        L.check(fill(ptr, S * PREFIX * dd, L.BF16, 3 + rank, tid, 0.0, 1.0, None))
+    torch.cuda.synchronize()
+    sd = VD.SpecDecoder(target, draft, k=k, mode=VD.DRAFT_ORACLE, oracle_p=p, seed=7 + rank)
+    sd.set_prefix(None, None, PREFIX)
+    greedy = sd.decode_batch(NEW_TOKENS, VD.DECODE_GREEDY)
+    g = sd.stats()
+    sd.set_reference(greedy)
+    sd.decode_batch(NEW_TOKENS, VD.DECODE_SPEC)  # warm-up (captures the pass graph)
+    p0 = sd.stats()["passes"]
+    spec = sd.decode_batch(NEW_TOKENS, VD.DECODE_SPEC)
+    st = sd.stats()
+    tokens = S * (NEW_TOKENS - 1)  # each stream's first token comes from its prefill
+    out = {"streams_per_gpu": S, "k": k, "p": p,
+           "tokens_per_s": round(tokens / (st["last_decode_ms"] / 1e3), 1),
+           "greedy_tokens_per_s": round(tokens / (g["last_decode_ms"] / 1e3), 1),
+           "passes": st["passes"] - p0, "decode_ms": round(st["last_decode_ms"], 1),
+           "prefill_ms_all_streams": round(st["last_prefill_ms"], 1),
+           "bit_exact_vs_batched_greedy": bool(np.array_equal(spec, greedy)),
+           "note": "decode-only device time; verify rows per pass = streams x (k+1) on the tensor cores"}
+    sd.close()
+    target.close()
+    draft.close()
+    return out
 
 
 # ---------------------------------------------------------------------------------------
@@ -753,6 +804,7 @@ def main():
     ap.add_argument("--workload", default="spec", choices=["spec", "gemm", "whisper"])
     ap.add_argument("--impl", default="vella", choices=["vella", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="spec workload: skip the multi-stream measurement")
     ap.add_argument("--shape", default="", help="gemm workload: one case 'bits,N,K,M' instead of the sweep")
     ap.add_argument("--profile-pass", action="store_true", help="short run for an ncu launch list")
     args = ap.parse_args()

@@ -327,11 +327,12 @@ def test_batched_greedy_equals_single_stream_greedy():
         m.close()
 
 
-@pytest.mark.parametrize("S,k", [(3, 4), (20, 3)])
+@pytest.mark.parametrize("S,k", [(3, 4), (20, 3), (32, 4)])
 def test_batched_spec_equals_batched_greedy(S, k):
     """Draft-and-verify over S streams in one batch emits each stream's greedy tokens bit for
     bit; S=3, K=4 keeps every GEMM on the small-M kernels (15 verify rows), S=20 puts the
-    greedy step (20 rows) and the verify (80 rows) on the tensor cores."""
+    greedy step (20 rows) and the verify (80 rows) on the tensor cores; S=32 verifies 160 rows
+    (two token tiles, argmax rows past 128 after 32-row draft launches on the same scratch)."""
     from vella_b200 import decode as VD
     P, n = 20, 40
     _, _, tb, db = _batch_models(S)

@@ -398,6 +398,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn
 // argmax per row with the lowest index on ties; NaN/Inf anywhere sets the flag
 // ---------------------------------------------------------------------------------------
 constexpr int kArgBlocks = 32;
+constexpr int kArgRowBytes = kArgBlocks * 8 + 16;  // partials (float2 each) + counter, 16-byte slots
 
 __device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
   if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
@@ -405,7 +406,7 @@ __device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
 
 template <typename T>
 __global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logits, int V, size_t ld,
-                                                     int* __restrict__ ys, float2* part, int* ctr, int* nonfinite) {
+                                                     int* __restrict__ ys, char* scratch, int* nonfinite) {
   using A = Act<T>;
   pdl_wait();
   pdl_launch_next();
@@ -448,17 +449,19 @@ __global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logit
   __syncthreads();
   if (threadIdx.x == 0) {
     for (int w = 1; w < 8; ++w) better(bv, bi, sv[w], si[w]);
-    part[m * kArgBlocks + b] = make_float2(bv, __int_as_float(bi));
+    float2* part = reinterpret_cast<float2*>(scratch + (size_t)m * kArgRowBytes);
+    int* ctr = reinterpret_cast<int*>(part + kArgBlocks);
+    part[b] = make_float2(bv, __int_as_float(bi));
     __threadfence();
-    const int prev = atomicAdd(ctr + m, 1);
+    const int prev = atomicAdd(ctr, 1);
     s_last = prev == kArgBlocks - 1;
     if (s_last) {
-      ctr[m] = 0;
+      *ctr = 0;
       __threadfence();
       float fv = -INFINITY;
       int fi = INT32_MAX;
       for (int k = 0; k < kArgBlocks; ++k) {
-        const float2 p = __ldcg(part + m * kArgBlocks + k);
+        const float2 p = __ldcg(part + k);
         better(fv, fi, p.x, __float_as_int(p.y));
       }
       ys[m] = fi == INT32_MAX ? 0 : fi;
@@ -563,22 +566,20 @@ int launch_attention(int dtype, const void* q, const void* kc, const void* vc, v
   return launch_attention_ex(dtype, v, 1, pr, 1, rows, H, KV, hd, max_seq, scale, s);
 }
 
-size_t argmax_scratch_bytes(int max_rows) {
-  return (size_t)max_rows * kArgBlocks * sizeof(float2) + 256 + (size_t)max_rows * sizeof(int);
-}
+// One slot per logits row, at a fixed offset whatever the launch's row count: the row's
+// kArgBlocks partial maxima, then its ticket counter (zero between launches).
+size_t argmax_scratch_bytes(int max_rows) { return (size_t)max_rows * kArgRowBytes + 256; }
 
 int launch_argmax(int dtype, const void* logits, int rows, int V, size_t ld, int* ys, void* scratch,
                   int* nonfinite, cudaStream_t s) {
   if (rows <= 0) return VELLA_OK;
-  // layout: counters [rows] first (256-byte slot... sized by the caller), then partials
-  int* ctr = static_cast<int*>(scratch);
-  float2* part = reinterpret_cast<float2*>(static_cast<char*>(scratch) + 256 + ((size_t)rows * sizeof(int) + 255) / 256 * 256);
+  char* sc = static_cast<char*>(scratch);
   const dim3 grid(rows, kArgBlocks);
   if (dtype == VELLA_BF16)
     return launch_kernel(argmax_kernel<__nv_bfloat16>, grid, dim3(256), 0, s,
-                         static_cast<const __nv_bfloat16*>(logits), V, ld, ys, part, ctr, nonfinite);
-  return launch_kernel(argmax_kernel<__half>, grid, dim3(256), 0, s, static_cast<const __half*>(logits), V, ld, ys,
-                       part, ctr, nonfinite);
+                         static_cast<const __nv_bfloat16*>(logits), V, ld, ys, sc, nonfinite);
+  return launch_kernel(argmax_kernel<__half>, grid, dim3(256), 0, s, static_cast<const __half*>(logits), V, ld, ys, sc,
+                       nonfinite);
 }
 
 }  // namespace vella

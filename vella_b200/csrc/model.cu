@@ -421,7 +421,7 @@ int model_tensor(Model* m, const std::string& name, int layer, void** ptr, size_
   };
   if (name == "embed") return ret(m->embed, (size_t)c.vocab * c.d_model * e);
   if (name == "final_norm") return ret(m->final_norm, (size_t)c.d_model * e);
-  if (name == "prefix") return ret(m->prefix, (size_t)c.max_prefix * c.d_model * e);
+  if (name == "prefix") return ret(m->prefix, (size_t)m->streams * m->prefix_ss * e);  // [streams][max_prefix][d]
   if (name == "logits") return ret(m->logits, (size_t)kMaxRows * c.vocab * e);
   if (name == "kv") return ret(m->kv, m->kv_bytes);
   const size_t dot = name.find('.');
