@@ -205,6 +205,17 @@ typedef struct vella_spec_cfg {
   int32_t n_eos;
   int32_t eos[8];
   int32_t use_graphs; /* 1: replay each pass as one CUDA graph */
+  /* 0: greedy acceptance (argmax; the reference's decodeMTP, :364-369).  > 0: stochastic
+   * acceptance at this temperature, which the reference does not have (speculative sampling:
+   * Leviathan et al. 2023, Chen et al. 2023): tokens follow softmax(logits / temperature) of
+   * the target exactly.  The draft samples its proposals from softmax(draft logits /
+   * temperature) (the oracle draft keeps its mixture: reference token with probability
+   * oracle_p, else uniform); draft j is accepted when u < p(x_j) / q(x_j); at the first
+   * rejection the token is drawn from max(0, p - q) renormalised; after K acceptances the
+   * bonus token is drawn from p.  The first token after the prefill and plain (greedy-mode)
+   * steps are drawn from p.  Uniforms are Philox-4x32-10 keyed by `seed`, with counters
+   * (pass or step, position, purpose, stream), so a run is reproducible. */
+  float temperature;
 } vella_spec_cfg;
 
 typedef struct vella_spec_stats {

@@ -352,3 +352,86 @@ def test_batched_spec_equals_batched_greedy(S, k):
     assert st["passes"] > 0 and sum(st["accepted"][1:]) > sum(st["accepted"][:1])
     for x in (sb, so, tb, db):
         x.close()
+
+
+def _chi2(counts, probs, n):
+    """Chi-square statistic over cells merged so every expected count is at least 5."""
+    order = np.argsort(-probs)
+    stat, obs, exp = 0.0, 0.0, 0.0
+    cells = 0
+    for i in order:
+        obs += counts[i]
+        exp += probs[i] * n
+        if exp >= 5:
+            stat += (obs - exp) ** 2 / exp
+            obs, exp = 0.0, 0.0
+            cells += 1
+    if exp > 0:
+        stat += (obs - exp) ** 2 / max(exp, 1e-9)
+        cells += 1
+    return stat, cells
+
+
+def _softmax(row, T):
+    z = (row - row.max()) / T
+    e = np.exp(z)
+    return e / e.sum()
+
+
+@pytest.mark.parametrize("spec", [True, False])
+def test_sampled_tokens_follow_the_target_distribution(spec):
+    """Stochastic acceptance (temperature 1): over 1024 streams with one prefix, the first
+    token (drawn after the prefill) and the second (drawn by draft-and-verify with rejections
+    against the residual, or by a plain sampling step) follow the target's softmax."""
+    from vella_b200 import decode as VD
+    S, P, V, T = 1024, 4, 16, 1.0
+    cfg = dict(n_layers=1, d_model=64, n_heads=1, n_kv_heads=1, head_dim=64, ffn=64, vocab=V, bits=0,
+               max_seq=32, max_prefix=8)
+    tb = VD.Model(VD.ModelConfig(**cfg, streams=S))
+    tb.init_random(41, 0.5)
+    db = VD.Model(VD.ModelConfig(**cfg, streams=S))
+    db.init_random(42, 0.5)
+    single = VD.Model(VD.ModelConfig(**cfg))
+    single.init_random(41, 0.5)
+    pre = prefix_of(P, 64, 43)
+    sb = VD.SpecDecoder(tb, db, k=2, seed=123, temperature=T)
+    sb.set_prefix(np.stack([pre] * S), np.stack([prefix_of(P, 64, 44)] * S))
+    toks = sb.decode_batch(3, VD.DECODE_SPEC if spec else VD.DECODE_GREEDY)
+    assert toks.min() >= 0 and toks.max() < V
+    # exact probabilities from the target's own logits (teacher forced, bf16)
+    p1 = _softmax(A.bf16_from_bits(single.score(pre, [0]))[0].astype(np.float64), T)
+    p2 = np.zeros(V)
+    for t1 in range(V):
+        row = A.bf16_from_bits(single.score(pre, [t1, 0]))[1].astype(np.float64)
+        p2 += p1[t1] * _softmax(row, T)
+    for col, probs in ((0, p1), (1, p2)):
+        counts = np.bincount(toks[:, col], minlength=V).astype(np.float64)
+        stat, cells = _chi2(counts, probs, S)
+        assert stat < 3.0 * cells + 20, (col, stat, cells, counts, probs * S)
+    if spec:
+        st = sb.stats()
+        assert st["passes"] > 0 and st["accepted"][0] > 0  # rejections happened (residual draws)
+    # same seed, same tokens; another seed, other tokens
+    again = sb.decode_batch(3, VD.DECODE_SPEC if spec else VD.DECODE_GREEDY)
+    assert np.array_equal(again, toks)
+    sb.close()
+    for m in (tb, db, single):
+        m.close()
+
+
+def test_sampled_oracle_draft_runs_and_is_reproducible(pair):
+    from vella_b200 import decode as VD
+    t, tc, d, dc = pair
+    P = 24
+    pre_t, pre_d = prefix_of(P, tc.d_model, 11), prefix_of(P, dc.d_model, 12)
+    ref, _ = greedy_tokens(t, d, P, pre_t, pre_d, 40)
+    outs = []
+    for seed in (5, 5, 6):
+        sd = VD.SpecDecoder(t, d, k=4, mode=VD.DRAFT_ORACLE, oracle_p=0.7, seed=seed, temperature=0.7)
+        sd.set_prefix(pre_t, pre_d, P)
+        sd.set_reference(ref)
+        outs.append(sd.decode_mtp(40).tokens)
+        assert sd.stats()["passes"] > 0
+        sd.close()
+    assert outs[0] == outs[1] and len(outs[0]) == 40
+    assert outs[0] != outs[2]

@@ -18,6 +18,8 @@
 // the next pass overwrites everything from there on (no copies, no trims).  The draft runs
 // its first step over the two positions L-2, L-1, so it catches up after a full acceptance
 // and after a rejection with the same graph.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -50,6 +52,14 @@ struct DevState {
 constexpr int kStateInts = sizeof(DevState) / sizeof(int);  // PosRef stride between streams
 
 __device__ __forceinline__ bool done(const DevState& x) { return x.quota > 0 && x.produced >= x.quota; }
+
+// The decode settings the sampling kernels read.
+struct vella_spec_cfg_dev {
+  uint64_t seed;
+  float temperature;
+  float oracle_p;
+  int draft_mode;
+};
 
 // One stream: st, tok and the logits rows of that stream's prefill forward.
 __global__ void prefill_finish_kernel(DevState* st, int* tok, const int* ys, const int* nf, const int* err_t,
@@ -136,6 +146,279 @@ __global__ void accept_kernel(DevState* st, int* tok, const int* ys, int K, cons
   x.produced += a + 1;
 }
 
+// ---- stochastic acceptance (temperature > 0) ------------------------------------------------
+// Uniform purposes in the Philox counter (pass or step, position, purpose, stream).
+constexpr uint32_t kPurposeDraft = 0x5A3D1u, kPurposeAccept = 0xACC01u, kPurposeResidual = 0xB0B05u,
+                   kPurposeFirst = 0xF1257u, kPurposeStep = 0x57E90u;
+constexpr int kSampThreads = 512;
+
+struct SampShared {
+  float red[kSampThreads / 32];
+  float part[kSampThreads];
+  float before, stat;
+  int seg, idx;
+};
+
+__device__ __forceinline__ float uni(const vella_spec_cfg_dev& c, uint32_t a, uint32_t b, uint32_t purpose, int s) {
+  return u01(philox4x32_10(U4{a, b, purpose, (uint32_t)s}, (uint32_t)c.seed, (uint32_t)(c.seed >> 32)).x);
+}
+
+__device__ float block_max(float v, SampShared& sh) {
+  v = warp_max(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh.red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = -INFINITY;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, sh.red[w]);
+    sh.stat = m;
+  }
+  __syncthreads();
+  return sh.stat;
+}
+
+__device__ float block_sum(float v, SampShared& sh) {
+  v = warp_sum(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh.red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += sh.red[w];
+    sh.stat = t;
+  }
+  __syncthreads();
+  return sh.stat;
+}
+
+// (max, sum of exp((l - max) / T)) of one logits row.
+template <typename T>
+__device__ float2 row_softmax_stats(const T* row, int V, float invT, SampShared& sh) {
+  float m = -INFINITY;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) m = fmaxf(m, Act<T>::to_f(row[v]));
+  m = block_max(m, sh);
+  float z = 0.0f;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) z += expf((Act<T>::to_f(row[v]) - m) * invT);
+  z = block_sum(z, sh);
+  return make_float2(m, z);
+}
+
+// Index drawn from the unnormalised weights w(0..V) with the uniform u: thread t owns the
+// contiguous range [t C, (t+1) C); the partial sums are scanned in thread order, so the
+// result depends only on the weights and u.  -1 when every weight is zero.
+template <typename W>
+__device__ int sample_icdf(W w, int V, float u, SampShared& sh) {
+  const int C = (V + (int)blockDim.x - 1) / (int)blockDim.x;
+  const int lo = min(V, (int)threadIdx.x * C), hi = min(V, lo + C);
+  float ps = 0.0f;
+  for (int v = lo; v < hi; ++v) ps += w(v);
+  __syncthreads();
+  sh.part[threadIdx.x] = ps;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.0f;
+    for (int t = 0; t < (int)blockDim.x; ++t) tot += sh.part[t];
+    const float target = u * tot;
+    float acc = 0.0f;
+    int seg = -1, last = -1;
+    for (int t = 0; t < (int)blockDim.x; ++t) {
+      const float p = sh.part[t];
+      if (p > 0.0f) last = t;
+      if (seg < 0 && acc + p > target) {
+        seg = t;
+        sh.before = acc;
+      }
+      acc += p;
+    }
+    if (seg < 0) {  // rounding at the top end: the last range with weight
+      seg = last;
+      sh.before = -1.0f;
+    }
+    sh.seg = seg;
+    sh.idx = -1;
+    sh.stat = target;
+  }
+  __syncthreads();
+  if ((int)threadIdx.x == sh.seg) {
+    const float target = sh.stat;
+    float acc = sh.before;
+    int found = -1, lastv = -1;
+    for (int v = lo; v < hi; ++v) {
+      const float x = w(v);
+      if (x > 0.0f) lastv = v;
+      if (found < 0 && sh.before >= 0.0f && acc + x > target) found = v;
+      acc += x;
+    }
+    sh.idx = found >= 0 ? found : lastv;
+  }
+  __syncthreads();
+  return sh.idx;
+}
+
+// Draft step i, stream blockIdx.x: x ~ softmax(draft logits / T) for position L + i; the
+// row and its (max, sum) are kept for the acceptance test.
+template <typename T>
+__global__ void __launch_bounds__(kSampThreads) draft_sample_kernel(DevState* st, int* tok, const T* logits, int i,
+                                                                    vella_spec_cfg_dev c, int vocab, int max_seq,
+                                                                    T* qrows, float2* qstats, int S) {
+  __shared__ SampShared sh;
+  pdl_wait();
+  pdl_launch_next();
+  const int s = blockIdx.x;
+  const DevState& x = st[s];
+  const T* row = logits + (size_t)s * vocab;
+  const float invT = 1.0f / c.temperature;
+  const float2 mz = row_softmax_stats(row, vocab, invT, sh);
+  const float u = uni(c, (uint32_t)x.pass, (uint32_t)i, kPurposeDraft, s);
+  int t = sample_icdf([&](int v) { return expf((Act<T>::to_f(row[v]) - mz.x) * invT); }, vocab, u, sh);
+  if (t < 0) t = 0;
+  T* q = qrows + ((size_t)i * S + s) * vocab;
+  for (int v = threadIdx.x; v < vocab; v += blockDim.x) q[v] = row[v];
+  if (threadIdx.x == 0) {
+    qstats[(size_t)i * S + s] = mz;
+    const int pos = x.L + i;
+    if (pos < max_seq) tok[(size_t)s * max_seq + pos] = t;
+  }
+}
+
+// q(v) of draft position j: the model draft's kept row, or the oracle draft's mixture.
+template <typename T>
+struct DraftQ {
+  const T* row;  // null: oracle draft
+  float m, z, invT;
+  int ref;       // oracle: reference token at this position, -1 when outside the reference
+  float p;
+  int vocab;
+  __device__ float operator()(int v) const {
+    if (row) return expf((Act<T>::to_f(row[v]) - m) * invT) / z;
+    const float base = (ref >= 0 ? 1.0f - p : 1.0f) / (float)vocab;
+    return v == ref ? base + p : base;
+  }
+};
+
+// Stochastic acceptance of stream blockIdx.x over its K + 1 verify rows.
+template <typename T>
+__global__ void __launch_bounds__(kSampThreads) accept_sampled_kernel(DevState* st, int* tok, const T* logits, int K,
+                                                                      vella_spec_cfg_dev c, int vocab, int max_seq,
+                                                                      const T* qrows, const float2* qstats, int S,
+                                                                      const int* ref, const int* nf, const int* err_t,
+                                                                      const int* err_d) {
+  __shared__ SampShared sh;
+  pdl_wait();
+  pdl_launch_next();
+  const int s = blockIdx.x;
+  DevState& x = st[s];
+  if (done(x)) {  // uniform across the block: every thread returns
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      x.nonfinite = *nf;
+      x.err |= *err_t | *err_d;
+      x.n_new = 0;
+    }
+    return;
+  }
+  int* tk = tok + (size_t)s * max_seq;
+  const int L = x.L;
+  const float invT = 1.0f / c.temperature;
+  int a = 0, bonus = -1;
+  for (int j = 0; j < K; ++j) {
+    const T* prow = logits + ((size_t)s * (K + 1) + j) * vocab;
+    const float2 pm = row_softmax_stats(prow, vocab, invT, sh);
+    const int xj = tk[L + j];
+    DraftQ<T> q{};
+    q.invT = invT;
+    q.vocab = vocab;
+    q.p = c.oracle_p;
+    if (c.draft_mode == VELLA_DRAFT_ORACLE) {
+      const int ri = L + j - x.P;
+      q.ref = (ri >= 0 && ri < x.ref_len) ? ref[(size_t)s * max_seq + ri] : -1;
+    } else {
+      q.row = qrows + ((size_t)j * S + s) * vocab;
+      const float2 qm = qstats[(size_t)j * S + s];
+      q.m = qm.x;
+      q.z = qm.y;
+    }
+    const float px = expf((Act<T>::to_f(prow[xj]) - pm.x) * invT) / pm.y;
+    const float qx = q(xj);
+    const float u = uni(c, (uint32_t)x.pass, (uint32_t)j, kPurposeAccept, s);
+    if (u * qx < px) {  // accept with probability min(1, p / q)
+      ++a;
+      continue;
+    }
+    const float u2 = uni(c, (uint32_t)x.pass, (uint32_t)j, kPurposeResidual, s);
+    bonus = sample_icdf(
+        [&](int v) { return fmaxf(0.0f, expf((Act<T>::to_f(prow[v]) - pm.x) * invT) / pm.y - q(v)); }, vocab, u2, sh);
+    if (bonus < 0)  // p == q everywhere: draw from p
+      bonus = sample_icdf([&](int v) { return expf((Act<T>::to_f(prow[v]) - pm.x) * invT); }, vocab, u2, sh);
+    break;
+  }
+  if (bonus < 0) {
+    const T* prow = logits + ((size_t)s * (K + 1) + K) * vocab;
+    const float2 pm = row_softmax_stats(prow, vocab, invT, sh);
+    const float u2 = uni(c, (uint32_t)x.pass, (uint32_t)K, kPurposeResidual, s);
+    bonus = sample_icdf([&](int v) { return expf((Act<T>::to_f(prow[v]) - pm.x) * invT); }, vocab, u2, sh);
+    if (bonus < 0) bonus = 0;
+  }
+  if (threadIdx.x == 0) {
+    x.nonfinite = *nf;
+    x.err |= *err_t | *err_d;
+    if (L + a < max_seq) tk[L + a] = bonus; else x.err |= 4;
+    for (int j = 0; j <= a; ++j) x.newtok[j] = tk[L + j];
+    x.n_new = a + 1;
+    x.L = L + a + 1;
+    x.pass += 1;
+    x.produced += a + 1;
+  }
+}
+
+// Plain sampling step of stream blockIdx.x: tok[L] ~ softmax(logits row s / T).  With
+// `first` the row is the stream's prefill logits (one row) and the state is not yet
+// advanced past the prefix (the prefill finish kernel already ran).
+template <typename T>
+__global__ void __launch_bounds__(kSampThreads) sample_commit_kernel(DevState* st, int* tok, const T* logits,
+                                                                     vella_spec_cfg_dev c, int vocab, int max_seq,
+                                                                     int first, int sbase, const int* nf,
+                                                                     const int* err_t) {
+  __shared__ SampShared sh;
+  pdl_wait();
+  pdl_launch_next();
+  const int s = blockIdx.x;
+  DevState& x = st[s];
+  const bool stop = !first && done(x);
+  if (stop) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      x.nonfinite = *nf;
+      x.err |= *err_t;
+      x.n_new = 0;
+    }
+    return;
+  }
+  const T* row = logits + (size_t)s * vocab;
+  const float invT = 1.0f / c.temperature;
+  const float2 mz = row_softmax_stats(row, vocab, invT, sh);
+  const float u = first ? uni(c, 0u, 0u, kPurposeFirst, sbase + s)
+                        : uni(c, (uint32_t)x.produced, 0u, kPurposeStep, sbase + s);
+  int t = sample_icdf([&](int v) { return expf((Act<T>::to_f(row[v]) - mz.x) * invT); }, vocab, u, sh);
+  if (t < 0) t = 0;
+  if (threadIdx.x == 0) {
+    int* tk = tok + (size_t)s * max_seq;
+    if (first) {  // replace the argmax the prefill finish kernel committed at position P
+      tk[x.P] = t;
+      x.newtok[0] = t;
+    } else {
+      x.nonfinite = *nf;
+      x.err |= *err_t;
+      const int L = x.L;
+      if (L < max_seq) tk[L] = t; else x.err |= 4;
+      x.L = L + 1;
+      x.n_new = 1;
+      x.newtok[0] = t;
+      x.produced += 1;
+    }
+  }
+}
+
 }  // namespace
 
 struct Spec {
@@ -160,6 +443,13 @@ struct Spec {
   std::string failure;
   vella_spec_stats stats{};
   cudaEvent_t ev0 = nullptr, ev1 = nullptr, evp = nullptr;  // decode start, end, prefill end
+  void* qrows = nullptr;     // [K][streams][vocab] the draft's logits rows (stochastic acceptance)
+  float2* qstats = nullptr;  // [K][streams] their (max, sum)
+
+  bool sampled() const { return cfg.temperature > 0.0f; }
+  vella_spec_cfg_dev dev_cfg() const {
+    return vella_spec_cfg_dev{cfg.seed, cfg.temperature, cfg.oracle_p, cfg.draft_mode};
+  }
 };
 
 namespace {
@@ -186,6 +476,33 @@ int sync_state(Spec* s) {
 
 PosRef state_pos(Spec* s, int off) { return PosRef{&s->dstate[0].L, off, 0, kStateInts}; }
 
+template <typename T>
+int launch_draft_sample(Spec* s, int i) {
+  const Model* d = s->draft;
+  return launch_kernel(draft_sample_kernel<T>, dim3(s->streams), dim3(kSampThreads), 0, s->stream, s->dstate, s->tok,
+                       static_cast<const T*>(d->logits), i, s->dev_cfg(), s->target->cfg.vocab, s->max_seq,
+                       static_cast<T*>(s->qrows), s->qstats, s->streams);
+}
+
+template <typename T>
+int launch_accept_sampled(Spec* s) {
+  const Model* t = s->target;
+  return launch_kernel(accept_sampled_kernel<T>, dim3(s->streams), dim3(kSampThreads), 0, s->stream, s->dstate,
+                       s->tok, static_cast<const T*>(t->logits), s->cfg.draft_k, s->dev_cfg(), t->cfg.vocab,
+                       s->max_seq, static_cast<const T*>(s->qrows), (const float2*)s->qstats, s->streams,
+                       (const int*)s->ref, (const int*)t->nonfinite, (const int*)t->err, (const int*)s->draft->err);
+}
+
+template <typename T>
+int launch_sample_commit(Spec* s, DevState* st, int* tok, int streams, int first, int sbase) {
+  const Model* t = s->target;
+  return launch_kernel(sample_commit_kernel<T>, dim3(streams), dim3(kSampThreads), 0, s->stream, st, tok,
+                       static_cast<const T*>(t->logits), s->dev_cfg(), t->cfg.vocab, s->max_seq, first, sbase,
+                       (const int*)t->nonfinite, (const int*)t->err);
+}
+
+bool bf16_of(const Spec* s) { return s->target->cfg.dtype == VELLA_BF16; }
+
 int enqueue_pass(Spec* s) {
   Model* t = s->target;
   Model* d = s->draft;
@@ -196,15 +513,20 @@ int enqueue_pass(Spec* s) {
     if ((rc = model_forward(d, state_pos(s, i == 0 ? -2 : i - 1), i == 0 ? 2 : 1, S, 0, s->tok, s->max_seq, Pp, 1,
                             s->stream)))
       return rc;
-    if ((rc = launch_kernel(propose_kernel, dim3(S), dim3(1), 0, s->stream, s->dstate, s->tok, (const int*)d->ys, i,
-                            s->cfg.draft_mode, s->cfg.oracle_p, s->cfg.seed, (const int*)s->ref, t->cfg.vocab,
-                            s->max_seq)))
-      return rc;
+    if (s->sampled() && s->cfg.draft_mode == VELLA_DRAFT_MODEL)
+      rc = bf16_of(s) ? launch_draft_sample<__nv_bfloat16>(s, i) : launch_draft_sample<__half>(s, i);
+    else
+      rc = launch_kernel(propose_kernel, dim3(S), dim3(1), 0, s->stream, s->dstate, s->tok, (const int*)d->ys, i,
+                         s->cfg.draft_mode, s->cfg.oracle_p, s->cfg.seed, (const int*)s->ref, t->cfg.vocab, s->max_seq);
+    if (rc) return rc;
   }
   if ((rc = model_forward(t, state_pos(s, -1), K + 1, S, 0, s->tok, s->max_seq, Pp, K + 1, s->stream))) return rc;
-  if ((rc = launch_kernel(accept_kernel, dim3(S), dim3(1), 0, s->stream, s->dstate, s->tok, (const int*)t->ys, K,
-                          (const int*)t->nonfinite, (const int*)t->err, (const int*)d->err, s->max_seq)))
-    return rc;
+  if (s->sampled())
+    rc = bf16_of(s) ? launch_accept_sampled<__nv_bfloat16>(s) : launch_accept_sampled<__half>(s);
+  else
+    rc = launch_kernel(accept_kernel, dim3(S), dim3(1), 0, s->stream, s->dstate, s->tok, (const int*)t->ys, K,
+                       (const int*)t->nonfinite, (const int*)t->err, (const int*)d->err, s->max_seq);
+  if (rc) return rc;
   // the draft's own logits never gate acceptance; the verify flag was copied into the states
   VELLA_CUDA_TRY(cudaMemsetAsync(d->nonfinite, 0, sizeof(int), s->stream));
   VELLA_CUDA_TRY(cudaMemsetAsync(t->nonfinite, 0, sizeof(int), s->stream));
@@ -216,9 +538,13 @@ int enqueue_greedy(Spec* s) {
   int rc;
   if ((rc = model_forward(t, state_pos(s, -1), 1, s->streams, 0, s->tok, s->max_seq, &s->dstate[0].P, 1, s->stream)))
     return rc;
-  if ((rc = launch_kernel(greedy_commit_kernel, dim3(s->streams), dim3(1), 0, s->stream, s->dstate, s->tok,
-                          (const int*)t->ys, (const int*)t->nonfinite, (const int*)t->err, s->max_seq)))
-    return rc;
+  if (s->sampled())
+    rc = bf16_of(s) ? launch_sample_commit<__nv_bfloat16>(s, s->dstate, s->tok, s->streams, 0, 0)
+                    : launch_sample_commit<__half>(s, s->dstate, s->tok, s->streams, 0, 0);
+  else
+    rc = launch_kernel(greedy_commit_kernel, dim3(s->streams), dim3(1), 0, s->stream, s->dstate, s->tok,
+                       (const int*)t->ys, (const int*)t->nonfinite, (const int*)t->err, s->max_seq);
+  if (rc) return rc;
   VELLA_CUDA_TRY(cudaMemsetAsync(t->nonfinite, 0, sizeof(int), s->stream));
   return VELLA_OK;
 }
@@ -291,6 +617,10 @@ int prefill_all(Spec* s, int quota) {
     if ((rc = run(t, true))) return rc;
     if ((rc = launch_kernel(prefill_finish_kernel, dim3(1), dim3(1), 0, s->stream, &s->dstate[j], tk,
                             (const int*)t->ys, (const int*)t->nonfinite, (const int*)t->err, s->max_seq)))
+      return rc;
+    if (s->sampled() &&
+        (rc = bf16_of(s) ? launch_sample_commit<__nv_bfloat16>(s, &s->dstate[j], tk, 1, 1, j)
+                         : launch_sample_commit<__half>(s, &s->dstate[j], tk, 1, 1, j)))
       return rc;
   }
   VELLA_CUDA_TRY(cudaMemsetAsync(t->nonfinite, 0, sizeof(int), s->stream));
@@ -487,6 +817,7 @@ int vella_spec_create(vella_model* target, vella_model* draft, const vella_spec_
   if (cfg->draft_k < 1 || cfg->draft_k + 1 > kMaxRows)
     return fail(VELLA_E_UNSUPPORTED, "vella_spec_create: draft_k %d (1..%d)", cfg->draft_k, kMaxRows - 1);
   if (cfg->n_eos < 0 || cfg->n_eos > 8) return fail(VELLA_E_INVALID, "vella_spec_create: n_eos %d", cfg->n_eos);
+  if (!(cfg->temperature >= 0.0f)) return fail(VELLA_E_INVALID, "vella_spec_create: temperature %g", cfg->temperature);
   VELLA_CUDA_TRY(cudaSetDevice(target->device));
   vella_spec* s = new vella_spec();
   s->target = target;
@@ -505,6 +836,10 @@ int vella_spec_create(vella_model* target, vella_model* draft, const vella_spec_
   cuda(cudaMallocHost(&s->hstate, S * sizeof(DevState)), "cudaMallocHost(state)");
   cuda(cudaMalloc(&s->tok, S * s->max_seq * sizeof(int)), "cudaMalloc(tokens)");
   cuda(cudaMalloc(&s->ref, S * s->max_seq * sizeof(int)), "cudaMalloc(reference)");
+  if (cfg->temperature > 0.0f && cfg->draft_mode == VELLA_DRAFT_MODEL && draft) {
+    cuda(cudaMalloc(&s->qrows, (size_t)cfg->draft_k * S * target->cfg.vocab * target->elt), "cudaMalloc(draft rows)");
+    cuda(cudaMalloc(&s->qstats, (size_t)cfg->draft_k * S * sizeof(float2)), "cudaMalloc(draft stats)");
+  }
   cuda(cudaEventCreate(&s->ev0), "cudaEventCreate");
   cuda(cudaEventCreate(&s->ev1), "cudaEventCreate");
   cuda(cudaEventCreate(&s->evp), "cudaEventCreate");
@@ -531,6 +866,8 @@ int vella_spec_destroy(vella_spec* s) {
   if (s->hstate) cudaFreeHost(s->hstate);
   if (s->tok) cudaFree(s->tok);
   if (s->ref) cudaFree(s->ref);
+  if (s->qrows) cudaFree(s->qrows);
+  if (s->qstats) cudaFree(s->qstats);
   if (s->ev0) cudaEventDestroy(s->ev0);
   if (s->ev1) cudaEventDestroy(s->ev1);
   if (s->evp) cudaEventDestroy(s->evp);

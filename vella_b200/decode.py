@@ -33,7 +33,7 @@ class ModelCfg(ctypes.Structure):
 class SpecCfg(ctypes.Structure):
     _fields_ = [("draft_k", ctypes.c_int32), ("draft_mode", ctypes.c_int32), ("oracle_p", ctypes.c_float),
                 ("seed", ctypes.c_uint64), ("n_eos", ctypes.c_int32), ("eos", ctypes.c_int32 * 8),
-                ("use_graphs", ctypes.c_int32)]
+                ("use_graphs", ctypes.c_int32), ("temperature", ctypes.c_float)]
 
 
 class SpecStats(ctypes.Structure):
@@ -153,9 +153,10 @@ class SpecDecoder:
     """Draft-and-verify decoding over a target (verifier) and an optional draft model."""
 
     def __init__(self, target: Model, draft: Optional[Model], k: int = 4, mode: int = DRAFT_MODEL,
-                 oracle_p: float = 0.0, seed: int = 0, eos: Sequence[int] = (), use_graphs: bool = True):
+                 oracle_p: float = 0.0, seed: int = 0, eos: Sequence[int] = (), use_graphs: bool = True,
+                 temperature: float = 0.0):
         eos_arr = (ctypes.c_int32 * 8)(*list(eos)[:8])
-        self.cfg = SpecCfg(k, mode, oracle_p, seed, len(list(eos)[:8]), eos_arr, int(use_graphs))
+        self.cfg = SpecCfg(k, mode, oracle_p, seed, len(list(eos)[:8]), eos_arr, int(use_graphs), temperature)
         self.handle = _vp()
         self.target, self.draft = target, draft
         _lib.check(_lib.lib().vella_spec_create(target.handle, draft.handle if draft else None,
