@@ -164,6 +164,8 @@ typedef struct vella_model_cfg {
   float rope_theta;
   int32_t streams;    /* independent sequences held at once (0 or 1: one); each has its own KV
                          cache [max_seq] and prefix buffer [max_prefix] */
+  int32_t rows_per_stream; /* decode rows per stream and forward, logits included (0: 16; up to
+                              64: tree verification needs one row per tree node) */
 } vella_model_cfg;
 
 typedef struct vella_model vella_model;
@@ -216,6 +218,21 @@ typedef struct vella_spec_cfg {
    * steps are drawn from p.  Uniforms are Philox-4x32-10 keyed by `seed`, with counters
    * (pass or step, position, purpose, stream), so a run is reproducible. */
   float temperature;
+  /* Tree verification when tree_depth > 0 (the reference verifies one chain; tree attention
+   * after SpecInfer, Miao et al. 2023): the draft expands a tree depth by depth, node i at
+   * depth d having tree_branching[d] children (nodes in breadth-first order, at most 64 with
+   * the root); with temperature 0 the children are the draft's top-b tokens, with temperature
+   * > 0 b independent samples (the oracle draft: each child the reference token with
+   * probability oracle_p while its ancestors follow the reference, else uniform).  One
+   * target forward verifies every node (each attends to the committed tokens and its own
+   * ancestors); greedy acceptance follows the child equal to the target's argmax, stochastic
+   * acceptance tries the children in order against the running residual; the accepted
+   * path's K/V are moved to consecutive cache slots.  draft_k is ignored.  The target must be
+   * created with rows_per_stream >= the node count.  Greedy tree decoding follows the same
+   * argmax rule as a chain but sums a node's ancestor keys in another order, so its tokens
+   * can differ from a chain decode's where two logits tie to rounding. */
+  int32_t tree_depth;
+  int32_t tree_branching[8];
 } vella_spec_cfg;
 
 typedef struct vella_spec_stats {

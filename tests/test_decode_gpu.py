@@ -435,3 +435,90 @@ def test_sampled_oracle_draft_runs_and_is_reproducible(pair):
         sd.close()
     assert outs[0] == outs[1] and len(outs[0]) == 40
     assert outs[0] != outs[2]
+
+
+def _argmax_consistent(single, pre, toks):
+    """Each token is the target's argmax (teacher forced) or within the logits tolerance of it."""
+    logits = A.bf16_from_bits(single.score(pre, list(toks))).astype(np.float64)
+    for j, t in enumerate(toks):
+        row = logits[j]
+        best = int(np.argmax(row))
+        assert t == best or row[best] - row[t] <= LOGIT_TOL, (j, t, best, row[best] - row[t])
+
+
+@pytest.mark.parametrize("mode", ["oracle", "self"])
+def test_tree_greedy_follows_target_argmax(mode):
+    """Tree verification (branching 3, 2, 2, 1: 33 draft nodes) with greedy acceptance over 4
+    streams: every emitted token is the target's argmax along the emitted sequence, and the
+    accepted paths are long (oracle p = 1 or a draft identical to the target)."""
+    from vella_b200 import decode as VD
+    S, P, n = 4, 20, 40
+    cfg_t = dict(n_layers=2, d_model=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=512, vocab=1000, bits=4,
+                 max_seq=160, max_prefix=128)
+    tb = VD.Model(VD.ModelConfig(**cfg_t, streams=S, rows_per_stream=64))
+    tb.init_random(31, 0.02)
+    if mode == "self":
+        db = VD.Model(VD.ModelConfig(**cfg_t, streams=S))
+        db.init_random(31, 0.02)
+        dd = 256
+    else:
+        db = VD.Model(VD.ModelConfig(1, 128, 2, 1, 64, 256, 1000, bits=0, max_seq=160, max_prefix=128, streams=S))
+        db.init_random(32, 0.05)
+        dd = 128
+    single = VD.Model(VD.ModelConfig(**cfg_t))
+    single.init_random(31, 0.02)
+    pre_t = np.stack([prefix_of(P, 256, 80 + j) for j in range(S)])
+    pre_d = np.stack([prefix_of(P, dd, 90 + j) for j in range(S)]) if mode == "oracle" else pre_t
+    greedy = VD.SpecDecoder(tb, db, k=4)
+    greedy.set_prefix(pre_t, pre_d)
+    ref = greedy.decode_batch(n, VD.DECODE_GREEDY)
+    greedy.close()
+    kw = dict(mode=VD.DRAFT_ORACLE, oracle_p=1.0, seed=3) if mode == "oracle" else dict(mode=VD.DRAFT_MODEL)
+    sd = VD.SpecDecoder(tb, db, k=4, tree=(3, 2, 2, 1), **kw)
+    sd.set_prefix(pre_t, pre_d)
+    if mode == "oracle":
+        sd.set_reference(ref)
+    toks = sd.decode_batch(n, VD.DECODE_SPEC)
+    st = sd.stats()
+    for j in range(S):
+        _argmax_consistent(single, pre_t[j], toks[j])
+    mean_new = sum((i + 1) * c for i, c in enumerate(st["accepted"])) / max(sum(st["accepted"]), 1)
+    assert mean_new > 3.0, st["accepted"]  # tree depth 4: up to 5 tokens per pass
+    sd.close()
+    for m in (tb, db, single):
+        m.close()
+
+
+def test_tree_sampled_tokens_follow_the_target_distribution():
+    """Stochastic tree acceptance (branching 3, 2): over 1024 streams with one prefix, the
+    second token follows the target's softmax (children tried in order against the running
+    residual)."""
+    from vella_b200 import decode as VD
+    S, P, V, T = 1024, 4, 16, 1.0
+    cfg = dict(n_layers=1, d_model=64, n_heads=1, n_kv_heads=1, head_dim=64, ffn=64, vocab=V, bits=0,
+               max_seq=32, max_prefix=8)
+    tb = VD.Model(VD.ModelConfig(**cfg, streams=S, rows_per_stream=16))
+    tb.init_random(41, 0.5)
+    db = VD.Model(VD.ModelConfig(**cfg, streams=S))
+    db.init_random(42, 0.5)
+    single = VD.Model(VD.ModelConfig(**cfg))
+    single.init_random(41, 0.5)
+    pre = prefix_of(P, 64, 43)
+    sb = VD.SpecDecoder(tb, db, k=2, seed=321, temperature=T, tree=(3, 2))
+    sb.set_prefix(np.stack([pre] * S), np.stack([prefix_of(P, 64, 44)] * S))
+    toks = sb.decode_batch(3, VD.DECODE_SPEC)
+    assert toks.min() >= 0 and toks.max() < V
+    p1 = _softmax(A.bf16_from_bits(single.score(pre, [0]))[0].astype(np.float64), T)
+    p2 = np.zeros(V)
+    for t1 in range(V):
+        row = A.bf16_from_bits(single.score(pre, [t1, 0]))[1].astype(np.float64)
+        p2 += p1[t1] * _softmax(row, T)
+    for col, probs in ((0, p1), (1, p2)):
+        counts = np.bincount(toks[:, col], minlength=V).astype(np.float64)
+        stat, cells = _chi2(counts, probs, S)
+        assert stat < 3.0 * cells + 20, (col, stat, cells, counts, probs * S)
+    st = sb.stats()
+    assert st["passes"] > 0 and st["accepted"][0] > 0
+    sb.close()
+    for m in (tb, db, single):
+        m.close()

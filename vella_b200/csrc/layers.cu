@@ -44,18 +44,25 @@ __device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
 template <typename T>
 __global__ void embed_rows_kernel(T* __restrict__ h, const T* __restrict__ table, const T* __restrict__ prefix,
                                   long long prefix_ss, const int* __restrict__ tok, int tok_ss, PosRef pr,
-                                  const int* __restrict__ Pdev, int d, int vocab, int max_seq, int* err) {
+                                  const int* __restrict__ Pdev, int d, int vocab, int max_seq, int* err, TreeView tv) {
   pdl_wait();
   pdl_launch_next();
   const int m = blockIdx.x;
   const int sidx = pr.stream_of(m);
-  const int pos = pr.pos(m);
+  int pos = pr.pos(m);
+  int node = -1;
+  if (tv.tok) {
+    const int r = pr.group ? m % pr.group : m;
+    node = tv.node0 + r;
+    pos = pos - r + tv.dep[node];
+  }
   const int P = Pdev[sidx * pr.stride];
   const T* src;
-  if (pos >= 0 && pos < P) {
+  if (node < 0 && pos >= 0 && pos < P) {
     src = prefix + (size_t)sidx * prefix_ss + (size_t)pos * d;
   } else {
-    int t = (pos >= 0 && pos < max_seq) ? tok[(size_t)sidx * tok_ss + pos] : -1;
+    int t = node >= 0 ? tv.tok[(size_t)sidx * tv.nodes + node]
+                      : ((pos >= 0 && pos < max_seq) ? tok[(size_t)sidx * tok_ss + pos] : -1);
     if (t < 0 || t >= vocab) {
       if (threadIdx.x == 0) atomicOr(err, 1);
       t = 0;
@@ -123,13 +130,24 @@ template <typename T>
 __global__ void rope_append_kernel(const T* __restrict__ qkv, T* __restrict__ q_out, T* __restrict__ kc,
                                    T* __restrict__ vc, const float2* __restrict__ cs, const T* __restrict__ qn,
                                    const T* __restrict__ kn, float eps, PosRef pr, int H, int KV, int hd,
-                                   int max_seq, int* err, long long kv_ss) {
+                                   int max_seq, int* err, long long kv_ss, TreeView tv) {
   using A = Act<T>;
   pdl_wait();
   pdl_launch_next();
   const int m = blockIdx.x, hidx = blockIdx.y, i = threadIdx.x;
   const int half = hd / 2;
-  const int pos = pr.pos(m);
+  int pos = pr.pos(m);   // RoPE position
+  int slot = pos;        // KV-cache slot
+  if (tv.dep) {
+    const int r = pr.group ? m % pr.group : m;
+    const int node = tv.node0 + r;
+    slot = pos - r + node;
+    pos = pos - r + tv.dep[node];
+  }
+  if (slot < 0 || slot >= max_seq) {
+    if (i == 0) atomicOr(err, 2);
+    return;
+  }
   const size_t sbase = (size_t)pr.stream_of(m) * kv_ss;
   if (pos < 0 || pos >= max_seq) {
     if (i == 0) atomicOr(err, 2);
@@ -160,11 +178,11 @@ __global__ void rope_append_kernel(const T* __restrict__ qkv, T* __restrict__ q_
     o[i + half] = A::from_f(y2);
   } else {
     const int kv = hidx - H;
-    T* ko = kc + sbase + ((size_t)kv * max_seq + pos) * hd;
+    T* ko = kc + sbase + ((size_t)kv * max_seq + slot) * hd;
     ko[i] = A::from_f(y1);
     ko[i + half] = A::from_f(y2);
     const T* vs = row + (size_t)(H + KV + kv) * hd;
-    T* vo = vc + sbase + ((size_t)kv * max_seq + pos) * hd;
+    T* vo = vc + sbase + ((size_t)kv * max_seq + slot) * hd;
     vo[i] = vs[i];
     vo[i + half] = vs[i + half];
   }
@@ -222,7 +240,9 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn
   const int mq0 = qb * QB;
   const int nq = min(QB, a.M - mq0);
   const int QR = nq * GQ;
-  const int tmax = a.causal ? pos0 + mq0 + nq : a.S;  // keys needed by the last query of this block
+  // keys needed by the last query of this block (tree mode: pos0 is the root slot, the rows
+  // are nodes tnode0 + mq0 .. and see keys up to their own slot)
+  const int tmax = a.causal ? pos0 + (a.v.tmask ? a.v.tnode0 : 0) + mq0 + nq : a.S;
   const int nact = (tmax + C - 1) / C;
   const int kend = min(tmax, a.S);   // key rows that exist
   const T* q = static_cast<const T*>(a.v.q) + (size_t)bz * a.v.q_bs;
@@ -319,9 +339,19 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn
       for (int i = 0; i < 4; ++i) {
         const int qr = rb + i;
         if (qr < QR) {
-          const int lim = a.causal ? pos0 + mq0 + qr / GQ : a.S - 1;  // last visible key
-          Ps[qr * PS + lane] = (k0 + lane <= lim) ? s[i][0] * a.scale : -INFINITY;
-          Ps[qr * PS + lane + 32] = (k0 + lane + 32 <= lim) ? s[i][1] * a.scale : -INFINITY;
+          bool v0, v1;
+          if (a.v.tmask) {  // committed keys below the root, then the node's ancestors and itself
+            const unsigned long long mk = a.v.tmask[a.v.tnode0 + mq0 + qr / GQ];
+            const int j0 = k0 + lane - pos0, j1 = j0 + 32;
+            v0 = j0 < 0 || (j0 < 64 && ((mk >> j0) & 1ull));
+            v1 = j1 < 0 || (j1 < 64 && ((mk >> j1) & 1ull));
+          } else {
+            const int lim = a.causal ? pos0 + mq0 + qr / GQ : a.S - 1;  // last visible key
+            v0 = k0 + lane <= lim;
+            v1 = k0 + lane + 32 <= lim;
+          }
+          Ps[qr * PS + lane] = v0 ? s[i][0] * a.scale : -INFINITY;
+          Ps[qr * PS + lane + 32] = v1 ? s[i][1] * a.scale : -INFINITY;
         }
       }
     }
@@ -493,15 +523,15 @@ int launch_attn_t(const AttnArgs& a, int batch, cudaStream_t s) {
 
 int launch_embed_rows_dev(int dtype, void* h, const void* table, const void* prefix, long long prefix_ss,
                           const int* tok, int tok_ss, PosRef pr, int rows, const int* P, int d, int vocab, int max_seq,
-                          int* err, cudaStream_t s) {
+                          int* err, cudaStream_t s, TreeView tv) {
   if (rows <= 0) return VELLA_OK;
   if (dtype == VELLA_BF16)
     return launch_kernel(embed_rows_kernel<__nv_bfloat16>, dim3(rows), dim3(256), 0, s, static_cast<__nv_bfloat16*>(h),
                          static_cast<const __nv_bfloat16*>(table), static_cast<const __nv_bfloat16*>(prefix), prefix_ss,
-                         tok, tok_ss, pr, P, d, vocab, max_seq, err);
+                         tok, tok_ss, pr, P, d, vocab, max_seq, err, tv);
   return launch_kernel(embed_rows_kernel<__half>, dim3(rows), dim3(256), 0, s, static_cast<__half*>(h),
                        static_cast<const __half*>(table), static_cast<const __half*>(prefix), prefix_ss, tok, tok_ss,
-                       pr, P, d, vocab, max_seq, err);
+                       pr, P, d, vocab, max_seq, err, tv);
 }
 
 int launch_rmsnorm(int dtype, void* out, const void* x, const void* w, int rows, int d, float eps,
@@ -518,7 +548,7 @@ int launch_rmsnorm(int dtype, void* out, const void* x, const void* w, int rows,
 
 int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* vc, const float2* cs,
                        const void* qn, const void* kn, float eps, PosRef pr, int rows, int H, int KV, int hd,
-                       int max_seq, int* err, cudaStream_t s, long long kv_ss) {
+                       int max_seq, int* err, cudaStream_t s, long long kv_ss, TreeView tv) {
   if (rows <= 0) return VELLA_OK;
   const dim3 grid(rows, H + KV);
   if (dtype == VELLA_BF16)
@@ -526,11 +556,11 @@ int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* 
                          static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(q_out),
                          static_cast<__nv_bfloat16*>(kc), static_cast<__nv_bfloat16*>(vc), cs,
                          static_cast<const __nv_bfloat16*>(qn), static_cast<const __nv_bfloat16*>(kn), eps, pr, H, KV,
-                         hd, max_seq, err, kv_ss);
+                         hd, max_seq, err, kv_ss, tv);
   return launch_kernel(rope_append_kernel<__half>, grid, dim3(hd / 2), 0, s, static_cast<const __half*>(qkv),
                        static_cast<__half*>(q_out), static_cast<__half*>(kc), static_cast<__half*>(vc), cs,
                        static_cast<const __half*>(qn), static_cast<const __half*>(kn), eps, pr, H, KV, hd, max_seq,
-                       err, kv_ss);
+                       err, kv_ss, tv);
 }
 
 int launch_attention_ex(int dtype, const AttnView& v, int batch, PosRef pr, int causal, int rows, int H, int KV,

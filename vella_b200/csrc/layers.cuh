@@ -21,6 +21,20 @@ struct PosRef {
   __device__ int pos(int m) const { return group ? base[(m / group) * stride] + off + m % group : *base + off + m; }
 };
 
+// Tree-mode rows (tree verification and tree drafting): row m of a stream is node
+// n = node0 + (m mod rows per stream) of that stream's draft tree, whose root sits at the
+// PosRef position of the row's stream minus its row index (the tree's root slot R).  The node's
+// token is tok[stream * nodes + n], its RoPE position R + dep[n] and its KV-cache slot R + n;
+// it attends to every key below R and to the tree keys of its ancestors and itself
+// (mask[n] bit j = node j).
+struct TreeView {
+  const int* tok = nullptr;
+  const int* dep = nullptr;
+  const unsigned long long* mask = nullptr;
+  int nodes = 0;
+  int node0 = 0;
+};
+
 constexpr int kAttnChunk = 64;   // keys per chunk (absolute-position aligned)
 constexpr int kAttnRows = 64;    // query rows x query heads per cluster (query block = 64 / GQ rows)
 constexpr int kAttnCluster = 8;  // CTAs per (kv head, query block); chunk c goes to CTA c % 8
@@ -37,6 +51,8 @@ struct AttnView {
   long long q_rs = 0, o_rs = 0;
   long long kv_hs = 0, kv_rs = 0;
   long long q_bs = 0, o_bs = 0, kv_bs = 0;
+  const unsigned long long* tmask = nullptr;  // tree mode: ancestors-or-self mask per node
+  int tnode0 = 0;                             // tree mode: node of row 0 of every batch
 };
 
 // dtype: 0 = bf16, 1 = fp16 everywhere below.
@@ -45,7 +61,7 @@ struct AttnView {
 // of tok[s * tok_ss + p].
 int launch_embed_rows_dev(int dtype, void* h, const void* table, const void* prefix, long long prefix_ss,
                           const int* tok, int tok_ss, PosRef pr, int rows, const int* P, int d, int vocab, int max_seq,
-                          int* err, cudaStream_t s);
+                          int* err, cudaStream_t s, TreeView tv = TreeView{});
 // out row i = RMSNorm(x row src(i)), src(i) = (i / tail) * group + group - tail + i % tail:
 // the last `tail` rows of every `group` rows (group == tail: every row).
 int launch_rmsnorm(int dtype, void* out, const void* x, const void* w, int rows, int d, float eps,
@@ -53,7 +69,7 @@ int launch_rmsnorm(int dtype, void* out, const void* x, const void* w, int rows,
 // RoPE of q/k and K/V append; stream s's cache starts kv_ss elements after stream 0's.
 int launch_rope_append(int dtype, const void* qkv, void* q_out, void* kc, void* vc, const float2* cs,
                        const void* qn, const void* kn, float eps, PosRef pr, int rows, int H, int KV, int hd,
-                       int max_seq, int* err, cudaStream_t s, long long kv_ss = 0);
+                       int max_seq, int* err, cudaStream_t s, long long kv_ss = 0, TreeView tv = TreeView{});
 int launch_attention(int dtype, const void* q, const void* kc, const void* vc, void* out, PosRef pr, int rows,
                      int H, int KV, int hd, int max_seq, float scale, cudaStream_t s);
 // General form: causal (query at position *pr.base + pr.off + m sees keys 0..that) or not

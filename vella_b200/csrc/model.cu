@@ -245,6 +245,8 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
     return fail(VELLA_E_UNSUPPORTED, "vella_model_create: d_model, ffn and n_heads*head_dim must be multiples of 64");
   if (c.max_prefix > c.max_seq) return fail(VELLA_E_INVALID, "vella_model_create: max_prefix > max_seq");
   if (c.streams < 0 || c.streams > 4096) return fail(VELLA_E_INVALID, "vella_model_create: streams %d", c.streams);
+  if (c.rows_per_stream < 0 || c.rows_per_stream > 64)
+    return fail(VELLA_E_INVALID, "vella_model_create: rows_per_stream %d (0..64)", c.rows_per_stream);
   VELLA_CUDA_TRY(cudaSetDevice(device));
   Model* m = new Model();
   m->cfg = c;
@@ -294,7 +296,8 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
   m->kv_ss = (long long)c.n_layers * 2 * KV * c.max_seq * hd;
   m->kv_bytes = (size_t)m->streams * m->kv_ss * e;
   m->prefix_ss = (long long)std::max(c.max_prefix, 1) * d;
-  m->max_rows = std::max(kChunkRows, m->streams * kMaxRows);
+  m->rps = c.rows_per_stream > 0 ? c.rows_per_stream : kMaxRows;
+  m->max_rows = std::max(kChunkRows, m->streams * m->rps);
   // ---- activations and scratch ------------------------------------------------------------
   size_t ws = 0;
   for (const Layer& L : m->layers) {
@@ -306,7 +309,7 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
   }
   ws = std::max(ws, gemm_ws_for(m->lm_head, bits, c.dtype, VELLA_EPI_NONE));
   m->gemm_ws_bytes = ws;
-  const size_t R = m->max_rows, RL = (size_t)m->streams * kMaxRows;
+  const size_t R = m->max_rows, RL = (size_t)m->streams * m->rps;
   const size_t sizes[] = {
       m->kv_bytes,                                  // 0 kv
       (size_t)m->streams * m->prefix_ss * e,        // 1 prefix
@@ -422,7 +425,7 @@ int model_tensor(Model* m, const std::string& name, int layer, void** ptr, size_
   if (name == "embed") return ret(m->embed, (size_t)c.vocab * c.d_model * e);
   if (name == "final_norm") return ret(m->final_norm, (size_t)c.d_model * e);
   if (name == "prefix") return ret(m->prefix, (size_t)m->streams * m->prefix_ss * e);  // [streams][max_prefix][d]
-  if (name == "logits") return ret(m->logits, (size_t)kMaxRows * c.vocab * e);
+  if (name == "logits") return ret(m->logits, (size_t)m->streams * m->rps * c.vocab * e);
   if (name == "kv") return ret(m->kv, m->kv_bytes);
   const size_t dot = name.find('.');
   const std::string head = name.substr(0, dot), part = dot == std::string::npos ? "" : name.substr(dot + 1);
@@ -452,11 +455,11 @@ int model_gemm(Model* m, const QWeight& w, const void* x, int rows, void* out, i
 }
 
 int model_forward(Model* m, PosRef pr, int rows, int streams, int stream0, const int* tok, int tok_ss, const int* P,
-                  int logits_rows, cudaStream_t s) {
+                  int logits_rows, cudaStream_t s, const TreeView* tree) {
   const vella_model_cfg& c = m->cfg;
   const int M = rows * streams;
   if (rows <= 0 || streams <= 0 || stream0 < 0 || stream0 + streams > m->streams || M > m->max_rows ||
-      logits_rows > std::min(rows, kMaxRows) || logits_rows < 0)
+      logits_rows > std::min(rows, m->rps) || logits_rows < 0)
     return fail(VELLA_E_INVALID, "forward: %d rows x %d streams from %d, %d logits rows", rows, streams, stream0,
                 logits_rows);
   const int d = c.d_model, H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, dt = c.dtype;
@@ -465,9 +468,12 @@ int model_forward(Model* m, PosRef pr, int rows, int streams, int stream0, const
   const size_t e = m->elt;
   const char* prefix = static_cast<const char*>(m->prefix) + (size_t)stream0 * m->prefix_ss * e;
   const size_t kv0 = (size_t)stream0 * m->kv_ss * e;
+  const TreeView tv = tree ? *tree : TreeView{};
+  if (tree && (!tree->tok || !tree->dep || !tree->mask || tree->node0 + rows > tree->nodes || tree->nodes > 64))
+    return fail(VELLA_E_INVALID, "forward: tree rows %d from node %d of %d", rows, tree->node0, tree->nodes);
   int rc;
   if ((rc = launch_embed_rows_dev(dt, m->h, m->embed, prefix, m->prefix_ss, tok, tok_ss, pr, M, P, d, c.vocab,
-                                  c.max_seq, m->err, s)))
+                                  c.max_seq, m->err, s, tv)))
     return rc;
   for (int l = 0; l < c.n_layers; ++l) {
     Layer& L = m->layers[l];
@@ -476,7 +482,7 @@ int model_forward(Model* m, PosRef pr, int rows, int streams, int stream0, const
     if ((rc = launch_rmsnorm(dt, m->xn, m->h, L.attn_norm, M, d, c.rms_eps, s))) return rc;
     if ((rc = model_gemm(m, L.qkv, m->xn, M, m->qkv_out, VELLA_EPI_NONE, nullptr, nullptr, s))) return rc;
     if ((rc = launch_rope_append(dt, m->qkv_out, m->q, kc, vc, m->rope, L.q_norm, L.k_norm, c.rms_eps, pr, M, H, KV, hd,
-                                 c.max_seq, m->err, s, m->kv_ss)))
+                                 c.max_seq, m->err, s, m->kv_ss, tv)))
       return rc;
     AttnView v;
     v.q = m->q; v.out = m->attn;
@@ -484,6 +490,7 @@ int model_forward(Model* m, PosRef pr, int rows, int streams, int stream0, const
     v.q_bs = v.o_bs = (long long)rows * H * hd;
     v.k = kc; v.v = vc;
     v.kv_hs = (long long)c.max_seq * hd; v.kv_rs = hd; v.kv_bs = m->kv_ss;
+    v.tmask = tv.mask; v.tnode0 = tv.node0;
     if ((rc = launch_attention_ex(dt, v, streams, pr, 1, rows, H, KV, hd, c.max_seq, scale, s))) return rc;
     if ((rc = model_gemm(m, L.o, m->attn, M, m->h, VELLA_EPI_RESIDUAL, m->h, nullptr, s))) return rc;
     if ((rc = launch_rmsnorm(dt, m->xn, m->h, L.mlp_norm, M, d, c.rms_eps, s))) return rc;

@@ -50,13 +50,14 @@ struct Model {
   long long kv_ss = 0;      // elements between consecutive streams' caches
   void* prefix = nullptr;  // [streams][max_prefix][d]
   long long prefix_ss = 0;  // elements between consecutive streams' prefixes
-  int max_rows = 0;         // rows of the activation buffers (max(kChunkRows, streams * kMaxRows))
+  int rps = kMaxRows;       // decode rows per stream (cfg.rows_per_stream, default kMaxRows)
+  int max_rows = 0;         // rows of the activation buffers (max(kChunkRows, streams * rps))
   float2* rope = nullptr;  // [S][hd/2] (cos, sin)
   // activations and scratch
   void* act_arena = nullptr;
   void *h = nullptr, *xn = nullptr, *qkv_out = nullptr, *q = nullptr, *attn = nullptr, *mlp = nullptr;
-  void* logits = nullptr;  // [streams * kMaxRows, V]
-  int* ys = nullptr;       // [streams * kMaxRows]
+  void* logits = nullptr;  // [streams * rps, V]
+  int* ys = nullptr;       // [streams * rps]
   void* gemm_ws = nullptr;
   size_t gemm_ws_bytes = 0;
   void* argmax_sc = nullptr;
@@ -89,8 +90,9 @@ int model_tensor(Model* m, const std::string& name, int layer, void** ptr, size_
 // from tok (pos >= P) or the stream's prefix embeddings (pos < P).  When logits_rows > 0 the
 // last `logits_rows` rows of every stream go through the final norm and the LM head into
 // m->logits (stream-major) and their argmax into m->ys.
+// With `tree`, the rows are tree nodes (TreeView): pr then gives each stream's root slot.
 int model_forward(Model* m, PosRef pr, int rows, int streams, int stream0, const int* tok, int tok_ss, const int* P,
-                  int logits_rows, cudaStream_t s);
+                  int logits_rows, cudaStream_t s, const TreeView* tree = nullptr);
 
 // GEMM with the model's workspace.
 int model_gemm(Model* m, const QWeight& w, const void* x, int rows, void* out, int epilogue, const void* residual,

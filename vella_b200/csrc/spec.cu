@@ -419,6 +419,278 @@ __global__ void __launch_bounds__(kSampThreads) sample_commit_kernel(DevState* s
   }
 }
 
+// ---- tree drafting and verification ---------------------------------------------------------
+constexpr uint32_t kPurposeTree = 0x7EE01u;
+constexpr int kTreeMaxDepth = 8;
+
+struct TreeTopo {
+  int nodes, depth;
+  int level_start[kTreeMaxDepth + 2];  // first node of each depth; level_start[depth + 1] = nodes
+  const int* dep;                      // [nodes]
+  const int* first_child;              // [nodes]
+  const int* n_child;                  // [nodes]
+};
+
+struct TreePath {  // the accepted path of the last pass, for the KV compaction
+  int root;        // cache slot of the root (node 0)
+  int a;           // accepted nodes
+  int node[16];    // node of depth 1..a
+};
+
+__global__ void tree_root_kernel(const DevState* st, const int* tok, int* ttok, unsigned char* onpath, int N,
+                                 int max_seq) {
+  pdl_wait();
+  pdl_launch_next();
+  const int s = blockIdx.x;
+  ttok[(size_t)s * N] = tok[(size_t)s * max_seq + st[s].L - 1];
+  onpath[(size_t)s * N] = 1;
+}
+
+// Block argmax over v in [0, V) excluding `skip[0..n)`, lowest index on ties.
+template <typename T>
+__device__ int block_argmax_excl(const T* row, int V, const int* skip, int n, SampShared& sh) {
+  float bv = -INFINITY;
+  int bi = INT32_MAX;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    bool ex = false;
+    for (int j = 0; j < n; ++j) ex |= skip[j] == v;
+    if (ex) continue;
+    const float x = Act<T>::to_f(row[v]);
+    if (x > bv || (x == bv && v < bi)) { bv = x; bi = v; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+    sh.part[threadIdx.x >> 5] = bv;
+    sh.red[threadIdx.x >> 5] = __int_as_float(bi);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v0 = -INFINITY;
+    int i0 = INT32_MAX;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      const float ov = sh.part[w];
+      const int oi = __float_as_int(sh.red[w]);
+      if (ov > v0 || (ov == v0 && oi < i0)) { v0 = ov; i0 = oi; }
+    }
+    sh.idx = i0 == INT32_MAX ? 0 : i0;
+  }
+  __syncthreads();
+  return sh.idx;
+}
+
+// Children of the nodes at `depth` (block = one node of one stream): the draft's logits row
+// of the node (row blockIdx.x of the stream's rows at this depth) gives them.
+template <typename T>
+__global__ void __launch_bounds__(kSampThreads) tree_expand_kernel(const DevState* st, const T* logits, int depth,
+                                                                   TreeTopo tt, vella_spec_cfg_dev c, const int* ref,
+                                                                   int* ttok, unsigned char* onpath, int vocab,
+                                                                   int max_seq, T* qrows, float2* qstats, int S) {
+  __shared__ SampShared sh;
+  __shared__ int picked[16];
+  pdl_wait();
+  pdl_launch_next();
+  const int rows = tt.level_start[depth + 1] - tt.level_start[depth];
+  const int node = tt.level_start[depth] + blockIdx.x, s = blockIdx.y;
+  const int nc = tt.n_child[node], fc = tt.first_child[node];
+  if (nc == 0) return;
+  const int N = tt.nodes;
+  const DevState& x = st[s];
+  const T* row = logits + ((size_t)s * rows + blockIdx.x) * vocab;
+  if (c.draft_mode == VELLA_DRAFT_ORACLE) {
+    if (threadIdx.x == 0) {
+      for (int i = 0; i < nc; ++i) {
+        const int ch = fc + i;
+        const int ri = x.L - 1 + tt.dep[ch] - x.P;
+        const bool valid = onpath[(size_t)s * N + node] && ri >= 0 && ri < x.ref_len;
+        const U4 r = philox4x32_10(U4{(uint32_t)x.pass, (uint32_t)ch, kPurposeTree, (uint32_t)s}, (uint32_t)c.seed,
+                                   (uint32_t)(c.seed >> 32));
+        const int rt = valid ? ref[(size_t)s * max_seq + ri] : -1;
+        const int t = (valid && u01(r.x) < c.oracle_p) ? rt : min((int)(u01(r.y) * (float)vocab), vocab - 1);
+        ttok[(size_t)s * N + ch] = t;
+        onpath[(size_t)s * N + ch] = valid && t == rt;
+      }
+    }
+    return;
+  }
+  if (c.temperature <= 0.0f) {  // the draft's top-nc tokens
+    for (int i = 0; i < nc; ++i) {
+      const int t = block_argmax_excl(row, vocab, picked, i, sh);
+      if (threadIdx.x == 0) picked[i] = t;
+      __syncthreads();
+    }
+    if (threadIdx.x == 0)
+      for (int i = 0; i < nc; ++i) ttok[(size_t)s * N + fc + i] = picked[i];
+    return;
+  }
+  // nc independent samples of softmax(row / T); the row is kept for the acceptance test
+  const float invT = 1.0f / c.temperature;
+  const float2 mz = row_softmax_stats(row, vocab, invT, sh);
+  for (int i = 0; i < nc; ++i) {
+    const float u = uni(c, (uint32_t)x.pass, (uint32_t)(fc + i), kPurposeDraft, s);
+    int t = sample_icdf([&](int v) { return expf((Act<T>::to_f(row[v]) - mz.x) * invT); }, vocab, u, sh);
+    if (threadIdx.x == 0) ttok[(size_t)s * N + fc + i] = t < 0 ? 0 : t;
+  }
+  T* q = qrows + ((size_t)node * S + s) * vocab;
+  for (int v = threadIdx.x; v < vocab; v += blockDim.x) q[v] = row[v];
+  if (threadIdx.x == 0) qstats[(size_t)node * S + s] = mz;
+}
+
+// Tree acceptance of stream blockIdx.x over the verify rows of its N nodes.
+template <typename T>
+__global__ void __launch_bounds__(kSampThreads) tree_accept_kernel(
+    DevState* st, int* tok, const T* logits, const int* ys, TreeTopo tt, vella_spec_cfg_dev c, const int* ttok,
+    const unsigned char* onpath, const int* ref, const T* qrows, const float2* qstats, int S, float* resid,
+    TreePath* paths, int vocab, int max_seq, const int* nf, const int* err_t, const int* err_d) {
+  __shared__ SampShared sh;
+  __shared__ int s_u, s_a, s_acc, s_bonus, s_path[16];
+  pdl_wait();
+  pdl_launch_next();
+  const int s = blockIdx.x, N = tt.nodes;
+  DevState& x = st[s];
+  const bool stop = done(x);
+  __syncthreads();
+  if (stop) {
+    if (threadIdx.x == 0) {
+      x.nonfinite = *nf;
+      x.err |= *err_t | *err_d;
+      x.n_new = 0;
+      paths[s].a = 0;
+    }
+    return;
+  }
+  const int root = x.L - 1;
+  const int* tt_s = ttok + (size_t)s * N;
+  if (c.temperature <= 0.0f) {
+    if (threadIdx.x == 0) {
+      int u = 0, a = 0, y = 0;
+      for (;;) {
+        y = ys[(size_t)s * N + u];
+        int found = -1;
+        for (int i = 0; i < tt.n_child[u] && found < 0; ++i)
+          if (tt_s[tt.first_child[u] + i] == y) found = tt.first_child[u] + i;
+        if (found < 0) break;
+        s_path[a++] = found;
+        u = found;
+      }
+      s_a = a;
+      s_bonus = y;
+    }
+  } else {
+    const float invT = 1.0f / c.temperature;
+    float* r = resid + (size_t)s * vocab;
+    if (threadIdx.x == 0) {
+      s_u = 0;
+      s_a = 0;
+    }
+    __syncthreads();
+    for (;;) {
+      const int u = s_u;
+      const T* prow = logits + ((size_t)s * N + u) * vocab;
+      const float2 pm = row_softmax_stats(prow, vocab, invT, sh);
+      for (int v = threadIdx.x; v < vocab; v += blockDim.x) r[v] = expf((Act<T>::to_f(prow[v]) - pm.x) * invT) / pm.y;
+      __syncthreads();
+      DraftQ<T> q{};
+      q.invT = invT;
+      q.vocab = vocab;
+      q.p = c.oracle_p;
+      const int nc = tt.n_child[u], fc = tt.first_child[u];
+      if (c.draft_mode == VELLA_DRAFT_ORACLE) {
+        const int ri = root + tt.dep[u] + 1 - x.P;
+        q.ref = (nc > 0 && onpath[(size_t)s * N + u] && ri >= 0 && ri < x.ref_len) ? ref[(size_t)s * max_seq + ri] : -1;
+      } else if (nc > 0) {
+        q.row = qrows + ((size_t)u * S + s) * vocab;
+        const float2 qm = qstats[(size_t)u * S + s];
+        q.m = qm.x;
+        q.z = qm.y;
+      }
+      int acc = -1;
+      for (int i = 0; i < nc; ++i) {
+        const int ch = fc + i, xk = tt_s[ch];
+        const float uacc = uni(c, (uint32_t)x.pass, (uint32_t)ch, kPurposeAccept, s);
+        if (uacc * q(xk) < r[xk]) {
+          acc = ch;
+          break;
+        }
+        // rejected: the residual max(0, r - q), renormalised
+        float part = 0.0f;
+        for (int v = threadIdx.x; v < vocab; v += blockDim.x) {
+          const float w = fmaxf(0.0f, r[v] - q(v));
+          r[v] = w;
+          part += w;
+        }
+        const float tot = block_sum(part, sh);
+        if (tot > 0.0f)
+          for (int v = threadIdx.x; v < vocab; v += blockDim.x) r[v] /= tot;
+        __syncthreads();
+      }
+      if (acc >= 0) {
+        if (threadIdx.x == 0) {
+          s_path[s_a] = acc;
+          s_a += 1;
+          s_u = acc;
+        }
+        __syncthreads();
+        continue;
+      }
+      const float u2 = uni(c, (uint32_t)x.pass, (uint32_t)u, kPurposeResidual, s);
+      int b = sample_icdf([&](int v) { return r[v]; }, vocab, u2, sh);
+      if (b < 0) b = sample_icdf([&](int v) { return expf((Act<T>::to_f(prow[v]) - pm.x) * invT); }, vocab, u2, sh);
+      if (threadIdx.x == 0) s_bonus = b < 0 ? 0 : b;
+      break;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int a = s_a;
+    int* tk = tok + (size_t)s * max_seq;
+    x.nonfinite = *nf;
+    x.err |= *err_t | *err_d;
+    for (int j = 1; j <= a; ++j) {
+      const int t = tt_s[s_path[j - 1]];
+      if (root + j < max_seq) tk[root + j] = t; else x.err |= 4;
+      x.newtok[j - 1] = t;
+    }
+    if (root + a + 1 < max_seq) tk[root + a + 1] = s_bonus; else x.err |= 4;
+    x.newtok[a] = s_bonus;
+    x.n_new = a + 1;
+    x.L = root + a + 2;
+    x.pass += 1;
+    x.produced += a + 1;
+    TreePath& tp = paths[s];
+    tp.root = root;
+    tp.a = a;
+    for (int j = 0; j < a; ++j) tp.node[j] = s_path[j];
+  }
+}
+
+// Moves the K/V of the accepted path (slots root + node_j) to consecutive slots root + j, in
+// every layer of one model; block = (layer x kv head, stream), thread = head element.
+template <typename T>
+__global__ void tree_compact_kernel(T* kv, const TreePath* paths, int KV, int max_seq, int hd, long long kv_ss) {
+  pdl_wait();
+  pdl_launch_next();
+  const int s = blockIdx.y, l = blockIdx.x / KV, h = blockIdx.x % KV;
+  const TreePath& tp = paths[s];
+  const size_t plane = (size_t)KV * max_seq * hd;
+  T* kb = kv + (size_t)s * kv_ss + (size_t)l * 2 * plane + (size_t)h * max_seq * hd;
+  T* vb = kb + plane;
+  for (int j = 1; j <= tp.a; ++j) {  // ascending: a source is never an earlier destination
+    const int src = tp.root + tp.node[j - 1], dst = tp.root + j;
+    if (src != dst && src < max_seq && dst < max_seq)
+      for (int e = threadIdx.x; e < hd; e += blockDim.x) {
+        kb[(size_t)dst * hd + e] = kb[(size_t)src * hd + e];
+        vb[(size_t)dst * hd + e] = vb[(size_t)src * hd + e];
+      }
+    __syncthreads();
+  }
+}
+
 }  // namespace
 
 struct Spec {
@@ -443,8 +715,19 @@ struct Spec {
   std::string failure;
   vella_spec_stats stats{};
   cudaEvent_t ev0 = nullptr, ev1 = nullptr, evp = nullptr;  // decode start, end, prefill end
-  void* qrows = nullptr;     // [K][streams][vocab] the draft's logits rows (stochastic acceptance)
-  float2* qstats = nullptr;  // [K][streams] their (max, sum)
+  void* qrows = nullptr;     // [K or tree nodes][streams][vocab] the draft's rows (stochastic acceptance)
+  float2* qstats = nullptr;  // [K or tree nodes][streams] their (max, sum)
+  // tree verification (cfg.tree_depth > 0)
+  int tree_nodes = 0;
+  TreeTopo topo{};
+  int* tree_dev = nullptr;                  // dep[N] | first_child[N] | n_child[N]
+  unsigned long long* tree_mask = nullptr;  // [N] ancestors-or-self
+  int* ttok = nullptr;                      // [streams][N] tree tokens
+  unsigned char* onpath = nullptr;          // [streams][N] oracle draft: node follows the reference
+  TreePath* paths = nullptr;                // [streams]
+  float* resid = nullptr;                   // [streams][vocab] running residual (stochastic tree acceptance)
+
+  int span() const { return tree_nodes ? tree_nodes : cfg.draft_k + 1; }  // slots a pass writes from L - 1
 
   bool sampled() const { return cfg.temperature > 0.0f; }
   vella_spec_cfg_dev dev_cfg() const {
@@ -503,7 +786,78 @@ int launch_sample_commit(Spec* s, DevState* st, int* tok, int streams, int first
 
 bool bf16_of(const Spec* s) { return s->target->cfg.dtype == VELLA_BF16; }
 
+TreeView tree_view(Spec* s, int node0) {
+  TreeView v;
+  v.tok = s->ttok;
+  v.dep = s->tree_dev;
+  v.mask = s->tree_mask;
+  v.nodes = s->tree_nodes;
+  v.node0 = node0;
+  return v;
+}
+
+template <typename T>
+int launch_tree_expand(Spec* s, int depth) {
+  const int rows = s->topo.level_start[depth + 1] - s->topo.level_start[depth];
+  return launch_kernel(tree_expand_kernel<T>, dim3(rows, s->streams), dim3(kSampThreads), 0, s->stream,
+                       (const DevState*)s->dstate, static_cast<const T*>(s->draft->logits), depth, s->topo,
+                       s->dev_cfg(), (const int*)s->ref, s->ttok, s->onpath, s->target->cfg.vocab, s->max_seq,
+                       static_cast<T*>(s->qrows), s->qstats, s->streams);
+}
+
+template <typename T>
+int launch_tree_accept(Spec* s) {
+  const Model* t = s->target;
+  return launch_kernel(tree_accept_kernel<T>, dim3(s->streams), dim3(kSampThreads), 0, s->stream, s->dstate, s->tok,
+                       static_cast<const T*>(t->logits), (const int*)t->ys, s->topo, s->dev_cfg(),
+                       (const int*)s->ttok, (const unsigned char*)s->onpath, (const int*)s->ref,
+                       static_cast<const T*>(s->qrows), (const float2*)s->qstats, s->streams, s->resid, s->paths,
+                       t->cfg.vocab, s->max_seq, (const int*)t->nonfinite, (const int*)t->err,
+                       (const int*)s->draft->err);
+}
+
+template <typename T>
+int launch_tree_compact(Spec* s, Model* m) {
+  const vella_model_cfg& c = m->cfg;
+  return launch_kernel(tree_compact_kernel<T>, dim3(c.n_layers * c.n_kv_heads, s->streams), dim3(c.head_dim), 0,
+                       s->stream, static_cast<T*>(m->kv), (const TreePath*)s->paths, c.n_kv_heads, c.max_seq,
+                       c.head_dim, m->kv_ss);
+}
+
+// One tree pass: the draft expands the tree depth by depth (step 0 over the two committed
+// positions L-2, L-1 gives the root's children; step k over the nodes of depth k), the target
+// verifies every node in one forward, the acceptance walks the tree, and the accepted path's
+// K/V move to consecutive slots in both models.
+int enqueue_tree_pass(Spec* s) {
+  Model* t = s->target;
+  Model* d = s->draft;
+  const int S = s->streams, N = s->tree_nodes, D = s->topo.depth;
+  const int* Pp = &s->dstate[0].P;
+  const bool bf = bf16_of(s);
+  int rc;
+  if ((rc = launch_kernel(tree_root_kernel, dim3(S), dim3(1), 0, s->stream, (const DevState*)s->dstate,
+                          (const int*)s->tok, s->ttok, s->onpath, N, s->max_seq)))
+    return rc;
+  if ((rc = model_forward(d, state_pos(s, -2), 2, S, 0, s->tok, s->max_seq, Pp, 1, s->stream))) return rc;
+  if ((rc = bf ? launch_tree_expand<__nv_bfloat16>(s, 0) : launch_tree_expand<__half>(s, 0))) return rc;
+  for (int k = 1; k < D; ++k) {
+    const int rows = s->topo.level_start[k + 1] - s->topo.level_start[k];
+    const TreeView tv = tree_view(s, s->topo.level_start[k]);
+    if ((rc = model_forward(d, state_pos(s, -1), rows, S, 0, s->tok, s->max_seq, Pp, rows, s->stream, &tv))) return rc;
+    if ((rc = bf ? launch_tree_expand<__nv_bfloat16>(s, k) : launch_tree_expand<__half>(s, k))) return rc;
+  }
+  const TreeView tv = tree_view(s, 0);
+  if ((rc = model_forward(t, state_pos(s, -1), N, S, 0, s->tok, s->max_seq, Pp, N, s->stream, &tv))) return rc;
+  if ((rc = bf ? launch_tree_accept<__nv_bfloat16>(s) : launch_tree_accept<__half>(s))) return rc;
+  if ((rc = bf ? launch_tree_compact<__nv_bfloat16>(s, t) : launch_tree_compact<__half>(s, t))) return rc;
+  if ((rc = bf ? launch_tree_compact<__nv_bfloat16>(s, d) : launch_tree_compact<__half>(s, d))) return rc;
+  VELLA_CUDA_TRY(cudaMemsetAsync(d->nonfinite, 0, sizeof(int), s->stream));
+  VELLA_CUDA_TRY(cudaMemsetAsync(t->nonfinite, 0, sizeof(int), s->stream));
+  return VELLA_OK;
+}
+
 int enqueue_pass(Spec* s) {
+  if (s->tree_nodes) return enqueue_tree_pass(s);
   Model* t = s->target;
   Model* d = s->draft;
   const int K = s->cfg.draft_k, S = s->streams;
@@ -679,7 +1033,7 @@ int decode_mtp(Spec* s, int max_tokens, Decoded* out) {
   out->tokens.push_back(t);
   const int K = s->cfg.draft_k;
   while ((int)out->tokens.size() < max_tokens) {
-    if (s->hstate->L + K + 1 > s->max_seq) {
+    if (s->hstate->L - 1 + s->span() > s->max_seq) {
       out->capacity = true;
       return VELLA_OK;
     }
@@ -818,6 +1172,48 @@ int vella_spec_create(vella_model* target, vella_model* draft, const vella_spec_
     return fail(VELLA_E_UNSUPPORTED, "vella_spec_create: draft_k %d (1..%d)", cfg->draft_k, kMaxRows - 1);
   if (cfg->n_eos < 0 || cfg->n_eos > 8) return fail(VELLA_E_INVALID, "vella_spec_create: n_eos %d", cfg->n_eos);
   if (!(cfg->temperature >= 0.0f)) return fail(VELLA_E_INVALID, "vella_spec_create: temperature %g", cfg->temperature);
+  // tree topology (breadth-first): dep, parent mask, children ranges, level starts
+  std::vector<int> dep, fch, nch;
+  std::vector<unsigned long long> mask;
+  TreeTopo topo{};
+  if (cfg->tree_depth != 0) {
+    if (!draft) return fail(VELLA_E_UNSUPPORTED, "vella_spec_create: tree verification needs a draft model");
+    if (cfg->tree_depth < 1 || cfg->tree_depth > kTreeMaxDepth)
+      return fail(VELLA_E_UNSUPPORTED, "vella_spec_create: tree_depth %d (1..%d)", cfg->tree_depth, kTreeMaxDepth);
+    dep = {0};
+    mask = {1ull};
+    std::vector<int> parent = {-1};
+    topo.depth = cfg->tree_depth;
+    topo.level_start[0] = 0;
+    topo.level_start[1] = 1;
+    int maxlevel = 1;
+    for (int k = 1; k <= topo.depth; ++k) {
+      const int b = cfg->tree_branching[k - 1];
+      if (b < 1 || b > 16) return fail(VELLA_E_INVALID, "vella_spec_create: tree_branching[%d] = %d", k - 1, b);
+      for (int p = topo.level_start[k - 1]; p < topo.level_start[k]; ++p)
+        for (int i = 0; i < b; ++i) {
+          const int n = (int)dep.size();
+          if (n >= 64) return fail(VELLA_E_UNSUPPORTED, "vella_spec_create: more than 64 tree nodes");
+          dep.push_back(k);
+          parent.push_back(p);
+          mask.push_back(mask[p] | (1ull << n));
+        }
+      topo.level_start[k + 1] = (int)dep.size();
+      maxlevel = std::max(maxlevel, topo.level_start[k + 1] - topo.level_start[k]);
+    }
+    const int N = (int)dep.size();
+    topo.nodes = N;
+    fch.assign(N, 0);
+    nch.assign(N, 0);
+    for (int n = N - 1; n >= 1; --n) {
+      fch[parent[n]] = n;  // the lowest child index, scanning downwards
+      nch[parent[n]] += 1;
+    }
+    if (target->rps < N)
+      return fail(VELLA_E_INVALID, "vella_spec_create: the target needs rows_per_stream >= %d tree nodes", N);
+    if (draft->rps < std::max(2, maxlevel))
+      return fail(VELLA_E_INVALID, "vella_spec_create: the draft needs rows_per_stream >= %d", std::max(2, maxlevel));
+  }
   VELLA_CUDA_TRY(cudaSetDevice(target->device));
   vella_spec* s = new vella_spec();
   s->target = target;
@@ -836,9 +1232,34 @@ int vella_spec_create(vella_model* target, vella_model* draft, const vella_spec_
   cuda(cudaMallocHost(&s->hstate, S * sizeof(DevState)), "cudaMallocHost(state)");
   cuda(cudaMalloc(&s->tok, S * s->max_seq * sizeof(int)), "cudaMalloc(tokens)");
   cuda(cudaMalloc(&s->ref, S * s->max_seq * sizeof(int)), "cudaMalloc(reference)");
+  const size_t qn = topo.nodes ? (size_t)topo.nodes : (size_t)cfg->draft_k;
   if (cfg->temperature > 0.0f && cfg->draft_mode == VELLA_DRAFT_MODEL && draft) {
-    cuda(cudaMalloc(&s->qrows, (size_t)cfg->draft_k * S * target->cfg.vocab * target->elt), "cudaMalloc(draft rows)");
-    cuda(cudaMalloc(&s->qstats, (size_t)cfg->draft_k * S * sizeof(float2)), "cudaMalloc(draft stats)");
+    cuda(cudaMalloc(&s->qrows, qn * S * target->cfg.vocab * target->elt), "cudaMalloc(draft rows)");
+    cuda(cudaMalloc(&s->qstats, qn * S * sizeof(float2)), "cudaMalloc(draft stats)");
+  }
+  if (topo.nodes) {
+    const int N = topo.nodes;
+    s->tree_nodes = N;
+    s->topo = topo;
+    cuda(cudaMalloc(&s->tree_dev, 3 * (size_t)N * sizeof(int)), "cudaMalloc(tree)");
+    cuda(cudaMalloc(&s->tree_mask, (size_t)N * sizeof(unsigned long long)), "cudaMalloc(tree mask)");
+    cuda(cudaMalloc(&s->ttok, S * N * sizeof(int)), "cudaMalloc(tree tokens)");
+    cuda(cudaMalloc(&s->onpath, S * N), "cudaMalloc(tree path flags)");
+    cuda(cudaMalloc(&s->paths, S * sizeof(TreePath)), "cudaMalloc(tree paths)");
+    if (cfg->temperature > 0.0f)
+      cuda(cudaMalloc(&s->resid, S * target->cfg.vocab * sizeof(float)), "cudaMalloc(residual)");
+    if (rc == VELLA_OK) {
+      std::vector<int> host(3 * (size_t)N);
+      std::copy(dep.begin(), dep.end(), host.begin());
+      std::copy(fch.begin(), fch.end(), host.begin() + N);
+      std::copy(nch.begin(), nch.end(), host.begin() + 2 * N);
+      cuda(cudaMemcpy(s->tree_dev, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice), "cudaMemcpy");
+      cuda(cudaMemcpy(s->tree_mask, mask.data(), N * sizeof(unsigned long long), cudaMemcpyHostToDevice), "cudaMemcpy");
+      cuda(cudaMemset(s->paths, 0, S * sizeof(TreePath)), "cudaMemset");
+      s->topo.dep = s->tree_dev;
+      s->topo.first_child = s->tree_dev + N;
+      s->topo.n_child = s->tree_dev + 2 * N;
+    }
   }
   cuda(cudaEventCreate(&s->ev0), "cudaEventCreate");
   cuda(cudaEventCreate(&s->ev1), "cudaEventCreate");
@@ -868,6 +1289,9 @@ int vella_spec_destroy(vella_spec* s) {
   if (s->ref) cudaFree(s->ref);
   if (s->qrows) cudaFree(s->qrows);
   if (s->qstats) cudaFree(s->qstats);
+  for (void* p : {(void*)s->tree_dev, (void*)s->tree_mask, (void*)s->ttok, (void*)s->onpath, (void*)s->paths,
+                  (void*)s->resid})
+    if (p) cudaFree(p);
   if (s->ev0) cudaEventDestroy(s->ev0);
   if (s->ev1) cudaEventDestroy(s->ev1);
   if (s->evp) cudaEventDestroy(s->evp);
@@ -925,7 +1349,7 @@ int vella_spec_step(vella_spec* s, int32_t* out_tokens, int32_t* n_out) {
   if (!s || !out_tokens || !n_out) return fail(VELLA_E_INVALID, "vella_spec_step: NULL argument");
   if (!s->draft) return fail(VELLA_E_UNSUPPORTED, "vella_spec_step: no draft model");
   if (s->hstate->L < s->P + 1) return fail(VELLA_E_INVALID, "vella_spec_step: prefill first");
-  if (s->hstate->L + s->cfg.draft_k + 1 > s->max_seq) return fail(VELLA_E_INVALID, "vella_spec_step: KV capacity reached");
+  if (s->hstate->L - 1 + s->span() > s->max_seq) return fail(VELLA_E_INVALID, "vella_spec_step: KV capacity reached");
   if (s->streams != 1) return fail(VELLA_E_UNSUPPORTED, "vella_spec_step: %d streams (use vella_spec_decode_batch)", s->streams);
   VELLA_CUDA_TRY(cudaSetDevice(s->device));
   const int rc = run_unit(s, true);
@@ -1017,10 +1441,9 @@ int vella_spec_decode_batch(vella_spec* s, int32_t mode, int32_t max_tokens, int
   if (mode != VELLA_DECODE_SPEC && mode != VELLA_DECODE_GREEDY)
     return fail(VELLA_E_INVALID, "vella_spec_decode_batch: mode %d (SPEC or GREEDY)", mode);
   if (mode == VELLA_DECODE_SPEC && !s->draft) return fail(VELLA_E_UNSUPPORTED, "vella_spec_decode_batch: no draft model");
-  const int K = s->cfg.draft_k;
-  if (max_tokens < 1 || s->P + max_tokens + K + 1 > s->max_seq)
+  if (max_tokens < 1 || s->P + max_tokens + s->span() > s->max_seq)
     return fail(VELLA_E_INVALID, "vella_spec_decode_batch: prefix %d + %d tokens (+%d) exceed max_seq %d", s->P,
-                max_tokens, K + 1, s->max_seq);
+                max_tokens, s->span(), s->max_seq);
   VELLA_CUDA_TRY(cudaSetDevice(s->device));
   VELLA_CUDA_TRY(cudaEventRecord(s->ev0, s->stream));
   int rc;

@@ -27,13 +27,15 @@ class ModelCfg(ctypes.Structure):
                 ("n_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("ffn", ctypes.c_int32),
                 ("vocab", ctypes.c_int32), ("bits", ctypes.c_int32), ("dtype", ctypes.c_int32),
                 ("qk_norm", ctypes.c_int32), ("max_seq", ctypes.c_int32), ("max_prefix", ctypes.c_int32),
-                ("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float), ("streams", ctypes.c_int32)]
+                ("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float), ("streams", ctypes.c_int32),
+                ("rows_per_stream", ctypes.c_int32)]
 
 
 class SpecCfg(ctypes.Structure):
     _fields_ = [("draft_k", ctypes.c_int32), ("draft_mode", ctypes.c_int32), ("oracle_p", ctypes.c_float),
                 ("seed", ctypes.c_uint64), ("n_eos", ctypes.c_int32), ("eos", ctypes.c_int32 * 8),
-                ("use_graphs", ctypes.c_int32), ("temperature", ctypes.c_float)]
+                ("use_graphs", ctypes.c_int32), ("temperature", ctypes.c_float), ("tree_depth", ctypes.c_int32),
+                ("tree_branching", ctypes.c_int32 * 8)]
 
 
 class SpecStats(ctypes.Structure):
@@ -93,11 +95,12 @@ class ModelConfig:
     rms_eps: float = 1e-6
     rope_theta: float = 1e6
     streams: int = 1
+    rows_per_stream: int = 16
 
     def c(self) -> ModelCfg:
         return ModelCfg(self.n_layers, self.d_model, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn,
                         self.vocab, self.bits, self.dtype, int(self.qk_norm), self.max_seq, self.max_prefix,
-                        self.rms_eps, self.rope_theta, self.streams)
+                        self.rms_eps, self.rope_theta, self.streams, self.rows_per_stream)
 
 
 class Model:
@@ -154,9 +157,11 @@ class SpecDecoder:
 
     def __init__(self, target: Model, draft: Optional[Model], k: int = 4, mode: int = DRAFT_MODEL,
                  oracle_p: float = 0.0, seed: int = 0, eos: Sequence[int] = (), use_graphs: bool = True,
-                 temperature: float = 0.0):
+                 temperature: float = 0.0, tree: Sequence[int] = ()):
         eos_arr = (ctypes.c_int32 * 8)(*list(eos)[:8])
-        self.cfg = SpecCfg(k, mode, oracle_p, seed, len(list(eos)[:8]), eos_arr, int(use_graphs), temperature)
+        br = (ctypes.c_int32 * 8)(*list(tree)[:8])
+        self.cfg = SpecCfg(k, mode, oracle_p, seed, len(list(eos)[:8]), eos_arr, int(use_graphs), temperature,
+                           len(list(tree)[:8]), br)
         self.handle = _vp()
         self.target, self.draft = target, draft
         _lib.check(_lib.lib().vella_spec_create(target.handle, draft.handle if draft else None,
