@@ -87,17 +87,21 @@ struct QgemmPlan {
   int zchunks;    // ceil(M / 16)
   size_t workspace;
   bool stream = false;  // persistent bulk-copy kernel (qgemm_stream.cu)
-  int ctas = 0;         // its grid (one CTA per SM)
+  int ctas = 0;         // its grid (one CTA per SM, or two with `light`)
+  bool light = false;   // two 96-register CTAs per SM (int4 calls with many units)
   bool tc = false;      // tensor-core kernel for M > 16 (tc_gemm.cu)
 };
 
 // qgemm_stream.cu
 bool stream_eligible(const vella_qgemm_desc& d);
 int stream_units(const vella_qgemm_desc& d, int* rowblocks, int* nkc);
+// True when the call runs two CTAs per SM; depends on (N, K, format, SM count) only.
+bool stream_light(const vella_qgemm_desc& d, int rowblocks, int nkc, int sms);
 size_t stream_partial_bytes(int P);
-int stream_launch(const vella_qgemm_desc& d, int P, const void* x, const void* w, const void* scales,
+int stream_flag_count(int P);  // ints of the flag region (zero between calls)
+int stream_launch(const vella_qgemm_desc& d, int P, bool light, const void* x, const void* w, const void* scales,
                   const void* biases, const void* up_w, const void* up_scales, const void* up_biases,
-                  const void* bias, const void* residual, void* out, int* counters, float* partial,
+                  const void* bias, const void* residual, void* out, int* flags, float* partial,
                   cudaStream_t stream);
 int stream_fault_status(int clear);
 

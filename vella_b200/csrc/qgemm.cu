@@ -461,9 +461,11 @@ bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* p) {
     stream_units(d, &rb, &nkc);
     p->stream = true;
     // one CTA per SM, but never more CTAs than units: every CTA owns at least one unit
-    p->ctas = (int)std::min<long long>(num_sms(dev), (long long)rb * nkc);
+    const int sms = num_sms(dev);
+    p->light = stream_light(d, rb, nkc, sms);
+    p->ctas = (int)std::min<long long>((p->light ? 2 : 1) * (long long)sms, (long long)rb * nkc);
     p->rowblocks = rb;
-    p->workspace = counter_region((size_t)rb) + stream_partial_bytes(p->ctas);
+    p->workspace = counter_region((size_t)stream_flag_count(p->ctas)) + stream_partial_bytes(p->ctas);
     return true;
   }
   if (p->splits > 1) {
@@ -482,9 +484,9 @@ int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& p, const void* x, c
   if (d.m == 0 || d.n == 0) return VELLA_OK;
   if (p.tc) return tc_launch(d, x, w, scales, biases, up_w, up_scales, up_biases, bias, residual, out, stream);
   if (p.stream) {
-    int* counters = static_cast<int*>(ws);
-    float* partial = reinterpret_cast<float*>(static_cast<char*>(ws) + counter_region((size_t)p.rowblocks));
-    return stream_launch(d, p.ctas, x, w, scales, biases, up_w, up_scales, up_biases, bias, residual, out, counters,
+    int* flags = static_cast<int*>(ws);
+    float* partial = reinterpret_cast<float*>(static_cast<char*>(ws) + counter_region((size_t)stream_flag_count(p.ctas)));
+    return stream_launch(d, p.ctas, p.light, x, w, scales, biases, up_w, up_scales, up_biases, bias, residual, out, flags,
                          partial, stream);
   }
   Args a{};

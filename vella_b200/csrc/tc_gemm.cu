@@ -153,7 +153,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   constexpr uint32_t IDESC = f16_idesc(A::kMagic == 128.0f, kTcRows, kTcTok);
 
   extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // (offsetting the shared array itself keeps its address space: shared loads, not generic ones)
+  unsigned char* smem = smem_raw + ((1024u - (saddr(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + LY::BAR);
   uint64_t* ready = full + NS;
   uint64_t* empty = ready + NS;
