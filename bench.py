@@ -250,6 +250,10 @@ PREFIX, NEW_TOKENS = 750, 448
 SWEEP = [(4, 0.5), (4, 0.7), (4, 0.9), (8, 0.5), (8, 0.7), (8, 0.9)]
 HEADLINE = (4, 0.7)
 BATCH_STREAMS = 32  # streams per GPU of the batched measurement
+# Tree verification with stochastic acceptance: 256 streams over the box's 8 GPUs, i.e. 32 per
+# GPU; branching 3 at depth 1, then 2, 2, 1 (33 draft nodes + the root = 34 verify rows per
+# stream); temperature 0.7; the real (random-init) draft model proposes.
+TREE_STREAMS, TREE_BRANCHING, TREE_TEMPERATURE, TREE_TOKENS = 32, (3, 2, 2, 1), 0.7, 64
 
 
 def expected_tokens_per_pass(k, p):
@@ -478,6 +482,12 @@ def run_spec(args, rank, world):
     draft.close()
     if not args.no_batched:
         line["batched"] = run_spec_batched(rank, local, BATCH_STREAMS, k, p)
+        line["batched"]["tokens_per_s_all_gpus"] = round(
+            world * BATCH_STREAMS * (NEW_TOKENS - 1) / dist_max(dist, line["batched"]["decode_ms"] / 1e3, dev), 1)
+    if not args.no_tree:
+        line["tree"] = run_spec_tree(rank, local, TREE_STREAMS, TREE_BRANCHING, TREE_TEMPERATURE, TREE_TOKENS)
+        line["tree"]["tokens_per_s_all_gpus"] = round(
+            world * line["tree"]["tokens"] / dist_max(dist, line["tree"]["decode_ms"] / 1e3, dev), 1)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -522,6 +532,62 @@ def run_spec_batched(rank, local, S, k, p):
            "prefill_ms_all_streams": round(st["last_prefill_ms"], 1),
            "bit_exact_vs_batched_greedy": bool(np.array_equal(spec, greedy)),
            "note": "decode-only device time; verify rows per pass = streams x (k+1) on the tensor cores"}
+    sd.close()
+    target.close()
+    draft.close()
+    return out
+
+
+def run_spec_tree(rank, local, S, branching, temperature, new_tokens):
+    """S streams per GPU decoded with tree verification and stochastic acceptance: per pass
+    the draft expands the tree depth by depth (one batched draft forward per depth, children
+    sampled from the draft's softmax at `temperature`), the target verifies every stream's
+    whole tree in one forward (S x (nodes + 1) rows, tree-attention masks), and each stream
+    accepts along the tree by rejection sampling against the running residual (Philox
+    uniforms per pass/node/stream).  Random-init weights: the acceptance rate is whatever the
+    two random models' softmaxes give, reported beside the throughput."""
+    import torch
+    from vella_b200 import _lib as L
+    from vella_b200 import decode as VD
+    nodes = 0
+    width = 1
+    for b in branching:
+        width *= b
+        nodes += width
+    rows = nodes + 1
+    max_seq = PREFIX + new_tokens + 2 * rows + 16
+    tc = VD.ModelConfig(**TARGET, max_seq=max_seq, max_prefix=PREFIX, rope_theta=1e6, streams=S,
+                        rows_per_stream=rows)
+    dc = VD.ModelConfig(**DRAFT, max_seq=max_seq, max_prefix=PREFIX, rope_theta=1e6, streams=S)
+    target = VD.Model(tc, local)
+    target.init_random(1, 0.02)
+    draft = VD.Model(dc, local)
+    draft.init_random(2, 0.02)
+    fill = L.lib().vella_fill_normal
+    for m, dd, tid in ((target, TARGET["d_model"], 31), (draft, DRAFT["d_model"], 32)):
+        ptr, _ = m.tensor("prefix")
+        L.check(fill(ptr, S * PREFIX * dd, L.BF16, 5 + rank, tid, 0.0, 1.0, None))
+    torch.cuda.synchronize()
+    sd = VD.SpecDecoder(target, draft, k=len(branching), mode=VD.DRAFT_MODEL, seed=11 + rank,
+                        temperature=temperature, tree=branching)
+    sd.set_prefix(None, None, PREFIX)
+    sd.decode_batch(new_tokens, VD.DECODE_SPEC)  # warm-up: prefill, graph capture
+    st0 = sd.stats()
+    out_toks = sd.decode_batch(new_tokens, VD.DECODE_SPEC)
+    st = sd.stats()
+    passes = st["passes"] - st0["passes"]
+    hist = [a - b for a, b in zip(st["accepted"], st0["accepted"])]
+    tokens = S * (new_tokens - 1)  # each stream's first token comes from its prefill
+    sampled = int(out_toks.size)
+    out = {"streams_per_gpu": S, "streams_all_gpus_at_8": 8 * S, "branching": list(branching),
+           "draft_nodes": nodes, "verify_rows_per_pass": S * rows, "temperature": temperature,
+           "draft": "bf16 draft model, random init (children sampled from its softmax)",
+           "new_tokens_per_stream": new_tokens, "tokens": tokens,
+           "tokens_per_s": round(tokens / (st["last_decode_ms"] / 1e3), 1),
+           "passes": passes, "tokens_per_stream_pass": round(tokens / max(passes * S, 1), 3),
+           "accepted_hist": hist[:len(branching) + 1], "decode_ms": round(st["last_decode_ms"], 1),
+           "prefill_ms_all_streams": round(st["last_prefill_ms"], 1), "tokens_checked": sampled,
+           "note": "decode-only device time; 32 streams per GPU is the 8-GPU share of 256 streams"}
     sd.close()
     target.close()
     draft.close()
@@ -805,6 +871,7 @@ def main():
     ap.add_argument("--impl", default="vella", choices=["vella", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="spec workload: skip the multi-stream measurement")
+    ap.add_argument("--no-tree", action="store_true", help="spec workload: skip the tree + sampling measurement")
     ap.add_argument("--shape", default="", help="gemm workload: one case 'bits,N,K,M' instead of the sweep")
     ap.add_argument("--profile-pass", action="store_true", help="short run for an ncu launch list")
     args = ap.parse_args()
