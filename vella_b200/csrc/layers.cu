@@ -189,14 +189,20 @@ __global__ void rope_append_kernel(const T* __restrict__ qkv, T* __restrict__ q_
 }
 
 // ---------------------------------------------------------------------------------------
-// Decode attention.  One thread-block cluster of kAttnCluster CTAs per (kv head, query
-// block).  Keys are cut into chunks of kAttnChunk at absolute positions and chunk c is
-// processed by CTA c % kAttnCluster, which keeps a running (max, sum, output) per query
-// row over its chunks in chunk order (fp32 scores and probabilities).  The CTAs then
-// combine their partial rows through distributed shared memory in rank order.  Query at
-// position p sees keys 0..p; a chunk with no visible key leaves a row's state unchanged
-// bit for bit (scale exp(0) = 1, added terms exact zeros), so a row's result does not
-// depend on the other rows of the launch.
+// Attention on the tensor cores (mma.sync m16n8k16, fp32 accumulation).  One thread-block
+// cluster of kAttnCluster CTAs per (kv head, query block, batch); a query block is up to 64
+// "head rows" (query rows x the GQ query heads of the kv head), 16 per warp.  Keys are cut
+// into chunks of kAttnChunk at absolute positions and chunk c is processed by CTA
+// c % kAttnCluster, which keeps a running (max, sum, output) per head row over its chunks in
+// chunk order: S = Q.K^T on the tensor cores, scale and mask in fp32, the online softmax in
+// fp32, and O += P.V with P split into two activation-dtype terms (P = hi + lo, both
+// multiplied on the tensor cores), so P keeps about 16 significant bits.  The CTAs then
+// combine their partial rows through distributed shared memory in rank order.  The query at
+// position p sees keys 0..p (tree mode: the keys below the root slot plus its ancestors and
+// itself); a chunk with no visible key leaves a row's state unchanged bit for bit (scale
+// exp(0) = 1, added terms exact zeros), and every row's arithmetic is independent of the
+// other rows of the launch.  K/V chunks travel by cp.async into a double buffer; keys past
+// the last needed one are zero-filled (stale cache rows are never multiplied).
 // ---------------------------------------------------------------------------------------
 struct AttnArgs {
   AttnView v;
@@ -208,34 +214,73 @@ struct AttnArgs {
   float scale;
 };
 
+template <int HD>
+struct AttnLayout {
+  static constexpr int RS = HD + 8;                         // padded row stride (elements): ldmatrix conflict-free
+  static constexpr int TILE = kAttnChunk * RS * 2;           // one [64 x HD] activation tile (bytes)
+  static constexpr int Q_OFF = 0, K_OFF = TILE, V_OFF = 3 * TILE;  // Q, K[2], V[2]
+  static constexpr int OS = HD + 4;                          // combine: fp32 row stride
+  static constexpr int BYTES = 5 * TILE + 2 * kAttnRows * 4;  // + running max / sum per row
+  static_assert(kAttnRows * OS * 4 <= 4 * TILE, "combine rows fit over the K/V buffers");
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ldsm4t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (sizeof(T) == 2 && Act<T>::kMagic == 128.0f) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  } else {
+    const __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
+}
+
 template <typename T, int HD>
-__global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn_kernel(const AttnArgs a) {
+__global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(128) attn_kernel(const AttnArgs a) {
+  using LY = AttnLayout<HD>;
   constexpr int C = kAttnChunk;
   constexpr int CS = kAttnCluster;
-  constexpr int KS = HD + 4;  // padded fp32 row stride of K/V/Q/O in shared memory
-  constexpr int PS = C + 4;
-  constexpr int V8 = HD / 8;            // 16-byte vectors per key row
-  constexpr int LDI = C * V8 / 256;     // vectors of K (and of V) per thread and chunk
-  static_assert(LDI * 256 == C * V8, "chunk loads must tile the block");
-  extern __shared__ __align__(16) float sm[];
-  const int GQ = a.H / a.KV;
-  const int QB = a.QB;
-  constexpr int QRmax = kAttnRows;
-  float* Ks = sm;
-  float* Vs = Ks + C * KS;
-  float* Qs = Vs + C * KS;
-  float* Os = Qs + QRmax * KS;
-  float* Ps = Os + QRmax * KS;
-  float* Mx = Ps + QRmax * PS;  // running max per row
-  float* Ls = Mx + QRmax;       // running sum of probabilities
-  float* Al = Ls + QRmax;       // rescale factor of the current chunk
+  constexpr int RS = LY::RS;
+  constexpr int NK = HD / 16;  // k16 steps of Q.K^T
+  constexpr int ND = HD / 8;   // n8 tiles of the output
+  extern __shared__ __align__(128) unsigned char asmem[];
+  T* Qs = reinterpret_cast<T*>(asmem + LY::Q_OFF);
+  T* Ks = reinterpret_cast<T*>(asmem + LY::K_OFF);
+  T* Vs = reinterpret_cast<T*>(asmem + LY::V_OFF);
+  float* Mx = reinterpret_cast<float*>(asmem + 5 * LY::TILE);
+  float* Ls = Mx + kAttnRows;
+  float* Os = reinterpret_cast<float*>(asmem + LY::K_OFF);  // combine: reuses the K/V buffers
 
   cg::cluster_group cl = cg::this_cluster();
-  const int r = (int)cl.block_rank();
+  const int rank = (int)cl.block_rank();
   const int kvh = blockIdx.x / CS, qb = blockIdx.y, bz = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = lane >> 2, cq = lane & 3;
   pdl_wait();
   pdl_launch_next();
+  const int GQ = a.H / a.KV;
+  const int QB = a.QB;
   const int pos0 = a.causal ? a.pr.base[bz * a.pr.stride] + a.pr.off : 0;
   const int mq0 = qb * QB;
   const int nq = min(QB, a.M - mq0);
@@ -244,182 +289,205 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(256) attn
   // are nodes tnode0 + mq0 .. and see keys up to their own slot)
   const int tmax = a.causal ? pos0 + (a.v.tmask ? a.v.tnode0 : 0) + mq0 + nq : a.S;
   const int nact = (tmax + C - 1) / C;
-  const int kend = min(tmax, a.S);   // key rows that exist
+  const int kend = min(tmax, a.S);  // key rows that exist
   const T* q = static_cast<const T*>(a.v.q) + (size_t)bz * a.v.q_bs;
   const T* kbase = static_cast<const T*>(a.v.k) + (size_t)bz * a.v.kv_bs + (size_t)kvh * a.v.kv_hs;
   const T* vbase = static_cast<const T*>(a.v.v) + (size_t)bz * a.v.kv_bs + (size_t)kvh * a.v.kv_hs;
 
-  for (int i = tid; i < QR * KS; i += 256) Os[i] = 0.0f;
-  for (int i = tid; i < QR; i += 256) { Mx[i] = -INFINITY; Ls[i] = 0.0f; }
-  for (int e0 = 0; e0 < QR * V8; e0 += 4 * 256) {
-    uint4 raw[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int e = e0 + u * 256 + tid;
-      if (e < QR * V8) {
-        const int qr = e / V8, d8 = (e % V8) * 8;
-        raw[u] = *reinterpret_cast<const uint4*>(q + (size_t)(mq0 + qr / GQ) * a.v.q_rs + (size_t)(kvh * GQ + qr % GQ) * HD + d8);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int e = e0 + u * 256 + tid;
-      if (e < QR * V8) {
-        const int qr = e / V8, d8 = (e % V8) * 8;
-        const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          Qs[qr * KS + d8 + 2 * t] = Act<T>::lo(w[t]);
-          Qs[qr * KS + d8 + 2 * t + 1] = Act<T>::hi(w[t]);
-        }
-      }
-    }
+  // Q block: head row hr = query mq0 + hr / GQ, head kvh * GQ + hr % GQ; rows >= QR are zeros
+  for (int e = tid; e < kAttnRows * (HD / 8); e += 128) {
+    const int hr = e / (HD / 8), d8 = (e % (HD / 8)) * 8;
+    const bool ok = hr < QR;
+    const T* src = ok ? q + (size_t)(mq0 + hr / GQ) * a.v.q_rs + (size_t)(kvh * GQ + hr % GQ) * HD + d8 : q;
+    cp_async16(Qs + hr * RS + d8, src, ok);
   }
-
-  // K/V of a chunk travel through registers so that the next chunk's loads overlap this
-  // chunk's arithmetic; keys at or past tmax read as zeros (their rows may be stale).
-  uint4 kr[LDI], vr[LDI];
-  auto fetch = [&](int c) {
+  cp_async_commit();
+  auto fetch = [&](int c, int buf) {
     const int k0 = c * C;
-#pragma unroll
-    for (int u = 0; u < LDI; ++u) {
-      const int e = u * 256 + tid, j = e / V8, d8 = (e % V8) * 8;
-      if (k0 + j < kend) {
-        kr[u] = *reinterpret_cast<const uint4*>(kbase + (size_t)(k0 + j) * a.v.kv_rs + d8);
-        vr[u] = *reinterpret_cast<const uint4*>(vbase + (size_t)(k0 + j) * a.v.kv_rs + d8);
-      } else {
-        kr[u] = vr[u] = make_uint4(0u, 0u, 0u, 0u);
-      }
+    T* kd = Ks + buf * C * RS;
+    T* vd = Vs + buf * C * RS;
+    for (int e = tid; e < C * (HD / 8); e += 128) {
+      const int j = e / (HD / 8), d8 = (e % (HD / 8)) * 8;
+      const bool ok = k0 + j < kend;
+      const size_t off = ok ? (size_t)(k0 + j) * a.v.kv_rs + d8 : 0;
+      cp_async16(kd + j * RS + d8, kbase + off, ok);
+      cp_async16(vd + j * RS + d8, vbase + off, ok);
     }
+    cp_async_commit();
   };
-  auto stash = [&]() {
-#pragma unroll
-    for (int u = 0; u < LDI; ++u) {
-      const int e = u * 256 + tid, j = e / V8, d8 = (e % V8) * 8;
-      const uint32_t kw[4] = {kr[u].x, kr[u].y, kr[u].z, kr[u].w};
-      const uint32_t vw[4] = {vr[u].x, vr[u].y, vr[u].z, vr[u].w};
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        Ks[j * KS + d8 + 2 * t] = Act<T>::lo(kw[t]);
-        Ks[j * KS + d8 + 2 * t + 1] = Act<T>::hi(kw[t]);
-        Vs[j * KS + d8 + 2 * t] = Act<T>::lo(vw[t]);
-        Vs[j * KS + d8 + 2 * t + 1] = Act<T>::hi(vw[t]);
-      }
-    }
-  };
+  if (rank < nact) fetch(rank, 0);
 
-  constexpr int RS = 256 / HD;
-  const int d = tid % HD, rset = tid / HD;
-  if (r < nact) fetch(r);
-  for (int c = r; c < nact; c += CS) {
+  // per thread: head rows w*16 + r (accumulator elements 0, 1) and + 8 (elements 2, 3)
+  const int hr0 = warp * 16 + r, hr1 = hr0 + 8;
+  const bool live = warp * 16 < QR;  // this warp has at least one real row
+  float o[ND][4];
+#pragma unroll
+  for (int u = 0; u < ND; ++u) o[u][0] = o[u][1] = o[u][2] = o[u][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  // last visible key of the two rows (causal, non-tree), their tree masks
+  const int qi0 = mq0 + hr0 / GQ, qi1 = mq0 + hr1 / GQ;
+  const int lim0 = a.causal ? pos0 + qi0 : a.S - 1, lim1 = a.causal ? pos0 + qi1 : a.S - 1;
+  unsigned long long mk0 = 0, mk1 = 0;
+  if (a.v.tmask) {
+    mk0 = hr0 < QR ? a.v.tmask[a.v.tnode0 + qi0] : 0ull;
+    mk1 = hr1 < QR ? a.v.tmask[a.v.tnode0 + qi1] : 0ull;
+  }
+  uint32_t qf[NK][4];
+
+  int buf = 0;
+  bool first = true;
+  for (int c = rank; c < nact; c += CS, buf ^= 1) {
     const int k0 = c * C;
-    __syncthreads();  // the previous chunk's P.V has finished reading Ks/Vs
-    stash();
-    if (c + CS < nact) fetch(c + CS);
+    if (c + CS < nact) {
+      fetch(c + CS, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
     __syncthreads();
-
-    // ---- scores: warp w takes 4-row blocks, lane j takes keys j and j + 32 -----------
-    for (int rb = warp * 4; rb < QR; rb += 32) {
-      float s[4][2];
+    if (first) {
+      first = false;
+      if (live) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) s[i][0] = s[i][1] = 0.0f;
-      for (int dd = 0; dd < HD; dd += 4) {
-        const float4 ka = *reinterpret_cast<const float4*>(Ks + lane * KS + dd);
-        const float4 kb = *reinterpret_cast<const float4*>(Ks + (lane + 32) * KS + dd);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float4 qv = *reinterpret_cast<const float4*>(Qs + min(rb + i, QR - 1) * KS + dd);
-          s[i][0] = fmaf(qv.x, ka.x, s[i][0]); s[i][0] = fmaf(qv.y, ka.y, s[i][0]);
-          s[i][0] = fmaf(qv.z, ka.z, s[i][0]); s[i][0] = fmaf(qv.w, ka.w, s[i][0]);
-          s[i][1] = fmaf(qv.x, kb.x, s[i][1]); s[i][1] = fmaf(qv.y, kb.y, s[i][1]);
-          s[i][1] = fmaf(qv.z, kb.z, s[i][1]); s[i][1] = fmaf(qv.w, kb.w, s[i][1]);
+        for (int kk = 0; kk < NK; ++kk) {
+          const int idx = lane >> 3;
+          ldsm4(qf[kk], Qs + (warp * 16 + (idx & 1) * 8 + (lane & 7)) * RS + kk * 16 + (idx >> 1) * 8);
         }
       }
+    }
+    if (live) {
+      const T* kt = Ks + buf * C * RS;
+      const T* vt = Vs + buf * C * RS;
+      // ---- S = Q K^T: 8 n8 tiles of keys -------------------------------------------------
+      float sc[C / 8][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int qr = rb + i;
-        if (qr < QR) {
-          bool v0, v1;
-          if (a.v.tmask) {  // committed keys below the root, then the node's ancestors and itself
-            const unsigned long long mk = a.v.tmask[a.v.tnode0 + mq0 + qr / GQ];
-            const int j0 = k0 + lane - pos0, j1 = j0 + 32;
-            v0 = j0 < 0 || (j0 < 64 && ((mk >> j0) & 1ull));
-            v1 = j1 < 0 || (j1 < 64 && ((mk >> j1) & 1ull));
+      for (int t = 0; t < C / 8; ++t) sc[t][0] = sc[t][1] = sc[t][2] = sc[t][3] = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < NK; ++kk)
+#pragma unroll
+        for (int t = 0; t < C / 8; t += 2) {
+          uint32_t b[4];
+          const int idx = lane >> 3;
+          ldsm4(b, kt + (8 * (t + (idx >> 1)) + (lane & 7)) * RS + kk * 16 + (idx & 1) * 8);
+          mma16816<T>(sc[t], qf[kk], b[0], b[1]);
+          mma16816<T>(sc[t + 1], qf[kk], b[2], b[3]);
+        }
+      // ---- scale, mask, online softmax (rows hr0: elements 0,1; hr1: elements 2,3) ---------
+      float cm0 = -INFINITY, cm1 = -INFINITY;
+#pragma unroll
+      for (int t = 0; t < C / 8; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = k0 + 8 * t + 2 * cq + (e & 1);
+          bool vis;
+          if (a.v.tmask) {
+            const int j = key - pos0;
+            const unsigned long long mk = (e >> 1) ? mk1 : mk0;
+            vis = j < 0 || (j < 64 && ((mk >> j) & 1ull));
           } else {
-            const int lim = a.causal ? pos0 + mq0 + qr / GQ : a.S - 1;  // last visible key
-            v0 = k0 + lane <= lim;
-            v1 = k0 + lane + 32 <= lim;
+            vis = key <= ((e >> 1) ? lim1 : lim0);
           }
-          Ps[qr * PS + lane] = v0 ? s[i][0] * a.scale : -INFINITY;
-          Ps[qr * PS + lane + 32] = v1 ? s[i][1] * a.scale : -INFINITY;
+          const float v = vis ? sc[t][e] * a.scale : -INFINITY;
+          sc[t][e] = v;
+          if (e >> 1) cm1 = fmaxf(cm1, v); else cm0 = fmaxf(cm0, v);
         }
+      cm0 = fmaxf(cm0, __shfl_xor_sync(0xffffffffu, cm0, 1));
+      cm0 = fmaxf(cm0, __shfl_xor_sync(0xffffffffu, cm0, 2));
+      cm1 = fmaxf(cm1, __shfl_xor_sync(0xffffffffu, cm1, 1));
+      cm1 = fmaxf(cm1, __shfl_xor_sync(0xffffffffu, cm1, 2));
+      const float mn0 = fmaxf(m0, cm0), mn1 = fmaxf(m1, cm1);
+      const float al0 = mn0 == -INFINITY ? 1.0f : (m0 == -INFINITY ? 0.0f : expf(m0 - mn0));
+      const float al1 = mn1 == -INFINITY ? 1.0f : (m1 == -INFINITY ? 0.0f : expf(m1 - mn1));
+      float ps0 = 0.0f, ps1 = 0.0f;
+#pragma unroll
+      for (int t = 0; t < C / 8; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float mn = (e >> 1) ? mn1 : mn0;
+          const float v = sc[t][e];
+          const float pe = (mn == -INFINITY || v == -INFINITY) ? 0.0f : expf(v - mn);
+          sc[t][e] = pe;
+          if (e >> 1) ps1 += pe; else ps0 += pe;
+        }
+      ps0 += __shfl_xor_sync(0xffffffffu, ps0, 1);
+      ps0 += __shfl_xor_sync(0xffffffffu, ps0, 2);
+      ps1 += __shfl_xor_sync(0xffffffffu, ps1, 1);
+      ps1 += __shfl_xor_sync(0xffffffffu, ps1, 2);
+      l0 = fmaf(l0, al0, ps0);
+      l1 = fmaf(l1, al1, ps1);
+      m0 = mn0;
+      m1 = mn1;
+#pragma unroll
+      for (int u = 0; u < ND; ++u) {
+        o[u][0] *= al0; o[u][1] *= al0;
+        o[u][2] *= al1; o[u][3] *= al1;
       }
-    }
-    __syncthreads();
-
-    // ---- running softmax: warp per row --------------------------------------------------
-    for (int qr = warp; qr < QR; qr += 8) {
-      const float v0 = Ps[qr * PS + lane], v1 = Ps[qr * PS + lane + 32];
-      const float mo = Mx[qr];
-      const float mn = fmaxf(mo, warp_max(fmaxf(v0, v1)));
-      float p0 = 0.0f, p1 = 0.0f, alpha = 1.0f;
-      if (mn != -INFINITY) {
-        p0 = v0 == -INFINITY ? 0.0f : expf(v0 - mn);
-        p1 = v1 == -INFINITY ? 0.0f : expf(v1 - mn);
-        alpha = mo == -INFINITY ? 0.0f : expf(mo - mn);
-      }
-      const float l = warp_sum(p0 + p1);
-      Ps[qr * PS + lane] = p0;
-      Ps[qr * PS + lane + 32] = p1;
-      if (lane == 0) {
-        Mx[qr] = mn;
-        Ls[qr] = fmaf(Ls[qr], alpha, l);
-        Al[qr] = alpha;
-      }
-    }
-    __syncthreads();
-
-    // ---- O = O * alpha + P.V: thread (d, row set), 4 rows at a time --------------------
-    for (int rb = rset * 4; rb < QR; rb += RS * 4) {
-      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      for (int j = 0; j < C; j += 4) {
-        const float v0 = Vs[j * KS + d], v1 = Vs[(j + 1) * KS + d], v2 = Vs[(j + 2) * KS + d],
-                    v3 = Vs[(j + 3) * KS + d];
+      // ---- O += P V, P = hi + lo in the activation dtype ---------------------------------
+#pragma unroll
+      for (int j = 0; j < C / 16; ++j) {
+        uint32_t ph[4], pl[4];
+        const float* s0 = sc[2 * j];
+        const float* s1 = sc[2 * j + 1];
+        const float f[4][2] = {{s0[0], s0[1]}, {s0[2], s0[3]}, {s1[0], s1[1]}, {s1[2], s1[3]}};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const float4 p = *reinterpret_cast<const float4*>(Ps + min(rb + i, QR - 1) * PS + j);
-          acc[i] = fmaf(p.x, v0, acc[i]); acc[i] = fmaf(p.y, v1, acc[i]);
-          acc[i] = fmaf(p.z, v2, acc[i]); acc[i] = fmaf(p.w, v3, acc[i]);
+          ph[i] = pack2<T>(f[i][0], f[i][1]);
+          const T* hv = reinterpret_cast<const T*>(&ph[i]);
+          pl[i] = pack2<T>(f[i][0] - Act<T>::to_f(hv[0]), f[i][1] - Act<T>::to_f(hv[1]));
+        }
+#pragma unroll
+        for (int u = 0; u < ND; u += 2) {
+          uint32_t b[4];
+          const int idx = lane >> 3;
+          ldsm4t(b, vt + (16 * j + (idx & 1) * 8 + (lane & 7)) * RS + 8 * (u + (idx >> 1)));
+          mma16816<T>(o[u], ph, b[0], b[1]);
+          mma16816<T>(o[u], pl, b[0], b[1]);
+          mma16816<T>(o[u + 1], ph, b[2], b[3]);
+          mma16816<T>(o[u + 1], pl, b[2], b[3]);
         }
       }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (rb + i < QR) Os[(rb + i) * KS + d] = fmaf(Os[(rb + i) * KS + d], Al[rb + i], acc[i]);
     }
+    __syncthreads();  // every warp is done with this buffer before it is refilled
   }
+  cp_async_wait<0>();
+  __syncthreads();
 
-  // ---- combine the cluster's partial rows in rank order; CTA r owns rows r, r + CS, … --
+  // ---- partial rows to shared memory, combine across the cluster in rank order -----------
+  if (cq == 0) {
+    Mx[hr0] = m0; Ls[hr0] = l0;
+    Mx[hr1] = m1; Ls[hr1] = l1;
+  }
+#pragma unroll
+  for (int u = 0; u < ND; ++u) {
+    const int d = 8 * u + 2 * cq;
+    Os[hr0 * LY::OS + d] = o[u][0];
+    Os[hr0 * LY::OS + d + 1] = o[u][1];
+    Os[hr1 * LY::OS + d] = o[u][2];
+    Os[hr1 * LY::OS + d + 1] = o[u][3];
+  }
   cl.sync();
   T* out = static_cast<T*>(a.v.out) + (size_t)bz * a.v.o_bs;
-  for (int qr = r + CS * rset; qr < QR; qr += CS * RS) {
+  constexpr int RSETS = 128 / HD;
+  const int d = tid % HD, rset = tid / HD;
+  for (int qr = rank + CS * rset; qr < QR; qr += CS * RSETS) {
     float mr[CS], lr[CS], orr[CS];
 #pragma unroll
     for (int i = 0; i < CS; ++i) {
       mr[i] = *cl.map_shared_rank(Mx + qr, i);
       lr[i] = *cl.map_shared_rank(Ls + qr, i);
-      orr[i] = *cl.map_shared_rank(Os + qr * KS + d, i);
+      orr[i] = *cl.map_shared_rank(Os + qr * LY::OS + d, i);
     }
     float mx = -INFINITY;
 #pragma unroll
     for (int i = 0; i < CS; ++i) mx = fmaxf(mx, mr[i]);
-    float o = 0.0f, l = 0.0f;
+    float ov = 0.0f, l = 0.0f;
 #pragma unroll
     for (int i = 0; i < CS; ++i) {
       const float w = mr[i] == -INFINITY ? 0.0f : expf(mr[i] - mx);
-      o = fmaf(w, orr[i], o);
+      ov = fmaf(w, orr[i], ov);
       l = fmaf(w, lr[i], l);
     }
-    out[(size_t)(mq0 + qr / GQ) * a.v.o_rs + (size_t)(kvh * GQ + qr % GQ) * HD + d] = Act<T>::from_f(o / l);
+    out[(size_t)(mq0 + qr / GQ) * a.v.o_rs + (size_t)(kvh * GQ + qr % GQ) * HD + d] = Act<T>::from_f(ov / l);
   }
   cl.sync();  // keep this CTA's shared memory alive until every peer has read it
 }
@@ -499,10 +567,7 @@ __global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logit
   }
 }
 
-size_t attn_smem_bytes(int hd) {
-  const size_t ks = hd + 4, ps = kAttnChunk + 4, qr = kAttnRows;
-  return (2 * kAttnChunk * ks + 2 * qr * ks + qr * ps + 3 * qr) * sizeof(float);
-}
+size_t attn_smem_bytes(int hd) { return hd == 128 ? AttnLayout<128>::BYTES : AttnLayout<64>::BYTES; }
 
 template <typename T, int HD>
 int launch_attn_t(const AttnArgs& a, int batch, cudaStream_t s) {
@@ -516,7 +581,7 @@ int launch_attn_t(const AttnArgs& a, int batch, cudaStream_t s) {
     configured[dev & 63] = 1;
   }
   const int nqb = (a.M + a.QB - 1) / a.QB;
-  return launch_kernel(attn_kernel<T, HD>, dim3(a.KV * kAttnCluster, nqb, batch), dim3(256), smem, s, a);
+  return launch_kernel(attn_kernel<T, HD>, dim3(a.KV * kAttnCluster, nqb, batch), dim3(128), smem, s, a);
 }
 
 }  // namespace
