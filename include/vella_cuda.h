@@ -324,6 +324,11 @@ typedef struct vella_whisper_cfg {
   int32_t bits;        /* decoder Linears and token embedding: 0 (dense), 4 or 8 (MLX affine, g64) */
   int32_t dtype;       /* VELLA_F16 | VELLA_BF16 */
   float eps;           /* LayerNorm epsilon (1e-5) */
+  /* Independent audio streams held by the handle (0 or 1: one).  Each has its own window,
+   * cross-attention K/V, self-attention cache and tokens; vella_whisper_decode_batch steps
+   * all of them with one decoder forward per token (one row per stream).  The reference runs
+   * one window per model call (WhisperModel.swift:341-400). */
+  int32_t streams;
 } vella_whisper_cfg;
 
 typedef struct vella_whisper_stats {
@@ -350,14 +355,21 @@ VELLA_API int vella_whisper_init_random(vella_whisper* w, uint64_t seed, float s
  * enc_ln, dec_ln, embed (token embedding = vocabulary projection), dec_pos, and the
  * activation enc_out [n_audio, d_model]. */
 VELLA_API int vella_whisper_tensor(vella_whisper* w, const char* name, int32_t layer, void** ptr, size_t* bytes);
-/* Encoder over one window: mel fp32 [n_mels][2 * n_audio] (host or device), then the cross-
- * attention K/V of every decoder layer. */
+/* Encoder over one window per stream: mel fp32 [streams][n_mels][2 * n_audio] (host or
+ * device), then the cross-attention K/V of every decoder layer, per stream. */
 VELLA_API int vella_whisper_encode(vella_whisper* w, const float* mel, int32_t on_host);
 /* Greedy decode after the prompt (n_prompt <= 16 tokens): up to max_tokens tokens, stopping
  * after `eot` when eot >= 0 (not emitted).  out_tokens (host) receives *n_out tokens. */
 VELLA_API int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int32_t n_prompt, int32_t max_tokens,
                                    int32_t eot, int32_t* out_tokens, int32_t* n_out);
-/* Teacher-forced logits [T, vocab] (dtype) of the token sequence (positions 0..T-1). */
+/* Greedy decode of every stream (streams > 1 or 1): the same prompt (n_prompt <= 16) for
+ * each, then max_tokens tokens per stream, one decoder forward of `streams` rows per token
+ * (one CUDA graph), no end-of-text stop.  out_tokens (host) [streams][max_tokens].  The
+ * stats' tokens field counts all streams' tokens. */
+VELLA_API int vella_whisper_decode_batch(vella_whisper* w, const int32_t* prompt, int32_t n_prompt,
+                                         int32_t max_tokens, int32_t* out_tokens);
+/* Teacher-forced logits [T, vocab] (dtype) of the token sequence (positions 0..T-1); one-
+ * stream handles only (as vella_whisper_decode). */
 VELLA_API int vella_whisper_score(vella_whisper* w, const int32_t* tokens, int32_t T, void* logits, int32_t on_host);
 VELLA_API int vella_whisper_get_stats(const vella_whisper* w, vella_whisper_stats* out);
 

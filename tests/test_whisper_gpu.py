@@ -174,3 +174,55 @@ def test_bad_arguments_are_rejected():
         m.score([1, 2, 700])                     # token id out of range
     assert len(m.decode([1, 2], 8).tokens) == 8  # the handle still works afterwards
     m.close()
+
+
+def test_batched_streams_equal_single_stream_decodes():
+    """Three streams in one handle (one decoder row per stream per step, the small-M GEMM path):
+    each stream's tokens are exactly those of a one-stream handle decoding its window alone,
+    and a second batched decode (graph replay) repeats them."""
+    from dataclasses import replace
+
+    from vella_b200 import whisper as VW
+    S, n = 3, 16
+    prompt = [50258, 50259, 50359, 50363]
+    mels = np.stack([mel_of(VW.TINY, 30 + st) for st in range(S)])
+    mb = VW.Whisper(replace(VW.TINY, streams=S))
+    mb.init_random(5, 0.02)
+    mb.encode(mels)
+    got = mb.decode_batch(prompt, n)
+    assert got.shape == (S, n)
+    assert np.array_equal(mb.decode_batch(prompt, n), got)
+    st_ = mb.stats()
+    assert st_["tokens"] == S * n and st_["decode_ms"] > 0
+    mb.close()
+    single, _ = make(VW.TINY, seed=5)
+    for st in range(S):
+        single.encode(mels[st])
+        assert single.decode(prompt, n).tokens == list(got[st]), st
+    single.close()
+
+
+def test_many_streams_follow_the_oracle():
+    """Twenty streams (decoder rows on the tensor-core GEMM): the first and last streams'
+    tokens are the oracle's argmax wherever its top-2 margin exceeds the logits tolerance."""
+    from dataclasses import replace
+
+    from vella_b200 import _lib
+    from vella_b200 import whisper as VW
+    S, n = 20, 12
+    prompt = [50258, 50259, 50359, 50363]
+    m, oc = make(replace(VW.TINY, streams=S), seed=6)
+    W = oracle_weights(m, oc)
+    mels = np.stack([mel_of(oc, 50 + st) for st in range(S)])
+    m.encode(mels)
+    got = m.decode_batch(prompt, n)
+    for st in (0, S - 1):
+        enc_ref = Wh.encoder(oc, W, mels[st])
+        logits = Wh.score(oc, W, enc_ref, prompt + list(got[st][:-1]))[len(prompt) - 1:]
+        for j, t in enumerate(got[st]):
+            row = logits[j]
+            best = int(np.argmax(row))
+            assert t == best or row[best] - row[t] <= LOGIT_TOL, (st, j, t, best)
+    with pytest.raises(_lib.VellaError):
+        m.decode(prompt, 4)  # one-stream entry point on a multi-stream handle
+    m.close()

@@ -125,12 +125,13 @@ __global__ void __launch_bounds__(256) wembed_kernel(T* __restrict__ h, const vo
   using A = Act<T>;
   pdl_wait();
   pdl_launch_next();
-  int p = *pr.base + pr.off + (int)blockIdx.x;
-  if (p >= max_target) {
+  const int m = (int)blockIdx.x;
+  int p = pr.pos(m);
+  if (p < 0 || p >= max_target) {
     if (threadIdx.x == 0) atomicOr(err, 4);
-    p = max_target - 1;
+    p = p < 0 ? 0 : max_target - 1;
   }
-  int t = tok[p];
+  int t = tok[(size_t)pr.stream_of(m) * max_target + p];
   if (t < 0 || t >= vocab) {
     if (threadIdx.x == 0) atomicOr(err, 1);
     t = 0;
@@ -151,15 +152,20 @@ __global__ void __launch_bounds__(256) wembed_kernel(T* __restrict__ h, const vo
 }
 
 // Appends the k and v parts of qkv rows [rows, 3d] to the self-attention cache
-// [heads][S][hd] of one layer at positions *pr.base + pr.off + m.
+// [heads][S][hd] of one layer at position pr.pos(m); row m's stream cache starts kv_ss
+// elements per stream after stream 0's.
 template <typename T>
 __global__ void __launch_bounds__(256) wappend_kernel(const T* __restrict__ qkv, T* __restrict__ kc,
-                                                      T* __restrict__ vc, PosRef pr, int d, int hd, int S) {
+                                                      T* __restrict__ vc, PosRef pr, int d, int hd, int S,
+                                                      long long kv_ss) {
   pdl_wait();
   pdl_launch_next();
   const int m = blockIdx.x;
-  const int p = *pr.base + pr.off + m;
-  if (p >= S) return;
+  const int p = pr.pos(m);
+  if (p < 0 || p >= S) return;
+  const size_t so = (size_t)pr.stream_of(m) * kv_ss;
+  kc += so;
+  vc += so;
   const T* row = qkv + (size_t)m * 3 * d;
   for (int i = threadIdx.x; i < d; i += blockDim.x) {
     const int h = i / hd, j = i % hd;
@@ -168,13 +174,16 @@ __global__ void __launch_bounds__(256) wappend_kernel(const T* __restrict__ qkv,
   }
 }
 
-// tok[*L] = ys[0]; *L += 1.
-__global__ void wcommit_kernel(int* L, int* tok, const int* ys, int max_target, int* err) {
+// Stream s (thread s): tok[s][L[s]] = ys[s * ys_stride + ys_off]; L[s] += 1.
+__global__ void wcommit_kernel(int* L, int* tok, const int* ys, int max_target, int* err, int streams, int ys_stride,
+                               int ys_off) {
   pdl_wait();
   pdl_launch_next();
-  const int p = *L;
-  if (p < max_target) tok[p] = ys[0]; else *err |= 4;
-  *L = p + 1;
+  const int st = (int)(blockIdx.x * blockDim.x + threadIdx.x);
+  if (st >= streams) return;
+  const int p = L[st];
+  if (p < max_target) tok[(size_t)st * max_target + p] = ys[st * ys_stride + ys_off]; else atomicOr(err, 4);
+  L[st] = p + 1;
 }
 
 // Zeroes columns [c0, ld) of a row-major [rows, ld] array of 16-bit elements.
@@ -216,6 +225,8 @@ size_t up256(size_t b) { return (b + 255) / 256 * 256; }
 struct vella_whisper {
   vella_whisper_cfg cfg{};
   int device = 0;
+  int S = 1;           // streams
+  int R = 0;           // decoder rows per forward: S * kWRows
   size_t elt = 2;
   int kp1 = 0;  // conv1 K padded to a multiple of 64
   void* arena = nullptr;
@@ -228,14 +239,17 @@ struct vella_whisper {
   std::vector<vella::WDec> dec;
   // activations
   void* act = nullptr;
-  float* mel = nullptr;                          // [n_mels][2 n_audio]
+  float* mel = nullptr;                          // [S][n_mels][2 n_audio]
   void *col = nullptr, *x0 = nullptr;            // im2col, conv1 output [2A, d]
   void *eh = nullptr, *en = nullptr, *eqkv = nullptr, *eatt = nullptr, *ef = nullptr, *enc_out = nullptr;
-  void* xkv = nullptr;                           // [dec_layers][A][2d]
-  void* kv = nullptr;                            // [dec_layers][2][H][max_target][hd]
+  void* xkv = nullptr;                           // [S][dec_layers][A][2d]
+  void* kv = nullptr;                            // [S][dec_layers][2][H][max_target][hd]
   void *dh = nullptr, *dn = nullptr, *dqkv = nullptr, *datt = nullptr, *dq2 = nullptr, *df = nullptr;
-  void* logits = nullptr;                        // [kWRows, V]
-  int *ys = nullptr, *tok = nullptr, *L = nullptr, *dzero = nullptr, *err = nullptr, *nonfinite = nullptr;
+  void* logits = nullptr;                        // [R, V]
+  int *ys = nullptr;                             // [R]
+  int *tok = nullptr;                            // [S][max_target]
+  int *L = nullptr, *dzero = nullptr;            // [S] lengths, [S] zeros
+  int *err = nullptr, *nonfinite = nullptr;
   void* argmax_sc = nullptr;
   void* gemm_ws = nullptr;
   size_t gemm_ws_bytes = 0;
@@ -298,6 +312,12 @@ int embed_t(vella_whisper* w, PosRef pr, int rows, cudaStream_t s) {
                        (const int*)w->tok, pr, c.d_model, c.vocab, c.max_target, w->err);
 }
 
+// Elements of one stream's self-attention cache and of its cross-attention K/V.
+long long kv_stream_elems(const vella_whisper_cfg& c) {
+  return (long long)c.dec_layers * 2 * c.heads * c.max_target * (c.d_model / c.heads);
+}
+long long xkv_stream_elems(const vella_whisper_cfg& c) { return (long long)c.dec_layers * c.n_audio * 2 * c.d_model; }
+
 template <typename T>
 int append_t(vella_whisper* w, int l, PosRef pr, int rows, cudaStream_t s) {
   const vella_whisper_cfg& c = w->cfg;
@@ -305,7 +325,7 @@ int append_t(vella_whisper* w, int l, PosRef pr, int rows, cudaStream_t s) {
   const size_t per = (size_t)c.heads * c.max_target * hd;
   T* kc = static_cast<T*>(w->kv) + (size_t)l * 2 * per;
   return launch_kernel(wappend_kernel<T>, dim3(rows), dim3(256), 0, s, static_cast<const T*>(w->dqkv), kc, kc + per, pr,
-                       c.d_model, hd, c.max_target);
+                       c.d_model, hd, c.max_target, kv_stream_elems(c));
 }
 
 void* kcache(vella_whisper* w, int l) {
@@ -319,10 +339,13 @@ void* vcache(vella_whisper* w, int l) {
   return static_cast<char*>(w->kv) + ((size_t)l * 2 + 1) * per;
 }
 
-// Decoder over `rows` positions starting at *pr.base + pr.off (tokens from w->tok); the
-// last `logits_rows` rows go through the vocabulary projection and the argmax.
-int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, cudaStream_t s) {
+// Decoder over `rows` rows, `streams` streams of rows / streams consecutive rows each (row m
+// at position pr.pos(m) of stream pr.stream_of(m); tokens from w->tok); the last
+// `logits_rows` rows go through the vocabulary projection and the argmax.
+int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, int streams, cudaStream_t s) {
   const vella_whisper_cfg& c = w->cfg;
+  if (streams < 1 || rows % streams) return fail(VELLA_E_INVALID, "whisper decoder: %d rows over %d streams", rows, streams);
+  const int rps = rows / streams;
   const int d = c.d_model, H = c.heads, hd = d / H, dt = c.dtype;
   const float scale = 1.0f / std::sqrt((float)hd);
   const bool bf = dt == VELLA_BF16;
@@ -338,7 +361,8 @@ int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, cuda
     sv.k = kcache(w, l); sv.v = vcache(w, l);
     sv.kv_hs = (long long)c.max_target * hd; sv.kv_rs = hd;
     sv.out = w->datt; sv.o_rs = d;
-    if ((rc = launch_attention_ex(dt, sv, 1, pr, 1, rows, H, H, hd, c.max_target, scale, s))) return rc;
+    sv.q_bs = (long long)rps * 3 * d; sv.o_bs = (long long)rps * d; sv.kv_bs = kv_stream_elems(c);
+    if ((rc = launch_attention_ex(dt, sv, streams, pr, 1, rps, H, H, hd, c.max_target, scale, s))) return rc;
     if ((rc = gemm(w, L.o, w->datt, rows, w->dh, VELLA_EPI_BIAS_RESIDUAL, w->dh, s))) return rc;
     if ((rc = layernorm(w, w->dn, w->dh, L.ln2, rows, s))) return rc;
     if ((rc = gemm(w, L.cq, w->dn, rows, w->dq2, VELLA_EPI_BIAS, nullptr, s))) return rc;
@@ -348,7 +372,9 @@ int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, cuda
     cv.k = xk; cv.v = xk + (size_t)d * w->elt;
     cv.kv_hs = hd; cv.kv_rs = 2LL * d;
     cv.out = w->datt; cv.o_rs = d;
-    if ((rc = launch_attention_ex(dt, cv, 1, PosRef{w->dzero, 0}, 0, rows, H, H, hd, c.n_audio, scale, s))) return rc;
+    cv.q_bs = (long long)rps * d; cv.o_bs = (long long)rps * d; cv.kv_bs = xkv_stream_elems(c);
+    if ((rc = launch_attention_ex(dt, cv, streams, PosRef{w->dzero, 0}, 0, rps, H, H, hd, c.n_audio, scale, s)))
+      return rc;
     if ((rc = gemm(w, L.co, w->datt, rows, w->dh, VELLA_EPI_BIAS_RESIDUAL, w->dh, s))) return rc;
     if ((rc = layernorm(w, w->dn, w->dh, L.ln3, rows, s))) return rc;
     if ((rc = gemm(w, L.fc1, w->dn, rows, w->df, VELLA_EPI_BIAS_GELU, nullptr, s))) return rc;
@@ -364,13 +390,15 @@ int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, cuda
   return VELLA_OK;
 }
 
-int encoder_forward(vella_whisper* w, cudaStream_t s) {
+// Encoder of stream `st`'s window, then that stream's cross-attention K/V.
+int encoder_forward(vella_whisper* w, int st, cudaStream_t s) {
   const vella_whisper_cfg& c = w->cfg;
   const int d = c.d_model, H = c.heads, hd = d / H, A = c.n_audio, dt = c.dtype;
   const float scale = 1.0f / std::sqrt((float)hd);
   int rc;
   // conv1 over the 2A mel frames (mel is [n_mels][2A]: x(t, c) = mel[c * 2A + t])
-  if ((rc = im2col<float>(w, w->col, w->mel, c.n_mels, 1, 2 * A, 1, 2LL * A, w->kp1, 2 * A, s))) return rc;
+  const float* mel = w->mel + (size_t)st * c.n_mels * 2 * A;
+  if ((rc = im2col<float>(w, w->col, mel, c.n_mels, 1, 2 * A, 1, 2LL * A, w->kp1, 2 * A, s))) return rc;
   if ((rc = gemm(w, w->conv1, w->col, 2 * A, w->x0, VELLA_EPI_BIAS_GELU, nullptr, s))) return rc;
   // conv2, stride 2, + positions
   if (dt == VELLA_BF16) rc = im2col<__nv_bfloat16>(w, w->col, static_cast<const __nv_bfloat16*>(w->x0), d, 2, 2 * A, d, 1, 3 * d, A, s);
@@ -394,7 +422,7 @@ int encoder_forward(vella_whisper* w, cudaStream_t s) {
   }
   if ((rc = layernorm(w, w->enc_out, w->eh, w->enc_ln, A, s))) return rc;
   for (int l = 0; l < c.dec_layers; ++l) {
-    char* xk = static_cast<char*>(w->xkv) + (size_t)l * A * 2 * d * w->elt;
+    char* xk = static_cast<char*>(w->xkv) + ((size_t)st * xkv_stream_elems(c) + (size_t)l * A * 2 * d) * w->elt;
     if ((rc = gemm(w, w->dec[l].ckv, w->enc_out, A, xk, VELLA_EPI_BIAS, nullptr, s))) return rc;
   }
   return VELLA_OK;
@@ -454,6 +482,11 @@ void rebase_lin(WLin& L, char* base) {
 }
 void rebase_norm(WNorm& N, char* base) { rebase(N.w, base); rebase(N.b, base); }
 
+int commit(vella_whisper* w, int ys_stride, int ys_off, cudaStream_t s) {
+  return launch_kernel(wcommit_kernel, dim3((w->S + 127) / 128), dim3(128), 0, s, w->L, w->tok, (const int*)w->ys,
+                       w->cfg.max_target, w->err, w->S, ys_stride, ys_off);
+}
+
 size_t ws_for(const WLin& L, int dtype, int epi) {
   vella_qgemm_desc d{kWRows, L.q.n, L.q.k, L.bits, 64, dtype, epi};
   QgemmPlan p;
@@ -464,9 +497,9 @@ int run_step(vella_whisper* w) {
   cudaStream_t s = w->stream;
   auto enqueue = [&]() -> int {
     int rc;
-    if ((rc = decoder_forward(w, PosRef{w->L, -1}, 1, 1, s))) return rc;
-    return launch_kernel(wcommit_kernel, dim3(1), dim3(1), 0, s, w->L, w->tok, (const int*)w->ys, w->cfg.max_target,
-                         w->err);
+    // one row per stream at its last committed token
+    if ((rc = decoder_forward(w, PosRef{w->L, -1, 1, 1}, w->S, w->S, w->S, s))) return rc;
+    return commit(w, 1, 0, s);
   };
   if (!w->step_warm) {
     const int rc = enqueue();
@@ -536,10 +569,13 @@ int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whi
   if (c.bits != 0 && c.bits != 4 && c.bits != 8) return fail(VELLA_E_UNSUPPORTED, "vella_whisper_create: bits %d", c.bits);
   if (c.dtype != VELLA_F16 && c.dtype != VELLA_BF16) return fail(VELLA_E_UNSUPPORTED, "vella_whisper_create: dtype");
   if (!(c.eps > 0.0f)) return fail(VELLA_E_INVALID, "vella_whisper_create: eps");
+  if (c.streams < 0 || c.streams > 1024) return fail(VELLA_E_INVALID, "vella_whisper_create: %d streams", c.streams);
   VELLA_CUDA_TRY(cudaSetDevice(device));
   auto* w = new vella_whisper();
   w->cfg = c;
   w->device = device;
+  w->S = c.streams > 0 ? c.streams : 1;
+  w->R = w->S * kWRows;
   w->elt = 2;
   const size_t e = w->elt;
   const int d = c.d_model, A = c.n_audio, F = c.ffn, V = c.vocab, B = c.bits;
@@ -586,22 +622,21 @@ int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whi
   }
   ws = std::max(ws, ws_for(w->embed, c.dtype, VELLA_EPI_NONE));
   w->gemm_ws_bytes = ws;
-  const size_t R = kWRows;
-  const size_t hdim = (size_t)hd;
+  const size_t R = (size_t)w->R, S = (size_t)w->S;
   Planner Q;
-  const size_t o_mel = Q.take((size_t)c.n_mels * 2 * A * sizeof(float));
+  const size_t o_mel = Q.take(S * c.n_mels * 2 * A * sizeof(float));
   const size_t o_col = Q.take(std::max((size_t)2 * A * w->kp1, (size_t)A * 3 * d) * e);
   const size_t o_x0 = Q.take((size_t)2 * A * d * e);
   const size_t o_eh = Q.take((size_t)A * d * e), o_en = Q.take((size_t)A * d * e);
   const size_t o_eqkv = Q.take((size_t)A * 3 * d * e), o_eatt = Q.take((size_t)A * d * e);
   const size_t o_ef = Q.take((size_t)A * F * e), o_out = Q.take((size_t)A * d * e);
-  const size_t o_xkv = Q.take((size_t)c.dec_layers * A * 2 * d * e);
-  const size_t o_kv = Q.take((size_t)c.dec_layers * 2 * c.heads * c.max_target * hdim * e);
+  const size_t o_xkv = Q.take(S * (size_t)xkv_stream_elems(c) * e);
+  const size_t o_kv = Q.take(S * (size_t)kv_stream_elems(c) * e);
   const size_t o_dh = Q.take(R * d * e), o_dn = Q.take(R * d * e), o_dqkv = Q.take(R * 3 * d * e);
   const size_t o_datt = Q.take(R * d * e), o_dq2 = Q.take(R * d * e), o_df = Q.take(R * F * e);
   const size_t o_logits = Q.take(R * (size_t)V * e);
-  const size_t o_ints = Q.take((R + (size_t)c.max_target + 8) * sizeof(int));
-  const size_t o_amx = Q.take(argmax_scratch_bytes(kWRows) + 512);
+  const size_t o_ints = Q.take((R + S * c.max_target + 2 * S + 8) * sizeof(int));
+  const size_t o_amx = Q.take(argmax_scratch_bytes(w->R) + 512);
   const size_t o_ws = Q.take(std::max<size_t>(ws, 256));
   auto cleanup = [&]() {
     if (w->act) cudaFree(w->act);
@@ -643,10 +678,10 @@ int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whi
   int* ints = reinterpret_cast<int*>(ab + o_ints);
   w->ys = ints;
   w->tok = ints + R;
-  w->L = w->tok + c.max_target;
-  w->dzero = w->L + 1;
-  w->err = w->L + 2;
-  w->nonfinite = w->L + 3;
+  w->L = w->tok + S * c.max_target;
+  w->dzero = w->L + S;
+  w->err = w->dzero + S;  // err and nonfinite are adjacent (check_flags reads both)
+  w->nonfinite = w->err + 1;
   w->argmax_sc = ab + o_amx;
   w->gemm_ws = ab + o_ws;
   *out = w;
@@ -783,9 +818,10 @@ int vella_whisper_encode(vella_whisper* w, const float* mel, int32_t on_host) {
   const vella_whisper_cfg& c = w->cfg;
   cudaStream_t s = w->stream;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
-  VELLA_CUDA_TRY(cudaMemcpyAsync(w->mel, mel, (size_t)c.n_mels * 2 * c.n_audio * sizeof(float),
+  VELLA_CUDA_TRY(cudaMemcpyAsync(w->mel, mel, (size_t)w->S * c.n_mels * 2 * c.n_audio * sizeof(float),
                                  on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, s));
-  int rc = encoder_forward(w, s);
+  int rc = VELLA_OK;
+  for (int st = 0; st < w->S && rc == VELLA_OK; ++st) rc = encoder_forward(w, st, s);
   if (rc) return rc;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev1, s));
   VELLA_CUDA_TRY(cudaEventSynchronize(w->ev1));
@@ -801,6 +837,7 @@ int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int32_t n_prom
     return fail(VELLA_E_INVALID, "vella_whisper_decode: NULL argument");
   const vella_whisper_cfg& c = w->cfg;
   if (!w->encoded) return fail(VELLA_E_INVALID, "vella_whisper_decode: encode first");
+  if (w->S != 1) return fail(VELLA_E_INVALID, "vella_whisper_decode: %d streams: use vella_whisper_decode_batch", w->S);
   if (n_prompt < 1 || n_prompt > kWRows) return fail(VELLA_E_INVALID, "vella_whisper_decode: prompt of %d tokens (1..%d)", n_prompt, kWRows);
   if (max_tokens < 0 || n_prompt + max_tokens > c.max_target)
     return fail(VELLA_E_INVALID, "vella_whisper_decode: %d + %d positions exceed max_target %d", n_prompt, max_tokens,
@@ -814,10 +851,9 @@ int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int32_t n_prom
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->tok, init.data(), n_prompt * sizeof(int), cudaMemcpyHostToDevice, s));
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->L, &n_prompt, sizeof(int), cudaMemcpyHostToDevice, s));
   VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
-  int rc = decoder_forward(w, PosRef{w->dzero, 0}, n_prompt, 1, s);
+  int rc = decoder_forward(w, PosRef{w->dzero, 0}, n_prompt, 1, 1, s);
   if (rc) return rc;
-  if ((rc = launch_kernel(wcommit_kernel, dim3(1), dim3(1), 0, s, w->L, w->tok, (const int*)w->ys, c.max_target, w->err)))
-    return rc;
+  if ((rc = commit(w, 0, 0, s))) return rc;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev1, s));
   int produced = 1;
   std::vector<int> toks;
@@ -856,6 +892,7 @@ int vella_whisper_score(vella_whisper* w, const int32_t* tokens, int32_t T, void
   if (!w || !tokens || !logits) return fail(VELLA_E_INVALID, "vella_whisper_score: NULL argument");
   const vella_whisper_cfg& c = w->cfg;
   if (!w->encoded) return fail(VELLA_E_INVALID, "vella_whisper_score: encode first");
+  if (w->S != 1) return fail(VELLA_E_INVALID, "vella_whisper_score: one-stream handles only");
   if (T < 1 || T > c.max_target) return fail(VELLA_E_INVALID, "vella_whisper_score: %d tokens", T);
   VELLA_CUDA_TRY(cudaSetDevice(w->device));
   cudaStream_t s = w->stream;
@@ -864,12 +901,53 @@ int vella_whisper_score(vella_whisper* w, const int32_t* tokens, int32_t T, void
   int rc;
   for (int s0 = 0; s0 < T; s0 += kWRows) {
     const int rows = std::min(kWRows, T - s0);
-    if ((rc = decoder_forward(w, PosRef{w->dzero, s0}, rows, rows, s))) return rc;
+    if ((rc = decoder_forward(w, PosRef{w->dzero, s0}, rows, rows, 1, s))) return rc;
     VELLA_CUDA_TRY(cudaMemcpyAsync(static_cast<char*>(logits) + (size_t)s0 * lrow, w->logits, (size_t)rows * lrow,
                                    on_host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, s));
   }
   VELLA_CUDA_TRY(cudaStreamSynchronize(s));
   return check_flags(w, "vella_whisper_score");
+}
+
+int vella_whisper_decode_batch(vella_whisper* w, const int32_t* prompt, int32_t n_prompt, int32_t max_tokens,
+                               int32_t* out_tokens) {
+  if (!w || !prompt || (max_tokens > 0 && !out_tokens))
+    return fail(VELLA_E_INVALID, "vella_whisper_decode_batch: NULL argument");
+  const vella_whisper_cfg& c = w->cfg;
+  if (!w->encoded) return fail(VELLA_E_INVALID, "vella_whisper_decode_batch: encode first");
+  if (n_prompt < 1 || n_prompt > kWRows)
+    return fail(VELLA_E_INVALID, "vella_whisper_decode_batch: prompt of %d tokens (1..%d)", n_prompt, kWRows);
+  if (max_tokens < 0 || n_prompt + max_tokens > c.max_target)
+    return fail(VELLA_E_INVALID, "vella_whisper_decode_batch: %d + %d positions exceed max_target %d", n_prompt,
+                max_tokens, c.max_target);
+  if (max_tokens == 0) return VELLA_OK;
+  VELLA_CUDA_TRY(cudaSetDevice(w->device));
+  cudaStream_t s = w->stream;
+  const int S = w->S;
+  std::vector<int> toks((size_t)S * c.max_target, 0), lens(S, n_prompt);
+  for (int st = 0; st < S; ++st) std::copy(prompt, prompt + n_prompt, toks.begin() + (size_t)st * c.max_target);
+  VELLA_CUDA_TRY(cudaMemcpyAsync(w->tok, toks.data(), toks.size() * sizeof(int), cudaMemcpyHostToDevice, s));
+  VELLA_CUDA_TRY(cudaMemcpyAsync(w->L, lens.data(), S * sizeof(int), cudaMemcpyHostToDevice, s));
+  VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
+  // the prompts of all streams in one forward (stream st: rows st * n_prompt .., positions
+  // 0 .. n_prompt - 1), then each stream's first token from its last prompt row
+  int rc = decoder_forward(w, PosRef{w->dzero, 0, n_prompt, 1}, S * n_prompt, S * n_prompt, S, s);
+  if (rc) return rc;
+  if ((rc = commit(w, n_prompt, n_prompt - 1, s))) return rc;
+  VELLA_CUDA_TRY(cudaEventRecord(w->ev1, s));
+  for (int i = 1; i < max_tokens; ++i)
+    if ((rc = run_step(w))) return rc;
+  VELLA_CUDA_TRY(cudaEventRecord(w->ev2, s));
+  VELLA_CUDA_TRY(cudaMemcpyAsync(toks.data(), w->tok, toks.size() * sizeof(int), cudaMemcpyDeviceToHost, s));
+  VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+  cudaEventElapsedTime(&w->stats.prefill_ms, w->ev0, w->ev1);
+  cudaEventElapsedTime(&w->stats.decode_ms, w->ev1, w->ev2);
+  if ((rc = check_flags(w, "vella_whisper_decode_batch"))) return rc;
+  for (int st = 0; st < S; ++st)
+    std::copy(toks.begin() + (size_t)st * c.max_target + n_prompt,
+              toks.begin() + (size_t)st * c.max_target + n_prompt + max_tokens, out_tokens + (size_t)st * max_tokens);
+  w->stats.tokens = S * max_tokens;
+  return VELLA_OK;
 }
 
 int vella_whisper_get_stats(const vella_whisper* w, vella_whisper_stats* out) {

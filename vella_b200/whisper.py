@@ -21,7 +21,8 @@ class WhisperCfg(ctypes.Structure):
     _fields_ = [("n_mels", ctypes.c_int32), ("d_model", ctypes.c_int32), ("heads", ctypes.c_int32),
                 ("enc_layers", ctypes.c_int32), ("dec_layers", ctypes.c_int32), ("ffn", ctypes.c_int32),
                 ("vocab", ctypes.c_int32), ("n_audio", ctypes.c_int32), ("max_target", ctypes.c_int32),
-                ("bits", ctypes.c_int32), ("dtype", ctypes.c_int32), ("eps", ctypes.c_float)]
+                ("bits", ctypes.c_int32), ("dtype", ctypes.c_int32), ("eps", ctypes.c_float),
+                ("streams", ctypes.c_int32)]
 
 
 class WhisperStats(ctypes.Structure):
@@ -38,6 +39,7 @@ for _name, _res, _args in [
                                             ctypes.POINTER(ctypes.c_size_t)]),
     ("vella_whisper_encode", ctypes.c_int, [_vp, _vp, _i32]),
     ("vella_whisper_decode", ctypes.c_int, [_vp, _pi32, _i32, _i32, _i32, _pi32, _pi32]),
+    ("vella_whisper_decode_batch", ctypes.c_int, [_vp, _pi32, _i32, _i32, _pi32]),
     ("vella_whisper_score", ctypes.c_int, [_vp, _pi32, _i32, _vp, _i32]),
     ("vella_whisper_get_stats", ctypes.c_int, [_vp, ctypes.POINTER(WhisperStats)]),
 ]:
@@ -58,10 +60,11 @@ class WhisperConfig:
     bits: int = 4
     dtype: int = _lib.F16
     eps: float = 1e-5
+    streams: int = 1  # independent windows decoded together (decode_batch)
 
     def c(self) -> WhisperCfg:
         return WhisperCfg(self.n_mels, self.d_model, self.heads, self.enc_layers, self.dec_layers, self.ffn,
-                          self.vocab, self.n_audio, self.max_target, self.bits, self.dtype, self.eps)
+                          self.vocab, self.n_audio, self.max_target, self.bits, self.dtype, self.eps, self.streams)
 
 
 TINY = WhisperConfig()  # Whisper-tiny shapes, int4 decoder (config 1)
@@ -103,10 +106,12 @@ class Whisper:
         return p.value, n.value
 
     def encode(self, mel, on_host: Optional[bool] = None):
-        """mel: numpy fp32 [n_mels, 2 * n_audio] (host) or a device pointer / torch tensor."""
+        """mel: numpy fp32 [n_mels, 2 * n_audio] ([streams, n_mels, 2 * n_audio] with several
+        streams) on the host, or a device pointer / torch tensor."""
         if isinstance(mel, np.ndarray):
             m = np.ascontiguousarray(mel, np.float32)
-            assert m.shape == (self.cfg.n_mels, 2 * self.cfg.n_audio), m.shape
+            shape = (self.cfg.n_mels, 2 * self.cfg.n_audio)
+            assert m.shape[-2:] == shape and m.size == max(self.cfg.streams, 1) * shape[0] * shape[1], m.shape
             _lib.check(_lib.lib().vella_whisper_encode(self.h, m.ctypes.data, 1))
         else:
             ptr = mel if isinstance(mel, int) else mel.data_ptr()
@@ -119,6 +124,15 @@ class Whisper:
         _lib.check(_lib.lib().vella_whisper_decode(self.h, pr, len(prompt), max_tokens, eot, out, ctypes.byref(n)))
         st = self.stats()
         return DecodeResult(list(out[: n.value]), st["prefill_ms"], st["decode_ms"])
+
+    def decode_batch(self, prompt: Sequence[int], max_tokens: int) -> np.ndarray:
+        """Greedy tokens [streams, max_tokens] of every stream after the same prompt."""
+        S = max(self.cfg.streams, 1)
+        pr = (ctypes.c_int32 * len(prompt))(*prompt)
+        out = np.zeros((S, max(max_tokens, 1)), np.int32)
+        _lib.check(_lib.lib().vella_whisper_decode_batch(self.h, pr, len(prompt), max_tokens,
+                                                         out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))))
+        return out[:, :max_tokens]
 
     def score(self, tokens: Sequence[int]) -> np.ndarray:
         """Teacher-forced logits [T, vocab] as storage (float16, or bf16 bits as uint16)."""
