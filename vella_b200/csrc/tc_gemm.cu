@@ -9,15 +9,18 @@
 // the epilogue is the library's: SiLU gate, then bias, then GELU, then residual, one rounding
 // (SmallMGEMM.swift:745-753).
 //
-// CTA tile: 128 weight rows (the MMA's M side) x 128 tokens (its N side) x all of K, streamed
-// in stages of 64 K elements (one quantization group):
-//   warp 0      TMA producer: the x tile [128 tokens x 64] (128-byte swizzle, out-of-range
+// CTA tile: 128 weight rows (the MMA's M side) x up to 256 tokens (its N side: the call's
+// remaining rows rounded up to 16, so a small call spends no tensor time on padding) x all
+// of K, streamed in stages of 64 K elements (one quantization group); each weight tile is
+// dequantised once per 256 tokens:
+//   warp 0      TMA producer: the x tile [256 tokens x 64] (128-byte swizzle, out-of-range
 //               tokens zero-filled) and the stage's weights (dense: directly into the MMA's
 //               operand tile; quantized: the raw code rows).
 //   warp 1      allocates tensor memory; one thread issues 4 MMAs (K = 16 each) per stage and
 //               commits them to the stage's "empty" barrier; frees tensor memory at the end.
 //   warps 2..5  thread = weight row: turns the stage's codes into the operand tile (128-byte
-//               swizzled K-major rows), then runs the epilogue out of tensor memory.
+//               swizzled K-major rows; scales and biases read 8 groups at a time, a block
+//               ahead), then runs the epilogue out of tensor memory.
 // Every wait is bounded (sm100::kWaitCycles); a wait that runs out records a fault
 // (vella_qgemm reports it) and the kernel finishes without waiting again.
 //
@@ -47,7 +50,7 @@ namespace {
 using namespace sm100;
 
 constexpr int kTcRows = 128;     // weight rows per CTA (MMA M)
-constexpr int kTcTok = 128;      // tokens per CTA (MMA N)
+constexpr int kTcTok = 256;      // tokens per CTA (largest MMA N)
 constexpr int kTcK = 64;         // K elements per stage
 constexpr int kTcThreads = 192;  // 6 warps
 
@@ -58,10 +61,12 @@ struct TcLayout {
   static constexpr int B_BYTES = kTcTok * 128;                    // [128 tokens x 64]
   static constexpr int RAW_BYTES = BITS ? kTcRows * kTcK * BITS / 8 : 0;
   static constexpr int STAGE = NA * A_BYTES + B_BYTES + NA * RAW_BYTES;  // multiple of 1024
-  static constexpr int NS = STAGE <= 40 * 1024 ? 5 : (STAGE <= 48 * 1024 ? 4 : 3);
+  static constexpr int total(int ns) { return 1024 + ns * STAGE + (3 * ns + 1) * 8 + 16; }
+  static constexpr int NS =
+      total(5) <= 227 * 1024 ? 5 : (total(4) <= 227 * 1024 ? 4 : (total(3) <= 227 * 1024 ? 3 : 2));
   static constexpr int TX = B_BYTES + (BITS ? NA * RAW_BYTES : NA * A_BYTES);
   static constexpr int BAR = NS * STAGE;  // barrier block offset
-  static constexpr int TOTAL = 1024 + BAR + (3 * NS + 1) * 8 + 16;
+  static constexpr int TOTAL = total(NS);
   static constexpr uint32_t COLS = GATE ? 2 * kTcTok : kTcTok;  // tensor-memory columns
   static_assert(STAGE % 1024 == 0, "stage tiles must stay 1024-byte aligned");
   static_assert(TOTAL <= 227 * 1024, "shared memory");
@@ -78,6 +83,7 @@ struct TcArgs {
   int gelu;                // GELU after the bias
   void* out;               // [M, N]
   int M, N, K, G;
+  int tt;                  // tokens per CTA: 128 or 256 (the x box height)
 };
 
 // One weight row's 64 codes of a stage -> 8 chunks of 8 operand elements (16 bytes each).
@@ -150,7 +156,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   using LY = TcLayout<BITS, GATE>;
   constexpr int NS = LY::NS;
   constexpr int WPG = BITS ? kTcK * BITS / 32 : 0;  // 32-bit code words per row and stage
-  constexpr uint32_t IDESC = f16_idesc(A::kMagic == 128.0f, kTcRows, kTcTok);
 
   extern __shared__ unsigned char smem_raw[];
   // (offsetting the shared array itself keeps its address space: shared loads, not generic ones)
@@ -165,8 +170,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   auto tileR = [&](int st, int i) { return smem + st * LY::STAGE + LY::NA * LY::A_BYTES + LY::B_BYTES + i * LY::RAW_BYTES; };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tok0 = blockIdx.x * kTcTok, row0 = blockIdx.y * kTcRows;
+  const int tok0 = blockIdx.x * a.tt, row0 = blockIdx.y * kTcRows;
   const int G = a.G;
+  // MMA N: this tile's tokens rounded up to 16 (a row's sums do not depend on N)
+  const int ntok = min(a.tt, (a.M - tok0 + 15) / 16 * 16);
+  const uint32_t tx = (uint32_t)(a.tt * 128 + (BITS ? LY::NA * LY::RAW_BYTES : LY::NA * LY::A_BYTES));
+  const uint32_t idesc = f16_idesc(A::kMagic == 128.0f, kTcRows, ntok);
 
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -198,7 +207,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
       };
       const int npre = min(G, NS);
       for (int g = 0; g < npre; ++g) {
-        mbar_expect_tx(&full[g], LY::TX);
+        mbar_expect_tx(&full[g], tx);
         weights(g, g);
       }
       pdl_wait();  // x is written by the previous kernel
@@ -210,7 +219,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
           atomicOr(&g_tc_fault, 1);
           break;
         }
-        mbar_expect_tx(&full[st], LY::TX);
+        mbar_expect_tx(&full[st], tx);
         weights(g, st);
         tma2d(tileB(st), &a.tx, g * kTcK, tok0, &full[st]);
         issued = g + 1;
@@ -236,8 +245,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         for (int kk = 0; kk < kTcK / 16; ++kk) {
           const uint64_t bd = kmajor_sw128_desc(b0 + kk * 32);
           const uint32_t acc = (g > 0 || kk > 0) ? 1u : 0u;
-          mma_f16_ss(tmem, kmajor_sw128_desc(a0 + kk * 32), bd, IDESC, acc);
-          if constexpr (GATE) mma_f16_ss(tmem + kTcTok, kmajor_sw128_desc(saddr(tileA(st, 1)) + kk * 32), bd, IDESC, acc);
+          mma_f16_ss(tmem, kmajor_sw128_desc(a0 + kk * 32), bd, idesc, acc);
+          if constexpr (GATE) mma_f16_ss(tmem + kTcTok, kmajor_sw128_desc(saddr(tileA(st, 1)) + kk * 32), bd, idesc, acc);
         }
         mma_commit(&empty[st]);
       }
@@ -251,43 +260,75 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     const int n = row0 + r;
     const bool nv = n < a.N;
     if constexpr (BITS != 0) {
-      const T* sp = static_cast<const T*>(a.s) + (size_t)(nv ? n : 0) * G;
-      const T* bp = static_cast<const T*>(a.b) + (size_t)(nv ? n : 0) * G;
-      const T* usp = static_cast<const T*>(a.us) + (size_t)(nv ? n : 0) * G;
-      const T* ubp = static_cast<const T*>(a.ub) + (size_t)(nv ? n : 0) * G;
-      const T zero = A::from_f(0.0f);
-      T s0 = nv ? sp[0] : zero, b0 = nv ? bp[0] : zero, us0 = zero, ub0 = zero;
-      if constexpr (GATE) { us0 = nv ? usp[0] : zero; ub0 = nv ? ubp[0] : zero; }
-      for (int g = 0; g < G; ++g) {
-        const int st = g % NS;
-        // next group's scale and bias, fetched while this stage's codes are in flight
-        const bool more = nv && g + 1 < G;
-        const T s1 = more ? sp[g + 1] : zero, b1 = more ? bp[g + 1] : zero;
-        T us1 = zero, ub1 = zero;
-        if constexpr (GATE) { us1 = more ? usp[g + 1] : zero; ub1 = more ? ubp[g + 1] : zero; }
-        if (!mbar_wait(&full[st], (uint32_t)((g / NS) & 1))) {
-          atomicOr(&g_tc_fault, 8);
-          break;
-        }
+      // scales/biases of this row: blocks of 8 groups (two 32-bit words = 4 packed values
+      // each half), the next block's loads in flight while this one is used
+      const size_t rowg = (size_t)(nv ? n : 0) * G;
+      const bool vec = (G % 8) == 0;  // rows start 16-byte aligned: one 16-byte load per array
+      auto load_block = [&](const void* base, int gb, uint32_t (&wv)[4]) {
+        const T* p = static_cast<const T*>(base) + rowg + gb;
+        if (!nv || gb >= G) {
+          wv[0] = wv[1] = wv[2] = wv[3] = 0u;
+        } else if (vec) {
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+          wv[0] = v.x; wv[1] = v.y; wv[2] = v.z; wv[3] = v.w;
+        } else {
+          const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
 #pragma unroll
-        for (int i = 0; i < LY::NA; ++i) {
-          const uint4* src = reinterpret_cast<const uint4*>(tileR(st, i) + r * WPG * 4);
-          uint32_t raw[WPG];
-#pragma unroll
-          for (int v = 0; v < WPG / 4; ++v) {
-            const uint4 q = src[v];
-            raw[4 * v] = q.x; raw[4 * v + 1] = q.y; raw[4 * v + 2] = q.z; raw[4 * v + 3] = q.w;
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t lo = gb + 2 * j < G ? q[2 * j] : 0u, hi = gb + 2 * j + 1 < G ? q[2 * j + 1] : 0u;
+            wv[j] = lo | (hi << 16);
           }
-          uint4 o[8];
-          dequant_row<T, BITS>(raw, i ? us0 : s0, i ? ub0 : b0, o);
-          unsigned char* dst = tileA(st, i) + r * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + ((c ^ (r & 7)) << 4)) = o[c];
         }
-        fence_proxy_async();
-        mbar_arrive(&ready[st]);
-        s0 = s1; b0 = b1;
-        if constexpr (GATE) { us0 = us1; ub0 = ub1; }
+      };
+      auto half_of = [](const uint32_t (&wv)[4], int j) {
+        const uint32_t w2 = wv[j >> 1];
+        const uint16_t h = (j & 1) ? (uint16_t)(w2 >> 16) : (uint16_t)(w2 & 0xFFFFu);
+        return *reinterpret_cast<const T*>(&h);
+      };
+      uint32_t sc[4], bc[4], sn[4], bn[4], usc[4], ubc[4], usn[4], ubn[4];
+      load_block(a.s, 0, sc);
+      load_block(a.b, 0, bc);
+      if constexpr (GATE) { load_block(a.us, 0, usc); load_block(a.ub, 0, ubc); }
+      bool ok = true;
+      for (int gb = 0; gb < G && ok; gb += 8) {
+        load_block(a.s, gb + 8, sn);
+        load_block(a.b, gb + 8, bn);
+        if constexpr (GATE) { load_block(a.us, gb + 8, usn); load_block(a.ub, gb + 8, ubn); }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int g = gb + j;
+          if (g >= G) break;
+          const int st = g % NS;
+          if (!mbar_wait(&full[st], (uint32_t)((g / NS) & 1))) {
+            atomicOr(&g_tc_fault, 8);
+            ok = false;
+            break;
+          }
+#pragma unroll
+          for (int i = 0; i < LY::NA; ++i) {
+            const uint4* src = reinterpret_cast<const uint4*>(tileR(st, i) + r * WPG * 4);
+            uint32_t raw[WPG];
+#pragma unroll
+            for (int v = 0; v < WPG / 4; ++v) {
+              const uint4 q = src[v];
+              raw[4 * v] = q.x; raw[4 * v + 1] = q.y; raw[4 * v + 2] = q.z; raw[4 * v + 3] = q.w;
+            }
+            uint4 o[8];
+            const T sj = i ? half_of(usc, j) : half_of(sc, j);
+            const T bj = i ? half_of(ubc, j) : half_of(bc, j);
+            dequant_row<T, BITS>(raw, sj, bj, o);
+            unsigned char* dst = tileA(st, i) + r * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + ((c ^ (r & 7)) << 4)) = o[c];
+          }
+          fence_proxy_async();
+          mbar_arrive(&ready[st]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sc[j] = sn[j]; bc[j] = bn[j];
+          if constexpr (GATE) { usc[j] = usn[j]; ubc[j] = ubn[j]; }
+        }
       }
     }
     // ---- epilogue ------------------------------------------------------------------------
@@ -301,7 +342,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
       const T* res = static_cast<const T*>(a.res);
       T* out = static_cast<T*>(a.out);
       const float bn = (bias && nv) ? A::to_f(bias[n]) : 0.0f;
-      for (int c0 = 0; c0 < kTcTok && tok0 + c0 < a.M; c0 += 32) {
+      for (int c0 = 0; c0 < ntok && tok0 + c0 < a.M; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem + lane_base + c0, v);
         uint32_t u[32];
@@ -340,7 +381,7 @@ int launch_tc_t(const TcArgs& a, cudaStream_t stream) {
     VELLA_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::TOTAL));
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
-  const dim3 grid((a.M + kTcTok - 1) / kTcTok, (a.N + kTcRows - 1) / kTcRows);
+  const dim3 grid((a.M + a.tt - 1) / a.tt, (a.N + kTcRows - 1) / kTcRows);
   return launch_kernel(k, grid, dim3(kTcThreads), LY::TOTAL, stream, a);
 }
 
@@ -369,9 +410,18 @@ int tc_launch(const vella_qgemm_desc& d, const void* x, const void* w, const voi
   a.gelu = epi_gelu(d.epilogue);
   a.out = out;
   a.M = d.m; a.N = d.n; a.K = d.k; a.G = d.k / kTcK;
+  // 256 tokens per CTA dequantise each weight tile half as often; 128 when the wide tiles
+  // would leave SMs idle (a row's value is the same either way)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = -1;
+  }
+  const long long rtiles = (d.n + kTcRows - 1) / kTcRows;
+  a.tt = ((long long)(d.m + kTcTok - 1) / kTcTok) * rtiles >= num_sms(dev) ? kTcTok : kTcTok / 2;
   int rc;
   const uint64_t xrow = (uint64_t)d.k * 2;
-  if ((rc = make_tensor_map(&a.tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, x, d.k, d.m, xrow, kTcK, kTcTok,
+  if ((rc = make_tensor_map(&a.tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, x, d.k, d.m, xrow, kTcK, a.tt,
                             CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if (d.bits == 0) {
