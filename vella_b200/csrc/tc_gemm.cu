@@ -18,9 +18,11 @@
 //               operand tile; quantized: the raw code rows).
 //   warp 1      allocates tensor memory; one thread issues 4 MMAs (K = 16 each) per stage and
 //               commits them to the stage's "empty" barrier; frees tensor memory at the end.
-//   warps 2..5  thread = weight row: turns the stage's codes into the operand tile (128-byte
-//               swizzled K-major rows; scales and biases read 8 groups at a time, a block
-//               ahead), then runs the epilogue out of tensor memory.
+//   warps 2..9  two threads per weight row (warps w and w + 4 share the row window of
+//               tensor-memory lanes 32 (w % 4) ..): each turns half of the stage's codes of
+//               its row into the operand tile (128-byte swizzled K-major rows; scales and
+//               biases read 8 groups at a time, a block ahead), then the pair runs the
+//               epilogue out of tensor memory on alternate 32-column chunks.
 // Every wait is bounded (sm100::kWaitCycles); a wait that runs out records a fault
 // (vella_qgemm reports it) and the kernel finishes without waiting again.
 //
@@ -52,7 +54,7 @@ using namespace sm100;
 constexpr int kTcRows = 128;     // weight rows per CTA (MMA M)
 constexpr int kTcTok = 256;      // tokens per CTA (largest MMA N)
 constexpr int kTcK = 64;         // K elements per stage
-constexpr int kTcThreads = 192;  // 6 warps
+constexpr int kTcThreads = 320;  // 10 warps
 
 template <int BITS, bool GATE>
 struct TcLayout {
@@ -86,17 +88,18 @@ struct TcArgs {
   int tt;                  // tokens per CTA: 128 or 256 (the x box height)
 };
 
-// One weight row's 64 codes of a stage -> 8 chunks of 8 operand elements (16 bytes each).
+// CH chunks of 8 codes of one weight row (8: the stage's 64, 4: half of them) -> CH chunks
+// of 8 operand elements (16 bytes each).
 // Codes are exact in T as magic + q (bf16: 128 + q for 4-bit codes; fp16: 1024 + q for 4- and
 // 8-bit codes); subtracting the magic is exact, the fma rounds once.  8-bit codes with bf16
 // go through fp32 (bf16 cannot hold 128 + q for q >= 128).
-template <typename T, int BITS>
-__device__ __forceinline__ void dequant_row(const uint32_t* raw, T s, T b, uint4 (&o)[8]) {
+template <typename T, int BITS, int CH>
+__device__ __forceinline__ void dequant_row(const uint32_t* raw, T s, T b, uint4 (&o)[CH]) {
   using A = Act<T>;
   if constexpr (BITS == 8 && sizeof(T) == 2 && A::kMagic == 128.0f) {  // bf16, 8-bit codes
     const float fs = A::to_f(s), fb = A::to_f(b);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 0; c < CH; ++c) {
       uint32_t w2[2] = {raw[2 * c], raw[2 * c + 1]};
       uint32_t r[4];
 #pragma unroll
@@ -126,7 +129,7 @@ __device__ __forceinline__ void dequant_row(const uint32_t* raw, T s, T b, uint4
     };
     if constexpr (BITS == 4) {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < CH; ++c) {
         const uint32_t w = raw[c];  // elements 8c .. 8c+7, low nibble first
         const uint32_t p04 = and_or(w, 0x000F000Fu, mag), p15 = and_or(w >> 4, 0x000F000Fu, mag);
         const uint32_t p26 = and_or(w >> 8, 0x000F000Fu, mag), p37 = and_or(w >> 12, 0x000F000Fu, mag);
@@ -135,7 +138,7 @@ __device__ __forceinline__ void dequant_row(const uint32_t* raw, T s, T b, uint4
       }
     } else {  // fp16, 8-bit codes
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < CH; ++c) {
         uint32_t r[4];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -180,7 +183,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&ready[s], 128);
+      mbar_init(&ready[s], 256);
       mbar_init(&empty[s], 1);
     }
     mbar_init(accf, 1);
@@ -254,9 +257,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     }
     __syncwarp();
   } else {
-    // ---- transform (quantized formats) and epilogue: thread = weight row -------------------
+    // ---- transform (quantized formats) and epilogue: two threads per weight row ------------
     pdl_wait();
     const int r = 32 * (warp & 3) + lane;  // tensor-memory lane of this warp's window
+    const int hf = (warp - 2) >> 2;        // which half of the row's codes / which column chunks
     const int n = row0 + r;
     const bool nv = n < a.N;
     if constexpr (BITS != 0) {
@@ -306,20 +310,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
           }
 #pragma unroll
           for (int i = 0; i < LY::NA; ++i) {
-            const uint4* src = reinterpret_cast<const uint4*>(tileR(st, i) + r * WPG * 4);
-            uint32_t raw[WPG];
+            constexpr int HW = WPG / 2;  // code words of half a row
+            const uint4* src = reinterpret_cast<const uint4*>(tileR(st, i) + r * WPG * 4 + hf * HW * 4);
+            uint32_t raw[HW];
 #pragma unroll
-            for (int v = 0; v < WPG / 4; ++v) {
+            for (int v = 0; v < HW / 4; ++v) {
               const uint4 q = src[v];
               raw[4 * v] = q.x; raw[4 * v + 1] = q.y; raw[4 * v + 2] = q.z; raw[4 * v + 3] = q.w;
             }
-            uint4 o[8];
+            uint4 o[4];
             const T sj = i ? half_of(usc, j) : half_of(sc, j);
             const T bj = i ? half_of(ubc, j) : half_of(bc, j);
-            dequant_row<T, BITS>(raw, sj, bj, o);
+            dequant_row<T, BITS, 4>(raw, sj, bj, o);
             unsigned char* dst = tileA(st, i) + r * 128;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + ((c ^ (r & 7)) << 4)) = o[c];
+            for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(dst + (((4 * hf + c) ^ (r & 7)) << 4)) = o[c];
           }
           fence_proxy_async();
           mbar_arrive(&ready[st]);
@@ -342,7 +347,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
       const T* res = static_cast<const T*>(a.res);
       T* out = static_cast<T*>(a.out);
       const float bn = (bias && nv) ? A::to_f(bias[n]) : 0.0f;
-      for (int c0 = 0; c0 < ntok && tok0 + c0 < a.M; c0 += 32) {
+      for (int c0 = 32 * hf; c0 < ntok && tok0 + c0 < a.M; c0 += 64) {
         uint32_t v[32];
         tmem_ld32(tmem + lane_base + c0, v);
         uint32_t u[32];
