@@ -18,11 +18,12 @@
 //               operand tile; quantized: the raw code rows).
 //   warp 1      allocates tensor memory; one thread issues 4 MMAs (K = 16 each) per stage and
 //               commits them to the stage's "empty" barrier; frees tensor memory at the end.
-//   warps 2..9  two threads per weight row (warps w and w + 4 share the row window of
-//               tensor-memory lanes 32 (w % 4) ..): each turns half of the stage's codes of
-//               its row into the operand tile (128-byte swizzled K-major rows; scales and
-//               biases read 8 groups at a time, a block ahead), then the pair runs the
-//               epilogue out of tensor memory on alternate 32-column chunks.
+//   warps 2..   two (quantized) or four (dense) threads per weight row (warps w, w + 4, ..
+//               share the row window of
+//               tensor-memory lanes 32 (w % 4) ..): each turns a slice of the stage's codes
+//               of its row into the operand tile (128-byte swizzled K-major rows; scales and
+//               biases read 8 groups at a time, a block ahead), then they run the epilogue
+//               out of tensor memory on interleaved 32-column chunks.
 // Every wait is bounded (sm100::kWaitCycles); a wait that runs out records a fault
 // (vella_qgemm reports it) and the kernel finishes without waiting again.
 //
@@ -54,7 +55,10 @@ using namespace sm100;
 constexpr int kTcRows = 128;     // weight rows per CTA (MMA M)
 constexpr int kTcTok = 256;      // tokens per CTA (largest MMA N)
 constexpr int kTcK = 64;         // K elements per stage
-constexpr int kTcThreads = 320;  // 10 warps
+// Transform/epilogue warps: 8 for the quantized formats (two threads per weight row), 16 for
+// dense weights (no transform: four threads per row share the epilogue).
+template <int BITS> constexpr int tc_xw() { return BITS ? 8 : 16; }
+template <int BITS> constexpr int tc_threads() { return 64 + 32 * tc_xw<BITS>(); }
 
 template <int BITS, bool GATE>
 struct TcLayout {
@@ -154,8 +158,10 @@ __device__ __forceinline__ void dequant_row(const uint32_t* raw, T s, T b, uint4
 }
 
 template <typename T, int BITS, bool GATE>
-__global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ TcArgs a) {
+__global__ void __launch_bounds__(tc_threads<BITS>(), 1) tc_gemm_kernel(const __grid_constant__ TcArgs a) {
   using A = Act<T>;
+  constexpr int kTcXW = tc_xw<BITS>();
+  constexpr int kTcParts = kTcXW / 4;  // threads per weight row (each a slice of its codes)
   using LY = TcLayout<BITS, GATE>;
   constexpr int NS = LY::NS;
   constexpr int WPG = BITS ? kTcK * BITS / 32 : 0;  // 32-bit code words per row and stage
@@ -183,7 +189,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&ready[s], 256);
+      mbar_init(&ready[s], 32 * kTcXW);
       mbar_init(&empty[s], 1);
     }
     mbar_init(accf, 1);
@@ -260,7 +266,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     // ---- transform (quantized formats) and epilogue: two threads per weight row ------------
     pdl_wait();
     const int r = 32 * (warp & 3) + lane;  // tensor-memory lane of this warp's window
-    const int hf = (warp - 2) >> 2;        // which half of the row's codes / which column chunks
+    const int hf = (warp - 2) >> 2;        // which slice of the row's codes / which column chunks
     const int n = row0 + r;
     const bool nv = n < a.N;
     if constexpr (BITS != 0) {
@@ -310,21 +316,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
           }
 #pragma unroll
           for (int i = 0; i < LY::NA; ++i) {
-            constexpr int HW = WPG / 2;  // code words of half a row
-            const uint4* src = reinterpret_cast<const uint4*>(tileR(st, i) + r * WPG * 4 + hf * HW * 4);
+            constexpr int HW = WPG / kTcParts;  // code words of this thread's slice
+            constexpr int CH = 8 / kTcParts;    // 8-element chunks of the slice
+            const unsigned char* sp0 = tileR(st, i) + r * WPG * 4 + hf * HW * 4;
             uint32_t raw[HW];
+            if constexpr (HW >= 4) {
 #pragma unroll
-            for (int v = 0; v < HW / 4; ++v) {
-              const uint4 q = src[v];
-              raw[4 * v] = q.x; raw[4 * v + 1] = q.y; raw[4 * v + 2] = q.z; raw[4 * v + 3] = q.w;
+              for (int v = 0; v < HW / 4; ++v) {
+                const uint4 q = reinterpret_cast<const uint4*>(sp0)[v];
+                raw[4 * v] = q.x; raw[4 * v + 1] = q.y; raw[4 * v + 2] = q.z; raw[4 * v + 3] = q.w;
+              }
+            } else {
+              const uint2 q = *reinterpret_cast<const uint2*>(sp0);
+              raw[0] = q.x; raw[1] = q.y;
             }
-            uint4 o[4];
+            uint4 o[CH];
             const T sj = i ? half_of(usc, j) : half_of(sc, j);
             const T bj = i ? half_of(ubc, j) : half_of(bc, j);
-            dequant_row<T, BITS, 4>(raw, sj, bj, o);
+            dequant_row<T, BITS, CH>(raw, sj, bj, o);
             unsigned char* dst = tileA(st, i) + r * 128;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(dst + (((4 * hf + c) ^ (r & 7)) << 4)) = o[c];
+            for (int c = 0; c < CH; ++c) *reinterpret_cast<uint4*>(dst + (((CH * hf + c) ^ (r & 7)) << 4)) = o[c];
           }
           fence_proxy_async();
           mbar_arrive(&ready[st]);
@@ -347,7 +359,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
       const T* res = static_cast<const T*>(a.res);
       T* out = static_cast<T*>(a.out);
       const float bn = (bias && nv) ? A::to_f(bias[n]) : 0.0f;
-      for (int c0 = 32 * hf; c0 < ntok && tok0 + c0 < a.M; c0 += 64) {
+      for (int c0 = 32 * hf; c0 < ntok && tok0 + c0 < a.M; c0 += 32 * kTcParts) {
         uint32_t v[32];
         tmem_ld32(tmem + lane_base + c0, v);
         uint32_t u[32];
@@ -387,7 +399,7 @@ int launch_tc_t(const TcArgs& a, cudaStream_t stream) {
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
   const dim3 grid((a.M + a.tt - 1) / a.tt, (a.N + kTcRows - 1) / kTcRows);
-  return launch_kernel(k, grid, dim3(kTcThreads), LY::TOTAL, stream, a);
+  return launch_kernel(k, grid, dim3(tc_threads<BITS>()), LY::TOTAL, stream, a);
 }
 
 template <typename T, int BITS>
