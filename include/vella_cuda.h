@@ -353,7 +353,8 @@ VELLA_API int vella_whisper_init_random(vella_whisper* w, uint64_t seed, float s
  * dec.ln2, dec.cq, dec.ckv (cross k|v rows, k's bias zero), dec.co, dec.ln3, dec.fc1, dec.fc2;
  * whole model: conv1 (K padded to a multiple of 64 with zero columns), conv2, enc_pos,
  * enc_ln, dec_ln, embed (token embedding = vocabulary projection), dec_pos, and the
- * activation enc_out [n_audio, d_model]. */
+ * activations enc_out [n_audio, d_model] (the last encoded window) and xkv (the cross-
+ * attention K|V of every stream and decoder layer, [streams][dec_layers][n_audio][2 d_model]). */
 VELLA_API int vella_whisper_tensor(vella_whisper* w, const char* name, int32_t layer, void** ptr, size_t* bytes);
 /* Encoder over one window per stream: mel fp32 [streams][n_mels][2 * n_audio] (host or
  * device), then the cross-attention K/V of every decoder layer, per stream. */

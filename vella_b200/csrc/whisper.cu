@@ -778,6 +778,7 @@ int vella_whisper_tensor(vella_whisper* w, const char* name, int32_t layer, void
   if (n == "enc_pos") return ret(w->enc_pos, (size_t)c.n_audio * c.d_model * e);
   if (n == "dec_pos") return ret(w->dec_pos, (size_t)c.max_target * c.d_model * e);
   if (n == "enc_out") return ret(w->enc_out, (size_t)c.n_audio * c.d_model * e);
+  if (n == "xkv") return ret(w->xkv, (size_t)w->S * xkv_stream_elems(c) * e);
   if (head == "conv1") return lin(w->conv1, part);
   if (head == "conv2") return lin(w->conv2, part);
   if (head == "embed") return lin(w->embed, part);
