@@ -891,6 +891,23 @@ def run_profile_pass(args):
     return {"profile": "prefill(16) + 2 passes", "passes": sd.stats()["passes"]}
 
 
+def run_profile_tree(args):
+    """A short tree-verification run for an ncu launch list: the headline shapes cut to 4
+    target and 2 draft layers (per-layer kernels are what the list is for), 32 streams, a
+    64-position prefix, branching 3,2,2,1 at temperature 0.7, 4 tokens per stream after a
+    2-token warm-up decode."""
+    global PREFIX, TARGET, DRAFT
+    saved = PREFIX, TARGET, DRAFT
+    PREFIX = 64
+    TARGET = dict(TARGET, n_layers=4)
+    DRAFT = dict(DRAFT, n_layers=2)
+    try:
+        r = run_spec_tree(0, 0, TREE_STREAMS, TREE_BRANCHING, TREE_TEMPERATURE, 4)
+    finally:
+        PREFIX, TARGET, DRAFT = saved
+    return {"profile": "tree verification, 4+2 layers, 32 streams", "passes": r["passes"]}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -903,9 +920,13 @@ def main():
     ap.add_argument("--no-tree", action="store_true", help="spec workload: skip the tree + sampling measurement")
     ap.add_argument("--shape", default="", help="gemm workload: one case 'bits,N,K,M' instead of the sweep")
     ap.add_argument("--profile-pass", action="store_true", help="short run for an ncu launch list")
+    ap.add_argument("--profile-tree", action="store_true", help="short tree-verification run for an ncu launch list")
     args = ap.parse_args()
     if args.profile_pass:
         print(json.dumps(run_profile_pass(args)))
+        return
+    if args.profile_tree:
+        print(json.dumps(run_profile_tree(args)))
         return
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

@@ -170,8 +170,7 @@ __global__ void rope_append_kernel(const T* __restrict__ qkv, T* __restrict__ q_
     x2 = A::to_f(A::from_f(A::to_f(nw[i + half]) * A::to_f(A::from_f(x2 * r))));
   }
   const float2 c = cs[(size_t)pos * half + i];
-  const float y1 = x1 * c.x - x2 * c.y;
-  const float y2 = x1 * c.y + x2 * c.x;
+  const float y1 = rope_rot1(x1, x2, c), y2 = rope_rot2(x1, x2, c);
   if (is_q) {
     T* o = q_out + ((size_t)m * H + hidx) * hd;
     o[i] = A::from_f(y1);

@@ -35,6 +35,29 @@ struct TreeView {
   int node0 = 0;
 };
 
+// Half rotation of RoPE with one rounding order everywhere (the standalone kernel and the
+// fused GEMM epilogue): y1 = x1 cos - x2 sin, y2 = x1 sin + x2 cos.
+__device__ __forceinline__ float rope_rot1(float x1, float x2, float2 c) {
+  return __fmaf_rn(x1, c.x, -__fmul_rn(x2, c.y));
+}
+__device__ __forceinline__ float rope_rot2(float x1, float x2, float2 c) {
+  return __fmaf_rn(x1, c.y, __fmul_rn(x2, c.x));
+}
+
+// RoPE + KV-append epilogue of the q|k|v projection (head_dim 128, no q/k norm, no tree),
+// fused into the small-M streaming GEMM: output rows of head h < H go to q [M][H][128]
+// rotated, h < H + KV to the K cache at the row's position rotated, the rest to the V cache.
+struct RopeEpi {
+  const float2* cs = nullptr;  // [positions][64] (cos, sin)
+  void* q = nullptr;
+  void* kc = nullptr;          // layer's K cache of stream 0; stream s adds s * kv_ss elements
+  void* vc = nullptr;
+  PosRef pr{};
+  int H = 0, KV = 0, max_seq = 0;
+  long long kv_ss = 0;
+  int* err = nullptr;          // bit 1: a position past the cache
+};
+
 constexpr int kAttnChunk = 64;   // keys per chunk (absolute-position aligned)
 constexpr int kAttnRows = 64;    // query rows x query heads per cluster (query block = 64 / GQ rows)
 constexpr int kAttnCluster = 8;  // CTAs per (kv head, query block); chunk c goes to CTA c % 8

@@ -445,13 +445,23 @@ int model_tensor(Model* m, const std::string& name, int layer, void** ptr, size_
 }
 
 int model_gemm(Model* m, const QWeight& w, const void* x, int rows, void* out, int epilogue, const void* residual,
-               const QWeight* up, cudaStream_t s) {
+               const QWeight* up, cudaStream_t s, const RopeEpi* rope) {
   vella_qgemm_desc d{rows, w.n, w.k, m->cfg.bits, 64, m->cfg.dtype, epilogue};
   QgemmPlan p;
   if (!qgemm_plan(d, &p)) return fail(VELLA_E_UNSUPPORTED, "model gemm %dx%dx%d", rows, w.n, w.k);
   if (p.workspace > m->gemm_ws_bytes) return fail(VELLA_E_INVALID, "model gemm workspace too small");
   return qgemm_launch(d, p, x, w.w, w.s, w.b, up ? up->w : nullptr, up ? up->s : nullptr, up ? up->b : nullptr,
-                      nullptr, residual, out, m->gemm_ws, s);
+                      nullptr, residual, out, m->gemm_ws, s, rope);
+}
+
+// True when the q|k|v projection of M rows runs on the streaming kernel, which can apply
+// RoPE and append K/V in its epilogue (head_dim 128, no q/k norm, no tree rows).
+bool fuse_rope(Model* m, const Layer& L, int M, const TreeView* tree) {
+  const vella_model_cfg& c = m->cfg;
+  if (tree || L.q_norm || L.k_norm || c.head_dim != 128) return false;
+  vella_qgemm_desc d{M, L.qkv.n, L.qkv.k, c.bits, 64, c.dtype, VELLA_EPI_NONE};
+  QgemmPlan p;
+  return qgemm_plan(d, &p) && p.stream;
 }
 
 int model_forward(Model* m, PosRef pr, int rows, int streams, int stream0, const int* tok, int tok_ss, const int* P,
@@ -480,10 +490,17 @@ int model_forward(Model* m, PosRef pr, int rows, int streams, int stream0, const
     char* kc = static_cast<char*>(m->kcache(l)) + kv0;
     char* vc = static_cast<char*>(m->vcache(l)) + kv0;
     if ((rc = launch_rmsnorm(dt, m->xn, m->h, L.attn_norm, M, d, c.rms_eps, s))) return rc;
-    if ((rc = model_gemm(m, L.qkv, m->xn, M, m->qkv_out, VELLA_EPI_NONE, nullptr, nullptr, s))) return rc;
-    if ((rc = launch_rope_append(dt, m->qkv_out, m->q, kc, vc, m->rope, L.q_norm, L.k_norm, c.rms_eps, pr, M, H, KV, hd,
-                                 c.max_seq, m->err, s, m->kv_ss, tv)))
-      return rc;
+    if (fuse_rope(m, L, M, tree)) {
+      RopeEpi re;
+      re.cs = m->rope; re.q = m->q; re.kc = kc; re.vc = vc; re.pr = pr;
+      re.H = H; re.KV = KV; re.max_seq = c.max_seq; re.kv_ss = m->kv_ss; re.err = m->err;
+      if ((rc = model_gemm(m, L.qkv, m->xn, M, m->qkv_out, VELLA_EPI_NONE, nullptr, nullptr, s, &re))) return rc;
+    } else {
+      if ((rc = model_gemm(m, L.qkv, m->xn, M, m->qkv_out, VELLA_EPI_NONE, nullptr, nullptr, s))) return rc;
+      if ((rc = launch_rope_append(dt, m->qkv_out, m->q, kc, vc, m->rope, L.q_norm, L.k_norm, c.rms_eps, pr, M, H, KV,
+                                   hd, c.max_seq, m->err, s, m->kv_ss, tv)))
+        return rc;
+    }
     AttnView v;
     v.q = m->q; v.out = m->attn;
     v.q_rs = v.o_rs = (long long)H * hd;

@@ -94,8 +94,8 @@ int model_tensor(Model* m, const std::string& name, int layer, void** ptr, size_
 int model_forward(Model* m, PosRef pr, int rows, int streams, int stream0, const int* tok, int tok_ss, const int* P,
                   int logits_rows, cudaStream_t s, const TreeView* tree = nullptr);
 
-// GEMM with the model's workspace.
+// GEMM with the model's workspace (rope: the streaming kernel's RoPE + KV-append epilogue).
 int model_gemm(Model* m, const QWeight& w, const void* x, int rows, void* out, int epilogue, const void* residual,
-               const QWeight* up, cudaStream_t s);
+               const QWeight* up, cudaStream_t s, const RopeEpi* rope = nullptr);
 
 }  // namespace vella

@@ -39,6 +39,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "layers.cuh"
 #include "sm100.cuh"
 
 namespace vella {
@@ -94,6 +95,8 @@ struct SArgs {
   int* flags;      // [P][kRowWarps]: partial published, per warp (reset by the gatherer)
   int M, N, K, G, rowblocks, nkc, P;
   int has_bias, has_res, gelu;
+  int rope;     // RoPE + KV-append epilogue (q|k|v projection, 128-row blocks = heads)
+  RopeEpi re;
 };
 
 using namespace sm100;
@@ -614,6 +617,54 @@ __global__ void __launch_bounds__(kThreads, LIGHT ? 2 : 1) qgemm_stream_kernel(c
         epilogue(rb, up);
       }
       named_sync(kBarPair0 + pw, 64);  // the exchange area is free again
+    } else if (a.rope) {
+      // head rb: dims 0..63 live in warps 0..3, their rotation partners 64..127 in warps
+      // 4..7; both are rounded to T first (the projection's output), then rotated
+      const int pw = warp & 3;
+      float* rp = red + pw * 16 * TOK;
+      if (warp >= 4) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) rp[((e >> 1) * 8 + r) * TOK + nt * 8 + 2 * cq + (e & 1)] = acc[nt][e];
+      }
+      named_sync(kBarPair0 + pw, 64);
+      if (warp < 4) {
+        const RopeEpi& re = a.re;
+        const int H = re.H, KV = re.KV;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int tok = nt * 8 + 2 * cq + (e & 1);
+            if (tok >= mc) continue;
+            const int i = (e >> 1) ? slot1 : slot0;  // 0..63
+            const float x1 = A::to_f(A::from_f(acc[nt][e]));
+            const float x2 = A::to_f(A::from_f(rp[((e >> 1) * 8 + r) * TOK + nt * 8 + 2 * cq + (e & 1)]));
+            const int pos = re.pr.pos(tok);
+            if (pos < 0 || pos >= re.max_seq) {
+              atomicOr(re.err, 2);
+              continue;
+            }
+            float y1 = x1, y2 = x2;
+            if (rb < H + KV) {
+              const float2 c = re.cs[(size_t)pos * 64 + i];
+              y1 = rope_rot1(x1, x2, c);
+              y2 = rope_rot2(x1, x2, c);
+            }
+            T* dst;
+            if (rb < H) {
+              dst = static_cast<T*>(re.q) + ((size_t)tok * H + rb) * 128;
+            } else {
+              const size_t so = (size_t)re.pr.stream_of(tok) * re.kv_ss;
+              T* base = static_cast<T*>(rb < H + KV ? re.kc : re.vc) + so;
+              dst = base + ((size_t)(rb < H + KV ? rb - H : rb - H - KV) * re.max_seq + pos) * 128;
+            }
+            dst[i] = A::from_f(y1);
+            dst[i + 64] = A::from_f(y2);
+          }
+      }
+      named_sync(kBarPair0 + pw, 64);
     } else {
       epilogue(rb, acc);
     }
@@ -676,7 +727,7 @@ int stream_flag_count(int P) { return P * kRowWarps; }
 int stream_launch(const vella_qgemm_desc& d, int P, bool light, const void* x, const void* w, const void* scales,
                   const void* biases, const void* up_w, const void* up_scales, const void* up_biases,
                   const void* bias, const void* residual, void* out, int* flags, float* partial,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, const RopeEpi* rope) {
   SArgs a;
   std::memset(&a, 0, sizeof a);
   const bool gate = d.epilogue == VELLA_EPI_SILU_GATE;
@@ -718,6 +769,12 @@ int stream_launch(const vella_qgemm_desc& d, int P, bool light, const void* x, c
   a.has_bias = epi_bias(d.epilogue);
   a.has_res = epi_residual(d.epilogue);
   a.gelu = epi_gelu(d.epilogue);
+  if (rope) {
+    if (gate || d.epilogue != VELLA_EPI_NONE || d.n % 128 != 0 || d.n / 128 != rope->H + 2 * rope->KV)
+      return fail(VELLA_E_INVALID, "stream GEMM: RoPE epilogue needs a plain q|k|v projection of 128-row heads");
+    a.rope = 1;
+    a.re = *rope;
+  }
   if (light && d.bits != 4) return fail(VELLA_E_INVALID, "stream GEMM: two CTAs per SM only for int4");
   if (d.dtype == VELLA_BF16) {
     switch (d.bits) {
