@@ -255,11 +255,13 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   }
 }
 
-template <typename T, int HD>
-__global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(128) attn_kernel(const AttnArgs a) {
+// CS = kAttnCluster: the key chunks of a query block are split over a cluster (decode: one
+// query block per stream); CS = 1: one CTA walks all chunks of its query block (launches
+// with several query blocks per stream: tree verification, prefill, the Whisper encoder).
+template <typename T, int HD, int CS>
+__global__ void __cluster_dims__(CS, 1, 1) __launch_bounds__(128) attn_kernel(const AttnArgs a) {
   using LY = AttnLayout<HD>;
   constexpr int C = kAttnChunk;
-  constexpr int CS = kAttnCluster;
   constexpr int RS = LY::RS;
   constexpr int NK = HD / 16;  // k16 steps of Q.K^T
   constexpr int ND = HD / 8;   // n8 tiles of the output
@@ -568,19 +570,25 @@ __global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logit
 
 size_t attn_smem_bytes(int hd) { return hd == 128 ? AttnLayout<128>::BYTES : AttnLayout<64>::BYTES; }
 
-template <typename T, int HD>
-int launch_attn_t(const AttnArgs& a, int batch, cudaStream_t s) {
+template <typename T, int HD, int CS>
+int launch_attn_cs(const AttnArgs& a, int nqb, int batch, cudaStream_t s) {
   const size_t smem = attn_smem_bytes(HD);
   static int configured[64] = {0};
   int dev = 0;
   VELLA_CUDA_TRY(cudaGetDevice(&dev));
   if (!configured[dev & 63]) {
-    VELLA_CUDA_TRY(cudaFuncSetAttribute(attn_kernel<T, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    VELLA_CUDA_TRY(cudaFuncSetAttribute(attn_kernel<T, HD, CS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)attn_smem_bytes(HD)));
     configured[dev & 63] = 1;
   }
+  return launch_kernel(attn_kernel<T, HD, CS>, dim3(a.KV * CS, nqb, batch), dim3(128), smem, s, a);
+}
+
+template <typename T, int HD>
+int launch_attn_t(const AttnArgs& a, int batch, cudaStream_t s) {
   const int nqb = (a.M + a.QB - 1) / a.QB;
-  return launch_kernel(attn_kernel<T, HD>, dim3(a.KV * kAttnCluster, nqb, batch), dim3(128), smem, s, a);
+  // one query block per stream: split its keys over a cluster; several: a CTA per block
+  return nqb > 1 ? launch_attn_cs<T, HD, 1>(a, nqb, batch, s) : launch_attn_cs<T, HD, kAttnCluster>(a, nqb, batch, s);
 }
 
 }  // namespace
