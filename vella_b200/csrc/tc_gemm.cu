@@ -270,13 +270,20 @@ __global__ void __launch_bounds__(tc_threads<BITS>(), 1) tc_gemm_kernel(const __
     const int n = row0 + r;
     const bool nv = n < a.N;
     if constexpr (BITS != 0) {
+      // transform mapping: adjacent lanes take the slices of one weight row, so the lanes of
+      // a quarter-warp read contiguous code bytes (the epilogue keeps thread = tensor-memory
+      // lane); the swizzled operand writes of those lanes fall in distinct 16-byte units
+      const int xi = (warp - 2) * 32 + lane;
+      const int tr = xi / kTcParts, tp = xi % kTcParts;
+      const int tn = row0 + tr;
+      const bool tnv = tn < a.N;
       // scales/biases of this row: blocks of 8 groups (two 32-bit words = 4 packed values
       // each half), the next block's loads in flight while this one is used
-      const size_t rowg = (size_t)(nv ? n : 0) * G;
+      const size_t rowg = (size_t)(tnv ? tn : 0) * G;
       const bool vec = (G % 8) == 0;  // rows start 16-byte aligned: one 16-byte load per array
       auto load_block = [&](const void* base, int gb, uint32_t (&wv)[4]) {
         const T* p = static_cast<const T*>(base) + rowg + gb;
-        if (!nv || gb >= G) {
+        if (!tnv || gb >= G) {
           wv[0] = wv[1] = wv[2] = wv[3] = 0u;
         } else if (vec) {
           const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
@@ -318,7 +325,7 @@ __global__ void __launch_bounds__(tc_threads<BITS>(), 1) tc_gemm_kernel(const __
           for (int i = 0; i < LY::NA; ++i) {
             constexpr int HW = WPG / kTcParts;  // code words of this thread's slice
             constexpr int CH = 8 / kTcParts;    // 8-element chunks of the slice
-            const unsigned char* sp0 = tileR(st, i) + r * WPG * 4 + hf * HW * 4;
+            const unsigned char* sp0 = tileR(st, i) + tr * WPG * 4 + tp * HW * 4;
             uint32_t raw[HW];
             if constexpr (HW >= 4) {
 #pragma unroll
@@ -334,9 +341,9 @@ __global__ void __launch_bounds__(tc_threads<BITS>(), 1) tc_gemm_kernel(const __
             const T sj = i ? half_of(usc, j) : half_of(sc, j);
             const T bj = i ? half_of(ubc, j) : half_of(bc, j);
             dequant_row<T, BITS, CH>(raw, sj, bj, o);
-            unsigned char* dst = tileA(st, i) + r * 128;
+            unsigned char* dst = tileA(st, i) + tr * 128;
 #pragma unroll
-            for (int c = 0; c < CH; ++c) *reinterpret_cast<uint4*>(dst + (((CH * hf + c) ^ (r & 7)) << 4)) = o[c];
+            for (int c = 0; c < CH; ++c) *reinterpret_cast<uint4*>(dst + (((CH * tp + c) ^ (tr & 7)) << 4)) = o[c];
           }
           fence_proxy_async();
           mbar_arrive(&ready[st]);
