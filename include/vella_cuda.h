@@ -336,7 +336,26 @@ typedef struct vella_whisper_stats {
   float prefill_ms;  /* last decode: the prompt's forward and first token                     */
   float decode_ms;   /* last decode: every following step                                     */
   int32_t tokens;    /* tokens produced by the last decode                                    */
+  float sum_logprob; /* with token rules set: the log-probabilities of the chosen tokens of the
+                        last decode (end-of-text included), summed in step order (stream 0)    */
 } vella_whisper_stats;
+
+/* Token rules of the reference's GPU-side greedy (WhisperModel.pipelinedGreedy with its rule
+ * masks, WhisperModel.swift:311-372): per step the suppress list (and at the first step the
+ * begin-suppress list) is masked; the token's log-probability is taken under the final row;
+ * no-timestamps is never chosen; the first token is a timestamp in
+ * [timestamp_begin, timestamp_begin + round(n_audio / 30)]; text is masked when the
+ * timestamps' total probability beats every text token; after a timestamp, timestamps are
+ * masked when the token before it was one too (or there is none), else text below eot. */
+typedef struct vella_whisper_rules {
+  int32_t eot;
+  int32_t no_timestamps;
+  int32_t timestamp_begin;
+  const int32_t* suppress;        /* host array of token ids */
+  int32_t n_suppress;
+  const int32_t* begin_suppress;  /* host array of token ids, first step only */
+  int32_t n_begin_suppress;
+} vella_whisper_rules;
 
 typedef struct vella_whisper vella_whisper;
 
@@ -369,6 +388,9 @@ VELLA_API int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int3
  * stats' tokens field counts all streams' tokens. */
 VELLA_API int vella_whisper_decode_batch(vella_whisper* w, const int32_t* prompt, int32_t n_prompt,
                                          int32_t max_tokens, int32_t* out_tokens);
+/* Token rules for the following decodes (NULL: plain argmax, the default).  The ids must lie
+ * in the vocabulary with eot < timestamp_begin; the masks are built on the device here. */
+VELLA_API int vella_whisper_set_rules(vella_whisper* w, const vella_whisper_rules* rules);
 /* Teacher-forced logits [T, vocab] (dtype) of the token sequence (positions 0..T-1); one-
  * stream handles only (as vella_whisper_decode). */
 VELLA_API int vella_whisper_score(vella_whisper* w, const int32_t* tokens, int32_t T, void* logits, int32_t on_host);

@@ -20,7 +20,8 @@ Arithmetic as the library's kernels store it: every GEMM accumulates in fp32 and
 once after its epilogue (bias, GELU, residual); LayerNorm statistics in fp32 with the
 normalised value rounded to the activation dtype before ``w * x + b`` (``WhisperFusedDecode
 .swift:204-251``, the MLX row algorithm, here with one final rounding); GELU is the erf form.
-Plain greedy argmax (the reference's suppress/timestamp rules are not part of this path).
+Greedy argmax, plain or under the token rules of the reference's GPU-side greedy
+(``WhisperModel.swift:311-372``, ``rule_select`` below).
 
 Parity: the reference (Swift + MLX) cannot run on this machine; the floating-point
 arithmetic is parity unpinned against MLX.  The sinusoid table rule is pinned by the
@@ -215,3 +216,69 @@ def greedy(cfg: WhisperConfig, W: dict, enc: np.ndarray, prompt, n_tokens: int):
         row = logits(cfg, W, hid)[0]
         pos += 1
     return toks, np.stack(rows)
+
+
+# ---------------------------------------------------------------------------------------
+# Token rules of the reference's GPU-side greedy decode (WhisperModel.swift:311-372)
+# ---------------------------------------------------------------------------------------
+
+@dataclass
+class TokenRules:
+    """Token ids and suppress lists of a checkpoint's tokenizer and generation config."""
+    eot: int
+    no_timestamps: int
+    timestamp_begin: int
+    suppress: tuple = ()
+    begin_suppress: tuple = ()
+    max_source_positions: int = 1500  # encoder frames; 30 s windows
+
+    def last_allowed(self) -> int:
+        # Swift's Double.rounded() rounds half away from zero (WhisperModel.swift:321)
+        q = self.max_source_positions / 30.0
+        return self.timestamp_begin + int(math.floor(q + 0.5))
+
+
+def _lse(x: np.ndarray) -> float:
+    m = float(np.max(x))
+    if m == -math.inf:
+        return -math.inf
+    return m + math.log(float(np.sum(np.exp((x - m).astype(np.float64)))))
+
+
+def rule_select(row: np.ndarray, step: int, prev, before_prev, r: TokenRules):
+    """One choice of the rules (``select`` at WhisperModel.swift:340-359): the suppress mask
+    (begin-suppress too at step 0), log-probabilities of the filtered row, text masked when the
+    timestamp tokens' total probability beats every text token, no-timestamps always masked,
+    step 0 limited to the first timestamps; after a timestamp, timestamps are masked when the
+    token before it was one as well (or there is none), else text up to end-of-text.  Returns
+    the token (lowest index among equal maxima) and its log-probability under the final row."""
+    f = np.asarray(row, np.float64).copy()
+    V = f.shape[0]
+    begin = r.timestamp_begin
+    sup = list(r.suppress) + (list(r.begin_suppress) if step == 0 else [])
+    for t in sup:
+        if 0 <= t < V:
+            f[t] = -math.inf
+    lse = _lse(f)
+    lp = f - lse
+    ts_mass = _lse(lp[begin:])
+    max_text = float(np.max(lp[:begin]))
+    mask = np.zeros(V)
+    mask[r.no_timestamps] = -math.inf
+    if step == 0:
+        mask[:begin] = -math.inf
+        la = r.last_allowed()
+        if la + 1 < V:
+            mask[la + 1:] = -math.inf
+    if ts_mass > max_text:
+        mask[:begin] = -math.inf
+    if prev is not None:
+        last = prev >= begin
+        pen = before_prev >= begin if before_prev is not None else True
+        if last and pen:
+            mask[begin:] = -math.inf
+        if last and not pen:
+            mask[:r.eot] = -math.inf
+    final = f + mask
+    tok = int(np.argmax(final))
+    return tok, float(final[tok] - _lse(final)), final

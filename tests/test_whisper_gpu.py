@@ -232,3 +232,67 @@ def test_many_streams_follow_the_oracle():
     with pytest.raises(_lib.VellaError):
         m.decode(prompt, 4)  # one-stream entry point on a multi-stream handle
     m.close()
+
+
+def _rule_choices(row, step, prev, before_prev, r, tol):
+    """Tokens the rules may choose from a row known to within `tol` per logit: the oracle's
+    choice and every token within 2*tol of it, for the row as given and with the timestamp
+    block moved by +-2*tol (which covers a flip of the timestamp-mass comparison)."""
+    ok = set()
+    for shift in (0.0, 2 * tol, -2 * tol):
+        x = np.asarray(row, np.float64).copy()
+        x[r.timestamp_begin:] += shift
+        tok, _, final = Wh.rule_select(x, step, prev, before_prev, r)
+        if np.isfinite(final[tok]):
+            ok |= set(np.nonzero(final >= final[tok] - 2 * tol)[0].tolist())
+    return ok
+
+
+def test_token_rules_follow_the_oracle(tiny):
+    """Decode with the reference's token rules (suppress and begin-suppress masks, timestamp
+    rules, no-timestamps masked): every token is one the oracle's rules allow on the
+    teacher-forced row, the first token is a timestamp and the second is not, the summed
+    log-probability matches the oracle's, a two-stream handle's stream 0 repeats the
+    one-stream decode, and clearing the rules restores plain argmax."""
+    from dataclasses import replace
+
+    from vella_b200 import _lib
+    from vella_b200 import whisper as VW
+    m, oc, W, mel, enc_ref = tiny
+    prompt = [50258, 50259, 50359, 50363]
+    n = 16
+    plain = m.decode(prompt, n).tokens
+    V = oc.vocab
+    r = Wh.TokenRules(eot=50257, no_timestamps=V - 3, timestamp_begin=V - 2,
+                      suppress=[220, 50256, plain[1], plain[3]], begin_suppress=[50257, 220])
+    with pytest.raises(_lib.VellaError):
+        m.set_rules(eot=V, no_timestamps=V - 3, timestamp_begin=V - 2)
+    with pytest.raises(_lib.VellaError):
+        m.set_rules(eot=V - 1, no_timestamps=V - 3, timestamp_begin=V - 2)
+    m.set_rules(r.eot, r.no_timestamps, r.timestamp_begin, r.suppress, r.begin_suppress)
+    try:
+        got = m.decode(prompt, n).tokens
+        lp_gpu = m.stats()["sum_logprob"]
+        assert len(got) == n
+        assert got[0] >= r.timestamp_begin and got[1] < r.timestamp_begin, got[:2]
+        logits = Wh.score(oc, W, enc_ref, prompt + got[:-1])[len(prompt) - 1:]
+        lp_ref = 0.0
+        for j, t in enumerate(got):
+            prev = got[j - 1] if j >= 1 else None
+            bprev = got[j - 2] if j >= 2 else None
+            assert t in _rule_choices(logits[j], j, prev, bprev, r, LOGIT_TOL), (j, t)
+            _, _, final = Wh.rule_select(logits[j], j, prev, bprev, r)
+            lp_ref += float(final[t] - Wh._lse(final))
+        assert abs(lp_gpu - lp_ref) <= 2 * LOGIT_TOL * n, (lp_gpu, lp_ref)
+        assert m.decode(prompt, n).tokens == got  # replayed step graph
+    finally:
+        m.set_rules(None)
+    assert m.decode(prompt, n).tokens == plain
+    mb = VW.Whisper(replace(VW.TINY, streams=2))
+    mb.init_random(5, 0.02)
+    mb.encode(np.stack([mel, mel_of(oc, 8)]))
+    mb.set_rules(r.eot, r.no_timestamps, r.timestamp_begin, r.suppress, r.begin_suppress)
+    both = mb.decode_batch(prompt, n)
+    assert list(both[0]) == got
+    assert abs(mb.stats()["sum_logprob"] - lp_gpu) <= 1e-3 * max(1.0, abs(lp_gpu))
+    mb.close()

@@ -40,3 +40,39 @@ def test_layernorm_normalises_rows():
     y = Wh.layernorm(x, np.ones(384, np.float32), np.zeros(384, np.float32), 1e-5, "f32")
     assert np.allclose(y.mean(axis=1), 0, atol=1e-5)
     assert np.allclose(y.var(axis=1), 1, atol=1e-3)
+
+
+def test_token_rules_known_answers():
+    """Each rule of the reference's GPU-side greedy (WhisperModel.swift:311-372) on hand-made
+    rows: suppress lists, no-timestamps, step 0 limited to [begin, begin + frames / 30], text
+    masked when the timestamps' total probability beats every text token, and the two rules
+    after a timestamp."""
+    from oracle import whisper as Wh
+    r = Wh.TokenRules(eot=90, no_timestamps=99, timestamp_begin=100, suppress=(5,), begin_suppress=(7,),
+                      max_source_positions=300)
+    assert r.last_allowed() == 110
+    V = 130
+    row = np.full(V, -5.0, np.float32)
+    # step 0: text, end-of-text and late timestamps are masked; the best early timestamp wins
+    row0 = row.copy(); row0[3] = 9.0; row0[120] = 8.0; row0[104] = 2.0
+    tok, lp, final = Wh.rule_select(row0, 0, None, None, r)
+    assert tok == 104 and np.isneginf(final[:100]).all() and np.isneginf(final[111:]).all()
+    assert lp < 0
+    # later steps, text dominates: the suppressed token loses, the next best text token wins
+    row1 = row.copy(); row1[5] = 20.0; row1[6] = 19.0
+    assert Wh.rule_select(row1, 3, 10, 11, r)[0] == 6
+    row1[7] = 30.0  # begin-suppress applies at step 0 only
+    assert Wh.rule_select(row1, 3, 10, 11, r)[0] == 7
+    # no-timestamps is never chosen
+    row2 = row.copy(); row2[99] = 50.0; row2[40] = 1.0
+    assert Wh.rule_select(row2, 2, 10, 11, r)[0] == 40
+    # timestamp mass beats the best text token: text is masked
+    row3 = row.copy(); row3[100:] = 3.0; row3[40] = 4.0
+    assert Wh.rule_select(row3, 2, 10, 11, r)[0] >= 100
+    # after a timestamp preceded by text: text up to end-of-text masked (end-of-text allowed)
+    row4 = row.copy(); row4[40] = 9.0; row4[90] = 1.0; row4[95] = 2.0
+    assert Wh.rule_select(row4, 2, 105, 11, r)[0] == 95
+    # after two timestamps: every timestamp masked, text allowed
+    row5 = row.copy(); row5[40] = 3.0; row5[120] = 2.0
+    tok, lp, final = Wh.rule_select(row5, 3, 105, 104, r)
+    assert tok == 40 and np.isneginf(final[100:]).all() and np.isfinite(lp)

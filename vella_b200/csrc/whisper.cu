@@ -186,6 +186,122 @@ __global__ void wcommit_kernel(int* L, int* tok, const int* ys, int max_target, 
   L[st] = p + 1;
 }
 
+// ---- token rules of the reference's GPU-side greedy (WhisperModel.swift:311-372) --------
+struct WRules {
+  int eot, no_ts, begin, last_allowed;
+};
+constexpr int kRuleThreads = 512;
+
+__device__ __forceinline__ float rule_block_max(float v, float* red) {
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = -INFINITY;
+  for (int i = 0; i < kRuleThreads / 32; ++i) t = fmaxf(t, red[i]);
+  __syncthreads();
+  return t;
+}
+__device__ __forceinline__ float rule_block_sum(float v, float* red) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.0f;
+  for (int i = 0; i < kRuleThreads / 32; ++i) t += red[i];  // warps in order
+  __syncthreads();
+  return t;
+}
+
+// One choice per stream (block s, logits row s * rs + ro): the suppress mask of the step
+// (begin-suppress as well at step 0), log-probabilities of the filtered row, the timestamp
+// rules, argmax (lowest index among equal maxima) and the chosen token's log-probability
+// under the final row, added to lpsum[s].  The step is the stream's generated-token count
+// L[s] - n_prompt; the rules read the stream's two last generated tokens.
+template <typename T>
+__global__ void __launch_bounds__(kRuleThreads) wrules_kernel(const T* __restrict__ logits, int vocab, int rs, int ro,
+                                                               int* ys, float* lpsum, int* nonfinite,
+                                                               const float* __restrict__ sup_first,
+                                                               const float* __restrict__ sup_later, const int* L,
+                                                               const int* tok, const int* nprompt, int max_target,
+                                                               WRules r) {
+  using A = Act<T>;
+  __shared__ float red[kRuleThreads / 32];
+  __shared__ int redi[kRuleThreads / 32];
+  pdl_wait();
+  pdl_launch_next();
+  const int s = blockIdx.x, row = s * rs + ro;
+  const T* lg = logits + (size_t)row * vocab;
+  const int Ls = L[s], step = Ls - *nprompt;
+  const float* sup = step == 0 ? sup_first : sup_later;
+  // maxima of the filtered row (all tokens, text tokens); finiteness of the raw row
+  float mall = -INFINITY, mtext = -INFINITY;
+  bool bad = false;
+  for (int v = threadIdx.x; v < vocab; v += kRuleThreads) {
+    const float raw = A::to_f(lg[v]);
+    if (!isfinite(raw)) bad = true;
+    const float f = raw + sup[v];
+    mall = fmaxf(mall, f);
+    if (v < r.begin) mtext = fmaxf(mtext, f);
+  }
+  if (bad) atomicOr(nonfinite, 1);
+  mall = rule_block_max(mall, red);
+  mtext = rule_block_max(mtext, red);
+  float zall = 0.0f, zts = 0.0f;
+  for (int v = threadIdx.x; v < vocab; v += kRuleThreads) {
+    const float e = expf(A::to_f(lg[v]) + sup[v] - mall);
+    zall += e;
+    if (v >= r.begin) zts += e;
+  }
+  zall = rule_block_sum(zall, red);
+  zts = rule_block_sum(zts, red);
+  const float lse = mall + logf(zall);
+  const float ts_mass = logf(zts) + mall - lse, max_text = mtext - lse;
+  // the rules of this step
+  const bool first = step == 0;
+  const bool text_off = first || ts_mass > max_text;
+  bool ts_off = false, below_eot_off = false;
+  if (step >= 1) {
+    // the host keeps n_prompt + max_tokens <= max_target; the clamp keeps the reads in the row
+    const int* tk = tok + (size_t)s * max_target;
+    const int l1 = min(Ls - 1, max_target - 1), l2 = max(min(Ls - 2, max_target - 1), 0);
+    const bool last = tk[l1] >= r.begin;
+    const bool pen = step >= 2 ? tk[l2] >= r.begin : true;
+    ts_off = last && pen;
+    below_eot_off = last && !pen;
+  }
+  auto final = [&](int v) {
+    const float f = A::to_f(lg[v]) + sup[v];
+    const bool off = v == r.no_ts || (v < r.begin ? text_off : ts_off) || (below_eot_off && v < r.eot) ||
+                     (first && v > r.last_allowed);
+    return off ? -INFINITY : f;
+  };
+  float bv = -INFINITY;
+  int bi = INT32_MAX;
+  for (int v = threadIdx.x; v < vocab; v += kRuleThreads) {
+    const float f = final(v);
+    if (f > bv || (f == bv && v < bi)) { bv = f; bi = v; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { red[threadIdx.x >> 5] = bv; redi[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  bv = -INFINITY;
+  bi = INT32_MAX;
+  for (int i = 0; i < kRuleThreads / 32; ++i)
+    if (red[i] > bv || (red[i] == bv && redi[i] < bi)) { bv = red[i]; bi = redi[i]; }
+  __syncthreads();
+  float z = 0.0f;
+  for (int v = threadIdx.x; v < vocab; v += kRuleThreads) z += expf(final(v) - bv);
+  z = rule_block_sum(z, red);
+  if (threadIdx.x == 0) {
+    ys[row] = bi == INT32_MAX ? 0 : bi;
+    lpsum[s] += -logf(z);  // final[token] is the maximum
+  }
+}
+
 // Zeroes columns [c0, ld) of a row-major [rows, ld] array of 16-bit elements.
 __global__ void zero_cols_kernel(uint16_t* w, int ld, int c0) {
   for (int c = c0 + threadIdx.x; c < ld; c += blockDim.x) w[(size_t)blockIdx.x * ld + c] = 0;
@@ -251,6 +367,12 @@ struct vella_whisper {
   int *L = nullptr, *dzero = nullptr;            // [S] lengths, [S] zeros
   int *err = nullptr, *nonfinite = nullptr;
   void* argmax_sc = nullptr;
+  // token rules (vella_whisper_set_rules)
+  bool rules_on = false;
+  vella::WRules rules{};
+  float* rule_masks = nullptr;  // [2][vocab]: first step, later steps (0 or -inf)
+  float* lpsum = nullptr;       // [S] summed log-probabilities of the current decode
+  int* nprompt = nullptr;       // prompt length of the current decode
   void* gemm_ws = nullptr;
   size_t gemm_ws_bytes = 0;
   cudaStream_t stream = nullptr;
@@ -341,8 +463,11 @@ void* vcache(vella_whisper* w, int l) {
 
 // Decoder over `rows` rows, `streams` streams of rows / streams consecutive rows each (row m
 // at position pr.pos(m) of stream pr.stream_of(m); tokens from w->tok); the last
-// `logits_rows` rows go through the vocabulary projection and the argmax.
-int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, int streams, cudaStream_t s) {
+// `logits_rows` rows go through the vocabulary projection and the argmax, or, with token
+// rules set and rule_rs >= 0, stream s's choice comes from logits row s * rule_rs + rule_ro
+// under the rules.
+int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, int streams, cudaStream_t s,
+                    int rule_rs = -1, int rule_ro = 0) {
   const vella_whisper_cfg& c = w->cfg;
   if (streams < 1 || rows % streams) return fail(VELLA_E_INVALID, "whisper decoder: %d rows over %d streams", rows, streams);
   const int rps = rows / streams;
@@ -384,6 +509,19 @@ int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, int 
   if (logits_rows > 0) {
     const char* xr = static_cast<const char*>(w->dn) + (size_t)(rows - logits_rows) * d * w->elt;
     if ((rc = gemm(w, w->embed, xr, logits_rows, w->logits, VELLA_EPI_NONE, nullptr, s))) return rc;
+    if (w->rules_on && rule_rs >= 0) {
+      const float* sf = w->rule_masks;
+      const float* sl = w->rule_masks + c.vocab;
+      if (bf)
+        return launch_kernel(wrules_kernel<__nv_bfloat16>, dim3(streams), dim3(kRuleThreads), 0, s,
+                             static_cast<const __nv_bfloat16*>(w->logits), c.vocab, rule_rs, rule_ro, w->ys, w->lpsum,
+                             w->nonfinite, sf, sl, (const int*)w->L, (const int*)w->tok, (const int*)w->nprompt,
+                             c.max_target, w->rules);
+      return launch_kernel(wrules_kernel<__half>, dim3(streams), dim3(kRuleThreads), 0, s,
+                           static_cast<const __half*>(w->logits), c.vocab, rule_rs, rule_ro, w->ys, w->lpsum,
+                           w->nonfinite, sf, sl, (const int*)w->L, (const int*)w->tok, (const int*)w->nprompt,
+                           c.max_target, w->rules);
+    }
     if ((rc = launch_argmax(dt, w->logits, logits_rows, c.vocab, (size_t)c.vocab, w->ys, w->argmax_sc, w->nonfinite, s)))
       return rc;
   }
@@ -498,7 +636,7 @@ int run_step(vella_whisper* w) {
   auto enqueue = [&]() -> int {
     int rc;
     // one row per stream at its last committed token
-    if ((rc = decoder_forward(w, PosRef{w->L, -1, 1, 1}, w->S, w->S, w->S, s))) return rc;
+    if ((rc = decoder_forward(w, PosRef{w->L, -1, 1, 1}, w->S, w->S, w->S, s, 1, 0))) return rc;
     return commit(w, 1, 0, s);
   };
   if (!w->step_warm) {
@@ -637,6 +775,7 @@ int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whi
   const size_t o_logits = Q.take(R * (size_t)V * e);
   const size_t o_ints = Q.take((R + S * c.max_target + 2 * S + 8) * sizeof(int));
   const size_t o_amx = Q.take(argmax_scratch_bytes(w->R) + 512);
+  const size_t o_rule = Q.take((S + 64) * sizeof(float));
   const size_t o_ws = Q.take(std::max<size_t>(ws, 256));
   auto cleanup = [&]() {
     if (w->act) cudaFree(w->act);
@@ -683,6 +822,8 @@ int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whi
   w->err = w->dzero + S;  // err and nonfinite are adjacent (check_flags reads both)
   w->nonfinite = w->err + 1;
   w->argmax_sc = ab + o_amx;
+  w->lpsum = reinterpret_cast<float*>(ab + o_rule);
+  w->nprompt = reinterpret_cast<int*>(w->lpsum + S);
   w->gemm_ws = ab + o_ws;
   *out = w;
   return VELLA_OK;
@@ -693,6 +834,7 @@ int vella_whisper_destroy(vella_whisper* w) {
   cudaSetDevice(w->device);
   if (w->stream) cudaStreamSynchronize(w->stream);
   if (w->step_exec) cudaGraphExecDestroy(w->step_exec);
+  if (w->rule_masks) cudaFree(w->rule_masks);
   for (cudaEvent_t e : {w->ev0, w->ev1, w->ev2})
     if (e) cudaEventDestroy(e);
   if (w->act) cudaFree(w->act);
@@ -851,8 +993,10 @@ int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int32_t n_prom
   std::copy(prompt, prompt + n_prompt, init.begin());
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->tok, init.data(), n_prompt * sizeof(int), cudaMemcpyHostToDevice, s));
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->L, &n_prompt, sizeof(int), cudaMemcpyHostToDevice, s));
+  VELLA_CUDA_TRY(cudaMemcpyAsync(w->nprompt, &n_prompt, sizeof(int), cudaMemcpyHostToDevice, s));
+  VELLA_CUDA_TRY(cudaMemsetAsync(w->lpsum, 0, sizeof(float), s));
   VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
-  int rc = decoder_forward(w, PosRef{w->dzero, 0}, n_prompt, 1, 1, s);
+  int rc = decoder_forward(w, PosRef{w->dzero, 0}, n_prompt, 1, 1, s, 0, 0);
   if (rc) return rc;
   if ((rc = commit(w, 0, 0, s))) return rc;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev1, s));
@@ -880,6 +1024,8 @@ int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int32_t n_prom
   VELLA_CUDA_TRY(cudaStreamSynchronize(s));
   cudaEventElapsedTime(&w->stats.prefill_ms, w->ev0, w->ev1);
   cudaEventElapsedTime(&w->stats.decode_ms, w->ev1, w->ev2);
+  w->stats.sum_logprob = 0.0f;
+  if (w->rules_on) VELLA_CUDA_TRY(cudaMemcpy(&w->stats.sum_logprob, w->lpsum, sizeof(float), cudaMemcpyDeviceToHost));
   if ((rc = check_flags(w, "vella_whisper_decode"))) return rc;
   int n = produced;
   if (eot >= 0 && n > 0 && toks[n - 1] == eot) --n;  // the end-of-text token is not emitted
@@ -929,10 +1075,13 @@ int vella_whisper_decode_batch(vella_whisper* w, const int32_t* prompt, int32_t 
   for (int st = 0; st < S; ++st) std::copy(prompt, prompt + n_prompt, toks.begin() + (size_t)st * c.max_target);
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->tok, toks.data(), toks.size() * sizeof(int), cudaMemcpyHostToDevice, s));
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->L, lens.data(), S * sizeof(int), cudaMemcpyHostToDevice, s));
+  VELLA_CUDA_TRY(cudaMemcpyAsync(w->nprompt, &n_prompt, sizeof(int), cudaMemcpyHostToDevice, s));
+  VELLA_CUDA_TRY(cudaMemsetAsync(w->lpsum, 0, S * sizeof(float), s));
   VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
   // the prompts of all streams in one forward (stream st: rows st * n_prompt .., positions
   // 0 .. n_prompt - 1), then each stream's first token from its last prompt row
-  int rc = decoder_forward(w, PosRef{w->dzero, 0, n_prompt, 1}, S * n_prompt, S * n_prompt, S, s);
+  int rc = decoder_forward(w, PosRef{w->dzero, 0, n_prompt, 1}, S * n_prompt, S * n_prompt, S, s, n_prompt,
+                           n_prompt - 1);
   if (rc) return rc;
   if ((rc = commit(w, n_prompt, n_prompt - 1, s))) return rc;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev1, s));
@@ -943,11 +1092,53 @@ int vella_whisper_decode_batch(vella_whisper* w, const int32_t* prompt, int32_t 
   VELLA_CUDA_TRY(cudaStreamSynchronize(s));
   cudaEventElapsedTime(&w->stats.prefill_ms, w->ev0, w->ev1);
   cudaEventElapsedTime(&w->stats.decode_ms, w->ev1, w->ev2);
+  w->stats.sum_logprob = 0.0f;
+  if (w->rules_on) VELLA_CUDA_TRY(cudaMemcpy(&w->stats.sum_logprob, w->lpsum, sizeof(float), cudaMemcpyDeviceToHost));
   if ((rc = check_flags(w, "vella_whisper_decode_batch"))) return rc;
   for (int st = 0; st < S; ++st)
     std::copy(toks.begin() + (size_t)st * c.max_target + n_prompt,
               toks.begin() + (size_t)st * c.max_target + n_prompt + max_tokens, out_tokens + (size_t)st * max_tokens);
   w->stats.tokens = S * max_tokens;
+  return VELLA_OK;
+}
+
+int vella_whisper_set_rules(vella_whisper* w, const vella_whisper_rules* rules) {
+  if (!w) return fail(VELLA_E_INVALID, "vella_whisper_set_rules: NULL handle");
+  VELLA_CUDA_TRY(cudaSetDevice(w->device));
+  const vella_whisper_cfg& c = w->cfg;
+  const int V = c.vocab;
+  if (rules) {
+    const vella_whisper_rules& r = *rules;
+    auto in = [&](int t) { return t >= 0 && t < V; };
+    if (!in(r.eot) || !in(r.no_timestamps) || !in(r.timestamp_begin) || r.eot >= r.timestamp_begin ||
+        r.n_suppress < 0 || r.n_begin_suppress < 0 || (r.n_suppress > 0 && !r.suppress) ||
+        (r.n_begin_suppress > 0 && !r.begin_suppress))
+      return fail(VELLA_E_INVALID, "vella_whisper_set_rules: token ids outside the vocabulary of %d or eot >= "
+                  "timestamp_begin", V);
+  }
+  VELLA_CUDA_TRY(cudaStreamSynchronize(w->stream));
+  // the captured step holds the previous selection kernel
+  if (w->step_exec) {
+    cudaGraphExecDestroy(w->step_exec);
+    w->step_exec = nullptr;
+  }
+  w->step_warm = false;
+  if (!rules) {
+    w->rules_on = false;
+    return VELLA_OK;
+  }
+  const vella_whisper_rules& r = *rules;
+  std::vector<float> m(2 * (size_t)V, 0.0f);  // first step, later steps
+  for (int i = 0; i < r.n_suppress; ++i)
+    if (r.suppress[i] >= 0 && r.suppress[i] < V) m[r.suppress[i]] = m[(size_t)V + r.suppress[i]] = -INFINITY;
+  for (int i = 0; i < r.n_begin_suppress; ++i)
+    if (r.begin_suppress[i] >= 0 && r.begin_suppress[i] < V) m[r.begin_suppress[i]] = -INFINITY;
+  if (!w->rule_masks) VELLA_CUDA_TRY(cudaMalloc(&w->rule_masks, m.size() * sizeof(float)));
+  VELLA_CUDA_TRY(cudaMemcpy(w->rule_masks, m.data(), m.size() * sizeof(float), cudaMemcpyHostToDevice));
+  // Swift's Double.rounded(): half away from zero (WhisperModel.swift:321)
+  w->rules = WRules{r.eot, r.no_timestamps, r.timestamp_begin,
+                    r.timestamp_begin + (int)std::floor((double)c.n_audio / 30.0 + 0.5)};
+  w->rules_on = true;
   return VELLA_OK;
 }
 

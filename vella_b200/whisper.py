@@ -27,7 +27,13 @@ class WhisperCfg(ctypes.Structure):
 
 class WhisperStats(ctypes.Structure):
     _fields_ = [("encode_ms", ctypes.c_float), ("prefill_ms", ctypes.c_float), ("decode_ms", ctypes.c_float),
-                ("tokens", ctypes.c_int32)]
+                ("tokens", ctypes.c_int32), ("sum_logprob", ctypes.c_float)]
+
+
+class WhisperRules(ctypes.Structure):
+    _fields_ = [("eot", ctypes.c_int32), ("no_timestamps", ctypes.c_int32), ("timestamp_begin", ctypes.c_int32),
+                ("suppress", ctypes.POINTER(ctypes.c_int32)), ("n_suppress", ctypes.c_int32),
+                ("begin_suppress", ctypes.POINTER(ctypes.c_int32)), ("n_begin_suppress", ctypes.c_int32)]
 
 
 _vp, _i32, _pi32 = ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)
@@ -42,6 +48,7 @@ for _name, _res, _args in [
     ("vella_whisper_decode_batch", ctypes.c_int, [_vp, _pi32, _i32, _i32, _pi32]),
     ("vella_whisper_score", ctypes.c_int, [_vp, _pi32, _i32, _vp, _i32]),
     ("vella_whisper_get_stats", ctypes.c_int, [_vp, ctypes.POINTER(WhisperStats)]),
+    ("vella_whisper_set_rules", ctypes.c_int, [_vp, ctypes.POINTER(WhisperRules)]),
 ]:
     _lib.declare(_name, _res, _args)
 
@@ -133,6 +140,19 @@ class Whisper:
         _lib.check(_lib.lib().vella_whisper_decode_batch(self.h, pr, len(prompt), max_tokens,
                                                          out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))))
         return out[:, :max_tokens]
+
+    def set_rules(self, eot: Optional[int] = None, no_timestamps: int = 0, timestamp_begin: int = 0,
+                  suppress: Sequence[int] = (), begin_suppress: Sequence[int] = ()):
+        """Token rules of the reference's GPU-side greedy for the following decodes (suppress
+        and begin-suppress masks, timestamp rules, summed log-probabilities in the stats);
+        ``eot=None`` returns to plain argmax."""
+        if eot is None:
+            _lib.check(_lib.lib().vella_whisper_set_rules(self.h, None))
+            return
+        sup = (ctypes.c_int32 * max(len(suppress), 1))(*suppress)
+        bsup = (ctypes.c_int32 * max(len(begin_suppress), 1))(*begin_suppress)
+        r = WhisperRules(eot, no_timestamps, timestamp_begin, sup, len(suppress), bsup, len(begin_suppress))
+        _lib.check(_lib.lib().vella_whisper_set_rules(self.h, ctypes.byref(r)))
 
     def score(self, tokens: Sequence[int]) -> np.ndarray:
         """Teacher-forced logits [T, vocab] as storage (float16, or bf16 bits as uint16)."""
