@@ -391,6 +391,14 @@ VELLA_API int vella_whisper_decode_batch(vella_whisper* w, const int32_t* prompt
 /* Token rules for the following decodes (NULL: plain argmax, the default).  The ids must lie
  * in the vocabulary with eot < timestamp_begin; the masks are built on the device here. */
 VELLA_API int vella_whisper_set_rules(vella_whisper* w, const vella_whisper_rules* rules);
+/* Temperature of the following decodes (the reference's fallback attempts, WhisperModel.swift:
+ * 218-292, and its sample() at :447-454): 0 is argmax; at temperature > 0 (token rules
+ * required) each step draws argmax(final / temperature + Gumbel noise), the noise from
+ * Philox-4x32-10 keyed by `seed` on counter (token / 4, step, stream, draw), word token % 4,
+ * u = (2 * (bits >> 9) + 1) / 2^24, noise -log(-log u).  The caller picks `draw` (e.g. the
+ * attempt index) so that attempts draw different noise and a request replays exactly.  The
+ * log-probability sum in the stats stays that of the unscaled final row, as the reference's. */
+VELLA_API int vella_whisper_set_sampling(vella_whisper* w, float temperature, uint64_t seed, uint32_t draw);
 /* Teacher-forced logits [T, vocab] (dtype) of the token sequence (positions 0..T-1); one-
  * stream handles only (as vella_whisper_decode). */
 VELLA_API int vella_whisper_score(vella_whisper* w, const int32_t* tokens, int32_t T, void* logits, int32_t on_host);

@@ -21,7 +21,9 @@ once after its epilogue (bias, GELU, residual); LayerNorm statistics in fp32 wit
 normalised value rounded to the activation dtype before ``w * x + b`` (``WhisperFusedDecode
 .swift:204-251``, the MLX row algorithm, here with one final rounding); GELU is the erf form.
 Greedy argmax, plain or under the token rules of the reference's GPU-side greedy
-(``WhisperModel.swift:311-372``, ``rule_select`` below).
+(``WhisperModel.swift:311-372``, ``rule_select`` below); the temperature fallback's sampled
+attempts, compression ratio and attempt verdict (``WhisperModel.swift:218-292, 434-454``,
+``rule_sample`` / ``attempt_verdict`` below).
 
 Parity: the reference (Swift + MLX) cannot run on this machine; the floating-point
 arithmetic is parity unpinned against MLX.  The sinusoid table rule is pinned by the
@@ -282,3 +284,76 @@ def rule_select(row: np.ndarray, step: int, prev, before_prev, r: TokenRules):
     final = f + mask
     tok = int(np.argmax(final))
     return tok, float(final[tok] - _lse(final)), final
+
+
+# ---------------------------------------------------------------------------------------
+# Temperature fallback (WhisperModel.swift:218-292, sample() :447-454, compressionRatio
+# :434-445): an attempt at temperature T > 0 draws each token from softmax(final / T); the
+# library's draw is Gumbel-max with Philox-4x32-10 noise (MLX's categorical is Gumbel-max
+# as well, on its own generator, so the draws themselves are not comparable with MLX's).
+# ---------------------------------------------------------------------------------------
+
+_PHILOX_M0, _PHILOX_M1 = np.uint64(0xD2511F53), np.uint64(0xCD9E8D57)
+
+
+def philox4x32_10_np(c0, c1, c2, c3, k0: int, k1: int):
+    """Philox-4x32-10 over arrays of counters (uint32 words), the same rounds as
+    ``oracle.decoder.philox4x32_10``; returns four uint32 arrays."""
+    M = np.uint64(0xFFFFFFFF)
+    c0, c1, c2, c3 = (np.asarray(v, np.uint64) & M for v in (c0, c1, c2, c3))
+    c0, c1, c2, c3 = np.broadcast_arrays(c0, c1, c2, c3)
+    k0, k1 = int(k0) & 0xFFFFFFFF, int(k1) & 0xFFFFFFFF
+    for _ in range(10):
+        p0 = _PHILOX_M0 * c0
+        p1 = _PHILOX_M1 * c2
+        hi0, lo0 = p0 >> np.uint64(32), p0 & M
+        hi1, lo1 = p1 >> np.uint64(32), p1 & M
+        c0, c1, c2, c3 = (hi1 ^ c1 ^ np.uint64(k0)) & M, lo1, (hi0 ^ c3 ^ np.uint64(k1)) & M, lo0
+        k0 = (k0 + 0x9E3779B9) & 0xFFFFFFFF
+        k1 = (k1 + 0xBB67AE85) & 0xFFFFFFFF
+    return [x.astype(np.uint32) for x in (c0, c1, c2, c3)]
+
+
+def gumbel_noise(seed: int, draw: int, step: int, stream: int, vocab: int) -> np.ndarray:
+    """Noise of every token at one step: Philox on counter (v // 4, step, stream, draw) keyed
+    by the seed, word v % 4, u = (2 * (bits >> 9) + 1) / 2**24 (exact in fp32), -log(-log u)."""
+    v = np.arange(vocab, dtype=np.uint64)
+    words = philox4x32_10_np(v >> np.uint64(2), step, stream, draw, seed & 0xFFFFFFFF, seed >> 32)
+    bits = np.choose((v & np.uint64(3)).astype(np.int64), words).astype(np.uint64)
+    u = (np.uint64(2) * (bits >> np.uint64(9)) + np.uint64(1)).astype(np.float64) / 16777216.0
+    return -np.log(-np.log(u))
+
+
+def rule_sample(row, step: int, prev, before_prev, r: TokenRules, temperature: float, seed: int, draw: int,
+                stream: int = 0):
+    """One sampled choice under the rules: argmax(final / temperature + noise) and the token's
+    log-probability under the unscaled final row (the reference adds ``filtered[next] -
+    logSumExp(filtered)``, WhisperModel.swift:264-265).  Returns (token, logprob, keys, final)."""
+    _, _, final = rule_select(row, step, prev, before_prev, r)
+    keys = final / temperature + gumbel_noise(seed, draw, step, stream, final.shape[0])
+    tok = int(np.argmax(keys))
+    return tok, float(final[tok] - _lse(final)), keys, final
+
+
+def compression_ratio(text: str) -> float:
+    """UTF-8 bytes over zlib-compressed bytes at the default level; 0 for empty text
+    (WhisperModel.swift:434-445)."""
+    import zlib
+    raw = text.encode("utf-8")
+    return 0.0 if not raw else len(raw) / len(zlib.compress(raw, 6))
+
+
+def attempt_verdict(sum_logprob: float, n_tokens: int, text: str, no_speech_prob: float = 0.0) -> str:
+    """After one attempt (WhisperModel.swift:285-291): the average log-probability counts the
+    end-of-text step (n_tokens + 1); 'empty' when the window is probably silence, 'accept' when
+    the average is >= -1 and the compression ratio <= 2.4, else 'retry' at the next temperature
+    (the last temperature's attempt stands if every one asks for a retry)."""
+    average = sum_logprob / (n_tokens + 1)
+    if no_speech_prob > 0.6 and average < -1:
+        return "empty"
+    if average >= -1 and compression_ratio(text) <= 2.4:
+        return "accept"
+    return "retry"
+
+
+FALLBACK_TEMPERATURES = (0.0, 0.2, 0.4, 0.6, 0.8, 1.0)  # WhisperModel.swift:218-219

@@ -296,3 +296,48 @@ def test_token_rules_follow_the_oracle(tiny):
     assert list(both[0]) == got
     assert abs(mb.stats()["sum_logprob"] - lp_gpu) <= 1e-3 * max(1.0, abs(lp_gpu))
     mb.close()
+
+
+def test_sampled_attempts_follow_the_oracle(tiny):
+    """Temperature 0.7 under the token rules: every token is within the logits tolerance of
+    the oracle's Gumbel-max draw (same Philox noise) on the teacher-forced row, the summed
+    log-probability is the oracle's for those tokens, the same (seed, draw) replays, another
+    draw gives another sequence, and the fallback loop ends on its last temperature when
+    every attempt's average log-probability is below -1."""
+    m, oc, W, mel, enc_ref = tiny
+    prompt = [50258, 50259, 50359, 50363]
+    n, T, seed = 12, 0.7, 0x5EED
+    V = oc.vocab
+    r = Wh.TokenRules(eot=50257, no_timestamps=V - 3, timestamp_begin=V - 2, suppress=[220, 50256],
+                      begin_suppress=[50257, 220])
+    m.set_rules(r.eot, r.no_timestamps, r.timestamp_begin, r.suppress, r.begin_suppress)
+    try:
+        m.set_sampling(T, seed, 3)
+        got = m.decode(prompt, n).tokens
+        lp_gpu = m.stats()["sum_logprob"]
+        assert m.decode(prompt, n).tokens == got
+        m.set_sampling(T, seed, 4)
+        assert m.decode(prompt, n).tokens != got
+        logits = Wh.score(oc, W, enc_ref, prompt + got[:-1])[len(prompt) - 1:]
+        lp_ref = 0.0
+        tol = 2 * LOGIT_TOL / T + 1e-3
+        for j, t in enumerate(got):
+            prev = got[j - 1] if j >= 1 else None
+            bprev = got[j - 2] if j >= 2 else None
+            ok = set()
+            for shift in (0.0, 2 * LOGIT_TOL, -2 * LOGIT_TOL):
+                x = np.asarray(logits[j], np.float64).copy()
+                x[r.timestamp_begin:] += shift
+                tok, _, keys, _ = Wh.rule_sample(x, j, prev, bprev, r, T, seed, 3)
+                ok |= set(np.nonzero(keys >= keys[tok] - tol)[0].tolist())
+            assert t in ok, (j, t)
+            _, _, final = Wh.rule_select(logits[j], j, prev, bprev, r)
+            lp_ref += float(final[t] - Wh._lse(final))
+        assert abs(lp_gpu - lp_ref) <= 2 * LOGIT_TOL * n, (lp_gpu, lp_ref)
+        res = m.decode_with_fallback(prompt, n, eot=-1, seed=seed)
+        assert res.attempts == 6 and res.temperature == 1.0 and res.avg_logprob < -1
+        m.set_sampling(1.0, seed, 5)
+        assert m.decode(prompt, n).tokens == res.tokens
+    finally:
+        m.set_sampling(0.0)
+        m.set_rules(None)

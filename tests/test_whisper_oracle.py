@@ -76,3 +76,95 @@ def test_token_rules_known_answers():
     row5 = row.copy(); row5[40] = 3.0; row5[120] = 2.0
     tok, lp, final = Wh.rule_select(row5, 3, 105, 104, r)
     assert tok == 40 and np.isneginf(final[100:]).all() and np.isfinite(lp)
+
+
+def test_vectorised_philox_matches_the_scalar_rounds():
+    from oracle import decoder as D
+    rng = np.random.default_rng(4)
+    for _ in range(20):
+        c = [int(x) for x in rng.integers(0, 2**32, 4, dtype=np.uint64)]
+        k = [int(x) for x in rng.integers(0, 2**32, 2, dtype=np.uint64)]
+        got = Wh.philox4x32_10_np(*[np.array([x], np.uint64) for x in c], *k)
+        assert tuple(int(g[0]) for g in got) == D.philox4x32_10(c, k)
+
+
+def test_gumbel_noise_word_layout_and_moments():
+    from oracle import decoder as D
+    g = Wh.gumbel_noise(0x5EED, 2, 7, 3, 4099)
+    # token 4098: counter (1024, step 7, stream 3, draw 2), word 2
+    w = D.philox4x32_10((1024, 7, 3, 2), (0x5EED, 0))[2]
+    u = (2 * (w >> 9) + 1) / 2**24
+    assert g[4098] == -math.log(-math.log(u))
+    big = Wh.gumbel_noise(1, 0, 0, 0, 200000)
+    assert abs(big.mean() - np.euler_gamma) < 0.01 and abs(big.std() - math.pi / math.sqrt(6)) < 0.01
+
+
+def test_rule_sample_draws_from_the_tempered_final_row():
+    """Frequencies of Gumbel-max draws over many (step, draw) counters follow
+    softmax(final / T) on a small row; tokens the rules mask are never drawn."""
+    r = Wh.TokenRules(eot=5, no_timestamps=6, timestamp_begin=7, suppress=(1,), max_source_positions=30)
+    row = np.array([0.0, 3.0, 0.5, 1.0, -1.0, 0.2, 4.0, -9.0, -9.0, -9.0])
+    T = 0.7
+    counts = np.zeros(row.size)
+    for d in range(3000):
+        tok, lp, keys, final = Wh.rule_sample(row, 5, 2, 3, r, T, 99, d)
+        counts[tok] += 1
+        assert math.isclose(lp, final[tok] - Wh._lse(final))
+    _, _, final = Wh.rule_select(row, 5, 2, 3, r)
+    p = np.exp(final / T - Wh._lse(final / T))
+    assert counts[1] == counts[6] == 0
+    assert np.abs(counts / counts.sum() - p).max() < 0.03
+
+
+def test_attempt_verdict_and_compression_ratio_match_the_library():
+    import zlib
+
+    from vella_b200 import whisper as VW
+    assert Wh.compression_ratio("") == VW.compression_ratio("") == 0.0
+    text = "the cat sat on the mat " * 12
+    assert Wh.compression_ratio(text) == VW.compression_ratio(text) == len(text) / len(zlib.compress(text.encode()))
+    assert Wh.compression_ratio(text) > 2.4
+    for lp, n, t, ns in [(-3.0, 5, "", 0.0), (-7.0, 5, "", 0.0), (-7.0, 5, "", 0.9), (-3.0, 5, "", 0.9),
+                         (-3.0, 5, text, 0.0), (-6.0, 5, "short text", 0.0)]:
+        assert Wh.attempt_verdict(lp, n, t, ns) == VW.attempt_verdict(lp, n, t, ns)
+    assert Wh.attempt_verdict(-6.0, 5, "", 0.0) == "accept"      # average -1 is kept
+    assert Wh.attempt_verdict(-6.1, 5, "", 0.0) == "retry"
+    assert Wh.attempt_verdict(-6.1, 5, "", 0.61) == "empty"
+    assert Wh.attempt_verdict(-3.0, 5, text, 0.0) == "retry"     # compression ratio above 2.4
+
+
+class _FakeHandle:
+    """The decode / stats / set_sampling surface of a Whisper handle, scripted per temperature."""
+
+    def __init__(self, script):
+        self.script, self.calls, self.temp = script, [], None
+
+    def set_sampling(self, temperature, seed=0x5EED, draw=0):
+        self.calls.append((temperature, seed, draw))
+        self.temp = temperature
+
+    def decode(self, prompt, max_tokens, eot=-1):
+        from vella_b200.whisper import DecodeResult
+        return DecodeResult(list(self.script[self.temp][0]), 0.0, 0.0)
+
+    def stats(self):
+        return {"sum_logprob": self.script[self.temp][1]}
+
+
+def test_fallback_loop_follows_the_reference_order():
+    from vella_b200 import whisper as VW
+    run = VW.Whisper.decode_with_fallback
+    repeat = "la la la la la la la la la la la la la la la la la la"
+    script = {0.0: ([1, 2, 3], -9.0), 0.2: ([4, 4], -1.0), 0.4: ([5], -0.1), 0.6: ([6], -0.1), 0.8: ([7], -0.1),
+              1.0: ([8], -0.1)}
+    h = _FakeHandle(script)
+    res = run(h, [1], 8, 50257, seed=7)
+    assert res.tokens == [4, 4] and res.temperature == 0.2 and res.attempts == 2 and res.verdict == "accept"
+    assert h.calls == [(0.0, 7, 0), (0.2, 7, 1), (0.0, 7, 0)]  # back to argmax afterwards
+    # a repetitive text is rejected by the compression ratio: every attempt retries, the last stands
+    h = _FakeHandle(script)
+    res = run(h, [1], 8, 50257, detokenize=lambda t: repeat, seed=7)
+    assert res.attempts == 6 and res.temperature == 1.0 and res.tokens == [8] and res.verdict == "retry"
+    # probable silence empties the window at the first low-confidence attempt
+    res = run(_FakeHandle(script), [1], 8, 50257, no_speech_prob=0.9)
+    assert res.tokens == [] and res.attempts == 1 and res.verdict == "empty"

@@ -29,6 +29,7 @@
 #include "internal.h"
 #include "layers.cuh"
 #include "model.h"
+#include "philox.h"
 
 namespace vella {
 namespace {
@@ -190,7 +191,25 @@ __global__ void wcommit_kernel(int* L, int* tok, const int* ys, int max_target, 
 struct WRules {
   int eot, no_ts, begin, last_allowed;
 };
+// Per-decode values the captured step reads from device memory.
+struct WDecodeArgs {
+  int nprompt;        // prompt length
+  float temperature;  // 0: argmax; > 0: a draw from softmax(final row / temperature)
+  uint32_t seed_lo, seed_hi;
+  uint32_t draw;      // the caller's draw index (Philox counter word)
+};
 constexpr int kRuleThreads = 512;
+
+// Gumbel noise of token v at a step of stream s: Philox-4x32-10 on counter
+// (v / 4, step, s, draw), word v % 4, u = (2*(bits >> 9) + 1) / 2^24 in (0, 1), -log(-log u).
+__device__ __forceinline__ float rule_gumbel(const WDecodeArgs& a, int step, int s, int v) {
+  const vella::U4 r = vella::philox4x32_10(vella::U4{(uint32_t)v >> 2, (uint32_t)step, (uint32_t)s, a.draw},
+                                           a.seed_lo, a.seed_hi);
+  const int j = v & 3;
+  const uint32_t b = j == 0 ? r.x : j == 1 ? r.y : j == 2 ? r.z : r.w;
+  const float u = (float)(2u * (b >> 9) + 1u) * (1.0f / 16777216.0f);
+  return -logf(-logf(u));
+}
 
 __device__ __forceinline__ float rule_block_max(float v, float* red) {
   v = warp_max(v);
@@ -213,15 +232,16 @@ __device__ __forceinline__ float rule_block_sum(float v, float* red) {
 
 // One choice per stream (block s, logits row s * rs + ro): the suppress mask of the step
 // (begin-suppress as well at step 0), log-probabilities of the filtered row, the timestamp
-// rules, argmax (lowest index among equal maxima) and the chosen token's log-probability
-// under the final row, added to lpsum[s].  The step is the stream's generated-token count
-// L[s] - n_prompt; the rules read the stream's two last generated tokens.
+// rules, then argmax (lowest index among equal maxima) or, at a temperature, the Gumbel-max
+// draw argmax(final / temperature + g); the chosen token's log-probability under the final
+// row is added to lpsum[s].  The step is the stream's generated-token count L[s] - n_prompt;
+// the rules read the stream's two last generated tokens.
 template <typename T>
 __global__ void __launch_bounds__(kRuleThreads) wrules_kernel(const T* __restrict__ logits, int vocab, int rs, int ro,
                                                                int* ys, float* lpsum, int* nonfinite,
                                                                const float* __restrict__ sup_first,
                                                                const float* __restrict__ sup_later, const int* L,
-                                                               const int* tok, const int* nprompt, int max_target,
+                                                               const int* tok, const WDecodeArgs* da, int max_target,
                                                                WRules r) {
   using A = Act<T>;
   __shared__ float red[kRuleThreads / 32];
@@ -230,7 +250,9 @@ __global__ void __launch_bounds__(kRuleThreads) wrules_kernel(const T* __restric
   pdl_launch_next();
   const int s = blockIdx.x, row = s * rs + ro;
   const T* lg = logits + (size_t)row * vocab;
-  const int Ls = L[s], step = Ls - *nprompt;
+  const WDecodeArgs a = *da;
+  const int Ls = L[s], step = Ls - a.nprompt;
+  const bool sampled = a.temperature > 0.0f;
   const float* sup = step == 0 ? sup_first : sup_later;
   // maxima of the filtered row (all tokens, text tokens); finiteness of the raw row
   float mall = -INFINITY, mtext = -INFINITY;
@@ -274,31 +296,36 @@ __global__ void __launch_bounds__(kRuleThreads) wrules_kernel(const T* __restric
                      (first && v > r.last_allowed);
     return off ? -INFINITY : f;
   };
-  float bv = -INFINITY;
+  // choice key: the final logit, or final / temperature + Gumbel noise
+  float bk = -INFINITY, fmx = -INFINITY;
   int bi = INT32_MAX;
   for (int v = threadIdx.x; v < vocab; v += kRuleThreads) {
     const float f = final(v);
-    if (f > bv || (f == bv && v < bi)) { bv = f; bi = v; }
+    fmx = fmaxf(fmx, f);
+    const float k = sampled ? f / a.temperature + rule_gumbel(a, step, s, v) : f;
+    if (k > bk || (k == bk && v < bi)) { bk = k; bi = v; }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    if (ok > bk || (ok == bk && oi < bi)) { bk = ok; bi = oi; }
   }
-  if ((threadIdx.x & 31) == 0) { red[threadIdx.x >> 5] = bv; redi[threadIdx.x >> 5] = bi; }
+  if ((threadIdx.x & 31) == 0) { red[threadIdx.x >> 5] = bk; redi[threadIdx.x >> 5] = bi; }
   __syncthreads();
-  bv = -INFINITY;
+  bk = -INFINITY;
   bi = INT32_MAX;
   for (int i = 0; i < kRuleThreads / 32; ++i)
-    if (red[i] > bv || (red[i] == bv && redi[i] < bi)) { bv = red[i]; bi = redi[i]; }
+    if (red[i] > bk || (red[i] == bk && redi[i] < bi)) { bk = red[i]; bi = redi[i]; }
   __syncthreads();
+  fmx = rule_block_max(fmx, red);
   float z = 0.0f;
-  for (int v = threadIdx.x; v < vocab; v += kRuleThreads) z += expf(final(v) - bv);
+  for (int v = threadIdx.x; v < vocab; v += kRuleThreads) z += expf(final(v) - fmx);
   z = rule_block_sum(z, red);
   if (threadIdx.x == 0) {
-    ys[row] = bi == INT32_MAX ? 0 : bi;
-    lpsum[s] += -logf(z);  // final[token] is the maximum
+    const int t = bi == INT32_MAX ? 0 : bi;
+    ys[row] = t;
+    lpsum[s] += final(t) - fmx - logf(z);
   }
 }
 
@@ -372,7 +399,10 @@ struct vella_whisper {
   vella::WRules rules{};
   float* rule_masks = nullptr;  // [2][vocab]: first step, later steps (0 or -inf)
   float* lpsum = nullptr;       // [S] summed log-probabilities of the current decode
-  int* nprompt = nullptr;       // prompt length of the current decode
+  vella::WDecodeArgs* dargs = nullptr;  // per-decode values read by the selection kernel
+  float temperature = 0.0f;             // following decodes: 0 argmax, > 0 sampled
+  uint64_t seed = 0x5eed;
+  uint32_t draw = 0;                    // Philox counter word of the sampled decodes
   void* gemm_ws = nullptr;
   size_t gemm_ws_bytes = 0;
   cudaStream_t stream = nullptr;
@@ -515,11 +545,11 @@ int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, int 
       if (bf)
         return launch_kernel(wrules_kernel<__nv_bfloat16>, dim3(streams), dim3(kRuleThreads), 0, s,
                              static_cast<const __nv_bfloat16*>(w->logits), c.vocab, rule_rs, rule_ro, w->ys, w->lpsum,
-                             w->nonfinite, sf, sl, (const int*)w->L, (const int*)w->tok, (const int*)w->nprompt,
+                             w->nonfinite, sf, sl, (const int*)w->L, (const int*)w->tok, (const vella::WDecodeArgs*)w->dargs,
                              c.max_target, w->rules);
       return launch_kernel(wrules_kernel<__half>, dim3(streams), dim3(kRuleThreads), 0, s,
                            static_cast<const __half*>(w->logits), c.vocab, rule_rs, rule_ro, w->ys, w->lpsum,
-                           w->nonfinite, sf, sl, (const int*)w->L, (const int*)w->tok, (const int*)w->nprompt,
+                           w->nonfinite, sf, sl, (const int*)w->L, (const int*)w->tok, (const vella::WDecodeArgs*)w->dargs,
                            c.max_target, w->rules);
     }
     if ((rc = launch_argmax(dt, w->logits, logits_rows, c.vocab, (size_t)c.vocab, w->ys, w->argmax_sc, w->nonfinite, s)))
@@ -823,7 +853,7 @@ int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whi
   w->nonfinite = w->err + 1;
   w->argmax_sc = ab + o_amx;
   w->lpsum = reinterpret_cast<float*>(ab + o_rule);
-  w->nprompt = reinterpret_cast<int*>(w->lpsum + S);
+  w->dargs = reinterpret_cast<vella::WDecodeArgs*>(w->lpsum + S);
   w->gemm_ws = ab + o_ws;
   *out = w;
   return VELLA_OK;
@@ -974,6 +1004,16 @@ int vella_whisper_encode(vella_whisper* w, const float* mel, int32_t on_host) {
   return VELLA_OK;
 }
 
+// The selection kernel's per-decode values (prompt length, temperature, seed, draw) and
+// zeroed log-probability sums.
+static int decode_args(vella_whisper* w, int n_prompt, cudaStream_t s, const char* what) {
+  if (w->temperature > 0.0f && !w->rules_on) return fail(VELLA_E_INVALID, "%s: sampling needs token rules", what);
+  const WDecodeArgs a{n_prompt, w->temperature, (uint32_t)w->seed, (uint32_t)(w->seed >> 32), w->draw};
+  VELLA_CUDA_TRY(cudaMemcpyAsync(w->dargs, &a, sizeof(a), cudaMemcpyHostToDevice, s));
+  VELLA_CUDA_TRY(cudaMemsetAsync(w->lpsum, 0, w->S * sizeof(float), s));
+  return VELLA_OK;
+}
+
 int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int32_t n_prompt, int32_t max_tokens, int32_t eot,
                          int32_t* out_tokens, int32_t* n_out) {
   if (!w || !prompt || !n_out || (max_tokens > 0 && !out_tokens))
@@ -993,10 +1033,10 @@ int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int32_t n_prom
   std::copy(prompt, prompt + n_prompt, init.begin());
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->tok, init.data(), n_prompt * sizeof(int), cudaMemcpyHostToDevice, s));
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->L, &n_prompt, sizeof(int), cudaMemcpyHostToDevice, s));
-  VELLA_CUDA_TRY(cudaMemcpyAsync(w->nprompt, &n_prompt, sizeof(int), cudaMemcpyHostToDevice, s));
-  VELLA_CUDA_TRY(cudaMemsetAsync(w->lpsum, 0, sizeof(float), s));
+  int rc = decode_args(w, n_prompt, s, "vella_whisper_decode");
+  if (rc) return rc;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
-  int rc = decoder_forward(w, PosRef{w->dzero, 0}, n_prompt, 1, 1, s, 0, 0);
+  rc = decoder_forward(w, PosRef{w->dzero, 0}, n_prompt, 1, 1, s, 0, 0);
   if (rc) return rc;
   if ((rc = commit(w, 0, 0, s))) return rc;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev1, s));
@@ -1075,13 +1115,13 @@ int vella_whisper_decode_batch(vella_whisper* w, const int32_t* prompt, int32_t 
   for (int st = 0; st < S; ++st) std::copy(prompt, prompt + n_prompt, toks.begin() + (size_t)st * c.max_target);
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->tok, toks.data(), toks.size() * sizeof(int), cudaMemcpyHostToDevice, s));
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->L, lens.data(), S * sizeof(int), cudaMemcpyHostToDevice, s));
-  VELLA_CUDA_TRY(cudaMemcpyAsync(w->nprompt, &n_prompt, sizeof(int), cudaMemcpyHostToDevice, s));
-  VELLA_CUDA_TRY(cudaMemsetAsync(w->lpsum, 0, S * sizeof(float), s));
+  int rc = decode_args(w, n_prompt, s, "vella_whisper_decode_batch");
+  if (rc) return rc;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
   // the prompts of all streams in one forward (stream st: rows st * n_prompt .., positions
   // 0 .. n_prompt - 1), then each stream's first token from its last prompt row
-  int rc = decoder_forward(w, PosRef{w->dzero, 0, n_prompt, 1}, S * n_prompt, S * n_prompt, S, s, n_prompt,
-                           n_prompt - 1);
+  rc = decoder_forward(w, PosRef{w->dzero, 0, n_prompt, 1}, S * n_prompt, S * n_prompt, S, s, n_prompt,
+                       n_prompt - 1);
   if (rc) return rc;
   if ((rc = commit(w, n_prompt, n_prompt - 1, s))) return rc;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev1, s));
@@ -1139,6 +1179,16 @@ int vella_whisper_set_rules(vella_whisper* w, const vella_whisper_rules* rules) 
   w->rules = WRules{r.eot, r.no_timestamps, r.timestamp_begin,
                     r.timestamp_begin + (int)std::floor((double)c.n_audio / 30.0 + 0.5)};
   w->rules_on = true;
+  return VELLA_OK;
+}
+
+int vella_whisper_set_sampling(vella_whisper* w, float temperature, uint64_t seed, uint32_t draw) {
+  if (!w) return fail(VELLA_E_INVALID, "vella_whisper_set_sampling: NULL handle");
+  if (!(temperature >= 0.0f) || !std::isfinite(temperature))
+    return fail(VELLA_E_INVALID, "vella_whisper_set_sampling: temperature %g", (double)temperature);
+  w->temperature = temperature;
+  w->seed = seed;
+  w->draw = draw;
   return VELLA_OK;
 }
 

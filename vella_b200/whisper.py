@@ -9,12 +9,46 @@ the encoder and projects the cross-attention K/V, ``decode`` the greedy loop.
 from __future__ import annotations
 
 import ctypes
+import zlib
 from dataclasses import dataclass
-from typing import Optional, Sequence
+from typing import Callable, List, Optional, Sequence
 
 import numpy as np
 
 from . import _lib
+
+
+FALLBACK_TEMPERATURES = (0.0, 0.2, 0.4, 0.6, 0.8, 1.0)  # WhisperModel.swift:218-219
+
+
+def compression_ratio(text: str) -> float:
+    """UTF-8 bytes over zlib-compressed bytes (default level); 0 for empty text
+    (``compressionRatio``, WhisperModel.swift:434-445)."""
+    raw = text.encode("utf-8")
+    return 0.0 if not raw else len(raw) / len(zlib.compress(raw, 6))
+
+
+def attempt_verdict(sum_logprob: float, n_tokens: int, text: str, no_speech_prob: float = 0.0) -> str:
+    """'empty', 'accept' or 'retry' after one attempt (WhisperModel.swift:285-291): the
+    average log-probability counts the end-of-text step; no-speech above 0.6 with an average
+    below -1 empties the window; an average >= -1 with a compression ratio <= 2.4 accepts."""
+    average = sum_logprob / (n_tokens + 1)
+    if no_speech_prob > 0.6 and average < -1:
+        return "empty"
+    if average >= -1 and compression_ratio(text) <= 2.4:
+        return "accept"
+    return "retry"
+
+
+@dataclass
+class FallbackResult:
+    tokens: List[int]
+    temperature: float
+    sum_logprob: float
+    avg_logprob: float
+    compression_ratio: float
+    attempts: int
+    verdict: str
 
 
 class WhisperCfg(ctypes.Structure):
@@ -49,6 +83,7 @@ for _name, _res, _args in [
     ("vella_whisper_score", ctypes.c_int, [_vp, _pi32, _i32, _vp, _i32]),
     ("vella_whisper_get_stats", ctypes.c_int, [_vp, ctypes.POINTER(WhisperStats)]),
     ("vella_whisper_set_rules", ctypes.c_int, [_vp, ctypes.POINTER(WhisperRules)]),
+    ("vella_whisper_set_sampling", ctypes.c_int, [_vp, ctypes.c_float, ctypes.c_uint64, ctypes.c_uint32]),
 ]:
     _lib.declare(_name, _res, _args)
 
@@ -153,6 +188,42 @@ class Whisper:
         bsup = (ctypes.c_int32 * max(len(begin_suppress), 1))(*begin_suppress)
         r = WhisperRules(eot, no_timestamps, timestamp_begin, sup, len(suppress), bsup, len(begin_suppress))
         _lib.check(_lib.lib().vella_whisper_set_rules(self.h, ctypes.byref(r)))
+
+    def set_sampling(self, temperature: float, seed: int = 0x5EED, draw: int = 0):
+        """Temperature of the following decodes (0: argmax; > 0 draws under the token rules,
+        Philox noise keyed by ``seed`` with counter word ``draw``)."""
+        _lib.check(_lib.lib().vella_whisper_set_sampling(self.h, float(temperature), int(seed) & (2**64 - 1),
+                                                         int(draw) & 0xFFFFFFFF))
+
+    def decode_with_fallback(self, prompt: Sequence[int], max_tokens: int, eot: int,
+                             detokenize: Optional[Callable[[List[int]], str]] = None,
+                             temperatures: Sequence[float] = FALLBACK_TEMPERATURES, seed: int = 0x5EED,
+                             no_speech_prob: float = 0.0) -> FallbackResult:
+        """The reference's temperature fallback for one window (``transcribeChunk``,
+        WhisperModel.swift:218-292): attempts at 0, 0.2, .. 1.0 until the average
+        log-probability (end-of-text step counted) is >= -1 and the compression ratio of
+        ``detokenize(tokens)`` is <= 2.4; an attempt whose average is < -1 while
+        ``no_speech_prob`` > 0.6 gives an empty window; if every attempt asks for a retry the
+        last one stands.  Token rules must be set.  Attempt i draws with counter word i.
+        Without ``detokenize`` the compression test passes (ratio 0, the reference's value for
+        empty text)."""
+        res = None
+        try:
+            for i, temp in enumerate(temperatures):
+                self.set_sampling(temp, seed, i)
+                out = self.decode(prompt, max_tokens, eot)
+                lp = float(self.stats()["sum_logprob"])
+                text = detokenize(out.tokens) if detokenize is not None else ""
+                verdict = attempt_verdict(lp, len(out.tokens), text, no_speech_prob)
+                res = FallbackResult(list(out.tokens), float(temp), lp, lp / (len(out.tokens) + 1),
+                                     compression_ratio(text), i + 1, verdict)
+                if verdict == "empty":
+                    res.tokens = []
+                if verdict != "retry":
+                    break
+        finally:
+            self.set_sampling(0.0, seed, 0)
+        return res
 
     def score(self, tokens: Sequence[int]) -> np.ndarray:
         """Teacher-forced logits [T, vocab] as storage (float16, or bf16 bits as uint16)."""
