@@ -308,8 +308,9 @@ VELLA_API int vella_spec_reset(vella_spec* spec);
  * conv2 -> GELU -> + sinusoid positions -> pre-LN blocks -> LayerNorm), the cross-attention
  * K/V of every decoder layer projected once, then decoder steps (self-attention over the KV
  * cache, cross-attention over the encoder frames, GELU MLP, tied vocabulary projection) with
- * plain greedy argmax on the device, one CUDA graph per step.  The token rules of the
- * reference's greedy (suppression, timestamps) are not applied.
+ * the token choice on the device, one CUDA graph per step: plain argmax, or the reference's
+ * token rules (vella_whisper_set_rules) and sampled fallback attempts
+ * (vella_whisper_set_sampling).
  */
 typedef struct vella_whisper_cfg {
   int32_t n_mels;      /* mel bins (80 | 128)                                           */
@@ -374,6 +375,8 @@ VELLA_API int vella_whisper_init_random(vella_whisper* w, uint64_t seed, float s
  * enc_ln, dec_ln, embed (token embedding = vocabulary projection), dec_pos, and the
  * activations enc_out [n_audio, d_model] (the last encoded window) and xkv (the cross-
  * attention K|V of every stream and decoder layer, [streams][dec_layers][n_audio][2 d_model]). */
+/* The configuration the handle was created with. */
+VELLA_API int vella_whisper_get_cfg(const vella_whisper* w, vella_whisper_cfg* out);
 VELLA_API int vella_whisper_tensor(vella_whisper* w, const char* name, int32_t layer, void** ptr, size_t* bytes);
 /* Encoder over one window per stream: mel fp32 [streams][n_mels][2 * n_audio] (host or
  * device), then the cross-attention K/V of every decoder layer, per stream. */
@@ -415,6 +418,40 @@ VELLA_API int32_t vella_fault_flags(int32_t clear);
 
 /* Library version string, e.g. "vella-b200 0.1 sm_100a". */
 VELLA_API const char* vella_version(void);
+
+/* ---- checkpoints (safetensors) ----------------------------------------------------------
+ *
+ * Replaces MLX.loadArrays over a model directory's *.safetensors shards (merged in the
+ * caller's order, later keys winning: WhisperModel.swift:676-684) and WhisperModel's key
+ * sanitising and derived precision (:483-651, :686-701).  Files are memory-mapped; tensor
+ * data pointers stay valid until vella_st_close.  Host-only: no device work.
+ */
+enum {
+  VELLA_ST_BF16 = 0, VELLA_ST_F16 = 1, VELLA_ST_F32 = 2, VELLA_ST_U32 = 3, VELLA_ST_I32 = 4, VELLA_ST_U8 = 5,
+  VELLA_ST_I8 = 6, VELLA_ST_I64 = 7, VELLA_ST_F64 = 8, VELLA_ST_U16 = 9, VELLA_ST_I16 = 10, VELLA_ST_BOOL = 11,
+  VELLA_ST_U64 = 12, VELLA_ST_F8_E4M3 = 13, VELLA_ST_F8_E5M2 = 14
+};
+typedef struct vella_st vella_st;
+VELLA_API int vella_st_open(const char* const* paths, int32_t n_paths, vella_st** out);
+VELLA_API int vella_st_close(vella_st* st);
+VELLA_API int vella_st_count(const vella_st* st, int32_t* n);
+/* index of `name`, or -1 */
+VELLA_API int vella_st_find(const vella_st* st, const char* name, int32_t* index);
+/* any output may be NULL; shape holds up to 8 dimensions */
+VELLA_API int vella_st_info(const vella_st* st, int32_t index, const char** name, int32_t* dtype, int32_t* ndim,
+                            int64_t* shape, const void** data, size_t* bytes);
+/* Whether a Hugging Face (model.encoder.layers.N...) or OpenAI/mlx-whisper (encoder.blocks.N...)
+ * checkpoint holds every tensor a handle of `cfg` needs, with matching shapes (float, or
+ * MLX-affine group 64 with the handle's bits for the decoder Linears and token embedding;
+ * float Linears of an int4/int8 handle are quantized at load, quantized encoder Linears are
+ * dequantized into the dense encoder).  Host-only; VELLA_E_INVALID names the first problem. */
+VELLA_API int vella_whisper_check_checkpoint(const vella_st* st, const vella_whisper_cfg* cfg);
+/* Fills the handle's weights from the checkpoint (checked first: a failed check leaves the
+ * handle unchanged).  q|k|v rows are concatenated with k's bias zero, cross k|v likewise;
+ * conv weights are read as PyTorch [out, in, 3] (Hugging Face) or [out, 3, in] (mlx-whisper);
+ * the encoder position table is kept (computed) unless the checkpoint supplies one.  The
+ * next decode needs a new vella_whisper_encode. */
+VELLA_API int vella_whisper_load(vella_whisper* w, const vella_st* st);
 
 #ifdef __cplusplus
 }

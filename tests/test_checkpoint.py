@@ -1,0 +1,443 @@
+"""Checkpoints: the safetensors reader, the Whisper key mapping and shape checks, config.json
+and the tokenizer's special ids (CPU), and loading a written checkpoint into a Whisper handle
+(B200: every tensor bit-equal to the handle it was written from, in the Hugging Face and
+mlx-whisper layouts, and the derived int4 precision bit-equal to the oracle's quantizer).
+
+The files are written here by ``write_safetensors`` (8-byte little-endian header length,
+JSON header of dtype / shape / data_offsets per tensor, then the data)."""
+import json
+import struct
+
+import numpy as np
+import pytest
+
+from oracle import affine as A
+
+_ST = {np.dtype(np.float16): "F16", np.dtype(np.float32): "F32", np.dtype(np.uint32): "U32",
+       np.dtype(np.int32): "I32", np.dtype(np.uint8): "U8", np.dtype(np.int64): "I64", np.dtype(np.float64): "F64"}
+
+
+def write_safetensors(path, tensors: dict, metadata=None, dtypes=None):
+    """tensors: name -> numpy array; dtypes: name -> safetensors dtype overriding the array's
+    (e.g. "BF16" for uint16 words)."""
+    header, blobs, off = {}, [], 0
+    if metadata is not None:
+        header["__metadata__"] = metadata
+    for name, a in tensors.items():
+        a = np.asarray(a, order="C")  # keeps 0-d arrays 0-d
+        b = a.tobytes()
+        dt = (dtypes or {}).get(name) or _ST[a.dtype]
+        header[name] = {"dtype": dt, "shape": list(a.shape), "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    h = json.dumps(header).encode()
+    h += b" " * (-len(h) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
+
+
+def _st(paths):
+    from vella_b200 import checkpoint as C
+    return C.SafeTensors([str(p) for p in paths])
+
+
+def test_reader_round_trips_dtypes_shapes_and_metadata(tmp_path):
+    rng = np.random.default_rng(0)
+    t = {"a.f16": rng.standard_normal((3, 5)).astype(np.float16),
+         "b.f32": rng.standard_normal(7).astype(np.float32),
+         "c.u32": rng.integers(0, 2**32, (2, 2, 2), dtype=np.uint64).astype(np.uint32),
+         "d.bf16": rng.integers(0, 2**16, (4,), dtype=np.uint64).astype(np.uint16),
+         "e.scalar": np.array(3.5, np.float32), "f.empty": np.zeros((0, 4), np.float16),
+         "g.unié": np.arange(3, dtype=np.int64)}
+    p = tmp_path / "m.safetensors"
+    write_safetensors(p, t, metadata={"format": "pt"}, dtypes={"d.bf16": "BF16"})
+    with _st([p]) as st:
+        assert sorted(st.keys()) == sorted(t)
+        assert st.info("d.bf16") == ("BF16", (4,))
+        assert st.info("e.scalar") == ("F32", ())
+        for k, a in t.items():
+            got = st.array(k)
+            assert got.shape == a.shape and np.array_equal(got.view(a.dtype), a), k
+        assert st.index("missing") == -1
+        with pytest.raises(KeyError):
+            st.info("missing")
+
+
+def test_later_shards_replace_earlier_keys(tmp_path):
+    a, b = tmp_path / "model-00001.safetensors", tmp_path / "model-00002.safetensors"
+    write_safetensors(a, {"x": np.ones(2, np.float32), "y": np.zeros(3, np.float16)})
+    write_safetensors(b, {"x": np.full(4, 2.0, np.float32)})
+    with _st([a, b]) as st:
+        assert len(st) == 2
+        assert np.array_equal(st.array("x"), np.full(4, 2.0, np.float32))
+        assert st.array("y").shape == (3,)
+
+
+@pytest.mark.parametrize("case", ["truncated", "bad_json", "offsets", "dtype", "short_data", "missing"])
+def test_malformed_files_are_rejected(tmp_path, case):
+    from vella_b200 import _lib
+    p = tmp_path / "bad.safetensors"
+    if case == "missing":
+        p = tmp_path / "absent.safetensors"
+    elif case == "truncated":
+        p.write_bytes(b"\x10\x00\x00")
+    elif case == "bad_json":
+        h = b'{"x": {"dtype": "F32", "shape": [1], "data_offsets": [0, 4]'
+        p.write_bytes(struct.pack("<Q", len(h)) + h + b"\0" * 4)
+    else:
+        shape, offs, dt = [2], [0, 8], "F32"
+        if case == "offsets":
+            offs = [0, 12]
+        if case == "dtype":
+            dt = "Q7"
+        body = 8 if case != "short_data" else 4
+        h = json.dumps({"x": {"dtype": dt, "shape": shape, "data_offsets": offs}}).encode()
+        p.write_bytes(struct.pack("<Q", len(h)) + h + b"\0" * body)
+    with pytest.raises(_lib.VellaError) as e:
+        _st([p])
+    assert e.value.code == _lib.E_INVALID
+
+
+# ---- a small Whisper checkpoint (shapes only; the values are random) -------------------
+
+def small_cfg(bits=4):
+    from vella_b200.whisper import WhisperConfig
+    return WhisperConfig(n_mels=8, d_model=64, heads=1, enc_layers=1, dec_layers=1, ffn=128, vocab=96, n_audio=16,
+                         max_target=8, bits=bits)
+
+
+def hf_tensors(cfg, quant_bits=0, rng=None):
+    """Hugging Face key layout with random float values (fp16); decoder Linears and the token
+    embedding MLX-affine packed when quant_bits is set."""
+    rng = rng or np.random.default_rng(1)
+    d, F, V = cfg.d_model, cfg.ffn, cfg.vocab
+    f = lambda *s: (rng.standard_normal(s) * 0.05).astype(np.float16)  # noqa: E731
+    t = {"model.encoder.conv1.weight": f(d, cfg.n_mels, 3), "model.encoder.conv1.bias": f(d),
+         "model.encoder.conv2.weight": f(d, d, 3), "model.encoder.conv2.bias": f(d),
+         "model.encoder.layer_norm.weight": f(d), "model.encoder.layer_norm.bias": f(d),
+         "model.decoder.layer_norm.weight": f(d), "model.decoder.layer_norm.bias": f(d),
+         "model.decoder.embed_positions.weight": f(cfg.max_target, d),
+         "proj_out.weight": f(V, d)}
+
+    def lin(prefix, n, k, bias=True, quant=False):
+        w = f(n, k)
+        if quant:
+            q, s, b = A.quantize(w.astype(np.float32), quant_bits, "f16")
+            t[prefix + ".weight"], t[prefix + ".scales"], t[prefix + ".biases"] = q, s, b
+        else:
+            t[prefix + ".weight"] = w
+        if bias:
+            t[prefix + ".bias"] = f(n)
+
+    lin("model.decoder.embed_tokens", V, d, bias=False, quant=bool(quant_bits))
+    for l in range(cfg.enc_layers):
+        p = f"model.encoder.layers.{l}."
+        for ln in ("self_attn_layer_norm", "final_layer_norm"):
+            t[p + ln + ".weight"], t[p + ln + ".bias"] = f(d), f(d)
+        for pr in ("q", "k", "v", "out"):
+            lin(p + f"self_attn.{pr}_proj", d, d, bias=pr != "k")
+        lin(p + "fc1", F, d)
+        lin(p + "fc2", d, F)
+    for l in range(cfg.dec_layers):
+        p = f"model.decoder.layers.{l}."
+        for ln in ("self_attn_layer_norm", "encoder_attn_layer_norm", "final_layer_norm"):
+            t[p + ln + ".weight"], t[p + ln + ".bias"] = f(d), f(d)
+        for att in ("self_attn", "encoder_attn"):
+            for pr in ("q", "k", "v", "out"):
+                lin(p + f"{att}.{pr}_proj", d, d, bias=pr != "k", quant=bool(quant_bits))
+        lin(p + "fc1", F, d, quant=bool(quant_bits))
+        lin(p + "fc2", d, F, quant=bool(quant_bits))
+    return t
+
+
+_MLX_ATTN = {"q_proj": "query", "k_proj": "key", "v_proj": "value", "out_proj": "out"}
+_MLX_LN = {"self_attn_layer_norm": "attn_ln", "encoder_attn_layer_norm": "cross_attn_ln", "final_layer_norm": "mlp_ln"}
+
+
+def to_mlx_names(t: dict) -> dict:
+    """The same tensors under OpenAI/mlx-whisper names, conv weights as [out, 3, in]."""
+    out = {}
+    for k, v in t.items():
+        if k == "proj_out.weight":
+            continue
+        if k.endswith("conv1.weight") or k.endswith("conv2.weight"):
+            v = np.ascontiguousarray(v.transpose(0, 2, 1))
+        n = k[len("model."):]
+        n = n.replace("encoder.embed_positions.weight", "encoder.positional_embedding")
+        n = n.replace("decoder.embed_positions.weight", "decoder.positional_embedding")
+        n = n.replace("decoder.embed_tokens.", "decoder.token_embedding.")
+        n = n.replace("encoder.layer_norm.", "encoder.ln_post.").replace("decoder.layer_norm.", "decoder.ln.")
+        if ".layers." in n:
+            stem, rest = n.split(".layers.", 1)
+            idx, suf = rest.split(".", 1)
+            for a, b in _MLX_LN.items():
+                suf = suf.replace(a + ".", b + ".")
+            suf = suf.replace("self_attn.", "attn.").replace("encoder_attn.", "cross_attn.")
+            for a, b in _MLX_ATTN.items():
+                suf = suf.replace(a + ".", b + ".")
+            suf = suf.replace("fc1.", "mlp1.").replace("fc2.", "mlp2.")
+            n = f"{stem}.blocks.{idx}.{suf}"
+        out[n] = v
+    out["alignment_heads"] = np.zeros((2, 2), np.uint8)
+    return out
+
+
+def _check(tmp_path, tensors, cfg, name="model.safetensors"):
+    from vella_b200 import checkpoint as C
+    p = tmp_path / name
+    write_safetensors(p, tensors)
+    with _st([p]) as st:
+        C.check_whisper_checkpoint(st, cfg)
+
+
+@pytest.mark.parametrize("quant", [0, 4])
+def test_whisper_checkpoint_layouts_pass_the_check(tmp_path, quant):
+    cfg = small_cfg(bits=4)
+    t = hf_tensors(cfg, quant_bits=quant)
+    _check(tmp_path, t, cfg, "hf.safetensors")
+    _check(tmp_path, to_mlx_names(t), cfg, "mlx.safetensors")
+    # a re-export without the top-level "model." prefix
+    _check(tmp_path, {k[6:] if k.startswith("model.") else k: v for k, v in t.items()}, cfg, "bare.safetensors")
+
+
+def test_whisper_checkpoint_problems_are_named(tmp_path):
+    from vella_b200 import _lib
+    cfg = small_cfg(bits=4)
+    t = hf_tensors(cfg)
+    gone = dict(t)
+    del gone["model.decoder.layers.0.encoder_attn.v_proj.bias"]
+    with pytest.raises(_lib.VellaError, match="encoder_attn.v_proj.bias"):
+        _check(tmp_path, gone, cfg)
+    bad = dict(t)
+    bad["model.encoder.layers.0.fc1.weight"] = np.zeros((cfg.ffn, cfg.d_model + 64), np.float16)
+    with pytest.raises(_lib.VellaError, match="fc1.weight"):
+        _check(tmp_path, bad, cfg)
+    short = dict(t)
+    short["model.decoder.embed_positions.weight"] = np.zeros((cfg.max_target - 1, cfg.d_model), np.float16)
+    with pytest.raises(_lib.VellaError, match="embed_positions"):
+        _check(tmp_path, short, cfg)
+    q8 = hf_tensors(cfg, quant_bits=8)
+    with pytest.raises(_lib.VellaError) as e:
+        _check(tmp_path, q8, cfg)  # an 8-bit checkpoint for a 4-bit handle
+    assert e.value.code == _lib.E_UNSUPPORTED
+
+
+def test_whisper_config_from_both_key_sets():
+    from vella_b200 import _lib
+    from vella_b200 import checkpoint as C
+    hf = {"num_mel_bins": 128, "d_model": 1280, "encoder_attention_heads": 20, "encoder_layers": 32,
+          "decoder_layers": 4, "encoder_ffn_dim": 5120, "vocab_size": 51866, "max_source_positions": 1500,
+          "max_target_positions": 448}
+    c = C.whisper_config(hf)
+    assert (c.n_mels, c.d_model, c.heads, c.enc_layers, c.dec_layers, c.ffn, c.vocab, c.bits, c.dtype) == \
+        (128, 1280, 20, 32, 4, 5120, 51866, 0, _lib.F16)
+    mlx = {"n_mels": 80, "n_audio_ctx": 1500, "n_audio_state": 384, "n_audio_head": 6, "n_audio_layer": 4,
+           "n_vocab": 51865, "n_text_ctx": 448, "n_text_state": 384, "n_text_head": 6, "n_text_layer": 4,
+           "quantization": {"group_size": 64, "bits": 4}}
+    c = C.whisper_config(mlx)
+    assert (c.n_mels, c.d_model, c.heads, c.ffn, c.vocab, c.bits) == (80, 384, 6, 1536, 51865, 4)
+    assert C.whisper_config(hf, bits=8).bits == 8  # derived precision
+    with pytest.raises(ValueError):
+        C.whisper_config(mlx, bits=8)
+    with pytest.raises(ValueError):
+        C.whisper_config({**mlx, "quantization": {"group_size": 32, "bits": 4}})
+
+
+def test_whisper_token_ids_and_suppress_lists(tmp_path):
+    from vella_b200 import checkpoint as C
+    (tmp_path / "config.json").write_text(json.dumps({"vocab_size": 51866, "decoder_start_token_id": 50258}))
+    (tmp_path / "generation_config.json").write_text(json.dumps({
+        "eos_token_id": 50257, "no_timestamps_token_id": 50364, "suppress_tokens": [1, 2, 7],
+        "begin_suppress_tokens": [220, 50257], "lang_to_id": {"<|en|>": 50259, "<|de|>": 50261},
+        "task_to_id": {"transcribe": 50360, "translate": 50359}, "is_multilingual": True}))
+    (tmp_path / "tokenizer_config.json").write_text(json.dumps({"added_tokens_decoder": {
+        "50258": {"content": "<|startoftranscript|>"}, "50361": {"content": "<|startoflm|>"},
+        "50362": {"content": "<|startofprev|>"}, "50363": {"content": "<|nospeech|>"},
+        "50260": {"content": "<|zh|>"}}}))
+    t = C.whisper_tokens(tmp_path)
+    assert (t.sot, t.eot, t.no_timestamps, t.timestamp_begin) == (50258, 50257, 50364, 50365)
+    assert t.suppress == [1, 2, 7, 50258, 50359, 50360, 50361, 50362, 50363]
+    assert t.begin_suppress == [220, 50257]
+    assert t.prompt("en") == [50258, 50259, 50360]
+    assert t.prompt("<|zh|>", task="translate") == [50258, 50260, 50359]
+    assert t.prompt(None, without_timestamps=True) == [50258, 50360, 50364]
+    assert t.rules()["timestamp_begin"] == 50365
+    # without generation or tokenizer files: the config's ids (WhisperTokenizer.swift:53)
+    bare = tmp_path / "bare"
+    bare.mkdir()
+    (bare / "config.json").write_text(json.dumps({"vocab_size": 51865}))
+    t = C.whisper_tokens(bare)
+    assert (t.sot, t.eot, t.no_timestamps, t.multilingual) == (50258, 50257, 50363, False)
+    assert t.begin_suppress == [220, 50257] and t.suppress == [50258]
+    (bare / "config.json").write_text(json.dumps({"vocab_size": 51864, "decoder_start_token_id": 50257}))
+    assert C.whisper_tokens(bare).no_timestamps == 50361  # English-only vocabulary: start + 104
+
+
+# ---- B200: loading into a handle ------------------------------------------------------
+
+def _download(model, name, layer=-1):
+    import torch
+
+    class _Dev:
+        def __init__(self, ptr, nbytes):
+            self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                             "version": 3}
+    ptr, nbytes = model.tensor(name, layer)
+    return torch.as_tensor(_Dev(ptr, nbytes), device="cuda").cpu().numpy()
+
+
+def _handle_tensors(cfg):
+    out = [("conv1.w", -1), ("conv1.bias", -1), ("conv2.w", -1), ("conv2.bias", -1), ("enc_pos", -1),
+           ("dec_pos", -1), ("enc_ln.weight", -1), ("enc_ln.bias", -1), ("dec_ln.weight", -1), ("dec_ln.bias", -1),
+           ("embed.w", -1)]
+    if cfg.bits:
+        out += [("embed.s", -1), ("embed.b", -1)]
+    for l in range(cfg.enc_layers):
+        for n in ("ln1", "ln2"):
+            out += [(f"enc.{n}.weight", l), (f"enc.{n}.bias", l)]
+        for n in ("qkv", "o", "fc1", "fc2"):
+            out += [(f"enc.{n}.w", l), (f"enc.{n}.bias", l)]
+    for l in range(cfg.dec_layers):
+        for n in ("ln1", "ln2", "ln3"):
+            out += [(f"dec.{n}.weight", l), (f"dec.{n}.bias", l)]
+        for n in ("qkv", "o", "cq", "ckv", "co", "fc1", "fc2"):
+            out += [(f"dec.{n}.w", l), (f"dec.{n}.bias", l)]
+            if cfg.bits:
+                out += [(f"dec.{n}.s", l), (f"dec.{n}.b", l)]
+    return out
+
+
+def export_hf(model, cfg):
+    """The handle's tensors as a Hugging Face checkpoint (decoder MLX-affine when bits)."""
+    d, F, V, C = cfg.d_model, cfg.ffn, cfg.vocab, cfg.n_mels
+    f16 = lambda name, layer=-1: _download(model, name, layer).view(np.float16)  # noqa: E731
+    u32 = lambda name, layer=-1: _download(model, name, layer).view(np.uint32)  # noqa: E731
+    kp1 = (3 * C + 63) // 64 * 64
+    t = {"model.encoder.conv1.weight": f16("conv1.w").reshape(d, kp1)[:, :3 * C].reshape(d, 3, C).transpose(0, 2, 1),
+         "model.encoder.conv1.bias": f16("conv1.bias"),
+         "model.encoder.conv2.weight": f16("conv2.w").reshape(d, 3, d).transpose(0, 2, 1),
+         "model.encoder.conv2.bias": f16("conv2.bias"),
+         "model.encoder.embed_positions.weight": f16("enc_pos").reshape(cfg.n_audio, d),
+         "model.decoder.embed_positions.weight": f16("dec_pos").reshape(cfg.max_target, d),
+         "model.encoder.layer_norm.weight": f16("enc_ln.weight"), "model.encoder.layer_norm.bias": f16("enc_ln.bias"),
+         "model.decoder.layer_norm.weight": f16("dec_ln.weight"), "model.decoder.layer_norm.bias": f16("dec_ln.bias")}
+
+    def lin(dst, rows, name, layer, k, bits, bias=True):
+        """Split the handle's Linear `name` by rows into the checkpoint Linears `dst`."""
+        if bits:
+            w = u32(f"{name}.w", layer).reshape(-1, k * bits // 32)
+            s = f16(f"{name}.s", layer).reshape(-1, k // 64)
+            b = f16(f"{name}.b", layer).reshape(-1, k // 64)
+        else:
+            w = f16(f"{name}.w", layer).reshape(-1, k)
+        bb = f16(f"{name}.bias", layer) if bias else None
+        r0 = 0
+        for prefix, n in zip(dst, rows):
+            t[prefix + ".weight"] = w[r0:r0 + n]
+            if bits:
+                t[prefix + ".scales"], t[prefix + ".biases"] = s[r0:r0 + n], b[r0:r0 + n]
+            if bb is not None and not prefix.endswith("k_proj"):
+                t[prefix + ".bias"] = bb[r0:r0 + n]
+            r0 += n
+
+    lin(["model.decoder.embed_tokens"], [V], "embed", -1, d, cfg.bits, bias=False)
+    for l in range(cfg.enc_layers):
+        p = f"model.encoder.layers.{l}."
+        for n, hf in (("ln1", "self_attn_layer_norm"), ("ln2", "final_layer_norm")):
+            t[p + hf + ".weight"], t[p + hf + ".bias"] = f16(f"enc.{n}.weight", l), f16(f"enc.{n}.bias", l)
+        lin([p + "self_attn.q_proj", p + "self_attn.k_proj", p + "self_attn.v_proj"], [d] * 3, "enc.qkv", l, d, 0)
+        lin([p + "self_attn.out_proj"], [d], "enc.o", l, d, 0)
+        lin([p + "fc1"], [F], "enc.fc1", l, d, 0)
+        lin([p + "fc2"], [d], "enc.fc2", l, F, 0)
+    b = cfg.bits
+    for l in range(cfg.dec_layers):
+        p = f"model.decoder.layers.{l}."
+        for n, hf in (("ln1", "self_attn_layer_norm"), ("ln2", "encoder_attn_layer_norm"), ("ln3", "final_layer_norm")):
+            t[p + hf + ".weight"], t[p + hf + ".bias"] = f16(f"dec.{n}.weight", l), f16(f"dec.{n}.bias", l)
+        lin([p + "self_attn.q_proj", p + "self_attn.k_proj", p + "self_attn.v_proj"], [d] * 3, "dec.qkv", l, d, b)
+        lin([p + "self_attn.out_proj"], [d], "dec.o", l, d, b)
+        lin([p + "encoder_attn.q_proj"], [d], "dec.cq", l, d, b)
+        lin([p + "encoder_attn.k_proj", p + "encoder_attn.v_proj"], [d, d], "dec.ckv", l, d, b)
+        lin([p + "encoder_attn.out_proj"], [d], "dec.co", l, d, b)
+        lin([p + "fc1"], [F], "dec.fc1", l, d, b)
+        lin([p + "fc2"], [d], "dec.fc2", l, F, b)
+    return {k: np.ascontiguousarray(v) for k, v in t.items()}
+
+
+def _write_dir(path, tensors, cfg_json, shards=1):
+    path.mkdir()
+    (path / "config.json").write_text(json.dumps(cfg_json))
+    keys = sorted(tensors)
+    for i in range(shards):
+        write_safetensors(path / f"model-{i + 1:05d}-of-{shards:05d}.safetensors",
+                          {k: tensors[k] for k in keys[i::shards]})
+
+
+def _hf_config(cfg, quant=None):
+    j = {"num_mel_bins": cfg.n_mels, "d_model": cfg.d_model, "encoder_attention_heads": cfg.heads,
+         "encoder_layers": cfg.enc_layers, "decoder_layers": cfg.dec_layers, "encoder_ffn_dim": cfg.ffn,
+         "vocab_size": cfg.vocab, "max_source_positions": cfg.n_audio, "max_target_positions": cfg.max_target}
+    if quant:
+        j["quantization"] = {"group_size": 64, "bits": quant}
+    return j
+
+
+@pytest.mark.gpu
+def test_loaded_handles_equal_their_source(tmp_path):
+    """Hugging Face (two shards) and mlx-whisper layouts of an int4 Whisper-tiny handle load into
+    handles whose every tensor is bit-equal to the source's, and which decode the same tokens."""
+    from vella_b200 import checkpoint as C
+    from vella_b200 import whisper as VW
+    cfg = VW.TINY
+    src = VW.Whisper(cfg)
+    src.init_random(11, 0.05)
+    t = export_hf(src, cfg)
+    mel = np.random.default_rng(3).standard_normal((cfg.n_mels, 2 * cfg.n_audio)).astype(np.float32)
+    src.encode(mel)
+    prompt = [50258, 50259, 50359, 50363]
+    want = src.decode(prompt, 12).tokens
+    names = _handle_tensors(cfg)
+    ref = {n: _download(src, *n) for n in names}
+    for tag, tensors, shards in (("hf", t, 2), ("mlx", to_mlx_names(t), 1)):
+        d = tmp_path / tag
+        _write_dir(d, tensors, _hf_config(cfg, quant=cfg.bits), shards)
+        m = C.load_whisper(d)
+        for n in names:
+            assert np.array_equal(_download(m, *n), ref[n]), (tag, n)
+        m.encode(mel)
+        assert m.decode(prompt, 12).tokens == want, tag
+        m.close()
+    src.close()
+
+
+@pytest.mark.gpu
+def test_derived_int4_matches_the_oracle_quantizer(tmp_path):
+    """A float (fp16) checkpoint loaded into an int4 handle: every decoder Linear and the token
+    embedding are the oracle's MLX-affine quantization of the float rows, bit for bit; the
+    dense encoder is the float values themselves."""
+    from vella_b200 import checkpoint as C
+    from vella_b200 import whisper as VW
+    from dataclasses import replace
+    cfg = replace(VW.TINY, bits=0)
+    src = VW.Whisper(cfg)
+    src.init_random(12, 0.05)
+    t = export_hf(src, cfg)
+    d = tmp_path / "float"
+    _write_dir(d, t, _hf_config(cfg))
+    m = C.load_whisper(d, bits=4)
+    D = cfg.d_model
+    for name, layer, parts, k in (("embed", -1, ["model.decoder.embed_tokens"], D),
+                                  ("dec.qkv", 0, [f"model.decoder.layers.0.self_attn.{p}_proj" for p in "qkv"], D),
+                                  ("dec.ckv", 1, [f"model.decoder.layers.1.encoder_attn.{p}_proj" for p in "kv"], D),
+                                  ("dec.fc2", 3, ["model.decoder.layers.3.fc2"], cfg.ffn)):
+        w = np.concatenate([t[p + ".weight"] for p in parts]).astype(np.float32)
+        q, s, b = A.quantize(w, 4, "f16")
+        assert np.array_equal(_download(m, f"{name}.w", layer).view(np.uint32).reshape(q.shape), q), name
+        assert np.array_equal(_download(m, f"{name}.s", layer).view(np.float16).reshape(s.shape), s), name
+        assert np.array_equal(_download(m, f"{name}.b", layer).view(np.float16).reshape(b.shape), b), name
+    assert np.array_equal(_download(m, "enc.fc1.w", 2), _download(src, "enc.fc1.w", 2))
+    m.close()
+    src.close()

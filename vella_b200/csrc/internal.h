@@ -127,4 +127,8 @@ int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& plan, const void* x
 int make_tensor_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz);
 
+// After a checkpoint load: the encoder output and cross-attention K/V are stale until the
+// next vella_whisper_encode (whisper.cu).
+int whisper_weights_loaded(vella_whisper* w);
+
 }  // namespace vella

@@ -722,6 +722,11 @@ int write_sinusoids(vella_whisper* w, cudaStream_t s) {
 
 using namespace vella;
 
+int vella::whisper_weights_loaded(vella_whisper* w) {
+  w->encoded = false;
+  return VELLA_OK;
+}
+
 extern "C" {
 
 int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whisper** out) {
@@ -919,6 +924,12 @@ int vella_whisper_init_random(vella_whisper* w, uint64_t seed, float std) {
   if ((rc = dense(w->dec_pos, (size_t)c.max_target * d, 0.0f, std))) return rc;
   if ((rc = dt == VELLA_BF16 ? write_sinusoids<__nv_bfloat16>(w, s) : write_sinusoids<__half>(w, s))) return rc;
   VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+  return VELLA_OK;
+}
+
+int vella_whisper_get_cfg(const vella_whisper* w, vella_whisper_cfg* out) {
+  if (!w || !out) return fail(VELLA_E_INVALID, "vella_whisper_get_cfg: NULL argument");
+  *out = w->cfg;
   return VELLA_OK;
 }
 
