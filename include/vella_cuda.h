@@ -180,6 +180,8 @@ VELLA_API int vella_model_init_random(vella_model* model, uint64_t seed, float s
  * "attn_norm", "mlp_norm", "q_norm", "k_norm", "qkv.w|s|b" (rows q, then k, then v),
  * "o.w|s|b", "gate.w|s|b", "up.w|s|b", "down.w|s|b". */
 VELLA_API int vella_model_tensor(vella_model* model, const char* name, int32_t layer, void** ptr, size_t* bytes);
+/* The configuration the model was created with. */
+VELLA_API int vella_model_get_cfg(const vella_model* model, vella_model_cfg* out);
 VELLA_API size_t vella_model_weight_bytes(const vella_model* model);
 /*
  * Teacher-forced scoring (the backbone over a whole prompt, as llm.backbone(...) +
@@ -452,6 +454,15 @@ VELLA_API int vella_whisper_check_checkpoint(const vella_st* st, const vella_whi
  * the encoder position table is kept (computed) unless the checkpoint supplies one.  The
  * next decode needs a new vella_whisper_encode. */
 VELLA_API int vella_whisper_load(vella_whisper* w, const vella_st* st);
+/* The same for a Qwen3-style decoder model (Qwen3ASRTextDecoder.swift:17-214, keys as
+ * Qwen3ASRModel.sanitize leaves them, :682-708, a "thinker." prefix stripped):
+ * model.embed_tokens (dense in the handle: an MLX-affine embedding is dequantized),
+ * model.norm, lm_head (the embedding when the checkpoint has none: tied), and per layer
+ * input_layernorm, post_attention_layernorm, self_attn.{q,k,v,o}_proj (q|k|v rows
+ * concatenated), self_attn.{q,k}_norm when cfg.qk_norm, mlp.{gate,up,down}_proj; float
+ * Linears of an int4/int8 model are quantized at load. */
+VELLA_API int vella_model_check_checkpoint(const vella_st* st, const vella_model_cfg* cfg);
+VELLA_API int vella_model_load(vella_model* model, const vella_st* st);
 
 #ifdef __cplusplus
 }

@@ -441,3 +441,188 @@ def test_derived_int4_matches_the_oracle_quantizer(tmp_path):
     assert np.array_equal(_download(m, "enc.fc1.w", 2), _download(src, "enc.fc1.w", 2))
     m.close()
     src.close()
+
+
+# ---- Qwen3-style decoder models ---------------------------------------------------------
+
+def small_model_cfg(bits=4, qk_norm=True):
+    from vella_b200.decode import ModelConfig
+    return ModelConfig(2, 256, 4, 2, 64, 512, 1000, bits=bits, qk_norm=qk_norm, max_seq=128, max_prefix=64)
+
+
+def qwen3_tensors(cfg, quant_bits=0, tied=False, prefix="", rng=None):
+    rng = rng or np.random.default_rng(2)
+    d, F, V, H, KV, hd = cfg.d_model, cfg.ffn, cfg.vocab, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    f = lambda *s: (rng.standard_normal(s) * 0.05).astype(np.float16)  # noqa: E731
+    t = {}
+
+    def lin(name, n, k, quant=bool(quant_bits)):
+        w = f(n, k)
+        if quant:
+            q, s, b = A.quantize(w.astype(np.float32), quant_bits, "f16")
+            t[name + ".weight"], t[name + ".scales"], t[name + ".biases"] = q, s, b
+        else:
+            t[name + ".weight"] = w
+
+    lin("model.embed_tokens", V, d)
+    t["model.norm.weight"] = f(d)
+    if not tied:
+        lin("lm_head", V, d)
+    for l in range(cfg.n_layers):
+        p = f"model.layers.{l}."
+        t[p + "input_layernorm.weight"], t[p + "post_attention_layernorm.weight"] = f(d), f(d)
+        if cfg.qk_norm:
+            t[p + "self_attn.q_norm.weight"], t[p + "self_attn.k_norm.weight"] = f(hd), f(hd)
+        lin(p + "self_attn.q_proj", H * hd, d)
+        lin(p + "self_attn.k_proj", KV * hd, d)
+        lin(p + "self_attn.v_proj", KV * hd, d)
+        lin(p + "self_attn.o_proj", d, H * hd)
+        lin(p + "mlp.gate_proj", F, d)
+        lin(p + "mlp.up_proj", F, d)
+        lin(p + "mlp.down_proj", d, F)
+    return {prefix + k: v for k, v in t.items()}
+
+
+def _check_model(tmp_path, tensors, cfg, name="model.safetensors"):
+    from vella_b200 import checkpoint as C
+    p = tmp_path / name
+    write_safetensors(p, tensors)
+    with _st([p]) as st:
+        C.check_model_checkpoint(st, cfg)
+
+
+@pytest.mark.parametrize("quant,tied,prefix", [(0, False, ""), (4, False, ""), (4, True, "thinker."), (0, True, "")])
+def test_qwen3_checkpoints_pass_the_check(tmp_path, quant, tied, prefix):
+    cfg = small_model_cfg(bits=4)
+    _check_model(tmp_path, qwen3_tensors(cfg, quant, tied, prefix), cfg)
+
+
+def test_qwen3_checkpoint_problems_are_named(tmp_path):
+    from vella_b200 import _lib
+    cfg = small_model_cfg(bits=4)
+    t = qwen3_tensors(cfg)
+    del t["model.layers.1.self_attn.k_norm.weight"]
+    with pytest.raises(_lib.VellaError, match="k_norm"):
+        _check_model(tmp_path, t, cfg)
+    _check_model(tmp_path, t, small_model_cfg(bits=4, qk_norm=False), "noqk.safetensors")  # not needed then
+    t = qwen3_tensors(cfg)
+    t["model.layers.0.self_attn.o_proj.weight"] = t["model.layers.0.self_attn.o_proj.weight"][:, :128].copy()
+    with pytest.raises(_lib.VellaError, match="o_proj"):
+        _check_model(tmp_path, t, cfg, "bad.safetensors")
+
+
+def test_qwen3_config():
+    from vella_b200 import _lib
+    from vella_b200 import checkpoint as C
+    j = {"num_hidden_layers": 28, "hidden_size": 2048, "num_attention_heads": 16, "num_key_value_heads": 8,
+         "head_dim": 128, "intermediate_size": 6144, "vocab_size": 151936, "rms_norm_eps": 1e-6,
+         "rope_theta": 1000000, "torch_dtype": "bfloat16"}
+    c = C.model_config(j, max_seq=1280)
+    assert (c.n_layers, c.d_model, c.n_heads, c.n_kv_heads, c.head_dim, c.ffn, c.vocab, c.bits, c.dtype,
+            c.max_seq) == (28, 2048, 16, 8, 128, 6144, 151936, 0, _lib.BF16, 1280)
+    asr = {"thinker_config": {"text_config": {**j, "torch_dtype": "float16"}},
+           "quantization": {"group_size": 64, "bits": 4}}
+    c = C.model_config(asr)
+    assert (c.bits, c.dtype, c.vocab) == (4, _lib.F16, 151936)
+
+
+def export_qwen3(model, cfg):
+    """The model handle's tensors as a Qwen3 checkpoint (MLX-affine when bits)."""
+    d, F, V, H, KV, hd = cfg.d_model, cfg.ffn, cfg.vocab, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    raw = lambda n, l=-1: _download(model, n, l)  # noqa: E731
+    t = {"model.embed_tokens.weight": raw("embed").view(np.float16).reshape(V, d),
+         "model.norm.weight": raw("final_norm").view(np.float16)}
+    b = cfg.bits
+
+    def lin(dst, rows, name, layer, k):
+        if b:
+            w = raw(f"{name}.w", layer).view(np.uint32).reshape(-1, k * b // 32)
+            s = raw(f"{name}.s", layer).view(np.float16).reshape(-1, k // 64)
+            bb = raw(f"{name}.b", layer).view(np.float16).reshape(-1, k // 64)
+        else:
+            w = raw(f"{name}.w", layer).view(np.float16).reshape(-1, k)
+        r0 = 0
+        for prefix, n in zip(dst, rows):
+            t[prefix + ".weight"] = w[r0:r0 + n]
+            if b:
+                t[prefix + ".scales"], t[prefix + ".biases"] = s[r0:r0 + n], bb[r0:r0 + n]
+            r0 += n
+
+    lin(["lm_head"], [V], "lm_head", -1, d)
+    for l in range(cfg.n_layers):
+        p = f"model.layers.{l}."
+        t[p + "input_layernorm.weight"] = raw("attn_norm", l).view(np.float16)
+        t[p + "post_attention_layernorm.weight"] = raw("mlp_norm", l).view(np.float16)
+        if cfg.qk_norm:
+            t[p + "self_attn.q_norm.weight"] = raw("q_norm", l).view(np.float16)
+            t[p + "self_attn.k_norm.weight"] = raw("k_norm", l).view(np.float16)
+        lin([p + "self_attn.q_proj", p + "self_attn.k_proj", p + "self_attn.v_proj"], [H * hd, KV * hd, KV * hd],
+            "qkv", l, d)
+        lin([p + "self_attn.o_proj"], [d], "o", l, H * hd)
+        lin([p + "mlp.gate_proj"], [F], "gate", l, d)
+        lin([p + "mlp.up_proj"], [F], "up", l, d)
+        lin([p + "mlp.down_proj"], [d], "down", l, F)
+    return {k: np.ascontiguousarray(v) for k, v in t.items()}
+
+
+def _model_tensors(cfg):
+    out = [("embed", -1), ("final_norm", -1), ("lm_head.w", -1)] + ([("lm_head.s", -1), ("lm_head.b", -1)] if cfg.bits else [])
+    for l in range(cfg.n_layers):
+        out += [("attn_norm", l), ("mlp_norm", l)] + ([("q_norm", l), ("k_norm", l)] if cfg.qk_norm else [])
+        for n in ("qkv", "o", "gate", "up", "down"):
+            out += [(f"{n}.w", l)] + ([(f"{n}.s", l), (f"{n}.b", l)] if cfg.bits else [])
+    return out
+
+
+def _qwen3_json(cfg, quant=None):
+    j = {"num_hidden_layers": cfg.n_layers, "hidden_size": cfg.d_model, "num_attention_heads": cfg.n_heads,
+         "num_key_value_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim, "intermediate_size": cfg.ffn,
+         "vocab_size": cfg.vocab, "rms_norm_eps": cfg.rms_eps, "rope_theta": cfg.rope_theta, "torch_dtype": "float16"}
+    if quant:
+        j["quantization"] = {"group_size": 64, "bits": quant}
+    return j
+
+
+@pytest.mark.gpu
+def test_loaded_models_equal_their_source_and_derive_int4(tmp_path):
+    """An int4 Qwen3-style model written as an MLX-quantized checkpoint (two shards, "thinker."
+    prefix) loads bit-equal, tensor by tensor; a float checkpoint with a tied
+    embedding loads into an int4 model whose lm_head and Linears are the oracle quantizer's
+    codes of the float rows."""
+    from dataclasses import replace
+
+    from vella_b200 import _lib
+    from vella_b200 import checkpoint as C
+    from vella_b200 import decode as VD
+    cfg = replace(small_model_cfg(bits=4), dtype=_lib.F16)
+    src = VD.Model(cfg)
+    src.init_random(21, 0.05)
+    t = export_qwen3(src, cfg)
+    d = tmp_path / "q4"
+    _write_dir(d, {"thinker." + k: v for k, v in t.items()}, _qwen3_json(cfg, quant=4), shards=2)
+    m = C.load_model(d, max_seq=cfg.max_seq, max_prefix=cfg.max_prefix)
+    assert m.cfg.bits == 4 and m.cfg.qk_norm and m.cfg.dtype == _lib.F16
+    for n in _model_tensors(cfg):
+        assert np.array_equal(_download(m, *n), _download(src, *n)), n
+    m.close()
+    # float source, tied embedding, derived int4
+    fcfg = replace(cfg, bits=0)
+    fsrc = VD.Model(fcfg)
+    fsrc.init_random(22, 0.05)
+    ft = export_qwen3(fsrc, fcfg)
+    del ft["lm_head.weight"]
+    d = tmp_path / "tied"
+    _write_dir(d, ft, _qwen3_json(fcfg))
+    m = C.load_model(d, bits=4, max_seq=cfg.max_seq, max_prefix=cfg.max_prefix)
+    emb = ft["model.embed_tokens.weight"]
+    assert np.array_equal(_download(m, "embed").view(np.float16).reshape(emb.shape), emb)
+    for name, layer, w in (("lm_head", -1, emb),
+                           ("qkv", 1, np.concatenate([ft[f"model.layers.1.self_attn.{p}_proj.weight"] for p in "qkv"])),
+                           ("down", 0, ft["model.layers.0.mlp.down_proj.weight"])):
+        q, s, b = A.quantize(w.astype(np.float32), 4, "f16")
+        assert np.array_equal(_download(m, f"{name}.w", layer).view(np.uint32).reshape(q.shape), q), name
+        assert np.array_equal(_download(m, f"{name}.s", layer).view(np.float16).reshape(s.shape), s), name
+        assert np.array_equal(_download(m, f"{name}.b", layer).view(np.float16).reshape(b.shape), b), name
+    m.close()
+    fsrc.close()
+    src.close()

@@ -1,4 +1,5 @@
-"""Model directories: safetensors shards, config.json and the Whisper token ids.
+"""Model directories: safetensors shards, config.json, the Whisper token ids, and the
+Qwen3-style decoder models of the draft-and-verify path.
 
 Mirrors the reference's ``WhisperModel.fromDirectory`` (``Worker/Sources/MLXAudioSTT/Whisper/
 WhisperModel.swift:653-723``): ``config.json`` (Hugging Face or OpenAI/mlx-whisper keys,
@@ -31,6 +32,8 @@ for _name, _res, _args in [
                                      ctypes.POINTER(ctypes.c_size_t)]),
     ("vella_whisper_check_checkpoint", ctypes.c_int, [_vp, _vp]),
     ("vella_whisper_load", ctypes.c_int, [_vp, _vp]),
+    ("vella_model_check_checkpoint", ctypes.c_int, [_vp, _vp]),
+    ("vella_model_load", ctypes.c_int, [_vp, _vp]),
 ]:
     _lib.declare(_name, _res, _args)
 
@@ -262,3 +265,56 @@ def whisper_tokens(model_dir) -> WhisperTokens:
     sup += [x for x in (t.transcribe, t.translate, t.prev_sot, t.sot_lm, t.no_speech, t.sot) if x is not None]
     t.suppress = sorted(set(sup))
     return t
+
+
+# ---------------------------------------------------------------------------------------
+# Qwen3-style decoder (the draft-and-verify target and draft)
+# ---------------------------------------------------------------------------------------
+
+def model_config(cfg: dict, bits: Optional[int] = None, dtype: Optional[int] = None, qk_norm: bool = True,
+                 **kw):
+    """A ``decode.ModelConfig`` from a Qwen3 config.json (or a Qwen3-ASR one, whose text model
+    sits under ``thinker_config.text_config``); ``bits`` as in ``whisper_config``; the dtype
+    from ``torch_dtype`` (bf16 unless it says float16); ``kw`` sets the handle's capacities
+    (max_seq, max_prefix, streams, rows_per_stream)."""
+    from .decode import ModelConfig
+    c = (cfg.get("thinker_config") or {}).get("text_config") or cfg.get("text_config") or cfg
+    q = cfg.get("quantization") or cfg.get("quantization_config") or c.get("quantization")
+    if q:
+        if int(q.get("group_size", 64)) != 64:
+            raise ValueError(f"quantized checkpoint with group size {q.get('group_size')} (the kernels use 64)")
+        if bits is not None and bits != int(q["bits"]):
+            raise ValueError("the checkpoint is already quantized")
+        bits = int(q["bits"])
+    if dtype is None:
+        dtype = _lib.F16 if str(c.get("torch_dtype", cfg.get("torch_dtype", ""))) == "float16" else _lib.BF16
+    d, H = c["hidden_size"], c["num_attention_heads"]
+    return ModelConfig(n_layers=c["num_hidden_layers"], d_model=d, n_heads=H,
+                       n_kv_heads=c.get("num_key_value_heads", H), head_dim=c.get("head_dim") or d // H,
+                       ffn=c["intermediate_size"], vocab=c["vocab_size"], bits=int(bits or 0), dtype=dtype,
+                       qk_norm=qk_norm, rms_eps=float(c.get("rms_norm_eps", 1e-6)),
+                       rope_theta=float(c.get("rope_theta", 1e6)), **kw)
+
+
+def check_model_checkpoint(st: SafeTensors, cfg) -> None:
+    c = cfg.c()
+    _lib.check(_lib.lib().vella_model_check_checkpoint(st.h, ctypes.byref(c)))
+
+
+def load_model(model_dir, bits: Optional[int] = None, dtype: Optional[int] = None, device: int = 0, **kw):
+    """A decoder model handle with the directory's weights; q/k RMSNorm when the checkpoint
+    has them."""
+    from .decode import Model
+    model_dir = Path(model_dir)
+    raw = json.loads((model_dir / "config.json").read_text())
+    with SafeTensors([str(p) for p in safetensors_files(model_dir)]) as st:
+        qk = any(st.index(pre + "model.layers.0.self_attn.q_norm.weight") >= 0 for pre in ("", "thinker."))
+        cfg = model_config(raw, bits, dtype, qk_norm=qk, **kw)
+        check_model_checkpoint(st, cfg)
+        m = Model(cfg, device)
+        try:
+            _lib.check(_lib.lib().vella_model_load(m.handle, st.h))
+        except Exception:
+            m.close()
+            raise
+    return m

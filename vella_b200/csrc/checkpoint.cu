@@ -28,6 +28,7 @@
 #include <cstdlib>
 #include <initializer_list>
 #include <cstring>
+#include <functional>
 #include <memory>
 #include <string>
 #include <unordered_map>
@@ -393,7 +394,7 @@ std::string hf_key(const std::string& k) {
 }
 
 // Canonical (Hugging Face) name -> entry, and whether conv weights are PyTorch [out, in, k].
-struct WView {
+struct KeyView {
   std::unordered_map<std::string, const StEntry*> by;
   bool hf = true;
   const StEntry* get(const std::string& k) const {
@@ -402,8 +403,8 @@ struct WView {
   }
 };
 
-WView whisper_view(const vella_st* st) {
-  WView v;
+KeyView whisper_view(const vella_st* st) {
+  KeyView v;
   for (const StEntry& e : st->entries)
     if (e.name.find(".blocks.") != std::string::npos) v.hf = false;
   for (const StEntry& e : st->entries) {
@@ -442,20 +443,24 @@ uint16_t act_bits(float v, int act) {
 
 // ---- the loader --------------------------------------------------------------------------
 
+// Checks (no `tensor` callback) or fills a handle's tensors from checkpoint entries; the
+// callback is the handle's tensor lookup (name, layer) -> device pointer and size.
+using TensorFn = std::function<int(const char*, int, void**, size_t*)>;
+
 struct Loader {
-  vella_whisper* w;  // nullptr: check only
-  vella_whisper_cfg c;
-  const WView& v;
+  TensorFn tensor;  // empty: check only
+  const KeyView& v;
   int act;
   cudaStream_t stream = nullptr;
+  bool w = false;   // filling (true) or checking
 
   int dest(const std::string& name, int layer, size_t want, void** p) {
     if (!w) return VELLA_OK;
     size_t bytes = 0;
-    int rc = vella_whisper_tensor(w, name.c_str(), layer, p, &bytes);
+    int rc = tensor(name.c_str(), layer, p, &bytes);
     if (rc) return rc;
     if (bytes != want)
-      return fail(VELLA_E_INVALID, "whisper load: '%s' holds %zu bytes, expected %zu", name.c_str(), bytes, want);
+      return fail(VELLA_E_INVALID, "checkpoint load: '%s' holds %zu bytes, expected %zu", name.c_str(), bytes, want);
     return VELLA_OK;
   }
   int put(void* d, const void* h, size_t bytes) {
@@ -466,7 +471,7 @@ struct Loader {
   }
   const StEntry* need(const std::string& k) {
     const StEntry* e = v.get(k);
-    if (!e) fail(VELLA_E_INVALID, "whisper checkpoint: missing '%s'", k.c_str());
+    if (!e) fail(VELLA_E_INVALID, "checkpoint: missing '%s'", k.c_str());
     return e;
   }
   static bool shape_is(const StEntry* e, std::initializer_list<int64_t> s) {
@@ -478,7 +483,7 @@ struct Loader {
     const StEntry* e = need(key);
     if (!e) return VELLA_E_INVALID;
     if (!is_float(*e) || !shape_is(e, {n}))
-      return fail(VELLA_E_INVALID, "whisper checkpoint: '%s' must be a float [%lld]", key.c_str(), (long long)n);
+      return fail(VELLA_E_INVALID, "checkpoint: '%s' must be a float [%lld]", key.c_str(), (long long)n);
     void* d = nullptr;
     int rc = dest(dname, layer, (size_t)n * 2, &d);
     if (rc || !w) return rc;
@@ -488,16 +493,16 @@ struct Loader {
   }
 
   // a [rows, d] position table: the first `rows` rows of the checkpoint's table
-  int table(const std::string& dname, const std::string& key, int64_t rows, bool optional) {
+  int table(const std::string& dname, const std::string& key, int64_t rows, int64_t dm, bool optional) {
     const StEntry* e = v.get(key);
-    if (!e) return optional ? VELLA_OK : fail(VELLA_E_INVALID, "whisper checkpoint: missing '%s'", key.c_str());
-    if (!is_float(*e) || e->shape.size() != 2 || e->shape[0] < rows || e->shape[1] != c.d_model)
-      return fail(VELLA_E_INVALID, "whisper checkpoint: '%s' must be a float [>= %lld, %d]", key.c_str(),
-                  (long long)rows, c.d_model);
+    if (!e) return optional ? VELLA_OK : fail(VELLA_E_INVALID, "checkpoint: missing '%s'", key.c_str());
+    if (!is_float(*e) || e->shape.size() != 2 || e->shape[0] < rows || e->shape[1] != dm)
+      return fail(VELLA_E_INVALID, "checkpoint: '%s' must be a float [>= %lld, %lld]", key.c_str(),
+                  (long long)rows, (long long)dm);
     void* d = nullptr;
-    int rc = dest(dname, -1, (size_t)rows * c.d_model * 2, &d);
+    int rc = dest(dname, -1, (size_t)(rows * dm) * 2, &d);
     if (rc || !w) return rc;
-    std::vector<uint16_t> h((size_t)rows * c.d_model);
+    std::vector<uint16_t> h((size_t)(rows * dm));
     for (size_t i = 0; i < h.size(); ++i) h[i] = act_bits(elem_f(*e, i), act);
     return put(d, h.data(), h.size() * 2);
   }
@@ -527,34 +532,34 @@ struct Loader {
       if (S[i]) {
         if (conv || !B[i] || W[i]->dtype != VELLA_ST_U32 || W[i]->shape.size() != 2 || W[i]->shape[0] != p.rows ||
             (W[i]->shape[1] * 32 != K * 4 && W[i]->shape[1] * 32 != K * 8))
-          return fail(VELLA_E_INVALID, "whisper checkpoint: '%s.weight' is not MLX-affine [%lld, %lld*bits/32] u32",
+          return fail(VELLA_E_INVALID, "checkpoint: '%s.weight' is not MLX-affine [%lld, %lld*bits/32] u32",
                       p.prefix.c_str(), (long long)p.rows, (long long)K);
         qb = (int)(W[i]->shape[1] * 32 / K);
         if (K % 64 || !is_float(*S[i]) || !is_float(*B[i]) || !shape_is(S[i], {p.rows, K / 64}) ||
             !shape_is(B[i], {p.rows, K / 64}))
-          return fail(VELLA_E_UNSUPPORTED, "whisper checkpoint: '%s' scales/biases are not [%lld, %lld] (group 64)",
+          return fail(VELLA_E_UNSUPPORTED, "checkpoint: '%s' scales/biases are not [%lld, %lld] (group 64)",
                       p.prefix.c_str(), (long long)p.rows, (long long)(K / 64));
       } else {
         const int64_t C = K / 3;
         const bool ok = is_float(*W[i]) && (conv ? shape_is(W[i], {p.rows, v.hf ? C : 3, v.hf ? 3 : C})
                                                   : shape_is(W[i], {p.rows, K}));
         if (!ok)
-          return fail(VELLA_E_INVALID, "whisper checkpoint: '%s.weight' must be a float %s", p.prefix.c_str(),
+          return fail(VELLA_E_INVALID, "checkpoint: '%s.weight' must be a float %s", p.prefix.c_str(),
                       conv ? "Conv1d weight (kernel 3)" : "matrix of the handle's shape");
       }
       if (qbits >= 0 && qbits != qb)
-        return fail(VELLA_E_UNSUPPORTED, "whisper checkpoint: '%s' mixes float and quantized parts", dname.c_str());
+        return fail(VELLA_E_UNSUPPORTED, "checkpoint: '%s' mixes float and quantized parts", dname.c_str());
       qbits = qb;
       if (with_bias && p.bias) {
         Bias[i] = need(p.prefix + ".bias");
         if (!Bias[i]) return VELLA_E_INVALID;
         if (!is_float(*Bias[i]) || !shape_is(Bias[i], {p.rows}))
-          return fail(VELLA_E_INVALID, "whisper checkpoint: '%s.bias' must be a float [%lld]", p.prefix.c_str(),
+          return fail(VELLA_E_INVALID, "checkpoint: '%s.bias' must be a float [%lld]", p.prefix.c_str(),
                       (long long)p.rows);
       }
     }
     if (qbits > 0 && bits > 0 && qbits != bits)
-      return fail(VELLA_E_UNSUPPORTED, "whisper checkpoint: '%s' is %d-bit, the handle %d-bit", dname.c_str(), qbits,
+      return fail(VELLA_E_UNSUPPORTED, "checkpoint: '%s' is %d-bit, the handle %d-bit", dname.c_str(), qbits,
                   bits);
     if (with_bias) {
       void* d = nullptr;
@@ -684,65 +689,129 @@ struct Loader {
     }
     cudaFree(tmp);
     if (rc) return rc;
-    if (e != cudaSuccess) return vella::cuda_fail(e, "whisper load: quantize");
-    return VELLA_OK;
-  }
-
-  int run() {
-    const int64_t d = c.d_model, F = c.ffn;
-    const int bits = c.bits;
-    const int64_t kp1 = (3 * c.n_mels + 63) / 64 * 64;
-    int rc;
-    const std::string E = "model.encoder.", D = "model.decoder.";
-    if ((rc = linear("conv1", -1, {{E + "conv1", d, true}}, 3 * c.n_mels, 0, kp1, true, true))) return rc;
-    if ((rc = linear("conv2", -1, {{E + "conv2", d, true}}, 3 * d, 0, 3 * d, true, true))) return rc;
-    if ((rc = table("enc_pos", E + "embed_positions.weight", c.n_audio, true))) return rc;
-    if ((rc = vec("enc_ln.weight", -1, E + "layer_norm.weight", d)) || (rc = vec("enc_ln.bias", -1, E + "layer_norm.bias", d)))
-      return rc;
-    for (int l = 0; l < c.enc_layers; ++l) {
-      const std::string p = E + "layers." + std::to_string(l) + ".";
-      if ((rc = vec("enc.ln1.weight", l, p + "self_attn_layer_norm.weight", d)) ||
-          (rc = vec("enc.ln1.bias", l, p + "self_attn_layer_norm.bias", d)) ||
-          (rc = vec("enc.ln2.weight", l, p + "final_layer_norm.weight", d)) ||
-          (rc = vec("enc.ln2.bias", l, p + "final_layer_norm.bias", d)))
-        return rc;
-      if ((rc = linear("enc.qkv", l,
-                       {{p + "self_attn.q_proj", d, true}, {p + "self_attn.k_proj", d, false},
-                        {p + "self_attn.v_proj", d, true}},
-                       d, 0, d, false, true)) ||
-          (rc = linear("enc.o", l, {{p + "self_attn.out_proj", d, true}}, d, 0, d, false, true)) ||
-          (rc = linear("enc.fc1", l, {{p + "fc1", F, true}}, d, 0, d, false, true)) ||
-          (rc = linear("enc.fc2", l, {{p + "fc2", d, true}}, F, 0, F, false, true)))
-        return rc;
-    }
-    if ((rc = linear("embed", -1, {{D + "embed_tokens", c.vocab, false}}, d, bits, d, false, false))) return rc;
-    if ((rc = table("dec_pos", D + "embed_positions.weight", c.max_target, false))) return rc;
-    if ((rc = vec("dec_ln.weight", -1, D + "layer_norm.weight", d)) || (rc = vec("dec_ln.bias", -1, D + "layer_norm.bias", d)))
-      return rc;
-    for (int l = 0; l < c.dec_layers; ++l) {
-      const std::string p = D + "layers." + std::to_string(l) + ".";
-      static const std::pair<const char*, const char*> norms[] = {
-          {"dec.ln1", "self_attn_layer_norm"}, {"dec.ln2", "encoder_attn_layer_norm"}, {"dec.ln3", "final_layer_norm"}};
-      for (const auto& nm : norms)
-        if ((rc = vec(std::string(nm.first) + ".weight", l, p + nm.second + ".weight", d)) ||
-            (rc = vec(std::string(nm.first) + ".bias", l, p + nm.second + ".bias", d)))
-          return rc;
-      if ((rc = linear("dec.qkv", l,
-                       {{p + "self_attn.q_proj", d, true}, {p + "self_attn.k_proj", d, false},
-                        {p + "self_attn.v_proj", d, true}},
-                       d, bits, d, false, true)) ||
-          (rc = linear("dec.o", l, {{p + "self_attn.out_proj", d, true}}, d, bits, d, false, true)) ||
-          (rc = linear("dec.cq", l, {{p + "encoder_attn.q_proj", d, true}}, d, bits, d, false, true)) ||
-          (rc = linear("dec.ckv", l, {{p + "encoder_attn.k_proj", d, false}, {p + "encoder_attn.v_proj", d, true}}, d,
-                       bits, d, false, true)) ||
-          (rc = linear("dec.co", l, {{p + "encoder_attn.out_proj", d, true}}, d, bits, d, false, true)) ||
-          (rc = linear("dec.fc1", l, {{p + "fc1", F, true}}, d, bits, d, false, true)) ||
-          (rc = linear("dec.fc2", l, {{p + "fc2", d, true}}, F, bits, F, false, true)))
-        return rc;
-    }
+    if (e != cudaSuccess) return vella::cuda_fail(e, "checkpoint load: quantize");
     return VELLA_OK;
   }
 };
+
+
+int whisper_tensors(Loader& L, const vella_whisper_cfg& c) {
+  const int64_t d = c.d_model, F = c.ffn;
+  const int bits = c.bits;
+  const int64_t kp1 = (3 * c.n_mels + 63) / 64 * 64;
+  int rc;
+  const std::string E = "model.encoder.", D = "model.decoder.";
+  if ((rc = L.linear("conv1", -1, {{E + "conv1", d, true}}, 3 * c.n_mels, 0, kp1, true, true))) return rc;
+  if ((rc = L.linear("conv2", -1, {{E + "conv2", d, true}}, 3 * d, 0, 3 * d, true, true))) return rc;
+  if ((rc = L.table("enc_pos", E + "embed_positions.weight", c.n_audio, d, true))) return rc;
+  if ((rc = L.vec("enc_ln.weight", -1, E + "layer_norm.weight", d)) || (rc = L.vec("enc_ln.bias", -1, E + "layer_norm.bias", d)))
+    return rc;
+  for (int l = 0; l < c.enc_layers; ++l) {
+    const std::string p = E + "layers." + std::to_string(l) + ".";
+    if ((rc = L.vec("enc.ln1.weight", l, p + "self_attn_layer_norm.weight", d)) ||
+        (rc = L.vec("enc.ln1.bias", l, p + "self_attn_layer_norm.bias", d)) ||
+        (rc = L.vec("enc.ln2.weight", l, p + "final_layer_norm.weight", d)) ||
+        (rc = L.vec("enc.ln2.bias", l, p + "final_layer_norm.bias", d)))
+      return rc;
+    if ((rc = L.linear("enc.qkv", l,
+                     {{p + "self_attn.q_proj", d, true}, {p + "self_attn.k_proj", d, false},
+                      {p + "self_attn.v_proj", d, true}},
+                     d, 0, d, false, true)) ||
+        (rc = L.linear("enc.o", l, {{p + "self_attn.out_proj", d, true}}, d, 0, d, false, true)) ||
+        (rc = L.linear("enc.fc1", l, {{p + "fc1", F, true}}, d, 0, d, false, true)) ||
+        (rc = L.linear("enc.fc2", l, {{p + "fc2", d, true}}, F, 0, F, false, true)))
+      return rc;
+  }
+  if ((rc = L.linear("embed", -1, {{D + "embed_tokens", c.vocab, false}}, d, bits, d, false, false))) return rc;
+  if ((rc = L.table("dec_pos", D + "embed_positions.weight", c.max_target, d, false))) return rc;
+  if ((rc = L.vec("dec_ln.weight", -1, D + "layer_norm.weight", d)) || (rc = L.vec("dec_ln.bias", -1, D + "layer_norm.bias", d)))
+    return rc;
+  for (int l = 0; l < c.dec_layers; ++l) {
+    const std::string p = D + "layers." + std::to_string(l) + ".";
+    static const std::pair<const char*, const char*> norms[] = {
+        {"dec.ln1", "self_attn_layer_norm"}, {"dec.ln2", "encoder_attn_layer_norm"}, {"dec.ln3", "final_layer_norm"}};
+    for (const auto& nm : norms)
+      if ((rc = L.vec(std::string(nm.first) + ".weight", l, p + nm.second + ".weight", d)) ||
+          (rc = L.vec(std::string(nm.first) + ".bias", l, p + nm.second + ".bias", d)))
+        return rc;
+    if ((rc = L.linear("dec.qkv", l,
+                     {{p + "self_attn.q_proj", d, true}, {p + "self_attn.k_proj", d, false},
+                      {p + "self_attn.v_proj", d, true}},
+                     d, bits, d, false, true)) ||
+        (rc = L.linear("dec.o", l, {{p + "self_attn.out_proj", d, true}}, d, bits, d, false, true)) ||
+        (rc = L.linear("dec.cq", l, {{p + "encoder_attn.q_proj", d, true}}, d, bits, d, false, true)) ||
+        (rc = L.linear("dec.ckv", l, {{p + "encoder_attn.k_proj", d, false}, {p + "encoder_attn.v_proj", d, true}}, d,
+                     bits, d, false, true)) ||
+        (rc = L.linear("dec.co", l, {{p + "encoder_attn.out_proj", d, true}}, d, bits, d, false, true)) ||
+        (rc = L.linear("dec.fc1", l, {{p + "fc1", F, true}}, d, bits, d, false, true)) ||
+        (rc = L.linear("dec.fc2", l, {{p + "fc2", d, true}}, F, bits, F, false, true)))
+      return rc;
+  }
+  return VELLA_OK;
+}
+
+// Qwen3-style decoder (Qwen3ASRTextDecoder.swift:17-214; keys as Qwen3ASRModel.sanitize
+// leaves them, Qwen3ASRModel.swift:682-708: a "thinker." prefix stripped):
+// model.embed_tokens, model.norm, lm_head (absent when tied to the embedding), and per layer
+// input_layernorm, post_attention_layernorm, self_attn.{q,k,v,o}_proj, self_attn.{q,k}_norm,
+// mlp.{gate,up,down}_proj, none with a bias.
+KeyView model_view(const vella_st* st) {
+  KeyView v;
+  for (const StEntry& e : st->entries) {
+    const std::string k = starts(e.name, "thinker.") ? e.name.substr(8) : e.name;
+    v.by[k] = &e;
+  }
+  return v;
+}
+
+int model_tensors(Loader& L, const vella_model_cfg& c) {
+  const int64_t d = c.d_model, F = c.ffn, hd = c.head_dim, H = c.n_heads, KV = c.n_kv_heads;
+  const int bits = c.bits;
+  int rc;
+  if ((rc = L.linear("embed", -1, {{"model.embed_tokens", c.vocab, false}}, d, 0, d, false, false)))
+    return rc;
+  if ((rc = L.vec("final_norm", -1, "model.norm.weight", d))) return rc;
+  // lm_head, or the embedding when the checkpoint ties them (no lm_head.weight)
+  const char* head = L.v.get("lm_head.weight") ? "lm_head" : "model.embed_tokens";
+  if ((rc = L.linear("lm_head", -1, {{head, c.vocab, false}}, d, bits, d, false, false))) return rc;
+  for (int l = 0; l < c.n_layers; ++l) {
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    if ((rc = L.vec("attn_norm", l, p + "input_layernorm.weight", d)) ||
+        (rc = L.vec("mlp_norm", l, p + "post_attention_layernorm.weight", d)))
+      return rc;
+    if (c.qk_norm && ((rc = L.vec("q_norm", l, p + "self_attn.q_norm.weight", hd)) ||
+                      (rc = L.vec("k_norm", l, p + "self_attn.k_norm.weight", hd))))
+      return rc;
+    if ((rc = L.linear("qkv", l,
+                       {{p + "self_attn.q_proj", H * hd, false}, {p + "self_attn.k_proj", KV * hd, false},
+                        {p + "self_attn.v_proj", KV * hd, false}},
+                       d, bits, d, false, false)) ||
+        (rc = L.linear("o", l, {{p + "self_attn.o_proj", d, false}}, H * hd, bits, H * hd, false, false)) ||
+        (rc = L.linear("gate", l, {{p + "mlp.gate_proj", F, false}}, d, bits, d, false, false)) ||
+        (rc = L.linear("up", l, {{p + "mlp.up_proj", F, false}}, d, bits, d, false, false)) ||
+        (rc = L.linear("down", l, {{p + "mlp.down_proj", d, false}}, F, bits, F, false, false)))
+      return rc;
+  }
+  return VELLA_OK;
+}
+
+// Checks every key and shape, then fills the handle on a private stream of the device that
+// holds `probe` (a device pointer of the handle).
+int check_then_fill(const KeyView& v, int act, const TensorFn& tensor, const void* probe,
+                    const std::function<int(Loader&)>& walk) {
+  Loader chk{TensorFn(), v, act};
+  int rc = walk(chk);
+  if (rc) return rc;  // a failed check leaves the handle as it was
+  cudaPointerAttributes at{};
+  VELLA_CUDA_TRY(cudaPointerGetAttributes(&at, probe));
+  VELLA_CUDA_TRY(cudaSetDevice(at.device));
+  Loader L{tensor, v, act};
+  L.w = true;
+  VELLA_CUDA_TRY(cudaStreamCreateWithFlags(&L.stream, cudaStreamNonBlocking));
+  rc = walk(L);
+  cudaStreamDestroy(L.stream);
+  return rc;
+}
 
 }  // namespace
 
@@ -796,9 +865,9 @@ int vella_st_info(const vella_st* st, int32_t index, const char** name, int32_t*
 
 int vella_whisper_check_checkpoint(const vella_st* st, const vella_whisper_cfg* cfg) {
   if (!st || !cfg) return fail(VELLA_E_INVALID, "vella_whisper_check_checkpoint: NULL argument");
-  const WView v = whisper_view(st);
-  Loader L{nullptr, *cfg, v, cfg->dtype};
-  return L.run();
+  const KeyView v = whisper_view(st);
+  Loader L{TensorFn(), v, cfg->dtype};
+  return whisper_tensors(L, *cfg);
 }
 
 int vella_whisper_load(vella_whisper* w, const vella_st* st) {
@@ -806,21 +875,36 @@ int vella_whisper_load(vella_whisper* w, const vella_st* st) {
   vella_whisper_cfg c{};
   int rc = vella_whisper_get_cfg(w, &c);
   if (rc) return rc;
-  void* p = nullptr;
+  void* probe = nullptr;
   size_t b = 0;
-  if ((rc = vella_whisper_tensor(w, "dec_pos", -1, &p, &b))) return rc;
-  cudaPointerAttributes at{};
-  VELLA_CUDA_TRY(cudaPointerGetAttributes(&at, p));
-  VELLA_CUDA_TRY(cudaSetDevice(at.device));
-  const WView v = whisper_view(st);
-  Loader L{nullptr, c, v, c.dtype};
-  if ((rc = L.run())) return rc;  // every key and shape first: a failed load leaves the handle as it was
-  L.w = w;
-  VELLA_CUDA_TRY(cudaStreamCreateWithFlags(&L.stream, cudaStreamNonBlocking));
-  rc = L.run();
-  cudaStreamDestroy(L.stream);
+  if ((rc = vella_whisper_tensor(w, "dec_pos", -1, &probe, &b))) return rc;
+  const KeyView v = whisper_view(st);
+  const TensorFn fn = [w](const char* n, int l, void** p, size_t* sz) { return vella_whisper_tensor(w, n, l, p, sz); };
+  rc = check_then_fill(v, c.dtype, fn, probe, [&c](Loader& L) { return whisper_tensors(L, c); });
+  return rc ? rc : vella::whisper_weights_loaded(w);
+}
+
+int vella_model_check_checkpoint(const vella_st* st, const vella_model_cfg* cfg) {
+  if (!st || !cfg) return fail(VELLA_E_INVALID, "vella_model_check_checkpoint: NULL argument");
+  const KeyView v = model_view(st);
+  Loader L{TensorFn(), v, cfg->dtype};
+  return model_tensors(L, *cfg);
+}
+
+int vella_model_load(vella_model* m, const vella_st* st) {
+  if (!m || !st) return fail(VELLA_E_INVALID, "vella_model_load: NULL argument");
+  vella_model_cfg c{};
+  int rc = vella_model_get_cfg(m, &c);
   if (rc) return rc;
-  return vella::whisper_weights_loaded(w);
+  void* probe = nullptr;
+  size_t b = 0;
+  if ((rc = vella_model_tensor(m, "embed", -1, &probe, &b))) return rc;
+  const KeyView v = model_view(st);
+  // the dense embedding is the tensor "embed" (the loader asks for "embed.w")
+  const TensorFn fn = [m](const char* n, int l, void** p, size_t* sz) {
+    return vella_model_tensor(m, std::strcmp(n, "embed.w") == 0 ? "embed" : n, l, p, sz);
+  };
+  return check_then_fill(v, c.dtype, fn, probe, [&c](Loader& L) { return model_tensors(L, c); });
 }
 
 }  // extern "C"

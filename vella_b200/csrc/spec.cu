@@ -1112,6 +1112,12 @@ int vella_model_init_random(vella_model* model, uint64_t seed, float std) {
   return model_init_random(model, seed, std, model->stream);
 }
 
+int vella_model_get_cfg(const vella_model* model, vella_model_cfg* out) {
+  if (!model || !out) return fail(VELLA_E_INVALID, "vella_model_get_cfg: NULL argument");
+  *out = model->cfg;
+  return VELLA_OK;
+}
+
 int vella_model_tensor(vella_model* model, const char* name, int32_t layer, void** ptr, size_t* bytes) {
   last_error_slot().clear();
   if (!model || !name || !ptr || !bytes) return fail(VELLA_E_INVALID, "vella_model_tensor: NULL argument");
