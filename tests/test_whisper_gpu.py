@@ -276,15 +276,23 @@ def test_token_rules_follow_the_oracle(tiny):
         assert len(got) == n
         assert got[0] >= r.timestamp_begin and got[1] < r.timestamp_begin, got[:2]
         logits = Wh.score(oc, W, enc_ref, prompt + got[:-1])[len(prompt) - 1:]
-        lp_ref = 0.0
+        lps = []
         for j, t in enumerate(got):
             prev = got[j - 1] if j >= 1 else None
             bprev = got[j - 2] if j >= 2 else None
             assert t in _rule_choices(logits[j], j, prev, bprev, r, LOGIT_TOL), (j, t)
             _, _, final = Wh.rule_select(logits[j], j, prev, bprev, r)
-            lp_ref += float(final[t] - Wh._lse(final))
+            lps.append(float(final[t] - Wh._lse(final)))
+        lp_ref = sum(lps)
         assert abs(lp_gpu - lp_ref) <= 2 * LOGIT_TOL * n, (lp_gpu, lp_ref)
         assert m.decode(prompt, n).tokens == got  # replayed step graph
+        # stopping at an end-of-text id: the tokens before it, and the sum up to it included
+        # (steps enqueued past it add nothing)
+        stop = got[9]
+        first = got.index(stop)
+        cut = m.decode(prompt, n, eot=stop)
+        assert cut.tokens == got[:first]
+        assert abs(m.stats()["sum_logprob"] - sum(lps[:first + 1])) <= 2 * LOGIT_TOL * (first + 1)
     finally:
         m.set_rules(None)
     assert m.decode(prompt, n).tokens == plain

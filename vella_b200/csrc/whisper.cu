@@ -197,6 +197,7 @@ struct WDecodeArgs {
   float temperature;  // 0: argmax; > 0: a draw from softmax(final row / temperature)
   uint32_t seed_lo, seed_hi;
   uint32_t draw;      // the caller's draw index (Philox counter word)
+  int stop;           // end-of-text id of the decode (-1: none): later steps add no log-probability
 };
 constexpr int kRuleThreads = 512;
 
@@ -234,11 +235,12 @@ __device__ __forceinline__ float rule_block_sum(float v, float* red) {
 // (begin-suppress as well at step 0), log-probabilities of the filtered row, the timestamp
 // rules, then argmax (lowest index among equal maxima) or, at a temperature, the Gumbel-max
 // draw argmax(final / temperature + g); the chosen token's log-probability under the final
-// row is added to lpsum[s].  The step is the stream's generated-token count L[s] - n_prompt;
-// the rules read the stream's two last generated tokens.
+// row is added to lpsum[s] until the stream has chosen the decode's end-of-text token (done[s]),
+// so steps enqueued past it change nothing the caller reads.  The step is the stream's
+// generated-token count L[s] - n_prompt; the rules read the stream's two last generated tokens.
 template <typename T>
 __global__ void __launch_bounds__(kRuleThreads) wrules_kernel(const T* __restrict__ logits, int vocab, int rs, int ro,
-                                                               int* ys, float* lpsum, int* nonfinite,
+                                                               int* ys, float* lpsum, int* done, int* nonfinite,
                                                                const float* __restrict__ sup_first,
                                                                const float* __restrict__ sup_later, const int* L,
                                                                const int* tok, const WDecodeArgs* da, int max_target,
@@ -325,7 +327,8 @@ __global__ void __launch_bounds__(kRuleThreads) wrules_kernel(const T* __restric
   if (threadIdx.x == 0) {
     const int t = bi == INT32_MAX ? 0 : bi;
     ys[row] = t;
-    lpsum[s] += final(t) - fmx - logf(z);
+    if (!done[s]) lpsum[s] += final(t) - fmx - logf(z);
+    if (t == a.stop) done[s] = 1;
   }
 }
 
@@ -399,6 +402,7 @@ struct vella_whisper {
   vella::WRules rules{};
   float* rule_masks = nullptr;  // [2][vocab]: first step, later steps (0 or -inf)
   float* lpsum = nullptr;       // [S] summed log-probabilities of the current decode
+  int* done = nullptr;          // [S] the stream chose the decode's end-of-text token
   vella::WDecodeArgs* dargs = nullptr;  // per-decode values read by the selection kernel
   float temperature = 0.0f;             // following decodes: 0 argmax, > 0 sampled
   uint64_t seed = 0x5eed;
@@ -544,11 +548,11 @@ int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, int 
       const float* sl = w->rule_masks + c.vocab;
       if (bf)
         return launch_kernel(wrules_kernel<__nv_bfloat16>, dim3(streams), dim3(kRuleThreads), 0, s,
-                             static_cast<const __nv_bfloat16*>(w->logits), c.vocab, rule_rs, rule_ro, w->ys, w->lpsum,
+                             static_cast<const __nv_bfloat16*>(w->logits), c.vocab, rule_rs, rule_ro, w->ys, w->lpsum, w->done,
                              w->nonfinite, sf, sl, (const int*)w->L, (const int*)w->tok, (const vella::WDecodeArgs*)w->dargs,
                              c.max_target, w->rules);
       return launch_kernel(wrules_kernel<__half>, dim3(streams), dim3(kRuleThreads), 0, s,
-                           static_cast<const __half*>(w->logits), c.vocab, rule_rs, rule_ro, w->ys, w->lpsum,
+                           static_cast<const __half*>(w->logits), c.vocab, rule_rs, rule_ro, w->ys, w->lpsum, w->done,
                            w->nonfinite, sf, sl, (const int*)w->L, (const int*)w->tok, (const vella::WDecodeArgs*)w->dargs,
                            c.max_target, w->rules);
     }
@@ -810,7 +814,7 @@ int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whi
   const size_t o_logits = Q.take(R * (size_t)V * e);
   const size_t o_ints = Q.take((R + S * c.max_target + 2 * S + 8) * sizeof(int));
   const size_t o_amx = Q.take(argmax_scratch_bytes(w->R) + 512);
-  const size_t o_rule = Q.take((S + 64) * sizeof(float));
+  const size_t o_rule = Q.take((2 * S + 64) * sizeof(float));
   const size_t o_ws = Q.take(std::max<size_t>(ws, 256));
   auto cleanup = [&]() {
     if (w->act) cudaFree(w->act);
@@ -858,7 +862,8 @@ int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whi
   w->nonfinite = w->err + 1;
   w->argmax_sc = ab + o_amx;
   w->lpsum = reinterpret_cast<float*>(ab + o_rule);
-  w->dargs = reinterpret_cast<vella::WDecodeArgs*>(w->lpsum + S);
+  w->done = reinterpret_cast<int*>(w->lpsum + S);
+  w->dargs = reinterpret_cast<vella::WDecodeArgs*>(w->done + S);
   w->gemm_ws = ab + o_ws;
   *out = w;
   return VELLA_OK;
@@ -1017,13 +1022,18 @@ int vella_whisper_encode(vella_whisper* w, const float* mel, int32_t on_host) {
 
 // The selection kernel's per-decode values (prompt length, temperature, seed, draw) and
 // zeroed log-probability sums.
-static int decode_args(vella_whisper* w, int n_prompt, cudaStream_t s, const char* what) {
+static int decode_args(vella_whisper* w, int n_prompt, int stop, cudaStream_t s, const char* what) {
   if (w->temperature > 0.0f && !w->rules_on) return fail(VELLA_E_INVALID, "%s: sampling needs token rules", what);
-  const WDecodeArgs a{n_prompt, w->temperature, (uint32_t)w->seed, (uint32_t)(w->seed >> 32), w->draw};
+  const WDecodeArgs a{n_prompt, w->temperature, (uint32_t)w->seed, (uint32_t)(w->seed >> 32), w->draw, stop};
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->dargs, &a, sizeof(a), cudaMemcpyHostToDevice, s));
   VELLA_CUDA_TRY(cudaMemsetAsync(w->lpsum, 0, w->S * sizeof(float), s));
+  VELLA_CUDA_TRY(cudaMemsetAsync(w->done, 0, w->S * sizeof(int), s));
   return VELLA_OK;
 }
+
+// Decoder steps enqueued between two end-of-text checks: the host reads the burst's tokens
+// once; steps past an end-of-text token are wasted work but change no returned value.
+constexpr int kStopBurst = 8;
 
 int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int32_t n_prompt, int32_t max_tokens, int32_t eot,
                          int32_t* out_tokens, int32_t* n_out) {
@@ -1044,42 +1054,45 @@ int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int32_t n_prom
   std::copy(prompt, prompt + n_prompt, init.begin());
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->tok, init.data(), n_prompt * sizeof(int), cudaMemcpyHostToDevice, s));
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->L, &n_prompt, sizeof(int), cudaMemcpyHostToDevice, s));
-  int rc = decode_args(w, n_prompt, s, "vella_whisper_decode");
+  int rc = decode_args(w, n_prompt, eot, s, "vella_whisper_decode");
   if (rc) return rc;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
   rc = decoder_forward(w, PosRef{w->dzero, 0}, n_prompt, 1, 1, s, 0, 0);
   if (rc) return rc;
   if ((rc = commit(w, 0, 0, s))) return rc;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev1, s));
-  int produced = 1;
-  std::vector<int> toks;
-  int t0 = 0;
-  if (eot >= 0) {
-    VELLA_CUDA_TRY(cudaMemcpyAsync(&t0, w->tok + n_prompt, sizeof(int), cudaMemcpyDeviceToHost, s));
-    VELLA_CUDA_TRY(cudaStreamSynchronize(s));
-  }
-  bool stop = eot >= 0 && t0 == eot;
-  while (!stop && produced < max_tokens) {
-    if ((rc = run_step(w))) return rc;
-    ++produced;
-    if (eot >= 0) {
-      int t = 0;
-      VELLA_CUDA_TRY(cudaMemcpyAsync(&t, w->tok + n_prompt + produced - 1, sizeof(int), cudaMemcpyDeviceToHost, s));
-      VELLA_CUDA_TRY(cudaStreamSynchronize(s));
-      stop = t == eot;
+  // steps in bursts; with an end-of-text id the host scans each burst's tokens (the first
+  // token included) and keeps everything up to the first end-of-text
+  int produced = 1, checked = 0, kept = -1;
+  std::vector<int> toks((size_t)max_tokens);
+  while (kept < 0) {
+    const int burst = eot >= 0 ? std::min(kStopBurst, max_tokens - produced) : max_tokens - produced;
+    for (int i = 0; i < burst; ++i)
+      if ((rc = run_step(w))) return rc;
+    produced += burst;
+    if (eot < 0) {
+      kept = produced;
+      break;
     }
+    VELLA_CUDA_TRY(cudaMemcpyAsync(toks.data() + checked, w->tok + n_prompt + checked, (produced - checked) * sizeof(int),
+                                   cudaMemcpyDeviceToHost, s));
+    VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+    for (int i = checked; i < produced && kept < 0; ++i)
+      if (toks[(size_t)i] == eot) kept = i + 1;
+    checked = produced;
+    if (produced == max_tokens && kept < 0) kept = produced;
   }
   VELLA_CUDA_TRY(cudaEventRecord(w->ev2, s));
-  toks.resize(produced);
-  VELLA_CUDA_TRY(cudaMemcpyAsync(toks.data(), w->tok + n_prompt, produced * sizeof(int), cudaMemcpyDeviceToHost, s));
+  if (eot < 0)
+    VELLA_CUDA_TRY(cudaMemcpyAsync(toks.data(), w->tok + n_prompt, produced * sizeof(int), cudaMemcpyDeviceToHost, s));
   VELLA_CUDA_TRY(cudaStreamSynchronize(s));
   cudaEventElapsedTime(&w->stats.prefill_ms, w->ev0, w->ev1);
   cudaEventElapsedTime(&w->stats.decode_ms, w->ev1, w->ev2);
   w->stats.sum_logprob = 0.0f;
   if (w->rules_on) VELLA_CUDA_TRY(cudaMemcpy(&w->stats.sum_logprob, w->lpsum, sizeof(float), cudaMemcpyDeviceToHost));
   if ((rc = check_flags(w, "vella_whisper_decode"))) return rc;
-  int n = produced;
-  if (eot >= 0 && n > 0 && toks[n - 1] == eot) --n;  // the end-of-text token is not emitted
+  int n = kept;
+  if (eot >= 0 && n > 0 && toks[(size_t)n - 1] == eot) --n;  // the end-of-text token is not emitted
   std::copy(toks.begin(), toks.begin() + n, out_tokens);
   *n_out = n;
   w->stats.tokens = n;
@@ -1126,7 +1139,7 @@ int vella_whisper_decode_batch(vella_whisper* w, const int32_t* prompt, int32_t 
   for (int st = 0; st < S; ++st) std::copy(prompt, prompt + n_prompt, toks.begin() + (size_t)st * c.max_target);
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->tok, toks.data(), toks.size() * sizeof(int), cudaMemcpyHostToDevice, s));
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->L, lens.data(), S * sizeof(int), cudaMemcpyHostToDevice, s));
-  int rc = decode_args(w, n_prompt, s, "vella_whisper_decode_batch");
+  int rc = decode_args(w, n_prompt, -1, s, "vella_whisper_decode_batch");
   if (rc) return rc;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
   // the prompts of all streams in one forward (stream st: rows st * n_prompt .., positions
