@@ -444,9 +444,13 @@ VELLA_API int vella_st_info(const vella_st* st, int32_t index, const char** name
                             int64_t* shape, const void** data, size_t* bytes);
 /* Whether a Hugging Face (model.encoder.layers.N...) or OpenAI/mlx-whisper (encoder.blocks.N...)
  * checkpoint holds every tensor a handle of `cfg` needs, with matching shapes (float, or
- * MLX-affine group 64 with the handle's bits for the decoder Linears and token embedding;
- * float Linears of an int4/int8 handle are quantized at load, quantized encoder Linears are
- * dequantized into the dense encoder).  Host-only; VELLA_E_INVALID names the first problem. */
+ * MLX-affine group 64 with the handle's bits for the decoder Linears and token embedding).
+ * A float checkpoint loaded into an int4/int8 handle is the reference's derived precision
+ * (WhisperModel.swift:694-701): the decoder Linears and the token embedding are quantized at
+ * load, and the encoder Linears, which the handle runs dense, hold their quantized values
+ * dequantized; the convolutions and position tables stay float.  Quantized encoder Linears of
+ * an already-quantized checkpoint are dequantized, its float ones kept.  Host-only;
+ * VELLA_E_INVALID names the first problem. */
 VELLA_API int vella_whisper_check_checkpoint(const vella_st* st, const vella_whisper_cfg* cfg);
 /* Fills the handle's weights from the checkpoint (checked first: a failed check leaves the
  * handle unchanged).  q|k|v rows are concatenated with k's bias zero, cross k|v likewise;

@@ -417,7 +417,8 @@ def test_loaded_handles_equal_their_source(tmp_path):
 def test_derived_int4_matches_the_oracle_quantizer(tmp_path):
     """A float (fp16) checkpoint loaded into an int4 handle: every decoder Linear and the token
     embedding are the oracle's MLX-affine quantization of the float rows, bit for bit; the
-    dense encoder is the float values themselves."""
+    dense encoder Linears hold those codes dequantized (the reference's derived precision
+    quantizes every Linear), the convolutions their float values."""
     from vella_b200 import checkpoint as C
     from vella_b200 import whisper as VW
     from dataclasses import replace
@@ -438,7 +439,11 @@ def test_derived_int4_matches_the_oracle_quantizer(tmp_path):
         assert np.array_equal(_download(m, f"{name}.w", layer).view(np.uint32).reshape(q.shape), q), name
         assert np.array_equal(_download(m, f"{name}.s", layer).view(np.float16).reshape(s.shape), s), name
         assert np.array_equal(_download(m, f"{name}.b", layer).view(np.float16).reshape(b.shape), b), name
-    assert np.array_equal(_download(m, "enc.fc1.w", 2), _download(src, "enc.fc1.w", 2))
+    for l in (0, 2):
+        w = t[f"model.encoder.layers.{l}.fc1.weight"].astype(np.float32)
+        deq = A.dequantize(*A.quantize(w, 4, "f16"), 4, "f16").astype(np.float16)
+        assert np.array_equal(_download(m, "enc.fc1.w", l).view(np.float16).reshape(deq.shape), deq), l
+    assert np.array_equal(_download(m, "conv2.w"), _download(src, "conv2.w"))
     m.close()
     src.close()
 

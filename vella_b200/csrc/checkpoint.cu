@@ -31,6 +31,7 @@
 #include <functional>
 #include <memory>
 #include <string>
+#include <type_traits>
 #include <unordered_map>
 #include <utility>
 #include <vector>
@@ -397,6 +398,7 @@ std::string hf_key(const std::string& k) {
 struct KeyView {
   std::unordered_map<std::string, const StEntry*> by;
   bool hf = true;
+  bool quantized = false;  // some tensor has MLX-affine scales (an already-quantized checkpoint)
   const StEntry* get(const std::string& k) const {
     const auto it = by.find(k);
     return it == by.end() ? nullptr : it->second;
@@ -410,7 +412,9 @@ KeyView whisper_view(const vella_st* st) {
   for (const StEntry& e : st->entries) {
     if (!v.hf && e.name == "alignment_heads") continue;
     const std::string k = v.hf ? hf_key(e.name) : mlx_key(e.name);
-    if (!k.empty()) v.by[k] = &e;
+    if (k.empty()) continue;
+    v.by[k] = &e;
+    if (k.size() > 7 && k.compare(k.size() - 7, 7, ".scales") == 0) v.quantized = true;
   }
   return v;
 }
@@ -441,6 +445,36 @@ uint16_t act_bits(float v, int act) {
   return o;
 }
 
+// ---- MLX-affine rows back to the activation dtype ------------------------------------------
+
+template <typename T>
+__device__ __forceinline__ float act_to_f(T v) {
+  if constexpr (std::is_same<T, __half>::value) return __half2float(v);
+  else return __bfloat162float(v);
+}
+template <typename T>
+__device__ __forceinline__ T act_from_f(float v) {
+  if constexpr (std::is_same<T, __half>::value) return __float2half_rn(v);
+  else return __float2bfloat16_rn(v);
+}
+
+// out[r, k] = T(scale * q + bias) for a packed [N, K*bits/32] weight with [N, K/64] scales and
+// biases: the multiply and the add each rounded to fp32, then one rounding to T (the value the
+// tensor-core GEMM dequantizes a weight to).
+template <typename T>
+__global__ void __launch_bounds__(256) dequant_rows_kernel(T* __restrict__ out, const uint32_t* __restrict__ packed,
+                                                           const T* __restrict__ s, const T* __restrict__ b,
+                                                           int64_t K, int bits, int64_t n) {
+  const int per = 32 / bits;
+  const uint32_t mask = (1u << bits) - 1u;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / K, k = i % K;
+    const uint32_t q = (packed[r * (K / per) + k / per] >> ((int)(k % per) * bits)) & mask;
+    const int64_t g = r * (K / 64) + k / 64;
+    out[i] = act_from_f<T>(__fadd_rn(__fmul_rn(act_to_f(s[g]), (float)q), act_to_f(b[g])));
+  }
+}
+
 // ---- the loader --------------------------------------------------------------------------
 
 // Checks (no `tensor` callback) or fills a handle's tensors from checkpoint entries; the
@@ -453,6 +487,9 @@ struct Loader {
   int act;
   cudaStream_t stream = nullptr;
   bool w = false;   // filling (true) or checking
+  // > 0: float Linears of a dense part of the handle hold their MLX-affine values at these
+  // bits (quantized, then dequantized), as the reference's derived precision quantizes them
+  int fake_bits = 0;
 
   int dest(const std::string& name, int layer, size_t want, void** p) {
     if (!w) return VELLA_OK;
@@ -578,6 +615,7 @@ struct Loader {
     }
     if (bits > 0 && qbits > 0) return copy_packed(dname, layer, parts, W, S, B, N, K, bits);
     if (bits > 0) return quantize(dname, layer, parts, W, N, K, bits);
+    if (qbits == 0 && fake_bits > 0 && !conv && kpad == K) return fake_quant(dname, layer, parts, W, N, K);
     return dense(dname, layer, parts, W, S, B, N, K, kpad, conv, qbits);
   }
 
@@ -644,8 +682,8 @@ struct Loader {
     return put(db, hb.data(), sb);
   }
 
-  // derived precision: the float rows (in the source dtype when every part shares it, else
-  // fp32) quantized on the device straight into the handle's packed weight, scales, biases
+  // derived precision: the float rows quantized on the device straight into the handle's
+  // packed weight, scales and biases
   int quantize(const std::string& dname, int layer, const std::vector<Part>& parts,
                const std::vector<const StEntry*>& W, int64_t N, int64_t K, int bits) {
     void *dw = nullptr, *ds = nullptr, *db = nullptr;
@@ -654,6 +692,47 @@ struct Loader {
     if ((rc = dest(dname + ".w", layer, wb, &dw)) || (rc = dest(dname + ".s", layer, sb, &ds)) ||
         (rc = dest(dname + ".b", layer, sb, &db)) || !w)
       return rc;
+    return quantize_into(parts, W, N, K, bits, dw, ds, db);
+  }
+
+  // the dense weight of a derived precision's Linear: MLX-affine at fake_bits, dequantized
+  int fake_quant(const std::string& dname, int layer, const std::vector<Part>& parts,
+                 const std::vector<const StEntry*>& W, int64_t N, int64_t K) {
+    void* d = nullptr;
+    int rc = dest(dname + ".w", layer, (size_t)(N * K) * 2, &d);
+    if (rc || !w) return rc;
+    const int bits = fake_bits;
+    const size_t wb = (size_t)N * (size_t)(K * bits / 32) * 4, sb = (size_t)N * (size_t)(K / 64) * 2;
+    void* tmp = nullptr;
+    VELLA_CUDA_TRY(cudaMalloc(&tmp, wb + 2 * sb));
+    char* t = static_cast<char*>(tmp);
+    rc = quantize_into(parts, W, N, K, bits, t, t + wb, t + wb + sb);
+    cudaError_t e = cudaSuccess;
+    if (!rc) {
+      const int64_t n = N * K;
+      const unsigned grid = (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16);
+      if (act == VELLA_F16)
+        dequant_rows_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<__half*>(d), reinterpret_cast<uint32_t*>(t),
+                                                               reinterpret_cast<__half*>(t + wb),
+                                                               reinterpret_cast<__half*>(t + wb + sb), K, bits, n);
+      else
+        dequant_rows_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+            static_cast<__nv_bfloat16*>(d), reinterpret_cast<uint32_t*>(t),
+            reinterpret_cast<__nv_bfloat16*>(t + wb), reinterpret_cast<__nv_bfloat16*>(t + wb + sb), K, bits, n);
+      e = cudaGetLastError();
+      if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    }
+    cudaFree(tmp);
+    if (rc) return rc;
+    if (e != cudaSuccess) return vella::cuda_fail(e, "checkpoint load: dequantize");
+    return VELLA_OK;
+  }
+
+  // the float rows (in the source dtype when every part shares it, else fp32) quantized on
+  // the device into packed weight, scales and biases
+  int quantize_into(const std::vector<Part>& parts, const std::vector<const StEntry*>& W, int64_t N, int64_t K,
+                    int bits, void* dw, void* ds, void* db) {
+    int rc = VELLA_OK;
     int src = W[0]->dtype;
     for (const StEntry* e : W)
       if (e->dtype != src) src = VELLA_ST_F32;
@@ -706,6 +785,9 @@ int whisper_tensors(Loader& L, const vella_whisper_cfg& c) {
   if ((rc = L.table("enc_pos", E + "embed_positions.weight", c.n_audio, d, true))) return rc;
   if ((rc = L.vec("enc_ln.weight", -1, E + "layer_norm.weight", d)) || (rc = L.vec("enc_ln.bias", -1, E + "layer_norm.bias", d)))
     return rc;
+  // a derived precision (float checkpoint, int handle) quantizes the encoder Linears too, as the
+  // reference's does; an already-quantized checkpoint's float tensors stay float
+  L.fake_bits = L.v.quantized ? 0 : bits;
   for (int l = 0; l < c.enc_layers; ++l) {
     const std::string p = E + "layers." + std::to_string(l) + ".";
     if ((rc = L.vec("enc.ln1.weight", l, p + "self_attn_layer_norm.weight", d)) ||
@@ -722,6 +804,7 @@ int whisper_tensors(Loader& L, const vella_whisper_cfg& c) {
         (rc = L.linear("enc.fc2", l, {{p + "fc2", d, true}}, F, 0, F, false, true)))
       return rc;
   }
+  L.fake_bits = 0;
   if ((rc = L.linear("embed", -1, {{D + "embed_tokens", c.vocab, false}}, d, bits, d, false, false))) return rc;
   if ((rc = L.table("dec_pos", D + "embed_positions.weight", c.max_target, d, false))) return rc;
   if ((rc = L.vec("dec_ln.weight", -1, D + "layer_norm.weight", d)) || (rc = L.vec("dec_ln.bias", -1, D + "layer_norm.bias", d)))
