@@ -377,6 +377,18 @@ VELLA_API int vella_whisper_init_random(vella_whisper* w, uint64_t seed, float s
  * enc_ln, dec_ln, embed (token embedding = vocabulary projection), dec_pos, and the
  * activations enc_out [n_audio, d_model] (the last encoded window) and xkv (the cross-
  * attention K|V of every stream and decoder layer, [streams][dec_layers][n_audio][2 d_model]). */
+/* Whisper's log-mel input features of `streams` windows of 16 kHz mono audio (device
+ * pointers; window s at audio + s * n_samples), each padded with zeros or trimmed to 30 s
+ * (480000 samples): reflect-padded STFT (400-point periodic Hann window, hop 160, 3000
+ * frames), power spectrum, Slaney mel filterbank (80 or 128 bins), log10 floored at the
+ * window's maximum - 8, (x + 4) / 4; out [streams][n_mels][3000] fp32, the layout
+ * vella_whisper_encode reads.  Replaces WhisperAudio.encoderFeatures (WhisperAudio.swift:
+ * 7-93) with MLXAudioCore.melFilters (MLXAudioCore/DSP.swift:44-135). */
+VELLA_API int vella_whisper_log_mel(const float* audio, int64_t n_samples, int32_t streams, int32_t n_mels,
+                                    float* out, vella_stream_t stream);
+/* The log-mel features of every stream's window (audio [streams][n_samples], on the host or
+ * the device), then vella_whisper_encode over them. */
+VELLA_API int vella_whisper_encode_audio(vella_whisper* w, const float* audio, int64_t n_samples, int32_t on_host);
 /* The configuration the handle was created with. */
 VELLA_API int vella_whisper_get_cfg(const vella_whisper* w, vella_whisper_cfg* out);
 VELLA_API int vella_whisper_tensor(vella_whisper* w, const char* name, int32_t layer, void** ptr, size_t* bytes);

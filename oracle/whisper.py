@@ -357,3 +357,64 @@ def attempt_verdict(sum_logprob: float, n_tokens: int, text: str, no_speech_prob
 
 
 FALLBACK_TEMPERATURES = (0.0, 0.2, 0.4, 0.6, 0.8, 1.0)  # WhisperModel.swift:218-219
+
+
+# ---------------------------------------------------------------------------------------
+# Log-mel input features (WhisperAudio.swift:7-93; MLXAudioCore/DSP.swift:44-135)
+# ---------------------------------------------------------------------------------------
+
+SAMPLE_RATE, N_FFT, HOP, WINDOW_SAMPLES = 16000, 400, 160, 480000
+
+
+def mel_filters(n_mels: int) -> np.ndarray:
+    """The reference's Slaney filterbank [201, n_mels], evaluated in fp32 as it does
+    (DSP.swift:44-135): mel points uniform between hz_to_mel(0) and hz_to_mel(8000), rising
+    edge on [low, center), falling on [center, high], each filter scaled by 2 / (high - low)."""
+    f32 = np.float32
+    sr, fmin, fmax = f32(SAMPLE_RATE), f32(0.0), f32(SAMPLE_RATE / 2.0)
+    f_sp, min_log_hz = f32(200.0) / f32(3.0), f32(1000.0)
+    min_log_mel = (min_log_hz - fmin) / f_sp
+    log_step = f32(np.log(f32(6.4))) / f32(27.0)
+
+    def hz_to_mel(f):
+        f = f32(f)
+        return (f - fmin) / f_sp if f < min_log_hz else min_log_mel + f32(np.log(f / min_log_hz)) / log_step
+
+    def mel_to_hz(m):
+        m = f32(m)
+        return fmin + f_sp * m if m < min_log_mel else min_log_hz * f32(np.exp(log_step * (m - min_log_mel)))
+
+    m0, m1 = hz_to_mel(fmin), hz_to_mel(fmax)
+    pts = [mel_to_hz(m0 + f32(i) * (m1 - m0) / f32(n_mels + 1)) for i in range(n_mels + 2)]
+    fb = np.zeros((N_FFT // 2 + 1, n_mels), np.float32)
+    for i in range(N_FFT // 2 + 1):
+        f = f32(i) * sr / f32(N_FFT)
+        for j in range(n_mels):
+            lo, c, hi = pts[j], pts[j + 1], pts[j + 2]
+            v = f32(0.0)
+            if lo <= f < c:
+                v = (f - lo) / (c - lo)
+            elif c <= f <= hi:
+                v = (hi - f) / (hi - c)
+            fb[i, j] = v * (f32(2.0) / (hi - lo))
+    return fb
+
+
+def log_mel(audio: np.ndarray, n_mels: int) -> np.ndarray:
+    """[n_mels, 3000] features of one window: pad with zeros or trim to 30 s, reflect-pad
+    200, frames of 400 every 160 (the last of 3001 dropped), periodic Hann window, |rfft|^2
+    (float64 here), mel projection, log10(max(., 1e-10)), floor at max - 8, (x + 4) / 4."""
+    a = np.zeros(WINDOW_SAMPLES, np.float32)
+    src = np.asarray(audio, np.float32).reshape(-1)[:WINDOW_SAMPLES]
+    a[:src.size] = src
+    padded = np.pad(a, N_FFT // 2, mode="reflect")
+    n_frames = 1 + (padded.size - N_FFT) // HOP
+    idx = np.arange(n_frames)[:, None] * HOP + np.arange(N_FFT)[None, :]
+    n = np.arange(N_FFT, dtype=np.float32)
+    win = np.float32(0.5) * (np.float32(1.0) - np.cos(np.float32(2.0 * np.pi) * n / np.float32(N_FFT)))
+    spec = np.fft.rfft(padded[idx].astype(np.float64) * win.astype(np.float64), axis=-1)
+    power = (spec.real ** 2 + spec.imag ** 2)[:-1]
+    mel = (power @ mel_filters(n_mels).astype(np.float64)).T
+    logs = np.log10(np.maximum(mel, 1e-10))
+    logs = np.maximum(logs, logs.max() - 8.0)
+    return ((logs + 4.0) / 4.0).astype(np.float32)

@@ -168,3 +168,32 @@ def test_fallback_loop_follows_the_reference_order():
     # probable silence empties the window at the first low-confidence attempt
     res = run(_FakeHandle(script), [1], 8, 50257, no_speech_prob=0.9)
     assert res.tokens == [] and res.attempts == 1 and res.verdict == "empty"
+
+
+def test_mel_filterbank_shape_and_peaks():
+    for n in (80, 128):
+        fb = Wh.mel_filters(n)
+        assert fb.shape == (201, n) and (fb >= 0).all()
+        # each triangle peaks at the bin nearest its center and is nonzero somewhere
+        assert (fb.max(axis=0) > 0).all()
+        peaks = fb.argmax(axis=0)
+        assert (np.diff(peaks) >= 0).all()
+    # Slaney area norm: each triangle has unit area in Hz, so its weights times the 40 Hz bin
+    # spacing sum to about 1
+    fb = Wh.mel_filters(80)
+    assert np.allclose(fb.sum(axis=0)[:10] * 40.0, 1.0, atol=0.05)
+
+
+def test_log_mel_properties():
+    # silence: every value at the floor of log10(1e-10) = -10, mapped to -1.5
+    assert np.array_equal(np.unique(Wh.log_mel(np.zeros(16000), 80)), np.array([-1.5], np.float32))
+    t = np.arange(16000 * 5) / 16000.0
+    tone = 0.5 * np.sin(2 * np.pi * 1000.0 * t)
+    m = Wh.log_mel(tone, 80)
+    assert m.shape == (80, 3000)
+    centers = Wh.mel_filters(80).argmax(axis=0) * 40.0
+    assert abs(centers[int(np.argmax(m[:, 100]))] - 1000.0) <= 80.0  # the 1 kHz tone's mel bin
+    assert m.max() - m.min() <= 2.0 + 1e-6  # floored 8 decades below the maximum, / 4
+    # trimming: samples past 30 s change nothing
+    long = np.concatenate([tone, np.zeros(480000), np.ones(1000)])
+    assert np.array_equal(Wh.log_mel(long, 80), Wh.log_mel(np.concatenate([tone, np.zeros(480000)])[:480000], 80))

@@ -127,6 +127,11 @@ int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& plan, const void* x
 int make_tensor_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz);
 
+// Whisper log-mel features of `streams` windows (audio window s at audio + s * audio_stride,
+// n_samples long, padded or trimmed to 30 s) into out [streams][n_mels][3000] (audio.cu).
+int launch_log_mel(const float* audio, int64_t audio_stride, int64_t n_samples, int streams, int n_mels, float* out,
+                   cudaStream_t stream);
+
 // After a checkpoint load: the encoder output and cross-attention K/V are stale until the
 // next vella_whisper_encode (whisper.cu).
 int whisper_weights_loaded(vella_whisper* w);

@@ -386,6 +386,8 @@ struct vella_whisper {
   // activations
   void* act = nullptr;
   float* mel = nullptr;                          // [S][n_mels][2 n_audio]
+  float* audio_buf = nullptr;                    // [S][n_samples] staged audio (encode_audio from the host)
+  size_t audio_cap = 0;
   void *col = nullptr, *x0 = nullptr;            // im2col, conv1 output [2A, d]
   void *eh = nullptr, *en = nullptr, *eqkv = nullptr, *eatt = nullptr, *ef = nullptr, *enc_out = nullptr;
   void* xkv = nullptr;                           // [S][dec_layers][A][2d]
@@ -875,6 +877,7 @@ int vella_whisper_destroy(vella_whisper* w) {
   if (w->stream) cudaStreamSynchronize(w->stream);
   if (w->step_exec) cudaGraphExecDestroy(w->step_exec);
   if (w->rule_masks) cudaFree(w->rule_masks);
+  if (w->audio_buf) cudaFree(w->audio_buf);
   for (cudaEvent_t e : {w->ev0, w->ev1, w->ev2})
     if (e) cudaEventDestroy(e);
   if (w->act) cudaFree(w->act);
@@ -1001,14 +1004,9 @@ int vella_whisper_tensor(vella_whisper* w, const char* name, int32_t layer, void
   return fail(VELLA_E_INVALID, "vella_whisper_tensor: unknown tensor '%s'", name);
 }
 
-int vella_whisper_encode(vella_whisper* w, const float* mel, int32_t on_host) {
-  if (!w || !mel) return fail(VELLA_E_INVALID, "vella_whisper_encode: NULL argument");
-  VELLA_CUDA_TRY(cudaSetDevice(w->device));
-  const vella_whisper_cfg& c = w->cfg;
+// The encoder of every stream over the mel features already in w->mel.
+static int encode_resident(vella_whisper* w) {
   cudaStream_t s = w->stream;
-  VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
-  VELLA_CUDA_TRY(cudaMemcpyAsync(w->mel, mel, (size_t)w->S * c.n_mels * 2 * c.n_audio * sizeof(float),
-                                 on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, s));
   int rc = VELLA_OK;
   for (int st = 0; st < w->S && rc == VELLA_OK; ++st) rc = encoder_forward(w, st, s);
   if (rc) return rc;
@@ -1018,6 +1016,47 @@ int vella_whisper_encode(vella_whisper* w, const float* mel, int32_t on_host) {
   if ((rc = check_flags(w, "vella_whisper_encode"))) return rc;
   w->encoded = true;
   return VELLA_OK;
+}
+
+int vella_whisper_encode(vella_whisper* w, const float* mel, int32_t on_host) {
+  if (!w || !mel) return fail(VELLA_E_INVALID, "vella_whisper_encode: NULL argument");
+  VELLA_CUDA_TRY(cudaSetDevice(w->device));
+  const vella_whisper_cfg& c = w->cfg;
+  cudaStream_t s = w->stream;
+  VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
+  VELLA_CUDA_TRY(cudaMemcpyAsync(w->mel, mel, (size_t)w->S * c.n_mels * 2 * c.n_audio * sizeof(float),
+                                 on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, s));
+  return encode_resident(w);
+}
+
+int vella_whisper_encode_audio(vella_whisper* w, const float* audio, int64_t n_samples, int32_t on_host) {
+  if (!w || !audio || n_samples < 0) return fail(VELLA_E_INVALID, "vella_whisper_encode_audio: NULL argument");
+  const vella_whisper_cfg& c = w->cfg;
+  if (2 * c.n_audio != 3000 || (c.n_mels != 80 && c.n_mels != 128))
+    return fail(VELLA_E_UNSUPPORTED, "vella_whisper_encode_audio: the 30 s log-mel window needs n_audio 1500 and "
+                "80 or 128 mel bins");
+  VELLA_CUDA_TRY(cudaSetDevice(w->device));
+  cudaStream_t s = w->stream;
+  const float* src = audio;
+  if (on_host) {
+    const size_t need = (size_t)w->S * (size_t)n_samples;
+    if (need > w->audio_cap) {
+      VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+      if (w->audio_buf) cudaFree(w->audio_buf);
+      w->audio_buf = nullptr;
+      w->audio_cap = 0;
+      VELLA_CUDA_TRY(cudaMalloc(&w->audio_buf, std::max<size_t>(need, 1) * sizeof(float)));
+      w->audio_cap = need;
+    }
+    src = w->audio_buf;
+  }
+  VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
+  if (on_host && n_samples > 0)
+    VELLA_CUDA_TRY(cudaMemcpyAsync(w->audio_buf, audio, (size_t)w->S * (size_t)n_samples * sizeof(float),
+                                   cudaMemcpyHostToDevice, s));
+  const int rc = launch_log_mel(src, n_samples, n_samples, w->S, c.n_mels, w->mel, s);
+  if (rc) return rc;
+  return encode_resident(w);
 }
 
 // The selection kernel's per-decode values (prompt length, temperature, seed, draw) and

@@ -21,6 +21,21 @@ from . import _lib
 FALLBACK_TEMPERATURES = (0.0, 0.2, 0.4, 0.6, 0.8, 1.0)  # WhisperModel.swift:218-219
 
 
+def log_mel(audio, n_mels: int = 80):
+    """Whisper's log-mel features [streams, n_mels, 3000] of windows of 16 kHz mono audio
+    ([streams, n] or [n]; CUDA tensors stay on their device), computed by the library."""
+    import torch
+    a = torch.as_tensor(audio, dtype=torch.float32)
+    if not a.is_cuda:
+        a = a.cuda()
+    a = a.reshape(-1, a.shape[-1]).contiguous()
+    out = torch.empty((a.shape[0], n_mels, 3000), dtype=torch.float32, device=a.device)
+    with torch.cuda.device(a.device):
+        st = torch.cuda.current_stream().cuda_stream
+        _lib.check(_lib.lib().vella_whisper_log_mel(a.data_ptr(), a.shape[1], a.shape[0], n_mels, out.data_ptr(), st))
+    return out
+
+
 def compression_ratio(text: str) -> float:
     """UTF-8 bytes over zlib-compressed bytes (default level); 0 for empty text
     (``compressionRatio``, WhisperModel.swift:434-445)."""
@@ -78,6 +93,8 @@ for _name, _res, _args in [
     ("vella_whisper_tensor", ctypes.c_int, [_vp, ctypes.c_char_p, _i32, ctypes.POINTER(_vp),
                                             ctypes.POINTER(ctypes.c_size_t)]),
     ("vella_whisper_encode", ctypes.c_int, [_vp, _vp, _i32]),
+    ("vella_whisper_encode_audio", ctypes.c_int, [_vp, _vp, ctypes.c_int64, _i32]),
+    ("vella_whisper_log_mel", ctypes.c_int, [_vp, ctypes.c_int64, _i32, _i32, _vp, _vp]),
     ("vella_whisper_decode", ctypes.c_int, [_vp, _pi32, _i32, _i32, _i32, _pi32, _pi32]),
     ("vella_whisper_decode_batch", ctypes.c_int, [_vp, _pi32, _i32, _i32, _pi32]),
     ("vella_whisper_score", ctypes.c_int, [_vp, _pi32, _i32, _vp, _i32]),
@@ -158,6 +175,18 @@ class Whisper:
         else:
             ptr = mel if isinstance(mel, int) else mel.data_ptr()
             _lib.check(_lib.lib().vella_whisper_encode(self.h, ptr, 0 if on_host is None else int(on_host)))
+
+    def encode_audio(self, audio):
+        """Log-mel features of every stream's window of 16 kHz mono audio ([streams, n] or [n],
+        a numpy array or a CUDA tensor), then the encoder."""
+        import torch
+        if isinstance(audio, torch.Tensor) and audio.is_cuda:
+            a = audio.float().contiguous()
+            _lib.check(_lib.lib().vella_whisper_encode_audio(self.h, a.data_ptr(), a.shape[-1], 0))
+            torch.cuda.current_stream().synchronize()
+            return
+        a = np.ascontiguousarray(np.asarray(audio, np.float32))
+        _lib.check(_lib.lib().vella_whisper_encode_audio(self.h, a.ctypes.data, a.shape[-1], 1))
 
     def decode(self, prompt: Sequence[int], max_tokens: int, eot: int = -1) -> DecodeResult:
         pr = (ctypes.c_int32 * len(prompt))(*prompt)
