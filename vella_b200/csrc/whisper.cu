@@ -1,11 +1,12 @@
-// Whisper encoder and decoder step on one GPU (one audio stream per handle).
+// Whisper encoder and decoder step on one GPU (one or more audio streams per handle).
 //
 // Reference: Worker/Sources/MLXAudioSTT/Whisper/WhisperLayers.swift:11-329 (attention with
 // k_proj unbiased, encoder conv1/conv2/positions/pre-LN blocks, decoder layers with self- and
 // cross-attention, tied vocabulary projection), WhisperFusedDecode.swift:105-259 (the fused
 // decode step: q|k|v as one projection with k's bias zero, the KV append, residual add +
-// LayerNorm), WhisperModel.swift:341-400 (greedy loop; its token rules are not applied) and
-// :554-569 (sinusoid table: double trig, rounded to fp32, then to the table dtype).
+// LayerNorm), WhisperModel.swift:341-400 (the greedy loop with its token rules, :311-372) and
+// :218-292 (the temperature fallback's sampled attempts), :554-569 (sinusoid table: double
+// trig, rounded to fp32, then to the table dtype).
 //
 // B200 layout: every weight in one arena; the encoder runs its GEMMs on the tensor cores
 // (M = 3000 / 1500 rows) and the attention as the library's clustered flash-decoding kernel

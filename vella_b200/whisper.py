@@ -4,7 +4,9 @@
 The model runs in the library (C++ host code, CUDA kernels, one CUDA graph per decoder step);
 this module marshals arguments for the tests and the benchmark.  Names follow the reference's
 ``WhisperModel`` (``Worker/Sources/MLXAudioSTT/Whisper/WhisperModel.swift``): ``encode`` runs
-the encoder and projects the cross-attention K/V, ``decode`` the greedy loop.
+the encoder and projects the cross-attention K/V (``encode_audio`` computes the log-mel
+features first), ``decode`` the greedy loop, under the token rules once ``set_rules`` is
+called, ``decode_with_fallback`` the temperature fallback.
 """
 from __future__ import annotations
 
