@@ -431,11 +431,39 @@ struct TreeTopo {
   const int* n_child;                  // [nodes]
 };
 
-struct TreePath {  // the accepted path of the last pass, for the KV compaction
-  int root;        // cache slot of the root (node 0)
-  int a;           // accepted nodes
-  int node[16];    // node of depth 1..a
+// One model's KV cache as the compaction sees it: per stream (kv_ss apart) and layer, a K and a
+// V plane of kv_heads blocks [max_seq][hd].
+template <typename T>
+struct KvPlanes {
+  T* kv;
+  long long kv_ss;
+  int layers, kv_heads, max_seq, hd;
 };
+
+// The whole block moves the K/V rows of stream s's accepted path (slots root + path[j - 1]) to
+// consecutive slots root + j, j = 1..a, in every layer and head; ascending j, one barrier per
+// j: a source is never an earlier destination (a node of depth j sits at slot >= root + j).
+template <typename T>
+__device__ void compact_path(const KvPlanes<T>& p, int s, int root, int a, const int* path) {
+  const size_t plane = (size_t)p.kv_heads * p.max_seq * p.hd;
+  T* base = p.kv + (size_t)s * p.kv_ss;
+  const int blocks = p.layers * 2 * p.kv_heads;  // (layer, K|V, head) blocks
+  const bool vec = (p.hd * (int)sizeof(T)) % 16 == 0;
+  const int per_row = vec ? p.hd * (int)sizeof(T) / 16 : p.hd;
+  for (int j = 1; j <= a; ++j) {
+    const int src = root + path[j - 1], dst = root + j;
+    if (src != dst && src < p.max_seq && dst < p.max_seq)
+      for (int e = threadIdx.x; e < blocks * per_row; e += blockDim.x) {
+        const int b = e / per_row, c = e % per_row;
+        T* blk = base + (size_t)(b / p.kv_heads) * plane + (size_t)(b % p.kv_heads) * p.max_seq * p.hd;
+        if (vec)
+          reinterpret_cast<uint4*>(blk + (size_t)dst * p.hd)[c] = reinterpret_cast<const uint4*>(blk + (size_t)src * p.hd)[c];
+        else
+          blk[(size_t)dst * p.hd + c] = blk[(size_t)src * p.hd + c];
+      }
+    __syncthreads();
+  }
+}
 
 __global__ void tree_root_kernel(const DevState* st, const int* tok, int* ttok, unsigned char* onpath, int N,
                                  int max_seq) {
@@ -541,12 +569,14 @@ __global__ void __launch_bounds__(kSampThreads) tree_expand_kernel(const DevStat
   if (threadIdx.x == 0) qstats[(size_t)node * S + s] = mz;
 }
 
-// Tree acceptance of stream blockIdx.x over the verify rows of its N nodes.
+// Tree acceptance of stream blockIdx.x over the verify rows of its N nodes, then the KV
+// compaction of the accepted path in the target's and the draft's caches (one launch after
+// the verify logits).
 template <typename T>
 __global__ void __launch_bounds__(kSampThreads) tree_accept_kernel(
     DevState* st, int* tok, const T* logits, const int* ys, TreeTopo tt, vella_spec_cfg_dev c, const int* ttok,
     const unsigned char* onpath, const int* ref, const T* qrows, const float2* qstats, int S, float* resid,
-    TreePath* paths, int vocab, int max_seq, const int* nf, const int* err_t, const int* err_d) {
+    KvPlanes<T> kt, KvPlanes<T> kd, int vocab, int max_seq, const int* nf, const int* err_t, const int* err_d) {
   __shared__ SampShared sh;
   __shared__ int s_u, s_a, s_acc, s_bonus, s_path[16];
   pdl_wait();
@@ -560,7 +590,6 @@ __global__ void __launch_bounds__(kSampThreads) tree_accept_kernel(
       x.nonfinite = *nf;
       x.err |= *err_t | *err_d;
       x.n_new = 0;
-      paths[s].a = 0;
     }
     return;
   }
@@ -662,33 +691,9 @@ __global__ void __launch_bounds__(kSampThreads) tree_accept_kernel(
     x.L = root + a + 2;
     x.pass += 1;
     x.produced += a + 1;
-    TreePath& tp = paths[s];
-    tp.root = root;
-    tp.a = a;
-    for (int j = 0; j < a; ++j) tp.node[j] = s_path[j];
   }
-}
-
-// Moves the K/V of the accepted path (slots root + node_j) to consecutive slots root + j, in
-// every layer of one model; block = (layer x kv head, stream), thread = head element.
-template <typename T>
-__global__ void tree_compact_kernel(T* kv, const TreePath* paths, int KV, int max_seq, int hd, long long kv_ss) {
-  pdl_wait();
-  pdl_launch_next();
-  const int s = blockIdx.y, l = blockIdx.x / KV, h = blockIdx.x % KV;
-  const TreePath& tp = paths[s];
-  const size_t plane = (size_t)KV * max_seq * hd;
-  T* kb = kv + (size_t)s * kv_ss + (size_t)l * 2 * plane + (size_t)h * max_seq * hd;
-  T* vb = kb + plane;
-  for (int j = 1; j <= tp.a; ++j) {  // ascending: a source is never an earlier destination
-    const int src = tp.root + tp.node[j - 1], dst = tp.root + j;
-    if (src != dst && src < max_seq && dst < max_seq)
-      for (int e = threadIdx.x; e < hd; e += blockDim.x) {
-        kb[(size_t)dst * hd + e] = kb[(size_t)src * hd + e];
-        vb[(size_t)dst * hd + e] = vb[(size_t)src * hd + e];
-      }
-    __syncthreads();
-  }
+  compact_path(kt, s, root, s_a, s_path);
+  compact_path(kd, s, root, s_a, s_path);
 }
 
 }  // namespace
@@ -724,7 +729,6 @@ struct Spec {
   unsigned long long* tree_mask = nullptr;  // [N] ancestors-or-self
   int* ttok = nullptr;                      // [streams][N] tree tokens
   unsigned char* onpath = nullptr;          // [streams][N] oracle draft: node follows the reference
-  TreePath* paths = nullptr;                // [streams]
   float* resid = nullptr;                   // [streams][vocab] running residual (stochastic tree acceptance)
 
   int span() const { return tree_nodes ? tree_nodes : cfg.draft_k + 1; }  // slots a pass writes from L - 1
@@ -806,22 +810,21 @@ int launch_tree_expand(Spec* s, int depth) {
 }
 
 template <typename T>
+KvPlanes<T> kv_planes(const Model* m) {
+  const vella_model_cfg& c = m->cfg;
+  return KvPlanes<T>{static_cast<T*>(m->kv), m->kv_ss, c.n_layers, c.n_kv_heads, c.max_seq, c.head_dim};
+}
+
+template <typename T>
 int launch_tree_accept(Spec* s) {
   const Model* t = s->target;
   return launch_kernel(tree_accept_kernel<T>, dim3(s->streams), dim3(kSampThreads), 0, s->stream, s->dstate, s->tok,
                        static_cast<const T*>(t->logits), (const int*)t->ys, s->topo, s->dev_cfg(),
                        (const int*)s->ttok, (const unsigned char*)s->onpath, (const int*)s->ref,
-                       static_cast<const T*>(s->qrows), (const float2*)s->qstats, s->streams, s->resid, s->paths,
+                       static_cast<const T*>(s->qrows), (const float2*)s->qstats, s->streams, s->resid,
+                       kv_planes<T>(t), kv_planes<T>(s->draft),
                        t->cfg.vocab, s->max_seq, (const int*)t->nonfinite, (const int*)t->err,
                        (const int*)s->draft->err);
-}
-
-template <typename T>
-int launch_tree_compact(Spec* s, Model* m) {
-  const vella_model_cfg& c = m->cfg;
-  return launch_kernel(tree_compact_kernel<T>, dim3(c.n_layers * c.n_kv_heads, s->streams), dim3(c.head_dim), 0,
-                       s->stream, static_cast<T*>(m->kv), (const TreePath*)s->paths, c.n_kv_heads, c.max_seq,
-                       c.head_dim, m->kv_ss);
 }
 
 // One tree pass: the draft expands the tree depth by depth (step 0 over the two committed
@@ -849,8 +852,6 @@ int enqueue_tree_pass(Spec* s) {
   const TreeView tv = tree_view(s, 0);
   if ((rc = model_forward(t, state_pos(s, -1), N, S, 0, s->tok, s->max_seq, Pp, N, s->stream, &tv))) return rc;
   if ((rc = bf ? launch_tree_accept<__nv_bfloat16>(s) : launch_tree_accept<__half>(s))) return rc;
-  if ((rc = bf ? launch_tree_compact<__nv_bfloat16>(s, t) : launch_tree_compact<__half>(s, t))) return rc;
-  if ((rc = bf ? launch_tree_compact<__nv_bfloat16>(s, d) : launch_tree_compact<__half>(s, d))) return rc;
   VELLA_CUDA_TRY(cudaMemsetAsync(d->nonfinite, 0, sizeof(int), s->stream));
   VELLA_CUDA_TRY(cudaMemsetAsync(t->nonfinite, 0, sizeof(int), s->stream));
   return VELLA_OK;
@@ -1251,7 +1252,6 @@ int vella_spec_create(vella_model* target, vella_model* draft, const vella_spec_
     cuda(cudaMalloc(&s->tree_mask, (size_t)N * sizeof(unsigned long long)), "cudaMalloc(tree mask)");
     cuda(cudaMalloc(&s->ttok, S * N * sizeof(int)), "cudaMalloc(tree tokens)");
     cuda(cudaMalloc(&s->onpath, S * N), "cudaMalloc(tree path flags)");
-    cuda(cudaMalloc(&s->paths, S * sizeof(TreePath)), "cudaMalloc(tree paths)");
     if (cfg->temperature > 0.0f)
       cuda(cudaMalloc(&s->resid, S * target->cfg.vocab * sizeof(float)), "cudaMalloc(residual)");
     if (rc == VELLA_OK) {
@@ -1261,7 +1261,6 @@ int vella_spec_create(vella_model* target, vella_model* draft, const vella_spec_
       std::copy(nch.begin(), nch.end(), host.begin() + 2 * N);
       cuda(cudaMemcpy(s->tree_dev, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice), "cudaMemcpy");
       cuda(cudaMemcpy(s->tree_mask, mask.data(), N * sizeof(unsigned long long), cudaMemcpyHostToDevice), "cudaMemcpy");
-      cuda(cudaMemset(s->paths, 0, S * sizeof(TreePath)), "cudaMemset");
       s->topo.dep = s->tree_dev;
       s->topo.first_child = s->tree_dev + N;
       s->topo.n_child = s->tree_dev + 2 * N;
@@ -1295,7 +1294,7 @@ int vella_spec_destroy(vella_spec* s) {
   if (s->ref) cudaFree(s->ref);
   if (s->qrows) cudaFree(s->qrows);
   if (s->qstats) cudaFree(s->qstats);
-  for (void* p : {(void*)s->tree_dev, (void*)s->tree_mask, (void*)s->ttok, (void*)s->onpath, (void*)s->paths,
+  for (void* p : {(void*)s->tree_dev, (void*)s->tree_mask, (void*)s->ttok, (void*)s->onpath,
                   (void*)s->resid})
     if (p) cudaFree(p);
   if (s->ev0) cudaEventDestroy(s->ev0);
