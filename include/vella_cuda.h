@@ -405,6 +405,15 @@ VELLA_API int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int3
  * stats' tokens field counts all streams' tokens. */
 VELLA_API int vella_whisper_decode_batch(vella_whisper* w, const int32_t* prompt, int32_t n_prompt,
                                          int32_t max_tokens, int32_t* out_tokens);
+/* The same with an end-of-text id: the host checks every stream's tokens once per burst of 8
+ * steps and stops when every stream has produced `eot` (or after max_tokens); n_out[s] counts
+ * stream s's tokens before its end-of-text, later entries of its out_tokens row are -1.  With
+ * token rules set each stream's log-probability sum stops at its end-of-text step. */
+VELLA_API int vella_whisper_decode_batch_eot(vella_whisper* w, const int32_t* prompt, int32_t n_prompt,
+                                             int32_t max_tokens, int32_t eot, int32_t* out_tokens, int32_t* n_out);
+/* The summed log-probabilities of the last decode's first n streams (token rules set; zeros
+ * otherwise). */
+VELLA_API int vella_whisper_get_logprobs(const vella_whisper* w, float* out, int32_t n);
 /* Token rules for the following decodes (NULL: plain argmax, the default).  The ids must lie
  * in the vocabulary with eot < timestamp_begin; the masks are built on the device here. */
 VELLA_API int vella_whisper_set_rules(vella_whisper* w, const vella_whisper_rules* rules);

@@ -374,3 +374,36 @@ def test_log_mel_matches_the_oracle_and_feeds_the_encoder(tiny):
     m.encode(got[0])
     assert np.array_equal(download(m, "enc_out"), from_audio)
     m.encode(mel)  # the fixture's window again
+
+
+def test_batched_end_of_text_and_log_probabilities_follow_single_streams():
+    """Three streams under the token rules with an end-of-text id: each stream's tokens and
+    summed log-probability equal those of a one-stream handle decoding its window alone."""
+    from dataclasses import replace
+
+    from vella_b200 import whisper as VW
+    S, n, std = 3, 16, 0.1
+    prompt = [50258, 50259, 50359, 50363]
+    V = VW.TINY.vocab
+    rules = dict(eot=50257, no_timestamps=V - 3, timestamp_begin=V - 2, suppress=[220], begin_suppress=[50257, 220])
+    mels = np.stack([mel_of(VW.TINY, 40 + st) for st in range(S)])
+    mb = VW.Whisper(replace(VW.TINY, streams=S))
+    mb.init_random(5, std)
+    mb.set_rules(**rules)
+    mb.encode(mels)
+    full = mb.decode_batch(prompt, n)
+    stop = int(full[0][5])  # ends stream 0 at its first occurrence; the others wherever it appears
+    got = mb.decode_batch(prompt, n, eot=stop)
+    lps = mb.logprobs()
+    single = VW.Whisper(VW.TINY)
+    single.init_random(5, std)
+    single.set_rules(**rules)
+    for st in range(S):
+        row = list(full[st])
+        want = row[:row.index(stop)] if stop in row else row
+        assert got[st] == want, st
+        single.encode(mels[st])
+        assert single.decode(prompt, n, eot=stop).tokens == want, st
+        assert abs(single.stats()["sum_logprob"] - lps[st]) <= 1e-4 * max(1.0, abs(lps[st])), st
+    single.close()
+    mb.close()

@@ -71,7 +71,9 @@ int device_workspace(size_t bytes, void** out) {
       cudaGetLastError();
       return fail(VELLA_E_OOM, "workspace allocation of %zu bytes failed", want);
     }
+    // zeroed before any stream uses it (callers' streams may be non-blocking)
     VELLA_CUDA_TRY(cudaMemset(p, 0, want));
+    VELLA_CUDA_TRY(cudaDeviceSynchronize());
     ws.ptr = p;
     ws.bytes = want;
   }

@@ -340,7 +340,9 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
     delete m;
     return fail(VELLA_E_OOM, "vella_model_create: %zu bytes of cache and buffers", total);
   }
-  VELLA_CUDA_TRY(cudaMemset(m->act_arena, 0, total));
+  // zeroed on the model's non-blocking stream and waited for before any kernel uses it
+  VELLA_CUDA_TRY(cudaMemsetAsync(m->act_arena, 0, total, m->stream));
+  VELLA_CUDA_TRY(cudaStreamSynchronize(m->stream));
   char* p = static_cast<char*>(m->act_arena);
   void* slots[16];
   for (int i = 0; i < 16; ++i) { slots[i] = p; p += up256(sizes[i]); }

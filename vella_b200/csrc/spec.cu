@@ -1271,8 +1271,10 @@ int vella_spec_create(vella_model* target, vella_model* draft, const vella_spec_
   cuda(cudaEventCreate(&s->evp), "cudaEventCreate");
   if (rc == VELLA_OK) {
     std::memset(s->hstate, 0, S * sizeof(DevState));
-    cuda(cudaMemset(s->dstate, 0, S * sizeof(DevState)), "cudaMemset");
-    cuda(cudaMemset(s->tok, 0, S * s->max_seq * sizeof(int)), "cudaMemset");
+    // on the handle's non-blocking stream, waited for: the passes run on that stream
+    cuda(cudaMemsetAsync(s->dstate, 0, S * sizeof(DevState), s->stream), "cudaMemsetAsync");
+    cuda(cudaMemsetAsync(s->tok, 0, S * s->max_seq * sizeof(int), s->stream), "cudaMemsetAsync");
+    cuda(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize");
   }
   if (rc != VELLA_OK) {
     vella_spec_destroy(s);

@@ -607,11 +607,13 @@ int check_flags(vella_whisper* w, const char* what) {
   int f[2] = {0, 0};
   VELLA_CUDA_TRY(cudaMemcpy(f, w->err, 2 * sizeof(int), cudaMemcpyDeviceToHost));
   if (f[0]) {
-    VELLA_CUDA_TRY(cudaMemset(w->err, 0, sizeof(int)));
+    VELLA_CUDA_TRY(cudaMemsetAsync(w->err, 0, sizeof(int), w->stream));
+    VELLA_CUDA_TRY(cudaStreamSynchronize(w->stream));
     return fail(VELLA_E_INVALID, "%s: error flags 0x%x (token id out of range or past max_target)", what, f[0]);
   }
   if (f[1]) {
-    VELLA_CUDA_TRY(cudaMemset(w->nonfinite, 0, sizeof(int)));
+    VELLA_CUDA_TRY(cudaMemsetAsync(w->nonfinite, 0, sizeof(int), w->stream));
+    VELLA_CUDA_TRY(cudaStreamSynchronize(w->stream));
     return fail(VELLA_E_NONFINITE, "%s: non-finite logits", what);
   }
   const int st = stream_fault_status(1), tc = tc_fault_status(1);
@@ -830,8 +832,12 @@ int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whi
     cleanup();
     return fail(VELLA_E_OOM, "vella_whisper_create: %zu + %zu bytes", P.off, Q.off);
   }
+  // the zeroing runs on the handle's own (non-blocking) stream and is waited for here: on the
+  // legacy stream it could still be running when the handle's first kernels write the arena
   if (cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaMemset(w->act, 0, Q.off) != cudaSuccess || cudaMemset(w->arena, 0, w->arena_bytes) != cudaSuccess ||
+      cudaMemsetAsync(w->act, 0, Q.off, w->stream) != cudaSuccess ||
+      cudaMemsetAsync(w->arena, 0, w->arena_bytes, w->stream) != cudaSuccess ||
+      cudaStreamSynchronize(w->stream) != cudaSuccess ||
       cudaEventCreate(&w->ev0) != cudaSuccess || cudaEventCreate(&w->ev1) != cudaSuccess ||
       cudaEventCreate(&w->ev2) != cudaSuccess) {
     cleanup();
@@ -1160,26 +1166,29 @@ int vella_whisper_score(vella_whisper* w, const int32_t* tokens, int32_t T, void
   return check_flags(w, "vella_whisper_score");
 }
 
-int vella_whisper_decode_batch(vella_whisper* w, const int32_t* prompt, int32_t n_prompt, int32_t max_tokens,
-                               int32_t* out_tokens) {
-  if (!w || !prompt || (max_tokens > 0 && !out_tokens))
-    return fail(VELLA_E_INVALID, "vella_whisper_decode_batch: NULL argument");
+// The batched decode: every stream from the same prompt, one decoder forward of S rows per
+// token.  With an end-of-text id (eot >= 0) the host scans each burst's tokens of every stream
+// and stops once every stream has produced it; n_out[s] counts the tokens before it, and the
+// tokens after a stream's end-of-text are -1 in out_tokens.
+static int decode_batch_impl(vella_whisper* w, const int32_t* prompt, int32_t n_prompt, int32_t max_tokens, int32_t eot,
+                             int32_t* out_tokens, int32_t* n_out, const char* what) {
+  if (!w || !prompt || (max_tokens > 0 && !out_tokens)) return fail(VELLA_E_INVALID, "%s: NULL argument", what);
   const vella_whisper_cfg& c = w->cfg;
-  if (!w->encoded) return fail(VELLA_E_INVALID, "vella_whisper_decode_batch: encode first");
-  if (n_prompt < 1 || n_prompt > kWRows)
-    return fail(VELLA_E_INVALID, "vella_whisper_decode_batch: prompt of %d tokens (1..%d)", n_prompt, kWRows);
+  if (!w->encoded) return fail(VELLA_E_INVALID, "%s: encode first", what);
+  if (n_prompt < 1 || n_prompt > kWRows) return fail(VELLA_E_INVALID, "%s: prompt of %d tokens (1..%d)", what, n_prompt, kWRows);
   if (max_tokens < 0 || n_prompt + max_tokens > c.max_target)
-    return fail(VELLA_E_INVALID, "vella_whisper_decode_batch: %d + %d positions exceed max_target %d", n_prompt,
-                max_tokens, c.max_target);
+    return fail(VELLA_E_INVALID, "%s: %d + %d positions exceed max_target %d", what, n_prompt, max_tokens, c.max_target);
+  const int S = w->S;
+  if (n_out)
+    for (int st = 0; st < S; ++st) n_out[st] = 0;
   if (max_tokens == 0) return VELLA_OK;
   VELLA_CUDA_TRY(cudaSetDevice(w->device));
   cudaStream_t s = w->stream;
-  const int S = w->S;
   std::vector<int> toks((size_t)S * c.max_target, 0), lens(S, n_prompt);
   for (int st = 0; st < S; ++st) std::copy(prompt, prompt + n_prompt, toks.begin() + (size_t)st * c.max_target);
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->tok, toks.data(), toks.size() * sizeof(int), cudaMemcpyHostToDevice, s));
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->L, lens.data(), S * sizeof(int), cudaMemcpyHostToDevice, s));
-  int rc = decode_args(w, n_prompt, -1, s, "vella_whisper_decode_batch");
+  int rc = decode_args(w, n_prompt, eot, s, what);
   if (rc) return rc;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev0, s));
   // the prompts of all streams in one forward (stream st: rows st * n_prompt .., positions
@@ -1189,20 +1198,67 @@ int vella_whisper_decode_batch(vella_whisper* w, const int32_t* prompt, int32_t 
   if (rc) return rc;
   if ((rc = commit(w, n_prompt, n_prompt - 1, s))) return rc;
   VELLA_CUDA_TRY(cudaEventRecord(w->ev1, s));
-  for (int i = 1; i < max_tokens; ++i)
-    if ((rc = run_step(w))) return rc;
+  std::vector<int> stop_at(S, -1);  // index of each stream's first end-of-text
+  int produced = 1, checked = 0, open = S;
+  for (;;) {
+    const int burst = eot >= 0 ? std::min(kStopBurst, max_tokens - produced) : max_tokens - produced;
+    for (int i = 0; i < burst; ++i)
+      if ((rc = run_step(w))) return rc;
+    produced += burst;
+    if (eot < 0) break;
+    const int n = produced - checked;
+    VELLA_CUDA_TRY(cudaMemcpy2DAsync(toks.data() + n_prompt + checked, c.max_target * sizeof(int),
+                                     w->tok + n_prompt + checked, c.max_target * sizeof(int), n * sizeof(int), S,
+                                     cudaMemcpyDeviceToHost, s));
+    VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+    for (int st = 0; st < S; ++st)
+      for (int i = checked; i < produced && stop_at[st] < 0; ++i)
+        if (toks[(size_t)st * c.max_target + n_prompt + i] == eot) {
+          stop_at[st] = i;
+          --open;
+        }
+    checked = produced;
+    if (open == 0 || produced == max_tokens) break;
+  }
   VELLA_CUDA_TRY(cudaEventRecord(w->ev2, s));
-  VELLA_CUDA_TRY(cudaMemcpyAsync(toks.data(), w->tok, toks.size() * sizeof(int), cudaMemcpyDeviceToHost, s));
+  if (eot < 0)
+    VELLA_CUDA_TRY(cudaMemcpyAsync(toks.data(), w->tok, toks.size() * sizeof(int), cudaMemcpyDeviceToHost, s));
   VELLA_CUDA_TRY(cudaStreamSynchronize(s));
   cudaEventElapsedTime(&w->stats.prefill_ms, w->ev0, w->ev1);
   cudaEventElapsedTime(&w->stats.decode_ms, w->ev1, w->ev2);
   w->stats.sum_logprob = 0.0f;
   if (w->rules_on) VELLA_CUDA_TRY(cudaMemcpy(&w->stats.sum_logprob, w->lpsum, sizeof(float), cudaMemcpyDeviceToHost));
-  if ((rc = check_flags(w, "vella_whisper_decode_batch"))) return rc;
-  for (int st = 0; st < S; ++st)
-    std::copy(toks.begin() + (size_t)st * c.max_target + n_prompt,
-              toks.begin() + (size_t)st * c.max_target + n_prompt + max_tokens, out_tokens + (size_t)st * max_tokens);
-  w->stats.tokens = S * max_tokens;
+  if ((rc = check_flags(w, what))) return rc;
+  int total = 0;
+  for (int st = 0; st < S; ++st) {
+    const int keep = stop_at[st] >= 0 ? stop_at[st] : produced;
+    const int* src = toks.data() + (size_t)st * c.max_target + n_prompt;
+    int32_t* dst = out_tokens + (size_t)st * max_tokens;
+    for (int i = 0; i < max_tokens; ++i) dst[i] = i < keep ? src[i] : -1;
+    if (n_out) n_out[st] = keep;
+    total += keep;
+  }
+  w->stats.tokens = total;
+  return VELLA_OK;
+}
+
+int vella_whisper_decode_batch(vella_whisper* w, const int32_t* prompt, int32_t n_prompt, int32_t max_tokens,
+                               int32_t* out_tokens) {
+  return decode_batch_impl(w, prompt, n_prompt, max_tokens, -1, out_tokens, nullptr, "vella_whisper_decode_batch");
+}
+
+int vella_whisper_decode_batch_eot(vella_whisper* w, const int32_t* prompt, int32_t n_prompt, int32_t max_tokens,
+                                   int32_t eot, int32_t* out_tokens, int32_t* n_out) {
+  if (!n_out) return fail(VELLA_E_INVALID, "vella_whisper_decode_batch_eot: NULL n_out");
+  return decode_batch_impl(w, prompt, n_prompt, max_tokens, eot, out_tokens, n_out, "vella_whisper_decode_batch_eot");
+}
+
+int vella_whisper_get_logprobs(const vella_whisper* w, float* out, int32_t n) {
+  if (!w || (n > 0 && !out)) return fail(VELLA_E_INVALID, "vella_whisper_get_logprobs: NULL argument");
+  if (n < 0 || n > w->S) return fail(VELLA_E_INVALID, "vella_whisper_get_logprobs: %d of %d streams", n, w->S);
+  VELLA_CUDA_TRY(cudaSetDevice(w->device));
+  VELLA_CUDA_TRY(cudaStreamSynchronize(w->stream));
+  if (n > 0) VELLA_CUDA_TRY(cudaMemcpy(out, w->lpsum, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost));
   return VELLA_OK;
 }
 

@@ -99,6 +99,8 @@ for _name, _res, _args in [
     ("vella_whisper_log_mel", ctypes.c_int, [_vp, ctypes.c_int64, _i32, _i32, _vp, _vp]),
     ("vella_whisper_decode", ctypes.c_int, [_vp, _pi32, _i32, _i32, _i32, _pi32, _pi32]),
     ("vella_whisper_decode_batch", ctypes.c_int, [_vp, _pi32, _i32, _i32, _pi32]),
+    ("vella_whisper_decode_batch_eot", ctypes.c_int, [_vp, _pi32, _i32, _i32, _i32, _pi32, _pi32]),
+    ("vella_whisper_get_logprobs", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_float), _i32]),
     ("vella_whisper_score", ctypes.c_int, [_vp, _pi32, _i32, _vp, _i32]),
     ("vella_whisper_get_stats", ctypes.c_int, [_vp, ctypes.POINTER(WhisperStats)]),
     ("vella_whisper_set_rules", ctypes.c_int, [_vp, ctypes.POINTER(WhisperRules)]),
@@ -198,14 +200,27 @@ class Whisper:
         st = self.stats()
         return DecodeResult(list(out[: n.value]), st["prefill_ms"], st["decode_ms"])
 
-    def decode_batch(self, prompt: Sequence[int], max_tokens: int) -> np.ndarray:
-        """Greedy tokens [streams, max_tokens] of every stream after the same prompt."""
+    def decode_batch(self, prompt: Sequence[int], max_tokens: int, eot: int = -1):
+        """Tokens of every stream after the same prompt: [streams, max_tokens] without an
+        end-of-text id, else one list per stream of its tokens before ``eot``."""
         S = max(self.cfg.streams, 1)
         pr = (ctypes.c_int32 * len(prompt))(*prompt)
         out = np.zeros((S, max(max_tokens, 1)), np.int32)
-        _lib.check(_lib.lib().vella_whisper_decode_batch(self.h, pr, len(prompt), max_tokens,
-                                                         out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))))
-        return out[:, :max_tokens]
+        optr = out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))
+        if eot < 0:
+            _lib.check(_lib.lib().vella_whisper_decode_batch(self.h, pr, len(prompt), max_tokens, optr))
+            return out[:, :max_tokens]
+        n = np.zeros(S, np.int32)
+        _lib.check(_lib.lib().vella_whisper_decode_batch_eot(self.h, pr, len(prompt), max_tokens, eot, optr,
+                                                             n.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))))
+        return [list(out[st, :n[st]]) for st in range(S)]
+
+    def logprobs(self) -> np.ndarray:
+        """Each stream's summed log-probability over the last decode (token rules set)."""
+        S = max(self.cfg.streams, 1)
+        out = np.zeros(S, np.float32)
+        _lib.check(_lib.lib().vella_whisper_get_logprobs(self.h, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), S))
+        return out
 
     def set_rules(self, eot: Optional[int] = None, no_timestamps: int = 0, timestamp_begin: int = 0,
                   suppress: Sequence[int] = (), begin_suppress: Sequence[int] = ()):
