@@ -5,7 +5,10 @@
  * Every entry point is `extern "C"`, takes plain pointers and sizes, and returns a status
  * code.  Device pointers are caller-owned CUDA device memory on the current device;
  * `vella_stream_t` is a `cudaStream_t` (NULL = the legacy default stream).  Calls are
- * asynchronous on the stream unless stated otherwise.  On any status other than VELLA_OK
+ * asynchronous on the stream unless stated otherwise.  The handle entry points (vella_spec_*,
+ * vella_model_*, vella_whisper_*) work on the handle's own non-blocking stream and return when
+ * their work is done; that stream does not wait for other streams, so device inputs passed to
+ * them must be complete when the call is made.  On any status other than VELLA_OK
  * `vella_last_error` returns a message for the calling thread.
  *
  * Reference interfaces replaced (paths inside the Vella repository):

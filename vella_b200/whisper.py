@@ -177,6 +177,10 @@ class Whisper:
             assert m.shape[-2:] == shape and m.size == max(self.cfg.streams, 1) * shape[0] * shape[1], m.shape
             _lib.check(_lib.lib().vella_whisper_encode(self.h, m.ctypes.data, 1))
         else:
+            if not isinstance(mel, int) and getattr(mel, "is_cuda", False):
+                import torch
+                # the handle's stream does not wait for torch's: the features must be complete
+                torch.cuda.current_stream(mel.device).synchronize()
             ptr = mel if isinstance(mel, int) else mel.data_ptr()
             _lib.check(_lib.lib().vella_whisper_encode(self.h, ptr, 0 if on_host is None else int(on_host)))
 
@@ -186,8 +190,8 @@ class Whisper:
         import torch
         if isinstance(audio, torch.Tensor) and audio.is_cuda:
             a = audio.float().contiguous()
+            torch.cuda.current_stream(a.device).synchronize()  # the handle's stream does not wait for torch's
             _lib.check(_lib.lib().vella_whisper_encode_audio(self.h, a.data_ptr(), a.shape[-1], 0))
-            torch.cuda.current_stream().synchronize()
             return
         a = np.ascontiguousarray(np.asarray(audio, np.float32))
         _lib.check(_lib.lib().vella_whisper_encode_audio(self.h, a.ctypes.data, a.shape[-1], 1))
