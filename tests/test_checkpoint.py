@@ -76,7 +76,7 @@ def test_later_shards_replace_earlier_keys(tmp_path):
         assert st.array("y").shape == (3,)
 
 
-@pytest.mark.parametrize("case", ["truncated", "bad_json", "offsets", "dtype", "short_data", "missing"])
+@pytest.mark.parametrize("case", ["truncated", "bad_json", "offsets", "dtype", "short_data", "missing", "overflow"])
 def test_malformed_files_are_rejected(tmp_path, case):
     from vella_b200 import _lib
     p = tmp_path / "bad.safetensors"
@@ -93,6 +93,8 @@ def test_malformed_files_are_rejected(tmp_path, case):
             offs = [0, 12]
         if case == "dtype":
             dt = "Q7"
+        if case == "overflow":  # 2**62 elements * 4 bytes wraps to 0 bytes in 64 bits
+            shape, offs = [2**62], [0, 0]
         body = 8 if case != "short_data" else 4
         h = json.dumps({"x": {"dtype": dt, "shape": shape, "data_offsets": offs}}).encode()
         p.write_bytes(struct.pack("<Q", len(h)) + h + b"\0" * body)
@@ -631,3 +633,53 @@ def test_loaded_models_equal_their_source_and_derive_int4(tmp_path):
     m.close()
     fsrc.close()
     src.close()
+
+
+def test_corrupted_files_are_rejected_without_crashing(tmp_path):
+    """Random byte flips, truncations and header rewrites of a valid file, opened in a child
+    process: each open either succeeds or raises VellaError (no crash, no hang)."""
+    import subprocess
+    import sys
+    rng = np.random.default_rng(11)
+    good = tmp_path / "good.safetensors"
+    write_safetensors(good, {"a": np.arange(12, dtype=np.float32).reshape(3, 4), "b": np.ones(5, np.float16),
+                             "c": np.zeros((2, 2), np.uint32)}, metadata={"k": "v"})
+    raw = good.read_bytes()
+    hlen = struct.unpack("<Q", raw[:8])[0]
+    cases = []
+    for i in range(60):
+        b = bytearray(raw)
+        kind = i % 4
+        if kind == 0:  # flip bytes inside the JSON header
+            for _ in range(rng.integers(1, 6)):
+                j = int(rng.integers(8, 8 + hlen))
+                b[j] = int(rng.integers(0, 256))
+        elif kind == 1:  # truncate anywhere
+            b = b[:int(rng.integers(0, len(b)))]
+        elif kind == 2:  # a wrong header length
+            b[:8] = struct.pack("<Q", int(rng.integers(0, 2 * len(b))))
+        else:  # a header with extreme or negative numbers
+            h = json.dumps({"x": {"dtype": "F32", "shape": [int(rng.integers(-5, 2**62))],
+                                  "data_offsets": [int(rng.integers(-10, 100)), int(rng.integers(-10, 2**62))]}})
+            hb = h.encode()
+            b = bytearray(struct.pack("<Q", len(hb)) + hb + bytes(16))
+        p = tmp_path / f"case{i}.safetensors"
+        p.write_bytes(bytes(b))
+        cases.append(str(p))
+    code = (
+        "import sys\n"
+        "from vella_b200 import _lib, checkpoint as C\n"
+        "ok = bad = 0\n"
+        "for p in sys.argv[1:]:\n"
+        "    try:\n"
+        "        st = C.SafeTensors([p]); [st.array(k) for k in st.keys()]; st.close(); ok += 1\n"
+        "    except _lib.VellaError:\n"
+        "        bad += 1\n"
+        "print(ok, bad)\n")
+    import os
+    root = str(__import__("pathlib").Path(__file__).resolve().parents[1])
+    r = subprocess.run([sys.executable, "-c", code, *cases], capture_output=True, text=True, timeout=120,
+                       cwd=root, env={**os.environ, "PYTHONPATH": root})
+    assert r.returncode == 0, r.stderr[-2000:]
+    ok, bad = map(int, r.stdout.split())
+    assert ok + bad == len(cases) and bad > 0

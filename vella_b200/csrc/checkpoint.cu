@@ -324,8 +324,15 @@ int st_add_file(vella_st* st, const char* path) {
       if (d.kind != JVal::Int || d.i < 0) return fail(VELLA_E_INVALID, "vella_st_open: '%s': bad shape", kv.first.c_str());
       e.shape.push_back(d.i);
     }
+    // the element count times the element size must not overflow (a huge shape over a few bytes)
+    unsigned long long n = (unsigned long long)e.esize;
+    bool overflow = false;
+    for (int64_t d : e.shape) {
+      if (d != 0 && n > ~0ull / (unsigned long long)d) overflow = true;
+      n *= (unsigned long long)d;
+    }
     const long long lo = off->arr[0].i, hi = off->arr[1].i;
-    if (lo < 0 || hi < lo || (unsigned long long)hi > dsize || (size_t)(hi - lo) != e.numel() * (size_t)e.esize)
+    if (overflow || lo < 0 || hi < lo || (unsigned long long)hi > dsize || (unsigned long long)(hi - lo) != n)
       return fail(VELLA_E_INVALID, "vella_st_open: '%s': tensor '%s' offsets [%lld, %lld) do not fit its shape or the file",
                   path, kv.first.c_str(), lo, hi);
     e.data = data + lo;
