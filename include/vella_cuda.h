@@ -492,6 +492,41 @@ VELLA_API int vella_whisper_load(vella_whisper* w, const vella_st* st);
 VELLA_API int vella_model_check_checkpoint(const vella_st* st, const vella_model_cfg* cfg);
 VELLA_API int vella_model_load(vella_model* model, const vella_st* st);
 
+/* ---- Nemotron-H Mamba-2 mixer core ------------------------------------------------------
+ *
+ * Replaces NTMamba's conv, SSM and gated norm (Worker/Sources/MLXAudioSTT/NemotronTranscribe/
+ * NemotronTranscribeDecoder.swift:126-360: nt_ssm_kernel, nt_ssm_initial_kernel, ntSSMAttn,
+ * ntComputeDt, NTGatedRMSNorm).  Rows are stream-major (row s * tokens + t).  `zxbcdt` is the
+ * in_proj output, rows of in_stride elements: gate [0, I), conv input [I, I + convDim), dt
+ * [I + convDim, I + convDim + heads), I = heads * head_dim, convDim = I + 2 * groups *
+ * state_dim.  Device pointers, asynchronous on `stream`; the in_proj / out_proj GEMMs are
+ * vella_qgemm calls.
+ */
+typedef struct vella_mamba_desc {
+  int32_t streams, tokens;  /* S sequences, T new positions each (1: decode step; more: chunk)  */
+  int32_t heads, head_dim;  /* mamba_num_heads, mamba_head_dim                                  */
+  int32_t groups;           /* n_groups (divides heads)                                         */
+  int32_t state_dim;        /* ssm_state_size: a multiple of 32, at most 256                    */
+  int32_t conv_kernel;      /* conv_kernel (1..8)                                               */
+  int32_t dtype;            /* VELLA_BF16 | VELLA_F16 (activations, conv weight and state)      */
+  int32_t in_stride;        /* elements between rows of zxbcdt (>= I + convDim + heads)         */
+  float dt_min, dt_max;     /* time_step_limit                                                  */
+  float eps;                /* layer_norm_epsilon of the gated norm                             */
+} vella_mamba_desc;
+/* xbc [S*T][convDim] = silu(causal depthwise conv over conv_state [S][K-1][convDim] then the T
+ * conv inputs; conv_w [convDim][K], conv_b [convDim] or NULL); conv_state keeps the last K-1
+ * conv inputs. */
+VELLA_API int vella_mamba_conv(const vella_mamba_desc* desc, const void* zxbcdt, const void* conv_w,
+                               const void* conv_b, void* conv_state, void* xbc, vella_stream_t stream);
+/* y [S*T][I]: per head h (group h / (heads / groups)) and channel d, for each row in order,
+ * dt = clip(softplus(dt_raw + dt_bias[h]), dt_min, dt_max), state = exp(-exp(a_log[h]) dt)
+ * state + x dt B, y = state . C + x D[h]; ssm_state [S][H][Dh][Ds] fp32, read and written. */
+VELLA_API int vella_mamba_ssm(const vella_mamba_desc* desc, const void* xbc, const void* zxbcdt, const float* a_log,
+                              const float* dt_bias, const float* D, float* ssm_state, void* y, vella_stream_t stream);
+/* out [S*T][I] = rms_norm(y * silu(gate)) over groups of I / groups channels, times norm_w [I]. */
+VELLA_API int vella_mamba_gated_norm(const vella_mamba_desc* desc, const void* y, const void* zxbcdt,
+                                     const void* norm_w, void* out, vella_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

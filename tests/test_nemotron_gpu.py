@@ -1,0 +1,101 @@
+"""Parity of the Mamba-2 mixer kernels (vella_mamba_* through the C ABI) with the oracle,
+each stage fed the device's own output of the stage before, so errors do not compound.
+
+Bars: conv output and gated norm within 2e-2 absolute (bf16 storage of O(1) values); the scan's
+output within 2e-2 of the oracle's and its fp32 state within 1e-4 relative; a 5-token chunk
+gives, bit for bit, the outputs and states of 5 one-token calls.
+"""
+import numpy as np
+import pytest
+
+from oracle import nemotron as N
+
+pytestmark = pytest.mark.gpu_pending
+
+
+def _bf16(t):
+    return t.float().cpu().numpy().astype(np.float64)
+
+
+def _setup(S, T, seed=0):
+    import torch
+
+    from vella_b200 import nemotron as VN
+    sh = VN.MambaShape(heads=8, head_dim=64, groups=2, state_dim=128, conv_kernel=4, dt_min=1e-3, dt_max=10.0)
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    dev = "cuda"
+    zx = (torch.randn(S * T, sh.in_width, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    conv_w = (torch.randn(sh.conv_dim, sh.conv_kernel, generator=g, device=dev) * 0.4).to(torch.bfloat16)
+    conv_b = (torch.randn(sh.conv_dim, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    cstate = (torch.randn(S, sh.conv_kernel - 1, sh.conv_dim, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    a_log = torch.randn(sh.heads, generator=g, device=dev) * 0.5
+    dt_bias = torch.randn(sh.heads, generator=g, device=dev) * 0.5
+    D = torch.randn(sh.heads, generator=g, device=dev)
+    state = torch.randn(S, sh.heads, sh.head_dim, sh.state_dim, generator=g, device=dev) * 0.1
+    norm_w = (1.0 + 0.1 * torch.randn(sh.inner, generator=g, device=dev)).to(torch.bfloat16)
+    return sh, zx, conv_w, conv_b, cstate, a_log, dt_bias, D, state, norm_w
+
+
+@pytest.mark.parametrize("S,T", [(1, 1), (2, 5), (3, 9)])
+def test_mixer_stages_match_the_oracle(S, T):
+    import torch
+
+    from vella_b200 import nemotron as VN
+    sh, zx, conv_w, conv_b, cstate, a_log, dt_bias, D, state, norm_w = _setup(S, T)
+    I, H, Dh, G, Ds = sh.inner, sh.heads, sh.head_dim, sh.groups, sh.state_dim
+    cs0, st0 = _bf16(cstate), state.double().cpu().numpy()
+    xbc = torch.empty(S * T, sh.conv_dim, dtype=torch.bfloat16, device="cuda")
+    VN.conv(sh, zx, conv_w, conv_b, cstate, xbc, S, T)
+    y = torch.empty(S * T, I, dtype=torch.bfloat16, device="cuda")
+    VN.ssm(sh, xbc, zx, a_log, dt_bias, D, state, y, S, T)
+    out = torch.empty_like(y)
+    VN.gated_norm(sh, y, zx, norm_w, out, S, T)
+    torch.cuda.synchronize()
+    z = _bf16(zx).reshape(S, T, -1)
+    xg, yg = _bf16(xbc).reshape(S, T, -1), _bf16(y).reshape(S, T, -1)
+    for s in range(S):
+        ref_x, ref_cs = N.conv_step(z[s][:, I:I + sh.conv_dim], _bf16(conv_w), _bf16(conv_b), cs0[s])
+        assert np.abs(xg[s] - ref_x).max() <= 2e-2
+        assert np.array_equal(_bf16(cstate)[s], ref_cs.astype(np.float32).astype(np.float64))
+        x, B, C = N.split_xbc(xg[s], H, Dh, G, Ds)
+        dt = N.compute_dt(z[s][:, I + sh.conv_dim:], dt_bias.cpu().numpy(), 1e-3, 10.0)
+        ref_y, ref_st = N.ssm_scan(x, B, C, dt, a_log.cpu().numpy(), D.cpu().numpy(), st0[s])
+        assert np.abs(yg[s] - ref_y.reshape(T, -1)).max() <= 2e-2 * max(1.0, np.abs(ref_y).max())
+        st = state[s].double().cpu().numpy()
+        assert np.abs(st - ref_st).max() <= 1e-4 * max(1.0, np.abs(ref_st).max())
+        ref_o = N.gated_rmsnorm(yg[s], z[s][:, :I], _bf16(norm_w), G, sh.eps)
+        assert np.abs(_bf16(out).reshape(S, T, -1)[s] - ref_o).max() <= 2e-2 * max(1.0, np.abs(ref_o).max())
+
+
+def test_a_chunk_equals_one_token_steps():
+    import torch
+
+    from vella_b200 import nemotron as VN
+    S, T = 2, 5
+    sh, zx, conv_w, conv_b, cstate, a_log, dt_bias, D, state, norm_w = _setup(S, T, seed=3)
+    cs_a, st_a = cstate.clone(), state.clone()
+    xbc = torch.empty(S * T, sh.conv_dim, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(S * T, sh.inner, dtype=torch.bfloat16, device="cuda")
+    VN.conv(sh, zx, conv_w, conv_b, cs_a, xbc, S, T)
+    VN.ssm(sh, xbc, zx, a_log, dt_bias, D, st_a, y, S, T)
+    cs_b, st_b = cstate.clone(), state.clone()
+    zr = zx.view(S, T, -1)
+    for t in range(T):
+        z1 = zr[:, t].contiguous()
+        x1 = torch.empty(S, sh.conv_dim, dtype=torch.bfloat16, device="cuda")
+        y1 = torch.empty(S, sh.inner, dtype=torch.bfloat16, device="cuda")
+        VN.conv(sh, z1, conv_w, conv_b, cs_b, x1, S, 1)
+        VN.ssm(sh, x1, z1, a_log, dt_bias, D, st_b, y1, S, 1)
+        assert torch.equal(x1, xbc.view(S, T, -1)[:, t]) and torch.equal(y1, y.view(S, T, -1)[:, t]), t
+    assert torch.equal(cs_a, cs_b) and torch.equal(st_a, st_b)
+
+
+def test_bad_descriptors_are_rejected():
+    import torch
+
+    from vella_b200 import _lib
+    from vella_b200 import nemotron as VN
+    sh = VN.MambaShape(heads=8, head_dim=64, groups=3, state_dim=100)
+    t = torch.zeros(4, 4096, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.VellaError):
+        VN.conv(sh, t, t, None, t, t, 1, 1)

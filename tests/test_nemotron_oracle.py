@@ -1,0 +1,71 @@
+"""The Mamba-2 mixer oracle against itself and the reference's forms (CPU only): the chunked
+causal conv equals token-by-token steps, the sequential scan equals the reference's SSD chunk
+form with a carried state, one-token steps equal a chunk, and the gated norm normalises
+per group."""
+import numpy as np
+
+from oracle import nemotron as N
+
+
+def _rand(rng, *shape, scale=1.0):
+    return rng.standard_normal(shape) * scale
+
+
+def test_conv_chunk_equals_steps():
+    rng = np.random.default_rng(0)
+    C, K, T = 24, 4, 7
+    w, b = _rand(rng, C, K), _rand(rng, C)
+    x, st = _rand(rng, T, C), _rand(rng, K - 1, C)
+    out, st_chunk = N.conv_step(x, w, b, st)
+    s = st.copy()
+    for t in range(T):
+        o, s = N.conv_step(x[t:t + 1], w, b, s)
+        assert np.allclose(o[0], out[t])
+    assert np.allclose(s, st_chunk) and np.allclose(st_chunk, x[-(K - 1):])
+
+
+def test_scan_equals_ssd_with_a_carried_state():
+    rng = np.random.default_rng(1)
+    T, H, Dh, G, Ds = 9, 8, 6, 2, 16
+    x = _rand(rng, T, H, Dh)
+    B, Cm = _rand(rng, T, G, Ds), _rand(rng, T, G, Ds)
+    dt = N.compute_dt(_rand(rng, T, H), _rand(rng, H), 1e-3, 10.0)
+    a_log, D = _rand(rng, H, scale=0.5), _rand(rng, H)
+    st0 = _rand(rng, H, Dh, Ds)
+    y1, s1 = N.ssm_scan(x, B, Cm, dt, a_log, D, st0)
+    y2, s2 = N.ssm_ssd(x, B, Cm, dt, a_log, D, st0)
+    assert np.allclose(y1, y2, rtol=1e-10, atol=1e-10) and np.allclose(s1, s2, rtol=1e-10, atol=1e-10)
+    # one token at a time (the step kernel) gives the same as the chunk
+    s = st0
+    for t in range(T):
+        y, s = N.ssm_scan(x[t:t + 1], B[t:t + 1], Cm[t:t + 1], dt[t:t + 1], a_log, D, s)
+        assert np.allclose(y[0], y1[t])
+    assert np.allclose(s, s1)
+
+
+def test_dt_is_clipped_softplus():
+    dt = N.compute_dt(np.array([[-50.0, 0.0, 50.0]]), np.zeros(3), 0.01, 5.0)
+    assert np.allclose(dt, [[0.01, np.log(2.0), 5.0]])
+
+
+def test_gated_norm_normalises_each_group():
+    rng = np.random.default_rng(2)
+    y, g = _rand(rng, 3, 32), _rand(rng, 3, 32)
+    out = N.gated_rmsnorm(y, g, np.ones(32), groups=4, eps=1e-12).reshape(3, 4, 8)
+    assert np.allclose((out * out).mean(axis=-1), 1.0)
+
+
+def test_mixer_state_carries_across_calls():
+    rng = np.random.default_rng(3)
+    H, Dh, G, Ds, K = 4, 8, 2, 32, 4
+    I = H * Dh
+    conv_dim = I + 2 * G * Ds
+    args = dict(H=H, Dh=Dh, G=G, Ds=Ds, lo=0.0, hi=float("inf"), eps=1e-5)
+    params = (_rand(rng, conv_dim, K, scale=0.3), _rand(rng, conv_dim, scale=0.1), _rand(rng, H, scale=0.3),
+              _rand(rng, H, scale=0.3), _rand(rng, H), 1.0 + _rand(rng, I, scale=0.1))
+    z = _rand(rng, 6, I + conv_dim + H)
+    cs0, ss0 = np.zeros((K - 1, conv_dim)), np.zeros((H, Dh, Ds))
+    full, cs_f, ss_f = N.mixer(z, *params, cs0, ss0, **args)
+    a, cs, ss = N.mixer(z[:4], *params, cs0, ss0, **args)
+    b, cs, ss = N.mixer(z[4:], *params, cs, ss, **args)
+    assert np.allclose(np.concatenate([a, b]), full) and np.allclose(ss, ss_f) and np.allclose(cs, cs_f)

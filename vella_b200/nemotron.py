@@ -1,0 +1,85 @@
+"""ctypes binding of the Nemotron-H Mamba-2 mixer core (``vella_mamba_*`` in
+``include/vella_cuda.h``), over torch tensors on the device.
+
+Names follow the reference's ``NTMamba`` (``Worker/Sources/MLXAudioSTT/NemotronTranscribe/
+NemotronTranscribeDecoder.swift:318-360``): ``conv`` is the cached causal conv with SiLU,
+``ssm`` the selective scan with its fp32 state, ``gated_norm`` NTGatedRMSNorm.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+from . import _lib
+
+
+class MambaDesc(ctypes.Structure):
+    _fields_ = [("streams", ctypes.c_int32), ("tokens", ctypes.c_int32), ("heads", ctypes.c_int32),
+                ("head_dim", ctypes.c_int32), ("groups", ctypes.c_int32), ("state_dim", ctypes.c_int32),
+                ("conv_kernel", ctypes.c_int32), ("dtype", ctypes.c_int32), ("in_stride", ctypes.c_int32),
+                ("dt_min", ctypes.c_float), ("dt_max", ctypes.c_float), ("eps", ctypes.c_float)]
+
+
+_vp = ctypes.c_void_p
+for _name, _args in [
+    ("vella_mamba_conv", [ctypes.POINTER(MambaDesc), _vp, _vp, _vp, _vp, _vp, _vp]),
+    ("vella_mamba_ssm", [ctypes.POINTER(MambaDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    ("vella_mamba_gated_norm", [ctypes.POINTER(MambaDesc), _vp, _vp, _vp, _vp, _vp]),
+]:
+    _lib.declare(_name, ctypes.c_int, _args)
+
+
+@dataclass
+class MambaShape:
+    heads: int
+    head_dim: int
+    groups: int
+    state_dim: int
+    conv_kernel: int = 4
+    dt_min: float = 0.0
+    dt_max: float = float("inf")
+    eps: float = 1e-5
+    dtype: int = _lib.BF16
+
+    @property
+    def inner(self) -> int:
+        return self.heads * self.head_dim
+
+    @property
+    def conv_dim(self) -> int:
+        return self.inner + 2 * self.groups * self.state_dim
+
+    @property
+    def in_width(self) -> int:
+        return self.inner + self.conv_dim + self.heads
+
+    def desc(self, streams: int, tokens: int, in_stride: int = 0) -> MambaDesc:
+        return MambaDesc(streams, tokens, self.heads, self.head_dim, self.groups, self.state_dim, self.conv_kernel,
+                         self.dtype, in_stride or self.in_width, self.dt_min, self.dt_max, self.eps)
+
+
+def _stream():
+    import torch
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def conv(shape: MambaShape, zxbcdt, conv_w, conv_b, conv_state, xbc, streams: int, tokens: int):
+    d = shape.desc(streams, tokens, zxbcdt.stride(0))
+    _lib.check(_lib.lib().vella_mamba_conv(ctypes.byref(d), _p(zxbcdt), _p(conv_w), _p(conv_b), _p(conv_state),
+                                           _p(xbc), _stream()))
+
+
+def ssm(shape: MambaShape, xbc, zxbcdt, a_log, dt_bias, D, state, y, streams: int, tokens: int):
+    d = shape.desc(streams, tokens, zxbcdt.stride(0))
+    _lib.check(_lib.lib().vella_mamba_ssm(ctypes.byref(d), _p(xbc), _p(zxbcdt), _p(a_log), _p(dt_bias), _p(D),
+                                          _p(state), _p(y), _stream()))
+
+
+def gated_norm(shape: MambaShape, y, zxbcdt, norm_w, out, streams: int, tokens: int):
+    d = shape.desc(streams, tokens, zxbcdt.stride(0))
+    _lib.check(_lib.lib().vella_mamba_gated_norm(ctypes.byref(d), _p(y), _p(zxbcdt), _p(norm_w), _p(out),
+                                                 _stream()))
