@@ -197,3 +197,46 @@ def test_log_mel_properties():
     # trimming: samples past 30 s change nothing
     long = np.concatenate([tone, np.zeros(480000), np.ones(1000)])
     assert np.array_equal(Wh.log_mel(long, 80), Wh.log_mel(np.concatenate([tone, np.zeros(480000)])[:480000], 80))
+
+
+class _FakeWhisperHandle:
+    """encode_audio / decode_with_fallback of a Whisper handle, scripted per window."""
+
+    def __init__(self, results):
+        from vella_b200.whisper import WhisperConfig
+        self.cfg = WhisperConfig()
+        self.results, self.encoded, self.calls = list(results), [], []
+
+    def encode_audio(self, audio):
+        self.encoded.append(np.asarray(audio).copy())
+
+    def decode_with_fallback(self, prompt, max_tokens, eot, detokenize, temps, seed, no_speech_prob, draw_base=0):
+        self.calls.append((list(prompt), max_tokens, eot, tuple(temps), seed, no_speech_prob, draw_base))
+        return self.results.pop(0)
+
+
+def test_generate_windows_prompt_and_text():
+    from vella_b200 import whisper as VW
+    from vella_b200.checkpoint import WhisperTokens
+    tok = WhisperTokens(sot=50258, eot=50257, no_timestamps=50364, timestamp_begin=50365, transcribe=50360,
+                        languages={"en": 50259}, multilingual=True)
+    mk = lambda t: VW.FallbackResult(t, 0.0, -1.0, -0.5, 1.0, 1, "accept")  # noqa: E731
+    fake = _FakeWhisperHandle([mk([1, 2]), mk([]), mk([7])])
+    words = {1: "hello", 2: " world", 7: " again "}
+    stt = VW.WhisperSTT(fake, tok, lambda ts: "".join(words[t] for t in ts), seed=9)
+    stereo = np.random.default_rng(0).standard_normal((16000 * 65, 2)).astype(np.float32)
+    out = stt.generate(stereo, language="en", max_tokens=1024)
+    # 65 s: windows of 30, 30 and 5 s, each the channel mean
+    assert [e.shape[0] for e in fake.encoded] == [480000, 480000, 80000]
+    assert np.allclose(fake.encoded[2], stereo[960000:].mean(axis=1))
+    assert all(c[0] == [50258, 50259, 50360] for c in fake.calls)
+    assert fake.calls[0][1] == 224 and fake.calls[0][3] == VW.FALLBACK_TEMPERATURES  # n_text_ctx / 2
+    assert [c[6] for c in fake.calls] == [0, 6, 12] and all(c[4] == 9 for c in fake.calls)
+    assert out.text == "hello world again"
+    assert out.segments == [{"text": "hello world", "start": 0.0, "end": 30.0},
+                            {"text": "again", "start": 60.0, "end": 65.0}]
+    assert (out.prompt_tokens, out.generation_tokens, out.total_tokens) == (9, 3, 12)
+    # a fixed temperature is the only attempt
+    fake = _FakeWhisperHandle([mk([1])])
+    VW.WhisperSTT(fake, tok, lambda ts: "x").generate(np.zeros(1000, np.float32), temperature=0.4)
+    assert fake.calls[0][3] == (0.4,)

@@ -248,19 +248,20 @@ class Whisper:
     def decode_with_fallback(self, prompt: Sequence[int], max_tokens: int, eot: int,
                              detokenize: Optional[Callable[[List[int]], str]] = None,
                              temperatures: Sequence[float] = FALLBACK_TEMPERATURES, seed: int = 0x5EED,
-                             no_speech_prob: float = 0.0) -> FallbackResult:
+                             no_speech_prob: float = 0.0, draw_base: int = 0) -> FallbackResult:
         """The reference's temperature fallback for one window (``transcribeChunk``,
         WhisperModel.swift:218-292): attempts at 0, 0.2, .. 1.0 until the average
         log-probability (end-of-text step counted) is >= -1 and the compression ratio of
         ``detokenize(tokens)`` is <= 2.4; an attempt whose average is < -1 while
         ``no_speech_prob`` > 0.6 gives an empty window; if every attempt asks for a retry the
-        last one stands.  Token rules must be set.  Attempt i draws with counter word i.
+        last one stands.  Token rules must be set.  Attempt i draws with counter word
+        draw_base + i.
         Without ``detokenize`` the compression test passes (ratio 0, the reference's value for
         empty text)."""
         res = None
         try:
             for i, temp in enumerate(temperatures):
-                self.set_sampling(temp, seed, i)
+                self.set_sampling(temp, seed, draw_base + i)
                 out = self.decode(prompt, max_tokens, eot)
                 lp = float(self.stats()["sum_logprob"])
                 text = detokenize(out.tokens) if detokenize is not None else ""
@@ -288,3 +289,76 @@ class Whisper:
         s = WhisperStats()
         _lib.check(_lib.lib().vella_whisper_get_stats(self.h, ctypes.byref(s)))
         return {f: getattr(s, f) for f, _ in WhisperStats._fields_}
+
+
+# ---------------------------------------------------------------------------------------
+# The plugin boundary: generate(audio:) of the reference's STTGenerationModel
+# ---------------------------------------------------------------------------------------
+
+SAMPLE_RATE, WINDOW_SAMPLES = 16000, 480000  # WhisperAudioConfig: 16 kHz, 30 s windows
+
+
+@dataclass
+class STTOutput:
+    """The fields of the reference's STTOutput (Shared/STTOutput.swift:34-88) this path fills."""
+    text: str
+    segments: Optional[List[dict]]
+    language: Optional[str]
+    prompt_tokens: int
+    generation_tokens: int
+    total_tokens: int
+    prompt_tps: float
+    generation_tps: float
+    total_time: float
+
+
+def chunk_audio(audio: np.ndarray) -> List[tuple]:
+    """``chunkAudioFor30sWindows`` (WhisperModel.swift:150-166): consecutive 30 s windows, the
+    last one shorter; (samples, offset in seconds) each."""
+    n = audio.shape[0]
+    if n <= WINDOW_SAMPLES:
+        return [(audio, 0.0)]
+    return [(audio[i:min(n, i + WINDOW_SAMPLES)], i / SAMPLE_RATE) for i in range(0, n, WINDOW_SAMPLES)]
+
+
+class WhisperSTT:
+    """``WhisperModel.generate(audio:generationParameters:)`` (WhisperModel.swift:84-140) over a
+    one-stream handle with its token rules set: mono mix-down, 30 s windows, per window the
+    log-mel features and the encoder on the device, the prompt, and the decode with the
+    temperature fallback (``decode_with_fallback``); the windows' trimmed texts joined by
+    spaces, a segment per non-empty window.  ``detokenize`` maps token ids to text (the
+    tokenizer is not part of this library).  Language detection is the caller's: pass the
+    language; ``no_speech_prob`` of a window, when known, comes through ``no_speech``."""
+
+    def __init__(self, model, tokens, detokenize: Callable[[List[int]], str], seed: int = 0x5EED,
+                 no_speech: Optional[Callable[[int], float]] = None):
+        self.model, self.tokens, self.detokenize, self.seed = model, tokens, detokenize, seed
+        self.no_speech = no_speech
+
+    def generate(self, audio, temperature: float = 0.0, language: Optional[str] = None,
+                 max_tokens: int = 1024) -> STTOutput:
+        import time
+        t0 = time.perf_counter()
+        a = np.asarray(audio, np.float32)
+        mono = a.mean(axis=-1) if a.ndim > 1 else a
+        # the reference hands Whisper its default sample_len, n_text_ctx / 2 (WhisperModel.swift:215-217)
+        limit = max(1, min(max_tokens, self.model.cfg.max_target // 2))
+        prompt = self.tokens.prompt(language, "transcribe", without_timestamps=False)
+        temps = FALLBACK_TEMPERATURES if temperature == 0 else (temperature,)
+        texts, segments, n_prompt, n_gen = [], [], 0, 0
+        for i, (chunk, offset) in enumerate(chunk_audio(mono)):
+            self.model.encode_audio(chunk)
+            # one seed per request; every window and attempt draws its own Philox counter word
+            res = self.model.decode_with_fallback(
+                prompt, min(limit, self.model.cfg.max_target - len(prompt)), self.tokens.eot, self.detokenize,
+                temps, self.seed, self.no_speech(i) if self.no_speech else 0.0, draw_base=i * len(temps))
+            n_prompt += len(prompt)
+            n_gen += len(res.tokens)
+            text = self.detokenize(res.tokens).strip() if res.tokens else ""
+            if text:
+                texts.append(text)
+                segments.append({"text": text, "start": offset, "end": offset + chunk.shape[0] / SAMPLE_RATE})
+        elapsed = time.perf_counter() - t0
+        return STTOutput(" ".join(texts), segments or None, language, n_prompt, n_gen, n_prompt + n_gen,
+                         n_prompt / elapsed if elapsed > 0 else 0.0, n_gen / elapsed if elapsed > 0 else 0.0, elapsed)
+
