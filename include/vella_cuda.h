@@ -417,6 +417,13 @@ VELLA_API int vella_whisper_decode_batch_eot(vella_whisper* w, const int32_t* pr
 /* The summed log-probabilities of the last decode's first n streams (token rules set; zeros
  * otherwise). */
 VELLA_API int vella_whisper_get_logprobs(const vella_whisper* w, float* out, int32_t n);
+/* Token by token (the reference's step-by-step loop for streaming callers, WhisperModel.swift:
+ * 244-276): vella_whisper_begin runs the prompt and returns the first token; each
+ * vella_whisper_step runs one decoder step (the captured graph) and returns the next.  The
+ * token rules, sampling and log-probability sum apply as in vella_whisper_decode; the caller
+ * stops at end-of-text.  One-stream handles. */
+VELLA_API int vella_whisper_begin(vella_whisper* w, const int32_t* prompt, int32_t n_prompt, int32_t* first);
+VELLA_API int vella_whisper_step(vella_whisper* w, int32_t* token);
 /* Token rules for the following decodes (NULL: plain argmax, the default).  The ids must lie
  * in the vocabulary with eot < timestamp_begin; the masks are built on the device here. */
 VELLA_API int vella_whisper_set_rules(vella_whisper* w, const vella_whisper_rules* rules);

@@ -407,3 +407,4 @@ def test_batched_end_of_text_and_log_probabilities_follow_single_streams():
         assert abs(single.stats()["sum_logprob"] - lps[st]) <= 1e-4 * max(1.0, abs(lps[st])), st
     single.close()
     mb.close()
+

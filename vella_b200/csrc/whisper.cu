@@ -416,6 +416,7 @@ struct vella_whisper {
   cudaGraphExec_t step_exec = nullptr;
   bool step_warm = false;
   bool encoded = false;
+  int step_pos = -1;            // vella_whisper_step: position of the next token (-1: no decode begun)
   cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
   vella_whisper_stats stats{};
 };
@@ -1014,6 +1015,7 @@ int vella_whisper_tensor(vella_whisper* w, const char* name, int32_t layer, void
 // The encoder of every stream over the mel features already in w->mel.
 static int encode_resident(vella_whisper* w) {
   cudaStream_t s = w->stream;
+  w->step_pos = -1;  // a new window ends any token-by-token decode
   int rc = VELLA_OK;
   for (int st = 0; st < w->S && rc == VELLA_OK; ++st) rc = encoder_forward(w, st, s);
   if (rc) return rc;
@@ -1093,6 +1095,7 @@ int vella_whisper_decode(vella_whisper* w, const int32_t* prompt, int32_t n_prom
     return fail(VELLA_E_INVALID, "vella_whisper_decode: %d + %d positions exceed max_target %d", n_prompt, max_tokens,
                 c.max_target);
   *n_out = 0;
+  w->step_pos = -1;  // the token buffer is rewritten
   if (max_tokens == 0) return VELLA_OK;
   VELLA_CUDA_TRY(cudaSetDevice(w->device));
   cudaStream_t s = w->stream;
@@ -1151,6 +1154,7 @@ int vella_whisper_score(vella_whisper* w, const int32_t* tokens, int32_t T, void
   if (!w->encoded) return fail(VELLA_E_INVALID, "vella_whisper_score: encode first");
   if (w->S != 1) return fail(VELLA_E_INVALID, "vella_whisper_score: one-stream handles only");
   if (T < 1 || T > c.max_target) return fail(VELLA_E_INVALID, "vella_whisper_score: %d tokens", T);
+  w->step_pos = -1;  // the token buffer is rewritten
   VELLA_CUDA_TRY(cudaSetDevice(w->device));
   cudaStream_t s = w->stream;
   VELLA_CUDA_TRY(cudaMemcpyAsync(w->tok, tokens, (size_t)T * sizeof(int), cudaMemcpyHostToDevice, s));
@@ -1179,6 +1183,7 @@ static int decode_batch_impl(vella_whisper* w, const int32_t* prompt, int32_t n_
   if (max_tokens < 0 || n_prompt + max_tokens > c.max_target)
     return fail(VELLA_E_INVALID, "%s: %d + %d positions exceed max_target %d", what, n_prompt, max_tokens, c.max_target);
   const int S = w->S;
+  w->step_pos = -1;  // the token buffer is rewritten
   if (n_out)
     for (int st = 0; st < S; ++st) n_out[st] = 0;
   if (max_tokens == 0) return VELLA_OK;
@@ -1251,6 +1256,45 @@ int vella_whisper_decode_batch_eot(vella_whisper* w, const int32_t* prompt, int3
                                    int32_t eot, int32_t* out_tokens, int32_t* n_out) {
   if (!n_out) return fail(VELLA_E_INVALID, "vella_whisper_decode_batch_eot: NULL n_out");
   return decode_batch_impl(w, prompt, n_prompt, max_tokens, eot, out_tokens, n_out, "vella_whisper_decode_batch_eot");
+}
+
+int vella_whisper_begin(vella_whisper* w, const int32_t* prompt, int32_t n_prompt, int32_t* first) {
+  if (!w || !prompt || !first) return fail(VELLA_E_INVALID, "vella_whisper_begin: NULL argument");
+  const vella_whisper_cfg& c = w->cfg;
+  w->step_pos = -1;
+  if (!w->encoded) return fail(VELLA_E_INVALID, "vella_whisper_begin: encode first");
+  if (w->S != 1) return fail(VELLA_E_INVALID, "vella_whisper_begin: %d streams: one-stream handles only", w->S);
+  if (n_prompt < 1 || n_prompt > kWRows || n_prompt >= c.max_target)
+    return fail(VELLA_E_INVALID, "vella_whisper_begin: prompt of %d tokens (1..%d)", n_prompt, kWRows);
+  VELLA_CUDA_TRY(cudaSetDevice(w->device));
+  cudaStream_t s = w->stream;
+  VELLA_CUDA_TRY(cudaMemcpyAsync(w->tok, prompt, n_prompt * sizeof(int), cudaMemcpyHostToDevice, s));
+  VELLA_CUDA_TRY(cudaMemcpyAsync(w->L, &n_prompt, sizeof(int), cudaMemcpyHostToDevice, s));
+  int rc = decode_args(w, n_prompt, -1, s, "vella_whisper_begin");
+  if (rc) return rc;
+  if ((rc = decoder_forward(w, PosRef{w->dzero, 0}, n_prompt, 1, 1, s, 0, 0))) return rc;
+  if ((rc = commit(w, 0, 0, s))) return rc;
+  VELLA_CUDA_TRY(cudaMemcpyAsync(first, w->tok + n_prompt, sizeof(int), cudaMemcpyDeviceToHost, s));
+  VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+  if ((rc = check_flags(w, "vella_whisper_begin"))) return rc;
+  w->step_pos = n_prompt + 1;
+  return VELLA_OK;
+}
+
+int vella_whisper_step(vella_whisper* w, int32_t* token) {
+  if (!w || !token) return fail(VELLA_E_INVALID, "vella_whisper_step: NULL argument");
+  if (w->step_pos < 0) return fail(VELLA_E_INVALID, "vella_whisper_step: call vella_whisper_begin first");
+  if (w->step_pos >= w->cfg.max_target)
+    return fail(VELLA_E_INVALID, "vella_whisper_step: max_target %d positions reached", w->cfg.max_target);
+  VELLA_CUDA_TRY(cudaSetDevice(w->device));
+  cudaStream_t s = w->stream;
+  int rc = run_step(w);
+  if (rc) return rc;
+  VELLA_CUDA_TRY(cudaMemcpyAsync(token, w->tok + w->step_pos, sizeof(int), cudaMemcpyDeviceToHost, s));
+  VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+  if ((rc = check_flags(w, "vella_whisper_step"))) return rc;
+  ++w->step_pos;
+  return VELLA_OK;
 }
 
 int vella_whisper_get_logprobs(const vella_whisper* w, float* out, int32_t n) {

@@ -101,6 +101,8 @@ for _name, _res, _args in [
     ("vella_whisper_decode_batch", ctypes.c_int, [_vp, _pi32, _i32, _i32, _pi32]),
     ("vella_whisper_decode_batch_eot", ctypes.c_int, [_vp, _pi32, _i32, _i32, _i32, _pi32, _pi32]),
     ("vella_whisper_get_logprobs", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_float), _i32]),
+    ("vella_whisper_begin", ctypes.c_int, [_vp, _pi32, _i32, _pi32]),
+    ("vella_whisper_step", ctypes.c_int, [_vp, _pi32]),
     ("vella_whisper_score", ctypes.c_int, [_vp, _pi32, _i32, _vp, _i32]),
     ("vella_whisper_get_stats", ctypes.c_int, [_vp, ctypes.POINTER(WhisperStats)]),
     ("vella_whisper_set_rules", ctypes.c_int, [_vp, ctypes.POINTER(WhisperRules)]),
@@ -218,6 +220,19 @@ class Whisper:
         _lib.check(_lib.lib().vella_whisper_decode_batch_eot(self.h, pr, len(prompt), max_tokens, eot, optr,
                                                              n.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))))
         return [list(out[st, :n[st]]) for st in range(S)]
+
+    def begin(self, prompt: Sequence[int]) -> int:
+        """Runs the prompt; returns the first token (then ``step()`` for each next one)."""
+        pr = (ctypes.c_int32 * len(prompt))(*prompt)
+        t = ctypes.c_int32()
+        _lib.check(_lib.lib().vella_whisper_begin(self.h, pr, len(prompt), ctypes.byref(t)))
+        return t.value
+
+    def step(self) -> int:
+        """One decoder step after ``begin``; returns the next token."""
+        t = ctypes.c_int32()
+        _lib.check(_lib.lib().vella_whisper_step(self.h, ctypes.byref(t)))
+        return t.value
 
     def logprobs(self) -> np.ndarray:
         """Each stream's summed log-probability over the last decode (token rules set)."""
