@@ -534,6 +534,23 @@ VELLA_API int vella_mamba_ssm(const vella_mamba_desc* desc, const void* xbc, con
 VELLA_API int vella_mamba_gated_norm(const vella_mamba_desc* desc, const void* y, const void* zxbcdt,
                                      const void* norm_w, void* out, vella_stream_t stream);
 
+/* ---- Nemotron-H MoE router -------------------------------------------------------------
+ *
+ * Replaces NTMoE's routing (NemotronTranscribeDecoder.swift:487-496): p = sigmoid(x . W^T) in
+ * fp32; the top_k experts of p + e_score_correction_bias (ties: lower expert index), listed by
+ * descending biased score; weights p at them, divided by their sum (+ 1e-20) when norm_topk
+ * and top_k > 1, times `scaling`.  x [rows][hidden] (dtype), router_w [experts][hidden] fp32,
+ * bias [experts] fp32; expert_idx [rows][top_k] int32, expert_w [rows][top_k] fp32.
+ */
+typedef struct vella_moe_route_desc {
+  int32_t rows, hidden, experts, top_k;  /* hidden <= 16384, experts <= 1024, top_k <= 32 */
+  int32_t norm_topk;                     /* norm_topk_prob */
+  float scaling;                         /* routed_scaling_factor */
+  int32_t dtype;                         /* VELLA_BF16 | VELLA_F16 */
+} vella_moe_route_desc;
+VELLA_API int vella_moe_route(const vella_moe_route_desc* desc, const void* x, const float* router_w,
+                              const float* bias, int32_t* expert_idx, float* expert_w, vella_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

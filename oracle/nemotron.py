@@ -1,4 +1,4 @@
-"""CPU restatement of Nemotron-H's Mamba-2 mixer core (test infrastructure only).
+"""CPU restatement of Nemotron-H's Mamba-2 mixer core and MoE routing (test infrastructure only).
 
 Follows ``Worker/Sources/MLXAudioSTT/NemotronTranscribe/NemotronTranscribeDecoder.swift``:
   * ``NTMamba.callAsFunction`` (:340-360): the in_proj output splits into gate [I], the conv
@@ -12,6 +12,9 @@ Follows ``Worker/Sources/MLXAudioSTT/NemotronTranscribe/NemotronTranscribeDecode
     x[d] dt B[g, s]; y[d] = sum_s state[d, s] C[g, s] + x[d] D[h]; the state is fp32;
   * ``NTGatedRMSNorm`` (:301-316): v = y * silu(gate) in fp32, RMS-normalised over groups of
     I / G elements (no weight), then times the weight.
+  * ``NTMoE`` routing (:487-496): sigmoid router scores in fp32, top-k by score plus the
+    correction bias, weights from the unbiased scores (optionally normalised), times the
+    routed scaling factor.
 
 ``ssm_scan`` is the sequential form the library's kernel computes; ``ssm_ssd`` restates the
 reference's SSD chunk form, and the tests check that the two agree in float64.  Parity
@@ -136,3 +139,24 @@ def mixer(zxbcdt, conv_w, conv_b, a_log, dt_bias, D, norm_w, conv_state, ssm_sta
     y, ssm_state = ssm_scan(x, B, C, dt, a_log, D, ssm_state)
     out = gated_rmsnorm(y.reshape(-1, I), gate, norm_w, G, eps)
     return out, conv_state, ssm_state
+
+
+def moe_route(x, router_w, bias, top_k: int, norm_topk: bool, scaling: float):
+    """``NTMoE`` routing (NemotronTranscribeDecoder.swift:487-496): p = sigmoid(x . W^T) in
+    fp32, experts chosen by the top_k of p + e_score_correction_bias (ties: lowest index; the
+    reference's argPartition leaves their order unspecified), weights p at the chosen experts,
+    divided by their sum (+ 1e-20) when norm_topk and top_k > 1, times the routed scaling
+    factor.  x [M, hidden], router_w [E, hidden].  Returns (idx [M, k] in descending biased
+    score, weight [M, k], biased scores [M, E])."""
+    logits = np.asarray(x, np.float64) @ np.asarray(router_w, np.float64).T
+    p = 1.0 / (1.0 + np.exp(-logits))
+    biased = p + np.asarray(bias, np.float64)
+    M, E = biased.shape
+    idx = np.zeros((M, top_k), np.int64)
+    for m in range(M):
+        order = sorted(range(E), key=lambda e: (-biased[m, e], e))
+        idx[m] = order[:top_k]
+    w = np.take_along_axis(p, idx, axis=1)
+    if top_k > 1 and norm_topk:
+        w = w / (w.sum(axis=1, keepdims=True) + 1e-20)
+    return idx, w * scaling, biased

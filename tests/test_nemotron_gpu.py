@@ -99,3 +99,25 @@ def test_bad_descriptors_are_rejected():
     t = torch.zeros(4, 4096, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(_lib.VellaError):
         VN.conv(sh, t, t, None, t, t, 1, 1)
+
+
+def test_moe_route_matches_the_oracle():
+    """The chosen experts equal the oracle's wherever the k-th and (k+1)-th biased scores are
+    apart by more than the fp32 dot-product error, and each expert's weight is within 1e-5."""
+    import torch
+
+    from vella_b200 import nemotron as VN
+    g = torch.Generator(device="cuda").manual_seed(7)
+    M, hidden, E, k = 9, 2688, 128, 6
+    x = torch.randn(M, hidden, generator=g, device="cuda").to(torch.bfloat16)
+    W = torch.randn(E, hidden, generator=g, device="cuda") * 0.02
+    b = torch.randn(E, generator=g, device="cuda") * 0.05
+    idx, w = VN.moe_route(x, W, b, k, True, 2.5)
+    ridx, rw, biased = N.moe_route(_bf16(x), W.double().cpu().numpy(), b.double().cpu().numpy(), k, True, 2.5)
+    idx, w = idx.cpu().numpy(), w.cpu().numpy()
+    for m in range(M):
+        srt = np.sort(biased[m])[::-1]
+        if srt[k - 1] - srt[k] > 1e-5:
+            assert set(idx[m]) == set(ridx[m]), m
+            got = dict(zip(idx[m].tolist(), w[m].tolist()))
+            assert max(abs(got[e] - v) for e, v in zip(ridx[m].tolist(), rw[m].tolist())) <= 1e-5, m

@@ -69,3 +69,18 @@ def test_mixer_state_carries_across_calls():
     a, cs, ss = N.mixer(z[:4], *params, cs0, ss0, **args)
     b, cs, ss = N.mixer(z[4:], *params, cs, ss, **args)
     assert np.allclose(np.concatenate([a, b]), full) and np.allclose(ss, ss_f) and np.allclose(cs, cs_f)
+
+
+def test_moe_route_properties():
+    rng = np.random.default_rng(4)
+    M, E, hd, k = 5, 16, 32, 4
+    x, W, b = _rand(rng, M, hd), _rand(rng, E, hd, scale=0.2), _rand(rng, E, scale=0.3)
+    idx, w, biased = N.moe_route(x, W, b, k, True, 2.5)
+    assert idx.shape == (M, k) and np.allclose(w.sum(axis=1), 2.5)
+    for m in range(M):
+        assert set(idx[m]) == set(np.argsort(-biased[m], kind="stable")[:k])
+        assert all(biased[m, idx[m, j]] >= biased[m, idx[m, j + 1]] for j in range(k - 1))
+    # the weights are the unbiased sigmoid scores
+    idx, w, _ = N.moe_route(x, W, b, k, False, 1.0)
+    p = 1.0 / (1.0 + np.exp(-(x @ W.T)))
+    assert np.allclose(w, np.take_along_axis(p, idx, axis=1))

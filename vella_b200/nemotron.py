@@ -83,3 +83,25 @@ def gated_norm(shape: MambaShape, y, zxbcdt, norm_w, out, streams: int, tokens: 
     d = shape.desc(streams, tokens, zxbcdt.stride(0))
     _lib.check(_lib.lib().vella_mamba_gated_norm(ctypes.byref(d), _p(y), _p(zxbcdt), _p(norm_w), _p(out),
                                                  _stream()))
+
+
+class MoeRouteDesc(ctypes.Structure):
+    _fields_ = [("rows", ctypes.c_int32), ("hidden", ctypes.c_int32), ("experts", ctypes.c_int32),
+                ("top_k", ctypes.c_int32), ("norm_topk", ctypes.c_int32), ("scaling", ctypes.c_float),
+                ("dtype", ctypes.c_int32)]
+
+
+_lib.declare("vella_moe_route", ctypes.c_int, [ctypes.POINTER(MoeRouteDesc), _vp, _vp, _vp, _vp, _vp, _vp])
+
+
+def moe_route(x, router_w, bias, top_k: int, norm_topk: bool, scaling: float):
+    """``NTMoE`` routing of the rows of x [rows, hidden] (bf16 or fp16 on the device): expert
+    indices [rows, top_k] int32 and weights [rows, top_k] fp32."""
+    import torch
+    M, hidden = x.shape
+    d = MoeRouteDesc(M, hidden, router_w.shape[0], top_k, int(norm_topk), scaling,
+                     _lib.BF16 if x.dtype == torch.bfloat16 else _lib.F16)
+    idx = torch.empty(M, top_k, dtype=torch.int32, device=x.device)
+    w = torch.empty(M, top_k, dtype=torch.float32, device=x.device)
+    _lib.check(_lib.lib().vella_moe_route(ctypes.byref(d), _p(x), _p(router_w), _p(bias), _p(idx), _p(w), _stream()))
+    return idx, w
