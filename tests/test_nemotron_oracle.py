@@ -84,3 +84,19 @@ def test_moe_route_properties():
     idx, w, _ = N.moe_route(x, W, b, k, False, 1.0)
     p = 1.0 / (1.0 + np.exp(-(x @ W.T)))
     assert np.allclose(w, np.take_along_axis(p, idx, axis=1))
+
+
+def test_mtp_draft_and_verify_equals_greedy():
+    """The reference's MTP loop with Mamba snapshot/restore and attention trims emits exactly
+    the greedy tokens; both the full-acceptance and the rollback branches run."""
+    c = N.HybridConfig()
+    seen = set()
+    for seed in range(4):
+        P = N.random_hybrid(c, seed)
+        emb = np.random.default_rng(100 + seed).standard_normal((7, c.hidden))
+        want = N.decode_greedy(c, P, emb, 24)
+        for depth in (2, 3):
+            got, hist = N.decode_mtp(c, P, emb, 24, depth)
+            assert got == want, (seed, depth)
+            seen |= {a == depth for a in hist}
+    assert seen == {True, False}
