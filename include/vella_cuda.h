@@ -551,6 +551,28 @@ typedef struct vella_moe_route_desc {
 VELLA_API int vella_moe_route(const vella_moe_route_desc* desc, const void* x, const float* router_w,
                               const float* bias, int32_t* expert_idx, float* expert_w, vella_stream_t stream);
 
+/* ---- Nemotron-H routed experts -----------------------------------------------------------
+ *
+ * Replaces NTSwitchMLP + NTMoE's weighted sum (NemotronTranscribeDecoder.swift:435-499):
+ * out[m] (+)= sum_j expert_w[m][j] * fc2_e(relu(fc1_e(x[m]))^2), e = expert_idx[m][j].  The
+ * experts' weights are stacked [experts][out][in]: MLX-affine (bits 4 | 8, group 64: packed
+ * uint32 [E][out][in*bits/32], scales and biases [E][out][in/64] in dtype) or dense (bits 0,
+ * [E][out][in] in dtype).  fc1 is [E][inter][hidden], fc2 [E][hidden][inter].  The shared
+ * expert (NTMLP, relu^2) is the same call with one expert, every row choosing it at weight 1,
+ * and accumulate = 1.  rows * top_k <= 4096 pairs; hidden and inter in 64..8192.
+ */
+typedef struct vella_moe_experts_desc {
+  int32_t rows, hidden, inter, experts, top_k;
+  int32_t bits;   /* 0, 4 or 8 */
+  int32_t dtype;  /* VELLA_BF16 | VELLA_F16 */
+} vella_moe_experts_desc;
+VELLA_API size_t vella_moe_experts_workspace_size(const vella_moe_experts_desc* desc);
+VELLA_API int vella_moe_experts(const vella_moe_experts_desc* desc, const void* x, const int32_t* expert_idx,
+                                const float* expert_w, const void* fc1_w, const void* fc1_scales,
+                                const void* fc1_biases, const void* fc2_w, const void* fc2_scales,
+                                const void* fc2_biases, void* out, int32_t accumulate, void* workspace,
+                                size_t workspace_bytes, vella_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -280,17 +280,24 @@ def attention(c: HybridConfig, W, x, kv: KV):
     return out.reshape(T, -1) @ W["o"].T
 
 
+def moe_experts(x, idx, w, fc1, fc2):
+    """NTSwitchMLP and the weighted sum (:435-499): out[m] = sum_j w[m, j] fc2[e] (relu(fc1[e]
+    x[m])^2), e = idx[m, j]; fc1 [E, inter, hidden], fc2 [E, hidden, inter]."""
+    x = np.asarray(x, np.float64)
+    out = np.zeros_like(x)
+    for m in range(x.shape[0]):
+        for j in range(idx.shape[1]):
+            e = idx[m, j]
+            h = np.maximum(np.asarray(fc1[e], np.float64) @ x[m], 0.0)
+            out[m] += w[m, j] * (np.asarray(fc2[e], np.float64) @ (h * h))
+    return out
+
+
 def moe(c: HybridConfig, W, x):
     """NTMoE: routed relu^2 experts weighted, plus the shared relu^2 MLP (:435-496)."""
     idx, w, _ = moe_route(x, W["router"], W["bias"], c.top_k, c.norm_topk, c.scaling)
-    out = np.zeros_like(x)
-    for m in range(x.shape[0]):
-        for j in range(c.top_k):
-            e = idx[m, j]
-            h = np.maximum(W["fc1"][e] @ x[m], 0.0)
-            out[m] += w[m, j] * (W["fc2"][e] @ (h * h))
     sh = np.maximum(x @ W["up"].T, 0.0)
-    return out + (sh * sh) @ W["down"].T
+    return moe_experts(x, idx, w, W["fc1"], W["fc2"]) + (sh * sh) @ W["down"].T
 
 
 def make_cache(c: HybridConfig):

@@ -121,3 +121,46 @@ def test_moe_route_matches_the_oracle():
             assert set(idx[m]) == set(ridx[m]), m
             got = dict(zip(idx[m].tolist(), w[m].tolist()))
             assert max(abs(got[e] - v) for e, v in zip(ridx[m].tolist(), rw[m].tolist())) <= 1e-5, m
+
+
+@pytest.mark.parametrize("bits", [4, 0])
+def test_moe_experts_match_the_oracle(bits):
+    """Routed experts (int4 MLX-affine or dense bf16) and the shared expert as a one-expert call
+    accumulated into the same output, against the oracle on the dequantized weights; relative
+    error 2e-2 of the output's scale."""
+    import torch
+
+    from oracle import affine as A
+    from vella_b200 import nemotron as VN
+    rng = np.random.default_rng(5)
+    M, hidden, inter, E, k, shared = 9, 256, 192, 8, 3, 128
+    x = torch.tensor(rng.standard_normal((M, hidden)), dtype=torch.bfloat16, device="cuda")
+    idx = torch.tensor(np.stack([rng.choice(E, k, replace=False) for _ in range(M)]), dtype=torch.int32, device="cuda")
+    wts = torch.tensor(rng.random((M, k)), dtype=torch.float32, device="cuda")
+
+    def weights(n_e, n_out, n_in):
+        w = (rng.standard_normal((n_e, n_out, n_in)) * 0.05).astype(np.float32)
+        if bits == 0:
+            wb = torch.tensor(w, dtype=torch.bfloat16)
+            return (wb.cuda(), None, None), wb.float().numpy().astype(np.float64)
+        qs = [A.quantize(w[e], bits, "bf16") for e in range(n_e)]
+        deq = np.stack([A.dequantize(*q, bits, "bf16") for q in qs]).astype(np.float64)
+        # raw words as int32 / int16 tensors (torch has few uint32 / uint16 operations), viewed as needed
+        t = lambda i, src, dst: torch.tensor(np.stack([q[i] for q in qs]).astype(src).view(dst)).cuda()  # noqa: E731
+        return (t(0, np.uint32, np.int32), t(1, np.uint16, np.int16).view(torch.bfloat16),
+                t(2, np.uint16, np.int16).view(torch.bfloat16)), deq
+
+    f1, d1 = weights(E, inter, hidden)
+    f2, d2 = weights(E, hidden, inter)
+    s1, e1 = weights(1, shared, hidden)
+    s2, e2 = weights(1, hidden, shared)
+    out = VN.moe_experts(x, idx, wts, f1, f2, inter, bits)
+    ones_i = torch.zeros(M, 1, dtype=torch.int32, device="cuda")
+    ones_w = torch.ones(M, 1, dtype=torch.float32, device="cuda")
+    VN.moe_experts(x, ones_i, ones_w, s1, s2, shared, bits, out=out, accumulate=True)
+    torch.cuda.synchronize()
+    xs = x.float().cpu().numpy().astype(np.float64)
+    ref = N.moe_experts(xs, idx.cpu().numpy(), wts.cpu().numpy().astype(np.float64), d1, d2)
+    ref += N.moe_experts(xs, np.zeros((M, 1), np.int64), np.ones((M, 1)), e1, e2)
+    got = out.float().cpu().numpy()
+    assert np.abs(got - ref).max() <= 2e-2 * np.abs(ref).max()

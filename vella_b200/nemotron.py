@@ -105,3 +105,32 @@ def moe_route(x, router_w, bias, top_k: int, norm_topk: bool, scaling: float):
     w = torch.empty(M, top_k, dtype=torch.float32, device=x.device)
     _lib.check(_lib.lib().vella_moe_route(ctypes.byref(d), _p(x), _p(router_w), _p(bias), _p(idx), _p(w), _stream()))
     return idx, w
+
+
+class MoeExpertsDesc(ctypes.Structure):
+    _fields_ = [("rows", ctypes.c_int32), ("hidden", ctypes.c_int32), ("inter", ctypes.c_int32),
+                ("experts", ctypes.c_int32), ("top_k", ctypes.c_int32), ("bits", ctypes.c_int32),
+                ("dtype", ctypes.c_int32)]
+
+
+_lib.declare("vella_moe_experts_workspace_size", ctypes.c_size_t, [ctypes.POINTER(MoeExpertsDesc)])
+_lib.declare("vella_moe_experts", ctypes.c_int, [ctypes.POINTER(MoeExpertsDesc)] + [_vp] * 11 + [ctypes.c_int32, _vp,
+                                                                                               ctypes.c_size_t, _vp])
+
+
+def moe_experts(x, expert_idx, expert_w, fc1, fc2, inter: int, bits: int, out=None, accumulate: bool = False):
+    """Routed relu^2 experts of the rows of x [rows, hidden] (device tensors): fc1 and fc2 are
+    (w, scales, biases) triples (scales/biases None for dense weights)."""
+    import torch
+    M, hidden = x.shape
+    E = fc1[0].shape[0]
+    d = MoeExpertsDesc(M, hidden, inter, E, expert_idx.shape[1], bits,
+                       _lib.BF16 if x.dtype == torch.bfloat16 else _lib.F16)
+    nbytes = int(_lib.lib().vella_moe_experts_workspace_size(ctypes.byref(d)))
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
+    if out is None:
+        out = torch.empty_like(x)
+    _lib.check(_lib.lib().vella_moe_experts(ctypes.byref(d), _p(x), _p(expert_idx), _p(expert_w), _p(fc1[0]),
+                                            _p(fc1[1]), _p(fc1[2]), _p(fc2[0]), _p(fc2[1]), _p(fc2[2]), _p(out),
+                                            int(accumulate), _p(ws), ws.numel(), _stream()))
+    return out
