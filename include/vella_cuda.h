@@ -387,6 +387,10 @@ VELLA_API int vella_whisper_init_random(vella_whisper* w, uint64_t seed, float s
  * window's maximum - 8, (x + 4) / 4; out [streams][n_mels][3000] fp32, the layout
  * vella_whisper_encode reads.  Replaces WhisperAudio.encoderFeatures (WhisperAudio.swift:
  * 7-93) with MLXAudioCore.melFilters (MLXAudioCore/DSP.swift:44-135). */
+/* The Slaney mel filterbank vella_whisper_log_mel projects on, [201][n_mels] fp32 row-major
+ * (host memory; host-only): MLXAudioCore.melFilters(sampleRate: 16000, nFft: 400, nMels:,
+ * fMin: 0, fMax: 8000, norm: "slaney", melScale: .slaney), MLXAudioCore/DSP.swift:44-135. */
+VELLA_API int vella_whisper_mel_filters(int32_t n_mels, float* out);
 VELLA_API int vella_whisper_log_mel(const float* audio, int64_t n_samples, int32_t streams, int32_t n_mels,
                                     float* out, vella_stream_t stream);
 /* The log-mel features of every stream's window (audio [streams][n_samples], on the host or

@@ -240,3 +240,21 @@ def test_generate_windows_prompt_and_text():
     fake = _FakeWhisperHandle([mk([1])])
     VW.WhisperSTT(fake, tok, lambda ts: "x").generate(np.zeros(1000, np.float32), temperature=0.4)
     assert fake.calls[0][3] == (0.4,)
+
+
+def test_library_mel_filterbank_matches_the_oracle():
+    """The library's host-side filterbank (the one the device log-mel projects on) against the
+    oracle's restatement of MLXAudioCore.melFilters: fp32 on both sides, libm and numpy may
+    differ by an ulp in log/exp."""
+    import ctypes
+
+    from vella_b200 import _lib
+    _lib.declare("vella_whisper_mel_filters", ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_float)])
+    for n in (80, 128):
+        out = np.zeros((201, n), np.float32)
+        _lib.check(_lib.lib().vella_whisper_mel_filters(n, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
+        ref = Wh.mel_filters(n)
+        # relative to each filter's peak: near a triangle's foot a weight is a difference of nearly
+        # equal frequencies, where an ulp in a mel point is a large relative change
+        assert (np.abs(out - ref) <= 1e-5 * ref.max(axis=0, keepdims=True)).all(), np.abs(out - ref).max()
+        assert ((out > 0) == (ref > 0)).all()

@@ -20,6 +20,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -201,6 +202,13 @@ int launch_log_mel(const float* audio, int64_t audio_stride, int64_t n_samples, 
 }
 
 }  // namespace vella
+
+extern "C" int vella_whisper_mel_filters(int32_t n_mels, float* out) {
+  if (!out || n_mels < 1 || n_mels > 512) return vella::fail(VELLA_E_INVALID, "vella_whisper_mel_filters: %d bins", n_mels);
+  const std::vector<float> fb = vella::slaney_filters(n_mels);
+  std::copy(fb.begin(), fb.end(), out);
+  return VELLA_OK;
+}
 
 extern "C" int vella_whisper_log_mel(const float* audio, int64_t n_samples, int32_t streams, int32_t n_mels,
                                      float* out, vella_stream_t stream) {
