@@ -396,6 +396,10 @@ VELLA_API int vella_whisper_log_mel(const float* audio, int64_t n_samples, int32
 /* The log-mel features of every stream's window (audio [streams][n_samples], on the host or
  * the device), then vella_whisper_encode over them. */
 VELLA_API int vella_whisper_encode_audio(vella_whisper* w, const float* audio, int64_t n_samples, int32_t on_host);
+/* The encoder position table the handle computes, [length][channels] fp32 before its rounding to
+ * the activation dtype (host memory; host-only): WhisperModel.whisperSinusoids (WhisperModel.swift:
+ * 554-569), double trig rounded once to fp32. */
+VELLA_API int vella_whisper_sinusoids(int32_t length, int32_t channels, float* out);
 /* The configuration the handle was created with. */
 VELLA_API int vella_whisper_get_cfg(const vella_whisper* w, vella_whisper_cfg* out);
 VELLA_API int vella_whisper_tensor(vella_whisper* w, const char* name, int32_t layer, void** ptr, size_t* bytes);

@@ -258,3 +258,17 @@ def test_library_mel_filterbank_matches_the_oracle():
         # equal frequencies, where an ulp in a mel point is a large relative change
         assert (np.abs(out - ref) <= 1e-5 * ref.max(axis=0, keepdims=True)).all(), np.abs(out - ref).max()
         assert ((out > 0) == (ref > 0)).all()
+
+
+def test_library_sinusoid_table_matches_the_oracle():
+    """The library's host-side encoder position table against the oracle's statement of the
+    reference rule (double trig, rounded once to fp32): bit for bit."""
+    import ctypes
+
+    from vella_b200 import _lib
+    _lib.declare("vella_whisper_sinusoids", ctypes.c_int, [ctypes.c_int32, ctypes.c_int32,
+                                                           ctypes.POINTER(ctypes.c_float)])
+    for A, C in ((1500, 384), (1500, 1280), (3, 4)):
+        out = np.zeros((A, C), np.float32)
+        _lib.check(_lib.lib().vella_whisper_sinusoids(A, C, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
+        assert np.array_equal(out, Wh.sinusoids(A, C, "f32"))

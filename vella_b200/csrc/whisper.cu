@@ -703,9 +703,10 @@ int run_step(vella_whisper* w) {
   return VELLA_OK;
 }
 
-template <typename T>
-int write_sinusoids(vella_whisper* w, cudaStream_t s) {
-  const int A = w->cfg.n_audio, C = w->cfg.d_model, half = C / 2;
+// The encoder's position table [A][C] in fp32 (WhisperModel.swift:554-569): half = C / 2,
+// increment ln(10000) / (half - 1), sin | cos halves of p * exp(-increment * i), in double.
+std::vector<float> sinusoid_table(int A, int C) {
+  const int half = C / 2;
   std::vector<float> table((size_t)A * C);
   const double inc = std::log(10000.0) / (double)std::max(half - 1, 1);
   for (int p = 0; p < A; ++p)
@@ -714,6 +715,12 @@ int write_sinusoids(vella_whisper* w, cudaStream_t s) {
       table[(size_t)p * C + i] = (float)std::sin(t);
       table[(size_t)p * C + half + i] = (float)std::cos(t);
     }
+  return table;
+}
+
+template <typename T>
+int write_sinusoids(vella_whisper* w, cudaStream_t s) {
+  const std::vector<float> table = sinusoid_table(w->cfg.n_audio, w->cfg.d_model);
   float* tmp = nullptr;
   VELLA_CUDA_TRY(cudaMalloc(&tmp, table.size() * sizeof(float)));
   cudaError_t e = cudaMemcpyAsync(tmp, table.data(), table.size() * sizeof(float), cudaMemcpyHostToDevice, s);
@@ -940,6 +947,14 @@ int vella_whisper_init_random(vella_whisper* w, uint64_t seed, float std) {
   if ((rc = dense(w->dec_pos, (size_t)c.max_target * d, 0.0f, std))) return rc;
   if ((rc = dt == VELLA_BF16 ? write_sinusoids<__nv_bfloat16>(w, s) : write_sinusoids<__half>(w, s))) return rc;
   VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+  return VELLA_OK;
+}
+
+int vella_whisper_sinusoids(int32_t length, int32_t channels, float* out) {
+  if (!out || length < 1 || channels < 2 || channels % 2)
+    return fail(VELLA_E_INVALID, "vella_whisper_sinusoids: %d x %d (channels even)", length, channels);
+  const std::vector<float> t = sinusoid_table(length, channels);
+  std::copy(t.begin(), t.end(), out);
   return VELLA_OK;
 }
 
