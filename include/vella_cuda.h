@@ -183,6 +183,10 @@ VELLA_API int vella_model_init_random(vella_model* model, uint64_t seed, float s
  * "attn_norm", "mlp_norm", "q_norm", "k_norm", "qkv.w|s|b" (rows q, then k, then v),
  * "o.w|s|b", "gate.w|s|b", "up.w|s|b", "down.w|s|b". */
 VELLA_API int vella_model_tensor(vella_model* model, const char* name, int32_t layer, void** ptr, size_t* bytes);
+/* The RoPE table the model handles use, [max_seq][head_dim / 2] (cos, sin) fp32 pairs (host memory;
+ * host-only): angle = pos * theta^(-2i / head_dim) in double, rounded once to fp32 (the
+ * non-traditional RoPE of Qwen3ASRTextDecoder.swift:47 and :76-82). */
+VELLA_API int vella_rope_table(int32_t max_seq, int32_t head_dim, float theta, float* out);
 /* The configuration the model was created with. */
 VELLA_API int vella_model_get_cfg(const vella_model* model, vella_model_cfg* out);
 VELLA_API size_t vella_model_weight_bytes(const vella_model* model);

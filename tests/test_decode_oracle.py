@@ -102,3 +102,19 @@ def test_draft_and_verify_emits_exactly_the_greedy_sequence():
 def test_oracle_proposal_rate():
     hits = sum(D.oracle_proposal(1, i, 0, 5, 0.7, 1000) == 5 for i in range(4000))
     assert abs(hits / 4000 - 0.7) < 0.03
+
+
+def test_library_rope_table_matches_the_oracle():
+    """The RoPE table the model handles upload (host code), bit for bit against the oracle's."""
+    import ctypes
+
+    import numpy as np
+
+    from oracle import decoder as D
+    from vella_b200 import _lib
+    _lib.declare("vella_rope_table", ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_float,
+                                                    ctypes.POINTER(ctypes.c_float)])
+    for S, hd, theta in ((1280, 128, 1e6), (64, 64, 1e4)):
+        out = np.zeros((S, hd // 2, 2), np.float32)
+        _lib.check(_lib.lib().vella_rope_table(S, hd, theta, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
+        assert np.array_equal(out, D.rope_table(S, hd, theta).astype(np.float32))

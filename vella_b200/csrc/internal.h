@@ -127,6 +127,10 @@ int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& plan, const void* x
 int make_tensor_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz);
 
+// The RoPE table [max_seq][head_dim / 2] of (cos, sin) pairs: angle = pos * theta^(-2i/hd) in
+// double, rounded once to fp32 (model.cu).
+void rope_table(int max_seq, int head_dim, float theta, float* out);
+
 // Whisper log-mel features of `streams` windows (audio window s at audio + s * audio_stride,
 // n_samples long, padded or trimmed to 30 s) into out [streams][n_mels][3000] (audio.cu).
 int launch_log_mel(const float* audio, int64_t audio_stride, int64_t n_samples, int streams, int n_mels, float* out,

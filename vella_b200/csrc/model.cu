@@ -232,6 +232,17 @@ size_t gemm_ws_for(const QWeight& w, int bits, int dtype, int epi) {
 
 }  // namespace
 
+void rope_table(int max_seq, int head_dim, float theta, float* out) {
+  const int half = head_dim / 2;
+  for (int pos = 0; pos < max_seq; ++pos)
+    for (int i = 0; i < half; ++i) {
+      const double inv = std::pow((double)theta, -2.0 * i / (double)head_dim);
+      const double ang = (double)pos * inv;
+      out[((size_t)pos * half + i) * 2] = (float)std::cos(ang);
+      out[((size_t)pos * half + i) * 2 + 1] = (float)std::sin(ang);
+    }
+}
+
 int model_create(const vella_model_cfg& c, int device, Model** out) {
   if (c.n_layers <= 0 || c.d_model <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.head_dim <= 0 ||
       c.ffn <= 0 || c.vocab <= 0 || c.max_seq <= 0 || c.max_prefix < 0)
@@ -360,15 +371,9 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
   m->dzero = flags + 2;
   m->score_P = flags + 3;
   m->score_tok = static_cast<int*>(slots[15]);
-  // RoPE table in double, rounded once to fp32: angle = pos * theta^(-2i/hd)
-  std::vector<float2> table((size_t)c.max_seq * (hd / 2));
-  for (int pos = 0; pos < c.max_seq; ++pos)
-    for (int i = 0; i < hd / 2; ++i) {
-      const double inv = std::pow((double)c.rope_theta, -2.0 * i / (double)hd);
-      const double ang = (double)pos * inv;
-      table[(size_t)pos * (hd / 2) + i] = make_float2((float)std::cos(ang), (float)std::sin(ang));
-    }
-  VELLA_CUDA_TRY(cudaMemcpy(m->rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  std::vector<float> table((size_t)c.max_seq * hd);
+  rope_table(c.max_seq, hd, c.rope_theta, table.data());
+  VELLA_CUDA_TRY(cudaMemcpy(m->rope, table.data(), table.size() * sizeof(float), cudaMemcpyHostToDevice));
   *out = m;
   return VELLA_OK;
 }

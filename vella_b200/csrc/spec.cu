@@ -1113,6 +1113,13 @@ int vella_model_init_random(vella_model* model, uint64_t seed, float std) {
   return model_init_random(model, seed, std, model->stream);
 }
 
+int vella_rope_table(int32_t max_seq, int32_t head_dim, float theta, float* out) {
+  if (!out || max_seq < 1 || head_dim < 2 || head_dim % 2 || !(theta > 0.0f))
+    return fail(VELLA_E_INVALID, "vella_rope_table: %d positions, head_dim %d, theta %g", max_seq, head_dim, (double)theta);
+  rope_table(max_seq, head_dim, theta, out);
+  return VELLA_OK;
+}
+
 int vella_model_get_cfg(const vella_model* model, vella_model_cfg* out) {
   if (!model || !out) return fail(VELLA_E_INVALID, "vella_model_get_cfg: NULL argument");
   *out = model->cfg;
