@@ -183,6 +183,13 @@ VELLA_API int vella_model_init_random(vella_model* model, uint64_t seed, float s
  * "attn_norm", "mlp_norm", "q_norm", "k_norm", "qkv.w|s|b" (rows q, then k, then v),
  * "o.w|s|b", "gate.w|s|b", "up.w|s|b", "down.w|s|b". */
 VELLA_API int vella_model_tensor(vella_model* model, const char* name, int32_t layer, void** ptr, size_t* bytes);
+/* The decode loop's repetition guard on host tokens (host-only): returns 1 when the tokens end
+ * in one block of at most 64 tokens repeated at least 20 times, and sets *kept to the length
+ * up to and including the block's first copy (NemotronTranscribeLoop.tail / cut,
+ * NemotronTranscribeText.swift:98-127); else 0 and *kept = n.  check_every_fourth: only when
+ * n >= 20 and n % 4 == 0 (endsInLoop, NemotronTranscribeModel.swift:296-302).  A negative
+ * status is an error. */
+VELLA_API int vella_loop_cut(const int32_t* tokens, int32_t n, int32_t check_every_fourth, int32_t* kept);
 /* The RoPE table the model handles use, [max_seq][head_dim / 2] (cos, sin) fp32 pairs (host memory;
  * host-only): angle = pos * theta^(-2i / head_dim) in double, rounded once to fp32 (the
  * non-traditional RoPE of Qwen3ASRTextDecoder.swift:47 and :76-82). */

@@ -118,3 +118,43 @@ def test_library_rope_table_matches_the_oracle():
         out = np.zeros((S, hd // 2, 2), np.float32)
         _lib.check(_lib.lib().vella_rope_table(S, hd, theta, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
         assert np.array_equal(out, D.rope_table(S, hd, theta).astype(np.float32))
+
+
+def _lib_cut(tokens, every_fourth=False):
+    import ctypes
+
+    import numpy as np
+
+    from vella_b200 import _lib
+    _lib.declare("vella_loop_cut", ctypes.c_int, [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, ctypes.c_int32,
+                                                  ctypes.POINTER(ctypes.c_int32)])
+    arr = np.ascontiguousarray(np.asarray(tokens, np.int32))
+    kept = ctypes.c_int32()
+    rc = _lib.lib().vella_loop_cut(arr.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), len(tokens),
+                                   int(every_fourth), ctypes.byref(kept))
+    assert rc in (0, 1)
+    return list(tokens[:kept.value]), bool(rc)
+
+
+def test_library_loop_guard_matches_the_known_answers_and_the_oracle():
+    """The library's host-side loop guard (the one the decode loop runs) on the reference's
+    known answers (NemotronTranscribeTests.swift:145-206) and on random sequences with and
+    without planted loops, against the oracle."""
+    import random
+    prefix, block = [5, 6, 7, 8, 9], [21, 22, 23]  # NemotronTranscribeTests.swift:157-177
+    tokens = prefix + block * 20
+    assert _lib_cut(tokens) == (prefix + block, True)
+    short = prefix + block * 19
+    assert _lib_cut(short) == (short, False)
+    assert _lib_cut(list(range(200))) == (list(range(200)), False)
+    assert _lib_cut([1] * 21, every_fourth=True) == ([1] * 21, False)  # 21 is not a multiple of 4
+    assert _lib_cut([1] * 20, every_fourth=True) == ([1], True)
+    rng = random.Random(3)
+    for _ in range(300):
+        head = [rng.randrange(6) for _ in range(rng.randrange(0, 40))]
+        blk = [rng.randrange(6) for _ in range(rng.randrange(1, 70))]
+        seq = head + blk * rng.randrange(1, 26) + [rng.randrange(6) for _ in range(rng.randrange(0, 3))]
+        assert _lib_cut(seq) == D.loop_cut(seq), seq
+        out = list(seq)
+        looped = D.ends_in_loop(out)
+        assert _lib_cut(seq, every_fourth=True) == (out, looped), seq

@@ -1113,6 +1113,14 @@ int vella_model_init_random(vella_model* model, uint64_t seed, float std) {
   return model_init_random(model, seed, std, model->stream);
 }
 
+int vella_loop_cut(const int32_t* tokens, int32_t n, int32_t check_every_fourth, int32_t* kept) {
+  if ((!tokens && n > 0) || n < 0 || !kept) return fail(VELLA_E_INVALID, "vella_loop_cut: NULL argument");
+  std::vector<int> t(tokens, tokens + n);
+  const bool looped = check_every_fourth ? ends_in_loop(t) : loop_cut(t);
+  *kept = looped ? (int32_t)t.size() : n;
+  return looped ? 1 : 0;
+}
+
 int vella_rope_table(int32_t max_seq, int32_t head_dim, float theta, float* out) {
   if (!out || max_seq < 1 || head_dim < 2 || head_dim % 2 || !(theta > 0.0f))
     return fail(VELLA_E_INVALID, "vella_rope_table: %d positions, head_dim %d, theta %g", max_seq, head_dim, (double)theta);
