@@ -592,6 +592,40 @@ VELLA_API int vella_moe_experts(const vella_moe_experts_desc* desc, const void* 
                                 const void* fc2_biases, void* out, int32_t accumulate, void* workspace,
                                 size_t workspace_bytes, vella_stream_t stream);
 
+/* ---- Nemotron-H backbone -----------------------------------------------------------------
+ *
+ * Replaces NTBackbone + the LM head (NemotronTranscribeDecoder.swift:508-571): a stack of
+ * Mamba-2 ('M'), attention without positional encoding ('*') and MoE ('E') blocks, each
+ * x + mixer(rmsnorm(x)), then norm_f, lm_head and argmax; one sequence per handle, the Mamba
+ * states and attention caches held in it.  Weights and states are filled / read through
+ * vella_nh_tensor: "embed" [vocab][hidden], "norm_f", "lm_head.w|s|b"; per layer "norm" and
+ * M: "in_proj.w|s|b" [I + convDim + m_heads][hidden], "out_proj.w|s|b", "conv_w", "conv_b",
+ *    "gnorm", "a_log", "dt_bias", "D" (fp32), "conv_state", "ssm_state" (fp32);
+ * *: "qkv.w|s|b" [(heads + 2 kv_heads) head_dim][hidden] (rows q | k | v), "o.w|s|b", "kv";
+ * E: "router", "router_bias" (fp32), "fc1.w|s|b" [experts][moe_inter][hidden], "fc2.w|s|b",
+ *    "shared_up.w|s|b" [shared_inter][hidden], "shared_down.w|s|b".
+ * Linears are MLX-affine at `bits` (4 | 8, group 64) or dense (0).
+ */
+typedef struct vella_nh_cfg {
+  int32_t vocab, hidden, heads, kv_heads, head_dim;        /* head_dim 64 | 128            */
+  int32_t m_heads, m_head_dim, state_dim, conv_kernel, groups;
+  int32_t moe_inter, shared_inter, experts, top_k, norm_topk;
+  float routed_scaling, dt_min, dt_max, eps;
+  int32_t bits, dtype;
+  int32_t max_seq;   /* attention cache positions */
+  int32_t max_rows;  /* rows per forward (1..512)  */
+  char pattern[128]; /* one of M, *, E per layer, NUL-terminated */
+} vella_nh_cfg;
+typedef struct vella_nh vella_nh;
+VELLA_API int vella_nh_create(const vella_nh_cfg* cfg, int32_t device, vella_nh** out);
+VELLA_API int vella_nh_destroy(vella_nh* model);
+VELLA_API int vella_nh_tensor(vella_nh* model, const char* name, int32_t layer, void** ptr, size_t* bytes);
+/* Runs `rows` new positions pos .. pos + rows - 1 (host tokens, or device embeddings [rows][hidden]:
+ * exactly one of them); the argmax of the last logits_rows rows into argmax_out (host), their
+ * logits into logits_out (device, may be NULL).  Synchronous. */
+VELLA_API int vella_nh_forward(vella_nh* model, const int32_t* tokens, const void* embeds, int32_t rows, int32_t pos,
+                               int32_t logits_rows, int32_t* argmax_out, void* logits_out);
+
 #ifdef __cplusplus
 }
 #endif

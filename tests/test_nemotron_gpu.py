@@ -164,3 +164,116 @@ def test_moe_experts_match_the_oracle(bits):
     ref += N.moe_experts(xs, np.zeros((M, 1), np.int64), np.ones((M, 1)), e1, e2)
     got = out.float().cpu().numpy()
     assert np.abs(got - ref).max() <= 2e-2 * np.abs(ref).max()
+
+
+def _hybrid_params(c, seed):
+    """Oracle parameters (float64) scaled by 1/sqrt(fan-in), rounded to bf16 as the device holds them."""
+    import torch
+    rng = np.random.default_rng(seed)
+    bf = lambda a: torch.tensor(a, dtype=torch.float32).to(torch.bfloat16).float().double().numpy()  # noqa: E731
+    r = lambda *s, sc=1.0: bf(rng.standard_normal(s) * sc)  # noqa: E731
+    lin = lambda n, k: r(n, k, sc=1.0 / np.sqrt(k))  # noqa: E731
+    d = c.hidden
+    layers = []
+    for kind in c.pattern:
+        L = {"kind": kind, "norm": 1.0 + r(d, sc=0.1)}
+        if kind == "M":
+            L.update(in_proj=lin(c.m_inner + c.conv_dim + c.m_heads, d), out_proj=lin(d, c.m_inner),
+                     conv_w=r(c.conv_dim, c.conv_k, sc=0.4), conv_b=r(c.conv_dim, sc=0.1),
+                     a_log=rng.standard_normal(c.m_heads) * 0.5, dt_bias=rng.standard_normal(c.m_heads) * 0.5,
+                     D=rng.standard_normal(c.m_heads), norm_w=1.0 + r(c.m_inner, sc=0.1))
+        elif kind == "*":
+            L.update(q=lin(c.heads * c.head_dim, d), k=lin(c.kv_heads * c.head_dim, d),
+                     v=lin(c.kv_heads * c.head_dim, d), o=lin(d, c.heads * c.head_dim))
+        else:
+            L.update(router=rng.standard_normal((c.experts, d)) / np.sqrt(d), bias=rng.standard_normal(c.experts) * 0.1,
+                     fc1=r(c.experts, c.moe_inter, d, sc=1.0 / np.sqrt(d)),
+                     fc2=r(c.experts, d, c.moe_inter, sc=1.0 / np.sqrt(c.moe_inter)),
+                     up=lin(c.shared_inter, d), down=lin(d, c.shared_inter))
+        layers.append(L)
+    return {"embed": r(c.vocab, d), "layers": layers, "norm_f": 1.0 + r(d, sc=0.1), "lm_head": lin(c.vocab, d)}
+
+
+def _upload(model, P, c):
+    import torch
+
+    class _Dev:
+        def __init__(self, ptr, nbytes):
+            self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                             "version": 3}
+
+    def put(name, layer, arr, dtype=torch.bfloat16):
+        ptr, nbytes = model.tensor(name, layer)
+        t = torch.tensor(np.ascontiguousarray(arr), dtype=torch.float32).to(dtype).cuda().view(torch.uint8).reshape(-1)
+        assert t.numel() == nbytes, (name, layer, t.numel(), nbytes)
+        torch.as_tensor(_Dev(ptr, nbytes), device="cuda").copy_(t)
+
+    put("embed", -1, P["embed"]); put("norm_f", -1, P["norm_f"]); put("lm_head.w", -1, P["lm_head"])
+    for l, L in enumerate(P["layers"]):
+        put("norm", l, L["norm"])
+        if L["kind"] == "M":
+            put("in_proj.w", l, L["in_proj"]); put("out_proj.w", l, L["out_proj"])
+            put("conv_w", l, L["conv_w"]); put("conv_b", l, L["conv_b"]); put("gnorm", l, L["norm_w"])
+            for n, key in (("a_log", "a_log"), ("dt_bias", "dt_bias"), ("D", "D")):
+                put(n, l, L[key], torch.float32)
+        elif L["kind"] == "*":
+            put("qkv.w", l, np.concatenate([L["q"], L["k"], L["v"]])); put("o.w", l, L["o"])
+        else:
+            put("router", l, L["router"], torch.float32); put("router_bias", l, L["bias"], torch.float32)
+            put("fc1.w", l, L["fc1"]); put("fc2.w", l, L["fc2"])
+            put("shared_up.w", l, L["up"]); put("shared_down.w", l, L["down"])
+    torch.cuda.synchronize()
+
+
+def test_backbone_matches_the_oracle_and_rolls_back():
+    """A dense bf16 Nemotron-H backbone ("M*EM*E") on the device against the oracle's float64
+    hybrid model: prefix logits within 3e-2 of the logit scale; every greedy token within that
+    margin of the oracle's argmax along the device's own sequence; and a verify pass undone by
+    restoring the Mamba states then run again gives the same tokens and logits, bit for bit."""
+    import torch
+
+    from vella_b200 import nemotron as VN
+    cfg = VN.NHConfig(vocab=512, hidden=256, heads=4, kv_heads=2, head_dim=64, m_heads=8, m_head_dim=32,
+                      state_dim=64, groups=2, moe_inter=128, shared_inter=128, experts=8, top_k=2,
+                      pattern="M*EM*E", routed_scaling=1.5, max_seq=64, max_rows=16)
+    oc = N.HybridConfig(vocab=512, hidden=256, heads=4, kv_heads=2, head_dim=64, m_heads=8, m_head_dim=32, state=64,
+                        conv_k=4, groups=2, moe_inter=128, shared_inter=128, experts=8, top_k=2, norm_topk=True,
+                        scaling=1.5, pattern="M*EM*E")
+    P = _hybrid_params(oc, 0)
+    m = VN.NHModel(cfg)
+    _upload(m, P, oc)
+    emb = torch.tensor(np.random.default_rng(1).standard_normal((8, 256)), dtype=torch.bfloat16, device="cuda")
+    logits = torch.empty(1, 512, dtype=torch.bfloat16, device="cuda")
+    first = m.forward(embeds=emb, pos=0, logits_rows=1, logits_out=logits)[0]
+    cache = N.make_cache(oc)
+    post = N.backbone(oc, P, emb.float().cpu().numpy().astype(np.float64), cache)
+    ref = post[-1] @ P["lm_head"].T
+    got = logits.float().cpu().numpy()[0]
+    tol = 3e-2 * np.abs(ref).max()
+    assert np.abs(got - ref).max() <= tol
+    toks = [first]
+    for t in range(1, 10):
+        toks.append(m.forward(tokens=[toks[-1]], pos=7 + t, logits_rows=1)[0])
+    # the oracle along the device's sequence
+    row = ref
+    for t in range(10):
+        assert row[toks[t]] >= row.max() - tol, t
+        if t < 9:
+            row = N.backbone(oc, P, P["embed"][[toks[t]]], cache)[-1] @ P["lm_head"].T
+    # a verify pass of 3 rows, rolled back (Mamba states restored), then run again
+    class _Dev:
+        def __init__(self, ptr, nbytes):
+            self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                             "version": 3}
+
+    states = [m.tensor(n, l) for l, k in enumerate(oc.pattern) if k == "M" for n in ("conv_state", "ssm_state")]
+    saved = [torch.as_tensor(_Dev(ptr, nb), device="cuda").clone() for ptr, nb in states]
+    lg1 = torch.empty(3, 512, dtype=torch.bfloat16, device="cuda")
+    a1 = m.forward(tokens=[5, 6, 7], pos=17, logits_rows=3, logits_out=lg1)
+    for (ptr, nb), buf in zip(states, saved):
+        torch.as_tensor(_Dev(ptr, nb), device="cuda").copy_(buf)
+    torch.cuda.synchronize()
+    lg2 = torch.empty(3, 512, dtype=torch.bfloat16, device="cuda")
+    a2 = m.forward(tokens=[5, 6, 7], pos=17, logits_rows=3, logits_out=lg2)
+    assert a1 == a2 and torch.equal(lg1, lg2)
+    m.close()

@@ -134,3 +134,105 @@ def moe_experts(x, expert_idx, expert_w, fc1, fc2, inter: int, bits: int, out=No
                                             _p(fc1[1]), _p(fc1[2]), _p(fc2[0]), _p(fc2[1]), _p(fc2[2]), _p(out),
                                             int(accumulate), _p(ws), ws.numel(), _stream()))
     return out
+
+
+# ---------------------------------------------------------------------------------------
+# The Nemotron-H backbone handle
+# ---------------------------------------------------------------------------------------
+
+class NHCfg(ctypes.Structure):
+    _fields_ = [("vocab", ctypes.c_int32), ("hidden", ctypes.c_int32), ("heads", ctypes.c_int32),
+                ("kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("m_heads", ctypes.c_int32),
+                ("m_head_dim", ctypes.c_int32), ("state_dim", ctypes.c_int32), ("conv_kernel", ctypes.c_int32),
+                ("groups", ctypes.c_int32), ("moe_inter", ctypes.c_int32), ("shared_inter", ctypes.c_int32),
+                ("experts", ctypes.c_int32), ("top_k", ctypes.c_int32), ("norm_topk", ctypes.c_int32),
+                ("routed_scaling", ctypes.c_float), ("dt_min", ctypes.c_float), ("dt_max", ctypes.c_float),
+                ("eps", ctypes.c_float), ("bits", ctypes.c_int32), ("dtype", ctypes.c_int32),
+                ("max_seq", ctypes.c_int32), ("max_rows", ctypes.c_int32), ("pattern", ctypes.c_char * 128)]
+
+
+for _name, _res, _args in [
+    ("vella_nh_create", ctypes.c_int, [ctypes.POINTER(NHCfg), ctypes.c_int32, ctypes.POINTER(_vp)]),
+    ("vella_nh_destroy", ctypes.c_int, [_vp]),
+    ("vella_nh_tensor", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int32, ctypes.POINTER(_vp),
+                                       ctypes.POINTER(ctypes.c_size_t)]),
+    ("vella_nh_forward", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int32), _vp, ctypes.c_int32, ctypes.c_int32,
+                                        ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), _vp]),
+]:
+    _lib.declare(_name, _res, _args)
+
+
+@dataclass
+class NHConfig:
+    """Shapes of a Nemotron-H backbone (the reference's NTDecoderConfig, NemotronTranscribeDecoder.swift:11-36)."""
+    vocab: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    m_heads: int
+    m_head_dim: int
+    state_dim: int
+    groups: int
+    moe_inter: int
+    shared_inter: int
+    experts: int
+    top_k: int
+    pattern: str
+    conv_kernel: int = 4
+    norm_topk: bool = True
+    routed_scaling: float = 1.0
+    dt_min: float = 0.0
+    dt_max: float = float("inf")
+    eps: float = 1e-5
+    bits: int = 0
+    dtype: int = _lib.BF16
+    max_seq: int = 2048
+    max_rows: int = 16
+
+    def c(self) -> NHCfg:
+        return NHCfg(self.vocab, self.hidden, self.heads, self.kv_heads, self.head_dim, self.m_heads, self.m_head_dim,
+                     self.state_dim, self.conv_kernel, self.groups, self.moe_inter, self.shared_inter, self.experts,
+                     self.top_k, int(self.norm_topk), self.routed_scaling, self.dt_min, self.dt_max, self.eps, self.bits,
+                     self.dtype, self.max_seq, self.max_rows, self.pattern.encode())
+
+
+class NHModel:
+    """A Nemotron-H backbone on one GPU (weights, Mamba states, attention caches)."""
+
+    def __init__(self, cfg: NHConfig, device: int = 0):
+        self.cfg = cfg
+        self.h = _vp()
+        c = cfg.c()
+        _lib.check(_lib.lib().vella_nh_create(ctypes.byref(c), device, ctypes.byref(self.h)))
+
+    def close(self):
+        if self.h:
+            _lib.lib().vella_nh_destroy(self.h)
+            self.h = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def tensor(self, name: str, layer: int = -1):
+        p, n = _vp(), ctypes.c_size_t()
+        _lib.check(_lib.lib().vella_nh_tensor(self.h, name.encode(), layer, ctypes.byref(p), ctypes.byref(n)))
+        return p.value, n.value
+
+    def forward(self, tokens=None, embeds=None, pos: int = 0, logits_rows: int = 1, logits_out=None):
+        """Runs the rows (host token ids, or a device tensor of embeddings [rows, hidden]) at
+        positions pos..; returns the argmax of the last logits_rows rows."""
+        out = (ctypes.c_int32 * max(logits_rows, 1))()
+        if tokens is not None:
+            tk = (ctypes.c_int32 * len(tokens))(*tokens)
+            rows = len(tokens)
+            _lib.check(_lib.lib().vella_nh_forward(self.h, tk, None, rows, pos, logits_rows, out, _p(logits_out)))
+        else:
+            import torch
+            torch.cuda.current_stream(embeds.device).synchronize()  # the handle's stream does not wait for torch's
+            _lib.check(_lib.lib().vella_nh_forward(self.h, None, _p(embeds), embeds.shape[0], pos, logits_rows, out,
+                                                   _p(logits_out)))
+        return list(out[:logits_rows])
