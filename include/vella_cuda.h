@@ -614,6 +614,7 @@ typedef struct vella_nh_cfg {
   int32_t bits, dtype;
   int32_t max_seq;   /* attention cache positions */
   int32_t max_rows;  /* rows per forward (1..512)  */
+  int32_t mtp;       /* 1: the MTP head (NTMTP: eh_proj, norms, attention + MoE block, own cache) */
   char pattern[128]; /* one of M, *, E per layer, NUL-terminated */
 } vella_nh_cfg;
 typedef struct vella_nh vella_nh;
@@ -622,9 +623,21 @@ VELLA_API int vella_nh_destroy(vella_nh* model);
 VELLA_API int vella_nh_tensor(vella_nh* model, const char* name, int32_t layer, void** ptr, size_t* bytes);
 /* Runs `rows` new positions pos .. pos + rows - 1 (host tokens, or device embeddings [rows][hidden]:
  * exactly one of them); the argmax of the last logits_rows rows into argmax_out (host), their
- * logits into logits_out (device, may be NULL).  Synchronous. */
+ * logits into logits_out (device, may be NULL), the post-norm_f hidden states of every row into
+ * hidden_out (device [rows][hidden], may be NULL).  Synchronous. */
 VELLA_API int vella_nh_forward(vella_nh* model, const int32_t* tokens, const void* embeds, int32_t rows, int32_t pos,
-                               int32_t logits_rows, int32_t* argmax_out, void* logits_out);
+                               int32_t logits_rows, int32_t* argmax_out, void* logits_out, void* hidden_out);
+/* The MTP head over `rows` pairs (next token or next embedding row, hidden row): x =
+ * eh_proj(concat(enorm(embed(next)),
+ * hnorm(hidden))), then its attention block (cache positions pos ..) and MoE block; x into
+ * x_out (device [rows][hidden], may be NULL: the next chained call's hidden), the argmax of
+ * lm_head(final_norm(x)) of the last logits_rows rows into argmax_out (host).  MTP tensors are
+ * "mtp.eh_proj.w|s|b", "mtp.enorm", "mtp.hnorm", "mtp.attn_norm", "mtp.qkv.w|s|b", "mtp.o.w|s|b",
+ * "mtp.kv", "mtp.moe_norm", "mtp.router", "mtp.router_bias", "mtp.fc1/fc2/shared_up/shared_down.w|s|b",
+ * "mtp.final_norm".  Synchronous. */
+VELLA_API int vella_nh_mtp_forward(vella_nh* model, const int32_t* next_tokens, const void* next_embeds,
+                                   const void* hidden, int32_t rows, int32_t pos, int32_t logits_rows,
+                                   int32_t* argmax_out, void* x_out);
 
 #ifdef __cplusplus
 }

@@ -191,7 +191,17 @@ def _hybrid_params(c, seed):
                      fc2=r(c.experts, d, c.moe_inter, sc=1.0 / np.sqrt(c.moe_inter)),
                      up=lin(c.shared_inter, d), down=lin(d, c.shared_inter))
         layers.append(L)
-    return {"embed": r(c.vocab, d), "layers": layers, "norm_f": 1.0 + r(d, sc=0.1), "lm_head": lin(c.vocab, d)}
+    mtp = {"eh": lin(d, 2 * d), "enorm": 1.0 + r(d, sc=0.1), "hnorm": 1.0 + r(d, sc=0.1),
+           "attn_norm": 1.0 + r(d, sc=0.1), "moe_norm": 1.0 + r(d, sc=0.1), "final_norm": 1.0 + r(d, sc=0.1),
+           "attn": {"q": lin(c.heads * c.head_dim, d), "k": lin(c.kv_heads * c.head_dim, d),
+                    "v": lin(c.kv_heads * c.head_dim, d), "o": lin(d, c.heads * c.head_dim)},
+           "moe": {"router": rng.standard_normal((c.experts, d)) / np.sqrt(d),
+                   "bias": rng.standard_normal(c.experts) * 0.1,
+                   "fc1": r(c.experts, c.moe_inter, d, sc=1.0 / np.sqrt(d)),
+                   "fc2": r(c.experts, d, c.moe_inter, sc=1.0 / np.sqrt(c.moe_inter)),
+                   "up": lin(c.shared_inter, d), "down": lin(d, c.shared_inter)}}
+    return {"embed": r(c.vocab, d), "layers": layers, "norm_f": 1.0 + r(d, sc=0.1), "lm_head": lin(c.vocab, d),
+            "mtp": mtp}
 
 
 def _upload(model, P, c):
@@ -222,6 +232,18 @@ def _upload(model, P, c):
             put("router", l, L["router"], torch.float32); put("router_bias", l, L["bias"], torch.float32)
             put("fc1.w", l, L["fc1"]); put("fc2.w", l, L["fc2"])
             put("shared_up.w", l, L["up"]); put("shared_down.w", l, L["down"])
+    if getattr(model.cfg, "mtp", False):
+        T = P["mtp"]
+        for n, key in (("enorm", "enorm"), ("hnorm", "hnorm"), ("attn_norm", "attn_norm"), ("moe_norm", "moe_norm"),
+                       ("final_norm", "final_norm")):
+            put("mtp." + n, -1, T[key])
+        put("mtp.eh_proj.w", -1, T["eh"])
+        put("mtp.qkv.w", -1, np.concatenate([T["attn"]["q"], T["attn"]["k"], T["attn"]["v"]]))
+        put("mtp.o.w", -1, T["attn"]["o"])
+        put("mtp.router", -1, T["moe"]["router"], torch.float32)
+        put("mtp.router_bias", -1, T["moe"]["bias"], torch.float32)
+        put("mtp.fc1.w", -1, T["moe"]["fc1"]); put("mtp.fc2.w", -1, T["moe"]["fc2"])
+        put("mtp.shared_up.w", -1, T["moe"]["up"]); put("mtp.shared_down.w", -1, T["moe"]["down"])
     torch.cuda.synchronize()
 
 
@@ -276,4 +298,41 @@ def test_backbone_matches_the_oracle_and_rolls_back():
     lg2 = torch.empty(3, 512, dtype=torch.bfloat16, device="cuda")
     a2 = m.forward(tokens=[5, 6, 7], pos=17, logits_rows=3, logits_out=lg2)
     assert a1 == a2 and torch.equal(lg1, lg2)
+    m.close()
+
+
+def test_mtp_head_and_draft_and_verify_on_the_device():
+    """The MTP head's output x matches the oracle's NTMTP within 3e-2 of its scale, and the
+    device decodeMTP loop (snapshot / restore of the Mamba states, attention rows overwritten,
+    the MTP cache trimmed) emits exactly the device's greedy tokens, with both the
+    full-acceptance and the rollback branch taken."""
+    import torch
+
+    from vella_b200 import nemotron as VN
+    kw = dict(vocab=16, hidden=256, heads=4, kv_heads=2, head_dim=64, m_heads=8, m_head_dim=32, groups=2,
+              moe_inter=128, shared_inter=128, experts=8, top_k=2)
+    cfg = VN.NHConfig(state_dim=64, pattern="M*EM*E", routed_scaling=1.5, max_seq=160, max_rows=16, mtp=True, **kw)
+    oc = N.HybridConfig(state=64, conv_k=4, norm_topk=True, scaling=1.5, pattern="M*EM*E", **kw)
+    P = _hybrid_params(oc, 3)
+    m = VN.NHModel(cfg)
+    _upload(m, P, oc)
+    # the head alone on 4 (next embedding, hidden) pairs
+    rng = np.random.default_rng(4)
+    e = torch.tensor(rng.standard_normal((4, 256)), dtype=torch.bfloat16, device="cuda")
+    h = torch.tensor(rng.standard_normal((4, 256)), dtype=torch.bfloat16, device="cuda")
+    x = torch.empty(4, 256, dtype=torch.bfloat16, device="cuda")
+    m.mtp_forward(h, 0, next_embeds=e, x_out=x)
+    ref, _ = N.mtp_forward(oc, P, e.float().cpu().numpy().astype(np.float64),
+                           h.float().cpu().numpy().astype(np.float64), N.KV())
+    assert np.abs(x.float().cpu().numpy() - ref).max() <= 3e-2 * np.abs(ref).max()
+    seen = set()
+    for seed in range(3):
+        emb = torch.tensor(np.random.default_rng(10 + seed).standard_normal((20, 256)), dtype=torch.bfloat16,
+                           device="cuda")
+        want = VN.decode_greedy(m, emb, 40)
+        for depth in (2, 3):
+            got, hist = VN.decode_mtp(m, emb, 40, depth)
+            assert got == want, (seed, depth)
+            seen |= {a == depth for a in hist}
+    assert seen == {True, False}
     m.close()

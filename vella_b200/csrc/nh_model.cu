@@ -52,6 +52,15 @@ struct NhLayer {
   NhLin fc1, fc2, sup, sdown;
 };
 
+// The MTP head (NTMTP, NemotronTranscribeDecoder.swift:578-606):
+// x = eh_proj(concat(enorm(e), hnorm(h))); x += attention(attn_norm(x)); x += MoE(moe_norm(x));
+// its own attention cache.
+struct NhMtp {
+  NhLin eh;
+  void *enorm = nullptr, *hnorm = nullptr, *final_norm = nullptr;
+  NhLayer attn, moe;  // kind '*' and 'E'
+};
+
 __global__ void nh_embed_kernel(uint16_t* h, const uint16_t* __restrict__ table, const int* __restrict__ tok, int d,
                                 int vocab, int* err) {
   pdl_wait();
@@ -75,6 +84,9 @@ struct vella_nh {
   size_t elt = 2;
   cudaStream_t stream = nullptr;
   std::vector<NhLayer> layers;
+  bool has_mtp = false;
+  NhMtp mtp;
+  void *cat = nullptr, *x2 = nullptr;  // MTP [rows][2 hidden] input, [rows][hidden] stream
   std::vector<void*> allocs;
   void *embed = nullptr, *norm_f = nullptr;
   NhLin lm_head;
@@ -129,6 +141,105 @@ vella_mamba_desc mamba_desc(const vella_nh* m, int rows) {
   d.state_dim = c.state_dim; d.conv_kernel = c.conv_kernel; d.dtype = c.dtype; d.in_stride = m->in_w;
   d.dt_min = c.dt_min; d.dt_max = c.dt_max; d.eps = c.eps;
   return d;
+}
+
+// Device tokens of `rows` host ids, then the embedding rows into `out`.
+int nh_embed(vella_nh* m, const int32_t* tokens, int rows, void* out) {
+  const vella_nh_cfg& c = m->cfg;
+  VELLA_CUDA_TRY(cudaMemcpyAsync(m->tok, tokens, rows * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+  return launch_kernel(nh_embed_kernel, dim3(rows), dim3(128), 0, m->stream, static_cast<uint16_t*>(out),
+                       static_cast<const uint16_t*>(m->embed), (const int*)m->tok, c.hidden, c.vocab, m->err);
+}
+
+// x += out_proj(gated_norm(ssm(conv(in_proj(rmsnorm(x))))))
+int nh_mamba_block(vella_nh* m, NhLayer& Ly, void* x, int rows) {
+  const vella_nh_cfg& c = m->cfg;
+  cudaStream_t s = m->stream;
+  const vella_mamba_desc md = mamba_desc(m, rows);
+  int rc;
+  if ((rc = launch_rmsnorm(c.dtype, m->xn, x, Ly.norm, rows, c.hidden, c.eps, s)) ||
+      (rc = nh_gemm(m, Ly.in_proj, m->xn, rows, m->big, false)) ||
+      (rc = vella_mamba_conv(&md, m->big, Ly.conv_w, Ly.conv_b, Ly.conv_state, m->xbc, s)) ||
+      (rc = vella_mamba_ssm(&md, m->xbc, m->big, Ly.a_log, Ly.dt_bias, Ly.Dv, Ly.ssm_state, m->y, s)) ||
+      (rc = vella_mamba_gated_norm(&md, m->y, m->big, Ly.gnorm, m->yn, s)))
+    return rc;
+  return nh_gemm(m, Ly.out_proj, m->yn, rows, x, true);
+}
+
+// x += o(attention(q, K/V cache)) of rmsnorm(x), keys appended at positions *dpos ..
+int nh_attention_block(vella_nh* m, NhLayer& Ly, void* x, int rows) {
+  const vella_nh_cfg& c = m->cfg;
+  cudaStream_t s = m->stream;
+  const int H = c.heads, KV = c.kv_heads, hd = c.head_dim, dt = c.dtype;
+  char* kc = static_cast<char*>(Ly.kv);
+  char* vc = kc + (size_t)KV * c.max_seq * hd * m->elt;
+  const PosRef pr{m->dpos, 0};
+  int rc;
+  if ((rc = launch_rmsnorm(dt, m->xn, x, Ly.norm, rows, c.hidden, c.eps, s)) ||
+      (rc = nh_gemm(m, Ly.qkv, m->xn, rows, m->big, false)) ||
+      (rc = launch_rope_append(dt, m->big, m->q, kc, vc, static_cast<const float2*>(m->ident), nullptr, nullptr, c.eps,
+                               pr, rows, H, KV, hd, c.max_seq, m->err, s)))
+    return rc;
+  AttnView v;
+  v.q = m->q; v.out = m->attn;
+  v.q_rs = v.o_rs = (long long)H * hd;
+  v.q_bs = v.o_bs = (long long)rows * H * hd;
+  v.k = kc; v.v = vc;
+  v.kv_hs = (long long)c.max_seq * hd; v.kv_rs = hd; v.kv_bs = 0;
+  if ((rc = launch_attention_ex(dt, v, 1, pr, 1, rows, H, KV, hd, c.max_seq, 1.0f / std::sqrt((float)hd), s)))
+    return rc;
+  return nh_gemm(m, Ly.o, m->attn, rows, x, true);
+}
+
+// x += routed experts + shared expert of rmsnorm(x)
+int nh_moe_block(vella_nh* m, NhLayer& Ly, void* x, int rows) {
+  const vella_nh_cfg& c = m->cfg;
+  cudaStream_t s = m->stream;
+  const int d = c.hidden, dt = c.dtype;
+  vella_moe_route_desc rd{rows, d, c.experts, c.top_k, c.norm_topk, c.routed_scaling, dt};
+  vella_moe_experts_desc xd{rows, d, c.moe_inter, c.experts, c.top_k, c.bits, dt};
+  vella_moe_experts_desc sd{rows, d, c.shared_inter, 1, 1, c.bits, dt};
+  int rc;
+  if ((rc = launch_rmsnorm(dt, m->xn, x, Ly.norm, rows, d, c.eps, s)) ||
+      (rc = vella_moe_route(&rd, m->xn, Ly.router, Ly.rbias, m->eidx, m->ew, s)) ||
+      (rc = vella_moe_experts(&xd, m->xn, m->eidx, m->ew, Ly.fc1.w, Ly.fc1.s, Ly.fc1.b, Ly.fc2.w, Ly.fc2.s, Ly.fc2.b,
+                              x, 1, m->moe_ws, m->moe_ws_bytes, s)))
+    return rc;
+  return vella_moe_experts(&sd, m->xn, m->zidx, m->ones, Ly.sup.w, Ly.sup.s, Ly.sup.b, Ly.sdown.w, Ly.sdown.s,
+                           Ly.sdown.b, x, 1, m->moe_ws, m->moe_ws_bytes, s);
+}
+
+// norm, LM head and argmax of the last logits_rows of `rows` rows of x
+int nh_head(vella_nh* m, const void* x, const void* norm, int rows, int logits_rows, int32_t* argmax_out,
+            void* logits_out) {
+  if (logits_rows <= 0) return VELLA_OK;
+  const vella_nh_cfg& c = m->cfg;
+  cudaStream_t s = m->stream;
+  int rc;
+  if ((rc = launch_rmsnorm(c.dtype, m->xn, x, norm, logits_rows, c.hidden, c.eps, s, rows, logits_rows)) ||
+      (rc = nh_gemm(m, m->lm_head, m->xn, logits_rows, m->logits, false)) ||
+      (rc = launch_argmax(c.dtype, m->logits, logits_rows, c.vocab, (size_t)c.vocab, m->ys, m->argmax_sc, m->nonfinite,
+                          s)))
+    return rc;
+  VELLA_CUDA_TRY(cudaMemcpyAsync(argmax_out, m->ys, logits_rows * sizeof(int), cudaMemcpyDeviceToHost, s));
+  if (logits_out)
+    VELLA_CUDA_TRY(cudaMemcpyAsync(logits_out, m->logits, (size_t)logits_rows * c.vocab * m->elt,
+                                   cudaMemcpyDeviceToDevice, s));
+  return VELLA_OK;
+}
+
+// waits for the handle's work and reports its flags
+int nh_finish(vella_nh* m, const char* what) {
+  cudaStream_t s = m->stream;
+  VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+  int f[2] = {0, 0};
+  VELLA_CUDA_TRY(cudaMemcpy(f, m->err, sizeof(f), cudaMemcpyDeviceToHost));
+  if (f[0] || f[1]) {
+    VELLA_CUDA_TRY(cudaMemsetAsync(m->err, 0, sizeof(f), s));
+    VELLA_CUDA_TRY(cudaStreamSynchronize(s));
+    return fail(f[1] ? VELLA_E_NONFINITE : VELLA_E_INVALID, "%s: flags 0x%x 0x%x", what, f[0], f[1]);
+  }
+  return VELLA_OK;
 }
 
 }  // namespace
@@ -199,6 +310,31 @@ int vella_nh_create(const vella_nh_cfg* cfg, int32_t device, vella_nh** out) {
       m->lin(Ly.sdown, d, c.shared_inter, 1, &rc);
       moe_inter = std::max({moe_inter, c.moe_inter, c.shared_inter});
     }
+  }
+  if (c.mtp) {
+    m->has_mtp = true;
+    NhMtp& t = m->mtp;
+    m->lin(t.eh, d, 2 * d, 1, &rc);
+    t.enorm = m->alloc((size_t)d * e, &rc);
+    t.hnorm = m->alloc((size_t)d * e, &rc);
+    t.final_norm = m->alloc((size_t)d * e, &rc);
+    t.attn.kind = '*';
+    t.attn.norm = m->alloc((size_t)d * e, &rc);
+    m->lin(t.attn.qkv, m->qkv_n, d, 1, &rc);
+    m->lin(t.attn.o, d, c.heads * c.head_dim, 1, &rc);
+    t.attn.kv = m->alloc((size_t)2 * c.kv_heads * c.max_seq * c.head_dim * e, &rc);
+    t.moe.kind = 'E';
+    t.moe.norm = m->alloc((size_t)d * e, &rc);
+    t.moe.router = static_cast<float*>(m->alloc((size_t)c.experts * d * 4, &rc));
+    t.moe.rbias = static_cast<float*>(m->alloc((size_t)c.experts * 4, &rc));
+    m->lin(t.moe.fc1, c.moe_inter, d, c.experts, &rc);
+    m->lin(t.moe.fc2, d, c.moe_inter, c.experts, &rc);
+    m->lin(t.moe.sup, c.shared_inter, d, 1, &rc);
+    m->lin(t.moe.sdown, d, c.shared_inter, 1, &rc);
+    moe_inter = std::max({moe_inter, c.moe_inter, c.shared_inter});
+    ws = std::max({ws, gemm_ws_for(m, d, 2 * d), gemm_ws_for(m, m->qkv_n, d), gemm_ws_for(m, d, c.heads * c.head_dim)});
+    m->cat = m->alloc((size_t)R * 2 * d * e, &rc);
+    m->x2 = m->alloc((size_t)R * d * e, &rc);
   }
   const int wide = std::max({m->in_w, m->qkv_n, d});
   m->h = m->alloc((size_t)R * d * e, &rc);
@@ -282,6 +418,30 @@ int vella_nh_tensor(vella_nh* m, const char* name, int32_t layer, void** ptr, si
   if (n == "embed") return ret(m->embed, (size_t)c.vocab * d * e);
   if (n == "norm_f") return ret(m->norm_f, d * e);
   if (head == "lm_head") return lin(m->lm_head, part);
+  if (n.rfind("mtp.", 0) == 0) {
+    if (!m->has_mtp) return fail(VELLA_E_INVALID, "vella_nh_tensor: '%s': the model has no MTP head", name);
+    NhMtp& t = m->mtp;
+    const std::string r = n.substr(4);
+    const size_t rdot = r.rfind('.');
+    const std::string rh = rdot == std::string::npos ? r : r.substr(0, rdot);
+    const std::string rp = rdot == std::string::npos ? "" : r.substr(rdot + 1);
+    if (rh == "eh_proj") return lin(t.eh, rp);
+    if (r == "enorm") return ret(t.enorm, d * e);
+    if (r == "hnorm") return ret(t.hnorm, d * e);
+    if (r == "final_norm") return ret(t.final_norm, d * e);
+    if (r == "attn_norm") return ret(t.attn.norm, d * e);
+    if (rh == "qkv") return lin(t.attn.qkv, rp);
+    if (rh == "o") return lin(t.attn.o, rp);
+    if (r == "kv") return ret(t.attn.kv, (size_t)2 * c.kv_heads * c.max_seq * c.head_dim * e);
+    if (r == "moe_norm") return ret(t.moe.norm, d * e);
+    if (r == "router") return ret(t.moe.router, (size_t)c.experts * d * 4);
+    if (r == "router_bias") return ret(t.moe.rbias, (size_t)c.experts * 4);
+    if (rh == "fc1") return lin(t.moe.fc1, rp);
+    if (rh == "fc2") return lin(t.moe.fc2, rp);
+    if (rh == "shared_up") return lin(t.moe.sup, rp);
+    if (rh == "shared_down") return lin(t.moe.sdown, rp);
+    return fail(VELLA_E_INVALID, "vella_nh_tensor: '%s' is not an MTP tensor", name);
+  }
   if (layer < 0 || layer >= m->L) return fail(VELLA_E_INVALID, "vella_nh_tensor: layer %d of %d", layer, m->L);
   NhLayer& Ly = m->layers[layer];
   if (n == "norm") return ret(Ly.norm, d * e);
@@ -312,7 +472,7 @@ int vella_nh_tensor(vella_nh* m, const char* name, int32_t layer, void** ptr, si
 }
 
 int vella_nh_forward(vella_nh* m, const int32_t* tokens, const void* embeds, int32_t rows, int32_t pos,
-                     int32_t logits_rows, int32_t* argmax_out, void* logits_out) {
+                     int32_t logits_rows, int32_t* argmax_out, void* logits_out, void* hidden_out) {
   if (!m || (!tokens == !embeds)) return fail(VELLA_E_INVALID, "vella_nh_forward: tokens or embeddings, one of them");
   const vella_nh_cfg& c = m->cfg;
   if (rows < 1 || rows > c.max_rows || pos < 0 || pos + rows > c.max_seq || logits_rows < 0 || logits_rows > rows ||
@@ -321,78 +481,63 @@ int vella_nh_forward(vella_nh* m, const int32_t* tokens, const void* embeds, int
                 c.max_rows, c.max_seq, logits_rows);
   VELLA_CUDA_TRY(cudaSetDevice(m->device));
   cudaStream_t s = m->stream;
-  const int d = c.hidden, dt = c.dtype, H = c.heads, KV = c.kv_heads, hd = c.head_dim;
+  const int d = c.hidden, dt = c.dtype;
   const size_t e = m->elt;
   int rc;
   VELLA_CUDA_TRY(cudaMemcpyAsync(m->dpos, &pos, sizeof(int), cudaMemcpyHostToDevice, s));
   if (tokens) {
-    VELLA_CUDA_TRY(cudaMemcpyAsync(m->tok, tokens, rows * sizeof(int), cudaMemcpyHostToDevice, s));
-    if ((rc = launch_kernel(nh_embed_kernel, dim3(rows), dim3(128), 0, s, static_cast<uint16_t*>(m->h),
-                            static_cast<const uint16_t*>(m->embed), (const int*)m->tok, d, c.vocab, m->err)))
-      return rc;
+    if ((rc = nh_embed(m, tokens, rows, m->h))) return rc;
   } else {
     VELLA_CUDA_TRY(cudaMemcpyAsync(m->h, embeds, (size_t)rows * d * e, cudaMemcpyDeviceToDevice, s));
   }
-  const PosRef pr{m->dpos, 0};
-  const float scale = 1.0f / std::sqrt((float)hd);
   for (int l = 0; l < m->L; ++l) {
     NhLayer& Ly = m->layers[l];
-    if ((rc = launch_rmsnorm(dt, m->xn, m->h, Ly.norm, rows, d, c.eps, s))) return rc;
-    if (Ly.kind == 'M') {
-      const vella_mamba_desc md = mamba_desc(m, rows);
-      if ((rc = nh_gemm(m, Ly.in_proj, m->xn, rows, m->big, false)) ||
-          (rc = vella_mamba_conv(&md, m->big, Ly.conv_w, Ly.conv_b, Ly.conv_state, m->xbc, s)) ||
-          (rc = vella_mamba_ssm(&md, m->xbc, m->big, Ly.a_log, Ly.dt_bias, Ly.Dv, Ly.ssm_state, m->y, s)) ||
-          (rc = vella_mamba_gated_norm(&md, m->y, m->big, Ly.gnorm, m->yn, s)) ||
-          (rc = nh_gemm(m, Ly.out_proj, m->yn, rows, m->h, true)))
-        return rc;
-    } else if (Ly.kind == '*') {
-      char* kc = static_cast<char*>(Ly.kv);
-      char* vc = kc + (size_t)KV * c.max_seq * hd * e;
-      if ((rc = nh_gemm(m, Ly.qkv, m->xn, rows, m->big, false)) ||
-          (rc = launch_rope_append(dt, m->big, m->q, kc, vc, static_cast<const float2*>(m->ident), nullptr, nullptr,
-                                   c.eps, pr, rows, H, KV, hd, c.max_seq, m->err, s)))
-        return rc;
-      AttnView v;
-      v.q = m->q; v.out = m->attn;
-      v.q_rs = v.o_rs = (long long)H * hd;
-      v.q_bs = v.o_bs = (long long)rows * H * hd;
-      v.k = kc; v.v = vc;
-      v.kv_hs = (long long)c.max_seq * hd; v.kv_rs = hd; v.kv_bs = 0;
-      if ((rc = launch_attention_ex(dt, v, 1, pr, 1, rows, H, KV, hd, c.max_seq, scale, s)) ||
-          (rc = nh_gemm(m, Ly.o, m->attn, rows, m->h, true)))
-        return rc;
-    } else {
-      vella_moe_route_desc rd{rows, d, c.experts, c.top_k, c.norm_topk, c.routed_scaling, dt};
-      vella_moe_experts_desc xd{rows, d, c.moe_inter, c.experts, c.top_k, c.bits, dt};
-      vella_moe_experts_desc sd{rows, d, c.shared_inter, 1, 1, c.bits, dt};
-      if ((rc = vella_moe_route(&rd, m->xn, Ly.router, Ly.rbias, m->eidx, m->ew, s)) ||
-          (rc = vella_moe_experts(&xd, m->xn, m->eidx, m->ew, Ly.fc1.w, Ly.fc1.s, Ly.fc1.b, Ly.fc2.w, Ly.fc2.s,
-                                  Ly.fc2.b, m->h, 1, m->moe_ws, m->moe_ws_bytes, s)) ||
-          (rc = vella_moe_experts(&sd, m->xn, m->zidx, m->ones, Ly.sup.w, Ly.sup.s, Ly.sup.b, Ly.sdown.w, Ly.sdown.s,
-                                  Ly.sdown.b, m->h, 1, m->moe_ws, m->moe_ws_bytes, s)))
-        return rc;
-    }
+    if (Ly.kind == 'M') rc = nh_mamba_block(m, Ly, m->h, rows);
+    else if (Ly.kind == '*') rc = nh_attention_block(m, Ly, m->h, rows);
+    else rc = nh_moe_block(m, Ly, m->h, rows);
+    if (rc) return rc;
   }
-  if (logits_rows > 0) {
-    if ((rc = launch_rmsnorm(dt, m->xn, m->h, m->norm_f, logits_rows, d, c.eps, s, rows, logits_rows)) ||
-        (rc = nh_gemm(m, m->lm_head, m->xn, logits_rows, m->logits, false)) ||
-        (rc = launch_argmax(dt, m->logits, logits_rows, c.vocab, (size_t)c.vocab, m->ys, m->argmax_sc, m->nonfinite, s)))
-      return rc;
-    VELLA_CUDA_TRY(cudaMemcpyAsync(argmax_out, m->ys, logits_rows * sizeof(int), cudaMemcpyDeviceToHost, s));
-    if (logits_out)
-      VELLA_CUDA_TRY(cudaMemcpyAsync(logits_out, m->logits, (size_t)logits_rows * c.vocab * e,
-                                     cudaMemcpyDeviceToDevice, s));
+  if (hidden_out) {  // the post-norm hidden states of every row (the MTP head's input)
+    if ((rc = launch_rmsnorm(dt, m->xn, m->h, m->norm_f, rows, d, c.eps, s))) return rc;
+    VELLA_CUDA_TRY(cudaMemcpyAsync(hidden_out, m->xn, (size_t)rows * d * e, cudaMemcpyDeviceToDevice, s));
   }
-  VELLA_CUDA_TRY(cudaStreamSynchronize(s));
-  int f[2] = {0, 0};
-  VELLA_CUDA_TRY(cudaMemcpy(f, m->err, sizeof(f), cudaMemcpyDeviceToHost));
-  if (f[0] || f[1]) {
-    VELLA_CUDA_TRY(cudaMemsetAsync(m->err, 0, sizeof(f), s));
-    VELLA_CUDA_TRY(cudaStreamSynchronize(s));
-    return fail(f[1] ? VELLA_E_NONFINITE : VELLA_E_INVALID, "vella_nh_forward: flags 0x%x 0x%x", f[0], f[1]);
+  if ((rc = nh_head(m, m->h, m->norm_f, rows, logits_rows, argmax_out, logits_out))) return rc;
+  return nh_finish(m, "vella_nh_forward");
+}
+
+int vella_nh_mtp_forward(vella_nh* m, const int32_t* next_tokens, const void* next_embeds, const void* hidden,
+                         int32_t rows, int32_t pos, int32_t logits_rows, int32_t* argmax_out, void* x_out) {
+  if (!m || !hidden || (!next_tokens == !next_embeds))
+    return fail(VELLA_E_INVALID, "vella_nh_mtp_forward: a hidden row and one of next tokens / next embeddings");
+  if (!m->has_mtp) return fail(VELLA_E_INVALID, "vella_nh_mtp_forward: the model has no MTP head");
+  const vella_nh_cfg& c = m->cfg;
+  if (rows < 1 || rows > c.max_rows || pos < 0 || pos + rows > c.max_seq || logits_rows < 0 || logits_rows > rows ||
+      (logits_rows > 0 && !argmax_out))
+    return fail(VELLA_E_INVALID, "vella_nh_mtp_forward: %d rows at %d, %d logits rows", rows, pos, logits_rows);
+  VELLA_CUDA_TRY(cudaSetDevice(m->device));
+  cudaStream_t s = m->stream;
+  const int d = c.hidden, dt = c.dtype;
+  const size_t e = m->elt, row = (size_t)d * e;
+  NhMtp& t = m->mtp;
+  int rc;
+  VELLA_CUDA_TRY(cudaMemcpyAsync(m->dpos, &pos, sizeof(int), cudaMemcpyHostToDevice, s));
+  // concat(enorm(embed(next)), hnorm(hidden)) -> eh_proj
+  if (next_tokens) {
+    if ((rc = nh_embed(m, next_tokens, rows, m->x2))) return rc;
+  } else {
+    VELLA_CUDA_TRY(cudaMemcpyAsync(m->x2, next_embeds, (size_t)rows * row, cudaMemcpyDeviceToDevice, s));
   }
-  return VELLA_OK;
+  if ((rc = launch_rmsnorm(dt, m->xn, m->x2, t.enorm, rows, d, c.eps, s))) return rc;
+  VELLA_CUDA_TRY(cudaMemcpy2DAsync(m->cat, 2 * row, m->xn, row, row, rows, cudaMemcpyDeviceToDevice, s));
+  if ((rc = launch_rmsnorm(dt, m->xn, hidden, t.hnorm, rows, d, c.eps, s))) return rc;
+  VELLA_CUDA_TRY(cudaMemcpy2DAsync(static_cast<char*>(m->cat) + row, 2 * row, m->xn, row, row, rows,
+                                   cudaMemcpyDeviceToDevice, s));
+  if ((rc = nh_gemm(m, t.eh, m->cat, rows, m->x2, false)) || (rc = nh_attention_block(m, t.attn, m->x2, rows)) ||
+      (rc = nh_moe_block(m, t.moe, m->x2, rows)))
+    return rc;
+  if (x_out) VELLA_CUDA_TRY(cudaMemcpyAsync(x_out, m->x2, (size_t)rows * row, cudaMemcpyDeviceToDevice, s));
+  if ((rc = nh_head(m, m->x2, t.final_norm, rows, logits_rows, argmax_out, nullptr))) return rc;
+  return nh_finish(m, "vella_nh_mtp_forward");
 }
 
 }  // extern "C"

@@ -148,7 +148,8 @@ class NHCfg(ctypes.Structure):
                 ("experts", ctypes.c_int32), ("top_k", ctypes.c_int32), ("norm_topk", ctypes.c_int32),
                 ("routed_scaling", ctypes.c_float), ("dt_min", ctypes.c_float), ("dt_max", ctypes.c_float),
                 ("eps", ctypes.c_float), ("bits", ctypes.c_int32), ("dtype", ctypes.c_int32),
-                ("max_seq", ctypes.c_int32), ("max_rows", ctypes.c_int32), ("pattern", ctypes.c_char * 128)]
+                ("max_seq", ctypes.c_int32), ("max_rows", ctypes.c_int32), ("mtp", ctypes.c_int32),
+                ("pattern", ctypes.c_char * 128)]
 
 
 for _name, _res, _args in [
@@ -157,7 +158,9 @@ for _name, _res, _args in [
     ("vella_nh_tensor", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int32, ctypes.POINTER(_vp),
                                        ctypes.POINTER(ctypes.c_size_t)]),
     ("vella_nh_forward", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int32), _vp, ctypes.c_int32, ctypes.c_int32,
-                                        ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), _vp]),
+                                        ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), _vp, _vp]),
+    ("vella_nh_mtp_forward", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int32), _vp, _vp, ctypes.c_int32,
+                                            ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), _vp]),
 ]:
     _lib.declare(_name, _res, _args)
 
@@ -189,12 +192,18 @@ class NHConfig:
     dtype: int = _lib.BF16
     max_seq: int = 2048
     max_rows: int = 16
+    mtp: bool = False
 
     def c(self) -> NHCfg:
         return NHCfg(self.vocab, self.hidden, self.heads, self.kv_heads, self.head_dim, self.m_heads, self.m_head_dim,
                      self.state_dim, self.conv_kernel, self.groups, self.moe_inter, self.shared_inter, self.experts,
                      self.top_k, int(self.norm_topk), self.routed_scaling, self.dt_min, self.dt_max, self.eps, self.bits,
-                     self.dtype, self.max_seq, self.max_rows, self.pattern.encode())
+                     self.dtype, self.max_seq, self.max_rows, int(self.mtp), self.pattern.encode())
+
+
+class _DevBytes:
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
 
 
 class NHModel:
@@ -222,17 +231,141 @@ class NHModel:
         _lib.check(_lib.lib().vella_nh_tensor(self.h, name.encode(), layer, ctypes.byref(p), ctypes.byref(n)))
         return p.value, n.value
 
-    def forward(self, tokens=None, embeds=None, pos: int = 0, logits_rows: int = 1, logits_out=None):
+    def forward(self, tokens=None, embeds=None, pos: int = 0, logits_rows: int = 1, logits_out=None,
+                hidden_out=None):
         """Runs the rows (host token ids, or a device tensor of embeddings [rows, hidden]) at
         positions pos..; returns the argmax of the last logits_rows rows."""
         out = (ctypes.c_int32 * max(logits_rows, 1))()
         if tokens is not None:
             tk = (ctypes.c_int32 * len(tokens))(*tokens)
             rows = len(tokens)
-            _lib.check(_lib.lib().vella_nh_forward(self.h, tk, None, rows, pos, logits_rows, out, _p(logits_out)))
+            _lib.check(_lib.lib().vella_nh_forward(self.h, tk, None, rows, pos, logits_rows, out, _p(logits_out),
+                                                   _p(hidden_out)))
         else:
             import torch
             torch.cuda.current_stream(embeds.device).synchronize()  # the handle's stream does not wait for torch's
             _lib.check(_lib.lib().vella_nh_forward(self.h, None, _p(embeds), embeds.shape[0], pos, logits_rows, out,
-                                                   _p(logits_out)))
+                                                   _p(logits_out), _p(hidden_out)))
         return list(out[:logits_rows])
+
+    def mtp_forward(self, hidden, pos: int, next_tokens=None, next_embeds=None, logits_rows: int = 1, x_out=None):
+        """The MTP head over (next token or embedding row, hidden row) pairs at MTP-cache
+        positions pos..; returns the argmax of the last logits_rows rows."""
+        import torch
+        torch.cuda.current_stream(hidden.device).synchronize()
+        out = (ctypes.c_int32 * max(logits_rows, 1))()
+        tk = None if next_tokens is None else (ctypes.c_int32 * len(next_tokens))(*next_tokens)
+        _lib.check(_lib.lib().vella_nh_mtp_forward(self.h, tk, _p(next_embeds), _p(hidden), hidden.shape[0], pos,
+                                                   logits_rows, out, _p(x_out)))
+        return list(out[:logits_rows])
+
+    def reset(self):
+        """A fresh sequence: the Mamba states zeroed (the reference makes a new cache per decode;
+        attention and MTP cache rows are overwritten from position 0)."""
+        for v in self.mamba_states():
+            v.zero_()
+
+    def mamba_states(self):
+        """Device views of every Mamba layer's conv and SSM states (for snapshot / restore)."""
+        import torch
+        views = []
+        for layer, kind in enumerate(self.cfg.pattern):
+            if kind == "M":
+                for name in ("conv_state", "ssm_state"):
+                    ptr, nbytes = self.tensor(name, layer)
+                    views.append(torch.as_tensor(_DevBytes(ptr, nbytes), device="cuda"))
+        return views
+
+
+def decode_greedy(model: NHModel, embeddings, max_tokens: int, eos=()):
+    """decodeGreedy (NemotronTranscribeModel.swift:266-290) on the device: the prefix in chunks
+    of max_rows, then one token per forward."""
+    R, T = model.cfg.max_rows, embeddings.shape[0]
+    model.reset()
+    t = None
+    for s0 in range(0, T, R):
+        t = model.forward(embeds=embeddings[s0:s0 + R].contiguous(), pos=s0)[0]
+    out, pos = [], T
+    while len(out) < max_tokens and t not in eos:
+        out.append(t)
+        t = model.forward(tokens=[t], pos=pos)[0]
+        pos += 1
+    return out
+
+
+def decode_mtp(model: NHModel, embeddings, max_tokens: int, depth: int, eos=()):
+    """decodeMTP (NemotronTranscribeModel.swift:306-396) on the device: depth chained MTP drafts
+    verified in one forward; on a partial acceptance the Mamba states are restored from the
+    pass's snapshot and the accepted prefix is fed again (the attention rows are overwritten);
+    the MTP cache drops its depth - 1 chain rows every pass.  Returns (tokens, accepted counts)."""
+    import torch
+    R, T, d = model.cfg.max_rows, embeddings.shape[0], model.cfg.hidden
+    dev = embeddings.device
+    hs = torch.empty(T, d, dtype=embeddings.dtype, device=dev)
+    model.reset()
+    t = None
+    for s0 in range(0, T, R):
+        t = model.forward(embeds=embeddings[s0:s0 + R].contiguous(), pos=s0, hidden_out=hs[s0:s0 + R])[0]
+    out, hist = [], []
+    if t in eos or max_tokens == 0:
+        return out, hist
+    out.append(t)
+    mlen = 0
+    x = torch.empty(R, d, dtype=embeddings.dtype, device=dev)
+
+    def embed_row(tok):
+        ptr, nbytes = model.tensor("embed")
+        table = torch.as_tensor(_DevBytes(ptr, nbytes), device=dev).view(embeddings.dtype).view(-1, d)
+        return table[tok:tok + 1]
+
+    def chain(x0, first):
+        nonlocal mlen
+        drafts, token, cur = [first], first, x0
+        for _ in range(depth - 1):
+            nx = torch.empty(1, d, dtype=embeddings.dtype, device=dev)
+            token = model.mtp_forward(cur, mlen, next_tokens=[token], x_out=nx)[0]
+            mlen += 1
+            cur = nx
+            drafts.append(token)
+        return drafts
+
+    nxt = torch.cat([embeddings[1:], embed_row(t)])
+    first = None
+    for s0 in range(0, T, R):
+        n = min(R, T - s0)
+        first = model.mtp_forward(hs[s0:s0 + n].contiguous(), mlen, next_embeds=nxt[s0:s0 + n].contiguous(),
+                                  x_out=x[:n])[0]
+        mlen += n
+    drafts = chain(x[n - 1:n].clone(), first)
+    pending, mtp_done, blen = [t], 0, T
+    while len(out) < max_tokens:
+        snapshot = [v.clone() for v in model.mamba_states()]
+        fed = pending + drafts
+        verified = torch.empty(len(fed), d, dtype=embeddings.dtype, device=dev)
+        ys = model.forward(tokens=fed, pos=blen, logits_rows=len(fed), hidden_out=verified)
+        k, a = len(pending), 0
+        while a < len(drafts) and ys[k - 1 + a] == drafts[a]:
+            a += 1
+        bonus = ys[k - 1 + a]
+        new = drafts[:a] + [bonus]
+        hist.append(a)
+        mlen -= depth - 1
+        upto = k + a
+        e_next = (fed[1:upto] + [bonus])[mtp_done:]
+        nx = torch.empty(len(e_next), d, dtype=embeddings.dtype, device=dev)
+        head = model.mtp_forward(verified[mtp_done:upto].contiguous(), mlen, next_tokens=e_next, x_out=nx)[0]
+        mlen += len(e_next)
+        drafts = chain(nx[-1:].clone(), head)
+        if upto == len(fed):  # every draft accepted
+            pending, mtp_done, blen = [bonus], 0, blen + len(fed)
+        else:
+            for v, s in zip(model.mamba_states(), snapshot):
+                v.copy_(s)
+            pending, mtp_done = fed[:upto] + [bonus], upto
+        for tok in new:
+            if tok in eos:
+                return out, hist
+            out.append(tok)
+            if len(out) >= max_tokens:
+                return out, hist
+    return out, hist
