@@ -100,3 +100,81 @@ def test_mtp_draft_and_verify_equals_greedy():
             assert got == want, (seed, depth)
             seen |= {a == depth for a in hist}
     assert seen == {True, False}
+
+
+class _OracleNH:
+    """The device handle's interface (forward / mtp_forward with positional caches, Mamba state
+    views, embedding rows) over the float64 oracle, to run the library's host decode loops on
+    the CPU."""
+
+    class _State:
+        def __init__(self, owner, layer, key):
+            self.owner, self.layer, self.key = owner, layer, key
+
+        def clone(self):
+            return self.owner.cache[self.layer][self.key].copy()
+
+        def copy_(self, arr):
+            self.owner.cache[self.layer][self.key] = arr.copy()
+
+        def zero_(self):
+            self.owner.cache[self.layer][self.key] = np.zeros_like(self.owner.cache[self.layer][self.key])
+
+    def __init__(self, c, P, max_rows=16):
+        import types
+        self.c, self.P = c, P
+        self.cfg = types.SimpleNamespace(max_rows=max_rows, hidden=c.hidden, pattern=c.pattern)
+        self.reset()
+
+    def reset(self):
+        self.cache, self.mkv = N.make_cache(self.c), N.KV()
+
+    def mamba_states(self):
+        return [self._State(self, l, k) for l, kind in enumerate(self.c.pattern) if kind == "M"
+                for k in ("conv", "state")]
+
+    def embedding_rows(self, tokens):
+        import torch
+        return torch.tensor(self.P["embed"][list(tokens)])
+
+    @staticmethod
+    def _at(kv, pos):  # a positional cache: rows from `pos` on are overwritten
+        if kv.k is not None:
+            kv.trim(kv.k.shape[0] - pos)
+
+    def forward(self, tokens=None, embeds=None, pos=0, logits_rows=1, logits_out=None, hidden_out=None):
+        x = self.P["embed"][list(tokens)] if tokens is not None else embeds.numpy().astype(np.float64)
+        for lc in self.cache:
+            if isinstance(lc, N.KV):
+                self._at(lc, pos)
+        post = N.backbone(self.c, self.P, x, self.cache)
+        if hidden_out is not None:
+            hidden_out.copy_(__import__("torch").tensor(post))
+        return list(N.head(self.P, post[post.shape[0] - logits_rows:]))
+
+    def mtp_forward(self, hidden, pos, next_tokens=None, next_embeds=None, logits_rows=1, x_out=None):
+        e = self.P["embed"][list(next_tokens)] if next_tokens is not None else next_embeds.numpy().astype(np.float64)
+        self._at(self.mkv, pos)
+        x, xo = N.mtp_forward(self.c, self.P, e, hidden.numpy().astype(np.float64), self.mkv)
+        if x_out is not None:
+            x_out.copy_(__import__("torch").tensor(x))
+        return list(N.head(self.P, xo[xo.shape[0] - logits_rows:]))
+
+
+def test_device_decode_loops_follow_the_reference_on_the_oracle():
+    """The library's host loops (vella_b200.nemotron decode_greedy / decode_mtp: prefix chunks of
+    max_rows, positional caches, the MTP cache trimmed each pass, Mamba states restored from a
+    snapshot) over an oracle-backed handle give the oracle's own greedy tokens."""
+    import torch
+
+    from vella_b200 import nemotron as VN
+    c = N.HybridConfig()
+    for seed in range(3):
+        P = N.random_hybrid(c, seed)
+        emb = np.random.default_rng(200 + seed).standard_normal((21, c.hidden))
+        want = N.decode_greedy(c, P, emb, 24)
+        fake = _OracleNH(c, P, max_rows=8)
+        assert VN.decode_greedy(fake, torch.tensor(emb), 24) == want
+        for depth in (2, 3):
+            got, hist = VN.decode_mtp(fake, torch.tensor(emb), 24, depth)
+            assert got == want, (seed, depth)

@@ -259,6 +259,14 @@ class NHModel:
                                                    logits_rows, out, _p(x_out)))
         return list(out[:logits_rows])
 
+    def embedding_rows(self, tokens):
+        """Rows of the token embedding table (a device view, [len(tokens), hidden])."""
+        import torch
+        ptr, nbytes = self.tensor("embed")
+        dt = torch.bfloat16 if self.cfg.dtype == _lib.BF16 else torch.float16
+        table = torch.as_tensor(_DevBytes(ptr, nbytes), device="cuda").view(dt).view(-1, self.cfg.hidden)
+        return table[list(tokens)]
+
     def reset(self):
         """A fresh sequence: the Mamba states zeroed (the reference makes a new cache per decode;
         attention and MTP cache rows are overwritten from position 0)."""
@@ -313,11 +321,6 @@ def decode_mtp(model: NHModel, embeddings, max_tokens: int, depth: int, eos=()):
     mlen = 0
     x = torch.empty(R, d, dtype=embeddings.dtype, device=dev)
 
-    def embed_row(tok):
-        ptr, nbytes = model.tensor("embed")
-        table = torch.as_tensor(_DevBytes(ptr, nbytes), device=dev).view(embeddings.dtype).view(-1, d)
-        return table[tok:tok + 1]
-
     def chain(x0, first):
         nonlocal mlen
         drafts, token, cur = [first], first, x0
@@ -329,7 +332,7 @@ def decode_mtp(model: NHModel, embeddings, max_tokens: int, depth: int, eos=()):
             drafts.append(token)
         return drafts
 
-    nxt = torch.cat([embeddings[1:], embed_row(t)])
+    nxt = torch.cat([embeddings[1:], model.embedding_rows([t]).to(embeddings.dtype)])
     first = None
     for s0 in range(0, T, R):
         n = min(R, T - s0)
