@@ -621,6 +621,13 @@ typedef struct vella_nh vella_nh;
 VELLA_API int vella_nh_create(const vella_nh_cfg* cfg, int32_t device, vella_nh** out);
 VELLA_API int vella_nh_destroy(vella_nh* model);
 VELLA_API int vella_nh_tensor(vella_nh* model, const char* name, int32_t layer, void** ptr, size_t* bytes);
+VELLA_API int vella_nh_get_cfg(const vella_nh* model, vella_nh_cfg* out);
+/* A Nemotron-H checkpoint: NVIDIA's NeMo keys (llm.model.*, experts stored [E][in][out], the MTP
+ * head's llm.mtp.* keys) or the MLX module tree (llm.backbone.*, lm_head, mtp.*), float (quantized
+ * at load for an int4/int8 handle) or MLX-affine at the handle's bits (NemotronTranscribeKeys.map,
+ * NemotronTranscribeText.swift:369-397; NemotronTranscribeModel.loadWeights :127-175). */
+VELLA_API int vella_nh_check_checkpoint(const vella_st* st, const vella_nh_cfg* cfg);
+VELLA_API int vella_nh_load(vella_nh* model, const vella_st* st);
 /* Runs `rows` new positions pos .. pos + rows - 1 (host tokens, or device embeddings [rows][hidden]:
  * exactly one of them); the argmax of the last logits_rows rows into argmax_out (host), their
  * logits into logits_out (device, may be NULL), the post-norm_f hidden states of every row into

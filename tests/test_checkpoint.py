@@ -683,3 +683,94 @@ def test_corrupted_files_are_rejected_without_crashing(tmp_path):
     assert r.returncode == 0, r.stderr[-2000:]
     ok, bad = map(int, r.stdout.split())
     assert ok + bad == len(cases) and bad > 0
+
+
+# ---- Nemotron-H ---------------------------------------------------------------------------
+
+def small_nh_cfg(bits=0, mtp=True):
+    from vella_b200.nemotron import NHConfig
+    return NHConfig(vocab=96, hidden=64, heads=2, kv_heads=1, head_dim=64, m_heads=4, m_head_dim=16, state_dim=32,
+                    groups=2, moe_inter=128, shared_inter=64, experts=4, top_k=2, pattern="M*E", bits=bits, mtp=mtp,
+                    max_seq=32, max_rows=8)
+
+
+def nemo_tensors(c, quant_bits=0, rng=None):
+    """NVIDIA NeMo key layout (llm.model.*, experts [E][in][out], llm.mtp.*) with random values."""
+    rng = rng or np.random.default_rng(6)
+    f = lambda *s: (rng.standard_normal(s) * 0.05).astype(np.float16)  # noqa: E731
+    d, I = c.hidden, c.m_heads * c.m_head_dim
+    conv = I + 2 * c.groups * c.state_dim
+    t = {"llm.model.embed_tokens.weight": f(c.vocab, d), "llm.model.norm.weight": f(d), "llm.lm_head.weight": f(c.vocab, d)}
+
+    def attn(p):
+        t[p + "q_proj.weight"] = f(c.heads * c.head_dim, d)
+        t[p + "k_proj.weight"] = f(c.kv_heads * c.head_dim, d)
+        t[p + "v_proj.weight"] = f(c.kv_heads * c.head_dim, d)
+        t[p + "o_proj.weight"] = f(d, c.heads * c.head_dim)
+
+    def moe(p):
+        t[p + "gate.weight"] = f(c.experts, d)
+        t[p + "gate.e_score_correction_bias"] = np.zeros(c.experts, np.float32)
+        t[p + "experts.gate_and_up_projs"] = f(c.experts, d, c.moe_inter)      # [E][in][out]
+        t[p + "experts.down_projs"] = f(c.experts, c.moe_inter, d)
+        t[p + "shared_experts.up_proj.weight"] = f(c.shared_inter, d)
+        t[p + "shared_experts.down_proj.weight"] = f(d, c.shared_inter)
+
+    for l, kind in enumerate(c.pattern):
+        p = f"llm.model.layers.{l}."
+        t[p + "norm.weight"] = f(d)
+        if kind == "M":
+            t[p + "mixer.in_proj.weight"] = f(I + conv + c.m_heads, d)
+            t[p + "mixer.out_proj.weight"] = f(d, I)
+            t[p + "mixer.conv1d.weight"] = f(conv, 1, c.conv_kernel)
+            t[p + "mixer.conv1d.bias"] = f(conv)
+            t[p + "mixer.norm.weight"] = f(I)
+            for n in ("A_log", "dt_bias", "D"):
+                t[p + "mixer." + n] = rng.standard_normal(c.m_heads).astype(np.float32)
+        elif kind == "*":
+            attn(p + "mixer.")
+        else:
+            moe(p + "mixer.")
+    if c.mtp:
+        m = "llm.mtp.layers."
+        t[m + "0.eh_proj.weight"] = f(d, 2 * d)
+        for n in ("enorm", "hnorm"):
+            t[m + f"0.{n}.weight"] = f(d)
+        t[m + "0.norm.weight"] = f(d)
+        attn(m + "0.mixer.")
+        t[m + "1.norm.weight"] = f(d)
+        moe(m + "1.mixer.")
+        t[m + "1.final_layernorm.weight"] = f(d)
+    t["llm.model.layers.0.mixer._extra_state"] = np.zeros(4, np.uint8)  # skipped like the reference
+    return t
+
+
+def test_nemotron_checkpoint_layout_passes_the_check(tmp_path):
+    from vella_b200 import checkpoint as C
+    c = small_nh_cfg()
+    p = tmp_path / "nh.safetensors"
+    write_safetensors(p, nemo_tensors(c))
+    with _st([p]) as st:
+        C.check_nh_checkpoint(st, c)
+        C.check_nh_checkpoint(st, small_nh_cfg(bits=4))  # float experts: derived at load
+
+
+def test_nemotron_checkpoint_problems_are_named(tmp_path):
+    from vella_b200 import _lib
+    from vella_b200 import checkpoint as C
+    c = small_nh_cfg()
+    t = nemo_tensors(c)
+    del t["llm.mtp.layers.1.final_layernorm.weight"]
+    p = tmp_path / "a.safetensors"
+    write_safetensors(p, t)
+    with _st([p]) as st:
+        with pytest.raises(_lib.VellaError, match="mtp.final_norm"):
+            C.check_nh_checkpoint(st, c)
+        C.check_nh_checkpoint(st, small_nh_cfg(mtp=False))  # no MTP head wanted: fine
+    t = nemo_tensors(c)
+    t["llm.model.layers.2.mixer.experts.down_projs"] = np.zeros((c.experts, c.hidden, c.moe_inter), np.float16)
+    p = tmp_path / "b.safetensors"
+    write_safetensors(p, t)
+    with _st([p]) as st:
+        with pytest.raises(_lib.VellaError, match="switch_mlp.fc2"):
+            C.check_nh_checkpoint(st, c)  # [E][out][in] where NeMo stores [E][in][out]

@@ -336,3 +336,42 @@ def test_mtp_head_and_draft_and_verify_on_the_device():
             seen |= {a == depth for a in hist}
     assert seen == {True, False}
     m.close()
+
+
+def test_nemo_checkpoint_loads_into_the_backbone(tmp_path):
+    """A NeMo-layout checkpoint loaded into a dense bf16 handle: the experts transposed from
+    [E][in][out], q|k|v stacked, the conv weight and router as stored (bf16 / fp32); a forward
+    runs; an int4 handle derives its codes from the same float checkpoint."""
+    import torch
+
+    from tests.test_checkpoint import nemo_tensors, small_nh_cfg, write_safetensors
+    from vella_b200 import checkpoint as C
+    c = small_nh_cfg()
+    t = nemo_tensors(c)
+    p = tmp_path / "nh.safetensors"
+    write_safetensors(p, t)
+    m = C.load_nh([p], c)
+
+    class _Dev:
+        def __init__(self, ptr, nbytes):
+            self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                             "version": 3}
+
+    def get(name, layer, dt=torch.bfloat16):
+        ptr, nb = m.tensor(name, layer)
+        return torch.as_tensor(_Dev(ptr, nb), device="cuda").view(dt).float().cpu().numpy()
+
+    bf = lambda a: torch.tensor(np.asarray(a, np.float32)).to(torch.bfloat16).float().numpy()  # noqa: E731
+    up = t["llm.model.layers.2.mixer.experts.gate_and_up_projs"]
+    assert np.array_equal(get("fc1.w", 2).reshape(c.experts, c.moe_inter, c.hidden), bf(up.transpose(0, 2, 1)))
+    qkv = np.concatenate([t[f"llm.model.layers.1.mixer.{n}_proj.weight"] for n in "qkv"])
+    assert np.array_equal(get("qkv.w", 1).reshape(qkv.shape), bf(qkv))
+    conv = t["llm.model.layers.0.mixer.conv1d.weight"]
+    assert np.array_equal(get("conv_w", 0).reshape(conv.shape[0], -1), bf(conv.reshape(conv.shape[0], -1)))
+    assert np.array_equal(get("router", 2, torch.float32), t["llm.model.layers.2.mixer.gate.weight"].astype(np.float32).reshape(-1))
+    assert np.array_equal(get("mtp.final_norm", -1), bf(t["llm.mtp.layers.1.final_layernorm.weight"]))
+    assert len(m.forward(tokens=[1, 2, 3], pos=0, logits_rows=3)) == 3
+    m.close()
+    m4 = C.load_nh([p], small_nh_cfg(bits=4))
+    assert len(m4.forward(tokens=[1, 2, 3], pos=0, logits_rows=1)) == 1
+    m4.close()

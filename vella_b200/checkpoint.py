@@ -34,6 +34,8 @@ for _name, _res, _args in [
     ("vella_whisper_load", ctypes.c_int, [_vp, _vp]),
     ("vella_model_check_checkpoint", ctypes.c_int, [_vp, _vp]),
     ("vella_model_load", ctypes.c_int, [_vp, _vp]),
+    ("vella_nh_check_checkpoint", ctypes.c_int, [_vp, _vp]),
+    ("vella_nh_load", ctypes.c_int, [_vp, _vp]),
 ]:
     _lib.declare(_name, _res, _args)
 
@@ -314,6 +316,32 @@ def load_model(model_dir, bits: Optional[int] = None, dtype: Optional[int] = Non
         m = Model(cfg, device)
         try:
             _lib.check(_lib.lib().vella_model_load(m.handle, st.h))
+        except Exception:
+            m.close()
+            raise
+    return m
+
+
+
+# ---------------------------------------------------------------------------------------
+# Nemotron-H (NeMo or MLX layout)
+# ---------------------------------------------------------------------------------------
+
+def check_nh_checkpoint(st: SafeTensors, cfg) -> None:
+    """Raises VellaError naming the first missing or mis-shaped tensor of a Nemotron-H checkpoint."""
+    c = cfg.c()
+    _lib.check(_lib.lib().vella_nh_check_checkpoint(st.h, ctypes.byref(c)))
+
+
+def load_nh(paths, cfg, device: int = 0):
+    """A Nemotron-H backbone handle (``vella_b200.nemotron.NHModel``) with the weights of the
+    safetensors files (in the order given)."""
+    from .nemotron import NHModel
+    with SafeTensors([str(p) for p in paths]) as st:
+        check_nh_checkpoint(st, cfg)
+        m = NHModel(cfg, device)
+        try:
+            _lib.check(_lib.lib().vella_nh_load(m.h, st.h))
         except Exception:
             m.close()
             raise

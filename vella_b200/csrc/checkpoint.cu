@@ -404,6 +404,7 @@ std::string hf_key(const std::string& k) {
 // Canonical (Hugging Face) name -> entry, and whether conv weights are PyTorch [out, in, k].
 struct KeyView {
   std::unordered_map<std::string, const StEntry*> by;
+  std::unordered_map<std::string, bool> transposed;  // stacked experts stored [E][in][out] (NeMo)
   bool hf = true;
   bool quantized = false;  // some tensor has MLX-affine scales (an already-quantized checkpoint)
   const StEntry* get(const std::string& k) const {
@@ -534,6 +535,100 @@ struct Loader {
     std::vector<uint16_t> h((size_t)n);
     for (int64_t i = 0; i < n; ++i) h[(size_t)i] = act_bits(elem_f(*e, (size_t)i), act);
     return put(d, h.data(), h.size() * 2);
+  }
+
+  // a float tensor of n elements (any of `shapes`) into an fp32 destination (routers, A_log, D, dt_bias)
+  int f32(const std::string& dname, int layer, const std::string& key, int64_t n) {
+    const StEntry* e = need(key);
+    if (!e) return VELLA_E_INVALID;
+    if (!is_float(*e) || (int64_t)e->numel() != n)
+      return fail(VELLA_E_INVALID, "checkpoint: '%s' must be a float tensor of %lld elements", key.c_str(), (long long)n);
+    void* d = nullptr;
+    int rc = dest(dname, layer, (size_t)n * 4, &d);
+    if (rc || !w) return rc;
+    std::vector<float> h((size_t)n);
+    for (int64_t i = 0; i < n; ++i) h[(size_t)i] = elem_f(*e, (size_t)i);
+    return put(d, h.data(), h.size() * 4);
+  }
+
+  // a float tensor of n elements into an activation-dtype destination, element order kept (a
+  // [C, 1, K] or [C, K, 1] depthwise conv weight is [C][K] in memory either way)
+  int flat(const std::string& dname, int layer, const std::string& key, int64_t n) {
+    const StEntry* e = need(key);
+    if (!e) return VELLA_E_INVALID;
+    if (!is_float(*e) || (int64_t)e->numel() != n)
+      return fail(VELLA_E_INVALID, "checkpoint: '%s' must be a float tensor of %lld elements", key.c_str(), (long long)n);
+    void* d = nullptr;
+    int rc = dest(dname, layer, (size_t)n * 2, &d);
+    if (rc || !w) return rc;
+    std::vector<uint16_t> h((size_t)n);
+    for (int64_t i = 0; i < n; ++i) h[(size_t)i] = act_bits(elem_f(*e, (size_t)i), act);
+    return put(d, h.data(), h.size() * 2);
+  }
+
+  // stacked experts [E][N][K] (or [E][K][N] when the view marks the key transposed): float
+  // (quantized at load for an int handle, or stored dense), or MLX-affine at the handle's bits
+  int experts(const std::string& dname, int layer, const std::string& key, int64_t E, int64_t N, int64_t K, int bits) {
+    const StEntry* W = need(key + ".weight");
+    if (!W) return VELLA_E_INVALID;
+    const StEntry* S = v.get(key + ".scales");
+    const StEntry* B = v.get(key + ".biases");
+    const auto ti = v.transposed.find(key + ".weight");
+    const bool tr = ti != v.transposed.end() && ti->second;
+    const size_t wb = bits ? (size_t)(E * N) * (size_t)(K * bits / 32) * 4 : (size_t)(E * N * K) * 2;
+    const size_t sb = bits ? (size_t)(E * N) * (size_t)(K / 64) * 2 : 0;
+    if (S) {
+      if (tr || !B || W->dtype != VELLA_ST_U32 || !bits || !shape_is(W, {E, N, K * bits / 32}) ||
+          !shape_is(S, {E, N, K / 64}) || !shape_is(B, {E, N, K / 64}) || !is_float(*S) || !is_float(*B))
+        return fail(VELLA_E_UNSUPPORTED, "checkpoint: '%s' must be MLX-affine [%lld, %lld, %lld] at %d bits",
+                    key.c_str(), (long long)E, (long long)N, (long long)K, bits);
+      void *dw = nullptr, *ds = nullptr, *db = nullptr;
+      int rc;
+      if ((rc = dest(dname + ".w", layer, wb, &dw)) || (rc = dest(dname + ".s", layer, sb, &ds)) ||
+          (rc = dest(dname + ".b", layer, sb, &db)) || !w)
+        return rc;
+      std::vector<uint16_t> hs(sb / 2), hb(sb / 2);
+      for (size_t g = 0; g < hs.size(); ++g) {
+        hs[g] = act_bits(elem_f(*S, g), act);
+        hb[g] = act_bits(elem_f(*B, g), act);
+      }
+      if ((rc = put(dw, W->data, wb)) || (rc = put(ds, hs.data(), sb))) return rc;
+      return put(db, hb.data(), sb);
+    }
+    if (!is_float(*W) || !(tr ? shape_is(W, {E, K, N}) : shape_is(W, {E, N, K})))
+      return fail(VELLA_E_INVALID, "checkpoint: '%s.weight' must be a float [%lld, %lld, %lld]%s", key.c_str(),
+                  (long long)E, (long long)(tr ? K : N), (long long)(tr ? N : K), tr ? " (in, out)" : "");
+    if (!w) {
+      void* dummy = nullptr;
+      return dest(dname + ".w", layer, wb, &dummy);
+    }
+    // [E * N][K] rows in fp32 (transposed when needed), then dense or quantized at load
+    std::vector<float> rows((size_t)(E * N * K));
+    for (int64_t e = 0; e < E; ++e)
+      for (int64_t n = 0; n < N; ++n)
+        for (int64_t k = 0; k < K; ++k)
+          rows[(size_t)((e * N + n) * K + k)] = elem_f(*W, tr ? (size_t)((e * K + k) * N + n) : (size_t)((e * N + n) * K + k));
+    void *dw = nullptr, *ds = nullptr, *db = nullptr;
+    int rc;
+    if ((rc = dest(dname + ".w", layer, wb, &dw))) return rc;
+    if (!bits) {
+      std::vector<uint16_t> h(rows.size());
+      for (size_t i = 0; i < rows.size(); ++i) h[i] = act_bits(rows[i], act);
+      return put(dw, h.data(), h.size() * 2);
+    }
+    if ((rc = dest(dname + ".s", layer, sb, &ds)) || (rc = dest(dname + ".b", layer, sb, &db))) return rc;
+    void* tmp = nullptr;
+    VELLA_CUDA_TRY(cudaMalloc(&tmp, rows.size() * 4));
+    vella_qgemm_desc qd{};
+    qd.m = 1; qd.n = (int32_t)(E * N); qd.k = (int32_t)K; qd.bits = bits; qd.group_size = 64; qd.dtype = act;
+    cudaError_t ce = cudaMemcpyAsync(tmp, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice, stream);
+    if (ce == cudaSuccess) {
+      rc = vella_quantize(&qd, VELLA_F32, tmp, dw, ds, db, stream);
+      ce = cudaStreamSynchronize(stream);
+    }
+    cudaFree(tmp);
+    if (rc) return rc;
+    return ce == cudaSuccess ? VELLA_OK : vella::cuda_fail(ce, "checkpoint load: quantize experts");
   }
 
   // a [rows, d] position table: the first `rows` rows of the checkpoint's table
@@ -885,6 +980,134 @@ int model_tensors(Loader& L, const vella_model_cfg& c) {
   return VELLA_OK;
 }
 
+// Nemotron-H (NemotronTranscribeKeys.map, NemotronTranscribeText.swift:369-397; NTMTP.nvidiaKeys,
+// NemotronTranscribeDecoder.swift:608-626): NVIDIA's NeMo keys (llm.model.*, llm.mtp.*) or the
+// MLX module tree (llm.backbone.*, mtp.*), onto backbone.* / lm_head / mtp.* names; NeMo's stacked
+// experts are [E][in][out] (marked transposed); a depthwise conv weight is [C][K] in memory in
+// every layout.
+KeyView nh_view(const vella_st* st) {
+  KeyView v;
+  static const std::pair<const char*, const char*> mtp_keys[] = {
+      {"llm.mtp.layers.0.eh_proj.weight", "mtp.eh_proj.weight"},
+      {"llm.mtp.layers.0.enorm.weight", "mtp.enorm.weight"},
+      {"llm.mtp.layers.0.hnorm.weight", "mtp.hnorm.weight"},
+      {"llm.mtp.layers.0.norm.weight", "mtp.attn_norm.weight"},
+      {"llm.mtp.layers.0.mixer.q_proj.weight", "mtp.attn.q_proj.weight"},
+      {"llm.mtp.layers.0.mixer.k_proj.weight", "mtp.attn.k_proj.weight"},
+      {"llm.mtp.layers.0.mixer.v_proj.weight", "mtp.attn.v_proj.weight"},
+      {"llm.mtp.layers.0.mixer.o_proj.weight", "mtp.attn.o_proj.weight"},
+      {"llm.mtp.layers.1.norm.weight", "mtp.moe_norm.weight"},
+      {"llm.mtp.layers.1.mixer.gate.weight", "mtp.moe.gate.weight"},
+      {"llm.mtp.layers.1.mixer.gate.e_score_correction_bias", "mtp.moe.gate.e_score_correction_bias"},
+      {"llm.mtp.layers.1.mixer.shared_experts.up_proj.weight", "mtp.moe.shared_experts.up_proj.weight"},
+      {"llm.mtp.layers.1.mixer.shared_experts.down_proj.weight", "mtp.moe.shared_experts.down_proj.weight"},
+      {"llm.mtp.layers.1.mixer.experts.gate_and_up_projs", "mtp.moe.switch_mlp.fc1.weight"},
+      {"llm.mtp.layers.1.mixer.experts.down_projs", "mtp.moe.switch_mlp.fc2.weight"},
+      {"llm.mtp.layers.1.final_layernorm.weight", "mtp.final_norm.weight"}};
+  auto replace_all = [](std::string k, const char* from, const char* to) {
+    for (size_t at = k.find(from); at != std::string::npos; at = k.find(from, at + std::strlen(to)))
+      k.replace(at, std::strlen(from), to);
+    return k;
+  };
+  for (const StEntry& e : st->entries) {
+    std::string k = e.name;
+    bool tr = false, known = false;
+    for (const auto& mk : mtp_keys)
+      if (k == mk.first) {
+        tr = starts(k, "llm.mtp.") && k.size() > 6 && k.compare(k.size() - 6, 6, "_projs") == 0;
+        k = mk.second;
+        known = true;
+      }
+    if (!known) {
+      if (starts(k, "llm.mtp.") || starts(k, "ctc_timestamp.") || k.find("._extra_state") != std::string::npos) continue;
+      if (starts(k, "llm.model.")) {
+        k = replace_all(k, "llm.model.embed_tokens.", "backbone.embeddings.");
+        k = replace_all(k, "llm.model.norm.", "backbone.norm_f.");
+        k = replace_all(k, "llm.model.layers.", "backbone.layers.");
+        k = replace_all(k, "._fp32_params.", ".");
+        if (k.find(".experts.gate_and_up_projs") != std::string::npos) {
+          k = replace_all(k, ".experts.gate_and_up_projs", ".switch_mlp.fc1.weight");
+          tr = true;
+        } else if (k.find(".experts.down_projs") != std::string::npos) {
+          k = replace_all(k, ".experts.down_projs", ".switch_mlp.fc2.weight");
+          tr = true;
+        }
+      } else if (starts(k, "llm.")) {
+        k = k.substr(4);  // llm.backbone.* / llm.lm_head.*
+      }
+    }
+    v.by[k] = &e;
+    if (tr) v.transposed[k] = true;
+    if (k.size() > 7 && k.compare(k.size() - 7, 7, ".scales") == 0) v.quantized = true;
+  }
+  return v;
+}
+
+int nh_attention_tensors(Loader& L, const vella_nh_cfg& c, const std::string& p, const std::string& dq, int layer) {
+  const int64_t d = c.hidden, hd = c.head_dim;
+  int rc;
+  if ((rc = L.linear(dq + "qkv", layer,
+                     {{p + "q_proj", c.heads * hd, false}, {p + "k_proj", c.kv_heads * hd, false},
+                      {p + "v_proj", c.kv_heads * hd, false}},
+                     d, c.bits, d, false, false)))
+    return rc;
+  return L.linear(dq + "o", layer, {{p + "o_proj", d, false}}, c.heads * hd, c.bits, c.heads * hd, false, false);
+}
+
+int nh_moe_tensors(Loader& L, const vella_nh_cfg& c, const std::string& p, const std::string& dq, int layer) {
+  const int64_t d = c.hidden;
+  int rc;
+  if ((rc = L.f32(dq + "router", layer, p + "gate.weight", (int64_t)c.experts * d)) ||
+      (rc = L.f32(dq + "router_bias", layer, p + "gate.e_score_correction_bias", c.experts)) ||
+      (rc = L.experts(dq + "fc1", layer, p + "switch_mlp.fc1", c.experts, c.moe_inter, d, c.bits)) ||
+      (rc = L.experts(dq + "fc2", layer, p + "switch_mlp.fc2", c.experts, d, c.moe_inter, c.bits)) ||
+      (rc = L.linear(dq + "shared_up", layer, {{p + "shared_experts.up_proj", c.shared_inter, false}}, d, c.bits, d,
+                     false, false)))
+    return rc;
+  return L.linear(dq + "shared_down", layer, {{p + "shared_experts.down_proj", d, false}}, c.shared_inter, c.bits,
+                  c.shared_inter, false, false);
+}
+
+int nh_tensors(Loader& L, const vella_nh_cfg& c) {
+  const int64_t d = c.hidden, I = (int64_t)c.m_heads * c.m_head_dim;
+  const int64_t conv_dim = I + 2LL * c.groups * c.state_dim, in_w = I + conv_dim + c.m_heads;
+  int rc;
+  if ((rc = L.linear("embed", -1, {{"backbone.embeddings", c.vocab, false}}, d, 0, d, false, false)) ||
+      (rc = L.vec("norm_f", -1, "backbone.norm_f.weight", d)) ||
+      (rc = L.linear("lm_head", -1, {{"lm_head", c.vocab, false}}, d, c.bits, d, false, false)))
+    return rc;
+  const int Lcount = (int)strnlen(c.pattern, sizeof(c.pattern));
+  for (int l = 0; l < Lcount; ++l) {
+    const std::string p = "backbone.layers." + std::to_string(l) + ".";
+    if ((rc = L.vec("norm", l, p + "norm.weight", d))) return rc;
+    const std::string mx = p + "mixer.";
+    if (c.pattern[l] == 'M') {
+      if ((rc = L.linear("in_proj", l, {{mx + "in_proj", in_w, false}}, d, c.bits, d, false, false)) ||
+          (rc = L.linear("out_proj", l, {{mx + "out_proj", d, false}}, I, c.bits, I, false, false)) ||
+          (rc = L.flat("conv_w", l, mx + "conv1d.weight", conv_dim * c.conv_kernel)) ||
+          (rc = L.flat("conv_b", l, mx + "conv1d.bias", conv_dim)) ||
+          (rc = L.flat("gnorm", l, mx + "norm.weight", I)) ||
+          (rc = L.f32("a_log", l, mx + "A_log", c.m_heads)) || (rc = L.f32("dt_bias", l, mx + "dt_bias", c.m_heads)) ||
+          (rc = L.f32("D", l, mx + "D", c.m_heads)))
+        return rc;
+    } else if (c.pattern[l] == '*') {
+      if ((rc = nh_attention_tensors(L, c, mx, "", l))) return rc;
+    } else {
+      if ((rc = nh_moe_tensors(L, c, mx, "", l))) return rc;
+    }
+  }
+  if (c.mtp) {
+    if ((rc = L.linear("mtp.eh_proj", -1, {{"mtp.eh_proj", d, false}}, 2 * d, c.bits, 2 * d, false, false)) ||
+        (rc = L.vec("mtp.enorm", -1, "mtp.enorm.weight", d)) || (rc = L.vec("mtp.hnorm", -1, "mtp.hnorm.weight", d)) ||
+        (rc = L.vec("mtp.attn_norm", -1, "mtp.attn_norm.weight", d)) ||
+        (rc = L.vec("mtp.moe_norm", -1, "mtp.moe_norm.weight", d)) ||
+        (rc = L.vec("mtp.final_norm", -1, "mtp.final_norm.weight", d)) ||
+        (rc = nh_attention_tensors(L, c, "mtp.attn.", "mtp.", -1)) || (rc = nh_moe_tensors(L, c, "mtp.moe.", "mtp.", -1)))
+      return rc;
+  }
+  return VELLA_OK;
+}
+
 // Checks every key and shape, then fills the handle on a private stream of the device that
 // holds `probe` (a device pointer of the handle).
 int check_then_fill(const KeyView& v, int act, const TensorFn& tensor, const void* probe,
@@ -972,6 +1195,30 @@ int vella_whisper_load(vella_whisper* w, const vella_st* st) {
   const TensorFn fn = [w](const char* n, int l, void** p, size_t* sz) { return vella_whisper_tensor(w, n, l, p, sz); };
   rc = check_then_fill(v, c.dtype, fn, probe, [&c](Loader& L) { return whisper_tensors(L, c); });
   return rc ? rc : vella::whisper_weights_loaded(w);
+}
+
+int vella_nh_check_checkpoint(const vella_st* st, const vella_nh_cfg* cfg) {
+  if (!st || !cfg) return fail(VELLA_E_INVALID, "vella_nh_check_checkpoint: NULL argument");
+  const KeyView v = nh_view(st);
+  Loader L{TensorFn(), v, cfg->dtype};
+  return nh_tensors(L, *cfg);
+}
+
+int vella_nh_load(vella_nh* m, const vella_st* st) {
+  if (!m || !st) return fail(VELLA_E_INVALID, "vella_nh_load: NULL argument");
+  vella_nh_cfg cfg{};
+  int rc = vella_nh_get_cfg(m, &cfg);
+  if (rc) return rc;
+  void* probe = nullptr;
+  size_t b = 0;
+  if ((rc = vella_nh_tensor(m, "norm_f", -1, &probe, &b))) return rc;
+  const KeyView v = nh_view(st);
+  // the dense embedding is the tensor "embed" (the loader asks for "embed.w")
+  const TensorFn fn = [m](const char* n, int l, void** p, size_t* sz) {
+    return vella_nh_tensor(m, std::strcmp(n, "embed.w") == 0 ? "embed" : n, l, p, sz);
+  };
+  const vella_nh_cfg c = cfg;
+  return check_then_fill(v, c.dtype, fn, probe, [&c](Loader& L) { return nh_tensors(L, c); });
 }
 
 int vella_model_check_checkpoint(const vella_st* st, const vella_model_cfg* cfg) {

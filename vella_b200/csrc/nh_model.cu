@@ -385,6 +385,12 @@ int vella_nh_create(const vella_nh_cfg* cfg, int32_t device, vella_nh** out) {
   return VELLA_OK;
 }
 
+int vella_nh_get_cfg(const vella_nh* m, vella_nh_cfg* out) {
+  if (!m || !out) return fail(VELLA_E_INVALID, "vella_nh_get_cfg: NULL argument");
+  *out = m->cfg;
+  return VELLA_OK;
+}
+
 int vella_nh_destroy(vella_nh* m) {
   if (!m) return VELLA_OK;
   cudaSetDevice(m->device);
