@@ -27,6 +27,8 @@ from __future__ import annotations
 
 import numpy as np
 
+from .decoder import ends_in_loop
+
 
 def silu(x):
     x = np.asarray(x, np.float64)
@@ -337,22 +339,32 @@ def mtp_forward(c: HybridConfig, P, e, h, kv: KV):
     return x, rmsnorm(x, M["final_norm"], c.eps)
 
 
-def decode_greedy(c: HybridConfig, P, embeddings, max_tokens: int, eos=()):
-    """decodeGreedy (:266-290): the prefix, then one token per backbone step."""
+def decode_greedy(c: HybridConfig, P, embeddings, max_tokens: int, eos=(), info=None):
+    """decodeGreedy (:266-290): the prefix, then one token per backbone step, stopping at a
+    repetition loop (endsInLoop, :285 and :296-302; ``info["looped"]`` is set)."""
     cache = make_cache(c)
     t = int(head(P, backbone(c, P, embeddings, cache)[-1]))
     out = []
+    if info is not None:
+        info["looped"] = False
     while len(out) < max_tokens and t not in eos:
         out.append(t)
+        if ends_in_loop(out):
+            if info is not None:
+                info["looped"] = True
+            break
         t = int(head(P, backbone(c, P, P["embed"][[t]], cache)[-1]))
     return out
 
 
-def decode_mtp(c: HybridConfig, P, embeddings, max_tokens: int, depth: int, eos=()):
+def decode_mtp(c: HybridConfig, P, embeddings, max_tokens: int, depth: int, eos=(), info=None):
     """decodeMTP (:306-396): depth chained MTP drafts verified by one backbone pass; on a
     partial acceptance the Mamba states go back to the pass's snapshot, the attention caches
     drop the whole feed, and the accepted prefix is fed again with the next drafts; the MTP
-    cache drops its depth - 1 chain entries every pass.  Returns (tokens, accepted counts)."""
+    cache drops its depth - 1 chain entries every pass; the decode stops at a repetition loop
+    (endsInLoop, :390; ``info["looped"]`` is set).  Returns (tokens, accepted counts)."""
+    if info is not None:
+        info["looped"] = False
     cache, mcache = make_cache(c), KV()
     post = backbone(c, P, embeddings, cache)
     t = int(head(P, post[-1]))
@@ -404,5 +416,9 @@ def decode_mtp(c: HybridConfig, P, embeddings, max_tokens: int, depth: int, eos=
                 return out, hist
             out.append(tok)
             if len(out) >= max_tokens:
+                return out, hist
+            if ends_in_loop(out):
+                if info is not None:
+                    info["looped"] = True
                 return out, hist
     return out, hist

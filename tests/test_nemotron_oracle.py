@@ -142,8 +142,13 @@ class _OracleNH:
         if kv.k is not None:
             kv.trim(kv.k.shape[0] - pos)
 
+    def _rows(self, n, what):  # the device handle's row limit (vella_nh_forward / vella_nh_mtp_forward)
+        if not 1 <= n <= self.cfg.max_rows:
+            raise ValueError(f"{what}: {n} rows (max_rows {self.cfg.max_rows})")
+
     def forward(self, tokens=None, embeds=None, pos=0, logits_rows=1, logits_out=None, hidden_out=None):
         x = self.P["embed"][list(tokens)] if tokens is not None else embeds.numpy().astype(np.float64)
+        self._rows(x.shape[0], "forward")
         for lc in self.cache:
             if isinstance(lc, N.KV):
                 self._at(lc, pos)
@@ -154,6 +159,7 @@ class _OracleNH:
 
     def mtp_forward(self, hidden, pos, next_tokens=None, next_embeds=None, logits_rows=1, x_out=None):
         e = self.P["embed"][list(next_tokens)] if next_tokens is not None else next_embeds.numpy().astype(np.float64)
+        self._rows(e.shape[0], "mtp_forward")
         self._at(self.mkv, pos)
         x, xo = N.mtp_forward(self.c, self.P, e, hidden.numpy().astype(np.float64), self.mkv)
         if x_out is not None:
@@ -178,3 +184,122 @@ def test_device_decode_loops_follow_the_reference_on_the_oracle():
         for depth in (2, 3):
             got, hist = VN.decode_mtp(fake, torch.tensor(emb), 24, depth)
             assert got == want, (seed, depth)
+
+
+def test_mtp_loop_commits_the_prefix_when_the_feed_would_pass_max_rows():
+    """With a large vocabulary the random MTP head's drafts almost never match, so the re-fed
+    prefix grows by one token every pass; with max_rows 8 the loop must commit it (forward it
+    again after the Mamba restore) long before 40 tokens, and still emit the oracle's greedy
+    tokens.  The oracle-backed handle rejects feeds above max_rows, as the device does."""
+    import dataclasses
+
+    import torch
+
+    from vella_b200 import nemotron as VN
+    c = dataclasses.replace(N.HybridConfig(), vocab=4000)
+    P = N.random_hybrid(c, 7)
+    emb = np.random.default_rng(7).standard_normal((11, c.hidden))
+    want = N.decode_greedy(c, P, emb, 44)
+    assert len(want) == 44
+    for depth in (2, 3):
+        fake = _OracleNH(c, P, max_rows=8)
+        got, hist = VN.decode_mtp(fake, torch.tensor(emb), 44, depth)
+        assert got == want, depth
+        assert sum(1 for a in hist if a < depth) >= 8 - depth  # enough rejections to need the commit
+        assert not fake.decode_looped
+
+
+class _ScriptedNH(_OracleNH):
+    """A handle whose greedy token at every absolute position comes from a script (the model
+    ignores its inputs), so repetition loops can be planted.  Hidden rows carry their absolute
+    position; the MTP head predicts the script's token two positions on with probability 1/2,
+    else a wrong token, so both acceptance branches run."""
+
+    def __init__(self, script, T, max_rows=8, seed=0):
+        import types
+        self.script, self.T, self.rng = list(script), T, np.random.default_rng(seed)
+        self.cfg = types.SimpleNamespace(max_rows=max_rows, hidden=4, pattern="M")
+        self.state = [np.zeros(1), np.zeros(1)]
+
+    def reset(self):
+        pass
+
+    def mamba_states(self):
+        owner = self
+
+        class _S:
+            def __init__(self, i):
+                self.i = i
+
+            def clone(self):
+                return owner.state[self.i].copy()
+
+            def copy_(self, a):
+                owner.state[self.i] = a.copy()
+
+            def zero_(self):
+                owner.state[self.i] = np.zeros(1)
+        return [_S(0), _S(1)]
+
+    def embedding_rows(self, tokens):
+        import torch
+        return torch.zeros(len(tokens), 4, dtype=torch.float64)
+
+    def _tok(self, p):  # the token at absolute position p (p >= T)
+        return self.script[p - self.T] if 0 <= p - self.T < len(self.script) else 0
+
+    def forward(self, tokens=None, embeds=None, pos=0, logits_rows=1, logits_out=None, hidden_out=None):
+        import torch
+        n = len(tokens) if tokens is not None else embeds.shape[0]
+        self._rows(n, "forward")
+        if hidden_out is not None:
+            h = torch.zeros(n, 4, dtype=hidden_out.dtype)
+            h[:, 0] = torch.arange(pos, pos + n, dtype=hidden_out.dtype)
+            hidden_out.copy_(h)
+        return [self._tok(p + 1) for p in range(pos + n - logits_rows, pos + n)]
+
+    def mtp_forward(self, hidden, pos, next_tokens=None, next_embeds=None, logits_rows=1, x_out=None):
+        import torch
+        n = hidden.shape[0]
+        self._rows(n, "mtp_forward")
+        p = [int(v) for v in hidden[:, 0].tolist()]
+        if x_out is not None:
+            x = torch.zeros(n, 4, dtype=x_out.dtype)
+            x[:, 0] = torch.tensor([q + 1 for q in p], dtype=x_out.dtype)
+            x_out.copy_(x)
+        good = [self._tok(q + 2) for q in p[n - logits_rows:]]
+        return [g if self.rng.random() < 0.5 else g + 1 for g in good]
+
+
+def test_decode_loops_stop_at_a_planted_repetition_loop():
+    """A block repeated 30 times after a few distinct tokens: greedy and MTP decoding stop where
+    the reference's endsInLoop stops (checked every 4 tokens once there are 20), keep one copy
+    of the block and set decode_looped; a script without a loop runs to max_tokens."""
+    import torch
+
+    from oracle import decoder as D
+    from vella_b200 import nemotron as VN
+    T = 6
+    emb = torch.zeros(T, 4, dtype=torch.float64)
+    for script in ([5, 6, 7, 8, 9] + [21, 22, 23] * 30, [3, 4] + [11] * 40, list(range(100, 190))):
+        want, looped = [], False
+        for tok in script[:80]:
+            want.append(tok)
+            if D.ends_in_loop(want):
+                looped = True
+                break
+        h = _ScriptedNH(script, T)
+        assert VN.decode_greedy(h, emb, 80) == want and h.decode_looped == looped, script[:8]
+        for depth in (2, 3):
+            h = _ScriptedNH(script, T, seed=depth)
+            got, _ = VN.decode_mtp(h, emb, 80, depth)
+            assert got == want and h.decode_looped == looped, (script[:8], depth)
+    # the oracle's own loops stop the same way
+    c = N.HybridConfig()
+    P = N.random_hybrid(c, 1)
+    P["lm_head"] = np.zeros_like(P["lm_head"])  # every argmax is token 0: a loop of one token
+    emb2 = np.random.default_rng(1).standard_normal((5, c.hidden))
+    info = {}
+    assert N.decode_greedy(c, P, emb2, 64, info=info) == [0] and info["looped"]
+    got, _ = N.decode_mtp(c, P, emb2, 64, 2, info=info)
+    assert got == [0] and info["looped"]

@@ -91,10 +91,11 @@ extern "C" int vella_qgemm_noalloc(const vella_qgemm_desc* desc, const void* x, 
       (quant && (!aligned(scales, 2) || !aligned(biases, 2))))
     return fail(VELLA_E_INVALID, "vella_qgemm_noalloc: 16-bit operands must be 2-byte aligned");
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  void* ws = nullptr;
-  if (plan.workspace) {
-    const int rc = noalloc_scratch(s, &ws);
-    if (rc != VELLA_OK) return rc;
-  }
+  // the set-up runs on every call, whether or not this shape's plan uses the scratch, so the
+  // first call on a device (whatever its shape) is the one that looks the array up and clears it
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(s, &scratch);
+  if (rc != VELLA_OK) return rc;
+  void* ws = plan.workspace ? scratch : nullptr;
   return qgemm_launch(d, plan, x, w, scales, biases, up_w, up_scales, up_biases, bias, residual, out, ws, s);
 }

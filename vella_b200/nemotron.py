@@ -114,7 +114,9 @@ class MoeExpertsDesc(ctypes.Structure):
 
 
 _lib.declare("vella_moe_experts_workspace_size", ctypes.c_size_t, [ctypes.POINTER(MoeExpertsDesc)])
-_lib.declare("vella_moe_experts", ctypes.c_int, [ctypes.POINTER(MoeExpertsDesc)] + [_vp] * 11 + [ctypes.c_int32, _vp,
+# desc, x, expert_idx, expert_w, fc1 (w, scales, biases), fc2 (w, scales, biases), out; accumulate, workspace,
+# workspace_bytes, stream
+_lib.declare("vella_moe_experts", ctypes.c_int, [ctypes.POINTER(MoeExpertsDesc)] + [_vp] * 10 + [ctypes.c_int32, _vp,
                                                                                                ctypes.c_size_t, _vp])
 
 
@@ -285,10 +287,34 @@ class NHModel:
         return views
 
 
+_lib.declare("vella_loop_cut", ctypes.c_int, [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.POINTER(ctypes.c_int32)])
+
+
+def ends_in_loop(out: list) -> bool:
+    """endsInLoop (NemotronTranscribeModel.swift:296-302) through the library's repetition guard
+    (vella_loop_cut): once there are at least 20 tokens and their count is a multiple of 4, a tail
+    of one block of at most 64 tokens repeated 20 times is cut to its first copy, in place, and
+    True is returned."""
+    n = len(out)
+    arr = (ctypes.c_int32 * max(n, 1))(*out)
+    kept = ctypes.c_int32(n)
+    rc = _lib.lib().vella_loop_cut(arr, n, 1, ctypes.byref(kept))
+    if rc < 0:
+        _lib.check(rc)
+    if rc == 1:
+        del out[kept.value:]
+        return True
+    return False
+
+
 def decode_greedy(model: NHModel, embeddings, max_tokens: int, eos=()):
     """decodeGreedy (NemotronTranscribeModel.swift:266-290) on the device: the prefix in chunks
-    of max_rows, then one token per forward."""
+    of max_rows, then one token per forward.  Like the reference, the decode stops at a
+    repetition loop (ends_in_loop after every token), keeps one copy of the repeated block and
+    sets ``model.decode_looped`` (the reference's ``decodeLooped``)."""
     R, T = model.cfg.max_rows, embeddings.shape[0]
+    model.decode_looped = False
     model.reset()
     t = None
     for s0 in range(0, T, R):
@@ -296,6 +322,9 @@ def decode_greedy(model: NHModel, embeddings, max_tokens: int, eos=()):
     out, pos = [], T
     while len(out) < max_tokens and t not in eos:
         out.append(t)
+        if ends_in_loop(out):
+            model.decode_looped = True
+            break
         t = model.forward(tokens=[t], pos=pos)[0]
         pos += 1
     return out
@@ -305,11 +334,22 @@ def decode_mtp(model: NHModel, embeddings, max_tokens: int, depth: int, eos=()):
     """decodeMTP (NemotronTranscribeModel.swift:306-396) on the device: depth chained MTP drafts
     verified in one forward; on a partial acceptance the Mamba states are restored from the
     pass's snapshot and the accepted prefix is fed again (the attention rows are overwritten);
-    the MTP cache drops its depth - 1 chain rows every pass.  Returns (tokens, accepted counts)."""
+    the MTP cache drops its depth - 1 chain rows every pass.  Returns (tokens, accepted counts).
+
+    Two points where the device handle differs from MLX, which takes a feed of any length:
+    vella_nh_forward takes at most max_rows rows, so once the re-fed prefix plus the next drafts
+    would pass max_rows, the accepted prefix is committed instead (forwarded again after the
+    restore, in chunks of at most max_rows, which leaves the Mamba states and attention rows
+    where the reference's next verify pass would leave them) and only the bonus token stays
+    pending; and, as in the reference, the decode stops at a repetition loop (ends_in_loop after
+    every emitted token) and sets ``model.decode_looped``."""
     import torch
     R, T, d = model.cfg.max_rows, embeddings.shape[0], model.cfg.hidden
+    if depth + 1 > R:
+        raise ValueError(f"decode_mtp: depth {depth} needs max_rows >= {depth + 1} (max_rows {R})")
     dev = embeddings.device
     hs = torch.empty(T, d, dtype=embeddings.dtype, device=dev)
+    model.decode_looped = False
     model.reset()
     t = None
     for s0 in range(0, T, R):
@@ -364,11 +404,20 @@ def decode_mtp(model: NHModel, embeddings, max_tokens: int, depth: int, eos=()):
         else:
             for v, s in zip(model.mamba_states(), snapshot):
                 v.copy_(s)
-            pending, mtp_done = fed[:upto] + [bonus], upto
+            if upto + 1 + depth > R:
+                # commit the accepted prefix: the next feed would not fit in max_rows rows
+                for c0 in range(0, upto, R):
+                    model.forward(tokens=fed[c0:min(upto, c0 + R)], pos=blen + c0, logits_rows=0)
+                pending, mtp_done, blen = [bonus], 0, blen + upto
+            else:
+                pending, mtp_done = fed[:upto] + [bonus], upto
         for tok in new:
             if tok in eos:
                 return out, hist
             out.append(tok)
             if len(out) >= max_tokens:
+                return out, hist
+            if ends_in_loop(out):
+                model.decode_looped = True
                 return out, hist
     return out, hist
