@@ -311,6 +311,15 @@ VELLA_API int vella_spec_decode(vella_spec* spec, int32_t mode, int32_t max_toke
 VELLA_API int vella_spec_decode_batch(vella_spec* spec, int32_t mode, int32_t max_tokens, int32_t* out_tokens,
                                       int32_t* n_out);
 VELLA_API int vella_spec_get_stats(const vella_spec* spec, vella_spec_stats* out);
+/* Device pointer and size of a decoder buffer, for inspecting the last pass (no counterpart in
+ * the reference, whose decode state is MLX arrays the caller can read; the parity tests replay
+ * a pass's acceptance from these).  Names: "draft_rows" [K or tree nodes][S][vocab] the draft
+ * logits rows the last pass sampled from (temperature > 0 with the model draft), "draft_stats"
+ * their (max, sum) float pairs, "tokens" [S][max_seq] int32 (committed tokens, and beyond the
+ * committed length the last pass's rejected drafts), "tree_tokens" [S][nodes] int32,
+ * "tree_topology" int32 depth[nodes] | first_child[nodes] | n_child[nodes].  The buffers
+ * belong to the decoder; the next call rewrites them. */
+VELLA_API int vella_spec_tensor(vella_spec* spec, const char* name, void** ptr, size_t* bytes);
 /* Test hook mirroring VELLA_TEST_OPTIMIZED_FAULT (NemotronTranscribeModel.swift:398-399). */
 VELLA_API int vella_spec_set_fault(vella_spec* spec, int32_t fault);
 /* Clear the sticky fallback and the statistics. */

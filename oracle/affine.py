@@ -26,6 +26,8 @@ test ``NemotronTranscribeDerivationTests.swift:134-138`` bounds the resulting er
 """
 from __future__ import annotations
 
+import contextlib
+
 import numpy as np
 
 GROUP = 64
@@ -171,8 +173,26 @@ def error_in_steps(source, packed, scales, biases, bits: int, dtype: str = "bf16
 EPILOGUES = ("none", "bias", "residual", "biasResidual", "siluGate", "biasGelu", "biasGeluResidual")
 
 
+_ENGINE = ["numpy"]
+
+
+@contextlib.contextmanager
+def c_accumulation():
+    """Inside the block, bf16 GEMM accumulations run in the C restatement of the same product
+    form (``oracle/c/oracle_gemm.c``, OpenMP over output rows), for model-sized shapes where
+    numpy takes minutes; fp16 ones stay in numpy."""
+    _ENGINE.append("c")
+    try:
+        yield
+    finally:
+        _ENGINE.pop()
+
+
 def _affine_acc(x32: np.ndarray, packed, scales, biases, bits: int, dtype: str, chunk: int = 4096):
     """fp32 accumulators [M, N] in product form: sum_g s*sum(x*q) + b*sum(x)."""
+    if _ENGINE[-1] == "c" and dtype == "bf16":
+        from . import cgemm
+        return cgemm.qgemm(x32, packed, scales, biases, bits)
     m, k = x32.shape
     g = k // GROUP
     xg = x32.reshape(m, g, GROUP)
@@ -191,6 +211,9 @@ def _affine_acc(x32: np.ndarray, packed, scales, biases, bits: int, dtype: str, 
 
 
 def _dense_acc(x32: np.ndarray, w, dtype: str) -> np.ndarray:
+    if _ENGINE[-1] == "c" and dtype == "bf16":
+        from . import cgemm
+        return cgemm.gemm_dense(x32, w)
     return x32 @ from_storage(w, dtype).T
 
 

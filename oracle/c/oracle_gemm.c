@@ -9,6 +9,7 @@
  * fp32 (the caller rounds).
  */
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 static inline float bf16_to_f32(uint16_t v) {
@@ -18,42 +19,50 @@ static inline float bf16_to_f32(uint16_t v) {
   return f;
 }
 
-/* out[M, N] = x[M, K] . W^T, W MLX-affine (bits 4 | 8), scales/biases as bf16 bits. */
-void oracle_qgemm_bf16(int M, int N, int K, int bits, const float* x, const uint32_t* w, const uint16_t* scales,
-                       const uint16_t* biases, float* out) {
+/* Rows of x are processed in blocks of this many, each block's accumulators in registers. */
+#define ORACLE_MB 16
+
+/* out[M, N] = x[M, K] . W^T, W MLX-affine (bits 4 | 8), scales/biases as bf16 bits.
+ * Returns 0, or -1 when the group sums cannot be allocated. */
+int oracle_qgemm_bf16(int M, int N, int K, int bits, const float* x, const uint32_t* w, const uint16_t* scales,
+                      const uint16_t* biases, float* out) {
   const int G = K / 64, per = 32 / bits, wpr = K / per;
   const uint32_t mask = (1u << bits) - 1u;
   /* per-row group sums of x, shared by all output rows */
-  float xs[16 * 1024];
-  float* xsum = (M * G <= 16 * 1024) ? xs : 0;
-  if (!xsum) return;
+  float* xsum = (float*)malloc((size_t)(M > 0 ? M : 1) * (G > 0 ? G : 1) * sizeof(float));
+  if (!xsum) return -1;
   for (int m = 0; m < M; ++m)
     for (int g = 0; g < G; ++g) {
       float s = 0.0f;
       for (int k = 0; k < 64; ++k) s += x[(size_t)m * K + g * 64 + k];
-      xsum[m * G + g] = s;
+      xsum[(size_t)m * G + g] = s;
     }
 #pragma omp parallel for schedule(static)
   for (int n = 0; n < N; ++n) {
-    float acc[16];
-    for (int m = 0; m < M; ++m) acc[m] = 0.0f;
     const uint32_t* row = w + (size_t)n * wpr;
-    for (int g = 0; g < G; ++g) {
-      float q[64];
-      for (int i = 0; i < 64 / per; ++i) {
-        const uint32_t word = row[g * (64 / per) + i];
-        for (int j = 0; j < per; ++j) q[i * per + j] = (float)((word >> (bits * j)) & mask);
+    for (int m0 = 0; m0 < M; m0 += ORACLE_MB) {
+      const int mb = M - m0 < ORACLE_MB ? M - m0 : ORACLE_MB;
+      float acc[ORACLE_MB];
+      for (int m = 0; m < mb; ++m) acc[m] = 0.0f;
+      for (int g = 0; g < G; ++g) {
+        float q[64];
+        for (int i = 0; i < 64 / per; ++i) {
+          const uint32_t word = row[g * (64 / per) + i];
+          for (int j = 0; j < per; ++j) q[i * per + j] = (float)((word >> (bits * j)) & mask);
+        }
+        const float s = bf16_to_f32(scales[(size_t)n * G + g]), b = bf16_to_f32(biases[(size_t)n * G + g]);
+        for (int m = 0; m < mb; ++m) {
+          const float* xr = x + (size_t)(m0 + m) * K + g * 64;
+          float d = 0.0f;
+          for (int k = 0; k < 64; ++k) d += xr[k] * q[k];
+          acc[m] += s * d + b * xsum[(size_t)(m0 + m) * G + g];
+        }
       }
-      const float s = bf16_to_f32(scales[(size_t)n * G + g]), b = bf16_to_f32(biases[(size_t)n * G + g]);
-      for (int m = 0; m < M; ++m) {
-        const float* xr = x + (size_t)m * K + g * 64;
-        float d = 0.0f;
-        for (int k = 0; k < 64; ++k) d += xr[k] * q[k];
-        acc[m] += s * d + b * xsum[m * G + g];
-      }
+      for (int m = 0; m < mb; ++m) out[(size_t)(m0 + m) * N + n] = acc[m];
     }
-    for (int m = 0; m < M; ++m) out[(size_t)m * N + n] = acc[m];
   }
+  free(xsum);
+  return 0;
 }
 
 /* out[M, N] = x[M, K] . W^T, W dense bf16 bits [N, K]. */

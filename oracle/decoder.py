@@ -278,3 +278,177 @@ def oracle_proposal(seed: int, pass_index: int, depth: int, reference_token, p: 
     if u01(r[0]) < np.float32(p) and reference_token is not None:
         return int(reference_token)
     return min(int(np.float32(u01(r[1])) * np.float32(vocab)), vocab - 1)
+
+
+# ---------------------------------------------------------------------------------------
+# Stochastic acceptance (temperature > 0) and tree verification
+# ---------------------------------------------------------------------------------------
+# The reference's draft-and-verify is greedy only (NemotronTranscribeModel.swift:364-369).
+# The sampled forms follow the published algorithms: speculative sampling (Leviathan, Kalman
+# and Matias, ICML 2023; Chen et al. 2023) -- draft x ~ q, accept with probability
+# min(1, p(x) / q(x)), on rejection draw from the normalised max(0, p - q), after K
+# acceptances draw the bonus from p -- and multi-candidate tree verification (SpecInfer,
+# Miao et al. 2023) -- the children of a node are tried in order against the running
+# residual r (r = p at the node; after a rejected child, r = normalise(max(0, r - q))); if
+# every child is rejected the bonus is drawn from r.  The uniforms are Philox-4x32-10 draws
+# on the counter (pass or step, position or node, purpose, stream) with the key (seed low,
+# seed high), the first 32-bit word mapped to [0, 1) by its top 24 bits.  Draws from a
+# distribution use the inverse CDF in vocabulary order: the first index whose running sum
+# exceeds u times the total.  Arithmetic here is float64; every decision also reports its
+# margin (the distance of the compared quantities, relative to their scale), so a caller
+# comparing with a float32 implementation can tell a rounding-level tie from a real
+# difference.
+
+PURPOSE_DRAFT, PURPOSE_ACCEPT, PURPOSE_RESIDUAL = 0x5A3D1, 0xACC01, 0xB0B05
+PURPOSE_FIRST, PURPOSE_STEP, PURPOSE_TREE, PURPOSE_PROPOSAL = 0xF1257, 0x57E90, 0x7EE01, 0x0D4A7
+
+
+def uniform(seed: int, a: int, b: int, purpose: int, stream: int) -> float:
+    """u in [0, 1) for the counter (a, b, purpose, stream)."""
+    r = philox4x32_10((a, b, purpose, stream), (seed & M32, (seed >> 32) & M32))
+    return u01(r[0])
+
+
+def softmax_t(logits_row, temperature: float) -> np.ndarray:
+    """softmax(l / T) in float64 of a logits row (values of the activation dtype)."""
+    z = np.asarray(logits_row, np.float64) / float(np.float32(temperature))
+    w = np.exp(z - z.max())
+    return w / w.sum()
+
+
+def icdf(weights, u: float):
+    """(index, margin) of the inverse-CDF draw from unnormalised weights w >= 0: the first v with
+    cumsum(w)[v] > u * sum(w) (the last positive weight when rounding leaves none), -1 when every
+    weight is zero.  margin = distance of u * sum(w) to the nearest bin edge / sum(w)."""
+    w = np.maximum(np.asarray(weights, np.float64), 0.0)
+    tot = w.sum()
+    if not tot > 0:
+        return -1, np.inf
+    cum = np.cumsum(w)
+    target = u * tot
+    idx = int(np.searchsorted(cum, target, side="right"))
+    if idx >= len(w):
+        idx = int(np.nonzero(w)[0][-1])
+    lo = cum[idx] - w[idx]
+    return idx, min(target - lo, cum[idx] - target) / tot
+
+
+def oracle_draft_q(vocab: int, ref_token, p: float) -> np.ndarray:
+    """q of the oracle draft: the reference token with probability p, else uniform (all uniform
+    when the position has no reference token)."""
+    q = np.full(vocab, (1.0 - p if ref_token is not None else 1.0) / vocab)
+    if ref_token is not None:
+        q[ref_token] += p
+    return q
+
+
+def sample_drafts(q_rows, temperature: float, seed: int, pass_index: int, stream: int = 0):
+    """K draft tokens of a pass, x_i ~ softmax(q_row_i / T) with u(pass, i, DRAFT, stream);
+    returns (tokens, min margin)."""
+    toks, margin = [], np.inf
+    for i, row in enumerate(q_rows):
+        t, m = icdf(softmax_t(row, temperature), uniform(seed, pass_index, i, PURPOSE_DRAFT, stream))
+        toks.append(max(t, 0))
+        margin = min(margin, m)
+    return toks, margin
+
+
+def sampled_accept(p_rows, qs, drafts, temperature: float, seed: int, pass_index: int, stream: int = 0):
+    """Speculative sampling over one pass: p_rows are the K + 1 target logits rows (row j at the
+    draft's position j), qs the K draft distributions (arrays over the vocabulary), drafts the
+    K drafted tokens.  Returns (accepted count a, bonus token, min margin)."""
+    K = len(drafts)
+    margin = np.inf
+    for j in range(K):
+        p = softmax_t(p_rows[j], temperature)
+        x = drafts[j]
+        u = uniform(seed, pass_index, j, PURPOSE_ACCEPT, stream)
+        lhs, rhs = u * qs[j][x], p[x]
+        margin = min(margin, abs(lhs - rhs) / max(lhs, rhs, 1e-300))
+        if lhs < rhs:
+            continue
+        u2 = uniform(seed, pass_index, j, PURPOSE_RESIDUAL, stream)
+        b, m = icdf(np.maximum(p - qs[j], 0.0), u2)
+        if b < 0:
+            b, m = icdf(p, u2)
+        return j, b, min(margin, m)
+    p = softmax_t(p_rows[K], temperature)
+    b, m = icdf(p, uniform(seed, pass_index, K, PURPOSE_RESIDUAL, stream))
+    return K, max(b, 0), min(margin, m)
+
+
+def tree_topology(branching):
+    """Breadth-first tree of the branching factors per depth: (depth, first_child, n_child) per
+    node, node 0 the root (the last committed token)."""
+    dep, first, nch = [0], [0], [0]
+    level = [0]
+    for d, b in enumerate(branching):
+        nxt = []
+        for u in level:
+            first[u], nch[u] = len(dep), b
+            for _ in range(b):
+                nxt.append(len(dep))
+                dep.append(d + 1)
+                first.append(0)
+                nch.append(0)
+        level = nxt
+    return np.array(dep), np.array(first), np.array(nch)
+
+
+def tree_children(q_rows, branching, temperature: float, seed: int, pass_index: int, stream: int = 0):
+    """Tree tokens of a pass drafted by sampling: every child c of node u is an independent draw
+    from softmax(q_rows[u] / T) with u(pass, c, DRAFT, stream).  q_rows maps each node with
+    children to its draft logits row.  Returns (tokens of nodes 1.., min margin)."""
+    dep, first, nch = tree_topology(branching)
+    toks = np.zeros(len(dep), np.int64)
+    margin = np.inf
+    for u in range(len(dep)):
+        if nch[u] == 0:
+            continue
+        q = softmax_t(q_rows[u], temperature)
+        for i in range(nch[u]):
+            c = first[u] + i
+            t, m = icdf(q, uniform(seed, pass_index, c, PURPOSE_DRAFT, stream))
+            toks[c] = max(t, 0)
+            margin = min(margin, m)
+    return toks, margin
+
+
+def tree_accept(p_rows, q_of, tokens, branching, temperature: float, seed: int, pass_index: int, stream: int = 0):
+    """Multi-candidate acceptance along the tree: p_rows[u] is the target's logits row at node u,
+    q_of(u) the draft distribution its children were drawn from, tokens[c] node c's token.
+    From the root, the children of the current node are tried in order: child c is accepted
+    when u(pass, c, ACCEPT) * q(x_c) < r(x_c), r the running residual (p at the node); after a
+    rejection r = normalise(max(0, r - q)).  The first accepted child becomes the current node;
+    when all are rejected, the bonus is drawn from r with u(pass, node, RESIDUAL) (from p when r
+    is all zero).  Returns (accepted path of nodes, bonus token, min margin)."""
+    dep, first, nch = tree_topology(branching)
+    path, u, margin = [], 0, np.inf
+    while True:
+        p = softmax_t(p_rows[u], temperature)
+        r = p.copy()
+        acc = -1
+        if nch[u]:
+            q = q_of(u)
+            for i in range(nch[u]):
+                c = first[u] + i
+                x = int(tokens[c])
+                ua = uniform(seed, pass_index, c, PURPOSE_ACCEPT, stream)
+                lhs, rhs = ua * q[x], r[x]
+                margin = min(margin, abs(lhs - rhs) / max(lhs, rhs, 1e-300))
+                if lhs < rhs:
+                    acc = c
+                    break
+                r = np.maximum(r - q, 0.0)
+                tot = r.sum()
+                if tot > 0:
+                    r = r / tot
+        if acc >= 0:
+            path.append(acc)
+            u = acc
+            continue
+        u2 = uniform(seed, pass_index, u, PURPOSE_RESIDUAL, stream)
+        b, m = icdf(r, u2)
+        if b < 0:
+            b, m = icdf(p, u2)
+        return path, max(b, 0), min(margin, m)

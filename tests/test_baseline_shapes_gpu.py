@@ -1,0 +1,183 @@
+"""Parity at the benchmark's own model shapes, through the C ABI, against the CPU oracle.
+
+The other decode tests use small models; these use two layers of the benchmark's models at
+their real dimensions, so the 5:1 GQA grouping with 40 query heads of 128, the 5120-wide
+residual stream, the 25600-wide MLP and the 151936-token vocabulary all run through the
+kernels the benchmark uses:
+
+* target: 2 layers of the 30B-class int4 target (d 5120, 40/8 heads of 128, FFN 25600,
+  vocab 151936, MLX-affine int4 group 64, RoPE theta 1e6), random init ~N(0, 0.02);
+* draft: 2 layers of the bf16 draft (d 2048, 16/8 heads of 128, FFN 6144, vocab 151936);
+* Whisper: one encoder and one decoder layer at large-v3-turbo shapes (d 1280, 20 heads of
+  64, FFN 5120, 128 mels, 1500 frames, vocab 51866, fp16).
+
+Bars (as in the small-model tests): teacher-forced logits max |error| <= 2e-2 on a sample
+of vocabulary rows (every position's top logit included); greedy tokens equal the
+oracle's argmax wherever its top-2 margin exceeds that tolerance; draft-and-verify emits
+exactly the greedy tokens.  The oracle's GEMM accumulations run in its C restatement
+(same product form) so the check takes seconds.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import affine as A
+from oracle import decoder as D
+from tests.test_decode_gpu import LOGIT_TOL, download, prefix_of
+
+pytestmark = pytest.mark.gpu
+
+TARGET = dict(n_layers=2, d=5120, H=40, KV=8, hd=128, ffn=25600, V=151936, bits=4)
+DRAFT = dict(n_layers=2, d=2048, H=16, KV=8, hd=128, ffn=6144, V=151936, bits=0)
+P, T = 64, 8  # prefix positions, teacher-forced tokens
+
+
+class _Dev:
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+
+class _EmbedRows:
+    """The few embedding rows the oracle reads (the 151936-row table stays on the device)."""
+
+    def __init__(self, model, d, tokens):
+        ptr, nbytes = model.tensor("embed")
+        table = torch.as_tensor(_Dev(ptr, nbytes), device="cuda").view(torch.int16).view(-1, d)
+        ids = sorted(set(int(t) for t in tokens))
+        rows = table[torch.tensor(ids, device="cuda")].cpu().numpy().view(np.uint16)
+        self.rows = {t: A.bf16_from_bits(r) for t, r in zip(ids, rows)}
+
+    def __getitem__(self, idx):
+        return np.stack([self.rows[int(i)] for i in np.atleast_1d(idx)])
+
+
+def _model(spec, seed):
+    from vella_b200 import decode as VD
+    mc = VD.ModelConfig(spec["n_layers"], spec["d"], spec["H"], spec["KV"], spec["hd"], spec["ffn"], spec["V"],
+                        bits=spec["bits"], max_seq=P + 64, max_prefix=P, rope_theta=1e6)
+    m = VD.Model(mc)
+    m.init_random(seed, 0.02)
+    oc = D.Config(spec["n_layers"], spec["d"], spec["H"], spec["KV"], spec["hd"], spec["ffn"], spec["V"],
+                  bits=spec["bits"], rope_theta=1e6)
+    return m, oc
+
+
+def _weights(model, cfg: D.Config, vocab_rows, tokens):
+    """Oracle weights of the device model: every layer, the final norm, the LM head restricted
+    to vocab_rows (its logits come out in that order) and the embedding rows of tokens."""
+    d, V = cfg.d_model, cfg.vocab
+    f = lambda a: A.bf16_from_bits(a.view(np.uint16))  # noqa: E731
+
+    def lin(name, layer, n, k, rows=None):
+        w = download(model, f"{name}.w", layer)
+        if cfg.bits:
+            out = {"w": w.view(np.uint32).reshape(n, k * cfg.bits // 32),
+                   "s": download(model, f"{name}.s", layer).view(np.uint16).reshape(n, k // 64),
+                   "b": download(model, f"{name}.b", layer).view(np.uint16).reshape(n, k // 64)}
+        else:
+            out = {"w": w.view(np.uint16).reshape(n, k)}
+        if rows is not None:
+            out = {key: np.ascontiguousarray(v[rows]) for key, v in out.items()}
+        return out
+
+    H, KV, hd, F = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn
+    W = {"embed": _EmbedRows(model, d, tokens), "final_norm": f(download(model, "final_norm")),
+         "lm_head": lin("lm_head", -1, V, d, rows=vocab_rows), "layers": []}
+    for layer in range(cfg.n_layers):
+        W["layers"].append({"attn_norm": f(download(model, "attn_norm", layer)),
+                            "mlp_norm": f(download(model, "mlp_norm", layer)),
+                            "qkv": lin("qkv", layer, (H + 2 * KV) * hd, d), "o": lin("o", layer, d, H * hd),
+                            "gate": lin("gate", layer, F, d), "up": lin("up", layer, F, d),
+                            "down": lin("down", layer, d, F)})
+    return W
+
+
+def _check_model(spec, seed):
+    """Teacher-forced logits of a P-position prefix plus T tokens against the oracle on a
+    sample of vocabulary rows (4096 random rows plus every position's device argmax)."""
+    m, oc = _model(spec, seed)
+    rng = np.random.default_rng(seed)
+    pre = prefix_of(P, oc.d_model, seed + 1)
+    toks = [int(t) for t in rng.integers(0, oc.vocab, T)]
+    got = A.bf16_from_bits(m.score(pre, toks))
+    assert got.shape == (T, oc.vocab) and np.isfinite(got).all()
+    rows = np.union1d(rng.choice(oc.vocab, 4096, replace=False), got.argmax(axis=1))
+    W = _weights(m, oc, rows, toks)
+    with A.c_accumulation():
+        ref = D.score(oc, W, A.bf16_from_bits(pre), toks, D.rope_table(P + T, oc.head_dim, oc.rope_theta))
+    err = float(np.abs(got[:, rows] - ref).max())
+    m.close()
+    return err
+
+
+def test_target_at_benchmark_dims_matches_oracle():
+    err = _check_model(TARGET, 31)
+    assert err <= LOGIT_TOL, err
+
+
+def test_draft_at_benchmark_dims_matches_oracle():
+    err = _check_model(DRAFT, 32)
+    assert err <= LOGIT_TOL, err
+
+
+def test_decode_at_benchmark_dims_follows_oracle_and_verify_equals_greedy():
+    """Greedy decoding at the target's dims (M = 1 streaming GEMMs, 5:1 GQA decode attention)
+    emits the oracle's argmax wherever its margin exceeds the tolerance, and draft-and-verify
+    with K = 4 (verify at M = 5), with the real draft and with the oracle draft, emits the same
+    tokens bit for bit."""
+    from vella_b200 import decode as VD
+    t, tc = _model(TARGET, 41)
+    d, dc = _model(DRAFT, 42)
+    pre_t, pre_d = prefix_of(P, tc.d_model, 43), prefix_of(P, dc.d_model, 44)
+    n = 12
+    sd = VD.SpecDecoder(t, d, k=4, mode=VD.DRAFT_MODEL)
+    sd.set_prefix(pre_t, pre_d, P)
+    longer = sd.decode_greedy(n + 8).tokens  # the oracle draft's continuation reaches past n
+    greedy = longer[:n]
+    assert len(greedy) == n
+    assert sd.decode_mtp(n).tokens == greedy
+    so = VD.SpecDecoder(t, d, k=4, mode=VD.DRAFT_ORACLE, oracle_p=0.7, seed=5)
+    so.set_prefix(pre_t, pre_d, P)
+    so.set_reference(longer)
+    assert so.decode_mtp(n).tokens == greedy
+    logits = A.bf16_from_bits(t.score(pre_t, greedy))
+    rows = np.union1d(np.random.default_rng(45).choice(tc.vocab, 4096, replace=False),
+                      np.concatenate([logits.argmax(axis=1), greedy]))
+    W = _weights(t, tc, rows, greedy)
+    with A.c_accumulation():
+        ref = D.score(tc, W, A.bf16_from_bits(pre_t), greedy, D.rope_table(P + n, tc.head_dim, tc.rope_theta))
+    col = {int(r): i for i, r in enumerate(rows)}
+    for j, tok in enumerate(greedy):
+        row = ref[j]
+        best = int(rows[int(np.argmax(row))])
+        assert tok == best or row[col[best]] - row[col[tok]] <= LOGIT_TOL, (j, tok, best)
+    for x in (sd, so, t, d):
+        x.close()
+
+
+def test_whisper_turbo_shapes_decoder_step_matches_oracle():
+    """One encoder and one decoder layer at large-v3-turbo shapes (fp16, dense): the encoder
+    output (relative RMS <= 1e-2) and the decoder's teacher-forced logits over a 4-token prompt
+    plus 12 tokens (max |error| <= 2e-2), cross-attention over all 1500 frames."""
+    from oracle import whisper as Wh
+    from tests.test_whisper_gpu import f16, mel_of, oracle_weights
+    from vella_b200 import whisper as VW
+    cfg = VW.WhisperConfig(n_mels=128, d_model=1280, heads=20, enc_layers=1, dec_layers=1, ffn=5120, vocab=51866,
+                           bits=0)
+    m = VW.Whisper(cfg)
+    m.init_random(9, 0.02)
+    oc = Wh.WhisperConfig(cfg.n_mels, cfg.d_model, cfg.heads, cfg.enc_layers, cfg.dec_layers, cfg.ffn, cfg.vocab,
+                          cfg.n_audio, cfg.max_target, cfg.bits, "f16", cfg.eps)
+    W = oracle_weights(m, oc)
+    mel = mel_of(oc, 10)
+    m.encode(mel)
+    enc_ref = Wh.encoder(oc, W, mel)
+    enc = f16(download(m, "enc_out")).astype(np.float32).reshape(oc.n_audio, oc.d_model)
+    assert np.isfinite(enc).all() and A.relative_rms(enc, enc_ref) <= 1e-2
+    toks = [50258, 50259, 50360, 50364] + [int(t) for t in np.random.default_rng(11).integers(0, 50000, 12)]
+    got = m.score(toks).astype(np.float32)
+    ref = Wh.score(oc, W, enc_ref, toks)
+    assert got.shape == ref.shape == (len(toks), oc.vocab)
+    err = float(np.abs(got - ref).max())
+    m.close()
+    assert err <= LOGIT_TOL, err

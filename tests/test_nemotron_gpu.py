@@ -309,11 +309,13 @@ def test_mtp_head_and_draft_and_verify_on_the_device():
     import torch
 
     from vella_b200 import nemotron as VN
-    kw = dict(vocab=16, hidden=256, heads=4, kv_heads=2, head_dim=64, m_heads=8, m_head_dim=32, groups=2,
+    # a 4-token vocabulary and parameter seed 8: on the oracle these decodes accept every draft
+    # in 18 passes, reject in the others, and one of them stops at a repetition loop
+    kw = dict(vocab=4, hidden=256, heads=4, kv_heads=2, head_dim=64, m_heads=8, m_head_dim=32, groups=2,
               moe_inter=128, shared_inter=128, experts=8, top_k=2)
     cfg = VN.NHConfig(state_dim=64, pattern="M*EM*E", routed_scaling=1.5, max_seq=160, max_rows=16, mtp=True, **kw)
     oc = N.HybridConfig(state=64, conv_k=4, norm_topk=True, scaling=1.5, pattern="M*EM*E", **kw)
-    P = _hybrid_params(oc, 3)
+    P = _hybrid_params(oc, 8)
     m = VN.NHModel(cfg)
     _upload(m, P, oc)
     # the head alone on 4 (next embedding, hidden) pairs
@@ -330,9 +332,10 @@ def test_mtp_head_and_draft_and_verify_on_the_device():
         emb = torch.tensor(np.random.default_rng(10 + seed).standard_normal((20, 256)), dtype=torch.bfloat16,
                            device="cuda")
         want = VN.decode_greedy(m, emb, 40)
+        looped = m.decode_looped
         for depth in (2, 3):
             got, hist = VN.decode_mtp(m, emb, 40, depth)
-            assert got == want, (seed, depth)
+            assert got == want and m.decode_looped == looped, (seed, depth)
             seen |= {a == depth for a in hist}
     assert seen == {True, False}
     m.close()

@@ -91,3 +91,28 @@ def test_golden_fixtures_reproduce():
         fresh = make_case(1000 + i, *spec)
         for key, val in fresh.items():
             assert np.array_equal(data[f"{name}/{key}"], val), (name, key)
+
+
+def test_c_restatement_equals_the_numpy_oracle():
+    """The oracle's C GEMM (used for model-sized checks and the CPU baseline) computes the same
+    product form as the numpy oracle: int4 / int8 / dense, row counts 1 to 40 (several blocks
+    of 16), within fp32 summation-order differences."""
+    import numpy as np
+
+    from oracle import affine as A
+    rng = np.random.default_rng(17)
+    for bits, m, n, k in [(4, 1, 96, 512), (4, 5, 130, 2048), (8, 17, 64, 1024), (4, 40, 33, 640), (0, 19, 70, 768)]:
+        x = A.to_storage(rng.standard_normal((m, k)).astype(np.float32), "bf16")
+        w = (rng.standard_normal((n, k)) * 0.05).astype(np.float32)
+        if bits:
+            p, s, b = A.quantize(w, bits)
+            ref = A.qgemm(x, p, s, b, bits=bits, raw=True)
+            with A.c_accumulation():
+                got = A.qgemm(x, p, s, b, bits=bits, raw=True)
+        else:
+            wd = A.to_storage(w, "bf16")
+            ref = A.qgemm(x, wd, bits=0, raw=True)
+            with A.c_accumulation():
+                got = A.qgemm(x, wd, bits=0, raw=True)
+        assert got.shape == ref.shape == (m, n)
+        assert np.abs(got - ref).max() <= 1e-5 * max(1.0, np.abs(ref).max()), (bits, m, n, k)

@@ -85,9 +85,10 @@ def test_every_class(bits, dtype, epi):
 
 
 @pytest.mark.parametrize("bits", [4, 8])
-@pytest.mark.parametrize("nk", [(5120, 5120), (1024, 5120), (25600, 5120), (5120, 25600)])
+@pytest.mark.parametrize("nk", [(5120, 5120), (1024, 5120), (25600, 5120), (5120, 25600), (151936, 5120)])
 def test_config2_shapes_sampled(bits, nk):
-    """Full config-2 shapes on the GPU; the oracle checks a random sample of output rows."""
+    """Full config-2 shapes on the GPU (the 151936 x 5120 LM head included: its own two-CTA-per-SM
+    plan); the oracle checks a random sample of output rows."""
     S = smallm()
     n, k = nk
     rng = np.random.default_rng(n + k + bits)

@@ -1511,6 +1511,26 @@ int vella_spec_get_stats(const vella_spec* s, vella_spec_stats* out) {
   return VELLA_OK;
 }
 
+int vella_spec_tensor(vella_spec* s, const char* name, void** ptr, size_t* bytes) {
+  last_error_slot().clear();
+  if (!s || !name || !ptr || !bytes) return fail(VELLA_E_INVALID, "vella_spec_tensor: NULL argument");
+  const std::string n(name);
+  const size_t S = (size_t)s->streams, V = (size_t)s->target->cfg.vocab;
+  const size_t qn = s->tree_nodes ? (size_t)s->tree_nodes : (size_t)s->cfg.draft_k;
+  void* p = nullptr;
+  size_t b = 0;
+  if (n == "draft_rows") { p = s->qrows; b = qn * S * V * s->target->elt; }
+  else if (n == "draft_stats") { p = s->qstats; b = qn * S * sizeof(float2); }
+  else if (n == "tokens") { p = s->tok; b = S * s->max_seq * sizeof(int); }
+  else if (n == "tree_tokens") { p = s->ttok; b = S * s->tree_nodes * sizeof(int); }
+  else if (n == "tree_topology") { p = s->tree_dev; b = 3 * (size_t)s->tree_nodes * sizeof(int); }
+  else return fail(VELLA_E_INVALID, "vella_spec_tensor: unknown name '%s'", name);
+  if (!p) return fail(VELLA_E_INVALID, "vella_spec_tensor: '%s' is not kept by this decoder's settings", name);
+  *ptr = p;
+  *bytes = b;
+  return VELLA_OK;
+}
+
 int vella_spec_set_fault(vella_spec* s, int32_t fault) {
   if (!s) return fail(VELLA_E_INVALID, "vella_spec_set_fault: NULL spec");
   s->fault = fault;

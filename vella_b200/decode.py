@@ -68,6 +68,7 @@ for _name, _res, _args in [
     ("vella_spec_decode_batch", ctypes.c_int, [_vp, _i32, _i32, _pi32, _pi32]),
     ("vella_spec_get_stats", ctypes.c_int, [_vp, ctypes.POINTER(SpecStats)]),
     ("vella_spec_set_fault", ctypes.c_int, [_vp, _i32]),
+    ("vella_spec_tensor", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_size_t)]),
     ("vella_spec_reset", ctypes.c_int, [_vp]),
 ]:
     _lib.declare(_name, _res, _args)
@@ -203,12 +204,19 @@ class SpecDecoder:
         return v.value
 
     def decode(self, max_tokens: int, mode: int = DECODE_AUTO) -> DecodeResult:
+        """One decode through vella_spec_decode.  The result's stats count this call only
+        (passes, greedy steps, fallbacks, runaway retries and the accepted-length histogram are
+        the differences of the handle's cumulative counters, which stats() returns)."""
         cap = max(max_tokens, 1)
         out = (ctypes.c_int32 * cap)()
         n, flags = ctypes.c_int32(), ctypes.c_int32()
+        before = self.stats()
         _lib.check(_lib.lib().vella_spec_decode(self.handle, mode, max_tokens, out, cap, ctypes.byref(n),
                                                 ctypes.byref(flags)))
         st = self.stats()
+        for key in ("passes", "greedy_steps", "fallbacks", "runaway_retries"):
+            st[key] -= before[key]
+        st["accepted"] = [a - b for a, b in zip(st["accepted"], before["accepted"])]
         return DecodeResult(list(out[:n.value]), flags.value, st["last_decode_ms"], st)
 
     def decode_greedy(self, max_tokens: int) -> DecodeResult:
@@ -233,6 +241,12 @@ class SpecDecoder:
                 "fallbacks": s.fallbacks, "runaway_retries": s.runaway_retries,
                 "draft_disabled": bool(s.draft_disabled), "last_decode_ms": s.last_decode_ms,
                 "last_tokens": s.last_tokens, "last_prefill_ms": s.last_prefill_ms}
+
+    def tensor(self, name: str):
+        """(device pointer, bytes) of a decoder buffer (vella_spec_tensor)."""
+        p, n = _vp(), ctypes.c_size_t()
+        _lib.check(_lib.lib().vella_spec_tensor(self.handle, name.encode(), ctypes.byref(p), ctypes.byref(n)))
+        return p.value, n.value
 
     def set_fault(self, fault: int):
         _lib.check(_lib.lib().vella_spec_set_fault(self.handle, fault))
