@@ -210,6 +210,30 @@ def _affine_acc(x32: np.ndarray, packed, scales, biases, bits: int, dtype: str, 
     return out
 
 
+def _dequant_acc(x32: np.ndarray, packed, scales, biases, bits: int, dtype: str, chunk: int = 4096):
+    """fp32 accumulators [M, N] of the dequantize-then-multiply form: every weight is first
+    rounded once to the activation dtype, W' = T(s * q + b), then sum_k x * W'.  This is the
+    form of quantized matmuls that stage dequantized weight tiles for a matrix unit (stock
+    MLX quantizedMM at large row counts, and the library's tensor-core GEMM for calls above 16
+    rows); the GEMV form above keeps s and b outside the sum."""
+    if _ENGINE[-1] == "c" and dtype == "bf16":
+        from . import cgemm
+        return cgemm.qgemm_tile(x32, packed, scales, biases, bits)
+    m, k = x32.shape
+    g = k // GROUP
+    s = from_storage(scales, dtype).astype(np.float64)
+    b = from_storage(biases, dtype).astype(np.float64)
+    n = packed.shape[0]
+    out = np.empty((m, n), dtype=np.float32)
+    for n0 in range(0, n, chunk):
+        n1 = min(n, n0 + chunk)
+        q = unpack(packed[n0:n1], bits).astype(np.float64).reshape(n1 - n0, g, GROUP)
+        w = q * s[n0:n1, :, None] + b[n0:n1, :, None]
+        w = round_to(w.astype(np.float32).reshape(n1 - n0, k), dtype)
+        out[:, n0:n1] = x32 @ w.T
+    return out
+
+
 def _dense_acc(x32: np.ndarray, w, dtype: str) -> np.ndarray:
     if _ENGINE[-1] == "c" and dtype == "bf16":
         from . import cgemm
@@ -229,19 +253,23 @@ def silu(a: np.ndarray) -> np.ndarray:
 
 
 def qgemm(x, w, scales=None, biases=None, *, bits: int = 4, dtype: str = "bf16",
-          epilogue: str = "none", bias=None, residual=None, up=None, raw: bool = False):
+          epilogue: str = "none", bias=None, residual=None, up=None, raw: bool = False, form: str = "product"):
     """out[M, N] = epilogue(x[M, K] . W^T) in the reference's order, rounded once.
 
     ``x``/``bias``/``residual`` are storage arrays of ``dtype``.  ``bits`` = 0 means dense
     W (storage of ``dtype``, [N, K]); otherwise ``w`` is the packed uint32 array with
     ``scales``/``biases``.  ``up`` = (w, scales, biases) of the up projection for
-    ``siluGate``.  ``raw`` returns the fp32 result before the final rounding.
+    ``siluGate``.  ``raw`` returns the fp32 result before the final rounding.  ``form``
+    selects the quantized accumulation: "product" (the GEMV's s * sum(x q) + b * sum(x)) or
+    "tile" (weights dequantized to the activation dtype first).
     """
     x32 = from_storage(x, dtype)
 
     def acc(wt, sc, bi):
         if bits == 0:
             return _dense_acc(x32, wt, dtype)
+        if form == "tile":
+            return _dequant_acc(x32, wt, sc, bi, bits, dtype)
         return _affine_acc(x32, wt, sc, bi, bits, dtype)
 
     a = acc(w, scales, biases)

@@ -65,6 +65,48 @@ int oracle_qgemm_bf16(int M, int N, int K, int bits, const float* x, const uint3
   return 0;
 }
 
+/* fp32 -> bf16 -> fp32, round to nearest even (finite inputs). */
+static inline float round_bf16(float f) {
+  uint32_t u;
+  memcpy(&u, &f, sizeof u);
+  u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+  memcpy(&f, &u, sizeof f);
+  return f;
+}
+
+/* out[M, N] = x[M, K] . W'^T with W' = bf16(scale * q + bias) (computed in double, rounded to
+ * float, then to bf16): the dequantize-then-multiply form of tile GEMMs. */
+void oracle_qgemm_tile_bf16(int M, int N, int K, int bits, const float* x, const uint32_t* w, const uint16_t* scales,
+                            const uint16_t* biases, float* out) {
+  const int G = K / 64, per = 32 / bits, wpr = K / per;
+  const uint32_t mask = (1u << bits) - 1u;
+#pragma omp parallel for schedule(static)
+  for (int n = 0; n < N; ++n) {
+    const uint32_t* row = w + (size_t)n * wpr;
+    for (int m0 = 0; m0 < M; m0 += ORACLE_MB) {
+      const int mb = M - m0 < ORACLE_MB ? M - m0 : ORACLE_MB;
+      float acc[ORACLE_MB];
+      for (int m = 0; m < mb; ++m) acc[m] = 0.0f;
+      for (int g = 0; g < G; ++g) {
+        float dq[64];
+        const double s = bf16_to_f32(scales[(size_t)n * G + g]), b = bf16_to_f32(biases[(size_t)n * G + g]);
+        for (int i = 0; i < 64 / per; ++i) {
+          const uint32_t word = row[g * (64 / per) + i];
+          for (int j = 0; j < per; ++j)
+            dq[i * per + j] = round_bf16((float)(s * (double)((word >> (bits * j)) & mask) + b));
+        }
+        for (int m = 0; m < mb; ++m) {
+          const float* xr = x + (size_t)(m0 + m) * K + g * 64;
+          float d = acc[m];
+          for (int k = 0; k < 64; ++k) d += xr[k] * dq[k];
+          acc[m] = d;
+        }
+      }
+      for (int m = 0; m < mb; ++m) out[(size_t)(m0 + m) * N + n] = acc[m];
+    }
+  }
+}
+
 /* out[M, N] = x[M, K] . W^T, W dense bf16 bits [N, K]. */
 void oracle_gemm_dense_bf16(int M, int N, int K, const float* x, const uint16_t* w, float* out) {
 #pragma omp parallel for schedule(static)

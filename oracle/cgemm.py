@@ -34,6 +34,7 @@ def lib():
         p = ctypes.c_void_p
         L.oracle_qgemm_bf16.argtypes = [ctypes.c_int] * 4 + [p] * 5
         L.oracle_qgemm_bf16.restype = ctypes.c_int
+        L.oracle_qgemm_tile_bf16.argtypes = [ctypes.c_int] * 4 + [p] * 5
         L.oracle_gemm_dense_bf16.argtypes = [ctypes.c_int] * 3 + [p] * 3
         L.oracle_threads.restype = ctypes.c_int
         _lib = L
@@ -50,6 +51,18 @@ def qgemm(x: np.ndarray, packed: np.ndarray, scales: np.ndarray, biases: np.ndar
                                  out.ctypes.data)
     if rc != 0:
         raise MemoryError("oracle_qgemm_bf16: group sums")
+    return out
+
+
+def qgemm_tile(x: np.ndarray, packed: np.ndarray, scales: np.ndarray, biases: np.ndarray, bits: int) -> np.ndarray:
+    """x . W'^T with every weight dequantized to bf16 first (oracle_qgemm_tile_bf16)."""
+    x = np.ascontiguousarray(x, np.float32)
+    m, k = x.shape
+    n = packed.shape[0]
+    out = np.empty((m, n), np.float32)
+    lib().oracle_qgemm_tile_bf16(m, n, k, bits, x.ctypes.data, np.ascontiguousarray(packed).ctypes.data,
+                                 np.ascontiguousarray(scales).ctypes.data, np.ascontiguousarray(biases).ctypes.data,
+                                 out.ctypes.data)
     return out
 
 

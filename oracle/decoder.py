@@ -74,12 +74,20 @@ def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float, dtype: str) -> np.ndarray:
     return A.round_to(w * A.round_to(x * r, dtype), dtype)
 
 
+# Quantized GEMMs of more than this many rows take the dequantize-then-multiply form (the
+# library's tensor-core GEMM; stock MLX quantizedMM at large row counts); up to it, the GEMV's
+# product form (SmallMGEMM.swift:662-755).
+TILE_ROWS = 16
+
+
 def linear(x: np.ndarray, W: dict, bits: int, dtype: str, epilogue="none", residual=None, up=None) -> np.ndarray:
     """The library GEMM's arithmetic: fp32 accumulation, epilogue, one rounding."""
     xs = A.to_storage(x, dtype)
     res = A.to_storage(residual, dtype) if residual is not None else None
     u = (up["w"], up.get("s"), up.get("b")) if up is not None else None
-    out = A.qgemm(xs, W["w"], W.get("s"), W.get("b"), bits=bits, dtype=dtype, epilogue=epilogue, residual=res, up=u)
+    form = "tile" if xs.shape[0] > TILE_ROWS else "product"
+    out = A.qgemm(xs, W["w"], W.get("s"), W.get("b"), bits=bits, dtype=dtype, epilogue=epilogue, residual=res, up=u,
+                  form=form)
     return A.from_storage(out, dtype)
 
 

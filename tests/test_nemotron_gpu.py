@@ -8,6 +8,7 @@ gives, bit for bit, the outputs and states of 5 one-token calls.
 import numpy as np
 import pytest
 
+from oracle import decoder as D
 from oracle import nemotron as N
 
 pytestmark = pytest.mark.gpu_pending
@@ -335,7 +336,13 @@ def test_mtp_head_and_draft_and_verify_on_the_device():
         looped = m.decode_looped
         for depth in (2, 3):
             got, hist = VN.decode_mtp(m, emb, 40, depth)
-            assert got == want and m.decode_looped == looped, (seed, depth)
+            if looped and len(got) == 40 and len(want) < 40:
+                # the reference's decodeMTP returns at maxTokens before its loop check
+                # (NemotronTranscribeModel.swift:389-390), decodeGreedy checks every token (:285):
+                # a loop completed by the 40th token is cut by greedy only
+                assert D.loop_cut(got) == (want, True) and not m.decode_looped, (seed, depth)
+            else:
+                assert got == want and m.decode_looped == looped, (seed, depth)
             seen |= {a == depth for a in hist}
     assert seen == {True, False}
     m.close()

@@ -109,6 +109,13 @@ def test_c_restatement_equals_the_numpy_oracle():
             ref = A.qgemm(x, p, s, b, bits=bits, raw=True)
             with A.c_accumulation():
                 got = A.qgemm(x, p, s, b, bits=bits, raw=True)
+            # the dequantize-then-multiply form: C equals numpy, and both stay within the
+            # rounding of one bf16 weight of the product form
+            ref_t = A.qgemm(x, p, s, b, bits=bits, raw=True, form="tile")
+            with A.c_accumulation():
+                got_t = A.qgemm(x, p, s, b, bits=bits, raw=True, form="tile")
+            assert np.abs(got_t - ref_t).max() <= 1e-5 * max(1.0, np.abs(ref_t).max()), (bits, m, n, k)
+            assert A.relative_rms(ref_t, ref) <= 1e-2
         else:
             wd = A.to_storage(w, "bf16")
             ref = A.qgemm(x, wd, bits=0, raw=True)

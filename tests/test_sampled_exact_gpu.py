@@ -51,13 +51,22 @@ def _models(target_rows=16, draft_rows=16):
     return t, d
 
 
-@pytest.mark.parametrize("mode", ["model", "oracle"])
+@pytest.mark.parametrize("mode", ["model", "oracle", "self"])
 def test_linear_sampled_acceptance_is_token_exact(mode):
+    """model: the random bf16 draft (rejections, residual draws); oracle: the oracle draft's
+    mixture q; self: a draft identical to the target, so every draft is accepted and the bonus
+    is drawn from the last verify row."""
     from vella_b200 import decode as VD
     K, P, V, passes = 4, 16, 1000, 30
     t, d = _models()
     pre_t, pre_d = prefix_of(P, 256, 63), prefix_of(P, 128, 64)
     ref = None
+    if mode == "self":
+        d.close()
+        d = VD.Model(VD.ModelConfig(2, 256, 4, 2, 64, 512, 1000, bits=4, max_seq=256, max_prefix=32,
+                                    rows_per_stream=16))
+        d.init_random(61, 0.08)
+        pre_d = pre_t
     if mode == "oracle":
         g = VD.SpecDecoder(t, d, k=K)
         g.set_prefix(pre_t, pre_d, P)
@@ -76,7 +85,7 @@ def test_linear_sampled_acceptance_is_token_exact(mode):
         new = sd.step()
         p_rows = _read(t.tensor("logits"), "bf16").reshape(-1, V)[:K + 1]
         dev_tok = _read(sd.tensor("tokens"), np.int32)
-        if mode == "model":
+        if mode != "oracle":
             q_rows = _read(sd.tensor("draft_rows"), "bf16").reshape(K, V)
             drafts, m1 = D.sample_drafts(q_rows, T, SEED, pi)
             qs = [D.softmax_t(r, T) for r in q_rows]
@@ -97,7 +106,10 @@ def test_linear_sampled_acceptance_is_token_exact(mode):
         rejections += a < K
         L += len(new)
     assert exact >= passes - 2 and ties <= 2, (exact, ties)
-    assert 0 < rejections < passes  # both the residual draw and the bonus-from-p draw ran
+    if mode == "self":
+        assert rejections <= 2, rejections  # q == p: the bonus comes from the last verify row
+    else:
+        assert rejections > 0  # the residual draw ran
     sd.close()
     t.close()
     d.close()
