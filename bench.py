@@ -138,19 +138,13 @@ def quantize_gpu(w, bits):
     return packed.contiguous(), scale.to(torch.bfloat16).contiguous(), bias.to(torch.bfloat16).contiguous()
 
 
-def run_gemm(args, rank, world):
+def gemm_plans(cases, dev, stream):
+    """Weights (copies rotating over > 3x L2), inputs and outputs of every (bits, N, K, M) case;
+    cases are (bits, n, k, [m, ..]).  Returns the plans and one shared workspace."""
     import torch
     from vella_b200 import smallm as S
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
-    torch.cuda.set_device(dev)
-    hbm, _, peak_kind = peaks()
     g = torch.Generator(device=dev).manual_seed(0)
-    stream = torch.cuda.Stream(device=dev)
-    plans = []  # (bits, n, k, m, copies, x, out, graph_calls)
-    cases = [(b, n, k, GEMM_MS) for b in (4, 8) for (n, k) in GEMM_SHAPES]
-    if args.shape:  # one (bits, N, K, M) case, e.g. a small capture for a profiler
-        b, n, k, m = (int(v) for v in args.shape.split(","))
-        cases = [(b, n, k, [m])]
+    plans = []  # (bits, n, k, m, weight copies, x, out)
     with torch.cuda.stream(stream):
         for bits, n, k, ms in cases:
             w = torch.randn(n, k, generator=g, device=dev) * 0.02
@@ -169,11 +163,15 @@ def run_gemm(args, rank, world):
                 out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
                 plans.append((bits, n, k, m, ws, x, out))
     torch.cuda.synchronize()
-    # one workspace for every graph (they replay one after another on one stream)
     ws_bytes = max(S.workspace_size(m, n, k, torch.bfloat16, bits) for bits, n, k, m, *_ in plans)
     workspace = torch.zeros(max(ws_bytes, 256) // 4 + 64, dtype=torch.int32, device=dev)
-    # one CUDA graph per (bits, shape, M): `reps` calls cycling through the weight copies
-    reps = 8
+    return plans, workspace
+
+
+def gemm_graphs(plans, workspace, stream, reps):
+    """One CUDA graph per case: `reps` calls cycling through its weight copies."""
+    import torch
+    from vella_b200 import smallm as S
     graphs = []
     for bits, n, k, m, ws, x, out in plans:
         with torch.cuda.stream(stream):
@@ -185,28 +183,58 @@ def run_gemm(args, rank, world):
                 S.matmul(x, ws[i % len(ws)], out=out, workspace=workspace)
         graphs.append(gr)
     torch.cuda.synchronize()
+    return graphs
+
+
+def gemm_time_each(plans, graphs, stream, reps, hbm, iters=4):
+    """Per case: mean call time from CUDA events on the launching stream (after a warm replay)."""
+    import torch
+    per = []
+    for (bits, n, k, m, ws, x, out), gr in zip(plans, graphs):
+        with torch.cuda.stream(stream):
+            gr.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(iters):
+                gr.replay()
+            e1.record()
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1000 / (iters * reps)
+        gbs = gemm_bytes(m, n, k, bits) / us / 1e3
+        per.append({"bits": bits, "n": n, "k": k, "m": m, "us": round(us, 3), "gbs": round(gbs, 1),
+                    "frac": round(gbs / hbm, 3), "tflops": round(2.0 * m * n * k / us / 1e6, 1)})
+    return per
+
+
+def m8_aggregate(per):
+    """Bytes-weighted HBM rate of the int4 calls of at most 8 rows."""
+    sel = [p for p in per if p["bits"] == 4 and p["m"] <= 8] or per
+    return sum(gemm_bytes(p["m"], p["n"], p["k"], p["bits"]) for p in sel) / sum(p["us"] for p in sel) / 1e3
+
+
+def run_gemm(args, rank, world):
+    import torch
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    hbm, _, peak_kind = peaks()
+    stream = torch.cuda.Stream(device=dev)
+    cases = [(b, n, k, GEMM_MS) for b in (4, 8) for (n, k) in GEMM_SHAPES]
+    if args.shape:  # one (bits, N, K, M) case, e.g. a small capture for a profiler
+        b, n, k, m = (int(v) for v in args.shape.split(","))
+        cases = [(b, n, k, [m])]
+    plans, workspace = gemm_plans(cases, dev, stream)
+    reps = 8
+    graphs = gemm_graphs(plans, workspace, stream, reps)
 
     def step():
         for gr in graphs:
             gr.replay()
 
-    for _ in range(args.warmup):
-        step()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
     torch.cuda.synchronize()
-    # per-config timing with events (for the sweep table and the roofline)
-    per = []
-    for (bits, n, k, m, ws, x, out), gr in zip(plans, graphs):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            e0.record()
-            for _ in range(4):
-                gr.replay()
-            e1.record()
-        e1.synchronize()
-        us = e0.elapsed_time(e1) * 1000 / (4 * reps)
-        per.append({"bits": bits, "n": n, "k": k, "m": m, "us": round(us, 3),
-                    "gbs": round(gemm_bytes(m, n, k, bits) / us / 1e3, 1),
-                    "tflops": round(2.0 * m * n * k / us / 1e6, 1)})
+    per = gemm_time_each(plans, graphs, stream, reps, hbm)
     with ClockSampler(dev.index) as clk:
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -219,10 +247,7 @@ def run_gemm(args, rank, world):
         ms = e0.elapsed_time(e1)
     total_bytes = sum(gemm_bytes(m, n, k, bits) for bits, n, k, m, *_ in plans) * reps * args.steps
     value = total_bytes / (ms / 1e3) / 1e9
-    m8 = [p for p in per if p["bits"] == 4 and p["m"] <= 8] or per
-    m8_bytes = sum(gemm_bytes(p["m"], p["n"], p["k"], p["bits"]) for p in m8)
-    m8_us = sum(p["us"] for p in m8)
-    dominant = m8_bytes / m8_us / 1e3
+    dominant = m8_aggregate(per)
     line = {
         "metric": "small-M int4/int8 GEMM HBM GB/s (sweep aggregate)",
         "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -240,6 +265,30 @@ def run_gemm(args, rank, world):
     return line
 
 
+def gemm_subline(dev, hbm, peak_kind):
+    """The config-2 GEMM shapes inside the default bench line: int4 at M in {1, 5, 8} and int8 at
+    M = 1 for every (N, K), each call timed alone (CUDA graph of 8 calls over rotating weight
+    copies, CUDA events), with its HBM fraction."""
+    import torch
+    stream = torch.cuda.Stream(device=dev)
+    cases = [(4, n, k, [1, 5, 8]) for (n, k) in GEMM_SHAPES] + [(8, n, k, [1]) for (n, k) in GEMM_SHAPES]
+    plans, workspace = gemm_plans(cases, dev, stream)
+    reps = 8
+    graphs = gemm_graphs(plans, workspace, stream, reps)
+    with torch.cuda.stream(stream):
+        for gr in graphs:
+            gr.replay()
+    per = gemm_time_each(plans, graphs, stream, reps, hbm)
+    agg = m8_aggregate(per)
+    del graphs, plans, workspace
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return {"unit": "GB/s", "peak": hbm, "peak_kind": peak_kind,
+            "int4_m_le_8_gbs": round(agg, 1), "int4_m_le_8_frac": round(agg / hbm, 3),
+            "note": "each call alone, weights rotated over copies > 3x L2; bytes = N*K*bits/8 + N*K/64*4 + M*K*2 + M*N*2",
+            "cases": per}
+
+
 # ---------------------------------------------------------------------------------------
 # 30B-class int4 draft-and-verify (the headline)
 # ---------------------------------------------------------------------------------------
@@ -253,7 +302,7 @@ BATCH_STREAMS = 32  # streams per GPU of the batched measurement
 # Tree verification with stochastic acceptance: 256 streams over the box's 8 GPUs, i.e. 32 per
 # GPU; branching 3 at depth 1, then 2, 2, 1 (33 draft nodes + the root = 34 verify rows per
 # stream); temperature 0.7; the real (random-init) draft model proposes.
-TREE_STREAMS, TREE_BRANCHING, TREE_TEMPERATURE, TREE_TOKENS = 32, (3, 2, 2, 1), 0.7, 64
+TREE_STREAMS, TREE_BRANCHING, TREE_TEMPERATURE, TREE_TOKENS = 32, (3, 2, 2, 1), 0.7, NEW_TOKENS
 
 
 def expected_tokens_per_pass(k, p):
@@ -475,11 +524,15 @@ def run_spec(args, rank, world):
         "init_s": round(init_s, 1),
     }
     if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(k, p)
+        line["cpu_baseline"] = cpu_baseline(k, p, tokens / max(passes, 1))
     for x in (sd, se):
         x.close()
     target.close()
     draft.close()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    if not args.no_gemm:
+        line["gemm"] = gemm_subline(dev, hbm, peak_kind)
     if not args.no_batched:
         line["batched"] = run_spec_batched(rank, local, BATCH_STREAMS, k, p)
         line["batched"]["tokens_per_s_all_gpus"] = round(
@@ -571,7 +624,7 @@ def run_spec_tree(rank, local, S, branching, temperature, new_tokens):
     sd = VD.SpecDecoder(target, draft, k=len(branching), mode=VD.DRAFT_MODEL, seed=11 + rank,
                         temperature=temperature, tree=branching)
     sd.set_prefix(None, None, PREFIX)
-    sd.decode_batch(new_tokens, VD.DECODE_SPEC)  # warm-up: prefill, graph capture
+    sd.decode_batch(16, VD.DECODE_SPEC)  # warm-up: prefill, graph capture
     st0 = sd.stats()
     out_toks = sd.decode_batch(new_tokens, VD.DECODE_SPEC)
     st = sd.stats()
@@ -637,17 +690,53 @@ def cpu_pass_seconds(k, layers_sampled=1):
     s0 = time.perf_counter()
     C.gemm_dense(rng.standard_normal((1, d["d_model"])).astype(np.float32), wd)
     d_lm = (time.perf_counter() - s0) * 8
-    per_pass = c["n_layers"] * t_layer + t_lm + k * (d["n_layers"] * d_layer + d_lm)
+    t_rows, d_rows = cpu_row_ops_seconds(c, k + 1), cpu_row_ops_seconds(d, 1)
+    per_pass = c["n_layers"] * (t_layer + t_rows) + t_lm + k * (d["n_layers"] * (d_layer + d_rows) + d_lm)
     return per_pass, C.threads()
 
 
-def cpu_baseline(k, p):
+CPU_CACHE = PREFIX + NEW_TOKENS // 2  # mean cache length over a 448-token decode after the prefix
+
+
+def cpu_row_ops_seconds(c, rows):
+    """One layer's row work in the numpy oracle: the two RMSNorms, RoPE of q and the new keys,
+    and causal GQA attention of `rows` query rows over a CPU_CACHE-position cache."""
+    import math
+
+    import numpy as np
+    from oracle import decoder as D
+    rng = np.random.default_rng(1)
+    d, H, KV, hd = c["d_model"], c["n_heads"], c["n_kv_heads"], c["head_dim"]
+    T = CPU_CACHE
+    x = rng.standard_normal((rows, d)).astype(np.float32)
+    w = np.ones(d, np.float32)
+    q = rng.standard_normal((rows, H, hd)).astype(np.float32)
+    kc = rng.standard_normal((T, KV, hd)).astype(np.float32)
+    vc = rng.standard_normal((T, KV, hd)).astype(np.float32)
+    pos = np.arange(T - rows, T)
+    table = np.zeros((T, hd // 2, 2), np.float32)
+    table[:, :, 0] = 1.0
+    s0 = time.perf_counter()
+    D.rmsnorm(x, w, 1e-6, "bf16")
+    D.rmsnorm(x, w, 1e-6, "bf16")
+    D.rope(q, pos, table, "bf16")
+    D.rope(kc[T - rows:], pos, table, "bf16")
+    D.attention(q, kc, vc, pos, 1.0 / math.sqrt(hd), "bf16")
+    return time.perf_counter() - s0
+
+
+def cpu_baseline(k, p, tokens_per_pass=None):
+    """The oracle's CPU restatement of one pass, on the host cores; tokens per pass from the GPU
+    run when given (else the oracle draft's expectation)."""
     per_pass, threads = cpu_pass_seconds(k)
-    tps = expected_tokens_per_pass(k, p) / per_pass
+    tpp = tokens_per_pass if tokens_per_pass else expected_tokens_per_pass(k, p)
+    tps = tpp / per_pass
     return {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
             "sample": f"C/OpenMP oracle GEMMs of 1 target layer (M={k + 1}), 1 draft layer (M=1) and 1/8 of each "
-                      f"LM head timed once, extrapolated to one pass (64+{k}x28 layers, both heads) and to "
-                      f"E[tokens/pass]={expected_tokens_per_pass(k, p):.2f}; attention and norms not counted"}
+                      f"LM head, plus the numpy oracle's RMSNorms, RoPE and attention of one layer of each over a "
+                      f"{CPU_CACHE}-position cache, timed once and extrapolated to one pass (64+{k}x28 layers, both "
+                      f"heads) at {tpp:.2f} tokens per pass "
+                      f"({'measured on the GPU' if tokens_per_pass else 'expected'})"}
 
 
 def run_reference(args, rank, world):
@@ -657,15 +746,20 @@ def run_reference(args, rank, world):
     for _ in range(args.warmup):
         cpu_pass_seconds(k)
     total, threads = 0.0, 1
+    w0 = time.perf_counter()
     for _ in range(args.steps):
         s, threads = cpu_pass_seconds(k)
         total += s
+    wall_ms = (time.perf_counter() - w0) * 1e3 / max(args.steps, 1)
     per_pass = total / max(args.steps, 1)
     tps = expected_tokens_per_pass(k, p) / per_pass
     sample = (f"one draft-and-verify pass per step (64 target layers at M={k + 1}, {k} draft steps of 28 layers, "
-              f"both LM heads) extrapolated from 1 timed layer each, C/OpenMP oracle GEMMs")
+              f"both LM heads) extrapolated from 1 timed layer each: C/OpenMP oracle GEMMs and the numpy oracle's "
+              f"norms, RoPE and attention over a {CPU_CACHE}-position cache; E[tokens/pass] "
+              f"{expected_tokens_per_pass(k, p):.2f}; ms_per_step is the wall time of one step's timed sample")
     return {"impl": "reference", "metric": "int4 draft-verify tokens/s/GPU (30B-class target, K=4, acceptance p=0.7)",
             "value": round(tps, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(wall_ms, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4 x fp32 (CPU)",
             "data": "synthetic", "config": {"workload": "30B-class int4 target + bf16 draft, K=4, p=0.7 (CPU restatement)"},
             "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
@@ -918,6 +1012,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="spec workload: skip the multi-stream measurement")
     ap.add_argument("--no-tree", action="store_true", help="spec workload: skip the tree + sampling measurement")
+    ap.add_argument("--no-gemm", action="store_true", help="spec workload: skip the config-2 GEMM sub-line")
     ap.add_argument("--shape", default="", help="gemm workload: one case 'bits,N,K,M' instead of the sweep")
     ap.add_argument("--profile-pass", action="store_true", help="short run for an ncu launch list")
     ap.add_argument("--profile-tree", action="store_true", help="short tree-verification run for an ncu launch list")

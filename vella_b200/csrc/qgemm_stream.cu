@@ -110,30 +110,44 @@ __device__ __forceinline__ long long unit0(int c, long long U, int P) { return (
 // when that began in an earlier CTA.  (row block, k chunk) advance one unit at a time; the
 // chunk count is divided by once per segment only.
 struct UnitWalk {
-  long long b[3], e[3];
-  int n, si;
+  // the current segment ends at e; up to two more segments [b1, e1), [b2, e2) follow (scalars,
+  // not arrays: a runtime-indexed array would live in local memory)
+  long long e, b1, e1, b2, e2;
+  int left;
   long long u;
   int rb, kc;
-  __device__ UnitWalk(long long u0, long long u1, int nkc) : n(0), si(0) {
+  __device__ UnitWalk(long long u0, long long u1, int nkc) : e(u1), b1(0), e1(0), b2(0), e2(0), left(0), u(u0) {
     const long long rf = u0 / nkc, rl = (u1 - 1) / nkc;
-    if (rl == rf) {
-      b[0] = u0; e[0] = u1; n = 1;
-    } else {
+    if (rl != rf) {
       const bool tail = u1 % nkc != 0, head = u0 % nkc != 0;
       const long long mb = head ? (rf + 1) * nkc : u0, me = tail ? rl * nkc : u1;
-      if (tail) { b[n] = rl * nkc; e[n] = u1; ++n; }
-      if (me > mb) { b[n] = mb; e[n] = me; ++n; }
-      if (head) { b[n] = u0; e[n] = (rf + 1) * nkc; ++n; }
+      int n = 0;
+      long long b0 = 0, e0 = 0;
+      auto push = [&](long long bb, long long ee) {
+        if (n == 0) { b0 = bb; e0 = ee; }
+        else if (n == 1) { b1 = bb; e1 = ee; }
+        else { b2 = bb; e2 = ee; }
+        ++n;
+      };
+      if (tail) push(rl * nkc, u1);
+      if (me > mb) push(mb, me);
+      if (head) push(u0, (rf + 1) * nkc);
+      u = b0;
+      e = e0;
+      left = n - 1;
     }
-    u = b[0];
     rb = (int)(u / nkc);
     kc = (int)(u % nkc);
   }
-  __device__ __forceinline__ bool seg_last() const { return u + 1 == e[si]; }
+  __device__ __forceinline__ bool seg_last() const { return u + 1 == e; }
   __device__ __forceinline__ void next(int nkc) {
-    if (++u == e[si]) {
-      if (++si < n) {
-        u = b[si];
+    if (++u == e) {
+      if (left > 0) {
+        u = b1;
+        e = e1;
+        b1 = b2;
+        e1 = e2;
+        --left;
         rb = (int)(u / nkc);
         kc = (int)(u % nkc);
       }
@@ -215,9 +229,7 @@ __global__ void __launch_bounds__(kThreads, LIGHT ? 2 : 1) qgemm_stream_kernel(c
   if (warp == kProducerWarp) {
     // ------------------------------- producer (one thread) ------------------------------
     if (lane != 0) return;
-    int fills[NS];
-#pragma unroll
-    for (int s = 0; s < NS; ++s) fills[s] = 0;
+    int issued = 0;  // units whose copies were issued; unit i fills stage i % NS
     // weights, scales and biases of a unit (constant data: may be read before the
     // preceding kernel has finished)
     auto issue_w = [&](const UnitWalk& w, int s) {
@@ -261,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, LIGHT ? 2 : 1) qgemm_stream_kernel(c
       UnitWalk cw = cur;
       for (int j = 0; j < npre; ++j, cw.next(nkc)) {
         mbar_expect_tx(&full[j], LY::TX);
-        fills[j]++;
+        ++issued;
         issue_w(cw, j);
       }
     }
@@ -277,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, LIGHT ? 2 : 1) qgemm_stream_kernel(c
         break;
       }
       mbar_expect_tx(&full[s], LY::TX);
-      fills[s]++;
+      ++issued;
       issue_w(cur, s);
       issue_x(cur, s);
       if (++s == NS) {
@@ -286,8 +298,10 @@ __global__ void __launch_bounds__(kThreads, LIGHT ? 2 : 1) qgemm_stream_kernel(c
       }
     }
     // Never leave with copies in flight: wait for the last fill of every stage.
-    for (int q = 0; q < NS; ++q)
-      if (fills[q] > 0 && !mbar_wait(&full[q], (uint32_t)((fills[q] - 1) & 1))) atomicOr(&g_stream_fault, 2);
+    for (int q = 0; q < NS; ++q) {
+      const int fq = issued > q ? (issued - 1 - q) / NS + 1 : 0;  // fills of stage q
+      if (fq > 0 && !mbar_wait(&full[q], (uint32_t)((fq - 1) & 1))) atomicOr(&g_stream_fault, 2);
+    }
     return;
   }
 
