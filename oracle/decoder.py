@@ -80,15 +80,16 @@ def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float, dtype: str) -> np.ndarray:
 TILE_ROWS = 16
 
 
-def linear(x: np.ndarray, W: dict, bits: int, dtype: str, epilogue="none", residual=None, up=None) -> np.ndarray:
-    """The library GEMM's arithmetic: fp32 accumulation, epilogue, one rounding."""
+def linear(x: np.ndarray, W: dict, bits: int, dtype: str, epilogue="none", residual=None, up=None,
+           raw: bool = False) -> np.ndarray:
+    """The library GEMM's arithmetic: fp32 accumulation, epilogue, one rounding (none with raw)."""
     xs = A.to_storage(x, dtype)
     res = A.to_storage(residual, dtype) if residual is not None else None
     u = (up["w"], up.get("s"), up.get("b")) if up is not None else None
     form = "tile" if xs.shape[0] > TILE_ROWS else "product"
     out = A.qgemm(xs, W["w"], W.get("s"), W.get("b"), bits=bits, dtype=dtype, epilogue=epilogue, residual=res, up=u,
-                  form=form)
-    return A.from_storage(out, dtype)
+                  form=form, raw=raw)
+    return out if raw else A.from_storage(out, dtype)
 
 
 def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, pos_q: np.ndarray, scale: float, dtype: str):
@@ -115,9 +116,9 @@ def rope(x: np.ndarray, pos: np.ndarray, table: np.ndarray, dtype: str) -> np.nd
     return A.round_to(np.concatenate([x1 * c - x2 * s, x1 * s + x2 * c], axis=-1), dtype)
 
 
-def forward(cfg: Config, W: dict, embeds: np.ndarray, table: np.ndarray) -> np.ndarray:
+def forward(cfg: Config, W: dict, embeds: np.ndarray, table: np.ndarray, raw_logits: bool = False) -> np.ndarray:
     """Causal forward of the whole sequence of input embeddings [T, d] (fp32, rounded to T);
-    returns the logits [T, V] (fp32 values of T)."""
+    returns the logits [T, V] (fp32 values of T; with raw_logits, before their final rounding)."""
     dt = cfg.dtype
     T = embeds.shape[0]
     H, KV, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
@@ -140,7 +141,7 @@ def forward(cfg: Config, W: dict, embeds: np.ndarray, table: np.ndarray) -> np.n
         act = linear(xn, L["gate"], cfg.bits, dt, "siluGate", up=L["up"])
         h = linear(act, L["down"], cfg.bits, dt, "residual", residual=h)
     xn = rmsnorm(h, W["final_norm"], cfg.rms_eps, dt)
-    return linear(xn, W["lm_head"], cfg.bits, dt)
+    return linear(xn, W["lm_head"], cfg.bits, dt, raw=raw_logits)
 
 
 def embed_sequence(W: dict, prefix: np.ndarray, tokens) -> np.ndarray:
@@ -150,10 +151,10 @@ def embed_sequence(W: dict, prefix: np.ndarray, tokens) -> np.ndarray:
     return np.concatenate(rows, axis=0)
 
 
-def score(cfg: Config, W: dict, prefix: np.ndarray, tokens, table: np.ndarray) -> np.ndarray:
+def score(cfg: Config, W: dict, prefix: np.ndarray, tokens, table: np.ndarray, raw_logits: bool = False) -> np.ndarray:
     """Logits predicting tokens[0..T) (positions P-1 .. P+T-2), teacher forced."""
     x = embed_sequence(W, prefix, list(tokens)[:-1])
-    return forward(cfg, W, x, table)[prefix.shape[0] - 1:]
+    return forward(cfg, W, x, table, raw_logits)[prefix.shape[0] - 1:]
 
 
 def first_argmax(row: np.ndarray) -> int:

@@ -12,7 +12,10 @@ kernels the benchmark uses:
   64, FFN 5120, 128 mels, 1500 frames, vocab 51866, fp16).
 
 Bars (as in the small-model tests): teacher-forced logits max |error| <= 2e-2 on a sample
-of vocabulary rows (every position's top logit included); greedy tokens equal the
+of vocabulary rows (every position's top logit included), measured against the oracle's
+fp32 logits before their bf16 rounding with half an ulp of the device's bf16 output on top
+(logits of these models reach 8-16, where one bf16 ulp is 0.0625: the output format alone
+is coarser than 2e-2 there); greedy tokens equal the
 oracle's argmax wherever its top-2 margin exceeds that tolerance; draft-and-verify emits
 exactly the greedy tokens.  The oracle's GEMM accumulations run in its C restatement
 (same product form) so the check takes seconds.
@@ -104,20 +107,29 @@ def _check_model(spec, seed):
     rows = np.union1d(rng.choice(oc.vocab, 4096, replace=False), got.argmax(axis=1))
     W = _weights(m, oc, rows, toks)
     with A.c_accumulation():
-        ref = D.score(oc, W, A.bf16_from_bits(pre), toks, D.rope_table(P + T, oc.head_dim, oc.rope_theta))
-    err = float(np.abs(got[:, rows] - ref).max())
+        ref = D.score(oc, W, A.bf16_from_bits(pre), toks, D.rope_table(P + T, oc.head_dim, oc.rope_theta),
+                      raw_logits=True)
     m.close()
-    return err
+    g = got[:, rows]
+    excess = np.abs(g - ref) - 0.5 * _bf16_ulp(g)
+    i = np.unravel_index(int(np.argmax(excess)), excess.shape)
+    return float(excess.max()), float(g[i]), float(ref[i])
+
+
+def _bf16_ulp(v):
+    """Spacing of bf16 values at |v| (8 significant bits)."""
+    e = np.floor(np.log2(np.maximum(np.abs(v), 2.0 ** -126)))
+    return 2.0 ** (e - 7)
 
 
 def test_target_at_benchmark_dims_matches_oracle():
-    err = _check_model(TARGET, 31)
-    assert err <= LOGIT_TOL, err
+    err, got, ref = _check_model(TARGET, 31)
+    assert err <= LOGIT_TOL, (err, got, ref)
 
 
 def test_draft_at_benchmark_dims_matches_oracle():
-    err = _check_model(DRAFT, 32)
-    assert err <= LOGIT_TOL, err
+    err, got, ref = _check_model(DRAFT, 32)
+    assert err <= LOGIT_TOL, (err, got, ref)
 
 
 def test_decode_at_benchmark_dims_follows_oracle_and_verify_equals_greedy():

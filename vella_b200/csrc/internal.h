@@ -88,15 +88,15 @@ struct QgemmPlan {
   int zchunks;    // ceil(M / 16)
   size_t workspace;
   bool stream = false;  // persistent bulk-copy kernel (qgemm_stream.cu)
-  int ctas = 0;         // its grid (one CTA per SM, or two with `light`)
-  bool light = false;   // two 96-register CTAs per SM (int4 calls with many units)
+  int ctas = 0;         // its grid: one CTA per SM, or two for int4 calls with many units
+  bool light = false;   // the compact 96-register, two-stage layout (int4): two fit one SM
   bool tc = false;      // tensor-core kernel for M > 16 (tc_gemm.cu)
 };
 
 // qgemm_stream.cu
 bool stream_eligible(const vella_qgemm_desc& d);
 int stream_units(const vella_qgemm_desc& d, int* rowblocks, int* nkc);
-// True when the call runs two CTAs per SM; depends on (N, K, format, SM count) only.
+// True when an int4 call runs two CTAs per SM; depends on (N, K, format, SM count) only.
 bool stream_light(const vella_qgemm_desc& d, int rowblocks, int nkc, int sms);
 size_t stream_partial_bytes(int P);
 int stream_flag_count(int P);  // ints of the flag region (zero between calls)

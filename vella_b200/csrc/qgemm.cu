@@ -462,8 +462,11 @@ bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* p) {
     p->stream = true;
     // one CTA per SM, but never more CTAs than units: every CTA owns at least one unit
     const int sms = num_sms(dev);
-    p->light = stream_light(d, rb, nkc, sms);
-    p->ctas = (int)std::min<long long>((p->light ? 2 : 1) * (long long)sms, (long long)rb * nkc);
+    // int4: the compact two-stage layout (96 registers, ~112 KB), two CTAs per SM for calls with
+    // many units; with one CTA per SM the other half of the SM takes the next kernel's CTA, which
+    // fetches its first weight stages while this call finishes
+    p->light = d.bits == 4;
+    p->ctas = (int)std::min<long long>((stream_light(d, rb, nkc, sms) ? 2 : 1) * (long long)sms, (long long)rb * nkc);
     p->rowblocks = rb;
     p->workspace = counter_region((size_t)stream_flag_count(p->ctas)) + stream_partial_bytes(p->ctas);
     return true;

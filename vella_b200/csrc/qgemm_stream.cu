@@ -63,8 +63,9 @@ template <> struct SFmt<4> { static constexpr int UG = 8, BPG = 32, WCH = 2, XCH
 template <> struct SFmt<8> { static constexpr int UG = 8, BPG = 64, WCH = 4, XCH = 2; };
 template <> struct SFmt<0> { static constexpr int UG = 4, BPG = 128, WCH = 4, XCH = 1; };
 
-// LIGHT: two CTAs per SM (96 registers a thread, two stages); twice the consumer warps per
-// SM for the int4 calls whose units keep both busy.
+// LIGHT: the compact layout (96 registers a thread, two stages), two of which fit one SM: the
+// int4 calls run two CTAs per SM when their units keep both busy, else one, which leaves room
+// for the next kernel's CTA to start its weight copies before this call ends.
 template <int BITS, int NT, bool LIGHT = false>
 struct Layout {
   static constexpr int TOK = NT * 8;
@@ -789,7 +790,7 @@ int stream_launch(const vella_qgemm_desc& d, int P, bool light, const void* x, c
     a.rope = 1;
     a.re = *rope;
   }
-  if (light && d.bits != 4) return fail(VELLA_E_INVALID, "stream GEMM: two CTAs per SM only for int4");
+  if (light && d.bits != 4) return fail(VELLA_E_INVALID, "stream GEMM: the compact layout is int4 only");
   if (d.dtype == VELLA_BF16) {
     switch (d.bits) {
       case 4:
