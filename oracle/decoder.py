@@ -116,9 +116,12 @@ def rope(x: np.ndarray, pos: np.ndarray, table: np.ndarray, dtype: str) -> np.nd
     return A.round_to(np.concatenate([x1 * c - x2 * s, x1 * s + x2 * c], axis=-1), dtype)
 
 
-def forward(cfg: Config, W: dict, embeds: np.ndarray, table: np.ndarray, raw_logits: bool = False) -> np.ndarray:
+def forward(cfg: Config, W: dict, embeds: np.ndarray, table: np.ndarray, raw_logits: bool = False,
+            logits_from: int = 0) -> np.ndarray:
     """Causal forward of the whole sequence of input embeddings [T, d] (fp32, rounded to T);
-    returns the logits [T, V] (fp32 values of T; with raw_logits, before their final rounding)."""
+    returns the logits [T - logits_from, V] of the rows from logits_from on (fp32 values of T;
+    with raw_logits, before their final rounding).  The LM head is one GEMM over those rows
+    only, as the library runs it, so its row count picks its form."""
     dt = cfg.dtype
     T = embeds.shape[0]
     H, KV, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
@@ -140,7 +143,7 @@ def forward(cfg: Config, W: dict, embeds: np.ndarray, table: np.ndarray, raw_log
         xn = rmsnorm(h, L["mlp_norm"], cfg.rms_eps, dt)
         act = linear(xn, L["gate"], cfg.bits, dt, "siluGate", up=L["up"])
         h = linear(act, L["down"], cfg.bits, dt, "residual", residual=h)
-    xn = rmsnorm(h, W["final_norm"], cfg.rms_eps, dt)
+    xn = rmsnorm(h[logits_from:], W["final_norm"], cfg.rms_eps, dt)
     return linear(xn, W["lm_head"], cfg.bits, dt, raw=raw_logits)
 
 
@@ -154,7 +157,7 @@ def embed_sequence(W: dict, prefix: np.ndarray, tokens) -> np.ndarray:
 def score(cfg: Config, W: dict, prefix: np.ndarray, tokens, table: np.ndarray, raw_logits: bool = False) -> np.ndarray:
     """Logits predicting tokens[0..T) (positions P-1 .. P+T-2), teacher forced."""
     x = embed_sequence(W, prefix, list(tokens)[:-1])
-    return forward(cfg, W, x, table, raw_logits)[prefix.shape[0] - 1:]
+    return forward(cfg, W, x, table, raw_logits, logits_from=prefix.shape[0] - 1)
 
 
 def first_argmax(row: np.ndarray) -> int:
