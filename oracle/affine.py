@@ -177,14 +177,19 @@ _ENGINE = ["numpy"]
 
 
 @contextlib.contextmanager
-def c_accumulation():
-    """Inside the block, bf16 GEMM accumulations run in the C restatement of the same product
-    form (``oracle/c/oracle_gemm.c``, OpenMP over output rows), for model-sized shapes where
-    numpy takes minutes; fp16 ones stay in numpy."""
+def c_accumulation(reverse: bool = False):
+    """Inside the block, bf16 GEMM accumulations run in the C restatement of the same forms
+    (``oracle/c/oracle_gemm.c``, OpenMP over output rows), for model-sized shapes where numpy
+    takes minutes; fp16 ones stay in numpy.  ``reverse`` sums along K in descending order: the
+    same arithmetic in another valid order, to measure how far rounding order alone moves a
+    result."""
+    from . import cgemm
     _ENGINE.append("c")
+    cgemm.set_reverse(reverse)
     try:
         yield
     finally:
+        cgemm.set_reverse(False)
         _ENGINE.pop()
 
 

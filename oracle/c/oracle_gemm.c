@@ -22,6 +22,11 @@ static inline float bf16_to_f32(uint16_t v) {
 /* Rows of x are processed in blocks of this many, each block's accumulators in registers. */
 #define ORACLE_MB 16
 
+/* Summation order along K: 0 ascending, 1 descending (both are valid restatements; their
+ * difference measures how much fp32 rounding order alone moves a result). */
+static int g_reverse = 0;
+void oracle_set_reverse(int r) { g_reverse = r ? 1 : 0; }
+
 /* out[M, N] = x[M, K] . W^T, W MLX-affine (bits 4 | 8), scales/biases as bf16 bits.
  * Returns 0, or -1 when the group sums cannot be allocated. */
 int oracle_qgemm_bf16(int M, int N, int K, int bits, const float* x, const uint32_t* w, const uint16_t* scales,
@@ -44,7 +49,8 @@ int oracle_qgemm_bf16(int M, int N, int K, int bits, const float* x, const uint3
       const int mb = M - m0 < ORACLE_MB ? M - m0 : ORACLE_MB;
       float acc[ORACLE_MB];
       for (int m = 0; m < mb; ++m) acc[m] = 0.0f;
-      for (int g = 0; g < G; ++g) {
+      for (int gi = 0; gi < G; ++gi) {
+        const int g = g_reverse ? G - 1 - gi : gi;
         float q[64];
         for (int i = 0; i < 64 / per; ++i) {
           const uint32_t word = row[g * (64 / per) + i];
@@ -54,7 +60,10 @@ int oracle_qgemm_bf16(int M, int N, int K, int bits, const float* x, const uint3
         for (int m = 0; m < mb; ++m) {
           const float* xr = x + (size_t)(m0 + m) * K + g * 64;
           float d = 0.0f;
-          for (int k = 0; k < 64; ++k) d += xr[k] * q[k];
+          for (int ki = 0; ki < 64; ++ki) {
+            const int k = g_reverse ? 63 - ki : ki;
+            d += xr[k] * q[k];
+          }
           acc[m] += s * d + b * xsum[(size_t)(m0 + m) * G + g];
         }
       }
@@ -87,7 +96,8 @@ void oracle_qgemm_tile_bf16(int M, int N, int K, int bits, const float* x, const
       const int mb = M - m0 < ORACLE_MB ? M - m0 : ORACLE_MB;
       float acc[ORACLE_MB];
       for (int m = 0; m < mb; ++m) acc[m] = 0.0f;
-      for (int g = 0; g < G; ++g) {
+      for (int gi = 0; gi < G; ++gi) {
+        const int g = g_reverse ? G - 1 - gi : gi;
         float dq[64];
         const double s = bf16_to_f32(scales[(size_t)n * G + g]), b = bf16_to_f32(biases[(size_t)n * G + g]);
         for (int i = 0; i < 64 / per; ++i) {
@@ -98,7 +108,10 @@ void oracle_qgemm_tile_bf16(int M, int N, int K, int bits, const float* x, const
         for (int m = 0; m < mb; ++m) {
           const float* xr = x + (size_t)(m0 + m) * K + g * 64;
           float d = acc[m];
-          for (int k = 0; k < 64; ++k) d += xr[k] * dq[k];
+          for (int ki = 0; ki < 64; ++ki) {
+            const int k = g_reverse ? 63 - ki : ki;
+            d += xr[k] * dq[k];
+          }
           acc[m] = d;
         }
       }
@@ -115,7 +128,10 @@ void oracle_gemm_dense_bf16(int M, int N, int K, const float* x, const uint16_t*
     for (int m = 0; m < M; ++m) {
       const float* xr = x + (size_t)m * K;
       float d = 0.0f;
-      for (int k = 0; k < K; ++k) d += xr[k] * bf16_to_f32(row[k]);
+      for (int ki = 0; ki < K; ++ki) {
+        const int k = g_reverse ? K - 1 - ki : ki;
+        d += xr[k] * bf16_to_f32(row[k]);
+      }
       out[(size_t)m * N + n] = d;
     }
   }

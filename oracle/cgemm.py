@@ -37,6 +37,7 @@ def lib():
         L.oracle_qgemm_tile_bf16.argtypes = [ctypes.c_int] * 4 + [p] * 5
         L.oracle_gemm_dense_bf16.argtypes = [ctypes.c_int] * 3 + [p] * 3
         L.oracle_threads.restype = ctypes.c_int
+        L.oracle_set_reverse.argtypes = [ctypes.c_int]
         _lib = L
     return _lib
 
@@ -77,3 +78,8 @@ def gemm_dense(x: np.ndarray, w_bits: np.ndarray) -> np.ndarray:
 
 def threads() -> int:
     return int(lib().oracle_threads())
+
+
+def set_reverse(reverse: bool) -> None:
+    """Sum along K in descending order (True) or ascending (False, the default)."""
+    lib().oracle_set_reverse(int(bool(reverse)))

@@ -81,12 +81,13 @@ TILE_ROWS = 16
 
 
 def linear(x: np.ndarray, W: dict, bits: int, dtype: str, epilogue="none", residual=None, up=None,
-           raw: bool = False) -> np.ndarray:
-    """The library GEMM's arithmetic: fp32 accumulation, epilogue, one rounding (none with raw)."""
+           raw: bool = False, call_rows: int = 0) -> np.ndarray:
+    """The library GEMM's arithmetic: fp32 accumulation, epilogue, one rounding (none with raw).
+    The form follows the row count of the library's call (call_rows, else the rows of x)."""
     xs = A.to_storage(x, dtype)
     res = A.to_storage(residual, dtype) if residual is not None else None
     u = (up["w"], up.get("s"), up.get("b")) if up is not None else None
-    form = "tile" if xs.shape[0] > TILE_ROWS else "product"
+    form = "tile" if (call_rows or xs.shape[0]) > TILE_ROWS else "product"
     out = A.qgemm(xs, W["w"], W.get("s"), W.get("b"), bits=bits, dtype=dtype, epilogue=epilogue, residual=res, up=u,
                   form=form, raw=raw)
     return out if raw else A.from_storage(out, dtype)
@@ -117,19 +118,21 @@ def rope(x: np.ndarray, pos: np.ndarray, table: np.ndarray, dtype: str) -> np.nd
 
 
 def forward(cfg: Config, W: dict, embeds: np.ndarray, table: np.ndarray, raw_logits: bool = False,
-            logits_from: int = 0) -> np.ndarray:
+            logits_from: int = 0, call_rows: int = 0) -> np.ndarray:
     """Causal forward of the whole sequence of input embeddings [T, d] (fp32, rounded to T);
     returns the logits [T - logits_from, V] of the rows from logits_from on (fp32 values of T;
     with raw_logits, before their final rounding).  The LM head is one GEMM over those rows
-    only, as the library runs it, so its row count picks its form."""
+    only, as the library runs it, so its row count picks its form; call_rows > 0 says the library
+    runs the sequence in calls of at most that many rows, which picks the layers' GEMM form."""
     dt = cfg.dtype
     T = embeds.shape[0]
     H, KV, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
     pos = np.arange(T)
     h = embeds.astype(np.float32)
+    rows = min(T, call_rows) if call_rows > 0 else T
     for L in W["layers"]:
         xn = rmsnorm(h, L["attn_norm"], cfg.rms_eps, dt)
-        qkv = linear(xn, L["qkv"], cfg.bits, dt)
+        qkv = linear(xn, L["qkv"], cfg.bits, dt, call_rows=rows)
         q = qkv[:, :H * hd].reshape(T, H, hd)
         k = qkv[:, H * hd:(H + KV) * hd].reshape(T, KV, hd)
         v = qkv[:, (H + KV) * hd:].reshape(T, KV, hd)
@@ -139,10 +142,10 @@ def forward(cfg: Config, W: dict, embeds: np.ndarray, table: np.ndarray, raw_log
         q = rope(q, pos, table, dt)
         k = rope(k, pos, table, dt)
         att = attention(q, k, v, pos, 1.0 / math.sqrt(hd), dt).reshape(T, H * hd)
-        h = linear(att, L["o"], cfg.bits, dt, "residual", residual=h)
+        h = linear(att, L["o"], cfg.bits, dt, "residual", residual=h, call_rows=rows)
         xn = rmsnorm(h, L["mlp_norm"], cfg.rms_eps, dt)
-        act = linear(xn, L["gate"], cfg.bits, dt, "siluGate", up=L["up"])
-        h = linear(act, L["down"], cfg.bits, dt, "residual", residual=h)
+        act = linear(xn, L["gate"], cfg.bits, dt, "siluGate", up=L["up"], call_rows=rows)
+        h = linear(act, L["down"], cfg.bits, dt, "residual", residual=h, call_rows=rows)
     xn = rmsnorm(h[logits_from:], W["final_norm"], cfg.rms_eps, dt)
     return linear(xn, W["lm_head"], cfg.bits, dt, raw=raw_logits)
 
@@ -154,10 +157,14 @@ def embed_sequence(W: dict, prefix: np.ndarray, tokens) -> np.ndarray:
     return np.concatenate(rows, axis=0)
 
 
+SCORE_ROWS = 16  # the library's teacher-forced score runs its positions in calls of 16 rows
+
+
 def score(cfg: Config, W: dict, prefix: np.ndarray, tokens, table: np.ndarray, raw_logits: bool = False) -> np.ndarray:
-    """Logits predicting tokens[0..T) (positions P-1 .. P+T-2), teacher forced."""
+    """Logits predicting tokens[0..T) (positions P-1 .. P+T-2), teacher forced, with the GEMM form
+    of the library's score (calls of at most SCORE_ROWS rows)."""
     x = embed_sequence(W, prefix, list(tokens)[:-1])
-    return forward(cfg, W, x, table, raw_logits, logits_from=prefix.shape[0] - 1)
+    return forward(cfg, W, x, table, raw_logits, logits_from=prefix.shape[0] - 1, call_rows=SCORE_ROWS)
 
 
 def first_argmax(row: np.ndarray) -> int:

@@ -11,14 +11,16 @@ kernels the benchmark uses:
 * Whisper: one encoder and one decoder layer at large-v3-turbo shapes (d 1280, 20 heads of
   64, FFN 5120, 128 mels, 1500 frames, vocab 51866, fp16).
 
-Bars (as in the small-model tests): teacher-forced logits max |error| <= 2e-2 on a sample
-of vocabulary rows (every position's top logit included), measured against the oracle's
-fp32 logits before their bf16 rounding with half an ulp of the device's bf16 output on top
-(logits of these models reach 8-16, where one bf16 ulp is 0.0625: the output format alone
-is coarser than 2e-2 there); greedy tokens equal the
-oracle's argmax wherever its top-2 margin exceeds that tolerance; draft-and-verify emits
-exactly the greedy tokens.  The oracle's GEMM accumulations run in its C restatement
-(same product form) so the check takes seconds.
+Bars.  Teacher-forced logits are compared on a sample of vocabulary rows (4096 random rows
+plus every position's device argmax) against the oracle's fp32 logits before their bf16
+rounding, with half an ulp of the device's bf16 output allowed on top.  At these dims the
+arithmetic is sensitive to rounding order: the oracle itself, run with its K sums ascending
+and then descending (the same operations in two valid orders), moves logits by a few
+hundredths (0.037 measured for a random 2-layer target).  So the small-model bar of 2e-2 is
+applied as max(2e-2, twice that in-test spread), and the relative RMS error of the sampled
+logits must stay within 1e-2.  Greedy tokens equal the oracle's argmax wherever its top-2
+margin exceeds 2e-2; draft-and-verify emits exactly the greedy tokens.  The oracle's GEMM
+accumulations run in its C restatement (same forms) so the check takes seconds.
 """
 import numpy as np
 import pytest
@@ -106,14 +108,18 @@ def _check_model(spec, seed):
     assert got.shape == (T, oc.vocab) and np.isfinite(got).all()
     rows = np.union1d(rng.choice(oc.vocab, 4096, replace=False), got.argmax(axis=1))
     W = _weights(m, oc, rows, toks)
+    table = D.rope_table(P + T, oc.head_dim, oc.rope_theta)
     with A.c_accumulation():
-        ref = D.score(oc, W, A.bf16_from_bits(pre), toks, D.rope_table(P + T, oc.head_dim, oc.rope_theta),
-                      raw_logits=True)
+        ref = D.score(oc, W, A.bf16_from_bits(pre), toks, table, raw_logits=True)
+    with A.c_accumulation(reverse=True):
+        ref_rev = D.score(oc, W, A.bf16_from_bits(pre), toks, table, raw_logits=True)
     m.close()
+    spread = float(np.abs(ref - ref_rev).max())
     g = got[:, rows]
     excess = np.abs(g - ref) - 0.5 * _bf16_ulp(g)
     i = np.unravel_index(int(np.argmax(excess)), excess.shape)
-    return float(excess.max()), float(g[i]), float(ref[i])
+    return {"err": float(excess.max()), "bar": max(LOGIT_TOL, 2.0 * spread), "spread": spread,
+            "rel_rms": A.relative_rms(g, ref), "got": float(g[i]), "ref": float(ref[i])}
 
 
 def _bf16_ulp(v):
@@ -123,13 +129,13 @@ def _bf16_ulp(v):
 
 
 def test_target_at_benchmark_dims_matches_oracle():
-    err, got, ref = _check_model(TARGET, 31)
-    assert err <= LOGIT_TOL, (err, got, ref)
+    r = _check_model(TARGET, 31)
+    assert r["err"] <= r["bar"] and r["rel_rms"] <= 1e-2, r
 
 
 def test_draft_at_benchmark_dims_matches_oracle():
-    err, got, ref = _check_model(DRAFT, 32)
-    assert err <= LOGIT_TOL, (err, got, ref)
+    r = _check_model(DRAFT, 32)
+    assert r["err"] <= r["bar"] and r["rel_rms"] <= 1e-2, r
 
 
 def test_decode_at_benchmark_dims_follows_oracle_and_verify_equals_greedy():
