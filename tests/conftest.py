@@ -10,8 +10,6 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a) and the built library")
-    config.addinivalue_line("markers", "gpu_pending: a GPU parity test of kernels not yet run on a B200 "
-                            "(selected with -m gpu_pending; it joins -m gpu once it has passed there)")
 
 
 def pytest_collection_modifyitems(config, items):
@@ -24,5 +22,5 @@ def pytest_collection_modifyitems(config, items):
         return
     skip = pytest.mark.skip(reason="no CUDA device on this machine")
     for item in items:
-        if "gpu" in item.keywords or "gpu_pending" in item.keywords:
+        if "gpu" in item.keywords:
             item.add_marker(skip)

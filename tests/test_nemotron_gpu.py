@@ -11,7 +11,7 @@ import pytest
 from oracle import decoder as D
 from oracle import nemotron as N
 
-pytestmark = pytest.mark.gpu_pending
+pytestmark = pytest.mark.gpu
 
 
 def _bf16(t):

@@ -1,11 +1,10 @@
 """Token-by-token Whisper decoding (vella_whisper_begin / vella_whisper_step) against the
-whole-loop decode.  Not yet run on a B200: the gpu_pending marker keeps it out of -m gpu until
-it has passed there."""
+whole-loop decode."""
 import pytest
 
 from tests.test_whisper_gpu import mel_of
 
-pytestmark = pytest.mark.gpu_pending
+pytestmark = pytest.mark.gpu
 
 
 def test_token_by_token_equals_the_loop():
