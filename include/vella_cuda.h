@@ -194,6 +194,17 @@ VELLA_API int vella_loop_cut(const int32_t* tokens, int32_t n, int32_t check_eve
  * host-only): angle = pos * theta^(-2i / head_dim) in double, rounded once to fp32 (the
  * non-traditional RoPE of Qwen3ASRTextDecoder.swift:47 and :76-82). */
 VELLA_API int vella_rope_table(int32_t max_seq, int32_t head_dim, float theta, float* out);
+/* Decode-sized forwards (at most 16 rows, no tree) of a model whose shapes suit it (dense or
+ * int4 weights whose GEMMs take the streaming kernel, head_dim 128, no q/k norm) run as one
+ * persistent cooperative launch -- every layer's ops separated by grid barriers, the weights
+ * streaming across them -- instead of seven launches per layer; on by default.  It computes the
+ * per-op kernels' arithmetic (bit for bit for dense weights; for int4 GEMMs that the per-op
+ * path splits over two CTAs per SM, the split-K boundaries differ, a rounding-level difference);
+ * every decode-sized forward agrees with every other bit for bit, so draft-and-verify still
+ * equals greedy.  on = 0 selects the per-op kernels (for comparisons);
+ * on = 1 for a model that cannot take it returns VELLA_E_UNSUPPORTED.  No counterpart in the
+ * reference (MLX schedules its own kernels). */
+VELLA_API int vella_model_set_persistent(vella_model* model, int32_t on);
 /* The configuration the model was created with. */
 VELLA_API int vella_model_get_cfg(const vella_model* model, vella_model_cfg* out);
 VELLA_API size_t vella_model_weight_bytes(const vella_model* model);
@@ -473,7 +484,8 @@ VELLA_API size_t vella_last_error(char* buf, size_t cap);
 
 /* Diagnostic with no counterpart in the reference: nonzero when a TMA/tensor-core pipeline
  * wait inside a kernel ran out of time since the last clear (bits 0-7: small-M streaming GEMM,
- * bits 8-15: tensor-core GEMM).  The kernel that gave up finished without its result.
+ * bits 8-15: tensor-core GEMM, bits 16-23: persistent decode forward).  The kernel that gave
+ * up finished without its result.
  * Synchronises with the device; clear != 0 resets the flags. */
 VELLA_API int32_t vella_fault_flags(int32_t clear);
 

@@ -100,8 +100,9 @@ size_t vella_last_error(char* buf, size_t cap) {
 int32_t vella_fault_flags(int32_t clear) {
   const int st = stream_fault_status(clear);
   const int tc = tc_fault_status(clear);
-  if (st < 0 || tc < 0) return -1;
-  return (st & 0xFF) | ((tc & 0xFF) << 8);
+  const int fw = fwd_fault_status(clear);
+  if (st < 0 || tc < 0 || fw < 0) return -1;
+  return (st & 0xFF) | ((tc & 0xFF) << 8) | ((fw & 0xFF) << 16);
 }
 
 const char* vella_version(void) { return "vella-b200 0.1 sm_100a"; }

@@ -105,6 +105,7 @@ int stream_launch(const vella_qgemm_desc& d, int P, bool light, const void* x, c
                   const void* bias, const void* residual, void* out, int* flags, float* partial,
                   cudaStream_t stream, const RopeEpi* rope = nullptr);
 int stream_fault_status(int clear);
+int fwd_fault_status(int clear);  // fwd_prog.cu: the persistent decode forward's flags
 
 // tc_gemm.cu
 bool tc_eligible(const vella_qgemm_desc& d);

@@ -374,6 +374,13 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
   std::vector<float> table((size_t)c.max_seq * hd);
   rope_table(c.max_seq, hd, c.rope_theta, table.data());
   VELLA_CUDA_TRY(cudaMemcpy(m->rope, table.data(), table.size() * sizeof(float), cudaMemcpyHostToDevice));
+  if (fwd_prog_model_ok(m)) {  // built now: a forward may first run under graph capture
+    const int rc = fwd_prog_build(m, &m->prog);
+    if (rc) {
+      model_destroy(m);
+      return rc;
+    }
+  }
   *out = m;
   return VELLA_OK;
 }
@@ -382,6 +389,7 @@ void model_destroy(Model* m) {
   if (!m) return;
   cudaSetDevice(m->device);
   cudaDeviceSynchronize();
+  if (m->prog) fwd_prog_destroy(m->prog);
   if (m->arena) cudaFree(m->arena);
   if (m->act_arena) cudaFree(m->act_arena);
   if (m->stream) cudaStreamDestroy(m->stream);
@@ -492,6 +500,13 @@ int model_forward(Model* m, PosRef pr, int rows, int streams, int stream0, const
   if ((rc = launch_embed_rows_dev(dt, m->h, m->embed, prefix, m->prefix_ss, tok, tok_ss, pr, M, P, d, c.vocab,
                                   c.max_seq, m->err, s, tv)))
     return rc;
+  if (!tree && m->prog && m->persistent && M <= kMaxRows && rows * (H / KV) <= kAttnRows) {
+    if ((rc = fwd_prog_run(m, m->prog, pr, rows, streams, stream0, logits_rows, s))) return rc;
+    if (logits_rows > 0)
+      return launch_argmax(dt, m->logits, logits_rows * streams, c.vocab, (size_t)c.vocab, m->ys, m->argmax_sc,
+                           m->nonfinite, s);
+    return VELLA_OK;
+  }
   for (int l = 0; l < c.n_layers; ++l) {
     Layer& L = m->layers[l];
     char* kc = static_cast<char*>(m->kcache(l)) + kv0;

@@ -32,6 +32,8 @@ struct Layer {
   QWeight qkv, o, gate, up, down;
 };
 
+struct FwdProg;  // fwd_prog.cu: the persistent decode forward's program of a model
+
 struct Model {
   vella_model_cfg cfg{};
   int device = 0;
@@ -67,6 +69,8 @@ struct Model {
   int* score_tok = nullptr;  // [max_seq] token ids of vella_model_score
   int* score_P = nullptr;    // prefix length of vella_model_score
   cudaStream_t stream = nullptr;  // stream of the model-level calls (init, score)
+  FwdProg* prog = nullptr;        // persistent decode forward (null: the model's shapes do not suit it)
+  bool persistent = true;         // decode-sized forwards run the persistent kernel when prog exists
 
   void* kcache(int l) const;
   void* vcache(int l) const;
@@ -93,6 +97,15 @@ int model_tensor(Model* m, const std::string& name, int layer, void** ptr, size_
 // With `tree`, the rows are tree nodes (TreeView): pr then gives each stream's root slot.
 int model_forward(Model* m, PosRef pr, int rows, int streams, int stream0, const int* tok, int tok_ss, const int* P,
                   int logits_rows, cudaStream_t s, const TreeView* tree = nullptr);
+
+// Persistent decode forward (fwd_prog.cu): one cooperative launch per forward of at most 16
+// rows, bit-identical to the per-op kernels.  fwd_prog_run expects the rows' embeddings in m->h
+// and leaves the logits of the last logits_rows rows of every stream in m->logits.
+bool fwd_prog_model_ok(const Model* m);
+int fwd_prog_build(Model* m, FwdProg** out);
+void fwd_prog_destroy(FwdProg* p);
+int fwd_prog_run(Model* m, FwdProg* p, PosRef pr, int rows, int streams, int stream0, int logits_rows, cudaStream_t s);
+int fwd_fault_status(int clear);
 
 // GEMM with the model's workspace (rope: the streaming kernel's RoPE + KV-append epilogue).
 int model_gemm(Model* m, const QWeight& w, const void* x, int rows, void* out, int epilogue, const void* residual,

@@ -744,9 +744,10 @@ namespace {
 // A GEMM pipeline whose wait ran out of time finished without its result: the decode that
 // used it is void.  Checked once per prefill and per decode call.
 int pipeline_faults() {
-  const int st = stream_fault_status(1), tc = tc_fault_status(1);
-  if (st < 0 || tc < 0) return fail(VELLA_E_CUDA, "cannot read the kernel fault flags");
-  if (st || tc) return fail(VELLA_E_CUDA, "a GEMM pipeline wait timed out (flags 0x%x / 0x%x)", st, tc);
+  const int st = stream_fault_status(1), tc = tc_fault_status(1), fw = fwd_fault_status(1);
+  if (st < 0 || tc < 0 || fw < 0) return fail(VELLA_E_CUDA, "cannot read the kernel fault flags");
+  if (st || tc || fw)
+    return fail(VELLA_E_CUDA, "a pipeline wait timed out (flags 0x%x / 0x%x / 0x%x)", st, tc, fw);
   return VELLA_OK;
 }
 
@@ -1125,6 +1126,15 @@ int vella_rope_table(int32_t max_seq, int32_t head_dim, float theta, float* out)
   if (!out || max_seq < 1 || head_dim < 2 || head_dim % 2 || !(theta > 0.0f))
     return fail(VELLA_E_INVALID, "vella_rope_table: %d positions, head_dim %d, theta %g", max_seq, head_dim, (double)theta);
   rope_table(max_seq, head_dim, theta, out);
+  return VELLA_OK;
+}
+
+int vella_model_set_persistent(vella_model* model, int32_t on) {
+  last_error_slot().clear();
+  if (!model) return fail(VELLA_E_INVALID, "vella_model_set_persistent: NULL model");
+  if (on && !model->prog)
+    return fail(VELLA_E_UNSUPPORTED, "vella_model_set_persistent: this model's shapes do not suit the persistent forward");
+  model->persistent = on != 0;
   return VELLA_OK;
 }
 

@@ -330,6 +330,7 @@ struct Epi {
   int gate, has_bias, has_res, gelu, rope;
   const RopeEpi* re;  // the RoPE epilogue's operands (rope != 0)
   int* fault;      // the kernel's fault flags (bit 4: a gather wait ran out of time)
+  const unsigned* abort = nullptr;  // when set and nonzero, a gather stops waiting
 };
 
 // End of a row block (or of a segment of this CTA's range) for one consumer warp: publish the
@@ -378,7 +379,7 @@ __device__ __forceinline__ void flush_rowblock(const Epi& a, int c, int rb, bool
         if (ld_flag(f) == 0) {
           const long long t0 = clock64();
           while (ld_flag(f) == 0) {
-            if (clock64() - t0 > kWaitCycles) {
+            if ((a.abort && *reinterpret_cast<const volatile unsigned*>(a.abort)) || clock64() - t0 > kWaitCycles) {
               atomicOr(a.fault, 16);
               break;
             }

@@ -68,6 +68,7 @@ for _name, _res, _args in [
     ("vella_spec_decode_batch", ctypes.c_int, [_vp, _i32, _i32, _pi32, _pi32]),
     ("vella_spec_get_stats", ctypes.c_int, [_vp, ctypes.POINTER(SpecStats)]),
     ("vella_spec_set_fault", ctypes.c_int, [_vp, _i32]),
+    ("vella_model_set_persistent", ctypes.c_int, [_vp, _i32]),
     ("vella_spec_tensor", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_size_t)]),
     ("vella_spec_reset", ctypes.c_int, [_vp]),
 ]:
@@ -127,6 +128,11 @@ class Model:
         p, n = _vp(), ctypes.c_size_t()
         _lib.check(_lib.lib().vella_model_tensor(self.handle, name.encode(), layer, ctypes.byref(p), ctypes.byref(n)))
         return p.value, n.value
+
+    def set_persistent(self, on: bool):
+        """Decode-sized forwards as one persistent launch (the default where the shapes allow)
+        or as per-op kernels (the same arithmetic; int4 GEMMs may differ in the last bits)."""
+        _lib.check(_lib.lib().vella_model_set_persistent(self.handle, int(bool(on))))
 
     def weight_bytes(self) -> int:
         return int(_lib.lib().vella_model_weight_bytes(self.handle))
