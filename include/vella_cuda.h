@@ -197,7 +197,8 @@ VELLA_API int vella_rope_table(int32_t max_seq, int32_t head_dim, float theta, f
 /* Decode-sized forwards (at most 16 rows, no tree) of a model whose shapes suit it (dense or
  * int4 weights whose GEMMs take the streaming kernel, head_dim 128, no q/k norm) run as one
  * persistent cooperative launch -- every layer's ops separated by grid barriers, the weights
- * streaming across them -- instead of seven launches per layer; on by default.  It computes the
+ * streaming across them -- instead of seven launches per layer; off by default (the per-op
+ * kernels are faster at the benchmark's 30B-class shapes).  It computes the
  * per-op kernels' arithmetic (bit for bit for dense weights; for int4 GEMMs that the per-op
  * path splits over two CTAs per SM, the split-K boundaries differ, a rounding-level difference);
  * every decode-sized forward agrees with every other bit for bit, so draft-and-verify still

@@ -2,16 +2,18 @@
 the per-op kernels and the oracle, on small models with head_dim 128 (the shapes it serves).
 
 Bars: dense weights -> logits bit-identical to the per-op path (same arithmetic, same unit
-partition); int4 weights -> within 2e-2 of the per-op path and of the oracle (its large GEMMs'
-split-K boundaries differ from the per-op path's two CTAs per SM); draft-and-verify with the
-persistent forward emits exactly its greedy tokens, single stream and three streams; a 5:1
-query-head grouping; switching it off and on is allowed only where the shapes suit it.
+partition); int4 weights -> within 2e-2 of the per-op path, and of the oracle's fp32 logits
+plus half a bf16 ulp, widened to twice the oracle's own rounding-order spread (its large
+GEMMs' split-K boundaries differ from the per-op path's two CTAs per SM); draft-and-verify
+with the persistent forward emits exactly its greedy tokens, single stream and three streams;
+a 5:1 query-head grouping; switching it on is refused where the shapes do not suit it.
 """
 import numpy as np
 import pytest
 
 from oracle import affine as A
 from oracle import decoder as D
+from tests.test_baseline_shapes_gpu import _bf16_ulp
 from tests.test_decode_gpu import LOGIT_TOL, oracle_weights, prefix_of
 
 pytestmark = pytest.mark.gpu
@@ -22,6 +24,7 @@ def _model(bits, d=256, H=2, KV=1, ffn=512, V=1000, layers=2, seed=1, std=0.05, 
     mc = VD.ModelConfig(layers, d, H, KV, 128, ffn, V, bits=bits, max_seq=256, max_prefix=64, **kw)
     m = VD.Model(mc)
     m.init_random(seed, std)
+    m.set_persistent(True)
     return m, D.Config(layers, d, H, KV, 128, ffn, V, bits=bits)
 
 
@@ -49,8 +52,19 @@ def test_int4_logits_match_per_op_path_and_oracle():
     on, off = _score(m, pre, toks, True), _score(m, pre, toks, False)
     assert np.isfinite(on).all()
     assert np.abs(on - off).max() <= LOGIT_TOL
-    ref = D.score(oc, oracle_weights(m, oc), A.bf16_from_bits(pre), toks, D.rope_table(64, 128, oc.rope_theta))
-    assert np.abs(on - ref).max() <= LOGIT_TOL
+    # against the oracle's fp32 logits before their bf16 rounding, half an ulp of the device's
+    # bf16 output allowed on top (logits of magnitude 2..4 have an ulp of 1.6e-2), and the bar
+    # widened to twice the oracle's own rounding-order spread (its K sums ascending vs
+    # descending) where that exceeds 2e-2
+    W, table = oracle_weights(m, oc), D.rope_table(64, 128, oc.rope_theta)
+    with A.c_accumulation():
+        ref = D.score(oc, W, A.bf16_from_bits(pre), toks, table, raw_logits=True)
+    with A.c_accumulation(reverse=True):
+        ref_rev = D.score(oc, W, A.bf16_from_bits(pre), toks, table, raw_logits=True)
+    spread = float(np.abs(ref - ref_rev).max())
+    err = float((np.abs(on - ref) - 0.5 * _bf16_ulp(on)).max())
+    assert err <= max(LOGIT_TOL, 2.0 * spread), (err, spread)
+    assert A.relative_rms(on, ref) <= 1e-2
     m.close()
 
 
@@ -95,7 +109,14 @@ def test_three_streams_verify_in_one_persistent_forward():
     spec = sb.decode_batch(32, VD.DECODE_SPEC)
     assert np.array_equal(spec, greedy)
     sb.close()
-    for x in (t, d):
+    t1, _ = _model(4, d=512, H=4, KV=2, ffn=1024, seed=21)
+    d1, _ = _model(0, seed=22)
+    for j in range(S):
+        g = VD.SpecDecoder(t1, d1, k=4)
+        g.set_prefix(pre_t[j], pre_d[j], 16)
+        assert g.decode_greedy(32).tokens == list(greedy[j]), j
+        g.close()
+    for x in (t, d, t1, d1):
         x.close()
 
 

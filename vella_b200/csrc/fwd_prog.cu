@@ -59,18 +59,27 @@ namespace {
 using namespace sk;
 
 enum : int { kOpNorm = 1, kOpGemm = 2, kOpAttn = 3, kOpCombine = 4 };
-constexpr int kMaps = 8;  // w, up, scales, biases, up scales, up biases, x (NT = 1), x (NT = 2)
+// The program's tensor maps, kernel parameters like the per-op kernels' (a descriptor in global
+// memory costs the TMA unit a fetch whenever it falls out of its cache): per weight kind its
+// weights, scales and biases over every layer (3D: element, row, layer; the layers' tensors
+// sit a constant stride apart in the weights arena).
+enum : int {
+  kMapQkv = 0, kMapO = 3, kMapGate = 6, kMapUp = 9, kMapDown = 12, kMapHead = 15,
+  kProgMaps = 18
+};
 constexpr int kSplit = kAttnCluster;  // key splits of the decode attention
 constexpr int kHD = 128;
+constexpr int kPrepWarps = 2;  // x preparation warps (alternate units), after the producer warp
+constexpr int kFwdThreads = (kRowWarps + 1 + kPrepWarps) * 32;
 
 struct ProgOp {
   int kind;
   // GEMM
   int N, K, rowblocks, nkc, gate, has_res, rope, head;
-  const CUtensorMap* maps;  // kMaps tensor maps (device memory)
+  int wm, um, layer;        // tensor maps: weights (+1 scales, +2 biases), up rows (gate); layer plane
   void* out;
   const void* res;
-  // NORM: y = rmsnorm(x) * w over d, all rows or the logits rows (tail)
+  // GEMM: x = the activation rows; NORM: y = rmsnorm(x) * w over d, all rows or the logits rows (tail)
   const void* x;
   void* y;
   const void* w;
@@ -83,6 +92,7 @@ struct ProgOp {
 
 // Per launch: the rows, their positions and the shared buffers.
 struct FwdArgs {
+  CUtensorMap tm[kProgMaps];
   const ProgOp* ops;
   int nops;
   int M;            // rows = rows_per_stream * streams, stream-major
@@ -109,23 +119,37 @@ struct FwdArgs {
 constexpr int kAttnRS = kHD + 8;                       // padded row stride of the attention tiles
 constexpr int kAttnTile = kAttnChunk * kAttnRS * 2;    // one [64 x 128] tile (bytes)
 
+// Each ring stage is split in two: the weight part (weights, scales, biases; TMA) and the x part
+// (the prepared B fragments and x sums, or a dense unit's raw x slice; written by the prep
+// warps), in two separate rings with the same stage index.  The attention tiles overlay the x
+// ring when it is large enough: during ATTN / COMBINE no x part is written (the next GEMM op's
+// preparation waits for the barrier after COMBINE), while the weight ring keeps filling.
+// Stage counts: as many as fit (4 for int4 at up to 8 rows: 144 KB of weights in flight per SM).
 template <int BITS, int NT>
 struct FwdLayout : Tile<BITS, NT> {
   using TL = Tile<BITS, NT>;
-  static constexpr int NS = 2;
-  static constexpr int KVB_TRY = 2;
-  static constexpr int bar_bytes() { return 4 * NS * 8 + 64; }
+  static constexpr int WST = (TL::TX_W + 1023) / 1024 * 1024;  // weight part of a stage
+  static constexpr int XST = (TL::XS + 1023) / 1024 * 1024;    // x part of a stage
+  static constexpr int kLimit = 227 * 1024;
+  static constexpr int bar_bytes(int ns) { return 4 * ns * 8 + 64; }
   static constexpr int attn_bytes(int kvb) { return (1 + 2 * kvb) * kAttnTile + 2 * kAttnRows * 4; }
-  static constexpr int total(int kvb) { return 1024 + NS * TL::STAGE + TL::RED + attn_bytes(kvb) + 32 * 4 + bar_bytes(); }
-  static constexpr int KVB = total(2) <= 227 * 1024 ? 2 : 1;  // K/V double buffering when it fits
+  static constexpr int total(int ns, int kvb) {
+    return 1024 + ns * (WST + XST) + TL::RED + (ns * XST >= attn_bytes(kvb) ? 0 : attn_bytes(kvb)) + 32 * 4 +
+           bar_bytes(ns);
+  }
+  static constexpr int NS = total(4, 1) <= kLimit ? 4 : total(3, 1) <= kLimit ? 3 : 2;
+  static constexpr int KVB = total(NS, 2) <= kLimit ? 2 : 1;  // K/V double buffering when it fits
   static constexpr int ATTN = attn_bytes(KVB);
-  static constexpr int RING = 0;
-  static constexpr int RED_OFF = NS * TL::STAGE;
-  static constexpr int ATTN_OFF = RED_OFF + TL::RED;
-  static constexpr int NRED_OFF = ATTN_OFF + ATTN;   // the norm's 32 floats
+  static constexpr bool OVERLAY = NS * XST >= ATTN;
+  static constexpr int W_OFF = 0;
+  static constexpr int X_OFF = NS * WST;
+  static constexpr int RED_OFF = X_OFF + NS * XST;
+  static constexpr int ATTN_OFF = OVERLAY ? X_OFF : RED_OFF + TL::RED;
+  static constexpr int NRED_OFF = RED_OFF + TL::RED + (OVERLAY ? 0 : ATTN);  // the norm's 32 floats
   static constexpr int BAR_OFF = NRED_OFF + 32 * 4;
-  static constexpr int TOTAL = 1024 + BAR_OFF + bar_bytes();
-  static_assert(TOTAL <= 227 * 1024, "shared memory");
+  static constexpr int TOTAL = 1024 + BAR_OFF + bar_bytes(NS);
+  static_assert(TOTAL <= kLimit, "shared memory");
+  static_assert(total(2, 1) <= kLimit, "two stages must fit");
 };
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -133,7 +157,16 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+// Shared-memory release / acquire between the threads of a CTA (a barrier seen by one thread
+// handed to another: causality is transitive through the pair).
+__device__ __forceinline__ void st_release_cta(unsigned* p, unsigned v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(saddr(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_cta(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(saddr(p)) : "memory");
+  return v;
+}
 
 template <typename T>
 __device__ __forceinline__ void load8_cg(const T* p, float (&v)[8]) {
@@ -156,19 +189,47 @@ __device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
   }
 }
 
-// The GEMM units of this CTA across the whole program, in program order.
+// The raw x slice of a dense unit ([TOK rows][256 elements], the layout the consumers read
+// their B fragments from) by one warp: rows [0, rows) of a row-major [.. x K] array from
+// column k0, zeros above.
+template <typename T, int NT>
+__device__ __forceinline__ void stage_x_dense(unsigned char* xs, const T* x, int K, int rows, int k0, int lane) {
+  constexpr int TOK = NT * 8;
+  uint4 v[TOK];
+#pragma unroll
+  for (int row = 0; row < TOK; ++row)
+    v[row] = row < rows ? __ldcg(reinterpret_cast<const uint4*>(x + (size_t)row * K + k0) + lane) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int row = 0; row < TOK; ++row) reinterpret_cast<uint4*>(xs + row * 512)[lane] = v[row];
+}
+
+// The GEMM units of this CTA across the whole program, in program order.  The fields of the
+// current op that the unit paths need are kept here (no global load per unit).
 struct GemmCursor {
   int op;           // current GEMM op (nops: done)
   long long u0, u1; // this CTA's unit range of that op
   UnitWalk w;
-  int i;            // units of the op done
-  __device__ GemmCursor() : op(-1), u0(0), u1(0), w(0, 0, 1), i(0) {}
+  int i, n;         // units of the op done, of the op in this CTA
+  int nkc, gate, wm, um, layer, K, head;
+  const void* x;    // the op's activation rows
+  __device__ GemmCursor()
+      : op(-1), u0(0), u1(0), w(0, 0, 1), i(0), n(0), nkc(1), gate(0), wm(0), um(0), layer(0), K(0), head(0), x(nullptr) {}
 };
 
+// A GEMM op's units are spread over its first min(P, U) CTAs, as the per-op kernel caps its grid
+// at the unit count: every CTA between a row block's first and last owner then holds some of
+// its units and publishes its partial sums (a CTA without units never would, and the row
+// block's gather would wait for it).
+__device__ __forceinline__ int op_ctas(const ProgOp& o, int P) {
+  const long long U = (long long)o.rowblocks * o.nkc;
+  return U < P ? (int)U : P;
+}
 __device__ __forceinline__ bool op_has_units(const ProgOp& o, int c, int P, long long* u0, long long* u1) {
   const long long U = (long long)o.rowblocks * o.nkc;
-  *u0 = unit0(c, U, P);
-  *u1 = unit0(c + 1, U, P);
+  const int Pe = op_ctas(o, P);
+  if (c >= Pe) return false;
+  *u0 = unit0(c, U, Pe);
+  *u1 = unit0(c + 1, U, Pe);
   return *u1 > *u0;
 }
 
@@ -177,8 +238,8 @@ __device__ __forceinline__ bool op_has_units(const ProgOp& o, int c, int P, long
 __device__ __forceinline__ bool cursor_next(GemmCursor& g, const FwdArgs& a, int c, int nops) {
   if (g.op >= 0 && g.op < nops) {
     ++g.i;
-    g.w.next(a.ops[g.op].nkc);
-    if (g.i < (int)(g.u1 - g.u0)) return true;
+    g.w.next(g.nkc);
+    if (g.i < g.n) return true;
   }
   for (int o = g.op + 1; o < nops; ++o) {
     const ProgOp& op = a.ops[o];
@@ -190,6 +251,15 @@ __device__ __forceinline__ bool cursor_next(GemmCursor& g, const FwdArgs& a, int
     g.u1 = u1;
     g.w = UnitWalk(u0, u1, op.nkc);
     g.i = 0;
+    g.n = (int)(u1 - u0);
+    g.nkc = op.nkc;
+    g.gate = op.gate;
+    g.wm = op.wm;
+    g.um = op.um;
+    g.layer = op.layer;
+    g.K = op.K;
+    g.head = op.head;
+    g.x = op.x;
     return true;
   }
   g.op = nops;
@@ -215,19 +285,36 @@ __device__ __forceinline__ bool barrier_ready(const FwdArgs& a, int i, bool spin
   return true;
 }
 
+// Abort: the grid-wide flag a.bar[1] (an L2 round trip: read at op barriers and while idle)
+// and this CTA's copy in shared memory (read on the per-unit paths).
 __device__ __forceinline__ bool aborted(const FwdArgs& a) {
   return *reinterpret_cast<volatile unsigned*>(a.bar + 1) != 0;
 }
-__device__ __forceinline__ void set_abort(const FwdArgs& a, int bit) {
+__device__ __forceinline__ void set_abort(const FwdArgs& a, int bit, volatile int* local) {
   atomicOr(&g_fwd_fault, bit);
   atomicExch(a.bar + 1, 1u);
+  *local = 1;
 }
 
 // ---------------------------------------------------------------------------------------
 // NORM: rmsnorm_kernel's arithmetic with the 256 consumer threads (ct = 0..255)
 // ---------------------------------------------------------------------------------------
+constexpr int kNormChunks = 4;  // 8-element chunks of a row per thread: d <= 256 * 8 * 4
+
+// The norm weight slices of consumer thread ct (a constant: loaded before the barrier wait).
 template <typename T>
-__device__ void norm_row(const ProgOp& o, const FwdArgs& a, int row, int ct, float* nred) {
+__device__ __forceinline__ void norm_weights(const ProgOp& o, int ct, uint4 (&wv)[kNormChunks]) {
+  const T* w = static_cast<const T*>(o.w);
+#pragma unroll
+  for (int k = 0; k < kNormChunks; ++k) {
+    const int i = ct * 8 + k * 2048;
+    wv[k] = i < o.d ? *reinterpret_cast<const uint4*>(w + i) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <typename T>
+__device__ void norm_row(const ProgOp& o, const FwdArgs& a, int row, int ct, float* nred,
+                         const uint4 (&wv)[kNormChunks]) {
   using A = Act<T>;
   const int d = o.d;
   int src = row;
@@ -236,12 +323,23 @@ __device__ void norm_row(const ProgOp& o, const FwdArgs& a, int row, int ct, flo
     src = (row / tail) * group + group - tail + row % tail;
   }
   const T* xr = static_cast<const T*>(o.x) + (size_t)src * d;
-  float ss = 0.0f;
-  for (int i = ct * 8; i < d; i += 256 * 8) {
-    float v[8];
-    load8_cg(xr + i, v);
+  uint4 xv[kNormChunks];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+  for (int k = 0; k < kNormChunks; ++k) {
+    const int i = ct * 8 + k * 2048;
+    xv[k] = i < d ? __ldcg(reinterpret_cast<const uint4*>(xr + i)) : make_uint4(0, 0, 0, 0);
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kNormChunks; ++k) {
+    if (ct * 8 + k * 2048 >= d) break;
+    const uint32_t w4[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float v0 = A::lo(w4[j]), v1 = A::hi(w4[j]);
+      ss = fmaf(v0, v0, ss);
+      ss = fmaf(v1, v1, ss);
+    }
   }
   ss = warp_sum(ss);
   if ((ct & 31) == 0) nred[ct >> 5] = ss;
@@ -254,16 +352,17 @@ __device__ void norm_row(const ProgOp& o, const FwdArgs& a, int row, int ct, flo
   named_sync(1, 256);
   const float r = 1.0f / sqrtf(nred[8] / (float)d + o.eps);
   T* out = static_cast<T*>(o.y) + (size_t)row * d;
-  const T* w = static_cast<const T*>(o.w);
-  for (int i = ct * 8; i < d; i += 256 * 8) {
-    float v[8], g[8];
-    load8_cg(xr + i, v);
-    load8(w + i, g);
+#pragma unroll
+  for (int k = 0; k < kNormChunks; ++k) {
+    const int i = ct * 8 + k * 2048;
+    if (i >= d) break;
+    const uint32_t xw[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
+    const uint32_t gw[4] = {wv[k].x, wv[k].y, wv[k].z, wv[k].w};
     uint32_t pk[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float a0 = g[2 * j] * A::to_f(A::from_f(v[2 * j] * r));
-      const float a1 = g[2 * j + 1] * A::to_f(A::from_f(v[2 * j + 1] * r));
+      const float a0 = A::lo(gw[j]) * A::to_f(A::from_f(A::lo(xw[j]) * r));
+      const float a1 = A::hi(gw[j]) * A::to_f(A::from_f(A::hi(xw[j]) * r));
       const T t0 = A::from_f(a0), t1 = A::from_f(a1);
       pk[j] = (uint32_t)reinterpret_cast<const unsigned short&>(t0) |
               ((uint32_t)reinterpret_cast<const unsigned short&>(t1) << 16);
@@ -275,7 +374,10 @@ __device__ void norm_row(const ProgOp& o, const FwdArgs& a, int row, int ct, flo
 
 // ---------------------------------------------------------------------------------------
 // ATTN / COMBINE: the decode attention (one query block per stream, keys split 8 ways) with
-// the 128 threads of consumer warps 0..3 (t = 0..127)
+// the 256 consumer threads (t = 0..255).  Warps w and w + 4 hold the same 16 head rows: both
+// compute their scores and softmax (the same operations, so the same values), and each
+// accumulates one half of the head dimension -- every output element gets the per-op
+// kernel's arithmetic with half its accumulator registers.
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src),
@@ -317,11 +419,12 @@ __device__ __forceinline__ size_t apart_item(const FwdArgs& a, int bz, int kvh, 
 template <typename T, int KVB>
 __device__ void attn_split(const ProgOp& o, const FwdArgs& a, int bz, int kvh, int split, int t, unsigned char* sm) {
   constexpr int C = kAttnChunk, RS = kAttnRS, HD = kHD;
-  constexpr int NK = HD / 16, ND = HD / 8;
+  constexpr int NK = HD / 16, ND = HD / 8, NH = ND / 2;  // NH: 8-column output tiles per half
   T* Qs = reinterpret_cast<T*>(sm);
   T* Ks = reinterpret_cast<T*>(sm + kAttnTile);
   T* Vs = reinterpret_cast<T*>(sm + (1 + KVB) * kAttnTile);
   const int warp = t >> 5, lane = t & 31;
+  const int rw = warp & 3, dh = warp >> 2;  // row warp (16 head rows), head-dimension half
   const int r = lane >> 2, cq = lane & 3;
   const int GQ = a.H / a.KV;
   const int pos0 = a.pr.group ? a.pr.base[bz * a.pr.stride] + a.pr.off : *a.pr.base + a.pr.off;
@@ -334,7 +437,7 @@ __device__ void attn_split(const ProgOp& o, const FwdArgs& a, int bz, int kvh, i
   const long long kvo = a.kv0 + (long long)bz * a.kv_ss + (long long)kvh * a.max_seq * HD;
   const T* kbase = static_cast<const T*>(o.kc) + kvo;
   const T* vbase = static_cast<const T*>(o.vc) + kvo;
-  for (int e = t; e < kAttnRows * (HD / 8); e += 128) {
+  for (int e = t; e < kAttnRows * (HD / 8); e += 256) {
     const int hr = e / (HD / 8), d8 = (e % (HD / 8)) * 8;
     const bool ok = hr < QR;
     const T* src = ok ? q + (size_t)(hr / GQ) * a.H * HD + (size_t)(kvh * GQ + hr % GQ) * HD + d8 : q;
@@ -345,7 +448,7 @@ __device__ void attn_split(const ProgOp& o, const FwdArgs& a, int bz, int kvh, i
     const int k0 = c * C;
     T* kd = Ks + buf * C * RS;
     T* vd = Vs + buf * C * RS;
-    for (int e = t; e < C * (HD / 8); e += 128) {
+    for (int e = t; e < C * (HD / 8); e += 256) {
       const int j = e / (HD / 8), d8 = (e % (HD / 8)) * 8;
       const bool ok = k0 + j < kend;
       const size_t off = ok ? (size_t)(k0 + j) * HD + d8 : 0;
@@ -354,11 +457,11 @@ __device__ void attn_split(const ProgOp& o, const FwdArgs& a, int bz, int kvh, i
     }
     cp_async_commit();
   };
-  const int hr0 = warp * 16 + r, hr1 = hr0 + 8;
-  const bool live = warp * 16 < QR;
-  float ov[ND][4];
+  const int hr0 = rw * 16 + r, hr1 = hr0 + 8;
+  const bool live = rw * 16 < QR;
+  float ov[NH][4];
 #pragma unroll
-  for (int u = 0; u < ND; ++u) ov[u][0] = ov[u][1] = ov[u][2] = ov[u][3] = 0.0f;
+  for (int u = 0; u < NH; ++u) ov[u][0] = ov[u][1] = ov[u][2] = ov[u][3] = 0.0f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
   const int qi0 = hr0 / GQ, qi1 = hr1 / GQ;
   const int lim0 = pos0 + qi0, lim1 = pos0 + qi1;
@@ -379,14 +482,14 @@ __device__ void attn_split(const ProgOp& o, const FwdArgs& a, int bz, int kvh, i
       fetch(c, 0);
       cp_async_wait<0>();
     }
-    named_sync(6, 128);
+    named_sync(6, 256);
     if (first) {
       first = false;
       if (live) {
 #pragma unroll
         for (int kk = 0; kk < NK; ++kk) {
           const int idx = lane >> 3;
-          ldsm4(qf[kk], Qs + (warp * 16 + (idx & 1) * 8 + (lane & 7)) * RS + kk * 16 + (idx >> 1) * 8);
+          ldsm4(qf[kk], Qs + (rw * 16 + (idx & 1) * 8 + (lane & 7)) * RS + kk * 16 + (idx >> 1) * 8);
         }
       }
     }
@@ -444,7 +547,7 @@ __device__ void attn_split(const ProgOp& o, const FwdArgs& a, int bz, int kvh, i
       m0 = mn0;
       m1 = mn1;
 #pragma unroll
-      for (int u = 0; u < ND; ++u) {
+      for (int u = 0; u < NH; ++u) {
         ov[u][0] *= al0; ov[u][1] *= al0;
         ov[u][2] *= al1; ov[u][3] *= al1;
       }
@@ -461,10 +564,10 @@ __device__ void attn_split(const ProgOp& o, const FwdArgs& a, int bz, int kvh, i
           pl[i] = pack2<T>(f[i][0] - Act<T>::to_f(hv[0]), f[i][1] - Act<T>::to_f(hv[1]));
         }
 #pragma unroll
-        for (int u = 0; u < ND; u += 2) {
+        for (int u = 0; u < NH; u += 2) {
           uint32_t b[4];
           const int idx = lane >> 3;
-          ldsm4t(b, vt + (16 * j + (idx & 1) * 8 + (lane & 7)) * RS + 8 * (u + (idx >> 1)));
+          ldsm4t(b, vt + (16 * j + (idx & 1) * 8 + (lane & 7)) * RS + 8 * (dh * NH + u + (idx >> 1)));
           mma16816<T>(ov[u], ph, b[0], b[1]);
           mma16816<T>(ov[u], pl, b[0], b[1]);
           mma16816<T>(ov[u + 1], ph, b[2], b[3]);
@@ -472,23 +575,23 @@ __device__ void attn_split(const ProgOp& o, const FwdArgs& a, int bz, int kvh, i
         }
       }
     }
-    named_sync(6, 128);  // every warp is done with this buffer before it is refilled
+    named_sync(6, 256);  // every warp is done with this buffer before it is refilled
     if constexpr (KVB == 2) buf ^= 1;
   }
   cp_async_wait<0>();
-  named_sync(6, 128);
+  named_sync(6, 256);
   // partial rows to global memory (every head row of the block, zeros where no key was seen)
   float* pp = a.apart + apart_item(a, bz, kvh, split);
   float* Mx = pp;
   float* Ls = pp + kAttnRows;
   float* Os = pp + 2 * kAttnRows;
-  if (cq == 0) {
+  if (cq == 0 && dh == 0) {
     Mx[hr0] = m0; Ls[hr0] = l0;
     Mx[hr1] = m1; Ls[hr1] = l1;
   }
 #pragma unroll
-  for (int u = 0; u < ND; ++u) {
-    const int dd = 8 * u + 2 * cq;
+  for (int u = 0; u < NH; ++u) {
+    const int dd = 8 * (dh * NH + u) + 2 * cq;
     *reinterpret_cast<float2*>(Os + hr0 * HD + dd) = make_float2(ov[u][0], ov[u][1]);
     *reinterpret_cast<float2*>(Os + hr1 * HD + dd) = make_float2(ov[u][2], ov[u][3]);
   }
@@ -502,7 +605,7 @@ __device__ void attn_combine(const FwdArgs& a, int bz, int kvh, int split, int t
   const int GQ = a.H / a.KV;
   const int QR = a.rows * GQ;
   const int d = t % HD, rset = t / HD;
-  constexpr int RSETS = 128 / HD;
+  constexpr int RSETS = 256 / HD;
   T* out = static_cast<T*>(a.attn) + (size_t)bz * a.rows * a.H * HD;
   for (int qr = split + kSplit * rset; qr < QR; qr += kSplit * RSETS) {
     float mr[kSplit], lr[kSplit], orr[kSplit];
@@ -531,26 +634,32 @@ __device__ void attn_combine(const FwdArgs& a, int bz, int kvh, int split, int t
 // the kernel
 // ---------------------------------------------------------------------------------------
 template <typename T, int BITS, int NT>
-__global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant__ FwdArgs a) {
+__global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_constant__ FwdArgs a) {
   using LY = FwdLayout<BITS, NT>;
   constexpr int NS = LY::NS, UG = LY::UG, BPG = SFmt<BITS>::BPG;
   constexpr bool kQuant = BITS != 0;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (saddr(smem_raw) & 1023u)) & 1023u);
+  unsigned char* wring = smem + LY::W_OFF;
+  unsigned char* xring = smem + LY::X_OFF;
   float* red = reinterpret_cast<float*>(smem + LY::RED_OFF);
   unsigned char* asm_ = smem + LY::ATTN_OFF;
   float* nred = reinterpret_cast<float*>(smem + LY::NRED_OFF);
   uint64_t* fullw = reinterpret_cast<uint64_t*>(smem + LY::BAR_OFF);
-  uint64_t* fullx = fullw + NS;
-  uint64_t* empty = fullx + NS;
+  uint64_t* empty = fullw + NS;
   uint64_t* prepared = empty + NS;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x, P = a.P, nops = a.nops;
+  __shared__ int s_abort_;
+  __shared__ unsigned s_passed_;  // the last op whose barrier a consumer thread saw pass (+ 1)
+  volatile int* s_abort = &s_abort_;
+  unsigned* s_passed = &s_passed_;
   if (tid == 0) {
+    s_abort_ = 0;
+    s_passed_ = 0;
     for (int s = 0; s < NS; ++s) {
       mbar_init(&fullw[s], 1);
-      mbar_init(&fullx[s], 1);
       mbar_init(&empty[s], kRowWarps);
       mbar_init(&prepared[s], 32);
     }
@@ -559,101 +668,94 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
   __syncthreads();
 
   if (warp == kProducerWarp) {
-    // ------------------------------- producer (one thread) ------------------------------
+    // ----------------------- weight producer (one thread) -----------------------------
+    // Weights do not depend on the activations: unit j's copies go out as soon as its stage is
+    // free (unit j - NS consumed), across barriers and non-GEMM ops.
     if (lane != 0) return;
-    GemmCursor gw, gx;  // next unit whose weights / x are to be issued
-    bool w_more = cursor_next(gw, a, c, nops), x_more = cursor_next(gx, a, c, nops);
-    long long wi = 0, xi = 0;  // units issued (weights / x); unit j uses stage j % NS
-    int ready_op = 0;          // ops known to have their inputs ready
-    const long long t0 = clock64();
-    while (x_more) {
-      if (aborted(a)) break;
-      bool progress = false;
-      if (xi < wi) {  // x of the oldest unit whose weights are in flight
-        const int op = gx.op;
-        if (op < ready_op || barrier_ready(a, op, false)) {
-          if (op >= ready_op) {
-            ready_op = op + 1;
-            fence_proxy_async_global();
-          }
-          const ProgOp& o = a.ops[op];
-          const int s = (int)(xi % NS);
-          unsigned char* st = smem + s * LY::STAGE;
-          const CUtensorMap* xm = o.maps + (NT == 1 ? 6 : 7);
-          mbar_expect_tx(&fullx[s], LY::TX_X);
+    GemmCursor g;
+    long long wi = 0;  // units issued; unit j uses stage j % NS
+    for (bool more = cursor_next(g, a, c, nops); more && !*s_abort; more = cursor_next(g, a, c, nops), ++wi) {
+      const int s = (int)(wi % NS);
+      if (wi >= NS && !mbar_wait(&empty[s], (uint32_t)((wi / NS - 1) & 1))) {
+        set_abort(a, 1, s_abort);
+        break;
+      }
+      uint64_t* bar = &fullw[s];
+      mbar_expect_tx(bar, LY::TX_W);
+      unsigned char* st = wring + s * LY::WST;
+      const int rb = g.w.rb, kc = g.w.kc, layer = g.layer;
+      const int w0 = kc * UG * BPG / 4;
 #pragma unroll
-          for (int j = 0; j < SFmt<BITS>::XCH; ++j)
-            tma2d(st + LY::XOFF + j * LY::XCHUNK, xm, gx.w.kc * UG * 64 + j * 256, 0, &fullx[s]);
-          ++xi;
-          x_more = cursor_next(gx, a, c, nops);
-          progress = true;
+      for (int q = 0; q < SFmt<BITS>::WCH; ++q) {
+        unsigned char* dst = st + q * LY::WCHUNK;
+        if (g.gate) {
+          tma3d(dst, &a.tm[g.wm], w0 + q * 32, rb * 64, layer, bar);
+          tma3d(dst + 64 * 128, &a.tm[g.um], w0 + q * 32, rb * 64, layer, bar);
+        } else {
+          tma3d(dst, &a.tm[g.wm], w0 + q * 32, rb * 128, layer, bar);
         }
       }
-      if (w_more && wi - xi < NS) {
-        const int s = (int)(wi % NS);
-        const long long use = wi / NS;
-        if (use == 0 || mbar_try(&empty[s], (uint32_t)((use - 1) & 1))) {
-          const ProgOp& o = a.ops[gw.op];
-          const int rb = gw.w.rb, kc = gw.w.kc;
-          unsigned char* st = smem + s * LY::STAGE;
-          const int w0 = kc * UG * BPG / 4;
-          mbar_expect_tx(&fullw[s], LY::TX_W);
-#pragma unroll
-          for (int j = 0; j < SFmt<BITS>::WCH; ++j) {
-            unsigned char* dst = st + j * LY::WCHUNK;
-            if (o.gate) {
-              tma2d(dst, o.maps + 0, w0 + j * 32, rb * 64, &fullw[s]);
-              tma2d(dst + 64 * 128, o.maps + 1, w0 + j * 32, rb * 64, &fullw[s]);
-            } else {
-              tma2d(dst, o.maps + 0, w0 + j * 32, rb * 128, &fullw[s]);
-            }
-          }
-          if constexpr (kQuant) {
-            unsigned char* ssb = st + LY::W_BYTES;
-            if (o.gate) {
-              tma2d(ssb, o.maps + 2, kc * 8, rb * 64, &fullw[s]);
-              tma2d(ssb + 64 * 16, o.maps + 4, kc * 8, rb * 64, &fullw[s]);
-              tma2d(ssb + kSlots * 16, o.maps + 3, kc * 8, rb * 64, &fullw[s]);
-              tma2d(ssb + kSlots * 16 + 64 * 16, o.maps + 5, kc * 8, rb * 64, &fullw[s]);
-            } else {
-              tma2d(ssb, o.maps + 2, kc * 8, rb * 128, &fullw[s]);
-              tma2d(ssb + kSlots * 16, o.maps + 3, kc * 8, rb * 128, &fullw[s]);
-            }
-          }
-          ++wi;
-          w_more = cursor_next(gw, a, c, nops);
-          progress = true;
+      if constexpr (kQuant) {
+        unsigned char* ssb = st + LY::W_BYTES;
+        if (g.gate) {
+          tma3d(ssb, &a.tm[g.wm + 1], kc * 8, rb * 64, layer, bar);
+          tma3d(ssb + 64 * 16, &a.tm[g.um + 1], kc * 8, rb * 64, layer, bar);
+          tma3d(ssb + kSlots * 16, &a.tm[g.wm + 2], kc * 8, rb * 64, layer, bar);
+          tma3d(ssb + kSlots * 16 + 64 * 16, &a.tm[g.um + 2], kc * 8, rb * 64, layer, bar);
+        } else {
+          tma3d(ssb, &a.tm[g.wm + 1], kc * 8, rb * 128, layer, bar);
+          tma3d(ssb + kSlots * 16, &a.tm[g.wm + 2], kc * 8, rb * 128, layer, bar);
         }
-      }
-      if (!progress) {
-        if (clock64() - t0 > 8 * kWaitCycles) {  // the whole program: far above any real forward
-          set_abort(a, 1);
-          break;
-        }
-        __nanosleep(32);
       }
     }
-    // never leave with copies in flight: the last weight and x fill of every stage
+    // never leave with copies in flight: the last fill of every stage
     for (int q = 0; q < NS; ++q) {
-      const long long fw = wi > q ? (wi - 1 - q) / NS + 1 : 0, fx = xi > q ? (xi - 1 - q) / NS + 1 : 0;
-      if (fw > 0 && !mbar_wait(&fullw[q], (uint32_t)((fw - 1) & 1))) atomicOr(&g_fwd_fault, 2);
-      if (fx > 0 && !mbar_wait(&fullx[q], (uint32_t)((fx - 1) & 1))) atomicOr(&g_fwd_fault, 2);
+      const long long f = wi > q ? (wi - 1 - q) / NS + 1 : 0;
+      if (f > 0 && !mbar_wait(&fullw[q], (uint32_t)((f - 1) & 1))) atomicOr(&g_fwd_fault, 2);
     }
     return;
   }
 
-  if (warp == kPrepWarp) {
-    // ----------------- x preparation: B fragments and group sums, once per stage -----------
-    if constexpr (kQuant) {
-      GemmCursor g;
-      long long j = 0;
-      for (bool more = cursor_next(g, a, c, nops); more; more = cursor_next(g, a, c, nops), ++j) {
-        const int s = (int)(j % NS);
-        const uint32_t ph = (uint32_t)((j / NS) & 1);
-        if (!aborted(a) && !(mbar_wait(&fullw[s], ph) && mbar_wait(&fullx[s], ph))) set_abort(a, 8);
-        if (!aborted(a)) prep_stage<T, BITS, NT>(smem + s * LY::STAGE, lane);
-        mbar_arrive(&prepared[s]);  // also after a fault, so that no consumer waits for it
+  const int LR = a.logits_rows * a.streams;
+  if (warp >= kPrepWarp) {
+    // ------------------ x preparation (two warps, alternate units) -----------------------
+    // Unit j's x slice is read from L2 (plain loads: the SM's TMA queue is busy with weights,
+    // and a slice behind them would land only when they do) once its stage is free (unit
+    // j - NS consumed) and the barrier before its op has passed (published by the consumer
+    // thread that waits on it, or waited on here).  Quantized: the B fragments and group sums;
+    // dense: the raw slice the consumers read their fragments from.  Rows >= M read as zeros.
+    const int pw = warp - kPrepWarp;
+    GemmCursor g;
+    long long j = 0;
+    int ready_op = 0;  // ops whose barrier this warp has seen pass
+    for (bool more = cursor_next(g, a, c, nops); more; more = cursor_next(g, a, c, nops), ++j) {
+      if ((int)(j % kPrepWarps) != pw) continue;
+      const int s = (int)(j % NS);
+      int go = !*s_abort;
+      if (lane == 0 && go) {
+        if (j >= NS && !mbar_wait(&empty[s], (uint32_t)((j / NS - 1) & 1))) {
+          set_abort(a, 8, s_abort);
+          go = 0;
+        }
+        if (go && g.op >= ready_op) {
+          if (ld_acquire_cta(s_passed) < (unsigned)g.op && !barrier_ready(a, g.op, true)) {  // bounded
+            *s_abort = 1;
+            go = 0;
+          } else {
+            ready_op = g.op + 1;
+          }
+        }
       }
+      __syncwarp();  // orders the other lanes' loads after lane 0's acquire
+      go = __shfl_sync(0xffffffffu, go, 0);
+      if (go) {
+        unsigned char* xs = xring + s * LY::XST;
+        const T* x = static_cast<const T*>(g.x);
+        const int rows = g.head ? LR : a.M, k0 = g.w.kc * UG * 64;
+        if constexpr (kQuant) prep_global<T, BITS, NT>(xs, x, g.K, rows, k0, lane);
+        else stage_x_dense<T, NT>(xs, x, g.K, rows, k0, lane);
+      }
+      mbar_arrive(&prepared[s]);  // also after a fault, so that no consumer waits for it
     }
     return;
   }
@@ -662,30 +764,41 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
   const int ct = tid;  // 0..255
   const int r = lane >> 2, cq = lane & 3;
   const int slot0 = 16 * warp + r, slot1 = slot0 + 8;
-  const WOff<BITS> woff(slot0, r, cq);
-  float acc[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.0f;
   long long j = 0;  // GEMM units consumed (ring position)
-  const int LR = a.logits_rows * a.streams;
   __shared__ int s_ok;
   for (int i = 0; i < nops; ++i) {
     // ---- wait for op i's inputs (every CTA done with op i - 1); one CTA-wide verdict, so every
     // branch below that reaches a named barrier is taken by all consumer threads or none ----
-    if (ct == 0) s_ok = !aborted(a) && barrier_ready(a, i, true) && !aborted(a);
+    // the op's descriptor into L1 while the barrier is waited on (its fields are read right after)
+    if (ct * 128 < (int)sizeof(ProgOp))
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char*>(&a.ops[i]) + ct * 128));
+    const ProgOp& o = a.ops[i];
+    uint4 wv[kNormChunks];
+    const int norm_rows = o.tail ? LR : a.M;
+    if (o.kind == kOpNorm && c < norm_rows) norm_weights<T>(o, ct, wv);  // in flight across the wait
+    if (ct == 0) {
+      s_ok = !*s_abort && !aborted(a) && barrier_ready(a, i, true) && !aborted(a);
+      if (!s_ok) *s_abort = 1;
+      else st_release_cta(s_passed, (unsigned)i);  // after the gpu-scope acquire of the barrier
+    }
     named_sync(1, 256);
     const bool ok = s_ok != 0;
-    const ProgOp& o = a.ops[i];
     if (o.kind == kOpGemm) {
       long long u0, u1;
       if (op_has_units(o, c, P, &u0, &u1)) {
+        // accumulators and fragment offsets live for this op only (every row block's flush
+        // leaves acc at zero), so the other ops' code has the registers
+        const WOff<BITS> woff(slot0, r, cq);
+        float acc[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[nt][e] = 0.0f;
         const int nkc = o.nkc;
         RopeEpi re;
         Epi ep;
         ep.bias = nullptr; ep.res = o.res; ep.out = o.out; ep.partial = a.partial; ep.flags = a.flags;
-        ep.N = o.N; ep.mc = o.head ? LR : a.M; ep.P = P; ep.U = (long long)o.rowblocks * nkc; ep.nkc = nkc;
+        ep.N = o.N; ep.mc = o.head ? LR : a.M; ep.P = op_ctas(o, P); ep.U = (long long)o.rowblocks * nkc; ep.nkc = nkc;
         ep.gate = o.gate; ep.has_bias = 0; ep.has_res = o.has_res; ep.gelu = 0; ep.rope = o.rope;
         ep.re = &re; ep.fault = &g_fwd_fault; ep.abort = a.bar + 1;
         if (o.rope) {
@@ -700,12 +813,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         for (int k = 0; k < nunits; ++k, ++j) {
           const int s = (int)(j % NS);
           const uint32_t ph = (uint32_t)((j / NS) & 1);
-          bool have = ok && !aborted(a);
+          bool have = ok && !*s_abort;
           if (have) {
-            have = mbar_wait(&fullw[s], ph) && mbar_wait(&fullx[s], ph) && (!kQuant || mbar_wait(&prepared[s], ph));
-            if (!have) set_abort(a, 4);
+            have = mbar_wait(&fullw[s], ph) && mbar_wait(&prepared[s], ph);
+            if (!have) set_abort(a, 4, s_abort);
           }
-          if (have) consume_stage<T, BITS, NT>(smem + s * LY::STAGE, acc, woff, lane, slot0, slot1);
+          if (have) consume_stage<T, BITS, NT>(wring + s * LY::WST, xring + s * LY::XST, acc, woff, lane, slot0, slot1);
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[s]);
           const int rb = cur.rb;
@@ -718,18 +831,17 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         }
       }
     } else if (o.kind == kOpNorm && ok) {
-      const int rows = o.tail ? LR : a.M;
-      for (int row = c; row < rows; row += P) norm_row<T>(o, a, row, ct, nred);
+      for (int row = c; row < norm_rows; row += P) norm_row<T>(o, a, row, ct, nred, wv);
     } else if (o.kind == kOpAttn && ok) {
       const int items = a.streams * a.KV * kSplit;
       for (int it = c; it < items; it += P) {
-        if (warp < 4) attn_split<T, LY::KVB>(o, a, it / (a.KV * kSplit), (it / kSplit) % a.KV, it % kSplit, ct, asm_);
+        attn_split<T, LY::KVB>(o, a, it / (a.KV * kSplit), (it / kSplit) % a.KV, it % kSplit, ct, asm_);
         named_sync(1, 256);
       }
     } else if (o.kind == kOpCombine && ok) {
       const int items = a.streams * a.KV * kSplit;
       for (int it = c; it < items; it += P)
-        if (warp < 4) attn_combine<T>(a, it / (a.KV * kSplit), (it / kSplit) % a.KV, it % kSplit, ct);
+        attn_combine<T>(a, it / (a.KV * kSplit), (it / kSplit) % a.KV, it % kSplit, ct);
     }
     // ---- arrive: this CTA is done with op i ----
     named_sync(1, 256);
@@ -750,7 +862,7 @@ struct FwdProg {
   int P = 0;
   std::vector<ProgOp> host_ops;
   ProgOp* ops = nullptr;
-  CUtensorMap* maps = nullptr;
+  CUtensorMap tm[kProgMaps];  // copied into every launch's parameters
   float* apart = nullptr;
   float* partial = nullptr;
   int* scratch = nullptr;  // bar[2] + pad, then flags [P][kRowWarps]
@@ -760,47 +872,61 @@ struct FwdProg {
 
 namespace {
 
-int ptr_ok(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
-
-int build_maps(const Model* m, const QWeight& w, const QWeight* up, const void* x, CUtensorMap* out) {
+// The weight maps of one kind (weights, scales, biases of every layer at maps[idx..idx + 2]):
+// 3D over (element, row, layer) with the layers' constant stride in the arena; a single
+// tensor (the LM head) is one plane.
+int kind_maps(const Model* m, int idx, const QWeight* const* per_layer, int layers, int rows_box, CUtensorMap* maps) {
   const vella_model_cfg& c = m->cfg;
-  const bool gate = up != nullptr;
-  const int rows_box = gate ? 64 : 128;
+  const QWeight& w = *per_layer[0];
   const int wbits = c.bits ? c.bits : 16;
-  const uint64_t words = (uint64_t)w.k * wbits / 32, row_bytes = (uint64_t)w.k * wbits / 8;
-  const uint64_t G = w.k / 64;
-  std::memset(out, 0, sizeof(CUtensorMap) * kMaps);
+  const uint64_t words = (uint64_t)w.k * wbits / 32, row_bytes = (uint64_t)w.k * wbits / 8, G = w.k / 64;
+  auto stride = [&](void* QWeight::*f, uint64_t one) -> uint64_t {
+    if (layers == 1) return (one + 15) / 16 * 16;
+    const uint64_t st = (uint64_t)(static_cast<char*>(per_layer[1]->*f) - static_cast<char*>(per_layer[0]->*f));
+    for (int l = 1; l < layers; ++l)
+      if ((uint64_t)(static_cast<char*>(per_layer[l]->*f) - static_cast<char*>(per_layer[0]->*f)) != st * l) return 0;
+    return st % 16 == 0 ? st : 0;
+  };
+  const uint64_t sw = stride(&QWeight::w, w.n * row_bytes);
+  if (!sw) return fail(VELLA_E_UNSUPPORTED, "persistent forward: layer weights not a constant stride apart");
+  int rc = make_tensor_map_3d(&maps[idx], CU_TENSOR_MAP_DATA_TYPE_UINT32, w.w, words, w.n, layers, row_bytes, sw, 32,
+                              rows_box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc || !c.bits) return rc;
+  const uint64_t ss = stride(&QWeight::s, w.n * G * 2), sb = stride(&QWeight::b, w.n * G * 2);
+  if (!ss || !sb) return fail(VELLA_E_UNSUPPORTED, "persistent forward: layer scales not a constant stride apart");
+  if ((rc = make_tensor_map_3d(&maps[idx + 1], CU_TENSOR_MAP_DATA_TYPE_UINT16, w.s, G, w.n, layers, G * 2, ss, 8,
+                               rows_box, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  return make_tensor_map_3d(&maps[idx + 2], CU_TENSOR_MAP_DATA_TYPE_UINT16, w.b, G, w.n, layers, G * 2, sb, 8, rows_box,
+                            CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+int build_prog_maps(const Model* m, CUtensorMap* maps) {
+  const vella_model_cfg& c = m->cfg;
+  const int L = c.n_layers;
+  std::memset(maps, 0, sizeof(CUtensorMap) * kProgMaps);
+  std::vector<const QWeight*> per(L);
+  const struct { int idx; QWeight Layer::*f; int rows_box; } kinds[] = {
+      {kMapQkv, &Layer::qkv, 128}, {kMapO, &Layer::o, 128}, {kMapGate, &Layer::gate, 64},
+      {kMapUp, &Layer::up, 64},    {kMapDown, &Layer::down, 128}};
   int rc;
-  if ((rc = make_tensor_map(&out[0], CU_TENSOR_MAP_DATA_TYPE_UINT32, w.w, words, w.n, row_bytes, 32, rows_box,
-                            CU_TENSOR_MAP_SWIZZLE_128B)))
-    return rc;
-  if (gate && (rc = make_tensor_map(&out[1], CU_TENSOR_MAP_DATA_TYPE_UINT32, up->w, words, up->n, row_bytes, 32,
-                                    rows_box, CU_TENSOR_MAP_SWIZZLE_128B)))
-    return rc;
-  if (c.bits) {
-    if ((rc = make_tensor_map(&out[2], CU_TENSOR_MAP_DATA_TYPE_UINT16, w.s, G, w.n, G * 2, 8, rows_box,
-                              CU_TENSOR_MAP_SWIZZLE_NONE)) ||
-        (rc = make_tensor_map(&out[3], CU_TENSOR_MAP_DATA_TYPE_UINT16, w.b, G, w.n, G * 2, 8, rows_box,
-                              CU_TENSOR_MAP_SWIZZLE_NONE)))
-      return rc;
-    if (gate && ((rc = make_tensor_map(&out[4], CU_TENSOR_MAP_DATA_TYPE_UINT16, up->s, G, up->n, G * 2, 8, rows_box,
-                                       CU_TENSOR_MAP_SWIZZLE_NONE)) ||
-                 (rc = make_tensor_map(&out[5], CU_TENSOR_MAP_DATA_TYPE_UINT16, up->b, G, up->n, G * 2, 8, rows_box,
-                                       CU_TENSOR_MAP_SWIZZLE_NONE))))
-      return rc;
+  for (const auto& k : kinds) {
+    for (int l = 0; l < L; ++l) per[l] = &(m->layers[l].*(k.f));
+    if ((rc = kind_maps(m, k.idx, per.data(), L, k.rows_box, maps))) return rc;
   }
-  // x: the activation buffer's rows (garbage rows beyond a call's M feed output columns that
-  // are never stored); one map per token tile height
-  for (int nt = 1; nt <= 2; ++nt)
-    if ((rc = make_tensor_map(&out[5 + nt], CU_TENSOR_MAP_DATA_TYPE_UINT16, x, w.k, m->max_rows, (uint64_t)w.k * 2, 256,
-                              nt * 8, CU_TENSOR_MAP_SWIZZLE_NONE)))
-      return rc;
+  const QWeight* head = &m->lm_head;
+  if ((rc = kind_maps(m, kMapHead, &head, 1, 128, maps))) return rc;
   return VELLA_OK;
 }
 
-ProgOp gemm_op(const QWeight& w, const QWeight* up, void* out, const void* res, int rope, int head, int bits) {
+ProgOp gemm_op(const QWeight& w, const QWeight* up, const void* x, void* out, const void* res, int rope, int head,
+               int bits, int wm, int layer) {
   ProgOp o{};
   o.kind = kOpGemm;
+  o.wm = wm;
+  o.um = kMapUp;
+  o.x = x;
+  o.layer = layer;
   o.gate = up != nullptr;
   o.N = w.n;
   o.K = w.k;
@@ -831,13 +957,14 @@ bool fwd_prog_model_ok(const Model* m) {
       c.n_heads / c.n_kv_heads > kAttnMaxGQ)
     return false;
   const int kq = c.bits ? 512 : 256;
-  return c.d_model % kq == 0 && (c.n_heads * kHD) % kq == 0 && c.ffn % kq == 0 && c.d_model % 8 == 0;
+  return c.d_model % kq == 0 && (c.n_heads * kHD) % kq == 0 && c.ffn % kq == 0 && c.d_model % 8 == 0 &&
+         c.d_model <= 256 * 8 * kNormChunks;
 }
 
 void fwd_prog_destroy(FwdProg* p) {
   if (!p) return;
   if (p->device >= 0) cudaSetDevice(p->device);
-  for (void* q : {(void*)p->ops, (void*)p->maps, (void*)p->apart, (void*)p->partial, (void*)p->scratch})
+  for (void* q : {(void*)p->ops, (void*)p->apart, (void*)p->partial, (void*)p->scratch})
     if (q) cudaFree(q);
   delete p;
 }
@@ -850,26 +977,17 @@ int fwd_prog_build(Model* m, FwdProg** out) {
   p->P = num_sms(m->device);
   const int L = c.n_layers;
   const int nops = 8 * L + 2;
-  std::vector<CUtensorMap> maps((size_t)(4 * L + 1) * kMaps);
   std::vector<ProgOp> ops;
   ops.reserve(nops);
   const int bits = c.bits;
-  int rc = VELLA_OK;
-  int mi = 0;  // GEMM index (tensor maps)
-  auto add_gemm = [&](ProgOp o, const QWeight& w, const QWeight* up, const void* x) {
-    if (rc) return;
-    rc = build_maps(m, w, up, x, &maps[(size_t)mi * kMaps]);
-    o.maps = reinterpret_cast<const CUtensorMap*>((size_t)mi * kMaps);  // index, rebased after the upload
-    ++mi;
-    ops.push_back(o);
-  };
+  int rc = build_prog_maps(m, p->tm);
   for (int l = 0; l < L; ++l) {
     Layer& Ly = m->layers[l];
     ops.push_back(norm_op(m->h, m->xn, Ly.attn_norm, c.d_model, c.rms_eps, 0));
-    ProgOp qkv = gemm_op(Ly.qkv, nullptr, m->qkv_out, nullptr, 1, 0, bits);
+    ProgOp qkv = gemm_op(Ly.qkv, nullptr, m->xn, m->qkv_out, nullptr, 1, 0, bits, kMapQkv, l);
     qkv.kc = m->kcache(l);
     qkv.vc = m->vcache(l);
-    add_gemm(qkv, Ly.qkv, nullptr, m->xn);
+    ops.push_back(qkv);
     ProgOp at{};
     at.kind = kOpAttn;
     at.kc = m->kcache(l);
@@ -877,13 +995,13 @@ int fwd_prog_build(Model* m, FwdProg** out) {
     ops.push_back(at);
     at.kind = kOpCombine;
     ops.push_back(at);
-    add_gemm(gemm_op(Ly.o, nullptr, m->h, m->h, 0, 0, bits), Ly.o, nullptr, m->attn);
+    ops.push_back(gemm_op(Ly.o, nullptr, m->attn, m->h, m->h, 0, 0, bits, kMapO, l));
     ops.push_back(norm_op(m->h, m->xn, Ly.mlp_norm, c.d_model, c.rms_eps, 0));
-    add_gemm(gemm_op(Ly.gate, &Ly.up, m->mlp, nullptr, 0, 0, bits), Ly.gate, &Ly.up, m->xn);
-    add_gemm(gemm_op(Ly.down, nullptr, m->h, m->h, 0, 0, bits), Ly.down, nullptr, m->mlp);
+    ops.push_back(gemm_op(Ly.gate, &Ly.up, m->xn, m->mlp, nullptr, 0, 0, bits, kMapGate, l));
+    ops.push_back(gemm_op(Ly.down, nullptr, m->mlp, m->h, m->h, 0, 0, bits, kMapDown, l));
   }
   ops.push_back(norm_op(m->h, m->xn, m->final_norm, c.d_model, c.rms_eps, 1));
-  add_gemm(gemm_op(m->lm_head, nullptr, m->logits, nullptr, 0, 1, bits), m->lm_head, nullptr, m->xn);
+  ops.push_back(gemm_op(m->lm_head, nullptr, m->xn, m->logits, nullptr, 0, 1, bits, kMapHead, 0));
   if (rc) {
     fwd_prog_destroy(p);
     return rc;
@@ -896,16 +1014,11 @@ int fwd_prog_build(Model* m, FwdProg** out) {
     if (e != cudaSuccess && rc == VELLA_OK) rc = cuda_fail(e, what);
   };
   cuda(cudaSetDevice(m->device), "cudaSetDevice");
-  cuda(cudaMalloc(&p->maps, maps.size() * sizeof(CUtensorMap)), "cudaMalloc(tensor maps)");
   cuda(cudaMalloc(&p->ops, ops.size() * sizeof(ProgOp)), "cudaMalloc(program)");
   cuda(cudaMalloc(&p->apart, apart_bytes), "cudaMalloc(attention partials)");
   cuda(cudaMalloc(&p->partial, (size_t)P * kTokMax * kSlots * sizeof(float)), "cudaMalloc(partials)");
   cuda(cudaMalloc(&p->scratch, p->scratch_bytes), "cudaMalloc(barrier)");
   if (rc == VELLA_OK) {
-    for (ProgOp& o : ops)
-      if (o.kind == kOpGemm) o.maps = p->maps + reinterpret_cast<size_t>(o.maps);
-    cuda(cudaMemcpyAsync(p->maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, m->stream),
-         "cudaMemcpy(tensor maps)");
     cuda(cudaMemcpyAsync(p->ops, ops.data(), ops.size() * sizeof(ProgOp), cudaMemcpyHostToDevice, m->stream),
          "cudaMemcpy(program)");
     cuda(cudaMemsetAsync(p->scratch, 0, p->scratch_bytes, m->stream), "cudaMemset(barrier)");
@@ -933,13 +1046,13 @@ int launch_fwd(const FwdArgs& a, cudaStream_t s) {
   if (!configured[dev & 63]) {
     VELLA_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::TOTAL));
     int per_sm = 0;
-    VELLA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, LY::TOTAL));
+    VELLA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kFwdThreads, LY::TOTAL));
     if (per_sm < 1) return fail(VELLA_E_CUDA, "persistent forward: no CTA fits an SM");
     configured[dev & 63] = 1;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.P);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(kFwdThreads);
   cfg.dynamicSmemBytes = LY::TOTAL;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -964,6 +1077,7 @@ int fwd_prog_run(Model* m, FwdProg* p, PosRef pr, int rows, int streams, int str
   if (M < 1 || M > kTokMax || rows * GQ > kAttnRows)
     return fail(VELLA_E_INVALID, "persistent forward: %d rows x %d streams", rows, streams);
   FwdArgs a{};
+  std::memcpy(a.tm, p->tm, sizeof(a.tm));
   a.ops = p->ops;
   a.nops = logits_rows > 0 ? p->nops : p->nops - 2;
   a.M = M;

@@ -127,6 +127,11 @@ int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& plan, const void* x
 // elements read as zeros (tma.cu).
 int make_tensor_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz);
+// 3D: `planes` such arrays plane_bytes apart (the same tensor of every layer), boxes one plane
+// deep.
+int make_tensor_map_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+                       uint64_t planes, uint64_t row_bytes, uint64_t plane_bytes, uint32_t box_inner, uint32_t box_rows,
+                       CUtensorMapSwizzle swz);
 
 // The RoPE table [max_seq][head_dim / 2] of (cos, sin) pairs: angle = pos * theta^(-2i/hd) in
 // double, rounded once to fp32 (model.cu).

@@ -70,7 +70,7 @@ struct Model {
   int* score_P = nullptr;    // prefix length of vella_model_score
   cudaStream_t stream = nullptr;  // stream of the model-level calls (init, score)
   FwdProg* prog = nullptr;        // persistent decode forward (null: the model's shapes do not suit it)
-  bool persistent = true;         // decode-sized forwards run the persistent kernel when prog exists
+  bool persistent = false;        // decode-sized forwards run the persistent kernel (needs prog)
 
   void* kcache(int l) const;
   void* vcache(int l) const;

@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, LIGHT ? 2 : 1) qgemm_stream_kernel(c
           abort_flag[0] = 1;
           atomicOr(&g_stream_fault, 8);
         }
-        if (!abort_flag[0]) prep_stage<T, BITS, NT>(smem + s * LY::STAGE, lane);
+        if (!abort_flag[0]) prep_stage<T, BITS, NT>(smem + s * LY::STAGE + XOFF, lane);
         mbar_arrive(&prepared[s]);  // also after a fault, so that no consumer waits for it
         if (++s == NS) {
           s = 0;
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, LIGHT ? 2 : 1) qgemm_stream_kernel(c
         atomicOr(&g_stream_fault, 4);
       }
     }
-    if (!abort_flag[0]) consume_stage<T, BITS, NT>(smem + s * LY::STAGE, acc, woff, lane, slot0, slot1);
+    if (!abort_flag[0]) consume_stage<T, BITS, NT>(smem + s * LY::STAGE, smem + s * LY::STAGE + XOFF, acc, woff, lane, slot0, slot1);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     if (++s == NS) {

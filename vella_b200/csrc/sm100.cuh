@@ -35,6 +35,16 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking test of a phase (test_wait never suspends the thread; try_wait may).
+__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(saddr(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait: false when the clock limit ran out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
   if (mbar_try(b, parity)) return true;
@@ -51,6 +61,22 @@ __device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* map, int c0,
           saddr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(saddr(bar))
       : "memory");
+}
+// 3D tensor-map load (no multicast) of box (c0, c1, c2), completing on bar.
+__device__ __forceinline__ void tma3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          saddr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(saddr(bar))
+      : "memory");
+}
+// L2 prefetch of one box of a 3D tensor map (no shared memory, no barrier; c0 aligned as for
+// a load).
+__device__ __forceinline__ void tma3d_prefetch_l2(const CUtensorMap* map, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
 }
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

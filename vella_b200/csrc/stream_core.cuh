@@ -58,6 +58,10 @@ struct Tile {
   static constexpr int STAGE = (TX + PB_BYTES + PX_BYTES + 1023) / 1024 * 1024;
   static constexpr int XOFF = W_BYTES + SB_BYTES;             // raw x slice within a stage
   static constexpr int POFF = XOFF + X_BYTES;                 // prepared B fragments, then x sums
+  // The x part of a stage (raw x slice, B fragments, x sums) may also live apart from the
+  // weight part: XS bytes, the B fragments P_REL bytes into it.
+  static constexpr int XS = X_BYTES + PB_BYTES + PX_BYTES;
+  static constexpr int P_REL = X_BYTES;
   static constexpr int RED = 64 * TOK * 4;                    // up-row sums handed to the gate warps
 };
 
@@ -143,33 +147,64 @@ __device__ __forceinline__ int ld_flag(const int* p) {
   return v;
 }
 
-// x preparation of one stage (the whole prep warp): the MMA's B fragments in the order the
-// code unpacking produces the A fragments, and sum(x) per group and token.
+// x preparation of one (group, token tile) of a stage by the prep warp: the MMA's B fragments
+// of the lane's 16 x values (v0, v1: row nt * 8 + r, columns g * 64 + cq * 16 ..) in the order
+// the code unpacking produces the A fragments, and sum(x) per group and token.
 template <typename T, int BITS, int NT>
-__device__ __forceinline__ void prep_stage(unsigned char* st, int lane) {
+__device__ __forceinline__ void prep_one(unsigned char* xs, int g, int nt, int lane, uint4 v0, uint4 v1) {
   using A = Act<T>;
   using TL = Tile<BITS, NT>;
   constexpr uint32_t kOne2 = A::kMagic == 128.0f ? 0x3F803F80u : 0x3C003C00u;
   const uint32_t ones[4] = {kOne2, kOne2, kOne2, kOne2};
   const int r = lane >> 2, cq = lane & 3;
-  float* px = reinterpret_cast<float*>(st + TL::POFF + TL::PB_BYTES);
+  float* px = reinterpret_cast<float*>(xs + TL::P_REL + TL::PB_BYTES);
+  const uint32_t nat[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+  uint32_t B[8];
+  permute_xs<BITS>(B, nat);
+  uint4* pb = reinterpret_cast<uint4*>(xs + TL::P_REL + (g * NT + nt) * 1024);
+  pb[lane] = make_uint4(B[0], B[1], B[2], B[3]);
+  pb[32 + lane] = make_uint4(B[4], B[5], B[6], B[7]);
+  float X[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) mma16816<T>(X, ones, B[2 * j], B[2 * j + 1]);
+  if (r == 0) *reinterpret_cast<float2*>(px + g * TL::TOK + nt * 8 + 2 * cq) = make_float2(X[0], X[1]);
+}
+
+// x preparation of one stage from the raw x slice in shared memory.  xs: the stage's x part
+// (raw x slice, then B fragments and x sums).
+template <typename T, int BITS, int NT>
+__device__ __forceinline__ void prep_stage(unsigned char* xs, int lane) {
+  using TL = Tile<BITS, NT>;
+  const int r = lane >> 2, cq = lane & 3;
 #pragma unroll
   for (int g = 0; g < TL::UG; ++g)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const unsigned char* xp = st + TL::XOFF + (g >> 2) * TL::XCHUNK + (nt * 8 + r) * 512 + (g & 3) * 128 + cq * 32;
-      const uint4 v0 = reinterpret_cast<const uint4*>(xp)[0], v1 = reinterpret_cast<const uint4*>(xp)[1];
-      const uint32_t nat[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-      uint32_t B[8];
-      permute_xs<BITS>(B, nat);
-      uint4* pb = reinterpret_cast<uint4*>(st + TL::POFF + (g * NT + nt) * 1024);
-      pb[lane] = make_uint4(B[0], B[1], B[2], B[3]);
-      pb[32 + lane] = make_uint4(B[4], B[5], B[6], B[7]);
-      float X[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) mma16816<T>(X, ones, B[2 * j], B[2 * j + 1]);
-      if (r == 0) *reinterpret_cast<float2*>(px + g * TL::TOK + nt * 8 + 2 * cq) = make_float2(X[0], X[1]);
+      const unsigned char* xp = xs + (g >> 2) * TL::XCHUNK + (nt * 8 + r) * 512 + (g & 3) * 128 + cq * 32;
+      prep_one<T, BITS, NT>(xs, g, nt, lane, reinterpret_cast<const uint4*>(xp)[0], reinterpret_cast<const uint4*>(xp)[1]);
     }
+}
+
+// The same from x in global memory: rows [0, rows) of a row-major [.. x K] array, columns k0 ..
+// k0 + UG * 64 (rows >= rows read as zeros).  L2 loads, one token tile's issued together
+// before its work.
+template <typename T, int BITS, int NT>
+__device__ __forceinline__ void prep_global(unsigned char* xs, const T* x, int K, int rows, int k0, int lane) {
+  using TL = Tile<BITS, NT>;
+  const int r = lane >> 2, cq = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    uint4 v[TL::UG][2];
+    const bool live = nt * 8 + r < rows;
+    const uint4* p = reinterpret_cast<const uint4*>(x + (size_t)(live ? nt * 8 + r : 0) * K + k0 + cq * 16);
+#pragma unroll
+    for (int g = 0; g < TL::UG; ++g) {
+      v[g][0] = live ? __ldcg(p + g * 8) : make_uint4(0, 0, 0, 0);
+      v[g][1] = live ? __ldcg(p + g * 8 + 1) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int g = 0; g < TL::UG; ++g) prep_one<T, BITS, NT>(xs, g, nt, lane, v[g][0], v[g][1]);
+  }
 }
 
 // Byte offsets of a consumer thread's weight fragments in a stage (row slot0; slot1 is 1024
@@ -193,10 +228,11 @@ template <int BITS> struct WOff {
 };
 
 // One stage's MMA work of a consumer warp: its 16 weight rows (slot0, slot1 = slot0 + 8 per
-// thread) across the unit's UG groups, accumulated into acc.
+// thread) across the unit's UG groups, accumulated into acc.  st: the stage's weight part
+// (weights, scales, biases); xs: its x part.
 template <typename T, int BITS, int NT>
-__device__ __forceinline__ void consume_stage(const unsigned char* st, float (&acc)[NT][4], const WOff<BITS>& woff,
-                                              int lane, int slot0, int slot1) {
+__device__ __forceinline__ void consume_stage(const unsigned char* st, const unsigned char* xs, float (&acc)[NT][4],
+                                              const WOff<BITS>& woff, int lane, int slot0, int slot1) {
   using A = Act<T>;
   using TL = Tile<BITS, NT>;
   constexpr int UG = TL::UG, TOK = TL::TOK, WPAT = WOff<BITS>::WPAT;
@@ -213,8 +249,8 @@ __device__ __forceinline__ void consume_stage(const unsigned char* st, float (&a
     const uint4 bv1 = *reinterpret_cast<const uint4*>(st + TL::W_BYTES + kSlots * 16 + slot1 * 16);
     const uint32_t sw0[4] = {sv0.x, sv0.y, sv0.z, sv0.w}, sw1[4] = {sv1.x, sv1.y, sv1.z, sv1.w};
     const uint32_t bw0[4] = {bv0.x, bv0.y, bv0.z, bv0.w}, bw1[4] = {bv1.x, bv1.y, bv1.z, bv1.w};
-    const uint4* pb = reinterpret_cast<const uint4*>(st + TL::POFF);
-    const float* px = reinterpret_cast<const float*>(st + TL::POFF + TL::PB_BYTES);
+    const uint4* pb = reinterpret_cast<const uint4*>(xs + TL::P_REL);
+    const float* px = reinterpret_cast<const float*>(xs + TL::P_REL + TL::PB_BYTES);
 #pragma unroll
     for (int g = 0; g < UG; ++g) {
       uint32_t B[NT][8];
@@ -289,7 +325,7 @@ __device__ __forceinline__ void consume_stage(const unsigned char* st, float (&a
     }
   } else {
     // dense weights: B fragments straight from the x slice (natural order)
-    const unsigned char* sx = st + TL::XOFF;
+    const unsigned char* sx = xs;
 #pragma unroll
     for (int g = 0; g < UG; ++g) {
       uint32_t B[NT][8];

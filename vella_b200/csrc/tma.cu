@@ -45,4 +45,19 @@ int make_tensor_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, ui
   return VELLA_OK;
 }
 
+int make_tensor_map_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+                       uint64_t planes, uint64_t row_bytes, uint64_t plane_bytes, uint32_t box_inner, uint32_t box_rows,
+                       CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(VELLA_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[3] = {inner, rows, planes};
+  const cuuint64_t strides[2] = {row_bytes, plane_bytes};
+  const cuuint32_t box[3] = {box_inner, box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(VELLA_E_INVALID, "cuTensorMapEncodeTiled (3D) failed (%d)", (int)r);
+  return VELLA_OK;
+}
+
 }  // namespace vella

@@ -130,8 +130,8 @@ class Model:
         return p.value, n.value
 
     def set_persistent(self, on: bool):
-        """Decode-sized forwards as one persistent launch (the default where the shapes allow)
-        or as per-op kernels (the same arithmetic; int4 GEMMs may differ in the last bits)."""
+        """Decode-sized forwards as one persistent launch (where the shapes allow) or as per-op
+        kernels (the default).  Same arithmetic; int4 GEMMs may differ in the last bits."""
         _lib.check(_lib.lib().vella_model_set_persistent(self.handle, int(bool(on))))
 
     def weight_bytes(self) -> int:
