@@ -1,10 +1,11 @@
 """The persistent decode forward (one cooperative launch per forward of at most 16 rows) against
 the per-op kernels and the oracle, on small models with head_dim 128 (the shapes it serves).
 
-Bars: dense weights -> logits bit-identical to the per-op path (same arithmetic, same unit
-partition); int4 weights -> within 2e-2 of the per-op path, and of the oracle's fp32 logits
-plus half a bf16 ulp, widened to twice the oracle's own rounding-order spread (its large
-GEMMs' split-K boundaries differ from the per-op path's two CTAs per SM); draft-and-verify
+Bars: logits within 2e-2 of the per-op path (the GEMMs' arithmetic is shared; the large int4
+GEMMs' split-K boundaries differ from the per-op path's two CTAs per SM, and the attention
+takes its keys in chunks of 32 instead of 64, so the online softmax rounds differently); dense
+weights -> within 2e-2 of the oracle; int4 weights -> within 2e-2 of the oracle's fp32 logits
+plus half a bf16 ulp, widened to twice the oracle's own rounding-order spread; draft-and-verify
 with the persistent forward emits exactly its greedy tokens, single stream and three streams;
 a 5:1 query-head grouping; switching it on is refused where the shapes do not suit it.
 """
@@ -33,13 +34,13 @@ def _score(m, pre, toks, persistent):
     return A.bf16_from_bits(m.score(pre, toks))
 
 
-def test_dense_logits_bit_identical_to_the_per_op_path():
+def test_dense_logits_match_per_op_path_and_oracle():
     m, oc = _model(0, seed=3)
     pre = prefix_of(20, oc.d_model, 4)
     toks = [int(t) for t in np.random.default_rng(5).integers(0, oc.vocab, 30)]
     on, off = _score(m, pre, toks, True), _score(m, pre, toks, False)
     assert np.isfinite(on).all()
-    assert np.array_equal(on, off)
+    assert np.abs(on - off).max() <= LOGIT_TOL
     ref = D.score(oc, oracle_weights(m, oc), A.bf16_from_bits(pre), toks, D.rope_table(64, 128, oc.rope_theta))
     assert np.abs(on - ref).max() <= LOGIT_TOL
     m.close()

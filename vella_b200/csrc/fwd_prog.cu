@@ -67,7 +67,7 @@ enum : int {
   kMapQkv = 0, kMapO = 3, kMapGate = 6, kMapUp = 9, kMapDown = 12, kMapHead = 15,
   kProgMaps = 18
 };
-constexpr int kSplit = kAttnCluster;  // key splits of the decode attention
+constexpr int kSplit = 16;  // key splits of the decode attention (chunk c at split c % kSplit)
 constexpr int kHD = 128;
 constexpr int kPrepWarps = 2;  // x preparation warps (alternate units), after the producer warp
 constexpr int kFwdThreads = (kRowWarps + 1 + kPrepWarps) * 32;
@@ -116,28 +116,34 @@ struct FwdArgs {
 // ---------------------------------------------------------------------------------------
 // shared memory
 // ---------------------------------------------------------------------------------------
-constexpr int kAttnRS = kHD + 8;                       // padded row stride of the attention tiles
-constexpr int kAttnTile = kAttnChunk * kAttnRS * 2;    // one [64 x 128] tile (bytes)
+constexpr int kAttnRS = kHD + 8;                    // padded row stride of the attention tiles
+constexpr int kFwdChunk = 32;                       // keys per attention chunk
+constexpr int kQTile = kAttnRows * kAttnRS * 2;     // the [64 head rows x 128] query tile (bytes)
+constexpr int kKVTile = kFwdChunk * kAttnRS * 2;    // one [32 keys x 128] K or V tile (bytes)
 
 // Each ring stage is split in two: the weight part (weights, scales, biases; TMA) and the x part
-// (the prepared B fragments and x sums, or a dense unit's raw x slice; written by the prep
-// warps), in two separate rings with the same stage index.  The attention tiles overlay the x
-// ring when it is large enough: during ATTN / COMBINE no x part is written (the next GEMM op's
-// preparation waits for the barrier after COMBINE), while the weight ring keeps filling.
-// Stage counts: as many as fit (4 for int4 at up to 8 rows: 144 KB of weights in flight per SM).
+// (quantized: the prepared B fragments and x sums; dense: the raw x slice the consumers read
+// their fragments from; written by the prep warps), in two separate rings with the same stage
+// index.  The attention tiles overlay the x ring when it is large enough: during ATTN / COMBINE
+// no x part is written (the next GEMM op's preparation waits for the barrier after COMBINE),
+// while the weight ring keeps filling.  Stage counts: as many as fit (int4: 5 at up to 8 rows,
+// 180 KB of weights in flight per SM -- the ring must cover the weights' landing latency plus
+// the time the consumers hold a stage).
 template <int BITS, int NT>
 struct FwdLayout : Tile<BITS, NT> {
   using TL = Tile<BITS, NT>;
-  static constexpr int WST = (TL::TX_W + 1023) / 1024 * 1024;  // weight part of a stage
-  static constexpr int XST = (TL::XS + 1023) / 1024 * 1024;    // x part of a stage
+  static constexpr int WST = (TL::TX_W + 1023) / 1024 * 1024;                // weight part of a stage
+  static constexpr int XS = BITS ? TL::PB_BYTES + TL::PX_BYTES : TL::X_BYTES;  // x part of a stage
+  static constexpr int XST = (XS + 127) / 128 * 128;
+  static constexpr int PREL = BITS ? 0 : TL::P_REL;  // B fragments within the x part
   static constexpr int kLimit = 227 * 1024;
-  static constexpr int bar_bytes(int ns) { return 4 * ns * 8 + 64; }
-  static constexpr int attn_bytes(int kvb) { return (1 + 2 * kvb) * kAttnTile + 2 * kAttnRows * 4; }
+  static constexpr int bar_bytes(int ns) { return 4 * ns * 8 + 64; }  // fullw, wempty, prepared, xempty
+  static constexpr int attn_bytes(int kvb) { return kQTile + 2 * kvb * kKVTile + 2 * kAttnRows * 4; }
   static constexpr int total(int ns, int kvb) {
     return 1024 + ns * (WST + XST) + TL::RED + (ns * XST >= attn_bytes(kvb) ? 0 : attn_bytes(kvb)) + 32 * 4 +
            bar_bytes(ns);
   }
-  static constexpr int NS = total(4, 1) <= kLimit ? 4 : total(3, 1) <= kLimit ? 3 : 2;
+  static constexpr int NS = total(5, 1) <= kLimit ? 5 : total(4, 1) <= kLimit ? 4 : total(3, 1) <= kLimit ? 3 : 2;
   static constexpr int KVB = total(NS, 2) <= kLimit ? 2 : 1;  // K/V double buffering when it fits
   static constexpr int ATTN = attn_bytes(KVB);
   static constexpr bool OVERLAY = NS * XST >= ATTN;
@@ -150,6 +156,7 @@ struct FwdLayout : Tile<BITS, NT> {
   static constexpr int TOTAL = 1024 + BAR_OFF + bar_bytes(NS);
   static_assert(TOTAL <= kLimit, "shared memory");
   static_assert(total(2, 1) <= kLimit, "two stages must fit");
+  static_assert(XST % 16 == 0 && RED_OFF % 16 == 0 && BAR_OFF % 8 == 0, "alignment");
 };
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -374,7 +381,7 @@ __device__ void norm_row(const ProgOp& o, const FwdArgs& a, int row, int ct, flo
 
 // ---------------------------------------------------------------------------------------
 // ATTN / COMBINE: the decode attention (one query block per stream, keys split 8 ways) with
-// the 256 consumer threads (t = 0..255).  Warps w and w + 4 hold the same 16 head rows: both
+// the 256 consumer threads (t = 0..255).  Warps 2r and 2r + 1 hold the same 16 head rows: both
 // compute their scores and softmax (the same operations, so the same values), and each
 // accumulates one half of the head dimension -- every output element gets the per-op
 // kernel's arithmetic with half its accumulator registers.
@@ -410,6 +417,25 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   }
 }
 
+// L2 prefetch of the K and V rows one key split of one (stream, kv head) reads: issued at the
+// start of the layer, so that the attention, which follows the q|k|v GEMM, reads its keys from
+// L2 instead of queueing behind that GEMM's weight traffic in HBM.
+template <typename T>
+__device__ void attn_prefetch(const ProgOp& o, const FwdArgs& a, int bz, int kvh, int split) {
+  constexpr int C = kFwdChunk, HD = kHD;
+  const int pos0 = a.pr.group ? a.pr.base[bz * a.pr.stride] + a.pr.off : *a.pr.base + a.pr.off;
+  const int tmax = pos0 + a.rows, kend = min(tmax, a.max_seq);
+  const long long kvo = a.kv0 + (long long)bz * a.kv_ss + (long long)kvh * a.max_seq * HD;
+  const T* kb = static_cast<const T*>(o.kc) + kvo;
+  const T* vb = static_cast<const T*>(o.vc) + kvo;
+  for (int c = split; c * C < kend; c += kSplit) {
+    const int n = min(C, kend - c * C);
+    const uint32_t bytes = (uint32_t)(n * HD * sizeof(T));
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(kb + (size_t)c * C * HD), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(vb + (size_t)c * C * HD), "r"(bytes) : "memory");
+  }
+}
+
 __device__ __forceinline__ size_t apart_item(const FwdArgs& a, int bz, int kvh, int split) {
   return (((size_t)bz * a.KV + kvh) * kSplit + split) * (size_t)(2 * kAttnRows + kAttnRows * kHD);
 }
@@ -418,13 +444,14 @@ __device__ __forceinline__ size_t apart_item(const FwdArgs& a, int bz, int kvh, 
 // the chunks c = split, split + 8, ... in order, written to a.apart.
 template <typename T, int KVB>
 __device__ void attn_split(const ProgOp& o, const FwdArgs& a, int bz, int kvh, int split, int t, unsigned char* sm) {
-  constexpr int C = kAttnChunk, RS = kAttnRS, HD = kHD;
+  constexpr int C = kFwdChunk, RS = kAttnRS, HD = kHD;
   constexpr int NK = HD / 16, ND = HD / 8, NH = ND / 2;  // NH: 8-column output tiles per half
   T* Qs = reinterpret_cast<T*>(sm);
-  T* Ks = reinterpret_cast<T*>(sm + kAttnTile);
-  T* Vs = reinterpret_cast<T*>(sm + (1 + KVB) * kAttnTile);
+  T* Ks = reinterpret_cast<T*>(sm + kQTile);
+  T* Vs = reinterpret_cast<T*>(sm + kQTile + KVB * kKVTile);
   const int warp = t >> 5, lane = t & 31;
-  const int rw = warp & 3, dh = warp >> 2;  // row warp (16 head rows), head-dimension half
+  const int rw = warp >> 1, dh = warp & 1;  // row warp (16 head rows), head-dimension half: the two
+                                            // warps of a row warp sit on different SMSPs
   const int r = lane >> 2, cq = lane & 3;
   const int GQ = a.H / a.KV;
   const int pos0 = a.pr.group ? a.pr.base[bz * a.pr.stride] + a.pr.off : *a.pr.base + a.pr.off;
@@ -646,8 +673,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
   unsigned char* asm_ = smem + LY::ATTN_OFF;
   float* nred = reinterpret_cast<float*>(smem + LY::NRED_OFF);
   uint64_t* fullw = reinterpret_cast<uint64_t*>(smem + LY::BAR_OFF);
-  uint64_t* empty = fullw + NS;
-  uint64_t* prepared = empty + NS;
+  uint64_t* wempty = fullw + NS;     // a stage's weight part consumed (copied to registers)
+  uint64_t* prepared = wempty + NS;
+  uint64_t* xempty = prepared + NS;  // a stage's x part consumed
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x, P = a.P, nops = a.nops;
@@ -660,7 +688,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     s_passed_ = 0;
     for (int s = 0; s < NS; ++s) {
       mbar_init(&fullw[s], 1);
-      mbar_init(&empty[s], kRowWarps);
+      mbar_init(&wempty[s], kRowWarps);
+      mbar_init(&xempty[s], kRowWarps);
       mbar_init(&prepared[s], 32);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -676,7 +705,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     long long wi = 0;  // units issued; unit j uses stage j % NS
     for (bool more = cursor_next(g, a, c, nops); more && !*s_abort; more = cursor_next(g, a, c, nops), ++wi) {
       const int s = (int)(wi % NS);
-      if (wi >= NS && !mbar_wait(&empty[s], (uint32_t)((wi / NS - 1) & 1))) {
+      if (wi >= NS && !mbar_wait(&wempty[s], (uint32_t)((wi / NS - 1) & 1))) {
         set_abort(a, 1, s_abort);
         break;
       }
@@ -733,7 +762,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       const int s = (int)(j % NS);
       int go = !*s_abort;
       if (lane == 0 && go) {
-        if (j >= NS && !mbar_wait(&empty[s], (uint32_t)((j / NS - 1) & 1))) {
+        if (j >= NS && !mbar_wait(&xempty[s], (uint32_t)((j / NS - 1) & 1))) {
           set_abort(a, 8, s_abort);
           go = 0;
         }
@@ -752,7 +781,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         unsigned char* xs = xring + s * LY::XST;
         const T* x = static_cast<const T*>(g.x);
         const int rows = g.head ? LR : a.M, k0 = g.w.kc * UG * 64;
-        if constexpr (kQuant) prep_global<T, BITS, NT>(xs, x, g.K, rows, k0, lane);
+        if constexpr (kQuant) prep_global<T, BITS, NT, LY::PREL>(xs, x, g.K, rows, k0, lane);
         else stage_x_dense<T, NT>(xs, x, g.K, rows, k0, lane);
       }
       mbar_arrive(&prepared[s]);  // also after a fault, so that no consumer waits for it
@@ -766,6 +795,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
   const int slot0 = 16 * warp + r, slot1 = slot0 + 8;
   long long j = 0;  // GEMM units consumed (ring position)
   __shared__ int s_ok;
+  __shared__ Epi s_ep;
+  __shared__ RopeEpi s_re;
   for (int i = 0; i < nops; ++i) {
     // ---- wait for op i's inputs (every CTA done with op i - 1); one CTA-wide verdict, so every
     // branch below that reaches a named barrier is taken by all consumer threads or none ----
@@ -795,17 +826,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
 #pragma unroll
           for (int e = 0; e < 4; ++e) acc[nt][e] = 0.0f;
         const int nkc = o.nkc;
-        RopeEpi re;
-        Epi ep;
-        ep.bias = nullptr; ep.res = o.res; ep.out = o.out; ep.partial = a.partial; ep.flags = a.flags;
-        ep.N = o.N; ep.mc = o.head ? LR : a.M; ep.P = op_ctas(o, P); ep.U = (long long)o.rowblocks * nkc; ep.nkc = nkc;
-        ep.gate = o.gate; ep.has_bias = 0; ep.has_res = o.has_res; ep.gelu = 0; ep.rope = o.rope;
-        ep.re = &re; ep.fault = &g_fwd_fault; ep.abort = a.bar + 1;
-        if (o.rope) {
-          re.cs = a.rope_cs; re.q = const_cast<void*>(a.q);
-          re.kc = static_cast<T*>(o.kc) + a.kv0; re.vc = static_cast<T*>(o.vc) + a.kv0;
-          re.pr = a.pr; re.H = a.H; re.KV = a.KV; re.max_seq = a.max_seq; re.kv_ss = a.kv_ss; re.err = a.err;
+        // the op's epilogue descriptors live in shared memory (read at row-block ends only), so
+        // the unit loop keeps its registers for the weights
+        if (ct == 0) {
+          Epi& ep = s_ep;
+          RopeEpi& re = s_re;
+          ep.bias = nullptr; ep.res = o.res; ep.out = o.out; ep.partial = a.partial; ep.flags = a.flags;
+          ep.N = o.N; ep.mc = o.head ? LR : a.M; ep.P = op_ctas(o, P); ep.U = (long long)o.rowblocks * nkc; ep.nkc = nkc;
+          ep.gate = o.gate; ep.has_bias = 0; ep.has_res = o.has_res; ep.gelu = 0; ep.rope = o.rope;
+          ep.re = &s_re; ep.fault = &g_fwd_fault; ep.abort = a.bar + 1;
+          if (o.rope) {
+            re.cs = a.rope_cs; re.q = const_cast<void*>(a.q);
+            re.kc = static_cast<T*>(o.kc) + a.kv0; re.vc = static_cast<T*>(o.vc) + a.kv0;
+            re.pr = a.pr; re.H = a.H; re.KV = a.KV; re.max_seq = a.max_seq; re.kv_ss = a.kv_ss; re.err = a.err;
+          }
         }
+        named_sync(1, 256);
         const int rf = (int)(u0 / nkc), rl = (int)((u1 - 1) / nkc);
         const bool head_shared = u0 % nkc != 0, tail_shared = u1 % nkc != 0;
         UnitWalk cur(u0, u1, nkc);
@@ -818,20 +854,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             have = mbar_wait(&fullw[s], ph) && mbar_wait(&prepared[s], ph);
             if (!have) set_abort(a, 4, s_abort);
           }
-          if (have) consume_stage<T, BITS, NT>(wring + s * LY::WST, xring + s * LY::XST, acc, woff, lane, slot0, slot1);
+          if (have)
+            consume_stage<T, BITS, NT, LY::PREL>(wring + s * LY::WST, xring + s * LY::XST, acc, woff, lane, slot0, slot1);
           __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[s]);
+          if (lane == 0) {
+            mbar_arrive(&wempty[s]);
+            mbar_arrive(&xempty[s]);
+          }
           const int rb = cur.rb;
           const bool flush = cur.seg_last() || cur.kc + 1 == nkc;
           cur.next(nkc);
           // every consumer warp flushes at the same row-block ends (the gate / RoPE pairing
           // synchronises warps w and w + 4), aborted or not
           if (flush)
-            flush_rowblock<T, NT>(ep, c, rb, rb == rl && tail_shared, rb == rf && head_shared, acc, red, warp, lane);
+            flush_rowblock<T, NT>(s_ep, c, rb, rb == rl && tail_shared, rb == rf && head_shared, acc, red, warp, lane);
         }
       }
     } else if (o.kind == kOpNorm && ok) {
       for (int row = c; row < norm_rows; row += P) norm_row<T>(o, a, row, ct, nred, wv);
+      if (ct == 0 && i + 2 < nops && !o.tail) {  // a layer's first norm: its attention's keys into L2
+        const ProgOp& at = a.ops[i + 2];
+        if (at.kind == kOpAttn)
+          for (int it = c; it < a.streams * a.KV * kSplit; it += P)
+            attn_prefetch<T>(at, a, it / (a.KV * kSplit), (it / kSplit) % a.KV, it % kSplit);
+      }
     } else if (o.kind == kOpAttn && ok) {
       const int items = a.streams * a.KV * kSplit;
       for (int it = c; it < items; it += P) {

@@ -59,7 +59,8 @@ struct Tile {
   static constexpr int XOFF = W_BYTES + SB_BYTES;             // raw x slice within a stage
   static constexpr int POFF = XOFF + X_BYTES;                 // prepared B fragments, then x sums
   // The x part of a stage (raw x slice, B fragments, x sums) may also live apart from the
-  // weight part: XS bytes, the B fragments P_REL bytes into it.
+  // weight part: XS bytes, the B fragments P_REL bytes into it (a layout without the raw slice
+  // passes its own offset, 0, to the functions below).
   static constexpr int XS = X_BYTES + PB_BYTES + PX_BYTES;
   static constexpr int P_REL = X_BYTES;
   static constexpr int RED = 64 * TOK * 4;                    // up-row sums handed to the gate warps
@@ -150,18 +151,18 @@ __device__ __forceinline__ int ld_flag(const int* p) {
 // x preparation of one (group, token tile) of a stage by the prep warp: the MMA's B fragments
 // of the lane's 16 x values (v0, v1: row nt * 8 + r, columns g * 64 + cq * 16 ..) in the order
 // the code unpacking produces the A fragments, and sum(x) per group and token.
-template <typename T, int BITS, int NT>
+template <typename T, int BITS, int NT, int PREL = Tile<BITS, NT>::P_REL>
 __device__ __forceinline__ void prep_one(unsigned char* xs, int g, int nt, int lane, uint4 v0, uint4 v1) {
   using A = Act<T>;
   using TL = Tile<BITS, NT>;
   constexpr uint32_t kOne2 = A::kMagic == 128.0f ? 0x3F803F80u : 0x3C003C00u;
   const uint32_t ones[4] = {kOne2, kOne2, kOne2, kOne2};
   const int r = lane >> 2, cq = lane & 3;
-  float* px = reinterpret_cast<float*>(xs + TL::P_REL + TL::PB_BYTES);
+  float* px = reinterpret_cast<float*>(xs + PREL + TL::PB_BYTES);
   const uint32_t nat[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
   uint32_t B[8];
   permute_xs<BITS>(B, nat);
-  uint4* pb = reinterpret_cast<uint4*>(xs + TL::P_REL + (g * NT + nt) * 1024);
+  uint4* pb = reinterpret_cast<uint4*>(xs + PREL + (g * NT + nt) * 1024);
   pb[lane] = make_uint4(B[0], B[1], B[2], B[3]);
   pb[32 + lane] = make_uint4(B[4], B[5], B[6], B[7]);
   float X[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -188,7 +189,7 @@ __device__ __forceinline__ void prep_stage(unsigned char* xs, int lane) {
 // The same from x in global memory: rows [0, rows) of a row-major [.. x K] array, columns k0 ..
 // k0 + UG * 64 (rows >= rows read as zeros).  L2 loads, one token tile's issued together
 // before its work.
-template <typename T, int BITS, int NT>
+template <typename T, int BITS, int NT, int PREL = Tile<BITS, NT>::P_REL>
 __device__ __forceinline__ void prep_global(unsigned char* xs, const T* x, int K, int rows, int k0, int lane) {
   using TL = Tile<BITS, NT>;
   const int r = lane >> 2, cq = lane & 3;
@@ -203,7 +204,7 @@ __device__ __forceinline__ void prep_global(unsigned char* xs, const T* x, int K
       v[g][1] = live ? __ldcg(p + g * 8 + 1) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int g = 0; g < TL::UG; ++g) prep_one<T, BITS, NT>(xs, g, nt, lane, v[g][0], v[g][1]);
+    for (int g = 0; g < TL::UG; ++g) prep_one<T, BITS, NT, PREL>(xs, g, nt, lane, v[g][0], v[g][1]);
   }
 }
 
@@ -227,122 +228,170 @@ template <int BITS> struct WOff {
   }
 };
 
+// The weight words of one group for a consumer thread: rows slot0 (w0) and slot1 (w1), WPG
+// 32-bit words each (int4: 2, int8: 4, dense: 8), read from a stage as the MMA wants them.
+template <int BITS> struct WGroup {
+  static constexpr int WPG = BITS == 4 ? 2 : (BITS == 8 ? 4 : 8);
+};
+template <int BITS, int NT>
+__device__ __forceinline__ void stage_wgroup(const unsigned char* st, const WOff<BITS>& woff, int g, uint32_t (&w0)[WGroup<BITS>::WPG],
+                                             uint32_t (&w1)[WGroup<BITS>::WPG]) {
+  using TL = Tile<BITS, NT>;
+  if constexpr (BITS == 4) {
+    const unsigned char* wrow = st + (g / 4) * TL::WCHUNK + woff.v[g % 4];
+    const uint2 u0v = *reinterpret_cast<const uint2*>(wrow);
+    const uint2 u1v = *reinterpret_cast<const uint2*>(wrow + 1024);
+    w0[0] = u0v.x; w0[1] = u0v.y; w1[0] = u1v.x; w1[1] = u1v.y;
+  } else if constexpr (BITS == 8) {
+    const unsigned char* wrow = st + (g / 2) * TL::WCHUNK + woff.v[g % 2];
+    const uint4 u0v = *reinterpret_cast<const uint4*>(wrow);
+    const uint4 u1v = *reinterpret_cast<const uint4*>(wrow + 1024);
+    w0[0] = u0v.x; w0[1] = u0v.y; w0[2] = u0v.z; w0[3] = u0v.w;
+    w1[0] = u1v.x; w1[1] = u1v.y; w1[2] = u1v.z; w1[3] = u1v.w;
+  } else {
+    const unsigned char* wbox = st + g * TL::WCHUNK;
+    const uint4 a0 = *reinterpret_cast<const uint4*>(wbox + woff.v[0]);
+    const uint4 a1 = *reinterpret_cast<const uint4*>(wbox + woff.v[1]);
+    const uint4 b0 = *reinterpret_cast<const uint4*>(wbox + woff.v[0] + 1024);
+    const uint4 b1 = *reinterpret_cast<const uint4*>(wbox + woff.v[1] + 1024);
+    w0[0] = a0.x; w0[1] = a0.y; w0[2] = a0.z; w0[3] = a0.w; w0[4] = a1.x; w0[5] = a1.y; w0[6] = a1.z; w0[7] = a1.w;
+    w1[0] = b0.x; w1[1] = b0.y; w1[2] = b0.z; w1[3] = b0.w; w1[4] = b1.x; w1[5] = b1.y; w1[6] = b1.z; w1[7] = b1.w;
+  }
+}
+// This warp's scales and biases of the unit's UG groups (quantized): 16 bytes per row, rows
+// slot0 / slot1: sb = {scales slot0, scales slot1, biases slot0, biases slot1} x 4 words.
+template <int BITS, int NT>
+__device__ __forceinline__ void stage_sb(const unsigned char* st, int slot0, int slot1, uint32_t (&sb)[16]) {
+  using TL = Tile<BITS, NT>;
+  const uint4 v[4] = {*reinterpret_cast<const uint4*>(st + TL::W_BYTES + slot0 * 16),
+                      *reinterpret_cast<const uint4*>(st + TL::W_BYTES + slot1 * 16),
+                      *reinterpret_cast<const uint4*>(st + TL::W_BYTES + kSlots * 16 + slot0 * 16),
+                      *reinterpret_cast<const uint4*>(st + TL::W_BYTES + kSlots * 16 + slot1 * 16)};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    sb[4 * i] = v[i].x; sb[4 * i + 1] = v[i].y; sb[4 * i + 2] = v[i].z; sb[4 * i + 3] = v[i].w;
+  }
+}
+
 // One stage's MMA work of a consumer warp: its 16 weight rows (slot0, slot1 = slot0 + 8 per
-// thread) across the unit's UG groups, accumulated into acc.  st: the stage's weight part
-// (weights, scales, biases); xs: its x part.
-template <typename T, int BITS, int NT>
-__device__ __forceinline__ void consume_stage(const unsigned char* st, const unsigned char* xs, float (&acc)[NT][4],
-                                              const WOff<BITS>& woff, int lane, int slot0, int slot1) {
+// thread) across the unit's UG groups, accumulated into acc.  The weight words of group g come
+// from wf(g, w0, w1); sb: the scales and biases (quantized); xs: the stage's x part, its B
+// fragments PREL bytes in.
+template <typename T, int BITS, int NT, int PREL, typename WF>
+__device__ __forceinline__ void consume_core(const unsigned char* xs, float (&acc)[NT][4], int lane,
+                                             const uint32_t (&sb)[16], const WF& wf) {
   using A = Act<T>;
   using TL = Tile<BITS, NT>;
-  constexpr int UG = TL::UG, TOK = TL::TOK, WPAT = WOff<BITS>::WPAT;
+  constexpr int UG = TL::UG, TOK = TL::TOK, WPG = WGroup<BITS>::WPG;
   constexpr uint32_t kMask = 0x000F000Fu;
   constexpr uint32_t kMag = A::kMagic2;
   constexpr float kOff = BITS == 4 ? A::kMagic : 17.0f * A::kMagic;
   const int r = lane >> 2, cq = lane & 3;
-  (void)r;
   if constexpr (BITS != 0) {
-    // this warp's scales and biases of the unit's UG groups: 16 bytes per row
-    const uint4 sv0 = *reinterpret_cast<const uint4*>(st + TL::W_BYTES + slot0 * 16);
-    const uint4 sv1 = *reinterpret_cast<const uint4*>(st + TL::W_BYTES + slot1 * 16);
-    const uint4 bv0 = *reinterpret_cast<const uint4*>(st + TL::W_BYTES + kSlots * 16 + slot0 * 16);
-    const uint4 bv1 = *reinterpret_cast<const uint4*>(st + TL::W_BYTES + kSlots * 16 + slot1 * 16);
-    const uint32_t sw0[4] = {sv0.x, sv0.y, sv0.z, sv0.w}, sw1[4] = {sv1.x, sv1.y, sv1.z, sv1.w};
-    const uint32_t bw0[4] = {bv0.x, bv0.y, bv0.z, bv0.w}, bw1[4] = {bv1.x, bv1.y, bv1.z, bv1.w};
-    const uint4* pb = reinterpret_cast<const uint4*>(xs + TL::P_REL);
-    const float* px = reinterpret_cast<const float*>(xs + TL::P_REL + TL::PB_BYTES);
+    const uint32_t* sw0 = sb;
+    const uint32_t* sw1 = sb + 4;
+    const uint32_t* bw0 = sb + 8;
+    const uint32_t* bw1 = sb + 12;
+    const uint4* pb = reinterpret_cast<const uint4*>(xs + PREL);
+    const float* px = reinterpret_cast<const float*>(xs + PREL + TL::PB_BYTES);
+    // Groups in pairs: the two groups' MMA chains are issued interleaved (each group's own sums
+    // keep their order, and acc takes group g before group g + 1).
+    constexpr int GP = 2;
 #pragma unroll
-    for (int g = 0; g < UG; ++g) {
-      uint32_t B[NT][8];
-      float X[NT][2];
+    for (int g0 = 0; g0 < UG; g0 += GP) {
+      uint32_t B[GP][NT][8];
+      float X[GP][NT][2];
+      uint32_t w0[GP][WPG], w1[GP][WPG];
+      float d[GP][NT][4];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const uint4 lo = pb[(g * NT + nt) * 64 + lane], hi = pb[(g * NT + nt) * 64 + 32 + lane];
-        B[nt][0] = lo.x; B[nt][1] = lo.y; B[nt][2] = lo.z; B[nt][3] = lo.w;
-        B[nt][4] = hi.x; B[nt][5] = hi.y; B[nt][6] = hi.z; B[nt][7] = hi.w;
-        const float2 xv = *reinterpret_cast<const float2*>(px + g * TOK + nt * 8 + 2 * cq);
-        X[nt][0] = xv.x;
-        X[nt][1] = xv.y;
+      for (int h = 0; h < GP; ++h) {
+        const int g = g0 + h;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const uint4 lo = pb[(g * NT + nt) * 64 + lane], hi = pb[(g * NT + nt) * 64 + 32 + lane];
+          B[h][nt][0] = lo.x; B[h][nt][1] = lo.y; B[h][nt][2] = lo.z; B[h][nt][3] = lo.w;
+          B[h][nt][4] = hi.x; B[h][nt][5] = hi.y; B[h][nt][6] = hi.z; B[h][nt][7] = hi.w;
+          const float2 xv = *reinterpret_cast<const float2*>(px + g * TOK + nt * 8 + 2 * cq);
+          X[h][nt][0] = xv.x;
+          X[h][nt][1] = xv.y;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) d[h][nt][e] = 0.0f;
+        }
+        wf(g, w0[h], w1[h]);
       }
-      const unsigned char* wrow = st + (g / WPAT) * TL::WCHUNK + woff.v[g % WPAT];  // row slot0
-      float d[NT][4];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) d[nt][e] = 0.0f;
       if constexpr (BITS == 4) {
-        const uint2 u0v = *reinterpret_cast<const uint2*>(wrow);
-        const uint2 u1v = *reinterpret_cast<const uint2*>(wrow + 1024);
-        const uint32_t w0[2] = {u0v.x, u0v.y}, w1[2] = {u1v.x, u1v.y};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int sh = (j & 1) * 8;
-          const uint32_t p0 = w0[j >> 1], p1 = w1[j >> 1];
-          const uint32_t af[4] = {and_or(p0 >> sh, kMask, kMag), and_or(p1 >> sh, kMask, kMag),
-                                  and_or(p0 >> (sh + 4), kMask, kMag), and_or(p1 >> (sh + 4), kMask, kMag)};
+        for (int j = 0; j < 4; ++j)
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma16816<T>(d[nt], af, B[nt][2 * j], B[nt][2 * j + 1]);
-        }
-      } else {
-        const uint4 u0v = *reinterpret_cast<const uint4*>(wrow);
-        const uint4 u1v = *reinterpret_cast<const uint4*>(wrow + 1024);
-        const uint32_t w0[4] = {u0v.x, u0v.y, u0v.z, u0v.w}, w1[4] = {u1v.x, u1v.y, u1v.z, u1v.w};
-        float dh[NT][4];
+          for (int h = 0; h < GP; ++h) {
+            const int sh = (j & 1) * 8;
+            const uint32_t p0 = w0[h][j >> 1], p1 = w1[h][j >> 1];
+            const uint32_t af[4] = {and_or(p0 >> sh, kMask, kMag), and_or(p1 >> sh, kMask, kMag),
+                                    and_or(p0 >> (sh + 4), kMask, kMag), and_or(p1 >> (sh + 4), kMask, kMag)};
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) dh[nt][e] = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t p0 = w0[j], p1 = w1[j];
-          const uint32_t lo[4] = {and_or(p0, kMask, kMag), and_or(p1, kMask, kMag), and_or(p0 >> 8, kMask, kMag),
-                                  and_or(p1 >> 8, kMask, kMag)};
-          const uint32_t hi[4] = {and_or(p0 >> 4, kMask, kMag), and_or(p1 >> 4, kMask, kMag),
-                                  and_or(p0 >> 12, kMask, kMag), and_or(p1 >> 12, kMask, kMag)};
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            mma16816<T>(d[nt], lo, B[nt][2 * j], B[nt][2 * j + 1]);
-            mma16816<T>(dh[nt], hi, B[nt][2 * j], B[nt][2 * j + 1]);
+            for (int nt = 0; nt < NT; ++nt) mma16816<T>(d[h][nt], af, B[h][nt][2 * j], B[h][nt][2 * j + 1]);
           }
-        }
+      } else {
+        float dh[GP][NT][4];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
+        for (int h = 0; h < GP; ++h)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) d[nt][e] = fmaf(16.0f, dh[nt][e], d[nt][e]);
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dh[h][nt][e] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int h = 0; h < GP; ++h) {
+            const uint32_t p0 = w0[h][j], p1 = w1[h][j];
+            const uint32_t lo[4] = {and_or(p0, kMask, kMag), and_or(p1, kMask, kMag), and_or(p0 >> 8, kMask, kMag),
+                                    and_or(p1 >> 8, kMask, kMag)};
+            const uint32_t hi[4] = {and_or(p0 >> 4, kMask, kMag), and_or(p1 >> 4, kMask, kMag),
+                                    and_or(p0 >> 12, kMask, kMag), and_or(p1 >> 12, kMask, kMag)};
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              mma16816<T>(d[h][nt], lo, B[h][nt][2 * j], B[h][nt][2 * j + 1]);
+              mma16816<T>(dh[h][nt], hi, B[h][nt][2 * j], B[h][nt][2 * j + 1]);
+            }
+          }
+#pragma unroll
+        for (int h = 0; h < GP; ++h)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) d[h][nt][e] = fmaf(16.0f, dh[h][nt][e], d[h][nt][e]);
       }
-      // scale/bias of group g: 16-bit half (g & 1) of word (g >> 1)
-      const float s0 = (g & 1) ? A::hi(sw0[g >> 1]) : A::lo(sw0[g >> 1]);
-      const float s1 = (g & 1) ? A::hi(sw1[g >> 1]) : A::lo(sw1[g >> 1]);
-      const float b0 = fmaf(-kOff, s0, (g & 1) ? A::hi(bw0[g >> 1]) : A::lo(bw0[g >> 1]));
-      const float b1 = fmaf(-kOff, s1, (g & 1) ? A::hi(bw1[g >> 1]) : A::lo(bw1[g >> 1]));
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        acc[nt][0] = fmaf(s0, d[nt][0], fmaf(b0, X[nt][0], acc[nt][0]));
-        acc[nt][1] = fmaf(s0, d[nt][1], fmaf(b0, X[nt][1], acc[nt][1]));
-        acc[nt][2] = fmaf(s1, d[nt][2], fmaf(b1, X[nt][0], acc[nt][2]));
-        acc[nt][3] = fmaf(s1, d[nt][3], fmaf(b1, X[nt][1], acc[nt][3]));
+      for (int h = 0; h < GP; ++h) {
+        const int g = g0 + h;
+        // scale/bias of group g: 16-bit half (g & 1) of word (g >> 1)
+        const float s0 = (g & 1) ? A::hi(sw0[g >> 1]) : A::lo(sw0[g >> 1]);
+        const float s1 = (g & 1) ? A::hi(sw1[g >> 1]) : A::lo(sw1[g >> 1]);
+        const float b0 = fmaf(-kOff, s0, (g & 1) ? A::hi(bw0[g >> 1]) : A::lo(bw0[g >> 1]));
+        const float b1 = fmaf(-kOff, s1, (g & 1) ? A::hi(bw1[g >> 1]) : A::lo(bw1[g >> 1]));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          acc[nt][0] = fmaf(s0, d[h][nt][0], fmaf(b0, X[h][nt][0], acc[nt][0]));
+          acc[nt][1] = fmaf(s0, d[h][nt][1], fmaf(b0, X[h][nt][1], acc[nt][1]));
+          acc[nt][2] = fmaf(s1, d[h][nt][2], fmaf(b1, X[h][nt][0], acc[nt][2]));
+          acc[nt][3] = fmaf(s1, d[h][nt][3], fmaf(b1, X[h][nt][1], acc[nt][3]));
+        }
       }
     }
   } else {
     // dense weights: B fragments straight from the x slice (natural order)
-    const unsigned char* sx = xs;
 #pragma unroll
     for (int g = 0; g < UG; ++g) {
       uint32_t B[NT][8];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const unsigned char* xp = sx + (g >> 2) * TL::XCHUNK + (nt * 8 + r) * 512 + (g & 3) * 128 + cq * 32;
+        const unsigned char* xp = xs + (g >> 2) * TL::XCHUNK + (nt * 8 + r) * 512 + (g & 3) * 128 + cq * 32;
         const uint4 v0 = reinterpret_cast<const uint4*>(xp)[0], v1 = reinterpret_cast<const uint4*>(xp)[1];
         B[nt][0] = v0.x; B[nt][1] = v0.y; B[nt][2] = v0.z; B[nt][3] = v0.w;
         B[nt][4] = v1.x; B[nt][5] = v1.y; B[nt][6] = v1.z; B[nt][7] = v1.w;
       }
-      const unsigned char* wbox = st + g * TL::WCHUNK;
-      const uint4 a0 = *reinterpret_cast<const uint4*>(wbox + woff.v[0]);
-      const uint4 a1 = *reinterpret_cast<const uint4*>(wbox + woff.v[1]);
-      const uint4 b0 = *reinterpret_cast<const uint4*>(wbox + woff.v[0] + 1024);
-      const uint4 b1 = *reinterpret_cast<const uint4*>(wbox + woff.v[1] + 1024);
-      const uint32_t w0[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const uint32_t w1[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      uint32_t w0[WPG], w1[WPG];
+      wf(g, w0, w1);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t af[4] = {w0[2 * j], w1[2 * j], w0[2 * j + 1], w1[2 * j + 1]};
@@ -351,6 +400,27 @@ __device__ __forceinline__ void consume_stage(const unsigned char* st, const uns
       }
     }
   }
+}
+
+// The weight fetcher of consume_core (a functor, so that it is inlined and the words stay in
+// registers): from the stage in shared memory.
+template <int BITS, int NT>
+struct StageW {
+  const unsigned char* st;
+  const WOff<BITS>& woff;
+  __device__ __forceinline__ void operator()(int g, uint32_t (&w0)[WGroup<BITS>::WPG], uint32_t (&w1)[WGroup<BITS>::WPG]) const {
+    stage_wgroup<BITS, NT>(st, woff, g, w0, w1);
+  }
+};
+
+// consume_core with the weights read from the stage as they are used.  st: the stage's weight
+// part (weights, scales, biases); xs: its x part.
+template <typename T, int BITS, int NT, int PREL = Tile<BITS, NT>::P_REL>
+__device__ __forceinline__ void consume_stage(const unsigned char* st, const unsigned char* xs, float (&acc)[NT][4],
+                                              const WOff<BITS>& woff, int lane, int slot0, int slot1) {
+  uint32_t sb[16];
+  if constexpr (BITS != 0) stage_sb<BITS, NT>(st, slot0, slot1, sb);
+  consume_core<T, BITS, NT, PREL>(xs, acc, lane, sb, StageW<BITS, NT>{st, woff});
 }
 
 // What happens to a finished row block.
