@@ -18,7 +18,7 @@
 //               operand tile; quantized: the raw code rows).
 //   warp 1      allocates tensor memory; one thread issues 4 MMAs (K = 16 each) per stage and
 //               commits them to the stage's "empty" barrier; frees tensor memory at the end.
-//   warps 2..   two (quantized) or four (dense) threads per weight row (warps w, w + 4, ..
+//   warps 2..   four threads per weight row (warps w, w + 4, ..
 //               share the row window of
 //               tensor-memory lanes 32 (w % 4) ..): each turns a slice of the stage's codes
 //               of its row into the operand tile (128-byte swizzled K-major rows; scales and
@@ -55,9 +55,10 @@ using namespace sm100;
 constexpr int kTcRows = 128;     // weight rows per CTA (MMA M)
 constexpr int kTcTok = 256;      // tokens per CTA (largest MMA N)
 constexpr int kTcK = 64;         // K elements per stage
-// Transform/epilogue warps: 8 for the quantized formats (two threads per weight row), 16 for
-// dense weights (no transform: four threads per row share the epilogue).
-template <int BITS> constexpr int tc_xw() { return BITS ? 8 : 16; }
+// Transform/epilogue warps: 16, four threads per weight row (quantized: each dequantises a
+// quarter of the row's codes per stage -- with 8 the transform's latency left the tensor pipe
+// idle half the time; dense: no transform, the four share the epilogue).
+template <int BITS> constexpr int tc_xw() { return 16; }
 template <int BITS> constexpr int tc_threads() { return 64 + 32 * tc_xw<BITS>(); }
 
 template <int BITS, bool GATE>
@@ -263,7 +264,7 @@ __global__ void __launch_bounds__(tc_threads<BITS>(), 1) tc_gemm_kernel(const __
     }
     __syncwarp();
   } else {
-    // ---- transform (quantized formats) and epilogue: two threads per weight row ------------
+    // ---- transform (quantized formats) and epilogue: four threads per weight row -----------
     pdl_wait();
     const int r = 32 * (warp & 3) + lane;  // tensor-memory lane of this warp's window
     const int hf = (warp - 2) >> 2;        // which slice of the row's codes / which column chunks
