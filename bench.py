@@ -541,10 +541,45 @@ def run_spec(args, rank, world):
         line["tree"] = run_spec_tree(rank, local, TREE_STREAMS, TREE_BRANCHING, TREE_TEMPERATURE, TREE_TOKENS)
         line["tree"]["tokens_per_s_all_gpus"] = round(
             world * line["tree"]["tokens"] / dist_max(dist, line["tree"]["decode_ms"] / 1e3, dev), 1)
+    if not args.no_whisper:
+        line["whisper"] = whisper_subline(rank, local, hbm, peak_kind)
+        for key, n in (("tokens_per_s_all_gpus", 1), ("streams_tokens_per_s_all_gpus", WHISPER_STREAMS)):
+            ms = line["whisper"]["decode_ms"] if n == 1 else line["whisper"]["streams"]["decode_ms"]
+            line["whisper"][key] = round(world * n * WHISPER_TOKENS / dist_max(dist, ms / 1e3, dev), 1)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     return line
+
+
+def whisper_subline(rank, local, hbm, peak_kind):
+    """Config 3 beside the headline: the Whisper decoder at large-v3-turbo shapes (fp16), one
+    stream (encode one 30 s window, 224 greedy tokens; one warm-up then one timed window) and
+    WHISPER_STREAMS streams in one handle.  Device times from the library's CUDA events."""
+    import numpy as np
+    from vella_b200 import whisper as VW
+    c = VW.TURBO
+    m = VW.Whisper(c, local)
+    m.init_random(1 + rank, 0.02)
+    mel = np.random.default_rng(2 + rank).standard_normal((c.n_mels, 2 * c.n_audio)).astype(np.float32)
+    m.encode(mel)
+    m.decode(WHISPER_PROMPT, WHISPER_TOKENS)
+    m.encode(mel)
+    enc_ms = m.stats()["encode_ms"]
+    r = m.decode(WHISPER_PROMPT, WHISPER_TOKENS)
+    m.close()
+    step_us = r.decode_ms / (WHISPER_TOKENS - 1) * 1e3
+    achieved = whisper_step_bytes(c) / (step_us * 1e-6) / 1e9
+    out = {"workload": "config 3: Whisper large-v3-turbo shapes (32 enc / 4 dec layers, d 1280, 20x64 heads, FFN 5120, "
+                       "V 51866), fp16 random weights ~N(0,0.02), 4-token prompt, 224 greedy tokens per window",
+           "tokens_per_s": round(WHISPER_TOKENS / ((r.prefill_ms + r.decode_ms) / 1e3), 1),
+           "decode_ms": round(r.prefill_ms + r.decode_ms, 2), "step_us": round(step_us, 1),
+           "encode_ms": round(enc_ms, 2),
+           "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(achieved / hbm, 3), "peak_kind": peak_kind,
+                        "kernel": "decoder step (algorithmic bytes / measured step time)"}}
+    out["streams"] = run_whisper_streams(rank, local, WHISPER_STREAMS)
+    return out
 
 
 def run_spec_batched(rank, local, S, k, p):
@@ -1013,6 +1048,7 @@ def main():
     ap.add_argument("--no-batched", action="store_true", help="spec workload: skip the multi-stream measurement")
     ap.add_argument("--no-tree", action="store_true", help="spec workload: skip the tree + sampling measurement")
     ap.add_argument("--no-gemm", action="store_true", help="spec workload: skip the config-2 GEMM sub-line")
+    ap.add_argument("--no-whisper", action="store_true", help="spec workload: skip the config-3 Whisper sub-line")
     ap.add_argument("--shape", default="", help="gemm workload: one case 'bits,N,K,M' instead of the sweep")
     ap.add_argument("--profile-pass", action="store_true", help="short run for an ncu launch list")
     ap.add_argument("--profile-tree", action="store_true", help="short tree-verification run for an ncu launch list")
