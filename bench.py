@@ -1037,6 +1037,24 @@ def run_profile_tree(args):
     return {"profile": "tree verification, 4+2 layers, 32 streams", "passes": r["passes"]}
 
 
+def run_profile_whisper(args):
+    """A short Whisper run for an ncu launch list: large-v3-turbo shapes, one 30 s window
+    encoded, the 4-token prompt, then 6 single decoder steps (the steps are what the list is for)."""
+    import numpy as np
+    import torch
+    from vella_b200 import whisper as VW
+    c = VW.TURBO
+    m = VW.Whisper(c, 0)
+    m.init_random(1, 0.02)
+    m.encode(np.random.default_rng(2).standard_normal((c.n_mels, 2 * c.n_audio)).astype(np.float32))
+    t = m.begin(WHISPER_PROMPT)
+    for _ in range(6):
+        t = m.step()
+    torch.cuda.synchronize()
+    m.close()
+    return {"profile": "Whisper turbo: encode + prompt + 6 decoder steps", "last_token": t}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1052,7 +1070,11 @@ def main():
     ap.add_argument("--shape", default="", help="gemm workload: one case 'bits,N,K,M' instead of the sweep")
     ap.add_argument("--profile-pass", action="store_true", help="short run for an ncu launch list")
     ap.add_argument("--profile-tree", action="store_true", help="short tree-verification run for an ncu launch list")
+    ap.add_argument("--profile-whisper", action="store_true", help="short Whisper decoder run for an ncu launch list")
     args = ap.parse_args()
+    if args.profile_whisper:
+        print(json.dumps(run_profile_whisper(args)))
+        return
     if args.profile_pass:
         print(json.dumps(run_profile_pass(args)))
         return
