@@ -20,6 +20,7 @@
 // and after a rejection with the same graph.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -155,6 +156,7 @@ constexpr int kSampThreads = 512;
 struct SampShared {
   float red[kSampThreads / 32];
   float part[kSampThreads];
+  int mm[2 * kSampThreads / 32];  // block_minmax's warp values
   float before, stat;
   int seg, idx;
 };
@@ -203,56 +205,203 @@ __device__ float2 row_softmax_stats(const T* row, int V, float invT, SampShared&
   return make_float2(m, z);
 }
 
+// Inclusive prefix sums of one value per thread over the block (warp shuffles, then the warp
+// totals: a fixed order), and the block total.
+__device__ float block_incl_scan(float v, SampShared& sh, float* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (int)(blockDim.x >> 5);
+  float x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();  // sh.red is free
+  if (lane == 31) sh.red[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    float t = lane < nw ? sh.red[lane] : 0.0f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    if (lane < nw) sh.red[lane] = t;
+  }
+  __syncthreads();
+  *total = sh.red[nw - 1];
+  return x + (w > 0 ? sh.red[w - 1] : 0.0f);
+}
+
+// Block-wide min of a (first) and max of b (second) over the threads.
+__device__ int2 block_minmax(int a, int b, SampShared& sh) {
+  int* scratch = sh.mm;
+  a = __reduce_min_sync(0xffffffffu, a);
+  b = __reduce_max_sync(0xffffffffu, b);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+    scratch[2 * (threadIdx.x >> 5)] = a;
+    scratch[2 * (threadIdx.x >> 5) + 1] = b;
+  }
+  __syncthreads();
+  int2 r = make_int2(0x7fffffff, -1);
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+    r.x = min(r.x, scratch[2 * w]);
+    r.y = max(r.y, scratch[2 * w + 1]);
+  }
+  return r;
+}
+
 // Index drawn from the unnormalised weights w(0..V) with the uniform u: thread t owns the
-// contiguous range [t C, (t+1) C); the partial sums are scanned in thread order, so the
-// result depends only on the weights and u.  -1 when every weight is zero.
+// contiguous range [t C, (t+1) C); the thread sums are prefix-summed in a fixed order (warp
+// shuffles, then the warp totals), the first thread whose running sum passes u * total scans
+// its range in vocabulary order.  The result depends only on the weights and u.  -1 when
+// every weight is zero.
 template <typename W>
 __device__ int sample_icdf(W w, int V, float u, SampShared& sh) {
   const int C = (V + (int)blockDim.x - 1) / (int)blockDim.x;
   const int lo = min(V, (int)threadIdx.x * C), hi = min(V, lo + C);
   float ps = 0.0f;
   for (int v = lo; v < hi; ++v) ps += w(v);
-  __syncthreads();
-  sh.part[threadIdx.x] = ps;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float tot = 0.0f;
-    for (int t = 0; t < (int)blockDim.x; ++t) tot += sh.part[t];
-    const float target = u * tot;
-    float acc = 0.0f;
-    int seg = -1, last = -1;
-    for (int t = 0; t < (int)blockDim.x; ++t) {
-      const float p = sh.part[t];
-      if (p > 0.0f) last = t;
-      if (seg < 0 && acc + p > target) {
-        seg = t;
-        sh.before = acc;
-      }
-      acc += p;
-    }
-    if (seg < 0) {  // rounding at the top end: the last range with weight
-      seg = last;
-      sh.before = -1.0f;
-    }
-    sh.seg = seg;
-    sh.idx = -1;
-    sh.stat = target;
-  }
-  __syncthreads();
-  if ((int)threadIdx.x == sh.seg) {
-    const float target = sh.stat;
-    float acc = sh.before;
+  float total;
+  const float incl = block_incl_scan(ps, sh, &total);
+  const float target = u * total;
+  // the first thread whose running sum passes the target, else the last with weight
+  const int2 mm = block_minmax(incl > target ? (int)threadIdx.x : 0x7fffffff, ps > 0.0f ? (int)threadIdx.x : -1, sh);
+  if (mm.y < 0) return -1;
+  const bool found_seg = mm.x != 0x7fffffff;
+  const int tseg = found_seg ? mm.x : mm.y;
+  if ((int)threadIdx.x == tseg) {
+    float a = found_seg ? incl - ps : -1.0f;
     int found = -1, lastv = -1;
     for (int v = lo; v < hi; ++v) {
       const float x = w(v);
       if (x > 0.0f) lastv = v;
-      if (found < 0 && sh.before >= 0.0f && acc + x > target) found = v;
-      acc += x;
+      if (found < 0 && a >= 0.0f && a + x > target) found = v;
+      a += x;
     }
     sh.idx = found >= 0 ? found : lastv;
   }
   __syncthreads();
   return sh.idx;
+}
+
+// ---- vocabulary sweeps split over a cluster (tree expansion and acceptance) --------------
+// A cluster of kTreeCluster CTAs shares one sweep: CTA rank r owns the contiguous range
+// [r VC, (r + 1) VC) of the vocabulary.  Each reduction combines one value per CTA, read
+// through distributed shared memory in rank order, so every CTA of the cluster gets the same
+// value whatever the scheduling, and every decision taken from it is uniform across the
+// cluster.  Exchange slots alternate: a slot is written again only after a later cluster
+// barrier, which every CTA reaches only once it has read the slot.
+constexpr int kTreeCluster = 8;
+namespace cg = cooperative_groups;
+
+struct ClSweep {
+  cg::cluster_group g;
+  int rank, lo, hi;  // this CTA's vocabulary range
+  int k;             // reductions so far
+  float* xch;        // [2] exchange slots in this CTA's shared memory
+  int* xidx;         // the index an inverse-CDF draw found (on the CTA that found it)
+  __device__ ClSweep(int V, float* x, int* xi) : g(cg::this_cluster()), k(0), xch(x), xidx(xi) {
+    rank = (int)g.block_rank();
+    const int VC = (V + kTreeCluster - 1) / kTreeCluster;
+    lo = min(V, rank * VC);
+    hi = min(V, lo + VC);
+  }
+  // v: this CTA's value (the same in all its threads); returns the max or the sum over ranks
+  __device__ float combine(float v, bool is_max) {
+    const int slot = k++ & 1;
+    if (threadIdx.x == 0) xch[slot] = v;
+    g.sync();
+    float r = is_max ? -INFINITY : 0.0f;
+    for (int i = 0; i < kTreeCluster; ++i) {
+      const float x = *g.map_shared_rank(xch + slot, i);
+      r = is_max ? fmaxf(r, x) : r + x;
+    }
+    return r;
+  }
+};
+
+// (max, sum of exp((l - max) / T)) of one logits row, over the cluster; the CTA's part of the
+// row is its slice (row entries lo .. hi - 1, staged in shared memory).
+template <typename T>
+__device__ float2 cl_softmax_stats(ClSweep& c, const T* slice, float invT, SampShared& sh) {
+  const int n = c.hi - c.lo;
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, Act<T>::to_f(slice[i]));
+  m = c.combine(block_max(m, sh), true);
+  float z = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) z += expf((Act<T>::to_f(slice[i]) - m) * invT);
+  z = c.combine(block_sum(z, sh), false);
+  return make_float2(m, z);
+}
+
+// The CTA's part of a row into shared memory (coalesced loads); the caller syncs.
+template <typename T>
+__device__ __forceinline__ void stage_slice(const ClSweep& c, const T* row, T* slice) {
+  for (int v = c.lo + threadIdx.x; v < c.hi; v += blockDim.x) slice[v - c.lo] = row[v];
+}
+// Dynamic shared memory of the cluster kernels: one CTA's slice of a vocabulary row.
+inline size_t cl_slice_bytes(int V, size_t elt) { return (size_t)((V + kTreeCluster - 1) / kTreeCluster) * elt; }
+
+// Index drawn from the unnormalised weights w(0..V) with the uniform u, over the cluster:
+// within a CTA each thread sums a contiguous slice, the slices are prefix-summed in a fixed
+// order; the CTA totals are scanned in rank order, then the owning CTA finds the first thread
+// whose running sum passes the target and that thread its range in vocabulary order.  -1 when
+// every weight is zero.
+template <typename W>
+__device__ int cl_icdf(ClSweep& c, W w, float u, SampShared& sh) {
+  const int n = c.hi - c.lo;
+  const int C = (n + (int)blockDim.x - 1) / (int)blockDim.x;
+  const int lo = c.lo + min(n, (int)threadIdx.x * C), hi = min(c.hi, lo + C);
+  float ps = 0.0f;
+  for (int v = lo; v < hi; ++v) ps += w(v);
+  float cta_total;
+  const float incl = block_incl_scan(ps, sh, &cta_total);
+  // the CTA totals, in rank order
+  const int slot = c.k++ & 1;
+  if (threadIdx.x == 0) c.xch[slot] = cta_total;
+  c.g.sync();
+  float tots[kTreeCluster];
+  float total = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kTreeCluster; ++i) {
+    tots[i] = *c.g.map_shared_rank(c.xch + slot, i);
+    total += tots[i];
+  }
+  const float target = u * total;
+  float acc = 0.0f, before = -1.0f;
+  int seg = -1, last = -1;
+#pragma unroll
+  for (int i = 0; i < kTreeCluster; ++i) {
+    if (tots[i] > 0.0f) last = i;
+    if (seg < 0 && acc + tots[i] > target) {
+      seg = i;
+      before = acc;
+    }
+    acc += tots[i];
+  }
+  if (seg < 0) seg = last;  // rounding at the top end (before -1: the last weight of that CTA)
+  if (seg < 0) return -1;   // every weight is zero (the same verdict on every CTA)
+  if (c.rank == seg) {
+    // the first thread whose running sum passes the target, else the last with weight
+    const bool hit = before >= 0.0f && before + incl > target;
+    const int2 mm = block_minmax(hit ? (int)threadIdx.x : 0x7fffffff, ps > 0.0f ? (int)threadIdx.x : -1, sh);
+    const bool found_seg = mm.x != 0x7fffffff;
+    const int tseg = found_seg ? mm.x : mm.y;
+    if ((int)threadIdx.x == tseg) {
+      float a = found_seg ? before + incl - ps : -1.0f;
+      int found = -1, lastv = -1;
+      for (int v = lo; v < hi; ++v) {
+        const float x = w(v);
+        if (x > 0.0f) lastv = v;
+        if (found < 0 && a >= 0.0f && a + x > target) found = v;
+        a += x;
+      }
+      *c.xidx = found >= 0 ? found : lastv;
+    }
+  }
+  c.g.sync();
+  return *c.g.map_shared_rank(c.xidx, seg);
 }
 
 // Draft step i, stream blockIdx.x: x ~ softmax(draft logits / T) for position L + i; the
@@ -444,7 +593,8 @@ struct KvPlanes {
 // consecutive slots root + j, j = 1..a, in every layer and head; ascending j, one barrier per
 // j: a source is never an earlier destination (a node of depth j sits at slot >= root + j).
 template <typename T>
-__device__ void compact_path(const KvPlanes<T>& p, int s, int root, int a, const int* path) {
+__device__ void compact_path(const KvPlanes<T>& p, int s, int root, int a, const int* path, int part = 0,
+                             int parts = 1) {
   const size_t plane = (size_t)p.kv_heads * p.max_seq * p.hd;
   T* base = p.kv + (size_t)s * p.kv_ss;
   const int blocks = p.layers * 2 * p.kv_heads;  // (layer, K|V, head) blocks
@@ -453,7 +603,7 @@ __device__ void compact_path(const KvPlanes<T>& p, int s, int root, int a, const
   for (int j = 1; j <= a; ++j) {
     const int src = root + path[j - 1], dst = root + j;
     if (src != dst && src < p.max_seq && dst < p.max_seq)
-      for (int e = threadIdx.x; e < blocks * per_row; e += blockDim.x) {
+      for (int e = part * blockDim.x + threadIdx.x; e < blocks * per_row; e += parts * blockDim.x) {
         const int b = e / per_row, c = e % per_row;
         T* blk = base + (size_t)(b / p.kv_heads) * plane + (size_t)(b % p.kv_heads) * p.max_seq * p.hd;
         if (vec)
@@ -512,26 +662,32 @@ __device__ int block_argmax_excl(const T* row, int V, const int* skip, int n, Sa
   return sh.idx;
 }
 
-// Children of the nodes at `depth` (block = one node of one stream): the draft's logits row
-// of the node (row blockIdx.x of the stream's rows at this depth) gives them.
+// Children of the nodes at `depth` (one cluster = one node of one stream): the draft's logits
+// row of the node (row blockIdx.x / kTreeCluster of the stream's rows at this depth) gives
+// them.  The sampled form sweeps the vocabulary over the cluster; the greedy and oracle forms
+// run on the cluster's first CTA.
 template <typename T>
-__global__ void __launch_bounds__(kSampThreads) tree_expand_kernel(const DevState* st, const T* logits, int depth,
-                                                                   TreeTopo tt, vella_spec_cfg_dev c, const int* ref,
-                                                                   int* ttok, unsigned char* onpath, int vocab,
-                                                                   int max_seq, T* qrows, float2* qstats, int S) {
+__global__ void __cluster_dims__(kTreeCluster, 1, 1) __launch_bounds__(kSampThreads)
+    tree_expand_kernel(const DevState* st, const T* logits, int depth, TreeTopo tt, vella_spec_cfg_dev c,
+                       const int* ref, int* ttok, unsigned char* onpath, int vocab, int max_seq, T* qrows,
+                       float2* qstats, int S) {
   __shared__ SampShared sh;
   __shared__ int picked[16];
+  __shared__ float xch[2];
+  __shared__ int xidx;
   pdl_wait();
   pdl_launch_next();
   const int rows = tt.level_start[depth + 1] - tt.level_start[depth];
-  const int node = tt.level_start[depth] + blockIdx.x, s = blockIdx.y;
+  const int item = blockIdx.x / kTreeCluster;
+  const int node = tt.level_start[depth] + item, s = blockIdx.y;
   const int nc = tt.n_child[node], fc = tt.first_child[node];
-  if (nc == 0) return;
+  if (nc == 0) return;  // the whole cluster
   const int N = tt.nodes;
   const DevState& x = st[s];
-  const T* row = logits + ((size_t)s * rows + blockIdx.x) * vocab;
+  const T* row = logits + ((size_t)s * rows + item) * vocab;
+  const bool first = blockIdx.x % kTreeCluster == 0;
   if (c.draft_mode == VELLA_DRAFT_ORACLE) {
-    if (threadIdx.x == 0) {
+    if (first && threadIdx.x == 0) {
       for (int i = 0; i < nc; ++i) {
         const int ch = fc + i;
         const int ri = x.L - 1 + tt.dep[ch] - x.P;
@@ -547,6 +703,7 @@ __global__ void __launch_bounds__(kSampThreads) tree_expand_kernel(const DevStat
     return;
   }
   if (c.temperature <= 0.0f) {  // the draft's top-nc tokens
+    if (!first) return;
     for (int i = 0; i < nc; ++i) {
       const int t = block_argmax_excl(row, vocab, picked, i, sh);
       if (threadIdx.x == 0) picked[i] = t;
@@ -557,36 +714,50 @@ __global__ void __launch_bounds__(kSampThreads) tree_expand_kernel(const DevStat
     return;
   }
   // nc independent samples of softmax(row / T); the row is kept for the acceptance test
+  extern __shared__ __align__(16) unsigned char cl_dyn[];
+  T* slice = reinterpret_cast<T*>(cl_dyn);
+  ClSweep cl(vocab, xch, &xidx);
+  stage_slice(cl, row, slice);
+  __syncthreads();
   const float invT = 1.0f / c.temperature;
-  const float2 mz = row_softmax_stats(row, vocab, invT, sh);
+  const float2 mz = cl_softmax_stats(cl, slice, invT, sh);
   for (int i = 0; i < nc; ++i) {
     const float u = uni(c, (uint32_t)x.pass, (uint32_t)(fc + i), kPurposeDraft, s);
-    int t = sample_icdf([&](int v) { return expf((Act<T>::to_f(row[v]) - mz.x) * invT); }, vocab, u, sh);
-    if (threadIdx.x == 0) ttok[(size_t)s * N + fc + i] = t < 0 ? 0 : t;
+    const int t =
+        cl_icdf(cl, [&](int v) { return expf((Act<T>::to_f(slice[v - cl.lo]) - mz.x) * invT); }, u, sh);
+    if (first && threadIdx.x == 0) ttok[(size_t)s * N + fc + i] = t < 0 ? 0 : t;
   }
   T* q = qrows + ((size_t)node * S + s) * vocab;
-  for (int v = threadIdx.x; v < vocab; v += blockDim.x) q[v] = row[v];
-  if (threadIdx.x == 0) qstats[(size_t)node * S + s] = mz;
+  for (int v = cl.lo + threadIdx.x; v < cl.hi; v += blockDim.x) q[v] = slice[v - cl.lo];
+  if (first && threadIdx.x == 0) qstats[(size_t)node * S + s] = mz;
+  cl.g.sync();  // no CTA leaves while another may still read its exchange slots
 }
 
-// Tree acceptance of stream blockIdx.x over the verify rows of its N nodes, then the KV
-// compaction of the accepted path in the target's and the draft's caches (one launch after
-// the verify logits).
+// Tree acceptance of stream blockIdx.x / kTreeCluster over the verify rows of its N nodes,
+// then the KV compaction of the accepted path in the target's and the draft's caches (one
+// launch after the verify logits).  The sampled walk sweeps the vocabulary over the cluster
+// (every decision is taken from cluster-wide values, so all its CTAs walk the same path); the
+// residual row lives in global memory, each CTA updating its own range, and single entries of
+// other ranges are read through L2 after a cluster barrier.  The compaction is split over the
+// cluster; the greedy walk runs on its first CTA.
 template <typename T>
-__global__ void __launch_bounds__(kSampThreads) tree_accept_kernel(
+__global__ void __cluster_dims__(kTreeCluster, 1, 1) __launch_bounds__(kSampThreads) tree_accept_kernel(
     DevState* st, int* tok, const T* logits, const int* ys, TreeTopo tt, vella_spec_cfg_dev c, const int* ttok,
     const unsigned char* onpath, const int* ref, const T* qrows, const float2* qstats, int S, float* resid,
     KvPlanes<T> kt, KvPlanes<T> kd, int vocab, int max_seq, const int* nf, const int* err_t, const int* err_d) {
   __shared__ SampShared sh;
   __shared__ int s_u, s_a, s_acc, s_bonus, s_path[16];
+  __shared__ float xch[2];
+  __shared__ int xidx;
   pdl_wait();
   pdl_launch_next();
-  const int s = blockIdx.x, N = tt.nodes;
+  const int s = blockIdx.x / kTreeCluster, part = blockIdx.x % kTreeCluster, N = tt.nodes;
+  const bool first = part == 0;
   DevState& x = st[s];
   const bool stop = done(x);
   __syncthreads();
-  if (stop) {
-    if (threadIdx.x == 0) {
+  if (stop) {  // the whole cluster
+    if (first && threadIdx.x == 0) {
       x.nonfinite = *nf;
       x.err |= *err_t | *err_d;
       x.n_new = 0;
@@ -595,7 +766,10 @@ __global__ void __launch_bounds__(kSampThreads) tree_accept_kernel(
   }
   const int root = x.L - 1;
   const int* tt_s = ttok + (size_t)s * N;
+  int parts = kTreeCluster;
   if (c.temperature <= 0.0f) {
+    if (!first) return;
+    parts = 1;
     if (threadIdx.x == 0) {
       int u = 0, a = 0, y = 0;
       for (;;) {
@@ -611,6 +785,9 @@ __global__ void __launch_bounds__(kSampThreads) tree_accept_kernel(
       s_bonus = y;
     }
   } else {
+    extern __shared__ __align__(16) unsigned char cl_dyn[];
+    T* slice = reinterpret_cast<T*>(cl_dyn);  // this CTA's part of the current verify row
+    ClSweep cl(vocab, xch, &xidx);
     const float invT = 1.0f / c.temperature;
     float* r = resid + (size_t)s * vocab;
     if (threadIdx.x == 0) {
@@ -621,9 +798,13 @@ __global__ void __launch_bounds__(kSampThreads) tree_accept_kernel(
     for (;;) {
       const int u = s_u;
       const T* prow = logits + ((size_t)s * N + u) * vocab;
-      const float2 pm = row_softmax_stats(prow, vocab, invT, sh);
-      for (int v = threadIdx.x; v < vocab; v += blockDim.x) r[v] = expf((Act<T>::to_f(prow[v]) - pm.x) * invT) / pm.y;
+      __syncthreads();  // the previous row's slice is no longer read
+      stage_slice(cl, prow, slice);
       __syncthreads();
+      const float2 pm = cl_softmax_stats(cl, slice, invT, sh);
+      for (int v = cl.lo + threadIdx.x; v < cl.hi; v += blockDim.x)
+        r[v] = expf((Act<T>::to_f(slice[v - cl.lo]) - pm.x) * invT) / pm.y;
+      cl.g.sync();  // the whole row is in place for the tests below
       DraftQ<T> q{};
       q.invT = invT;
       q.vocab = vocab;
@@ -642,23 +823,24 @@ __global__ void __launch_bounds__(kSampThreads) tree_accept_kernel(
       for (int i = 0; i < nc; ++i) {
         const int ch = fc + i, xk = tt_s[ch];
         const float uacc = uni(c, (uint32_t)x.pass, (uint32_t)ch, kPurposeAccept, s);
-        if (uacc * q(xk) < r[xk]) {
+        if (uacc * q(xk) < __ldcg(r + xk)) {
           acc = ch;
           break;
         }
         // rejected: the residual max(0, r - q), renormalised
-        float part = 0.0f;
-        for (int v = threadIdx.x; v < vocab; v += blockDim.x) {
-          const float w = fmaxf(0.0f, r[v] - q(v));
+        float part_sum = 0.0f;
+        for (int v = cl.lo + threadIdx.x; v < cl.hi; v += blockDim.x) {
+          const float w = fmaxf(0.0f, __ldcg(r + v) - q(v));
           r[v] = w;
-          part += w;
+          part_sum += w;
         }
-        const float tot = block_sum(part, sh);
+        const float tot = cl.combine(block_sum(part_sum, sh), false);
         if (tot > 0.0f)
-          for (int v = threadIdx.x; v < vocab; v += blockDim.x) r[v] /= tot;
-        __syncthreads();
+          for (int v = cl.lo + threadIdx.x; v < cl.hi; v += blockDim.x) r[v] = __ldcg(r + v) / tot;
+        cl.g.sync();
       }
       if (acc >= 0) {
+        __syncthreads();
         if (threadIdx.x == 0) {
           s_path[s_a] = acc;
           s_a += 1;
@@ -668,14 +850,15 @@ __global__ void __launch_bounds__(kSampThreads) tree_accept_kernel(
         continue;
       }
       const float u2 = uni(c, (uint32_t)x.pass, (uint32_t)u, kPurposeResidual, s);
-      int b = sample_icdf([&](int v) { return r[v]; }, vocab, u2, sh);
-      if (b < 0) b = sample_icdf([&](int v) { return expf((Act<T>::to_f(prow[v]) - pm.x) * invT); }, vocab, u2, sh);
+      int b = cl_icdf(cl, [&](int v) { return __ldcg(r + v); }, u2, sh);
+      if (b < 0) b = cl_icdf(cl, [&](int v) { return expf((Act<T>::to_f(slice[v - cl.lo]) - pm.x) * invT); }, u2, sh);
       if (threadIdx.x == 0) s_bonus = b < 0 ? 0 : b;
       break;
     }
+    cl.g.sync();  // no CTA leaves while another may still read its exchange slots
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (first && threadIdx.x == 0) {
     const int a = s_a;
     int* tk = tok + (size_t)s * max_seq;
     x.nonfinite = *nf;
@@ -692,8 +875,8 @@ __global__ void __launch_bounds__(kSampThreads) tree_accept_kernel(
     x.pass += 1;
     x.produced += a + 1;
   }
-  compact_path(kt, s, root, s_a, s_path);
-  compact_path(kd, s, root, s_a, s_path);
+  compact_path(kt, s, root, s_a, s_path, part, parts);
+  compact_path(kd, s, root, s_a, s_path, part, parts);
 }
 
 }  // namespace
@@ -801,10 +984,22 @@ TreeView tree_view(Spec* s, int node0) {
   return v;
 }
 
+// Shared memory of a cluster sweep kernel: one CTA's slice of a vocabulary row (above the
+// default 48 KB only for vocabularies of more than 196608 entries).
+template <typename K>
+int cl_smem(K kernel, int vocab, size_t elt, size_t* bytes) {
+  *bytes = cl_slice_bytes(vocab, elt);
+  if (*bytes > 48 * 1024) VELLA_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)*bytes));
+  return VELLA_OK;
+}
+
 template <typename T>
 int launch_tree_expand(Spec* s, int depth) {
   const int rows = s->topo.level_start[depth + 1] - s->topo.level_start[depth];
-  return launch_kernel(tree_expand_kernel<T>, dim3(rows, s->streams), dim3(kSampThreads), 0, s->stream,
+  size_t smem;
+  int rc;
+  if ((rc = cl_smem(tree_expand_kernel<T>, s->target->cfg.vocab, sizeof(T), &smem))) return rc;
+  return launch_kernel(tree_expand_kernel<T>, dim3(rows * kTreeCluster, s->streams), dim3(kSampThreads), smem, s->stream,
                        (const DevState*)s->dstate, static_cast<const T*>(s->draft->logits), depth, s->topo,
                        s->dev_cfg(), (const int*)s->ref, s->ttok, s->onpath, s->target->cfg.vocab, s->max_seq,
                        static_cast<T*>(s->qrows), s->qstats, s->streams);
@@ -819,7 +1014,11 @@ KvPlanes<T> kv_planes(const Model* m) {
 template <typename T>
 int launch_tree_accept(Spec* s) {
   const Model* t = s->target;
-  return launch_kernel(tree_accept_kernel<T>, dim3(s->streams), dim3(kSampThreads), 0, s->stream, s->dstate, s->tok,
+  size_t smem;
+  int rc;
+  if ((rc = cl_smem(tree_accept_kernel<T>, t->cfg.vocab, sizeof(T), &smem))) return rc;
+  return launch_kernel(tree_accept_kernel<T>, dim3(s->streams * kTreeCluster), dim3(kSampThreads), smem, s->stream,
+                       s->dstate, s->tok,
                        static_cast<const T*>(t->logits), (const int*)t->ys, s->topo, s->dev_cfg(),
                        (const int*)s->ttok, (const unsigned char*)s->onpath, (const int*)s->ref,
                        static_cast<const T*>(s->qrows), (const float2*)s->qstats, s->streams, s->resid,
