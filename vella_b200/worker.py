@@ -360,6 +360,7 @@ class WhisperRuntime:
     components = {"whisper_decoder": True, "whisper_encoder": True}
 
     def __init__(self, path: str):
+        import torch  # noqa: F401  (device memory figures in the status and metrics)
         from vella_b200 import checkpoint as C
         from vella_b200 import whisper as VW
         try:
@@ -401,13 +402,24 @@ def _process_memory() -> Dict[str, int]:
             "processPeakFootprintBytes": peak}
 
 
-def _device_memory() -> Dict[str, int]:
-    """(active, cached, peak) bytes of the CUDA allocator when torch has initialised it."""
+_PEAK = [0]
+
+
+def _device_memory(reset: bool = False) -> Dict[str, int]:
+    """Device bytes in use (the library allocates through the CUDA runtime, outside torch's
+    allocator, so this is the device's used memory: total minus free), the part torch's
+    allocator holds cached, and the running maximum of the samples since the last reset.
+    Zero until a GPU runtime has imported torch (the stub model never does)."""
+    if reset:
+        _PEAK[0] = 0
     t = sys.modules.get("torch")
-    if t is None or not t.cuda.is_available() or not t.cuda.is_initialized():
+    if t is None or not t.cuda.is_available():
         return {"active": 0, "cache": 0, "peak": 0}
-    active = t.cuda.memory_allocated()
-    return {"active": active, "cache": t.cuda.memory_reserved() - active, "peak": t.cuda.max_memory_allocated()}
+    free, total = t.cuda.mem_get_info()
+    cache = t.cuda.memory_reserved() - t.cuda.memory_allocated() if t.cuda.is_initialized() else 0
+    active = max(0, total - free - cache)
+    _PEAK[0] = max(_PEAK[0], active)
+    return {"active": active, "cache": cache, "peak": _PEAK[0]}
 
 
 def _gpu() -> Dict[str, Optional[str]]:
@@ -498,6 +510,7 @@ class Worker:
         if path == self.path:
             return
         self.release()
+        _device_memory(reset=True)
         t0 = time.monotonic()
         try:
             self.runtime = self._load(path, arch)
@@ -590,6 +603,8 @@ class Worker:
             if self.runtime is None:
                 raise RequestError()
             t0 = time.monotonic()
+            if not cold:
+                _device_memory(reset=True)
             response["text"] = self.runtime.transcribe(samples, options)
             self.applied = {"language": options.language, "vocabulary": options.vocabulary}
             response["applied"] = dict(self.applied)
