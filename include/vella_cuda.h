@@ -410,8 +410,12 @@ VELLA_API int vella_whisper_init_random(vella_whisper* w, uint64_t seed, float s
  * dec.ln2, dec.cq, dec.ckv (cross k|v rows, k's bias zero), dec.co, dec.ln3, dec.fc1, dec.fc2;
  * whole model: conv1 (K padded to a multiple of 64 with zero columns), conv2, enc_pos,
  * enc_ln, dec_ln, embed (token embedding = vocabulary projection), dec_pos, and the
- * activations enc_out [n_audio, d_model] (the last encoded window) and xkv (the cross-
- * attention K|V of every stream and decoder layer, [streams][dec_layers][n_audio][2 d_model]). */
+ * activations enc_out [n_audio, d_model] (the last encoded window), xkv (the cross-
+ * attention K|V of every stream and decoder layer, [streams][dec_layers][n_audio][2 d_model])
+ * and kv (the self-attention cache, [streams][dec_layers][K, V][heads][max_target][head_dim]).
+ * Setting VELLA_WHISPER_FUSE=0 in the environment before vella_whisper_create gives a handle
+ * that runs the decoder's LayerNorms and K/V appends as launches of their own instead of in
+ * the neighbouring kernels (the same values; for comparisons). */
 /* Whisper's log-mel input features of `streams` windows of 16 kHz mono audio (device
  * pointers; window s at audio + s * n_samples), each padded with zeros or trimmed to 30 s
  * (480000 samples): reflect-padded STFT (400-point periodic Hann window, hop 160, 3000

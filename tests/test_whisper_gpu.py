@@ -408,3 +408,35 @@ def test_batched_end_of_text_and_log_probabilities_follow_single_streams():
     single.close()
     mb.close()
 
+
+
+def test_fused_decoder_step_equals_unfused_launches(monkeypatch):
+    """The decoder's fusions (the first LayerNorm in the embedding kernel, the K/V append in
+    the q|k|v GEMM's epilogue, the other LayerNorms in the preceding GEMM's last CTA) change
+    no value: a handle created with VELLA_WHISPER_FUSE=0 (separate launches) decodes the same
+    tokens, leaves a bit-equal self-attention cache, and gives bit-equal logits for one- and
+    two-row forwards (the rows the LayerNorm tail takes), int4 and dense fp16."""
+    from dataclasses import replace
+
+    from vella_b200 import whisper as VW
+    prompt = [50258, 50259, 50359, 50363]
+    for cfg in (VW.TINY, replace(VW.TINY, bits=0)):
+        mel = mel_of(cfg, 41)
+        handles = []
+        for fuse in ("1", "0"):
+            monkeypatch.setenv("VELLA_WHISPER_FUSE", fuse)
+            h = VW.Whisper(cfg)
+            h.init_random(8, 0.1)
+            h.encode(mel)
+            handles.append(h)
+        monkeypatch.delenv("VELLA_WHISPER_FUSE")
+        fused, plain = handles
+        try:
+            a, b = fused.decode(prompt, 24), plain.decode(prompt, 24)
+            assert a.tokens == b.tokens
+            assert np.array_equal(download(fused, "kv"), download(plain, "kv"))
+            for toks in ([50258], [50258, 50259]):
+                assert np.array_equal(fused.score(toks), plain.score(toks)), toks
+        finally:
+            fused.close()
+            plain.close()

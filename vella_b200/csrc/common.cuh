@@ -113,4 +113,56 @@ __device__ __forceinline__ float warp_max(float v) {
 // GELU, erf form: 0.5 x (1 + erf(x / sqrt(2))) (MLX's default gelu).
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 
+constexpr int kLnMaxD = 2048;  // LayerNorm row length limit (8 values per thread)
+
+// LayerNorm of one row of D <= kLnMaxD values by 256 threads t = 0..255 (value i on thread
+// i % 256): fp32 mean and centred variance, x_hat rounded to T, then T(w * x_hat + b)
+// (WhisperFusedDecode.swift:204-251 row algorithm, one final rounding).  The row is read
+// with L2 loads (it may have been written by other CTAs of the same kernel); `sync` is the
+// 256 threads' barrier and `red` 8 floats of shared memory.  Every caller runs this same
+// sequence, so a row's result does not depend on which kernel normalises it.
+template <typename T, typename Sync>
+__device__ __forceinline__ void ln_row256(T* __restrict__ orow, const T* xr, const T* __restrict__ w,
+                                          const T* __restrict__ b, int D, float eps, int t, float* red, Sync sync) {
+  using A = Act<T>;
+  const int warp = t >> 5, lane = t & 31;
+  auto bsum = [&](float v) {
+    v = warp_sum(v);
+    sync();
+    if (lane == 0) red[warp] = v;
+    sync();
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += red[k];
+    return s;
+  };
+  float v[kLnMaxD / 256];
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kLnMaxD / 256; ++j) {
+    const int i = t + 256 * j;
+    v[j] = i < D ? A::to_f(__ldcg(xr + i)) : 0.0f;
+    s += v[j];
+  }
+  const float mean = bsum(s) / (float)D;
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kLnMaxD / 256; ++j) {
+    const int i = t + 256 * j;
+    if (i < D) {
+      v[j] -= mean;
+      ss = fmaf(v[j], v[j], ss);
+    }
+  }
+  const float r = sqrtf(bsum(ss) / (float)D + eps);
+#pragma unroll
+  for (int j = 0; j < kLnMaxD / 256; ++j) {
+    const int i = t + 256 * j;
+    if (i < D) {
+      const float xh = A::to_f(A::from_f(v[j] / r));
+      orow[i] = A::from_f(fmaf(A::to_f(w[i]), xh, A::to_f(b[i])));
+    }
+  }
+}
+
 }  // namespace vella

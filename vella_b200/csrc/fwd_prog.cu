@@ -834,7 +834,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
           ep.bias = nullptr; ep.res = o.res; ep.out = o.out; ep.partial = a.partial; ep.flags = a.flags;
           ep.N = o.N; ep.mc = o.head ? LR : a.M; ep.P = op_ctas(o, P); ep.U = (long long)o.rowblocks * nkc; ep.nkc = nkc;
           ep.gate = o.gate; ep.has_bias = 0; ep.has_res = o.has_res; ep.gelu = 0; ep.rope = o.rope;
-          ep.re = &s_re; ep.fault = &g_fwd_fault; ep.abort = a.bar + 1;
+          ep.re = &s_re; ep.fault = &g_fwd_fault; ep.abort = a.bar + 1; ep.ka = nullptr;
           if (o.rope) {
             re.cs = a.rope_cs; re.q = const_cast<void*>(a.q);
             re.kc = static_cast<T*>(o.kc) + a.kv0; re.vc = static_cast<T*>(o.vc) + a.kv0;

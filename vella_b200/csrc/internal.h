@@ -79,7 +79,9 @@ int launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, 
 int device_workspace(size_t bytes, void** out);
 
 // ---- GEMM (qgemm.cu) -------------------------------------------------------------------
-struct RopeEpi;  // layers.cuh
+struct RopeEpi;      // layers.cuh
+struct KvAppendEpi;  // layers.cuh
+struct NormEpi;      // layers.cuh
 struct QgemmPlan {
   int rows_out;   // output rows per CTA (128, or 64 with the SiLU gate)
   int rowblocks;  // ceil(N / rows_out)
@@ -103,7 +105,8 @@ int stream_flag_count(int P);  // ints of the flag region (zero between calls)
 int stream_launch(const vella_qgemm_desc& d, int P, bool light, const void* x, const void* w, const void* scales,
                   const void* biases, const void* up_w, const void* up_scales, const void* up_biases,
                   const void* bias, const void* residual, void* out, int* flags, float* partial,
-                  cudaStream_t stream, const RopeEpi* rope = nullptr);
+                  cudaStream_t stream, const RopeEpi* rope = nullptr, const KvAppendEpi* app = nullptr,
+                  const NormEpi* norm = nullptr, int* done = nullptr);
 int stream_fault_status(int clear);
 int fwd_fault_status(int clear);  // fwd_prog.cu: the persistent decode forward's flags
 
@@ -116,11 +119,13 @@ int tc_fault_status(int clear);
 
 bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* plan);
 
-// rope (small-M streaming plans only): RoPE + KV append instead of writing `out`.
+// Small-M streaming plans only: rope, RoPE + KV append instead of writing `out`; app, the
+// K/V append besides writing `out`; norm, LayerNorm of the output rows after the call.
 int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& plan, const void* x, const void* w,
                  const void* scales, const void* biases, const void* up_w, const void* up_scales,
                  const void* up_biases, const void* bias, const void* residual, void* out, void* ws,
-                 cudaStream_t stream, const RopeEpi* rope = nullptr);
+                 cudaStream_t stream, const RopeEpi* rope = nullptr, const KvAppendEpi* app = nullptr,
+                 const NormEpi* norm = nullptr);
 
 // 2D tensor map over a row-major array of `rows` rows of `inner` elements (`row_bytes`
 // apart), copied in boxes of box_inner x box_rows with the given swizzle; out-of-range

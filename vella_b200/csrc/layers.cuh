@@ -58,6 +58,27 @@ struct RopeEpi {
   int* err = nullptr;          // bit 1: a position past the cache
 };
 
+// K/V-append epilogue of a q|k|v projection without RoPE (the Whisper decoder's), fused into
+// the small-M streaming GEMM: output columns [d, 2d) of row m also go to the K cache
+// [heads][S][hd] of the row's stream at position pr.pos(m), columns [2d, 3d) to the V
+// cache (rows whose position lies outside [0, S) append nothing); `out` keeps all columns.
+struct KvAppendEpi {
+  void* kc = nullptr;  // the layer's K cache of stream 0; stream s adds s * kv_ss elements
+  void* vc = nullptr;
+  PosRef pr{};
+  int d = 0, hd = 0, S = 0;
+  long long kv_ss = 0;
+};
+
+// LayerNorm of a streaming GEMM's output rows (N <= 2048 columns, weight w and bias b of N
+// elements) into `out`, run once the whole GEMM has finished by its last CTA to finish.
+struct NormEpi {
+  void* out = nullptr;
+  const void* w = nullptr;
+  const void* b = nullptr;
+  float eps = 0.0f;
+};
+
 constexpr int kAttnChunk = 64;   // keys per chunk (absolute-position aligned)
 constexpr int kAttnRows = 64;    // query rows x query heads per cluster (query block = 64 / GQ rows)
 constexpr int kAttnCluster = 8;  // CTAs per (kv head, query block); chunk c goes to CTA c % 8

@@ -483,15 +483,19 @@ bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* p) {
 int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& p, const void* x, const void* w,
                  const void* scales, const void* biases, const void* up_w, const void* up_scales,
                  const void* up_biases, const void* bias, const void* residual, void* out, void* ws,
-                 cudaStream_t stream, const RopeEpi* rope) {
+                 cudaStream_t stream, const RopeEpi* rope, const KvAppendEpi* app, const NormEpi* norm) {
   if (d.m == 0 || d.n == 0) return VELLA_OK;
-  if (rope && !p.stream) return fail(VELLA_E_INVALID, "qgemm: the RoPE epilogue runs on the streaming kernel only");
+  if ((rope || app || norm) && !p.stream)
+    return fail(VELLA_E_INVALID, "qgemm: the RoPE, K/V-append and LayerNorm epilogues run on the streaming kernel only");
   if (p.tc) return tc_launch(d, x, w, scales, biases, up_w, up_scales, up_biases, bias, residual, out, stream);
   if (p.stream) {
     int* flags = static_cast<int*>(ws);
     float* partial = reinterpret_cast<float*>(static_cast<char*>(ws) + counter_region((size_t)stream_flag_count(p.ctas)));
+    // the LayerNorm tail's arrival counter: the last int of the counter region (the stream
+    // flags take stream_flag_count(ctas) ints from its start)
+    int* done = flags + kCounterRegion / sizeof(int) - 1;
     return stream_launch(d, p.ctas, p.light, x, w, scales, biases, up_w, up_scales, up_biases, bias, residual, out, flags,
-                         partial, stream, rope);
+                         partial, stream, rope, app, norm, done);
   }
   Args a{};
   a.x = x; a.w = static_cast<const uint32_t*>(w); a.sc = scales; a.bi = biases;

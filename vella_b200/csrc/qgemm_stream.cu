@@ -77,6 +77,11 @@ struct SArgs {
   int has_bias, has_res, gelu;
   int rope;     // RoPE + KV-append epilogue (q|k|v projection, 128-row blocks = heads)
   RopeEpi re;
+  int app;      // K/V-append epilogue (q|k|v projection without RoPE)
+  KvAppendEpi ka;
+  int norm;     // LayerNorm of the output rows by the last CTA
+  NormEpi ne;
+  int* done;    // CTAs past their epilogue (the last one resets it to zero)
 };
 
 template <typename T, int BITS, int NT, bool GATE, bool LIGHT>
@@ -231,6 +236,7 @@ __global__ void __launch_bounds__(kThreads, LIGHT ? 2 : 1) qgemm_stream_kernel(c
   ep.N = a.N; ep.mc = min(a.M, kTokMax); ep.P = P; ep.U = U; ep.nkc = nkc;
   ep.gate = GATE; ep.has_bias = a.has_bias; ep.has_res = a.has_res; ep.gelu = a.gelu; ep.rope = a.rope;
   ep.re = &a.re; ep.fault = &g_stream_fault;
+  ep.ka = a.app ? &a.ka : nullptr;
 
   UnitWalk cur(u0, u1, nkc);
   int s = 0;
@@ -256,6 +262,28 @@ __global__ void __launch_bounds__(kThreads, LIGHT ? 2 : 1) qgemm_stream_kernel(c
     cur.next(nkc);
     if (!flush) continue;
     flush_rowblock<T, NT>(ep, c, rb, rb == rl && tail_shared, rb == rf && head_shared, acc, red, warp, lane);
+  }
+  if (a.norm) {
+    // The output rows are complete once every CTA has arrived here; the last to arrive
+    // normalises them (no CTA waits for another).
+    __threadfence();
+    named_sync(kBarConsumers, kRowWarps * 32);
+    if (tid == 0) {
+      const int last = atomicAdd(a.done, 1) == P - 1;
+      if (last) {
+        __threadfence();
+        *a.done = 0;  // every CTA has arrived: zero for the next call
+      }
+      abort_flag[1] = last;
+    }
+    named_sync(kBarConsumers, kRowWarps * 32);
+    if (abort_flag[1]) {
+      const int D = a.N;
+      for (int m = 0; m < ep.mc; ++m)
+        ln_row256<T>(static_cast<T*>(a.ne.out) + (size_t)m * D, static_cast<const T*>(a.out) + (size_t)m * D,
+                     static_cast<const T*>(a.ne.w), static_cast<const T*>(a.ne.b), D, a.ne.eps, tid, red,
+                     [] { named_sync(kBarConsumers, kRowWarps * 32); });
+    }
   }
 }
 
@@ -314,7 +342,7 @@ int stream_flag_count(int P) { return P * kRowWarps; }
 int stream_launch(const vella_qgemm_desc& d, int P, bool light, const void* x, const void* w, const void* scales,
                   const void* biases, const void* up_w, const void* up_scales, const void* up_biases,
                   const void* bias, const void* residual, void* out, int* flags, float* partial,
-                  cudaStream_t stream, const RopeEpi* rope) {
+                  cudaStream_t stream, const RopeEpi* rope, const KvAppendEpi* app, const NormEpi* norm, int* done) {
   SArgs a;
   std::memset(&a, 0, sizeof a);
   const bool gate = d.epilogue == VELLA_EPI_SILU_GATE;
@@ -361,6 +389,19 @@ int stream_launch(const vella_qgemm_desc& d, int P, bool light, const void* x, c
       return fail(VELLA_E_INVALID, "stream GEMM: RoPE epilogue needs a plain q|k|v projection of 128-row heads");
     a.rope = 1;
     a.re = *rope;
+  }
+  if (app) {
+    if (gate || rope || app->d <= 0 || app->hd <= 0 || app->d % app->hd || d.n != 3 * app->d)
+      return fail(VELLA_E_INVALID, "stream GEMM: the K/V-append epilogue needs a q|k|v projection of 3 x d rows");
+    a.app = 1;
+    a.ka = *app;
+  }
+  if (norm) {
+    if (gate || rope || d.n > kLnMaxD || !done || !norm->out || !norm->w || !norm->b)
+      return fail(VELLA_E_INVALID, "stream GEMM: the LayerNorm tail needs at most %d output columns", kLnMaxD);
+    a.norm = 1;
+    a.ne = *norm;
+    a.done = done;
   }
   if (light && d.bits != 4) return fail(VELLA_E_INVALID, "stream GEMM: the compact layout is int4 only");
   if (d.dtype == VELLA_BF16) {

@@ -31,6 +31,7 @@ constexpr int kThreads = (kRowWarps + 2) * 32;
 constexpr int kSlots = 128;
 constexpr int kTokMax = 16;
 constexpr int kBarPair0 = 2;  // named barriers 2..5: gate-row warp w with up-row warp w + 4
+constexpr int kBarConsumers = 6;  // named barrier 6: the kRowWarps consumer warps
 
 // UG groups of 64 per unit; BPG bytes per row and group; WCH 128-byte column chunks of the
 // weight tile; XCH 256-element chunks of the x slice.
@@ -435,6 +436,7 @@ struct Epi {
   int nkc;
   int gate, has_bias, has_res, gelu, rope;
   const RopeEpi* re;  // the RoPE epilogue's operands (rope != 0)
+  const KvAppendEpi* ka = nullptr;  // the K/V-append epilogue's operands, when set
   int* fault;      // the kernel's fault flags (bit 4: a gather wait ran out of time)
   const unsigned* abort = nullptr;  // when set and nonzero, a gather stops waiting
 };
@@ -550,7 +552,18 @@ __device__ __forceinline__ void flush_rowblock(const Epi& a, int c, int rb, bool
         if (a.has_bias) v += A::to_f(bias[n]);
         if (a.gelu) v = gelu_erf(v);
         if (a.has_res) v += A::to_f(__ldcg(res + o));
-        out[o] = A::from_f(v);
+        const T tv = A::from_f(v);
+        out[o] = tv;
+        if (a.ka && n >= a.ka->d) {
+          const KvAppendEpi& ka = *a.ka;
+          const int p = ka.pr.pos(tok);
+          if (p >= 0 && p < ka.S) {
+            const bool isv = n >= 2 * ka.d;
+            const int i = n - (isv ? 2 : 1) * ka.d;
+            T* base = static_cast<T*>(isv ? ka.vc : ka.kc) + (size_t)ka.pr.stream_of(tok) * ka.kv_ss;
+            base[((size_t)(i / ka.hd) * ka.S + p) * ka.hd + i % ka.hd] = tv;
+          }
+        }
       }
   };
   if (a.gate) {

@@ -22,6 +22,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -36,61 +37,19 @@ namespace vella {
 namespace {
 
 constexpr int kWRows = 16;      // decoder rows per forward (prompt chunk / teacher-forced chunk)
-constexpr int kLnMaxD = 2048;   // LayerNorm row length limit (8 values per thread)
 
 // ---- kernels -------------------------------------------------------------------------------
 
-__device__ __forceinline__ float block_sum256(float v, float* red) {
-  v = warp_sum(v);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = 0.0f;
-#pragma unroll
-  for (int w = 0; w < 8; ++w) t += red[w];
-  return t;
-}
-
-// LayerNorm of one row per CTA: fp32 mean and centred variance, x_hat rounded to T, then
-// T(w * x_hat + b) (WhisperFusedDecode.swift:204-251 row algorithm, one final rounding).
+// LayerNorm of one row per CTA (ln_row256).
 template <typename T>
 __global__ void __launch_bounds__(256) layernorm_kernel(T* __restrict__ out, const T* __restrict__ x,
                                                         const T* __restrict__ w, const T* __restrict__ b, int D,
                                                         float eps) {
-  using A = Act<T>;
   __shared__ float red[8];
   pdl_wait();
   pdl_launch_next();
-  const T* xr = x + (size_t)blockIdx.x * D;
-  T* orow = out + (size_t)blockIdx.x * D;
-  float v[kLnMaxD / 256];
-  float s = 0.0f;
-#pragma unroll
-  for (int j = 0; j < kLnMaxD / 256; ++j) {
-    const int i = threadIdx.x + 256 * j;
-    v[j] = i < D ? A::to_f(xr[i]) : 0.0f;
-    s += v[j];
-  }
-  const float mean = block_sum256(s, red) / (float)D;
-  float ss = 0.0f;
-#pragma unroll
-  for (int j = 0; j < kLnMaxD / 256; ++j) {
-    const int i = threadIdx.x + 256 * j;
-    if (i < D) {
-      v[j] -= mean;
-      ss = fmaf(v[j], v[j], ss);
-    }
-  }
-  const float r = sqrtf(block_sum256(ss, red) / (float)D + eps);
-#pragma unroll
-  for (int j = 0; j < kLnMaxD / 256; ++j) {
-    const int i = threadIdx.x + 256 * j;
-    if (i < D) {
-      const float xh = A::to_f(A::from_f(v[j] / r));
-      orow[i] = A::from_f(fmaf(A::to_f(w[i]), xh, A::to_f(b[i])));
-    }
-  }
+  ln_row256<T>(out + (size_t)blockIdx.x * D, x + (size_t)blockIdx.x * D, w, b, D, eps, threadIdx.x, red,
+               [] { __syncthreads(); });
 }
 
 template <typename Tin> __device__ __forceinline__ float ld_f(const Tin* p) { return Act<Tin>::to_f(*p); }
@@ -118,12 +77,14 @@ __global__ void __launch_bounds__(256) im2col_kernel(T* __restrict__ out, const 
 }
 
 // h[m] = T(T(embed[tok[p]]) + dec_pos[p]) at p = *pr.base + pr.off + m; a quantized row is
-// T(scale * q + bias) (multiply, then add, each rounded to fp32).
+// T(scale * q + bias) (multiply, then add, each rounded to fp32).  With ln_out set, also
+// ln_out[m] = LayerNorm(h[m]) (the first decoder layer's, ln_row256).
 template <typename T, int BITS>
 __global__ void __launch_bounds__(256) wembed_kernel(T* __restrict__ h, const void* __restrict__ E,
                                                      const T* __restrict__ Es, const T* __restrict__ Eb,
                                                      const T* __restrict__ pos, const int* __restrict__ tok, PosRef pr,
-                                                     int d, int vocab, int max_target, int* err) {
+                                                     int d, int vocab, int max_target, int* err, T* ln_out,
+                                                     const T* ln_w, const T* ln_b, float eps) {
   using A = Act<T>;
   pdl_wait();
   pdl_launch_next();
@@ -150,6 +111,11 @@ __global__ void __launch_bounds__(256) wembed_kernel(T* __restrict__ h, const vo
       e = A::to_f(A::from_f(__fadd_rn(__fmul_rn(A::to_f(Es[g]), q), A::to_f(Eb[g]))));
     }
     h[(size_t)blockIdx.x * d + i] = A::from_f(e + A::to_f(pos[(size_t)p * d + i]));
+  }
+  if (ln_out) {  // each thread reads back the values it wrote (i = threadIdx.x + 256 j)
+    __shared__ float red[8];
+    ln_row256<T>(ln_out + (size_t)blockIdx.x * d, h + (size_t)blockIdx.x * d, ln_w, ln_b, d, eps, threadIdx.x, red,
+                 [] { __syncthreads(); });
   }
 }
 
@@ -416,6 +382,10 @@ struct vella_whisper {
   cudaGraphExec_t step_exec = nullptr;
   bool step_warm = false;
   bool encoded = false;
+  // decoder fusions: the first LayerNorm in the embedding kernel, the K/V append in the
+  // q|k|v GEMM's epilogue, the other LayerNorms in the preceding GEMM's tail (off with
+  // VELLA_WHISPER_FUSE=0 at creation: the same values through separate launches)
+  bool fuse = true;
   int step_pos = -1;            // vella_whisper_step: position of the next token (-1: no decode begun)
   cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
   vella_whisper_stats stats{};
@@ -424,13 +394,23 @@ struct vella_whisper {
 namespace vella {
 namespace {
 
+int plan(vella_whisper* w, const WLin& L, int rows, int epi, vella_qgemm_desc* d, QgemmPlan* p) {
+  *d = vella_qgemm_desc{rows, L.q.n, L.q.k, L.bits, 64, w->cfg.dtype, epi};
+  if (!qgemm_plan(*d, p)) return fail(VELLA_E_UNSUPPORTED, "whisper gemm %dx%dx%d bits %d", rows, L.q.n, L.q.k, L.bits);
+  if (p->workspace > w->gemm_ws_bytes) return fail(VELLA_E_INVALID, "whisper gemm workspace too small");
+  return VELLA_OK;
+}
+
+// app / norm: the streaming kernel's K/V-append epilogue and LayerNorm tail (the caller
+// checks that the plan is a streaming one).
 int gemm(vella_whisper* w, const WLin& L, const void* x, int rows, void* out, int epi, const void* residual,
-         cudaStream_t s) {
-  vella_qgemm_desc d{rows, L.q.n, L.q.k, L.bits, 64, w->cfg.dtype, epi};
+         cudaStream_t s, const KvAppendEpi* app = nullptr, const NormEpi* norm = nullptr) {
+  vella_qgemm_desc d;
   QgemmPlan p;
-  if (!qgemm_plan(d, &p)) return fail(VELLA_E_UNSUPPORTED, "whisper gemm %dx%dx%d bits %d", rows, L.q.n, L.q.k, L.bits);
-  if (p.workspace > w->gemm_ws_bytes) return fail(VELLA_E_INVALID, "whisper gemm workspace too small");
-  return qgemm_launch(d, p, x, L.q.w, L.q.s, L.q.b, nullptr, nullptr, nullptr, L.bias, residual, out, w->gemm_ws, s);
+  int rc = plan(w, L, rows, epi, &d, &p);
+  if (rc) return rc;
+  return qgemm_launch(d, p, x, L.q.w, L.q.s, L.q.b, nullptr, nullptr, nullptr, L.bias, residual, out, w->gemm_ws, s,
+                      nullptr, app, norm);
 }
 
 template <typename T>
@@ -445,6 +425,27 @@ int layernorm(vella_whisper* w, void* out, const void* x, const WNorm& n, int ro
                                     : layernorm_t<__half>(out, x, n, rows, D, w->cfg.eps, s);
 }
 
+// Rows up to which a decoder GEMM's last CTA runs the following LayerNorm (one row after
+// another, on its 256 consumer threads); more rows take a LayerNorm launch of a CTA per row.
+constexpr int kLnTailRows = 2;
+
+// A residual GEMM into w->dh, then `n` (when set) of its rows into w->dn: in the GEMM's tail
+// when the streaming kernel runs it with few rows (*normed = true), else left to the caller.
+int gemm_ln(vella_whisper* w, const WLin& L, const void* x, int rows, const WNorm* n, bool* normed, cudaStream_t s) {
+  *normed = false;
+  vella_qgemm_desc d;
+  QgemmPlan p;
+  int rc = plan(w, L, rows, VELLA_EPI_BIAS_RESIDUAL, &d, &p);
+  if (rc) return rc;
+  if (n && w->fuse && p.stream && rows <= kLnTailRows) {
+    NormEpi ne;
+    ne.out = w->dn; ne.w = n->w; ne.b = n->b; ne.eps = w->cfg.eps;
+    *normed = true;
+    return gemm(w, L, x, rows, w->dh, VELLA_EPI_BIAS_RESIDUAL, w->dh, s, nullptr, &ne);
+  }
+  return gemm(w, L, x, rows, w->dh, VELLA_EPI_BIAS_RESIDUAL, w->dh, s);
+}
+
 template <typename Tin>
 int im2col(vella_whisper* w, void* out, const Tin* x, int C, int stride, int T_in, long long ts, long long cs, int Kp,
            int rows, cudaStream_t s) {
@@ -455,21 +456,25 @@ int im2col(vella_whisper* w, void* out, const Tin* x, int C, int stride, int T_i
                        stride, T_in, ts, cs, Kp);
 }
 
+// The token embedding into w->dh, and with ln set its LayerNorm into w->dn.
 template <typename T>
-int embed_t(vella_whisper* w, PosRef pr, int rows, cudaStream_t s) {
+int embed_t(vella_whisper* w, PosRef pr, int rows, const WNorm* ln, cudaStream_t s) {
   const vella_whisper_cfg& c = w->cfg;
   auto* h = static_cast<T*>(w->dh);
+  T* lo = ln ? static_cast<T*>(w->dn) : nullptr;
+  const T* lw = ln ? static_cast<const T*>(ln->w) : nullptr;
+  const T* lb = ln ? static_cast<const T*>(ln->b) : nullptr;
   const auto* es = static_cast<const T*>(w->embed.q.s);
   const auto* eb = static_cast<const T*>(w->embed.q.b);
   const auto* pos = static_cast<const T*>(w->dec_pos);
   if (c.bits == 4)
     return launch_kernel(wembed_kernel<T, 4>, dim3(rows), dim3(256), 0, s, h, (const void*)w->embed.q.w, es, eb, pos,
-                         (const int*)w->tok, pr, c.d_model, c.vocab, c.max_target, w->err);
+                         (const int*)w->tok, pr, c.d_model, c.vocab, c.max_target, w->err, lo, lw, lb, c.eps);
   if (c.bits == 8)
     return launch_kernel(wembed_kernel<T, 8>, dim3(rows), dim3(256), 0, s, h, (const void*)w->embed.q.w, es, eb, pos,
-                         (const int*)w->tok, pr, c.d_model, c.vocab, c.max_target, w->err);
+                         (const int*)w->tok, pr, c.d_model, c.vocab, c.max_target, w->err, lo, lw, lb, c.eps);
   return launch_kernel(wembed_kernel<T, 0>, dim3(rows), dim3(256), 0, s, h, (const void*)w->embed.q.w, es, eb, pos,
-                       (const int*)w->tok, pr, c.d_model, c.vocab, c.max_target, w->err);
+                       (const int*)w->tok, pr, c.d_model, c.vocab, c.max_target, w->err, lo, lw, lb, c.eps);
 }
 
 // Elements of one stream's self-attention cache and of its cross-attention K/V.
@@ -513,12 +518,27 @@ int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, int 
   const float scale = 1.0f / std::sqrt((float)hd);
   const bool bf = dt == VELLA_BF16;
   int rc;
-  if ((rc = bf ? embed_t<__nv_bfloat16>(w, pr, rows, s) : embed_t<__half>(w, pr, rows, s))) return rc;
+  // normed: w->dn already holds the LayerNorm that comes next, of the current w->dh
+  bool normed = w->fuse && c.dec_layers > 0;
+  const WNorm* ln0 = normed ? &w->dec[0].ln1 : nullptr;
+  if ((rc = bf ? embed_t<__nv_bfloat16>(w, pr, rows, ln0, s) : embed_t<__half>(w, pr, rows, ln0, s))) return rc;
   for (int l = 0; l < c.dec_layers; ++l) {
     const WDec& L = w->dec[l];
-    if ((rc = layernorm(w, w->dn, w->dh, L.ln1, rows, s))) return rc;
-    if ((rc = gemm(w, L.qkv, w->dn, rows, w->dqkv, VELLA_EPI_BIAS, nullptr, s))) return rc;
-    if ((rc = bf ? append_t<__nv_bfloat16>(w, l, pr, rows, s) : append_t<__half>(w, l, pr, rows, s))) return rc;
+    if (!normed && (rc = layernorm(w, w->dn, w->dh, L.ln1, rows, s))) return rc;
+    {
+      vella_qgemm_desc qd;
+      QgemmPlan qp;
+      if ((rc = plan(w, L.qkv, rows, VELLA_EPI_BIAS, &qd, &qp))) return rc;
+      if (w->fuse && qp.stream) {
+        KvAppendEpi ka;
+        ka.kc = kcache(w, l); ka.vc = vcache(w, l); ka.pr = pr;
+        ka.d = d; ka.hd = hd; ka.S = c.max_target; ka.kv_ss = kv_stream_elems(c);
+        if ((rc = gemm(w, L.qkv, w->dn, rows, w->dqkv, VELLA_EPI_BIAS, nullptr, s, &ka))) return rc;
+      } else {
+        if ((rc = gemm(w, L.qkv, w->dn, rows, w->dqkv, VELLA_EPI_BIAS, nullptr, s))) return rc;
+        if ((rc = bf ? append_t<__nv_bfloat16>(w, l, pr, rows, s) : append_t<__half>(w, l, pr, rows, s))) return rc;
+      }
+    }
     AttnView sv;
     sv.q = w->dqkv; sv.q_rs = 3LL * d;
     sv.k = kcache(w, l); sv.v = vcache(w, l);
@@ -526,8 +546,8 @@ int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, int 
     sv.out = w->datt; sv.o_rs = d;
     sv.q_bs = (long long)rps * 3 * d; sv.o_bs = (long long)rps * d; sv.kv_bs = kv_stream_elems(c);
     if ((rc = launch_attention_ex(dt, sv, streams, pr, 1, rps, H, H, hd, c.max_target, scale, s))) return rc;
-    if ((rc = gemm(w, L.o, w->datt, rows, w->dh, VELLA_EPI_BIAS_RESIDUAL, w->dh, s))) return rc;
-    if ((rc = layernorm(w, w->dn, w->dh, L.ln2, rows, s))) return rc;
+    if ((rc = gemm_ln(w, L.o, w->datt, rows, &L.ln2, &normed, s))) return rc;
+    if (!normed && (rc = layernorm(w, w->dn, w->dh, L.ln2, rows, s))) return rc;
     if ((rc = gemm(w, L.cq, w->dn, rows, w->dq2, VELLA_EPI_BIAS, nullptr, s))) return rc;
     AttnView cv;
     char* xk = static_cast<char*>(w->xkv) + (size_t)l * c.n_audio * 2 * d * w->elt;
@@ -538,12 +558,13 @@ int decoder_forward(vella_whisper* w, PosRef pr, int rows, int logits_rows, int 
     cv.q_bs = (long long)rps * d; cv.o_bs = (long long)rps * d; cv.kv_bs = xkv_stream_elems(c);
     if ((rc = launch_attention_ex(dt, cv, streams, PosRef{w->dzero, 0}, 0, rps, H, H, hd, c.n_audio, scale, s)))
       return rc;
-    if ((rc = gemm(w, L.co, w->datt, rows, w->dh, VELLA_EPI_BIAS_RESIDUAL, w->dh, s))) return rc;
-    if ((rc = layernorm(w, w->dn, w->dh, L.ln3, rows, s))) return rc;
+    if ((rc = gemm_ln(w, L.co, w->datt, rows, &L.ln3, &normed, s))) return rc;
+    if (!normed && (rc = layernorm(w, w->dn, w->dh, L.ln3, rows, s))) return rc;
     if ((rc = gemm(w, L.fc1, w->dn, rows, w->df, VELLA_EPI_BIAS_GELU, nullptr, s))) return rc;
-    if ((rc = gemm(w, L.fc2, w->df, rows, w->dh, VELLA_EPI_BIAS_RESIDUAL, w->dh, s))) return rc;
+    const WNorm& next = l + 1 < c.dec_layers ? w->dec[l + 1].ln1 : w->dec_ln;
+    if ((rc = gemm_ln(w, L.fc2, w->df, rows, &next, &normed, s))) return rc;
   }
-  if ((rc = layernorm(w, w->dn, w->dh, w->dec_ln, rows, s))) return rc;
+  if (!normed && (rc = layernorm(w, w->dn, w->dh, w->dec_ln, rows, s))) return rc;
   if (logits_rows > 0) {
     const char* xr = static_cast<const char*>(w->dn) + (size_t)(rows - logits_rows) * d * w->elt;
     if ((rc = gemm(w, w->embed, xr, logits_rows, w->logits, VELLA_EPI_NONE, nullptr, s))) return rc;
@@ -764,6 +785,7 @@ int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whi
   auto* w = new vella_whisper();
   w->cfg = c;
   w->device = device;
+  if (const char* f = std::getenv("VELLA_WHISPER_FUSE")) w->fuse = std::strcmp(f, "0") != 0;
   w->S = c.streams > 0 ? c.streams : 1;
   w->R = w->S * kWRows;
   w->elt = 2;
@@ -993,6 +1015,7 @@ int vella_whisper_tensor(vella_whisper* w, const char* name, int32_t layer, void
   if (n == "dec_pos") return ret(w->dec_pos, (size_t)c.max_target * c.d_model * e);
   if (n == "enc_out") return ret(w->enc_out, (size_t)c.n_audio * c.d_model * e);
   if (n == "xkv") return ret(w->xkv, (size_t)w->S * xkv_stream_elems(c) * e);
+  if (n == "kv") return ret(w->kv, (size_t)w->S * kv_stream_elems(c) * e);
   if (head == "conv1") return lin(w->conv1, part);
   if (head == "conv2") return lin(w->conv2, part);
   if (head == "embed") return lin(w->embed, part);
