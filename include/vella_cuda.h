@@ -103,9 +103,10 @@ VELLA_API size_t vella_qgemm_workspace_size(const vella_qgemm_desc* desc);
  * call must not be inside CUDA graph capture; a grown workspace keeps the old buffer
  * alive, so graphs captured earlier stay valid, but they all share one buffer and must
  * not run concurrently.
- * The reduction order of a row depends only on (N, K, bits) and on which side of 16 rows the
- * call falls: a row of a call of M <= 16 rows is bit-identical to the same row computed alone,
- * and a row of a call above 16 rows to the same row in any other call above 16 rows.
+ * The reduction order of a row depends only on (N, K, bits) and on the call's row class
+ * (1-16, 17-256, above 256 rows): a row of a call of M <= 16 rows is bit-identical to the same
+ * row computed alone, and a row of a call of 17-256 rows (above 256) to the same row in any
+ * other call of 17-256 rows (above 256).
  */
 VELLA_API int vella_qgemm(const vella_qgemm_desc* desc, const void* x, const void* w, const void* scales,
                 const void* biases, const void* up_w, const void* up_scales, const void* up_biases,

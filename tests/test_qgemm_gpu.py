@@ -214,6 +214,37 @@ def test_tensor_core_every_class(bits, dtype, epi):
         assert_close(run_case(case, m, n, k, bits, dtype, epi), case["out"], dtype)
 
 
+@pytest.mark.parametrize("bits", [0, 4, 8])
+@pytest.mark.parametrize("epi", ["none", "biasResidual", "siluGate", "biasGeluResidual"])
+def test_tensor_core_k_splits(bits, epi):
+    """Calls of at most 256 rows with few row tiles split K over CTAs (N 256, K 4096: 4 splits;
+    N 200, K 2560: 2 uneven splits; N 136, K 3072: 3): each split's fp32 sums go through the
+    workspace and the tile's last split adds them in split order, then runs the epilogue.
+    Against the oracle, one and two token tiles, and above 256 rows (one split)."""
+    for m, n, k in [(40, 256, 4096), (130, 200, 2560), (250, 136, 3072), (300, 136, 3072)]:
+        case = make(m, n, k, bits, "bf16", epi, seed=m * 3 + bits)
+        assert_close(run_case(case, m, n, k, bits, "bf16", epi), case["out"], "bf16")
+
+
+def test_tensor_core_k_split_rows_invariant():
+    """The split count depends on (N, K) and the row class only: a row's value is the same at
+    every M of 17-256 rows, and at every M above 256."""
+    S = smallm()
+    n, k = 256, 4096
+    p, sc, bi = A.quantize((np.random.default_rng(6).standard_normal((n, k)) * 0.02).astype(np.float32), 4)
+    w = S.Weights(dev(p), dev(sc), dev(bi), 4)
+    x = A.to_storage(np.random.default_rng(7).standard_normal((300, k)).astype(np.float32), "bf16")
+    out = S.matmul(dev(x), w)
+    other = S.matmul(dev(x)[120:160], w)
+    third = S.matmul(dev(x)[20:220], w)
+    big = S.matmul(dev(x)[0:280], w)
+    torch.cuda.synchronize()
+    assert_close(host(out), A.qgemm(x, p, sc, bi, bits=4), "bf16")
+    assert_close(host(third), A.qgemm(x[20:220], p, sc, bi, bits=4), "bf16")
+    assert torch.equal(third[117].view(torch.int16), other[17].view(torch.int16))
+    assert torch.equal(out[137].view(torch.int16), big[137].view(torch.int16))
+
+
 def test_tensor_core_config2_shape_sampled():
     """A prefill-sized call (M 256, N 25600, K 5120, int4) against sampled oracle rows."""
     S = smallm()

@@ -110,11 +110,20 @@ int stream_launch(const vella_qgemm_desc& d, int P, bool light, const void* x, c
 int stream_fault_status(int clear);
 int fwd_fault_status(int clear);  // fwd_prog.cu: the persistent decode forward's flags
 
+// Bytes of a workspace's counter region (at least the fixed 128 KiB at its front) for
+// `counters` ints; scratch follows it (qgemm.cu).
+size_t counter_region(size_t counters);
+
 // tc_gemm.cu
 bool tc_eligible(const vella_qgemm_desc& d);
-int tc_launch(const vella_qgemm_desc& d, const void* x, const void* w, const void* scales, const void* biases,
-              const void* up_w, const void* up_scales, const void* up_biases, const void* bias,
-              const void* residual, void* out, cudaStream_t stream);
+// K splits of a tensor-core call (a function of N, K and the call's row class only, so that a
+// row's value does not depend on M within the class) and the workspace they need (zero for
+// one split).
+int tc_splits(const vella_qgemm_desc& d);
+size_t tc_workspace(const vella_qgemm_desc& d, int splits);
+int tc_launch(const vella_qgemm_desc& d, int splits, const void* x, const void* w, const void* scales,
+              const void* biases, const void* up_w, const void* up_scales, const void* up_biases, const void* bias,
+              const void* residual, void* out, void* ws, cudaStream_t stream);
 int tc_fault_status(int clear);
 
 bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* plan);

@@ -224,10 +224,17 @@ void rebase_q(QWeight& q, char* base, bool quant) {
   }
 }
 
-size_t gemm_ws_for(const QWeight& w, int bits, int dtype, int epi) {
-  vella_qgemm_desc d{kMaxRows, w.n, w.k, bits, 64, dtype, epi};
-  QgemmPlan p;
-  return qgemm_plan(d, &p) ? p.workspace : 0;
+// Workspace of a GEMM at the streaming kernel's largest call (16 rows), at the largest
+// tensor-core call that splits K (at most 256 rows; the splits keep fp32 sums for every row)
+// and at the model's largest call.
+size_t gemm_ws_for(const QWeight& w, int bits, int dtype, int epi, int rows) {
+  size_t ws = 0;
+  for (int m : {kMaxRows, std::min(rows, 256), rows}) {
+    vella_qgemm_desc d{m, w.n, w.k, bits, 64, dtype, epi};
+    QgemmPlan p;
+    if (qgemm_plan(d, &p)) ws = std::max(ws, p.workspace);
+  }
+  return ws;
 }
 
 }  // namespace
@@ -312,13 +319,14 @@ int model_create(const vella_model_cfg& c, int device, Model** out) {
   // ---- activations and scratch ------------------------------------------------------------
   size_t ws = 0;
   for (const Layer& L : m->layers) {
-    ws = std::max(ws, gemm_ws_for(L.qkv, bits, c.dtype, VELLA_EPI_NONE));
-    ws = std::max(ws, gemm_ws_for(L.o, bits, c.dtype, VELLA_EPI_RESIDUAL));
-    ws = std::max(ws, gemm_ws_for(L.gate, bits, c.dtype, VELLA_EPI_SILU_GATE));
-    ws = std::max(ws, gemm_ws_for(L.down, bits, c.dtype, VELLA_EPI_RESIDUAL));
+    const int R = m->max_rows;
+    ws = std::max(ws, gemm_ws_for(L.qkv, bits, c.dtype, VELLA_EPI_NONE, R));
+    ws = std::max(ws, gemm_ws_for(L.o, bits, c.dtype, VELLA_EPI_RESIDUAL, R));
+    ws = std::max(ws, gemm_ws_for(L.gate, bits, c.dtype, VELLA_EPI_SILU_GATE, R));
+    ws = std::max(ws, gemm_ws_for(L.down, bits, c.dtype, VELLA_EPI_RESIDUAL, R));
     break;  // every layer has the same shapes
   }
-  ws = std::max(ws, gemm_ws_for(m->lm_head, bits, c.dtype, VELLA_EPI_NONE));
+  ws = std::max(ws, gemm_ws_for(m->lm_head, bits, c.dtype, VELLA_EPI_NONE, m->max_rows));
   m->gemm_ws_bytes = ws;
   const size_t R = m->max_rows, RL = (size_t)m->streams * m->rps;
   const size_t sizes[] = {

@@ -129,9 +129,15 @@ int nh_gemm(vella_nh* m, const NhLin& l, const void* x, int rows, void* out, boo
                      m->gemm_ws, m->gemm_ws_bytes, m->stream);
 }
 
+// At the streaming kernel's largest call, at the largest tensor-core call that splits K (at
+// most 256 rows; the splits keep fp32 sums for every row) and at the largest call.
 size_t gemm_ws_for(const vella_nh* m, int n, int k) {
-  vella_qgemm_desc d{m->cfg.max_rows, n, k, m->cfg.bits, 64, m->cfg.dtype, VELLA_EPI_RESIDUAL};
-  return vella_qgemm_workspace_size(&d);
+  size_t ws = 0;
+  for (int rows : {std::min(16, m->cfg.max_rows), std::min(256, m->cfg.max_rows), m->cfg.max_rows}) {
+    vella_qgemm_desc d{rows, n, k, m->cfg.bits, 64, m->cfg.dtype, VELLA_EPI_RESIDUAL};
+    ws = std::max(ws, vella_qgemm_workspace_size(&d));
+  }
+  return ws;
 }
 
 vella_mamba_desc mamba_desc(const vella_nh* m, int rows) {

@@ -38,14 +38,7 @@
 #include "internal.h"
 
 namespace vella {
-namespace {
 
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
-constexpr int kSlots = 128;  // weight rows per CTA (gate: 64 gate + 64 up)
-constexpr int kKCMax = 32;
-constexpr int kTokMax = 16;  // tokens per pass (z chunk)
-constexpr int kAccStride = kSlots + 4;
 // The ticket counters sit at the front of the workspace in a region of this fixed size
 // (32768 counters), and the fp32 partials after it, so that calls of different shapes can
 // share one workspace: no shape's partials ever overwrite another shape's counters.
@@ -55,6 +48,15 @@ size_t counter_region(size_t counters) {
   const size_t bytes = (counters * sizeof(int) + 255) / 256 * 256;
   return bytes > kCounterRegion ? bytes : kCounterRegion;
 }
+
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kSlots = 128;  // weight rows per CTA (gate: 64 gate + 64 up)
+constexpr int kKCMax = 32;
+constexpr int kTokMax = 16;  // tokens per pass (z chunk)
+constexpr int kAccStride = kSlots + 4;
 
 struct Args {
   const void* x;
@@ -430,9 +432,10 @@ bool qgemm_plan(const vella_qgemm_desc& d, QgemmPlan* p) {
   if (!epi_valid(d.epilogue)) return false;
   p->stream = false;
   p->tc = false;
-  if (tc_eligible(d) && d.m <= (1 << 24)) {  // more than 16 rows: tensor cores, no workspace
+  if (tc_eligible(d) && d.m <= (1 << 24)) {  // more than 16 rows: tensor cores
     p->tc = true;
-    p->workspace = 0;
+    p->splits = tc_splits(d);
+    p->workspace = tc_workspace(d, p->splits);
     return true;
   }
   if (d.m > 256) return false;
@@ -487,7 +490,8 @@ int qgemm_launch(const vella_qgemm_desc& d, const QgemmPlan& p, const void* x, c
   if (d.m == 0 || d.n == 0) return VELLA_OK;
   if ((rope || app || norm) && !p.stream)
     return fail(VELLA_E_INVALID, "qgemm: the RoPE, K/V-append and LayerNorm epilogues run on the streaming kernel only");
-  if (p.tc) return tc_launch(d, x, w, scales, biases, up_w, up_scales, up_biases, bias, residual, out, stream);
+  if (p.tc)
+    return tc_launch(d, p.splits, x, w, scales, biases, up_w, up_scales, up_biases, bias, residual, out, ws, stream);
   if (p.stream) {
     int* flags = static_cast<int*>(ws);
     float* partial = reinterpret_cast<float*>(static_cast<char*>(ws) + counter_region((size_t)stream_flag_count(p.ctas)));

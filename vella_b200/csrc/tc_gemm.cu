@@ -55,6 +55,14 @@ using namespace sm100;
 constexpr int kTcRows = 128;     // weight rows per CTA (MMA M)
 constexpr int kTcTok = 256;      // tokens per CTA (largest MMA N)
 constexpr int kTcK = 64;         // K elements per stage
+// K splits of a call of at most kTcSplitRows rows, from (N, K) only: as many as keep two
+// 128-token tiles within one wave of 148 CTAs, at least 16 stages per split, at most 4.  Calls
+// whose row tiles alone fill the GPU (the 30B target's projections) and calls of more rows
+// (their token tiles fill it) take one.
+constexpr int kTcSplitRows = 256;
+constexpr int kTcWave = 148;
+constexpr int kTcMaxSplits = 4;
+constexpr int kTcMinSplitStages = 16;
 // Transform/epilogue warps: 16, four threads per weight row (quantized: each dequantises a
 // quarter of the row's codes per stage -- with 8 the transform's latency left the tensor pipe
 // idle half the time; dense: no transform, the four share the epilogue).
@@ -91,6 +99,10 @@ struct TcArgs {
   void* out;               // [M, N]
   int M, N, K, G;
   int tt;                  // tokens per CTA: 128 or 256 (the x box height)
+  int S;                   // K splits (blockIdx.z); above 1 the fp32 sums go through `part`
+  int Mp;                  // rows of a split's slice of `part` (M rounded up to tt)
+  float* part;             // [S][NA][Mp][N] fp32 sums of each split
+  int* cnt;                // [token tiles x row tiles] splits done (the last resets it)
 };
 
 // CH chunks of 8 codes of one weight row (8: the stage's 64, 4: half of them) -> CH chunks
@@ -182,6 +194,10 @@ __global__ void __launch_bounds__(tc_threads<BITS>(), 1) tc_gemm_kernel(const __
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tok0 = blockIdx.x * a.tt, row0 = blockIdx.y * kTcRows;
   const int G = a.G;
+  // this split's stages [g0, g1): whole blocks of 8 groups (the scale/bias loads' unit)
+  const int z = blockIdx.z, nblk = (G + 7) / 8;
+  const int g0 = 8 * (z * nblk / a.S), g1 = min(G, 8 * ((z + 1) * nblk / a.S));
+  const int NG = g1 - g0;
   // MMA N: this tile's tokens rounded up to 16 (a row's sums do not depend on N)
   const int ntok = min(a.tt, (a.M - tok0 + 15) / 16 * 16);
   const uint32_t tx = (uint32_t)(a.tt * 128 + (BITS ? LY::NA * LY::RAW_BYTES : LY::NA * LY::A_BYTES));
@@ -215,36 +231,37 @@ __global__ void __launch_bounds__(tc_threads<BITS>(), 1) tc_gemm_kernel(const __
           if constexpr (GATE) tma2d(tileR(st, 1), &a.tu, g * WPG, row0, &full[st]);
         }
       };
-      const int npre = min(G, NS);
-      for (int g = 0; g < npre; ++g) {
-        mbar_expect_tx(&full[g], tx);
-        weights(g, g);
+      // stage l of this split holds group g0 + l in ring slot l % NS
+      const int npre = min(NG, NS);
+      for (int l = 0; l < npre; ++l) {
+        mbar_expect_tx(&full[l], tx);
+        weights(g0 + l, l);
       }
       pdl_wait();  // x is written by the previous kernel
-      for (int g = 0; g < npre; ++g) tma2d(tileB(g), &a.tx, g * kTcK, tok0, &full[g]);
+      for (int l = 0; l < npre; ++l) tma2d(tileB(l), &a.tx, (g0 + l) * kTcK, tok0, &full[l]);
       int issued = npre;
-      for (int g = npre; g < G; ++g) {
-        const int st = g % NS, use = g / NS;
+      for (int l = npre; l < NG; ++l) {
+        const int st = l % NS, use = l / NS;
         if (!mbar_wait(&empty[st], (uint32_t)((use - 1) & 1))) {
           atomicOr(&g_tc_fault, 1);
           break;
         }
         mbar_expect_tx(&full[st], tx);
-        weights(g, st);
-        tma2d(tileB(st), &a.tx, g * kTcK, tok0, &full[st]);
-        issued = g + 1;
+        weights(g0 + l, st);
+        tma2d(tileB(st), &a.tx, (g0 + l) * kTcK, tok0, &full[st]);
+        issued = l + 1;
       }
       // every copy issued must land before the CTA may exit
-      for (int g = max(0, issued - NS); g < issued; ++g)
-        if (!mbar_wait(&full[g % NS], (uint32_t)((g / NS) & 1))) atomicOr(&g_tc_fault, 2);
+      for (int l = max(0, issued - NS); l < issued; ++l)
+        if (!mbar_wait(&full[l % NS], (uint32_t)((l / NS) & 1))) atomicOr(&g_tc_fault, 2);
     }
   } else if (warp == 1) {
     // ---- MMA issuer ---------------------------------------------------------------------
     pdl_wait();
     if (lane == 0) {
-      for (int g = 0; g < G; ++g) {
-        const int st = g % NS;
-        const uint32_t par = (uint32_t)((g / NS) & 1);
+      for (int l = 0; l < NG; ++l) {
+        const int st = l % NS;
+        const uint32_t par = (uint32_t)((l / NS) & 1);
         if (!mbar_wait(BITS ? &ready[st] : &full[st], par)) {
           atomicOr(&g_tc_fault, 4);
           break;
@@ -254,7 +271,7 @@ __global__ void __launch_bounds__(tc_threads<BITS>(), 1) tc_gemm_kernel(const __
 #pragma unroll
         for (int kk = 0; kk < kTcK / 16; ++kk) {
           const uint64_t bd = kmajor_sw128_desc(b0 + kk * 32);
-          const uint32_t acc = (g > 0 || kk > 0) ? 1u : 0u;
+          const uint32_t acc = (l > 0 || kk > 0) ? 1u : 0u;
           mma_f16_ss(tmem, kmajor_sw128_desc(a0 + kk * 32), bd, idesc, acc);
           if constexpr (GATE) mma_f16_ss(tmem + kTcTok, kmajor_sw128_desc(saddr(tileA(st, 1)) + kk * 32), bd, idesc, acc);
         }
@@ -304,20 +321,20 @@ __global__ void __launch_bounds__(tc_threads<BITS>(), 1) tc_gemm_kernel(const __
         return *reinterpret_cast<const T*>(&h);
       };
       uint32_t sc[4], bc[4], sn[4], bn[4], usc[4], ubc[4], usn[4], ubn[4];
-      load_block(a.s, 0, sc);
-      load_block(a.b, 0, bc);
-      if constexpr (GATE) { load_block(a.us, 0, usc); load_block(a.ub, 0, ubc); }
+      load_block(a.s, g0, sc);
+      load_block(a.b, g0, bc);
+      if constexpr (GATE) { load_block(a.us, g0, usc); load_block(a.ub, g0, ubc); }
       bool ok = true;
-      for (int gb = 0; gb < G && ok; gb += 8) {
+      for (int gb = g0; gb < g1 && ok; gb += 8) {
         load_block(a.s, gb + 8, sn);
         load_block(a.b, gb + 8, bn);
         if constexpr (GATE) { load_block(a.us, gb + 8, usn); load_block(a.ub, gb + 8, ubn); }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int g = gb + j;
-          if (g >= G) break;
-          const int st = g % NS;
-          if (!mbar_wait(&full[st], (uint32_t)((g / NS) & 1))) {
+          if (g >= g1) break;
+          const int st = (g - g0) % NS;
+          if (!mbar_wait(&full[st], (uint32_t)(((g - g0) / NS) & 1))) {
             atomicOr(&g_tc_fault, 8);
             ok = false;
             break;
@@ -359,31 +376,104 @@ __global__ void __launch_bounds__(tc_threads<BITS>(), 1) tc_gemm_kernel(const __
     // ---- epilogue ------------------------------------------------------------------------
     const bool ok = mbar_wait(accf, 0);
     tc_fence_after();
-    if (!ok) {
-      atomicOr(&g_tc_fault, 16);
-    } else {
-      const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-      const T* bias = static_cast<const T*>(a.bias);
-      const T* res = static_cast<const T*>(a.res);
-      T* out = static_cast<T*>(a.out);
+    if (!ok) atomicOr(&g_tc_fault, 16);
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    const T* bias = static_cast<const T*>(a.bias);
+    const T* res = static_cast<const T*>(a.res);
+    T* out = static_cast<T*>(a.out);
+    // GATE -> bias -> GELU -> residual, one rounding
+    auto finish = [&](int m, int col, float y, float up, float bcol) {
+      if constexpr (GATE) y = y / (1.0f + expf(-y)) * up;
+      y += bcol;
+      if (a.gelu) y = gelu_erf(y);
+      if (res) y += A::to_f(res[(size_t)m * a.N + col]);
+      out[(size_t)m * a.N + col] = A::from_f(y);
+    };
+    if (a.S == 1) {
       const float bn = (bias && nv) ? A::to_f(bias[n]) : 0.0f;
-      for (int c0 = 32 * hf; c0 < ntok && tok0 + c0 < a.M; c0 += 32 * kTcParts) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_base + c0, v);
-        uint32_t u[32];
-        if constexpr (GATE) tmem_ld32(tmem + lane_base + kTcTok + c0, u);
-        if (nv) {
+      if (ok) {
+        for (int c0 = 32 * hf; c0 < ntok && tok0 + c0 < a.M; c0 += 32 * kTcParts) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_base + c0, v);
+          uint32_t u[32];
+          if constexpr (GATE) tmem_ld32(tmem + lane_base + kTcTok + c0, u);
+          if (nv) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int m = tok0 + c0 + j;
-            if (m < a.M) {
-              float y = __uint_as_float(v[j]);
-              if constexpr (GATE) y = y / (1.0f + expf(-y)) * __uint_as_float(u[j]);
-              y += bn;
-              if (a.gelu) y = gelu_erf(y);
-              if (res) y += A::to_f(res[(size_t)m * a.N + n]);
-              out[(size_t)m * a.N + n] = A::from_f(y);
+            for (int j = 0; j < 32; ++j) {
+              const int m = tok0 + c0 + j;
+              if (m < a.M) finish(m, n, __uint_as_float(v[j]), GATE ? __uint_as_float(u[j]) : 0.0f, bn);
             }
+          }
+        }
+      }
+    } else {
+      // K split: this split's fp32 sums go to `part`; the tile's last split to arrive adds the
+      // splits' sums in split order and runs the epilogue (no split waits for another)
+      const size_t plane = (size_t)a.Mp * a.N;
+      float* pz = a.part + (size_t)z * LY::NA * plane;
+      if (ok) {
+        for (int c0 = 32 * hf; c0 < ntok && tok0 + c0 < a.M; c0 += 32 * kTcParts) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_base + c0, v);
+          uint32_t u[32];
+          if constexpr (GATE) tmem_ld32(tmem + lane_base + kTcTok + c0, u);
+          if (nv) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int m = tok0 + c0 + j;
+              if (m < a.M) {
+                pz[(size_t)m * a.N + n] = __uint_as_float(v[j]);
+                if constexpr (GATE) pz[plane + (size_t)m * a.N + n] = __uint_as_float(u[j]);
+              }
+            }
+          }
+        }
+      }
+      __threadfence();
+      named_sync(1, 32 * kTcXW);
+      volatile uint32_t* s_last = tslot + 1;
+      if (tid == 64) {
+        int* cp = a.cnt + blockIdx.y * gridDim.x + blockIdx.x;
+        const bool last = atomicAdd(cp, 1) == a.S - 1;
+        if (last) {
+          __threadfence();
+          *cp = 0;  // every split has arrived: zero for the next call
+        }
+        *s_last = last ? 1u : 0u;
+      }
+      named_sync(1, 32 * kTcXW);
+      if (*s_last) {
+        // the whole tile over the epilogue warps, a weight row per lane (coalesced along N);
+        // RB elements a thread at a time, their loads all in flight before any is added
+        constexpr int RB = 8;
+        const int et = tid - 64, rows = min(a.tt, a.M - tok0), total = rows * kTcRows;
+        for (int e0 = et; e0 < total; e0 += RB * 32 * kTcXW) {
+          float pv[RB][kTcMaxSplits], pu[RB][kTcMaxSplits];
+#pragma unroll
+          for (int r = 0; r < RB; ++r) {
+            const int e = e0 + r * 32 * kTcXW;
+            const int m = tok0 + (e >> 7), col = row0 + (e & (kTcRows - 1));
+            const bool in = e < total && col < a.N;
+            const size_t o = in ? (size_t)m * a.N + col : 0;
+#pragma unroll
+            for (int q = 0; q < kTcMaxSplits; ++q) {
+              pv[r][q] = in && q < a.S ? __ldcg(a.part + (size_t)q * LY::NA * plane + o) : 0.0f;
+              pu[r][q] = GATE && in && q < a.S ? __ldcg(a.part + ((size_t)q * LY::NA + 1) * plane + o) : 0.0f;
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < RB; ++r) {
+            const int e = e0 + r * 32 * kTcXW;
+            const int m = tok0 + (e >> 7), col = row0 + (e & (kTcRows - 1));
+            if (e >= total || col >= a.N) continue;
+            float y = pv[r][0], up = pu[r][0];
+#pragma unroll
+            for (int q = 1; q < kTcMaxSplits; ++q)
+              if (q < a.S) {
+                y += pv[r][q];
+                up += pu[r][q];
+              }
+            finish(m, col, y, up, bias ? A::to_f(bias[col]) : 0.0f);
           }
         }
       }
@@ -406,7 +496,7 @@ int launch_tc_t(const TcArgs& a, cudaStream_t stream) {
     VELLA_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::TOTAL));
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
-  const dim3 grid((a.M + a.tt - 1) / a.tt, (a.N + kTcRows - 1) / kTcRows);
+  const dim3 grid((a.M + a.tt - 1) / a.tt, (a.N + kTcRows - 1) / kTcRows, a.S);
   return launch_kernel(k, grid, dim3(tc_threads<BITS>()), LY::TOTAL, stream, a);
 }
 
@@ -424,9 +514,27 @@ bool tc_eligible(const vella_qgemm_desc& d) {
          (d.dtype == VELLA_BF16 || d.dtype == VELLA_F16);
 }
 
-int tc_launch(const vella_qgemm_desc& d, const void* x, const void* w, const void* scales, const void* biases,
-              const void* up_w, const void* up_scales, const void* up_biases, const void* bias,
-              const void* residual, void* out, cudaStream_t stream) {
+int tc_splits(const vella_qgemm_desc& d) {
+  if (d.m > kTcSplitRows) return 1;
+  const int rtiles = (d.n + kTcRows - 1) / kTcRows;
+  const int by_wave = kTcWave / (2 * rtiles);
+  const int by_stages = d.k / kTcK / kTcMinSplitStages;
+  return std::max(1, std::min(std::min(by_wave, by_stages), kTcMaxSplits));
+}
+
+// Counters for every (token tile, row tile) at 128-token tiles, then [S][NA][Mp][N] fp32 with Mp
+// the rows rounded up to 256 (either tile height fits).
+size_t tc_workspace(const vella_qgemm_desc& d, int splits) {
+  if (splits <= 1) return 0;
+  const size_t rtiles = (d.n + kTcRows - 1) / kTcRows, ttiles = (d.m + kTcTok / 2 - 1) / (kTcTok / 2);
+  const size_t mp = (size_t)(d.m + kTcTok - 1) / kTcTok * kTcTok;
+  const size_t na = d.epilogue == VELLA_EPI_SILU_GATE ? 2 : 1;
+  return counter_region(rtiles * ttiles) + (size_t)splits * na * mp * d.n * sizeof(float);
+}
+
+int tc_launch(const vella_qgemm_desc& d, int splits, const void* x, const void* w, const void* scales,
+              const void* biases, const void* up_w, const void* up_scales, const void* up_biases, const void* bias,
+              const void* residual, void* out, void* ws, cudaStream_t stream) {
   const bool gate = d.epilogue == VELLA_EPI_SILU_GATE;
   TcArgs a{};
   a.s = scales; a.b = biases; a.us = up_scales; a.ub = up_biases;
@@ -444,6 +552,14 @@ int tc_launch(const vella_qgemm_desc& d, const void* x, const void* w, const voi
   }
   const long long rtiles = (d.n + kTcRows - 1) / kTcRows;
   a.tt = ((long long)(d.m + kTcTok - 1) / kTcTok) * rtiles >= num_sms(dev) ? kTcTok : kTcTok / 2;
+  a.S = std::max(1, splits);
+  if (a.S > 1) {
+    if (!ws) return fail(VELLA_E_INVALID, "tensor-core GEMM: %d K splits need a workspace", a.S);
+    const size_t ttiles = (d.m + kTcTok / 2 - 1) / (kTcTok / 2);
+    a.cnt = static_cast<int*>(ws);
+    a.part = reinterpret_cast<float*>(static_cast<char*>(ws) + counter_region((size_t)rtiles * ttiles));
+    a.Mp = (d.m + a.tt - 1) / a.tt * a.tt;
+  }
   int rc;
   const uint64_t xrow = (uint64_t)d.k * 2;
   if ((rc = make_tensor_map(&a.tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, x, d.k, d.m, xrow, kTcK, a.tt,

@@ -21,6 +21,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <initializer_list>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -686,10 +687,17 @@ int commit(vella_whisper* w, int ys_stride, int ys_off, cudaStream_t s) {
                        w->cfg.max_target, w->err, w->S, ys_stride, ys_off);
 }
 
-size_t ws_for(const WLin& L, int dtype, int epi) {
-  vella_qgemm_desc d{kWRows, L.q.n, L.q.k, L.bits, 64, dtype, epi};
-  QgemmPlan p;
-  return qgemm_plan(d, &p) ? p.workspace : 0;
+// Workspace of a GEMM at each row count it runs at, and at 256 rows below those above it
+// (the largest tensor-core call that splits K; the splits keep fp32 sums for every row).
+size_t ws_for(const WLin& L, int dtype, int epi, std::initializer_list<int> rows) {
+  size_t ws = 0;
+  for (int r : rows)
+    for (int m : {r, std::min(r, 256)}) {
+      vella_qgemm_desc d{m, L.q.n, L.q.k, L.bits, 64, dtype, epi};
+      QgemmPlan p;
+      if (m > 0 && qgemm_plan(d, &p)) ws = std::max(ws, p.workspace);
+    }
+  return ws;
 }
 
 int run_step(vella_whisper* w) {
@@ -826,13 +834,25 @@ int vella_whisper_create(const vella_whisper_cfg* cfg, int32_t device, vella_whi
 
   // activations
   size_t ws = 0;
+  const int Rd = w->R;  // decoder rows of a forward over every stream
   for (const WDec& L : w->dec) {
-    for (const WLin* l : {&L.qkv, &L.cq, &L.ckv}) ws = std::max(ws, ws_for(*l, c.dtype, VELLA_EPI_BIAS));
-    for (const WLin* l : {&L.o, &L.co, &L.fc2}) ws = std::max(ws, ws_for(*l, c.dtype, VELLA_EPI_BIAS_RESIDUAL));
-    ws = std::max(ws, ws_for(L.fc1, c.dtype, VELLA_EPI_BIAS_GELU));
+    for (const WLin* l : {&L.qkv, &L.cq}) ws = std::max(ws, ws_for(*l, c.dtype, VELLA_EPI_BIAS, {kWRows, Rd}));
+    ws = std::max(ws, ws_for(L.ckv, c.dtype, VELLA_EPI_BIAS, {A}));
+    for (const WLin* l : {&L.o, &L.co, &L.fc2})
+      ws = std::max(ws, ws_for(*l, c.dtype, VELLA_EPI_BIAS_RESIDUAL, {kWRows, Rd}));
+    ws = std::max(ws, ws_for(L.fc1, c.dtype, VELLA_EPI_BIAS_GELU, {kWRows, Rd}));
     break;
   }
-  ws = std::max(ws, ws_for(w->embed, c.dtype, VELLA_EPI_NONE));
+  ws = std::max(ws, ws_for(w->embed, c.dtype, VELLA_EPI_NONE, {kWRows, Rd}));
+  for (const WEnc& L : w->enc) {
+    ws = std::max(ws, ws_for(L.qkv, c.dtype, VELLA_EPI_BIAS, {A}));
+    ws = std::max(ws, ws_for(L.o, c.dtype, VELLA_EPI_BIAS_RESIDUAL, {A}));
+    ws = std::max(ws, ws_for(L.fc2, c.dtype, VELLA_EPI_BIAS_RESIDUAL, {A}));
+    ws = std::max(ws, ws_for(L.fc1, c.dtype, VELLA_EPI_BIAS_GELU, {A}));
+    break;
+  }
+  ws = std::max(ws, ws_for(w->conv1, c.dtype, VELLA_EPI_BIAS_GELU, {2 * A}));
+  ws = std::max(ws, ws_for(w->conv2, c.dtype, VELLA_EPI_BIAS_GELU_RESIDUAL, {A}));
   w->gemm_ws_bytes = ws;
   const size_t R = (size_t)w->R, S = (size_t)w->S;
   Planner Q;
