@@ -335,10 +335,25 @@ __device__ float2 cl_softmax_stats(ClSweep& c, const T* slice, float invT, SampS
   return make_float2(m, z);
 }
 
+// Copies n elements from src to dst with 16-byte accesses when both are 16-byte aligned (the
+// whole block, coalesced), element by element otherwise.
+template <typename T>
+__device__ __forceinline__ void block_copy(T* dst, const T* src, int n) {
+  constexpr int E = 16 / sizeof(T);
+  if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0) {
+    const int nv = n / E;
+    for (int i = threadIdx.x; i < nv; i += blockDim.x)
+      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+    for (int i = nv * E + threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+  }
+}
+
 // The CTA's part of a row into shared memory (coalesced loads); the caller syncs.
 template <typename T>
 __device__ __forceinline__ void stage_slice(const ClSweep& c, const T* row, T* slice) {
-  for (int v = c.lo + threadIdx.x; v < c.hi; v += blockDim.x) slice[v - c.lo] = row[v];
+  block_copy(slice, row + c.lo, c.hi - c.lo);
 }
 // Dynamic shared memory of the cluster kernels: one CTA's slice of a vocabulary row.
 inline size_t cl_slice_bytes(int V, size_t elt) { return (size_t)((V + kTreeCluster - 1) / kTreeCluster) * elt; }
@@ -402,6 +417,68 @@ __device__ int cl_icdf(ClSweep& c, W w, float u, SampShared& sh) {
   }
   c.g.sync();
   return *c.g.map_shared_rank(c.xidx, seg);
+}
+
+// nd draws from the same unnormalised weights with the uniforms u[0..nd) (nd <= 16): the
+// per-thread sums, the block scan and the CTA totals are formed once, then each draw finds its
+// index exactly as cl_icdf does (the same values in the same order), the finds of all draws
+// behind one cluster barrier.  out[d] is -1 when every weight is zero; xidx: nd ints of this
+// CTA's shared memory.
+template <typename W>
+__device__ void cl_icdf_many(ClSweep& c, W w, const float* u, int nd, int* xidx, int* out, SampShared& sh) {
+  const int n = c.hi - c.lo;
+  const int C = (n + (int)blockDim.x - 1) / (int)blockDim.x;
+  const int lo = c.lo + min(n, (int)threadIdx.x * C), hi = min(c.hi, lo + C);
+  float ps = 0.0f;
+  for (int v = lo; v < hi; ++v) ps += w(v);
+  float cta_total;
+  const float incl = block_incl_scan(ps, sh, &cta_total);
+  const int slot = c.k++ & 1;
+  if (threadIdx.x == 0) c.xch[slot] = cta_total;
+  c.g.sync();
+  float tots[kTreeCluster];
+  float total = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kTreeCluster; ++i) {
+    tots[i] = *c.g.map_shared_rank(c.xch + slot, i);
+    total += tots[i];
+  }
+  int segs[16];
+  for (int d = 0; d < nd; ++d) {
+    const float target = u[d] * total;
+    float acc = 0.0f, before = -1.0f;
+    int seg = -1, last = -1;
+#pragma unroll
+    for (int i = 0; i < kTreeCluster; ++i) {
+      if (tots[i] > 0.0f) last = i;
+      if (seg < 0 && acc + tots[i] > target) {
+        seg = i;
+        before = acc;
+      }
+      acc += tots[i];
+    }
+    if (seg < 0) seg = last;  // rounding at the top end (before -1: the last weight of that CTA)
+    segs[d] = seg;
+    if (seg >= 0 && c.rank == seg) {
+      const bool hit = before >= 0.0f && before + incl > target;
+      const int2 mm = block_minmax(hit ? (int)threadIdx.x : 0x7fffffff, ps > 0.0f ? (int)threadIdx.x : -1, sh);
+      const bool found_seg = mm.x != 0x7fffffff;
+      const int tseg = found_seg ? mm.x : mm.y;
+      if ((int)threadIdx.x == tseg) {
+        float a = found_seg ? before + incl - ps : -1.0f;
+        int found = -1, lastv = -1;
+        for (int v = lo; v < hi; ++v) {
+          const float x = w(v);
+          if (x > 0.0f) lastv = v;
+          if (found < 0 && a >= 0.0f && a + x > target) found = v;
+          a += x;
+        }
+        xidx[d] = found >= 0 ? found : lastv;
+      }
+    }
+  }
+  c.g.sync();
+  for (int d = 0; d < nd; ++d) out[d] = segs[d] < 0 ? -1 : *c.g.map_shared_rank(xidx + d, segs[d]);
 }
 
 // Draft step i, stream blockIdx.x: x ~ softmax(draft logits / T) for position L + i; the
@@ -721,14 +798,15 @@ __global__ void __cluster_dims__(kTreeCluster, 1, 1) __launch_bounds__(kSampThre
   __syncthreads();
   const float invT = 1.0f / c.temperature;
   const float2 mz = cl_softmax_stats(cl, slice, invT, sh);
-  for (int i = 0; i < nc; ++i) {
-    const float u = uni(c, (uint32_t)x.pass, (uint32_t)(fc + i), kPurposeDraft, s);
-    const int t =
-        cl_icdf(cl, [&](int v) { return expf((Act<T>::to_f(slice[v - cl.lo]) - mz.x) * invT); }, u, sh);
-    if (first && threadIdx.x == 0) ttok[(size_t)s * N + fc + i] = t < 0 ? 0 : t;
-  }
+  float us[16];
+  int drawn[16];
+  for (int i = 0; i < nc; ++i) us[i] = uni(c, (uint32_t)x.pass, (uint32_t)(fc + i), kPurposeDraft, s);
+  cl_icdf_many(cl, [&](int v) { return expf((Act<T>::to_f(slice[v - cl.lo]) - mz.x) * invT); }, us, nc, picked,
+               drawn, sh);
+  if (first && threadIdx.x == 0)
+    for (int i = 0; i < nc; ++i) ttok[(size_t)s * N + fc + i] = drawn[i] < 0 ? 0 : drawn[i];
   T* q = qrows + ((size_t)node * S + s) * vocab;
-  for (int v = cl.lo + threadIdx.x; v < cl.hi; v += blockDim.x) q[v] = slice[v - cl.lo];
+  block_copy(q + cl.lo, slice, cl.hi - cl.lo);
   if (first && threadIdx.x == 0) qstats[(size_t)node * S + s] = mz;
   cl.g.sync();  // no CTA leaves while another may still read its exchange slots
 }
