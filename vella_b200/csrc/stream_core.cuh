@@ -481,21 +481,21 @@ __device__ __forceinline__ void flush_rowblock(const Epi& a, int c, int rb, bool
   if (gather) {
     // add the partial sums of the earlier CTAs (in CTA order), then this CTA's
     const int cf = cta_of((long long)rb * a.nkc, a.U, a.P);
-    if (lane == 0) {
-      for (int c2 = cf; c2 < c; ++c2) {
-        const int* f = wflags + (size_t)c2 * kRowWarps;
-        if (ld_flag(f) == 0) {
-          const long long t0 = clock64();
-          while (ld_flag(f) == 0) {
-            if ((a.abort && *reinterpret_cast<const volatile unsigned*>(a.abort)) || clock64() - t0 > kWaitCycles) {
-              atomicOr(a.fault, 16);
-              break;
-            }
+    // each lane reads one contributor's flag, so that up to 32 flags cost one round trip
+    // instead of one each; a lane whose flag is not yet set polls it, with the clock limit
+    for (int c2 = cf + lane; c2 < c; c2 += 32) {
+      const int* f = wflags + (size_t)c2 * kRowWarps;
+      if (ld_flag(f) == 0) {
+        const long long t0 = clock64();
+        while (ld_flag(f) == 0) {
+          if ((a.abort && *reinterpret_cast<const volatile unsigned*>(a.abort)) || clock64() - t0 > kWaitCycles) {
+            atomicOr(a.fault, 16);
+            break;
           }
         }
       }
-      __threadfence();
     }
+    __threadfence();
     __syncwarp();
     float sum[NT][4];
 #pragma unroll
@@ -530,8 +530,7 @@ __device__ __forceinline__ void flush_rowblock(const Epi& a, int c, int rb, bool
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[nt][e] = sum[nt][e] + acc[nt][e];
     __syncwarp();
-    if (lane == 0)  // consumed: leave the flags at zero for the next call
-      for (int c2 = cf; c2 < c; ++c2) wflags[(size_t)c2 * kRowWarps] = 0;
+    for (int c2 = cf + lane; c2 < c; c2 += 32) wflags[(size_t)c2 * kRowWarps] = 0;  // consumed: zero for the next call
   }
   const T* bias = static_cast<const T*>(a.bias);
   const T* res = static_cast<const T*>(a.res);
