@@ -519,7 +519,11 @@ int tc_splits(const vella_qgemm_desc& d) {
   const int rtiles = (d.n + kTcRows - 1) / kTcRows;
   const int by_wave = kTcWave / (2 * rtiles);
   const int by_stages = d.k / kTcK / kTcMinSplitStages;
-  return std::max(1, std::min(std::min(by_wave, by_stages), kTcMaxSplits));
+  int splits = std::max(1, std::min(std::min(by_wave, by_stages), kTcMaxSplits));
+  // a long K (a split keeps at least 100 stages: the 30B target's down projection) takes three
+  // splits while one token tile's splits fit one wave, even though two tiles then take two
+  if (d.k / kTcK / 3 >= 100 && 3 * rtiles <= kTcWave) splits = std::max(splits, 3);
+  return splits;
 }
 
 // Counters for every (token tile, row tile) at 128-token tiles, then [S][NA][Mp][N] fp32 with Mp
