@@ -24,12 +24,16 @@
 //               of its row into the operand tile (128-byte swizzled K-major rows; scales and
 //               biases read 8 groups at a time, a block ahead), then they run the epilogue
 //               out of tensor memory on interleaved 32-column chunks.
+// A call of at most 256 rows whose row tiles leave SMs idle splits K over blockIdx.z (the
+// split count from N and K only): each split writes its fp32 sums to the workspace, and the
+// tile's last split to arrive adds the splits' sums in split order and runs the epilogue.
 // Every wait is bounded (sm100::kWaitCycles); a wait that runs out records a fault
 // (vella_qgemm reports it) and the kernel finishes without waiting again.
 //
 // A row m of the output depends only on x[m, :] and the weights: the tensor core's per-
 // element accumulation order does not involve other tokens, so a row of a batched call is
-// bit-identical to the same row in any other call of more than 16 rows.
+// bit-identical to the same row in any other call of 17-256 rows (or of more than 256 rows:
+// the K split differs between the two classes).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
