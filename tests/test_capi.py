@@ -73,6 +73,27 @@ def test_workspace_depends_on_shape_not_rows():
     assert sizes[0] == sizes[1] == sizes[2] > 0
 
 
+def test_tensor_core_k_split_workspace_follows_the_row_classes():
+    """Calls of 17-256 rows whose row tiles leave SMs idle split K and need fp32 partial sums in
+    the workspace; calls of more than 256 rows, and shapes whose row tiles fill the GPU, do not.
+    The split count (hence each row's value) depends on N and K only within a class."""
+    L = _lib.lib()
+
+    def ws(m, n, k, bits=4, epi=0):
+        return L.vella_qgemm_workspace_size(ctypes.byref(_lib.QgemmDesc(m, n, k, bits, 64, _lib.BF16, epi)))
+
+    # bf16 draft down projection (16 row tiles, 96 stages): four splits below 257 rows
+    assert ws(32, 2048, 6144, 0) > 0 and ws(256, 2048, 6144, 0) > 0
+    assert ws(257, 2048, 6144, 0) == 0 and ws(1088, 2048, 6144, 0) == 0
+    # int4 down projection of the 30B target (K = 25600): three splits for the long K
+    assert ws(160, 5120, 25600) > 0 and ws(300, 5120, 25600) == 0
+    # the target's gate/up and LM head: their row tiles fill the GPU, one split
+    assert ws(160, 25600, 5120, 4, _lib.EPI["siluGate"]) == 0
+    assert ws(160, 151936, 5120) == 0
+    # the fp32 sums are sized for the rows rounded up to one 256-token tile
+    assert ws(32, 2048, 6144, 0) == ws(256, 2048, 6144, 0) >= 4 * 256 * 2048 * 4
+
+
 def test_unsupported_call_returns_status_not_crash():
     L = _lib.lib()
     d = _lib.QgemmDesc(4, 96, 520, 4, 64, _lib.BF16, 0)
